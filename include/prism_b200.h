@@ -1,0 +1,188 @@
+/*
+ * prism_b200.h -- C ABI of the B200 (sm_100a) quantized projection executor.
+ *
+ * This is the drop-in boundary for prism-inference's quantized decode path.
+ * Each entry point replaces one method of the reference's projection
+ * executor seam, `trait Pq2ProjectionExecutor`
+ * (reference src/kernels/projection.rs:16-350), or a CPU kernel the seam
+ * does not cover yet (cited per function).  A Rust host crate binds these
+ * symbols with `extern "C"` declarations (INTEGRATION.md shows the stub).
+ *
+ * Conventions
+ *  - Plain C types only; no CUDA or framework types.  `stream` arguments
+ *    are a `cudaStream_t` passed as `void*` (NULL = the executor's stream).
+ *  - Entry points without `_device` take HOST pointers and are synchronous:
+ *    they copy inputs in, run, copy outputs out and return a status.  The
+ *    `_device` variants take DEVICE pointers and only enqueue work; their
+ *    device-side errors surface at the next prism_b200_executor_sync().
+ *  - Status codes: PRISM_B200_OK (0) or one of PRISM_B200_E_*.  A device-side
+ *    failure (nonfinite output, bounded-wait timeout) is terminal for the
+ *    executor, as in the reference: no CPU replay; the output is zero-filled;
+ *    the executor reports PRISM_B200_E_FAULTED until
+ *    prism_b200_executor_reset().  Argument errors are decided before any
+ *    submission and leave the executor usable.
+ *  - One executor = one CUDA device + one stream.  Not thread-safe: callers
+ *    serialise, as the reference's `&mut self` executor scope does.
+ *  - Caller-owned buffers are never retained after a call returns
+ *    (reference src/kernels/projection.rs:10-13).
+ */
+#ifndef PRISM_B200_H
+#define PRISM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PRISM_B200_ABI_VERSION 1
+
+/* ---- status codes --------------------------------------------------- */
+#define PRISM_B200_OK 0
+#define PRISM_B200_E_INVALID 1     /* malformed arguments / extents          */
+#define PRISM_B200_E_UNSUPPORTED 2 /* tensor kind or geometry not served     */
+#define PRISM_B200_E_NONFINITE 3   /* nonfinite scale, activation or output  */
+#define PRISM_B200_E_DEVICE 4      /* CUDA runtime / allocation failure      */
+#define PRISM_B200_E_TIMEOUT 5     /* a bounded device wait expired          */
+#define PRISM_B200_E_FAULTED 6     /* executor closed by an earlier failure  */
+
+/* ---- tensor kinds (ggml / Prism type ids) --------------------------- */
+#define PRISM_B200_KIND_Q2_K 10
+#define PRISM_B200_KIND_Q8_K 15
+#define PRISM_B200_KIND_TQ2_0 35
+
+/* Native Q8_K activation block (reference tools/ternary/src/lib.rs:27-39):
+ * repr(C), 292 bytes. */
+typedef struct prism_b200_q8k_block {
+  float scale;
+  int8_t values[256];
+  int16_t sums[16];
+} prism_b200_q8k_block;
+
+/* A packed weight tensor in the reference's byte layout
+ * (reference src/model.rs:184-196 `Tensor`): `cols` = dimensions[0] (K),
+ * `rows` = product of the remaining dimensions, row-major rows of
+ * cols/256 blocks.  `data` is a host pointer of rows*cols/256*block bytes. */
+typedef struct prism_b200_tensor {
+  uint32_t kind;
+  uint64_t cols;
+  uint64_t rows;
+  const void *data;
+} prism_b200_tensor;
+
+typedef struct prism_b200_executor prism_b200_executor;
+typedef struct prism_b200_weight prism_b200_weight;
+
+/* ---- executor lifetime ---------------------------------------------- */
+
+/* Create an executor on CUDA device `device` with its own stream. */
+int prism_b200_executor_create(int device, prism_b200_executor **out);
+void prism_b200_executor_destroy(prism_b200_executor *ex);
+
+/* Stable arithmetic/placement identity string
+ * (reference src/kernels/projection.rs:18 `identity`). */
+const char *prism_b200_executor_identity(const prism_b200_executor *ex);
+
+/* Copies the last error message (NUL-terminated, truncated to `len`);
+ * returns the full message length. */
+size_t prism_b200_executor_last_error(const prism_b200_executor *ex, char *buf,
+                                      size_t len);
+
+/* Wait for all enqueued work; returns the first device-side status. */
+int prism_b200_executor_sync(prism_b200_executor *ex);
+
+/* The executor's own stream (a cudaStream_t), for callers that order their
+ * work or timing events against it. */
+void *prism_b200_executor_stream(const prism_b200_executor *ex);
+
+/* Clear a FAULTED executor (drops its sticky status, zeroes its scratch
+ * counters).  The caller restarts its scope, as the reference reopens a
+ * closed decoder scope. */
+int prism_b200_executor_reset(prism_b200_executor *ex);
+
+/* Eligibility from geometry alone, before any submission
+ * (reference src/kernels/projection.rs:41-46 `supports`).  Returns 1 when
+ * the tensor's kind is TQ2_0 or Q2_K and cols is a positive multiple of 256. */
+int prism_b200_executor_supports(const prism_b200_executor *ex,
+                                 const prism_b200_tensor *tensor);
+
+/* Submission count of one projection (reference
+ * src/kernels/projection.rs:28-35 `operation_count`): the number of
+ * 32-row x 256-column work units, or -1 when unsupported. */
+int64_t prism_b200_executor_operation_count(const prism_b200_executor *ex,
+                                            const prism_b200_tensor *tensor);
+
+/* ---- resident weights ----------------------------------------------- */
+
+/* Validate (finite fp16 scales, exact extents) and upload a weight once;
+ * it stays resident in HBM in the executor's tiled layout until released.
+ * Mirrors the resident tiles of the reference's DSP executor
+ * (reference docs/inference-efficiency.md:266-277). */
+int prism_b200_weight_upload(prism_b200_executor *ex,
+                             const prism_b200_tensor *tensor,
+                             prism_b200_weight **out);
+void prism_b200_weight_release(prism_b200_weight *w);
+
+/* ---- projections ---------------------------------------------------- */
+
+/* y = W x over already quantized Q8_K activations
+ * (reference src/kernels/projection.rs:48-60 `project`; per-row arithmetic
+ * of src/kernels/tquants.rs:270-287 and src/kernels/kquants.rs:346-420).
+ * `activation` holds cols/256 blocks; `out` receives rows floats.
+ * `fused` selects the PQ2 fused multiply-add contract in the reference and
+ * has no effect on TQ2_0 / Q2_K, whose reference dots have one order. */
+int prism_b200_project(prism_b200_executor *ex, const prism_b200_weight *w,
+                       const prism_b200_q8k_block *activation, int fused,
+                       float *out);
+int prism_b200_project_device(prism_b200_executor *ex,
+                              const prism_b200_weight *w,
+                              const void *activation_dev, int fused,
+                              float *out_dev, void *stream);
+
+/* Quantize x (n = cols floats) to Q8_K on the device and project
+ * (reference src/kernels.rs:1935-1987 `MatvecScratch::prepare` followed by
+ * `PreparedMatvec::matvec_into`; src/kernels/projection.rs:95-107
+ * `project_f32`).  `pinned` selects the pinned fused Q8_K rounding
+ * (reference src/kernels.rs:421-428); 0 is the Source contract. */
+int prism_b200_project_f32(prism_b200_executor *ex, const prism_b200_weight *w,
+                           const float *x, int pinned, float *out);
+
+/* Sibling projections sharing one activation vector, quantized once
+ * (reference src/kernels/projection.rs:112-131 `project_f32_group`;
+ * src/graph.rs:1869 `project_group_into_with_executor`). */
+int prism_b200_project_f32_group(prism_b200_executor *ex, size_t count,
+                                 const prism_b200_weight *const *weights,
+                                 const float *x, int pinned,
+                                 float *const *outs);
+
+/* Q8_K activation quantization of n floats (n % 256 == 0)
+ * (reference src/kernels.rs:463-522 `q8k_with_input`). */
+int prism_b200_quantize_q8k(prism_b200_executor *ex, const float *x, size_t n,
+                            int pinned, prism_b200_q8k_block *out);
+int prism_b200_quantize_q8k_device(prism_b200_executor *ex, const float *x_dev,
+                                   size_t n, int pinned, void *out_dev,
+                                   void *stream);
+
+/* The exact per-block integer dots of a projection, the parity observable
+ * of the int32 contract (reference src/kernels/tquants.rs:220-245
+ * `dot_tq2_block`; src/kernels/kquants.rs:162-200 `dot_q2_k_block`).
+ * TQ2_0 writes rows*nb int32 (`ints`); Q2_K writes isum to `ints` and the
+ * min-sum to `ints2` (each rows*nb int32).  Row-major [row][block]. */
+int prism_b200_block_dots(prism_b200_executor *ex, const prism_b200_weight *w,
+                          const prism_b200_q8k_block *activation,
+                          int32_t *ints, int32_t *ints2);
+
+/* ---- weight inspection ---------------------------------------------- */
+uint32_t prism_b200_weight_kind(const prism_b200_weight *w);
+uint64_t prism_b200_weight_rows(const prism_b200_weight *w);
+uint64_t prism_b200_weight_cols(const prism_b200_weight *w);
+/* Bytes the weight occupies in HBM (equal to its packed byte size plus the
+ * zero padding of the last 32-row tile). */
+uint64_t prism_b200_weight_device_bytes(const prism_b200_weight *w);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PRISM_B200_H */

@@ -1,0 +1,101 @@
+/*
+ * prism_oracle.h -- CPU restatement of the prism-inference reference arithmetic.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the parity checker for the
+ * B200 kernels and the timed CPU baseline in bench.py.  It is never linked
+ * into, loaded by, or called from the product library (libprism_b200.so).
+ *
+ * Every function restates the reference's "Source" arithmetic contract
+ * (the contract any synthetic / random-init model receives, reference
+ * src/graph.rs:3085-3110): binary32 products, binary64 sums where the
+ * reference sums in binary64, separate (unfused) multiply and add, and
+ * ties-to-even Q8_K rounding of the rounded binary32 product.
+ *
+ * Parity pin: the codec and dot functions reproduce the reference's golden
+ * fixtures bit for bit (the JSON files under tests/golden, extracted from the reference's
+ * tests/fixtures/upstream-tquants.json, upstream-kquants.json and
+ * swift-q8k-parity.json by tests/golden/make_golden.py).
+ */
+#ifndef PRISM_ORACLE_H
+#define PRISM_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (0 = ok).  Errors mirror the reference's `invalid(...)` sites. */
+#define PO_OK 0
+#define PO_E_INVALID 1
+#define PO_E_NONFINITE 3
+
+/* Native Q8_K activation block, reference tools/ternary/src/lib.rs:27-39
+ * (repr(C), 292 bytes: f32 scale, 256 x i8, 16 x i16 group sums). */
+typedef struct po_q8k_block {
+  float scale;
+  int8_t values[256];
+  int16_t sums[16];
+} po_q8k_block;
+
+/* Q8_0 record as stored by the KV cache extension: fp16 scale + 32 codes
+ * (34 bytes), built by the reference's Source Q8_0 codec
+ * (src/kernels.rs:552-617 with PINNED=false, NATIVE_SCALE=false). */
+typedef struct po_q8_0_block {
+  uint16_t d;
+  int8_t values[32];
+} po_q8_0_block;
+
+/* ---- binary16 ------------------------------------------------------- */
+float po_half_to_float(uint16_t h);
+uint16_t po_float_to_half(float f);
+float po_round_f16(float f);
+
+/* ---- activation quantizers ------------------------------------------ */
+int po_q8k_quantize(const float *x, size_t n, int pinned, po_q8k_block *out);
+int po_q8_0_quantize(const float *x, size_t n, po_q8_0_block *out);
+
+/* ---- TQ2_0 (ggml type 35, 66 B / 256 weights) ----------------------- */
+int po_tq2_decode(const uint8_t *blocks, size_t nblocks, float *out);
+int po_tq2_quantize(const float *x, size_t n, uint8_t *out);
+int po_tq2_block_dots(const uint8_t *w, const po_q8k_block *a, size_t nblocks,
+                      int32_t *ints);
+int po_tq2_dot(const uint8_t *w, const po_q8k_block *a, size_t nblocks,
+               float *out);
+
+/* ---- Q2_K (ggml type 10, 84 B / 256 weights) ------------------------ */
+int po_q2k_decode(const uint8_t *blocks, size_t nblocks, float *out);
+int po_q2k_block_dots(const uint8_t *w, const po_q8k_block *a, size_t nblocks,
+                      int32_t *isum, int32_t *msum);
+int po_q2k_dot(const uint8_t *w, const po_q8k_block *a, size_t nblocks,
+               float *out);
+
+/* ---- row-parallel matvec (CPU baseline) ----------------------------- */
+/* y[r] = dot(row r, a) for kind 35 or 10; rows split into contiguous
+ * chunks over `threads` workers as reference RowParallelism::fill does
+ * (src/kernels/parallel_rows.rs:507-542,602-628).  First error in row
+ * order wins; output is zero-filled on error. */
+int po_matvec(uint32_t kind, const uint8_t *w, size_t rows, size_t cols,
+              const po_q8k_block *a, float *y, int threads);
+int po_block_bytes(uint32_t kind);
+
+/* ---- float primitives (Source contract) ----------------------------- */
+float po_float_dot(const float *a, const float *b, size_t n);
+float po_f16_dot(const float *a, const uint16_t *b, size_t n);
+float po_silu(float v);
+float po_sigmoid(float v);
+int po_recurrent_decay(float alpha, float time_bias, float decay_weight,
+                       float *out);
+int po_rms_norm(const float *x, const float *w, size_t n, float eps,
+                float *out);
+int po_add_rms_norm(float *values, const float *delta, const float *w,
+                    size_t n, float eps, float *out);
+void po_l2_norm(float *x, size_t n, float eps);
+int po_softmax_round_f16(float *v, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,163 @@
+// common.cuh -- shared device helpers for the sm_100a kernels.
+//
+// Status word: every kernel reports failures by OR-ing a bit into a
+// device-resident status word that the host reads after the work it
+// enqueued (no __trap, no device assert).  Every spin-wait is bounded.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace prism {
+
+// Status bits (device side).  Host maps them to PRISM_B200_E_* codes.
+enum : unsigned {
+  kStatusNonfinite = 1u << 0,  // nonfinite activation scale or output
+  kStatusInvalid = 1u << 1,    // quantizer range violation
+  kStatusTimeout = 1u << 2,    // a bounded wait expired
+};
+
+// Upper bound on polls of an mbarrier (each poll suspends for a bounded
+// time in hardware); far above any legitimate latency.
+constexpr unsigned kMaxPolls = 1u << 24;
+
+__device__ __forceinline__ void report(unsigned *status, unsigned bit) {
+  atomicOr(status, bit);
+}
+
+// ---- binary16 <-> binary32, exact IEEE definitions ------------------------
+
+__device__ __forceinline__ float half_bits_to_float(uint16_t h) {
+  uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 31u;
+  uint32_t man = h & 1023u;
+  uint32_t bits;
+  if (exp == 0) {
+    if (man == 0) {
+      bits = sign;
+    } else {
+      // subnormal: man * 2^-24, normalise via the leading-zero count
+      int lz = __clz(man) - 21;  // zeros above bit 10 within the 11-bit field
+      man = (man << lz) & 1023u;
+      bits = sign | ((uint32_t)(113 - lz) << 23) | (man << 13);
+    }
+  } else if (exp == 31) {
+    bits = sign | 0x7f800000u | (man << 13);
+  } else {
+    bits = sign | ((exp + 112u) << 23) | (man << 13);
+  }
+  return __uint_as_float(bits);
+}
+
+// Round-to-nearest-even binary32 -> binary16 bits; NaN -> signed 0x7e00.
+__device__ __forceinline__ uint16_t float_to_half_bits(float f) {
+  uint32_t x = __float_as_uint(f);
+  uint16_t sign = (uint16_t)((x >> 16) & 0x8000u);
+  uint32_t ax = x & 0x7fffffffu;
+  if (ax > 0x7f800000u) return sign | 0x7e00u;
+  if (ax >= 0x477ff000u) return sign | 0x7c00u;
+  if (ax >= 0x38800000u) {
+    uint32_t h = ((((ax >> 23) - 112u) << 10) | ((ax & 0x7fffffu) >> 13));
+    uint32_t rem = ax & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h += 1u;
+    return sign | (uint16_t)h;
+  }
+  if (ax <= 0x33000000u) return sign;
+  uint32_t e = ax >> 23;
+  uint32_t m = (ax & 0x7fffffu) | 0x800000u;
+  uint32_t s = 126u - e;
+  uint32_t h = m >> s;
+  uint32_t rem = m & ((1u << s) - 1u);
+  uint32_t half = 1u << (s - 1u);
+  if (rem > half || (rem == half && (h & 1u))) h += 1u;
+  return sign | (uint16_t)h;
+}
+
+__device__ __forceinline__ float round_f16(float f) {
+  return half_bits_to_float(float_to_half_bits(f));
+}
+
+__device__ __forceinline__ bool is_finite_f(float v) {
+  return (__float_as_uint(v) & 0x7f800000u) != 0x7f800000u;
+}
+
+// ---- byte dot products -----------------------------------------------------
+
+// sum of 4 (unsigned byte of a) * (signed byte of b) + c
+__device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// ---- mbarrier + bulk async copy (sm_90+ PTX) -------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Order this thread's earlier generic-proxy shared accesses before later
+// async-proxy (bulk copy) writes to the same buffer.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// 1-D bulk copy global -> shared, completing `bytes` of transaction on bar.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes,
+                                         uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], "
+      "%2, [%3];" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait; returns false (and reports) if the phase never completed.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned parity,
+                                                  unsigned *status) {
+  for (unsigned i = 0; i < kMaxPolls; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  report(status, kStatusTimeout);
+  return false;
+}
+
+// ---- programmatic dependent launch -----------------------------------------
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+}  // namespace prism

@@ -1,0 +1,456 @@
+// prism_b200.cu -- C ABI of the quantized projection executor.
+//
+// Host side of the drop-in boundary declared in include/prism_b200.h.  Each
+// entry point validates its arguments before any submission (the
+// reference's eligibility-before-submission rule), enqueues sm_100a
+// kernels on the executor's stream, and for host-pointer variants waits
+// and reads the device status word.  There is no CPU fallback: when a
+// kernel cannot run, the call fails.
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+#include "executor.cuh"
+#include "matvec.cuh"
+#include "q8k.cuh"
+
+using namespace prism;
+
+namespace {
+
+constexpr size_t kMaxCols = 1u << 20;  // reference MAX_WIDTH (src/graph.rs:78)
+
+int status_to_code(unsigned st) {
+  if (st & kStatusTimeout) return PRISM_B200_E_TIMEOUT;
+  if (st & kStatusNonfinite) return PRISM_B200_E_NONFINITE;
+  if (st & kStatusInvalid) return PRISM_B200_E_INVALID;
+  return PRISM_B200_OK;
+}
+
+int cuda_fail(prism_b200_executor *ex, cudaError_t e, const char *what) {
+  return ex->fail(PRISM_B200_E_DEVICE, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CK(call, what)                                    \
+  do {                                                    \
+    cudaError_t _e = (call);                              \
+    if (_e != cudaSuccess) return cuda_fail(ex, _e, what); \
+  } while (0)
+
+int block_bytes(uint32_t kind) {
+  if (kind == PRISM_B200_KIND_TQ2_0) return 66;
+  if (kind == PRISM_B200_KIND_Q2_K) return 84;
+  return 0;
+}
+
+bool geometry_ok(const prism_b200_tensor *t) {
+  return t && block_bytes(t->kind) != 0 && t->cols > 0 && t->cols % 256 == 0 &&
+         t->cols <= kMaxCols && t->rows > 0 && t->rows <= (1ull << 31);
+}
+
+cudaStream_t pick(prism_b200_executor *ex, void *stream) {
+  return stream ? reinterpret_cast<cudaStream_t>(stream) : ex->stream;
+}
+
+int check_open(prism_b200_executor *ex) {
+  if (!ex) return PRISM_B200_E_INVALID;
+  if (ex->faulted)
+    return ex->fail(PRISM_B200_E_FAULTED, "executor closed by an earlier failure: %s",
+                    ex->last_error.c_str());
+  return PRISM_B200_OK;
+}
+
+template <int KIND, int MODE>
+cudaError_t launch_matvec_t(prism_b200_executor *ex, const prism_b200_weight *w,
+                            const void *act, float *y, int32_t *ints, int32_t *ints2,
+                            cudaStream_t s) {
+  constexpr int UNIT = UnitTraits<KIND>::bytes;
+  MatvecArgs a;
+  a.w = w->d_units;
+  a.act = static_cast<const uint8_t *>(act);
+  a.nb = w->nb;
+  a.ntiles = w->ntiles;
+  a.rows = (int)w->rows;
+  a.y = y;
+  a.partial = w->d_partial;
+  a.tile_cnt = w->d_cnt;
+  a.ints = ints;
+  a.ints2 = ints2;
+  a.status = ex->d_status;
+  long units = (long)w->ntiles * w->nb;
+  long grid = (units + kWarps - 1) / kWarps;
+  long cap = 2L * ex->num_sms;
+  if (grid > cap) grid = cap;
+  size_t smem = MatvecSmem::total(w->nb, UNIT);
+  auto kern = matvec_kernel<KIND, MODE, false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  kern<<<(unsigned)grid, kThreads, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_matvec(prism_b200_executor *ex, const prism_b200_weight *w, const void *act,
+                          float *y, cudaStream_t s) {
+  if (w->kind == PRISM_B200_KIND_TQ2_0)
+    return launch_matvec_t<35, kModeOutput>(ex, w, act, y, nullptr, nullptr, s);
+  return launch_matvec_t<10, kModeOutput>(ex, w, act, y, nullptr, nullptr, s);
+}
+
+cudaError_t launch_quantize(prism_b200_executor *ex, const float *x, size_t n, int pinned,
+                            void *out, cudaStream_t s) {
+  int nblocks = (int)(n / 256);
+  int grid = (nblocks * 32 + 255) / 256;
+  q8k_quantize_kernel<<<grid, 256, 0, s>>>(x, nblocks, pinned, static_cast<uint8_t *>(out),
+                                            ex->d_status);
+  return cudaGetLastError();
+}
+
+// Wait for the stream and fold the device status into a return code.  Any
+// device-side failure closes the executor (no CPU replay).
+int finish(prism_b200_executor *ex, cudaStream_t s) {
+  CK(cudaMemcpyAsync(ex->h_status, ex->d_status, sizeof(unsigned), cudaMemcpyDeviceToHost, s),
+     "status readback");
+  CK(cudaStreamSynchronize(s), "stream synchronize");
+  unsigned st = *ex->h_status;
+  if (st) {
+    ex->faulted = true;
+    int code = status_to_code(st);
+    return ex->fail(code, "device reported status 0x%x", st);
+  }
+  return PRISM_B200_OK;
+}
+
+int validate_weight(prism_b200_executor *ex, const prism_b200_weight *w) {
+  if (!w || w->ex != ex || !w->d_units)
+    return ex->fail(PRISM_B200_E_INVALID, "weight does not belong to this executor");
+  return PRISM_B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int prism_b200_executor_create(int device, prism_b200_executor **out) {
+  if (!out) return PRISM_B200_E_INVALID;
+  *out = nullptr;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count)
+    return PRISM_B200_E_DEVICE;
+  if (cudaSetDevice(device) != cudaSuccess) return PRISM_B200_E_DEVICE;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return PRISM_B200_E_DEVICE;
+  if (prop.major < 10) return PRISM_B200_E_UNSUPPORTED;  // sm_100a build only
+  auto *ex = new prism_b200_executor();
+  ex->device = device;
+  ex->num_sms = prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&ex->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&ex->d_status, 64) != cudaSuccess ||
+      cudaHostAlloc(reinterpret_cast<void **>(&ex->h_status), 64, cudaHostAllocDefault) !=
+          cudaSuccess ||
+      cudaMemset(ex->d_status, 0, 64) != cudaSuccess) {
+    prism_b200_executor_destroy(ex);
+    return PRISM_B200_E_DEVICE;
+  }
+  char id[512];
+  snprintf(id, sizeof(id),
+           "prism-b200:sm_%d%d:%s:tq2_0+q2_k:q8k-source:tile32-bulk:abi%d", prop.major,
+           prop.minor, prop.name, PRISM_B200_ABI_VERSION);
+  ex->identity = id;
+  *out = ex;
+  return PRISM_B200_OK;
+}
+
+void prism_b200_executor_destroy(prism_b200_executor *ex) {
+  if (!ex) return;
+  cudaSetDevice(ex->device);
+  if (ex->stream) cudaStreamSynchronize(ex->stream);
+  for (auto *w : std::set<prism_b200_weight *>(ex->weights)) prism_b200_weight_release(w);
+  ex->act.release();
+  ex->x.release();
+  ex->y.release();
+  ex->ints.release();
+  ex->ints2.release();
+  if (ex->d_status) cudaFree(ex->d_status);
+  if (ex->h_status) cudaFreeHost(ex->h_status);
+  if (ex->stream) cudaStreamDestroy(ex->stream);
+  delete ex;
+}
+
+const char *prism_b200_executor_identity(const prism_b200_executor *ex) {
+  return ex ? ex->identity.c_str() : "";
+}
+
+size_t prism_b200_executor_last_error(const prism_b200_executor *ex, char *buf, size_t len) {
+  if (!ex) return 0;
+  if (buf && len) {
+    size_t n = ex->last_error.size() < len - 1 ? ex->last_error.size() : len - 1;
+    memcpy(buf, ex->last_error.data(), n);
+    buf[n] = 0;
+  }
+  return ex->last_error.size();
+}
+
+void *prism_b200_executor_stream(const prism_b200_executor *ex) {
+  return ex ? reinterpret_cast<void *>(ex->stream) : nullptr;
+}
+
+int prism_b200_executor_sync(prism_b200_executor *ex) {
+  if (!ex) return PRISM_B200_E_INVALID;
+  cudaSetDevice(ex->device);
+  CK(cudaDeviceSynchronize(), "device synchronize");
+  return finish(ex, ex->stream);
+}
+
+int prism_b200_executor_reset(prism_b200_executor *ex) {
+  if (!ex) return PRISM_B200_E_INVALID;
+  cudaSetDevice(ex->device);
+  CK(cudaDeviceSynchronize(), "device synchronize");
+  CK(cudaMemset(ex->d_status, 0, 64), "status reset");
+  for (auto *w : ex->weights)
+    CK(cudaMemset(w->d_cnt, 0, sizeof(unsigned) * (size_t)w->ntiles), "counter reset");
+  ex->faulted = false;
+  ex->last_error.clear();
+  return PRISM_B200_OK;
+}
+
+int prism_b200_executor_supports(const prism_b200_executor *ex,
+                                 const prism_b200_tensor *tensor) {
+  return ex && geometry_ok(tensor) ? 1 : 0;
+}
+
+int64_t prism_b200_executor_operation_count(const prism_b200_executor *ex,
+                                            const prism_b200_tensor *tensor) {
+  if (!prism_b200_executor_supports(ex, tensor)) return -1;
+  int64_t tiles = (int64_t)((tensor->rows + kTileRows - 1) / kTileRows);
+  return tiles * (int64_t)(tensor->cols / 256);
+}
+
+int prism_b200_weight_upload(prism_b200_executor *ex, const prism_b200_tensor *t,
+                             prism_b200_weight **out) {
+  int st = check_open(ex);
+  if (st) return st;
+  if (!out || !t || !t->data) return ex->fail(PRISM_B200_E_INVALID, "null tensor or output");
+  *out = nullptr;
+  if (!geometry_ok(t))
+    return ex->fail(PRISM_B200_E_UNSUPPORTED, "unsupported kind %u or geometry %llux%llu",
+                    t->kind, (unsigned long long)t->cols, (unsigned long long)t->rows);
+  const int bb = block_bytes(t->kind);
+  const int nb = (int)(t->cols / 256);
+  const size_t nblocks = (size_t)t->rows * nb;
+  const uint8_t *src = static_cast<const uint8_t *>(t->data);
+  // reference `scale` (src/kernels.rs:152-154): every fp16 scale finite
+  for (size_t i = 0; i < nblocks; ++i) {
+    const uint8_t *blk = src + i * bb;
+    if (t->kind == PRISM_B200_KIND_TQ2_0) {
+      if ((blk[65] & 0x7c) == 0x7c) return ex->fail(PRISM_B200_E_NONFINITE, "nonfinite TQ2_0 scale");
+    } else {
+      if ((blk[81] & 0x7c) == 0x7c || (blk[83] & 0x7c) == 0x7c)
+        return ex->fail(PRISM_B200_E_NONFINITE, "nonfinite Q2_K scale");
+    }
+  }
+  cudaSetDevice(ex->device);
+  auto *w = new prism_b200_weight();
+  w->ex = ex;
+  w->kind = t->kind;
+  w->rows = t->rows;
+  w->cols = t->cols;
+  w->nb = nb;
+  w->ntiles = (int)((t->rows + kTileRows - 1) / kTileRows);
+  w->unit_bytes = t->kind == PRISM_B200_KIND_TQ2_0 ? kTq2Unit : kQ2kUnit;
+  w->device_bytes = (uint64_t)w->ntiles * nb * w->unit_bytes;
+  uint8_t *d_src = nullptr;
+  size_t src_bytes = nblocks * bb;
+  cudaError_t e = cudaMalloc(&w->d_units, w->device_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&w->d_partial, (size_t)w->ntiles * nb * kTileRows * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&w->d_cnt, (size_t)w->ntiles * 4);
+  if (e == cudaSuccess) e = cudaMemsetAsync(w->d_cnt, 0, (size_t)w->ntiles * 4, ex->stream);
+  if (e == cudaSuccess) e = cudaMalloc(&d_src, src_bytes);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(d_src, src, src_bytes, cudaMemcpyHostToDevice, ex->stream);
+  if (e == cudaSuccess) {
+    long threads = (long)w->ntiles * nb * kTileRows;
+    unsigned grid = (unsigned)((threads + 255) / 256);
+    if (t->kind == PRISM_B200_KIND_TQ2_0)
+      repack_kernel<35><<<grid, 256, 0, ex->stream>>>(d_src, (int)t->rows, nb, w->ntiles, w->d_units);
+    else
+      repack_kernel<10><<<grid, 256, 0, ex->stream>>>(d_src, (int)t->rows, nb, w->ntiles, w->d_units);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ex->stream);
+  if (d_src) cudaFree(d_src);
+  if (e != cudaSuccess) {
+    if (w->d_units) cudaFree(w->d_units);
+    if (w->d_partial) cudaFree(w->d_partial);
+    if (w->d_cnt) cudaFree(w->d_cnt);
+    delete w;
+    return cuda_fail(ex, e, "weight upload");
+  }
+  ex->weights.insert(w);
+  *out = w;
+  return PRISM_B200_OK;
+}
+
+void prism_b200_weight_release(prism_b200_weight *w) {
+  if (!w) return;
+  if (w->ex) {
+    cudaSetDevice(w->ex->device);
+    cudaStreamSynchronize(w->ex->stream);
+    w->ex->weights.erase(w);
+  }
+  if (w->d_units) cudaFree(w->d_units);
+  if (w->d_partial) cudaFree(w->d_partial);
+  if (w->d_cnt) cudaFree(w->d_cnt);
+  delete w;
+}
+
+uint32_t prism_b200_weight_kind(const prism_b200_weight *w) { return w ? w->kind : 0; }
+uint64_t prism_b200_weight_rows(const prism_b200_weight *w) { return w ? w->rows : 0; }
+uint64_t prism_b200_weight_cols(const prism_b200_weight *w) { return w ? w->cols : 0; }
+uint64_t prism_b200_weight_device_bytes(const prism_b200_weight *w) {
+  return w ? w->device_bytes : 0;
+}
+
+int prism_b200_project_device(prism_b200_executor *ex, const prism_b200_weight *w,
+                              const void *activation_dev, int fused, float *out_dev,
+                              void *stream) {
+  (void)fused;
+  int st = check_open(ex);
+  if (st) return st;
+  if ((st = validate_weight(ex, w))) return st;
+  if (!activation_dev || !out_dev) return ex->fail(PRISM_B200_E_INVALID, "null device buffer");
+  if (reinterpret_cast<uintptr_t>(activation_dev) % 4)
+    return ex->fail(PRISM_B200_E_INVALID, "activation must be 4-byte aligned");
+  cudaSetDevice(ex->device);
+  CK(launch_matvec(ex, w, activation_dev, out_dev, pick(ex, stream)), "matvec launch");
+  return PRISM_B200_OK;
+}
+
+int prism_b200_project(prism_b200_executor *ex, const prism_b200_weight *w,
+                       const prism_b200_q8k_block *activation, int fused, float *out) {
+  (void)fused;
+  int st = check_open(ex);
+  if (st) return st;
+  if ((st = validate_weight(ex, w))) return st;
+  if (!activation || !out) return ex->fail(PRISM_B200_E_INVALID, "null buffer");
+  cudaSetDevice(ex->device);
+  const size_t abytes = (size_t)w->nb * sizeof(prism_b200_q8k_block);
+  const size_t ybytes = (size_t)w->rows * sizeof(float);
+  CK(ex->act.ensure(abytes), "activation buffer");
+  CK(ex->y.ensure(ybytes), "output buffer");
+  cudaStream_t s = ex->stream;
+  CK(cudaMemcpyAsync(ex->act.ptr, activation, abytes, cudaMemcpyHostToDevice, s), "activation copy");
+  CK(launch_matvec(ex, w, ex->act.ptr, static_cast<float *>(ex->y.ptr), s), "matvec launch");
+  CK(cudaMemcpyAsync(out, ex->y.ptr, ybytes, cudaMemcpyDeviceToHost, s), "output copy");
+  st = finish(ex, s);
+  if (st) memset(out, 0, ybytes);
+  return st;
+}
+
+int prism_b200_quantize_q8k_device(prism_b200_executor *ex, const float *x_dev, size_t n,
+                                   int pinned, void *out_dev, void *stream) {
+  int st = check_open(ex);
+  if (st) return st;
+  if (!x_dev || !out_dev || n == 0 || n % 256 || n > kMaxCols)
+    return ex->fail(PRISM_B200_E_INVALID, "Q8_K activations require a multiple of 256 columns");
+  if (reinterpret_cast<uintptr_t>(x_dev) % 16 || reinterpret_cast<uintptr_t>(out_dev) % 4)
+    return ex->fail(PRISM_B200_E_INVALID, "misaligned device buffer");
+  cudaSetDevice(ex->device);
+  CK(launch_quantize(ex, x_dev, n, pinned, out_dev, pick(ex, stream)), "quantize launch");
+  return PRISM_B200_OK;
+}
+
+int prism_b200_quantize_q8k(prism_b200_executor *ex, const float *x, size_t n, int pinned,
+                            prism_b200_q8k_block *out) {
+  int st = check_open(ex);
+  if (st) return st;
+  if (!x || !out || n == 0 || n % 256 || n > kMaxCols)
+    return ex->fail(PRISM_B200_E_INVALID, "Q8_K activations require a multiple of 256 columns");
+  cudaSetDevice(ex->device);
+  const size_t abytes = n / 256 * sizeof(prism_b200_q8k_block);
+  CK(ex->x.ensure(n * 4), "input buffer");
+  CK(ex->act.ensure(abytes), "activation buffer");
+  cudaStream_t s = ex->stream;
+  CK(cudaMemcpyAsync(ex->x.ptr, x, n * 4, cudaMemcpyHostToDevice, s), "input copy");
+  CK(launch_quantize(ex, static_cast<float *>(ex->x.ptr), n, pinned, ex->act.ptr, s), "quantize");
+  CK(cudaMemcpyAsync(out, ex->act.ptr, abytes, cudaMemcpyDeviceToHost, s), "output copy");
+  st = finish(ex, s);
+  if (st) memset(out, 0, abytes);
+  return st;
+}
+
+int prism_b200_project_f32_group(prism_b200_executor *ex, size_t count,
+                                 const prism_b200_weight *const *weights, const float *x,
+                                 int pinned, float *const *outs) {
+  int st = check_open(ex);
+  if (st) return st;
+  if (!count || !weights || !x || !outs) return ex->fail(PRISM_B200_E_INVALID, "empty group");
+  const uint64_t cols = weights[0] ? weights[0]->cols : 0;
+  size_t total_rows = 0;
+  for (size_t i = 0; i < count; ++i) {
+    if ((st = validate_weight(ex, weights[i]))) return st;
+    if (weights[i]->cols != cols)
+      return ex->fail(PRISM_B200_E_INVALID, "mismatched projection group columns");
+    if (!outs[i]) return ex->fail(PRISM_B200_E_INVALID, "null output");
+    total_rows += weights[i]->rows;
+  }
+  cudaSetDevice(ex->device);
+  const size_t n = cols;
+  const size_t abytes = n / 256 * sizeof(prism_b200_q8k_block);
+  CK(ex->x.ensure(n * 4), "input buffer");
+  CK(ex->act.ensure(abytes), "activation buffer");
+  CK(ex->y.ensure(total_rows * 4), "output buffer");
+  cudaStream_t s = ex->stream;
+  CK(cudaMemcpyAsync(ex->x.ptr, x, n * 4, cudaMemcpyHostToDevice, s), "input copy");
+  CK(launch_quantize(ex, static_cast<float *>(ex->x.ptr), n, pinned, ex->act.ptr, s), "quantize");
+  size_t off = 0;
+  for (size_t i = 0; i < count; ++i) {
+    float *y = static_cast<float *>(ex->y.ptr) + off;
+    CK(launch_matvec(ex, weights[i], ex->act.ptr, y, s), "matvec launch");
+    CK(cudaMemcpyAsync(outs[i], y, weights[i]->rows * 4, cudaMemcpyDeviceToHost, s), "output copy");
+    off += weights[i]->rows;
+  }
+  st = finish(ex, s);
+  if (st)
+    for (size_t i = 0; i < count; ++i) memset(outs[i], 0, weights[i]->rows * 4);
+  return st;
+}
+
+int prism_b200_project_f32(prism_b200_executor *ex, const prism_b200_weight *w, const float *x,
+                           int pinned, float *out) {
+  const prism_b200_weight *ws[1] = {w};
+  float *os[1] = {out};
+  return prism_b200_project_f32_group(ex, 1, ws, x, pinned, os);
+}
+
+int prism_b200_block_dots(prism_b200_executor *ex, const prism_b200_weight *w,
+                          const prism_b200_q8k_block *activation, int32_t *ints,
+                          int32_t *ints2) {
+  int st = check_open(ex);
+  if (st) return st;
+  if ((st = validate_weight(ex, w))) return st;
+  if (!activation || !ints || (w->kind == PRISM_B200_KIND_Q2_K && !ints2))
+    return ex->fail(PRISM_B200_E_INVALID, "null buffer");
+  cudaSetDevice(ex->device);
+  const size_t abytes = (size_t)w->nb * sizeof(prism_b200_q8k_block);
+  const size_t ibytes = (size_t)w->rows * w->nb * 4;
+  CK(ex->act.ensure(abytes), "activation buffer");
+  CK(ex->ints.ensure(ibytes), "ints buffer");
+  CK(ex->ints2.ensure(ibytes), "ints buffer");
+  cudaStream_t s = ex->stream;
+  CK(cudaMemcpyAsync(ex->act.ptr, activation, abytes, cudaMemcpyHostToDevice, s), "activation copy");
+  cudaError_t e;
+  if (w->kind == PRISM_B200_KIND_TQ2_0)
+    e = launch_matvec_t<35, kModeInts>(ex, w, ex->act.ptr, nullptr,
+                                       static_cast<int32_t *>(ex->ints.ptr), nullptr, s);
+  else
+    e = launch_matvec_t<10, kModeInts>(ex, w, ex->act.ptr, nullptr,
+                                       static_cast<int32_t *>(ex->ints.ptr),
+                                       static_cast<int32_t *>(ex->ints2.ptr), s);
+  CK(e, "block dots launch");
+  CK(cudaMemcpyAsync(ints, ex->ints.ptr, ibytes, cudaMemcpyDeviceToHost, s), "ints copy");
+  if (w->kind == PRISM_B200_KIND_Q2_K)
+    CK(cudaMemcpyAsync(ints2, ex->ints2.ptr, ibytes, cudaMemcpyDeviceToHost, s), "ints copy");
+  return finish(ex, s);
+}
+
+}  // extern "C"

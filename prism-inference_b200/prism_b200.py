@@ -1,0 +1,265 @@
+"""Python binding of libprism_b200.so (the C ABI in include/prism_b200.h).
+
+This mirrors the reference's projection-executor seam,
+``trait Pq2ProjectionExecutor`` (reference src/kernels/projection.rs:16-350),
+for Python callers and for this repository's tests and benchmark: the same
+method names (``identity``, ``supports``, ``operation_count``, ``project``,
+``project_f32``, ``project_f32_group``), the same argument meaning, and the
+same failure behaviour (an error clears the output and closes the executor;
+no CPU replay).  All arithmetic runs in the CUDA library; importing this
+module on a machine without the built library fails loudly.
+"""
+import ctypes
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libprism_b200.so")
+
+OK = 0
+E_INVALID, E_UNSUPPORTED, E_NONFINITE, E_DEVICE, E_TIMEOUT, E_FAULTED = 1, 2, 3, 4, 5, 6
+KIND_Q2_K, KIND_Q8_K, KIND_TQ2_0 = 10, 15, 35
+BLOCK_BYTES = {KIND_TQ2_0: 66, KIND_Q2_K: 84}
+
+Q8K_DTYPE = np.dtype([("scale", "<f4"), ("values", "i1", (256,)), ("sums", "<i2", (16,))])
+assert Q8K_DTYPE.itemsize == 292
+
+
+class PrismB200Error(RuntimeError):
+    def __init__(self, code, message):
+        super().__init__("prism_b200 error %d: %s" % (code, message))
+        self.code = code
+
+
+class _Tensor(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_uint32), ("cols", ctypes.c_uint64),
+                ("rows", ctypes.c_uint64), ("data", ctypes.c_void_p)]
+
+
+_lib = None
+
+
+def load():
+    """Load the built library; raise if it is missing (no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError("libprism_b200.so is not built: run prism-inference_b200/build.py")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, sz, i32, u32, u64, i64 = (ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
+                                  ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int64)
+    P = ctypes.POINTER
+    sig = {
+        "prism_b200_executor_create": (i32, [i32, P(vp)]),
+        "prism_b200_executor_destroy": (None, [vp]),
+        "prism_b200_executor_identity": (ctypes.c_char_p, [vp]),
+        "prism_b200_executor_last_error": (sz, [vp, ctypes.c_char_p, sz]),
+        "prism_b200_executor_sync": (i32, [vp]),
+        "prism_b200_executor_stream": (vp, [vp]),
+        "prism_b200_executor_reset": (i32, [vp]),
+        "prism_b200_executor_supports": (i32, [vp, P(_Tensor)]),
+        "prism_b200_executor_operation_count": (i64, [vp, P(_Tensor)]),
+        "prism_b200_weight_upload": (i32, [vp, P(_Tensor), P(vp)]),
+        "prism_b200_weight_release": (None, [vp]),
+        "prism_b200_project": (i32, [vp, vp, vp, i32, vp]),
+        "prism_b200_project_device": (i32, [vp, vp, vp, i32, vp, vp]),
+        "prism_b200_project_f32": (i32, [vp, vp, vp, i32, vp]),
+        "prism_b200_project_f32_group": (i32, [vp, sz, P(vp), vp, i32, P(vp)]),
+        "prism_b200_quantize_q8k": (i32, [vp, vp, sz, i32, vp]),
+        "prism_b200_quantize_q8k_device": (i32, [vp, vp, sz, i32, vp, vp]),
+        "prism_b200_block_dots": (i32, [vp, vp, vp, vp, vp]),
+        "prism_b200_weight_kind": (u32, [vp]),
+        "prism_b200_weight_rows": (u64, [vp]),
+        "prism_b200_weight_cols": (u64, [vp]),
+        "prism_b200_weight_device_bytes": (u64, [vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def exported_symbols():
+    """Names of every function declared in include/prism_b200.h."""
+    import re
+    hdr = os.path.join(os.path.dirname(HERE), "include", "prism_b200.h")
+    with open(hdr) as f:
+        text = f.read()
+    return sorted(set(re.findall(r"\b(prism_b200_\w+)\s*\(", text)))
+
+
+@dataclass
+class Tensor:
+    """A packed weight in the reference's byte layout (reference
+    src/model.rs:184-196): ``cols`` = dimensions[0] (K), ``rows`` = N."""
+    kind: int
+    cols: int
+    rows: int
+    data: np.ndarray
+    name: str = ""
+
+    def _c(self):
+        self.data = np.ascontiguousarray(self.data, dtype=np.uint8)
+        return _Tensor(self.kind, self.cols, self.rows, self.data.ctypes.data)
+
+
+def _p(a):
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+class Weight:
+    def __init__(self, executor, handle, tensor):
+        self.executor = executor
+        self.handle = handle
+        self.kind, self.cols, self.rows = tensor.kind, tensor.cols, tensor.rows
+        self.name = tensor.name
+
+    @property
+    def device_bytes(self):
+        return load().prism_b200_weight_device_bytes(self.handle)
+
+    def release(self):
+        if self.handle:
+            load().prism_b200_weight_release(self.handle)
+            self.handle = None
+
+
+class ProjectionExecutor:
+    """B200 projection executor (one CUDA device, one stream)."""
+
+    def __init__(self, device=0):
+        L = load()
+        h = ctypes.c_void_p()
+        st = L.prism_b200_executor_create(device, ctypes.byref(h))
+        if st != OK:
+            raise PrismB200Error(st, "executor create failed on device %d" % device)
+        self.h = h
+        self._weights = {}
+
+    # -- lifetime --------------------------------------------------------
+    def close(self):
+        if self.h:
+            load().prism_b200_executor_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def last_error(self):
+        buf = ctypes.create_string_buffer(1024)
+        load().prism_b200_executor_last_error(self.h, buf, 1024)
+        return buf.value.decode()
+
+    def _check(self, st):
+        if st != OK:
+            raise PrismB200Error(st, self.last_error())
+
+    def identity(self):
+        return load().prism_b200_executor_identity(self.h).decode()
+
+    def sync(self):
+        self._check(load().prism_b200_executor_sync(self.h))
+
+    def stream(self):
+        """The executor's cudaStream_t as an integer handle."""
+        return load().prism_b200_executor_stream(self.h)
+
+    def reset(self):
+        self._check(load().prism_b200_executor_reset(self.h))
+
+    # -- eligibility -----------------------------------------------------
+    def supports(self, tensor):
+        t = tensor._c()
+        return bool(load().prism_b200_executor_supports(self.h, ctypes.byref(t)))
+
+    def operation_count(self, tensor):
+        t = tensor._c()
+        n = load().prism_b200_executor_operation_count(self.h, ctypes.byref(t))
+        return None if n < 0 else n
+
+    # -- weights ---------------------------------------------------------
+    def upload(self, tensor):
+        t = tensor._c()
+        h = ctypes.c_void_p()
+        self._check(load().prism_b200_weight_upload(self.h, ctypes.byref(t), ctypes.byref(h)))
+        return Weight(self, h, tensor)
+
+    def _weight(self, w):
+        if isinstance(w, Weight):
+            return w
+        key = id(w)
+        if key not in self._weights:
+            self._weights[key] = (w, self.upload(w))
+        return self._weights[key][1]
+
+    # -- projections -----------------------------------------------------
+    def project(self, weight, activation, fused=False):
+        """y = W x for prepared Q8_K activation blocks (reference
+        src/kernels/projection.rs:48-60)."""
+        w = self._weight(weight)
+        act = np.ascontiguousarray(activation, dtype=Q8K_DTYPE)
+        if act.size * 256 != w.cols:
+            raise PrismB200Error(E_INVALID, "activation extent differs from weight columns")
+        out = np.zeros(w.rows, dtype=np.float32)
+        self._check(load().prism_b200_project(self.h, w.handle, _p(act), int(fused), _p(out)))
+        return out
+
+    def project_device(self, weight, act_ptr, out_ptr, stream=None, fused=False):
+        w = self._weight(weight)
+        self._check(load().prism_b200_project_device(
+            self.h, w.handle, ctypes.c_void_p(act_ptr), int(fused), ctypes.c_void_p(out_ptr),
+            ctypes.c_void_p(stream) if stream else None))
+
+    def project_f32(self, weight, x, pinned=False, out=None):
+        w = self._weight(weight)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.size != w.cols:
+            raise PrismB200Error(E_INVALID, "matvec requires a matching activation vector")
+        if out is None:
+            out = np.zeros(w.rows, dtype=np.float32)
+        assert out.dtype == np.float32 and out.size == w.rows and out.flags.c_contiguous
+        self._check(load().prism_b200_project_f32(self.h, w.handle, _p(x), int(pinned), _p(out)))
+        return out
+
+    def project_f32_group(self, weights, x, pinned=False):
+        ws = [self._weight(w) for w in weights]
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        outs = [np.zeros(w.rows, dtype=np.float32) for w in ws]
+        wh = (ctypes.c_void_p * len(ws))(*[w.handle.value for w in ws])
+        oh = (ctypes.c_void_p * len(ws))(*[o.ctypes.data for o in outs])
+        self._check(load().prism_b200_project_f32_group(self.h, len(ws), wh, _p(x), int(pinned), oh))
+        return outs
+
+    def quantize_q8k(self, x, pinned=False):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.zeros(x.size // 256, dtype=Q8K_DTYPE)
+        self._check(load().prism_b200_quantize_q8k(self.h, _p(x), x.size, int(pinned), _p(out)))
+        return out
+
+    def quantize_q8k_device(self, x_ptr, n, out_ptr, pinned=False, stream=None):
+        self._check(load().prism_b200_quantize_q8k_device(
+            self.h, ctypes.c_void_p(x_ptr), n, int(pinned), ctypes.c_void_p(out_ptr),
+            ctypes.c_void_p(stream) if stream else None))
+
+    def block_dots(self, weight, activation):
+        w = self._weight(weight)
+        act = np.ascontiguousarray(activation, dtype=Q8K_DTYPE)
+        nb = w.cols // 256
+        ints = np.zeros((w.rows, nb), dtype=np.int32)
+        ints2 = np.zeros((w.rows, nb), dtype=np.int32)
+        self._check(load().prism_b200_block_dots(self.h, w.handle, _p(act), _p(ints), _p(ints2)))
+        return ints if w.kind == KIND_TQ2_0 else (ints, ints2)

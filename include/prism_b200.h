@@ -173,6 +173,16 @@ int prism_b200_block_dots(prism_b200_executor *ex, const prism_b200_weight *w,
                           const prism_b200_q8k_block *activation,
                           int32_t *ints, int32_t *ints2);
 
+/* ---- synthetic inputs ----------------------------------------------- */
+/* Fill `out` (host, rows*cols/256 blocks in the reference byte layout) with
+ * seeded random packed weights: TQ2_0 codes uniform in {-1, 0, +1}, Q2_K
+ * quants uniform in 0..3 with random 4-bit scales/mins; fp16 block scales
+ * uniform in [scale_lo, scale_hi] (Q2_K dmin in half that range).  No
+ * counterpart in the reference: it stands in for model files, which this
+ * benchmark does not use.  Deterministic in (seed, stream). */
+int prism_b200_synth_weights(uint32_t kind, uint64_t rows, uint64_t cols, uint64_t seed,
+                             uint64_t stream, float scale_lo, float scale_hi, void *out);
+
 /* ---- weight inspection ---------------------------------------------- */
 uint32_t prism_b200_weight_kind(const prism_b200_weight *w);
 uint64_t prism_b200_weight_rows(const prism_b200_weight *w);

@@ -169,3 +169,160 @@ def recurrent_decay(alpha, time_bias, decay_weight):
     out = np.zeros(1, dtype=np.float32)
     _check(lib().po_recurrent_decay(alpha, time_bias, decay_weight, _p(out)))
     return out[0]
+
+
+# ---- Qwen35 model oracle ----------------------------------------------------
+
+class _Cfg(ctypes.Structure):
+    _fields_ = [("hidden", ctypes.c_int32), ("layers", ctypes.c_int32), ("heads", ctypes.c_int32),
+                ("kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("rope_dim", ctypes.c_int32), ("rope_sections", ctypes.c_int32 * 4),
+                ("rope_base", ctypes.c_float), ("eps", ctypes.c_float), ("ffn", ctypes.c_int32),
+                ("vocab", ctypes.c_int32), ("ssm_state", ctypes.c_int32),
+                ("ssm_groups", ctypes.c_int32), ("ssm_values", ctypes.c_int32),
+                ("conv_kernel", ctypes.c_int32), ("full_interval", ctypes.c_int32),
+                ("context", ctypes.c_int32), ("weight_kind", ctypes.c_uint32)]
+
+
+W_SLOTS = ["attn_norm.weight", "post_attention_norm.weight", "ffn_gate.weight", "ffn_up.weight",
+           "ffn_down.weight", "attn_q.weight", "attn_k.weight", "attn_v.weight",
+           "attn_output.weight", "attn_q_norm.weight", "attn_k_norm.weight", "attn_qkv.weight",
+           "attn_gate.weight", "ssm_beta.weight", "ssm_alpha.weight", "ssm_out.weight",
+           "ssm_conv1d.weight", "ssm_dt.bias", "ssm_a", "ssm_norm.weight"]
+
+
+def _model_lib():
+    L = lib()
+    if not getattr(L, "_model_declared", False):
+        vp, i32 = ctypes.c_void_p, ctypes.c_int
+        for name, res, args in [
+            ("po_qwen35_create", vp, [vp, vp, vp]), ("po_qwen35_destroy", None, [vp]),
+            ("po_qwen35_reset", None, [vp]), ("po_qwen35_step", i32, [vp, ctypes.c_uint32, vp, i32]),
+            ("po_qwen35_position", ctypes.c_int32, [vp]),
+            ("po_qwen35_conv_state", vp, [vp, i32]), ("po_qwen35_matrix_state", vp, [vp, i32]),
+            ("po_qwen35_keys", vp, [vp, i32]), ("po_qwen35_values", vp, [vp, i32]),
+            ("po_qwen35_hidden", vp, [vp]), ("po_greedy", i32, [vp, ctypes.c_size_t, vp]),
+            ("po_gdn_head_step", i32, [vp, vp, vp, vp, vp, ctypes.c_float, ctypes.c_float, i32, i32, vp]),
+            ("po_gdn_head_prefill_exact", i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, vp]),
+            ("po_gdn_head_prefill_chunked", i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
+            ("po_rope_frequencies", None, [vp, i32, vp]),
+        ]:
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        L._model_declared = True
+    return L
+
+
+def make_cfg(cfg):
+    c = _Cfg()
+    for f, _ in _Cfg._fields_:
+        if f == "rope_sections":
+            c.rope_sections = (ctypes.c_int32 * 4)(*cfg.rope_sections)
+        else:
+            setattr(c, f, getattr(cfg, f))
+    return c
+
+
+class Qwen35:
+    """The reference decode step on the CPU (Source arithmetic)."""
+
+    def __init__(self, cfg, weights):
+        L = _model_lib()
+        self.cfg = cfg
+        self._keep = {k: np.ascontiguousarray(v) for k, v in weights.items()}
+        self._c = make_cfg(cfg)
+        g = (ctypes.c_void_p * 2)(self._keep["token_embd.weight"].ctypes.data,
+                                  self._keep["output_norm.weight"].ctypes.data)
+        n = cfg.layers * len(W_SLOTS)
+        arr = (ctypes.c_void_p * n)()
+        for l in range(cfg.layers):
+            for s, name in enumerate(W_SLOTS):
+                a = self._keep.get("blk.%d.%s" % (l, name))
+                arr[l * len(W_SLOTS) + s] = a.ctypes.data if a is not None else None
+        self._g, self._arr = g, arr
+        self.h = L.po_qwen35_create(ctypes.byref(self._c), g, arr)
+        self.L = L
+
+    def close(self):
+        if self.h:
+            self.L.po_qwen35_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def reset(self):
+        self.L.po_qwen35_reset(self.h)
+
+    @property
+    def position(self):
+        return self.L.po_qwen35_position(self.h)
+
+    def step(self, token, logits=True, threads=8):
+        out = np.zeros(self.cfg.vocab, np.float32) if logits else None
+        st = self.L.po_qwen35_step(self.h, int(token), _p(out) if logits else None, threads)
+        _check(st)
+        return out
+
+    def hidden(self):
+        p = self.L.po_qwen35_hidden(self.h)
+        return np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_float)),
+                                     (self.cfg.hidden,)).copy()
+
+    def matrix_state(self, layer):
+        c = self.cfg
+        p = self.L.po_qwen35_matrix_state(self.h, layer)
+        return np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_float)),
+                                     (c.ssm_values, c.ssm_state, c.ssm_state)).copy()
+
+    def conv_state(self, layer):
+        c = self.cfg
+        p = self.L.po_qwen35_conv_state(self.h, layer)
+        return np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_float)),
+                                     (c.conv_channels, c.conv_kernel - 1)).copy()
+
+    def keys(self, layer):
+        c = self.cfg
+        p = self.L.po_qwen35_keys(self.h, layer)
+        n = self.position
+        return np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_uint16)),
+                                     (c.context, c.kv_heads * c.head_dim))[:n].copy()
+
+    def values(self, layer):
+        c = self.cfg
+        p = self.L.po_qwen35_values(self.h, layer)
+        n = self.position
+        return np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_uint16)),
+                                     (c.context, c.kv_heads * c.head_dim))[:n].copy()
+
+
+def greedy(logits):
+    out = np.zeros(1, np.uint32)
+    _check(_model_lib().po_greedy(_p(np.ascontiguousarray(logits, np.float32)), logits.size, _p(out)))
+    return int(out[0])
+
+
+def gdn_head_step(prev, q, k, v, decay, beta):
+    rows, width = prev.shape
+    nxt = np.zeros_like(prev)
+    out = np.zeros(rows, np.float32)
+    _check(_model_lib().po_gdn_head_step(_p(prev), _p(nxt), _p(q), _p(k), _p(v), decay, beta,
+                                         rows, width, _p(out)))
+    return nxt, out
+
+
+def gdn_head_prefill(state, q, k, v, decay, beta, chunk=None):
+    """q, k: [T][width]; v: [T][rows]; returns (new state, out [T][rows])."""
+    state = np.array(state, np.float32, copy=True)
+    T, width = q.shape
+    rows = v.shape[1]
+    out = np.zeros((T, rows), np.float32)
+    args = [_p(state), _p(np.ascontiguousarray(q, np.float32)), _p(np.ascontiguousarray(k, np.float32)),
+            _p(np.ascontiguousarray(v, np.float32)), _p(np.ascontiguousarray(decay, np.float32)),
+            _p(np.ascontiguousarray(beta, np.float32)), T, rows, width]
+    if chunk is None:
+        _check(_model_lib().po_gdn_head_prefill_exact(*args, _p(out)))
+    else:
+        _check(_model_lib().po_gdn_head_prefill_chunked(*args, chunk, _p(out)))
+    return state, out

@@ -234,11 +234,29 @@ int po_tq2_quantize(const float *x, size_t n, uint8_t *out) {
   return PO_OK;
 }
 
+/* Signed digits (code-1) of the four 2-bit fields of every byte value
+ * (reference src/kernels/tquants.rs:45-57 TQ2_BYTE_LUT). */
+static int8_t g_tq2_lut[256][4];
+static pthread_once_t g_tq2_once = PTHREAD_ONCE_INIT;
+static void tq2_lut_init(void) {
+  for (int b = 0; b < 256; ++b)
+    for (int j = 0; j < 4; ++j) g_tq2_lut[b][j] = (int8_t)(((b >> (2 * j)) & 3) - 1);
+}
+
 /* reference src/kernels/tquants.rs:220-245 dot_tq2_block: exact i32 sum of
- * (code-1)*q over the block's 256 elements. */
+ * (code-1)*q over the block's 256 elements, one lookup per packed byte. */
 static inline int32_t tq2_block_int(const uint8_t *blk, const int8_t *q) {
+  pthread_once(&g_tq2_once, tq2_lut_init);
   int32_t sum = 0;
-  for (int i = 0; i < 256; ++i) sum += tq2_code(blk, i) * (int32_t)q[i];
+  for (int half = 0; half < 2; ++half) {
+    const uint8_t *bytes = blk + half * 32;
+    const int8_t *v = q + half * 128;
+    for (int col = 0; col < 32; ++col) {
+      const int8_t *d = g_tq2_lut[bytes[col]];
+      sum += d[0] * (int32_t)v[col] + d[1] * (int32_t)v[col + 32] +
+             d[2] * (int32_t)v[col + 64] + d[3] * (int32_t)v[col + 96];
+    }
+  }
   return sum;
 }
 

@@ -17,9 +17,16 @@ enum : unsigned {
   kStatusTimeout = 1u << 2,    // a bounded wait expired
 };
 
-// Upper bound on polls of an mbarrier (each poll suspends for a bounded
-// time in hardware); far above any legitimate latency.
-constexpr unsigned kMaxPolls = 1u << 24;
+// Upper bound on any device-side wait, in nanoseconds of %globaltimer: far
+// above any legitimate latency, short enough that a lost completion ends the
+// kernel with a status bit instead of hanging the GPU.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ void report(unsigned *status, unsigned bit) {
   atomicOr(status, bit);
@@ -146,10 +153,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
 // Bounded wait; returns false (and reports) if the phase never completed.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned parity,
                                                   unsigned *status) {
-  for (unsigned i = 0; i < kMaxPolls; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  report(status, kStatusTimeout);
-  return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      report(status, kStatusTimeout);
+      return false;
+    }
+  }
+  return true;
 }
 
 // ---- programmatic dependent launch -----------------------------------------

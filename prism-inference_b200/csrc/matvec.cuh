@@ -1,31 +1,30 @@
 // matvec.cuh -- batch-1 packed ternary / 2-bit projection on sm_100a.
 //
-// y[r] = sum_b term(r, b), where term is the reference's per-block binary32
+// y[r] = sum_b term(r, b): term is the reference's per-block binary32
 // contribution and the sum is the reference's sequential binary32 chain over
 // blocks (TQ2_0: reference src/kernels/tquants.rs:270-287; Q2_K:
-// src/kernels/kquants.rs:346-420 kind 10).  Integer block dots are exact.
+// src/kernels/kquants.rs:346-420 kind 10).  Integer block dots are exact, so
+// outputs are bit-identical to the reference's CPU kernels.
 //
-// Device weight layout ("tiled", built once at upload):
-//   rows are grouped in 32-row tiles (the last tile zero padded); a UNIT is
-//   one tile x one 256-column block, stored contiguously, units ordered
-//   tile-major then block:
-//     TQ2_0 unit (2112 B): qs[4 chunks][32 rows][16 B] | d[32 rows] fp16
-//     Q2_K  unit (2688 B): qs[4][32][16 B] | scales[32][16 B] |
-//                          d[32] fp16 | dmin[32] fp16
-//   Chunk c of a row's block is bytes 16c..16c+15 of its 64 quant bytes.
-//   The layout holds exactly the packed bytes (plus tile padding): HBM
-//   traffic per projection equals the reference's packed size.
+// Device weight layout ("tiled", built once at upload).  Rows are grouped in
+// tiles of H rows (H = 32, 16 or 8, chosen per weight so that small matrices
+// still yield enough tiles for every SM); the last tile is zero padded.  A
+// UNIT is one tile x one 256-column block; a tile's nb units are contiguous:
+//   TQ2_0 unit (66 H B): qs[4 chunks][H rows][16 B] | d[H] fp16
+//   Q2_K  unit (84 H B): qs[4][H][16 B] | scales[H][16 B] | d[H] | dmin[H]
+// Chunk c of a row's block is bytes 16c..16c+15 of its 64 quant bytes.  The
+// layout holds exactly the packed bytes (plus tile padding), so HBM traffic
+// equals the reference's packed size.
 //
-// Execution: each CTA owns a contiguous range of units, so its weight bytes
-// are one contiguous HBM range, streamed by 1-D bulk async copies
-// (cp.async.bulk) into per-warp shared-memory rings (kDepth slots per warp,
-// mbarrier completion).  Lane l of a warp computes row 32t+l of the unit:
-// weights are lane-private 16-byte chunks, activations are broadcast
-// 16-byte shared loads, byte products use dp4a.  Each unit's 32 terms go to
-// a scratch row [tile][block][32]; the warp that completes a tile (counter
-// reaches nb) sums its terms in block order -- exactly the reference's
-// chain -- and writes y.  The counter is reset by that warp for the next
-// launch.
+// Execution: persistent CTAs loop over tiles (t = blockIdx.x, += gridDim.x).
+// A tile is streamed into shared memory by 1-D bulk async copies
+// (cp.async.bulk, one mbarrier per unit) two tiles ahead (double buffer), so
+// the next tile's bytes are in flight while the current one is computed.
+// Warp w computes units b = w, w+8, ...: the 32 lanes cover the H rows x 4
+// chunks (L = 32/H lanes per row), weights are lane-private 16-byte shared
+// loads, activations are broadcast 16-byte shared loads, byte products use
+// dp4a and per-row integer partials combine exactly with shuffles.  Terms go
+// to shared memory; then H threads run each row's chain in block order.
 #pragma once
 
 #include "common.cuh"
@@ -33,39 +32,27 @@
 
 namespace prism {
 
-constexpr int kTileRows = 32;
-constexpr int kTq2Unit = 2112;
-constexpr int kQ2kUnit = 2688;
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kDepth = 4;
+constexpr int kMaxNb = 64;  // columns <= 16384 per projection
 
-template <int KIND>
-struct UnitTraits;
-template <>
-struct UnitTraits<35> {
-  static constexpr int bytes = kTq2Unit;
-};
-template <>
-struct UnitTraits<10> {
-  static constexpr int bytes = kQ2kUnit;
-};
+__host__ __device__ constexpr int unit_bytes(int kind, int h) {
+  return (kind == 35 ? 66 : 84) * h;
+}
 
-// Shared-memory layout of the matvec kernel (dynamic smem).
+// Shared-memory layout (dynamic smem), all offsets 16-byte aligned.
 struct MatvecSmem {
-  static __host__ __device__ constexpr int act_values(int nb) { return 0; }
-  static __host__ __device__ constexpr int act_scale(int nb) { return nb * 256; }
-  static __host__ __device__ constexpr int act_sums(int nb) { return nb * 256 + nb * 4; }
-  static __host__ __device__ constexpr int act_asum(int nb) { return nb * 256 + nb * 4 + nb * 32; }
-  static __host__ __device__ constexpr int bars(int nb) {
-    return ((nb * 256 + nb * 4 + nb * 32 + nb * 4) + 15) / 16 * 16;
-  }
-  static __host__ __device__ constexpr int slots(int nb) {
-    return (bars(nb) + kWarps * kDepth * 8 + 127) / 128 * 128;
-  }
-  static __host__ __device__ constexpr int total(int nb, int unit_bytes) {
-    return slots(nb) + kWarps * kDepth * unit_bytes;
-  }
+  int nb, h, unit;
+  __host__ __device__ MatvecSmem(int nb_, int h_, int unit_) : nb(nb_), h(h_), unit(unit_) {}
+  __host__ __device__ int act_values() const { return 0; }
+  __host__ __device__ int act_scale() const { return nb * 256; }
+  __host__ __device__ int act_sums() const { return act_scale() + nb * 4; }
+  __host__ __device__ int act_asum() const { return act_sums() + nb * 32; }
+  __host__ __device__ int terms() const { return (act_asum() + nb * 4 + 15) / 16 * 16; }
+  __host__ __device__ int bars() const { return (terms() + nb * h * 4 + 15) / 16 * 16; }
+  __host__ __device__ int bufs() const { return (bars() + 2 * nb * 8 + 127) / 128 * 128; }
+  __host__ __device__ int tile_bytes() const { return nb * unit; }
+  __host__ __device__ int total() const { return bufs() + 2 * tile_bytes(); }
 };
 
 enum MatvecMode : int {
@@ -75,26 +62,34 @@ enum MatvecMode : int {
 
 struct MatvecArgs {
   const uint8_t *w;      // tiled units
-  const uint8_t *act;    // nb AoS Q8_K blocks
+  const uint8_t *act;    // nb AoS Q8_K blocks (4-byte aligned)
   int nb;                // blocks per row
-  int ntiles;            // 32-row tiles
+  int ntiles;            // H-row tiles
   int rows;              // true rows
   float *y;              // rows floats (kModeOutput)
-  float *partial;        // ntiles*nb*32 floats scratch
-  unsigned *tile_cnt;    // ntiles counters, zero between launches
   int32_t *ints;         // rows*nb (kModeInts)
   int32_t *ints2;        // rows*nb (kModeInts, Q2_K min sums)
   unsigned *status;
 };
 
-// One unit's contribution for this lane's row: TQ2_0.
-__device__ __forceinline__ void tq2_unit(const uint8_t *slot, const int8_t *av, int asum,
-                                         float s, int lane, int &dot, float &term) {
-  const uint4 *qs = reinterpret_cast<const uint4 *>(slot);
+__device__ __forceinline__ unsigned byte_of(const uint4 &v, int g) {
+  unsigned w = (g < 4) ? v.x : (g < 8) ? v.y : (g < 12) ? v.z : v.w;
+  return (w >> (8 * (g & 3))) & 0xffu;
+}
+
+// Lane partial of a TQ2_0 unit: sum over this lane's chunks of code*q,
+// with plane j scaled by 4^j folded back exactly.
+template <int H>
+__device__ __forceinline__ int tq2_lane_partial(const uint8_t *unit, const int8_t *av,
+                                                int lane) {
+  constexpr int L = 32 / H;
+  const int r = lane % H, s = lane / H;
+  const uint4 *qs = reinterpret_cast<const uint4 *>(unit);
   int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint4 wq = qs[c * 32 + lane];
+  for (int i = 0; i < 4 / L; ++i) {
+    const int c = s + i * L;
+    uint4 wq = qs[c * H + r];
     const int8_t *base = av + (c >> 1) * 128 + (c & 1) * 16;
     int4 a0 = *reinterpret_cast<const int4 *>(base);
     int4 a1 = *reinterpret_cast<const int4 *>(base + 32);
@@ -117,29 +112,22 @@ __device__ __forceinline__ void tq2_unit(const uint8_t *slot, const int8_t *av, 
     acc3 = dp4a_us(wq.z & 0xc0c0c0c0u, a3.z, acc3);
     acc3 = dp4a_us(wq.w & 0xc0c0c0c0u, a3.w, acc3);
   }
-  // plane j products carry a factor 4^j; codes are weight+1, so subtract the
-  // block's activation sum to obtain sum((code-1)*q) exactly.
-  dot = acc0 + (acc1 >> 2) + (acc2 >> 4) + (acc3 >> 6) - asum;
-  uint16_t dh = reinterpret_cast<const uint16_t *>(slot + 2048)[lane];
-  float d = half_bits_to_float(dh);
-  term = __fmul_rn((float)dot, __fmul_rn(d, s));
+  return acc0 + (acc1 >> 2) + (acc2 >> 4) + (acc3 >> 6);
 }
 
-__device__ __forceinline__ unsigned byte_of(const uint4 &v, int g) {
-  unsigned w = (g < 4) ? v.x : (g < 8) ? v.y : (g < 12) ? v.z : v.w;
-  return (w >> (8 * (g & 3))) & 0xffu;
-}
-
-// One unit's contribution for this lane's row: Q2_K.
-__device__ __forceinline__ void q2k_unit(const uint8_t *slot, const int8_t *av,
-                                         const int16_t *asums, float s, int lane, int &isum,
-                                         int &msum, float &term) {
-  const uint4 *qs = reinterpret_cast<const uint4 *>(slot);
-  uint4 sc = reinterpret_cast<const uint4 *>(slot + 2048)[lane];
+// Lane partial of a Q2_K unit's scaled integer sum: sum_g sc_g * sum q*a
+// over this lane's chunks (each chunk x plane is exactly one 16-group).
+template <int H>
+__device__ __forceinline__ int q2k_lane_partial(const uint8_t *unit, const int8_t *av,
+                                                const uint4 &sc, int lane) {
+  constexpr int L = 32 / H;
+  const int r = lane % H, s = lane / H;
+  const uint4 *qs = reinterpret_cast<const uint4 *>(unit);
   int is = 0;
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint4 wq = qs[c * 32 + lane];
+  for (int i = 0; i < 4 / L; ++i) {
+    const int c = s + i * L;
+    uint4 wq = qs[c * H + r];
     const int8_t *base = av + (c >> 1) * 128 + (c & 1) * 16;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -149,35 +137,35 @@ __device__ __forceinline__ void q2k_unit(const uint8_t *slot, const int8_t *av,
       acc = dp4a_us(wq.y & m, a.y, acc);
       acc = dp4a_us(wq.z & m, a.z, acc);
       acc = dp4a_us(wq.w & m, a.w, acc);
+      // group g = 8*(c/2) + 2*j + (c%2); c is lane dependent when L > 1
       const int g = 8 * (c >> 1) + 2 * j + (c & 1);
       is += (int)(byte_of(sc, g) & 15u) * (acc >> (2 * j));
     }
   }
-  int ms = 0;
+  return is;
+}
+
+// Sum a per-lane integer over the L lanes that share a row (exact).
+template <int H>
+__device__ __forceinline__ int row_allreduce(int v) {
 #pragma unroll
-  for (int g = 0; g < 16; ++g) ms += (int)asums[g] * (int)(byte_of(sc, g) >> 4);
-  isum = is;
-  msum = ms;
-  const uint16_t *dd = reinterpret_cast<const uint16_t *>(slot + 2048 + 512);
-  float d = half_bits_to_float(dd[lane]);
-  float dmin = half_bits_to_float(dd[32 + lane]);
-  float t1 = __fmul_rn(__fmul_rn(s, d), (float)is);
-  float t2 = __fmul_rn(__fmul_rn(s, dmin), (float)ms);
-  term = __fsub_rn(t1, t2);
+  for (int off = H; off < 32; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
 }
 
 // Stage the Q8_K activation (AoS, 4-byte aligned) into shared memory as
 // values[nb][256] | scale[nb] | sums[nb][16] | asum[nb].
-__device__ __forceinline__ void stage_activation(const uint8_t *act, int nb, uint8_t *smem,
-                                                 unsigned *status) {
-  int8_t *values = reinterpret_cast<int8_t *>(smem + MatvecSmem::act_values(nb));
-  float *scale = reinterpret_cast<float *>(smem + MatvecSmem::act_scale(nb));
-  int16_t *sums = reinterpret_cast<int16_t *>(smem + MatvecSmem::act_sums(nb));
-  int *asum = reinterpret_cast<int *>(smem + MatvecSmem::act_asum(nb));
+__device__ __forceinline__ void stage_activation(const uint8_t *act, const MatvecSmem &L,
+                                                 uint8_t *smem, unsigned *status) {
+  const int nb = L.nb;
+  int8_t *values = reinterpret_cast<int8_t *>(smem + L.act_values());
+  float *scale = reinterpret_cast<float *>(smem + L.act_scale());
+  int16_t *sums = reinterpret_cast<int16_t *>(smem + L.act_sums());
+  int *asum = reinterpret_cast<int *>(smem + L.act_asum());
   const uint32_t *src = reinterpret_cast<const uint32_t *>(act);
   // 73 words per block: word 0 scale, words 1..64 values, 65..72 sums
   for (int i = threadIdx.x; i < nb * 73; i += blockDim.x) {
-    int b = i / 73, k = i % 73;
+    int b = i / 73, k = i - b * 73;
     uint32_t v = src[i];
     if (k == 0) {
       scale[b] = __uint_as_float(v);
@@ -188,7 +176,6 @@ __device__ __forceinline__ void stage_activation(const uint8_t *act, int nb, uin
     }
   }
   __syncthreads();
-  // per-block activation sums (from the codes), one warp per block
   int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int b = warp; b < nb; b += blockDim.x >> 5) {
     const int32_t *vw = reinterpret_cast<const int32_t *>(values + b * 256);
@@ -203,117 +190,141 @@ __device__ __forceinline__ void stage_activation(const uint8_t *act, int nb, uin
   __syncthreads();
 }
 
-template <int KIND, int MODE, bool PDL>
+// Issue the bulk copies of tile t into buffer `buf` (one mbarrier per unit).
+__device__ __forceinline__ void issue_tile(const uint8_t *w, long t, int nb, int unit,
+                                           uint8_t *buf, uint64_t *bars) {
+  const uint8_t *src = w + t * (long)nb * unit;
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+    mbar_arrive_expect_tx(&bars[b], unit);
+    bulk_g2s(buf + b * unit, src + (long)b * unit, unit, &bars[b]);
+  }
+}
+
+template <int KIND, int H, int MODE, bool PDL>
 __global__ void __launch_bounds__(kThreads) matvec_kernel(MatvecArgs args) {
-  constexpr int UNIT = UnitTraits<KIND>::bytes;
+  constexpr int UNIT = unit_bytes(KIND, H);
   extern __shared__ __align__(128) uint8_t smem[];
   const int nb = args.nb;
+  const MatvecSmem L(nb, H, UNIT);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long total_units = (long)args.ntiles * nb;
-  const long u0 = total_units * blockIdx.x / gridDim.x;
-  const long u1 = total_units * (blockIdx.x + 1) / gridDim.x;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars());  // [2][nb]
+  uint8_t *bufs = smem + L.bufs();                                  // [2][tile]
+  float *terms = reinterpret_cast<float *>(smem + L.terms());       // [nb][H]
 
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + MatvecSmem::bars(nb)) + warp * kDepth;
-  uint8_t *slots = smem + MatvecSmem::slots(nb) + (size_t)warp * kDepth * UNIT;
-
-  // Weights never depend on the previous kernel: start streaming them
-  // before waiting on the grid dependency.
-  if (lane == 0) {
-#pragma unroll
-    for (int k = 0; k < kDepth; ++k) mbar_init(&bars[k], 1);
+  for (int i = threadIdx.x; i < 2 * nb; i += blockDim.x) {
+    mbar_init(&bars[i], 1);
     mbar_init_fence();
-#pragma unroll
-    for (int k = 0; k < kDepth; ++k) {
-      long u = u0 + warp + (long)k * kWarps;
-      if (u < u1) {
-        mbar_arrive_expect_tx(&bars[k], UNIT);
-        bulk_g2s(slots + k * UNIT, args.w + u * UNIT, UNIT, &bars[k]);
-      }
-    }
   }
-  __syncwarp();
+  __syncthreads();
+  // Weights never depend on the previous kernel: stream the first two tiles
+  // before waiting on the grid dependency.
+  const int t0 = blockIdx.x;
+  if (t0 < args.ntiles) issue_tile(args.w, t0, nb, UNIT, bufs, bars);
+  if (t0 + (int)gridDim.x < args.ntiles)
+    issue_tile(args.w, t0 + gridDim.x, nb, UNIT, bufs + L.tile_bytes(), bars + nb);
   if (PDL) grid_dependency_wait();
-  stage_activation(args.act, nb, smem, args.status);
+  stage_activation(args.act, L, smem, args.status);
   if (PDL) grid_dependents_launch();
 
-  const int8_t *values = reinterpret_cast<const int8_t *>(smem + MatvecSmem::act_values(nb));
-  const float *ascale = reinterpret_cast<const float *>(smem + MatvecSmem::act_scale(nb));
-  const int16_t *asums = reinterpret_cast<const int16_t *>(smem + MatvecSmem::act_sums(nb));
-  const int *aasum = reinterpret_cast<const int *>(smem + MatvecSmem::act_asum(nb));
+  const int8_t *values = reinterpret_cast<const int8_t *>(smem + L.act_values());
+  const float *ascale = reinterpret_cast<const float *>(smem + L.act_scale());
+  const int16_t *asums = reinterpret_cast<const int16_t *>(smem + L.act_sums());
+  const int *aasum = reinterpret_cast<const int *>(smem + L.act_asum());
+  const int r = lane % H;
 
-  int i = 0;
-  for (long u = u0 + warp; u < u1; u += kWarps, ++i) {
-    const int k = i % kDepth;
-    const unsigned parity = (unsigned)(i / kDepth) & 1u;
-    if (!mbar_wait_bounded(&bars[k], parity, args.status)) break;
-    const uint8_t *slot = slots + k * UNIT;
-    const int t = (int)(u / nb), b = (int)(u % nb);
-    const int row = t * kTileRows + lane;
-    int dot = 0, dot2 = 0;
-    float term;
-    if (KIND == 35) {
-      tq2_unit(slot, values + b * 256, aasum[b], ascale[b], lane, dot, term);
-    } else {
-      q2k_unit(slot, values + b * 256, asums + b * 16, ascale[b], lane, dot, dot2, term);
-    }
-    __syncwarp();
-    // refill this slot with the warp's unit kDepth iterations ahead
-    const long un = u + (long)kDepth * kWarps;
-    if (lane == 0 && un < u1) {
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&bars[k], UNIT);
-      bulk_g2s(slots + k * UNIT, args.w + un * UNIT, UNIT, &bars[k]);
-    }
-    if (MODE == kModeInts) {
-      if (row < args.rows) {
-        args.ints[(size_t)row * nb + b] = dot;
-        if (KIND == 10) args.ints2[(size_t)row * nb + b] = dot2;
+  bool ok = true;
+  int it = 0;
+  for (int t = t0; t < args.ntiles; t += gridDim.x, ++it) {
+    const int k = it & 1;
+    const unsigned parity = (unsigned)(it >> 1) & 1u;
+    uint8_t *buf = bufs + k * L.tile_bytes();
+    uint64_t *bk = bars + k * nb;
+    const int row = t * H + r;
+    for (int b = warp; b < nb; b += kWarps) {
+      if (!mbar_wait_bounded(&bk[b], parity, args.status)) {
+        ok = false;
+        break;
       }
-      continue;
+      const uint8_t *unit = buf + b * UNIT;
+      const int8_t *av = values + b * 256;
+      const float s = ascale[b];
+      int dot, dot2 = 0;
+      float term;
+      if (KIND == 35) {
+        dot = row_allreduce<H>(tq2_lane_partial<H>(unit, av, lane)) - aasum[b];
+        const float d = half_bits_to_float(reinterpret_cast<const uint16_t *>(unit + 64 * H)[r]);
+        term = __fmul_rn((float)dot, __fmul_rn(d, s));
+      } else {
+        const uint4 sc = reinterpret_cast<const uint4 *>(unit + 64 * H)[r];
+        dot = row_allreduce<H>(q2k_lane_partial<H>(unit, av, sc, lane));
+        const int16_t *gs = asums + b * 16;
+        int ms = 0;
+#pragma unroll
+        for (int g = 0; g < 16; ++g) ms += (int)gs[g] * (int)(byte_of(sc, g) >> 4);
+        dot2 = ms;
+        const uint16_t *dd = reinterpret_cast<const uint16_t *>(unit + 80 * H);
+        const float d = half_bits_to_float(dd[r]);
+        const float dmin = half_bits_to_float(dd[H + r]);
+        const float t1 = __fmul_rn(__fmul_rn(s, d), (float)dot);
+        const float t2 = __fmul_rn(__fmul_rn(s, dmin), (float)ms);
+        term = __fsub_rn(t1, t2);
+      }
+      if (lane < H) {
+        if (MODE == kModeInts) {
+          if (row < args.rows) {
+            args.ints[(size_t)row * nb + b] = dot;
+            if (KIND == 10) args.ints2[(size_t)row * nb + b] = dot2;
+          }
+        } else {
+          terms[b * H + r] = term;
+        }
+      }
     }
-    // publish this unit's terms; the warp that completes the tile sums them
-    float *prow = args.partial + ((size_t)t * nb + b) * kTileRows;
-    prow[lane] = term;
-    __threadfence();
-    __syncwarp();
-    unsigned prev = 0;
-    if (lane == 0) prev = atomicAdd(&args.tile_cnt[t], 1u);
-    prev = __shfl_sync(0xffffffffu, prev, 0);
-    if (prev == (unsigned)(nb - 1)) {
-      __threadfence();
-      const float *pt = args.partial + (size_t)t * nb * kTileRows;
+    if (!__syncthreads_and(ok)) break;
+    if (MODE == kModeOutput && threadIdx.x < H) {
+      // the reference's chain: sum = 0; sum += term_b for b in order
       float sum = 0.0f;
-      for (int bb = 0; bb < nb; ++bb) sum = __fadd_rn(sum, __ldcg(pt + bb * kTileRows + lane));
-      if (row < args.rows) {
+      for (int b = 0; b < nb; ++b) sum = __fadd_rn(sum, terms[b * H + threadIdx.x]);
+      const int orow = t * H + threadIdx.x;
+      if (orow < args.rows) {
         if (!is_finite_f(sum)) report(args.status, kStatusNonfinite);
-        args.y[row] = sum;
+        args.y[orow] = sum;
       }
-      if (lane == 0) args.tile_cnt[t] = 0u;
+    }
+    __syncthreads();
+    // refill this buffer with the tile two steps ahead
+    const int tn = t + 2 * gridDim.x;
+    if (tn < args.ntiles) {
+      fence_proxy_async_smem();
+      issue_tile(args.w, tn, nb, UNIT, buf, bk);
     }
   }
-  // never leave bulk copies in flight into shared memory at exit: drain
-  // any slot that was armed but not consumed (only after a timeout break)
-  for (long u = u0 + warp + (long)i * kWarps; u < u1 && u < u0 + warp + (long)(i + kDepth) * kWarps;
-       u += kWarps, ++i) {
-    const int k = i % kDepth;
-    mbar_wait_bounded(&bars[k], (unsigned)(i / kDepth) & 1u, args.status);
+  if (!ok) {
+    // a wait expired: drain every armed copy (bounded) before exiting
+    for (int j = 0; j < 2; ++j) {
+      const int tj = t0 + (it + j) * gridDim.x;
+      if (tj >= args.ntiles) break;
+      const int kj = (it + j) & 1;
+      for (int b = threadIdx.x; b < nb; b += blockDim.x)
+        mbar_wait_bounded(&bars[kj * nb + b], (unsigned)((it + j) >> 1) & 1u, args.status);
+    }
   }
 }
 
 // ---- upload-time repack: reference row-major blocks -> tiled units ---------
-// One thread per (unit, lane).  src is the reference byte layout.
-template <int KIND>
+// One thread per (tile, block, row).  src is the reference byte layout.
+template <int KIND, int H>
 __global__ void repack_kernel(const uint8_t *__restrict__ src, int rows, int nb, int ntiles,
                               uint8_t *__restrict__ dst) {
-  constexpr int UNIT = UnitTraits<KIND>::bytes;
+  constexpr int UNIT = unit_bytes(KIND, H);
   constexpr int BB = KIND == 35 ? 66 : 84;
   long gid = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  long total = (long)ntiles * nb * kTileRows;
+  long total = (long)ntiles * nb * H;
   if (gid >= total) return;
-  int lane = (int)(gid % kTileRows);
-  long u = gid / kTileRows;
+  int r = (int)(gid % H);
+  long u = gid / H;
   int t = (int)(u / nb), b = (int)(u % nb);
-  int row = t * kTileRows + lane;
+  int row = t * H + r;
   uint8_t *unit = dst + u * UNIT;
   uint8_t blk[BB];
   if (row < rows) {
@@ -324,16 +335,16 @@ __global__ void repack_kernel(const uint8_t *__restrict__ src, int rows, int nb,
   }
   const int qoff = KIND == 35 ? 0 : 16;
   for (int c = 0; c < 4; ++c)
-    for (int i = 0; i < 16; ++i) unit[(c * 32 + lane) * 16 + i] = blk[qoff + c * 16 + i];
+    for (int i = 0; i < 16; ++i) unit[(c * H + r) * 16 + i] = blk[qoff + c * 16 + i];
   if (KIND == 35) {
-    unit[2048 + lane * 2] = blk[64];
-    unit[2048 + lane * 2 + 1] = blk[65];
+    unit[64 * H + r * 2] = blk[64];
+    unit[64 * H + r * 2 + 1] = blk[65];
   } else {
-    for (int i = 0; i < 16; ++i) unit[2048 + lane * 16 + i] = blk[i];
-    unit[2560 + lane * 2] = blk[80];
-    unit[2560 + lane * 2 + 1] = blk[81];
-    unit[2624 + lane * 2] = blk[82];
-    unit[2624 + lane * 2 + 1] = blk[83];
+    for (int i = 0; i < 16; ++i) unit[64 * H + r * 16 + i] = blk[i];
+    unit[80 * H + r * 2] = blk[80];
+    unit[80 * H + r * 2 + 1] = blk[81];
+    unit[82 * H + r * 2] = blk[82];
+    unit[82 * H + r * 2 + 1] = blk[83];
   }
 }
 

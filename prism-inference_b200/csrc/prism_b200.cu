@@ -11,14 +11,12 @@
 
 #include "common.cuh"
 #include "executor.cuh"
-#include "matvec.cuh"
-#include "q8k.cuh"
 
 using namespace prism;
 
 namespace {
 
-constexpr size_t kMaxCols = 1u << 20;  // reference MAX_WIDTH (src/graph.rs:78)
+constexpr size_t kMaxCols = (size_t)kMaxNb * 256;
 
 int status_to_code(unsigned st) {
   if (st & kStatusTimeout) return PRISM_B200_E_TIMEOUT;
@@ -31,9 +29,9 @@ int cuda_fail(prism_b200_executor *ex, cudaError_t e, const char *what) {
   return ex->fail(PRISM_B200_E_DEVICE, "%s: %s", what, cudaGetErrorString(e));
 }
 
-#define CK(call, what)                                    \
-  do {                                                    \
-    cudaError_t _e = (call);                              \
+#define CK(call, what)                                     \
+  do {                                                     \
+    cudaError_t _e = (call);                               \
     if (_e != cudaSuccess) return cuda_fail(ex, _e, what); \
   } while (0)
 
@@ -45,7 +43,7 @@ int block_bytes(uint32_t kind) {
 
 bool geometry_ok(const prism_b200_tensor *t) {
   return t && block_bytes(t->kind) != 0 && t->cols > 0 && t->cols % 256 == 0 &&
-         t->cols <= kMaxCols && t->rows > 0 && t->rows <= (1ull << 31);
+         t->cols <= kMaxCols && t->rows > 0 && t->rows <= (1ull << 30);
 }
 
 cudaStream_t pick(prism_b200_executor *ex, void *stream) {
@@ -58,52 +56,6 @@ int check_open(prism_b200_executor *ex) {
     return ex->fail(PRISM_B200_E_FAULTED, "executor closed by an earlier failure: %s",
                     ex->last_error.c_str());
   return PRISM_B200_OK;
-}
-
-template <int KIND, int MODE>
-cudaError_t launch_matvec_t(prism_b200_executor *ex, const prism_b200_weight *w,
-                            const void *act, float *y, int32_t *ints, int32_t *ints2,
-                            cudaStream_t s) {
-  constexpr int UNIT = UnitTraits<KIND>::bytes;
-  MatvecArgs a;
-  a.w = w->d_units;
-  a.act = static_cast<const uint8_t *>(act);
-  a.nb = w->nb;
-  a.ntiles = w->ntiles;
-  a.rows = (int)w->rows;
-  a.y = y;
-  a.partial = w->d_partial;
-  a.tile_cnt = w->d_cnt;
-  a.ints = ints;
-  a.ints2 = ints2;
-  a.status = ex->d_status;
-  long units = (long)w->ntiles * w->nb;
-  long grid = (units + kWarps - 1) / kWarps;
-  long cap = 2L * ex->num_sms;
-  if (grid > cap) grid = cap;
-  size_t smem = MatvecSmem::total(w->nb, UNIT);
-  auto kern = matvec_kernel<KIND, MODE, false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-  if (e != cudaSuccess) return e;
-  kern<<<(unsigned)grid, kThreads, smem, s>>>(a);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_matvec(prism_b200_executor *ex, const prism_b200_weight *w, const void *act,
-                          float *y, cudaStream_t s) {
-  if (w->kind == PRISM_B200_KIND_TQ2_0)
-    return launch_matvec_t<35, kModeOutput>(ex, w, act, y, nullptr, nullptr, s);
-  return launch_matvec_t<10, kModeOutput>(ex, w, act, y, nullptr, nullptr, s);
-}
-
-cudaError_t launch_quantize(prism_b200_executor *ex, const float *x, size_t n, int pinned,
-                            void *out, cudaStream_t s) {
-  int nblocks = (int)(n / 256);
-  int grid = (nblocks * 32 + 255) / 256;
-  q8k_quantize_kernel<<<grid, 256, 0, s>>>(x, nblocks, pinned, static_cast<uint8_t *>(out),
-                                            ex->d_status);
-  return cudaGetLastError();
 }
 
 // Wait for the stream and fold the device status into a return code.  Any
@@ -122,9 +74,14 @@ int finish(prism_b200_executor *ex, cudaStream_t s) {
 }
 
 int validate_weight(prism_b200_executor *ex, const prism_b200_weight *w) {
-  if (!w || w->ex != ex || !w->d_units)
+  if (!w || w->ex != ex || !w->dw.units)
     return ex->fail(PRISM_B200_E_INVALID, "weight does not belong to this executor");
   return PRISM_B200_OK;
+}
+
+cudaError_t project_on(prism_b200_executor *ex, const prism_b200_weight *w, const void *act,
+                       float *y, cudaStream_t s) {
+  return launch_matvec(w->dw, act, y, nullptr, nullptr, kModeOutput, ex->d_status, s, ex->pdl);
 }
 
 }  // namespace
@@ -144,6 +101,9 @@ int prism_b200_executor_create(int device, prism_b200_executor **out) {
   auto *ex = new prism_b200_executor();
   ex->device = device;
   ex->num_sms = prop.multiProcessorCount;
+  // PRISM_B200_PDL=0 turns programmatic dependent launch off (A/B timing)
+  const char *pdl = getenv("PRISM_B200_PDL");
+  ex->pdl = !(pdl && pdl[0] == '0');
   if (cudaStreamCreateWithFlags(&ex->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&ex->d_status, 64) != cudaSuccess ||
       cudaHostAlloc(reinterpret_cast<void **>(&ex->h_status), 64, cudaHostAllocDefault) !=
@@ -153,9 +113,8 @@ int prism_b200_executor_create(int device, prism_b200_executor **out) {
     return PRISM_B200_E_DEVICE;
   }
   char id[512];
-  snprintf(id, sizeof(id),
-           "prism-b200:sm_%d%d:%s:tq2_0+q2_k:q8k-source:tile32-bulk:abi%d", prop.major,
-           prop.minor, prop.name, PRISM_B200_ABI_VERSION);
+  snprintf(id, sizeof(id), "prism-b200:sm_%d%d:%s:tq2_0+q2_k:q8k-source:tiled-bulk:abi%d",
+           prop.major, prop.minor, prop.name, PRISM_B200_ABI_VERSION);
   ex->identity = id;
   *out = ex;
   return PRISM_B200_OK;
@@ -207,8 +166,6 @@ int prism_b200_executor_reset(prism_b200_executor *ex) {
   cudaSetDevice(ex->device);
   CK(cudaDeviceSynchronize(), "device synchronize");
   CK(cudaMemset(ex->d_status, 0, 64), "status reset");
-  for (auto *w : ex->weights)
-    CK(cudaMemset(w->d_cnt, 0, sizeof(unsigned) * (size_t)w->ntiles), "counter reset");
   ex->faulted = false;
   ex->last_error.clear();
   return PRISM_B200_OK;
@@ -222,7 +179,8 @@ int prism_b200_executor_supports(const prism_b200_executor *ex,
 int64_t prism_b200_executor_operation_count(const prism_b200_executor *ex,
                                             const prism_b200_tensor *tensor) {
   if (!prism_b200_executor_supports(ex, tensor)) return -1;
-  int64_t tiles = (int64_t)((tensor->rows + kTileRows - 1) / kTileRows);
+  const int h = choose_tile_height(tensor->kind, tensor->rows, tensor->cols, ex->num_sms);
+  int64_t tiles = (int64_t)((tensor->rows + h - 1) / h);
   return tiles * (int64_t)(tensor->cols / 256);
 }
 
@@ -243,45 +201,46 @@ int prism_b200_weight_upload(prism_b200_executor *ex, const prism_b200_tensor *t
   for (size_t i = 0; i < nblocks; ++i) {
     const uint8_t *blk = src + i * bb;
     if (t->kind == PRISM_B200_KIND_TQ2_0) {
-      if ((blk[65] & 0x7c) == 0x7c) return ex->fail(PRISM_B200_E_NONFINITE, "nonfinite TQ2_0 scale");
-    } else {
-      if ((blk[81] & 0x7c) == 0x7c || (blk[83] & 0x7c) == 0x7c)
-        return ex->fail(PRISM_B200_E_NONFINITE, "nonfinite Q2_K scale");
+      if ((blk[65] & 0x7c) == 0x7c)
+        return ex->fail(PRISM_B200_E_NONFINITE, "nonfinite TQ2_0 scale");
+    } else if ((blk[81] & 0x7c) == 0x7c || (blk[83] & 0x7c) == 0x7c) {
+      return ex->fail(PRISM_B200_E_NONFINITE, "nonfinite Q2_K scale");
     }
   }
   cudaSetDevice(ex->device);
   auto *w = new prism_b200_weight();
   w->ex = ex;
-  w->kind = t->kind;
-  w->rows = t->rows;
-  w->cols = t->cols;
-  w->nb = nb;
-  w->ntiles = (int)((t->rows + kTileRows - 1) / kTileRows);
-  w->unit_bytes = t->kind == PRISM_B200_KIND_TQ2_0 ? kTq2Unit : kQ2kUnit;
-  w->device_bytes = (uint64_t)w->ntiles * nb * w->unit_bytes;
+  DeviceWeight &dw = w->dw;
+  dw.kind = t->kind;
+  dw.rows = t->rows;
+  dw.cols = t->cols;
+  dw.nb = nb;
+  dw.h = choose_tile_height(t->kind, t->rows, t->cols, ex->num_sms);
+  dw.ntiles = (int)((t->rows + dw.h - 1) / dw.h);
+  dw.bytes = (uint64_t)dw.ntiles * nb * unit_bytes((int)t->kind, dw.h);
   uint8_t *d_src = nullptr;
-  size_t src_bytes = nblocks * bb;
-  cudaError_t e = cudaMalloc(&w->d_units, w->device_bytes);
-  if (e == cudaSuccess) e = cudaMalloc(&w->d_partial, (size_t)w->ntiles * nb * kTileRows * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&w->d_cnt, (size_t)w->ntiles * 4);
-  if (e == cudaSuccess) e = cudaMemsetAsync(w->d_cnt, 0, (size_t)w->ntiles * 4, ex->stream);
+  const size_t src_bytes = nblocks * bb;
+  cudaError_t e = configure_weight(dw, ex->num_sms);
+  if (e == cudaSuccess) e = cudaMalloc(&dw.units, dw.bytes);
   if (e == cudaSuccess) e = cudaMalloc(&d_src, src_bytes);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(d_src, src, src_bytes, cudaMemcpyHostToDevice, ex->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(d_src, src, src_bytes, cudaMemcpyHostToDevice, ex->stream);
   if (e == cudaSuccess) {
-    long threads = (long)w->ntiles * nb * kTileRows;
+    long threads = (long)dw.ntiles * nb * dw.h;
     unsigned grid = (unsigned)((threads + 255) / 256);
-    if (t->kind == PRISM_B200_KIND_TQ2_0)
-      repack_kernel<35><<<grid, 256, 0, ex->stream>>>(d_src, (int)t->rows, nb, w->ntiles, w->d_units);
-    else
-      repack_kernel<10><<<grid, 256, 0, ex->stream>>>(d_src, (int)t->rows, nb, w->ntiles, w->d_units);
+    const int rows = (int)t->rows;
+#define PRISM_RP(K, HH)                                                                   \
+  if (dw.kind == K && dw.h == HH)                                                         \
+    repack_kernel<K, HH><<<grid, 256, 0, ex->stream>>>(d_src, rows, nb, dw.ntiles, dw.units);
+    PRISM_RP(35, 32) PRISM_RP(35, 16) PRISM_RP(35, 8)
+    PRISM_RP(10, 32) PRISM_RP(10, 16) PRISM_RP(10, 8)
+#undef PRISM_RP
     e = cudaGetLastError();
   }
   if (e == cudaSuccess) e = cudaStreamSynchronize(ex->stream);
   if (d_src) cudaFree(d_src);
   if (e != cudaSuccess) {
-    if (w->d_units) cudaFree(w->d_units);
-    if (w->d_partial) cudaFree(w->d_partial);
-    if (w->d_cnt) cudaFree(w->d_cnt);
+    if (dw.units) cudaFree(dw.units);
     delete w;
     return cuda_fail(ex, e, "weight upload");
   }
@@ -297,17 +256,15 @@ void prism_b200_weight_release(prism_b200_weight *w) {
     cudaStreamSynchronize(w->ex->stream);
     w->ex->weights.erase(w);
   }
-  if (w->d_units) cudaFree(w->d_units);
-  if (w->d_partial) cudaFree(w->d_partial);
-  if (w->d_cnt) cudaFree(w->d_cnt);
+  if (w->dw.units) cudaFree(w->dw.units);
   delete w;
 }
 
-uint32_t prism_b200_weight_kind(const prism_b200_weight *w) { return w ? w->kind : 0; }
-uint64_t prism_b200_weight_rows(const prism_b200_weight *w) { return w ? w->rows : 0; }
-uint64_t prism_b200_weight_cols(const prism_b200_weight *w) { return w ? w->cols : 0; }
+uint32_t prism_b200_weight_kind(const prism_b200_weight *w) { return w ? w->dw.kind : 0; }
+uint64_t prism_b200_weight_rows(const prism_b200_weight *w) { return w ? w->dw.rows : 0; }
+uint64_t prism_b200_weight_cols(const prism_b200_weight *w) { return w ? w->dw.cols : 0; }
 uint64_t prism_b200_weight_device_bytes(const prism_b200_weight *w) {
-  return w ? w->device_bytes : 0;
+  return w ? w->dw.bytes : 0;
 }
 
 int prism_b200_project_device(prism_b200_executor *ex, const prism_b200_weight *w,
@@ -321,7 +278,7 @@ int prism_b200_project_device(prism_b200_executor *ex, const prism_b200_weight *
   if (reinterpret_cast<uintptr_t>(activation_dev) % 4)
     return ex->fail(PRISM_B200_E_INVALID, "activation must be 4-byte aligned");
   cudaSetDevice(ex->device);
-  CK(launch_matvec(ex, w, activation_dev, out_dev, pick(ex, stream)), "matvec launch");
+  CK(project_on(ex, w, activation_dev, out_dev, pick(ex, stream)), "matvec launch");
   return PRISM_B200_OK;
 }
 
@@ -333,13 +290,14 @@ int prism_b200_project(prism_b200_executor *ex, const prism_b200_weight *w,
   if ((st = validate_weight(ex, w))) return st;
   if (!activation || !out) return ex->fail(PRISM_B200_E_INVALID, "null buffer");
   cudaSetDevice(ex->device);
-  const size_t abytes = (size_t)w->nb * sizeof(prism_b200_q8k_block);
-  const size_t ybytes = (size_t)w->rows * sizeof(float);
+  const size_t abytes = (size_t)w->dw.nb * sizeof(prism_b200_q8k_block);
+  const size_t ybytes = (size_t)w->dw.rows * sizeof(float);
   CK(ex->act.ensure(abytes), "activation buffer");
   CK(ex->y.ensure(ybytes), "output buffer");
   cudaStream_t s = ex->stream;
-  CK(cudaMemcpyAsync(ex->act.ptr, activation, abytes, cudaMemcpyHostToDevice, s), "activation copy");
-  CK(launch_matvec(ex, w, ex->act.ptr, static_cast<float *>(ex->y.ptr), s), "matvec launch");
+  CK(cudaMemcpyAsync(ex->act.ptr, activation, abytes, cudaMemcpyHostToDevice, s),
+     "activation copy");
+  CK(project_on(ex, w, ex->act.ptr, static_cast<float *>(ex->y.ptr), s), "matvec launch");
   CK(cudaMemcpyAsync(out, ex->y.ptr, ybytes, cudaMemcpyDeviceToHost, s), "output copy");
   st = finish(ex, s);
   if (st) memset(out, 0, ybytes);
@@ -355,7 +313,8 @@ int prism_b200_quantize_q8k_device(prism_b200_executor *ex, const float *x_dev, 
   if (reinterpret_cast<uintptr_t>(x_dev) % 16 || reinterpret_cast<uintptr_t>(out_dev) % 4)
     return ex->fail(PRISM_B200_E_INVALID, "misaligned device buffer");
   cudaSetDevice(ex->device);
-  CK(launch_quantize(ex, x_dev, n, pinned, out_dev, pick(ex, stream)), "quantize launch");
+  CK(launch_quantize(x_dev, n, pinned, out_dev, ex->d_status, pick(ex, stream), ex->pdl),
+     "quantize launch");
   return PRISM_B200_OK;
 }
 
@@ -371,7 +330,9 @@ int prism_b200_quantize_q8k(prism_b200_executor *ex, const float *x, size_t n, i
   CK(ex->act.ensure(abytes), "activation buffer");
   cudaStream_t s = ex->stream;
   CK(cudaMemcpyAsync(ex->x.ptr, x, n * 4, cudaMemcpyHostToDevice, s), "input copy");
-  CK(launch_quantize(ex, static_cast<float *>(ex->x.ptr), n, pinned, ex->act.ptr, s), "quantize");
+  CK(launch_quantize(static_cast<float *>(ex->x.ptr), n, pinned, ex->act.ptr, ex->d_status, s,
+                     false),
+     "quantize");
   CK(cudaMemcpyAsync(out, ex->act.ptr, abytes, cudaMemcpyDeviceToHost, s), "output copy");
   st = finish(ex, s);
   if (st) memset(out, 0, abytes);
@@ -384,14 +345,15 @@ int prism_b200_project_f32_group(prism_b200_executor *ex, size_t count,
   int st = check_open(ex);
   if (st) return st;
   if (!count || !weights || !x || !outs) return ex->fail(PRISM_B200_E_INVALID, "empty group");
-  const uint64_t cols = weights[0] ? weights[0]->cols : 0;
+  if ((st = validate_weight(ex, weights[0]))) return st;
+  const uint64_t cols = weights[0]->dw.cols;
   size_t total_rows = 0;
   for (size_t i = 0; i < count; ++i) {
     if ((st = validate_weight(ex, weights[i]))) return st;
-    if (weights[i]->cols != cols)
+    if (weights[i]->dw.cols != cols)
       return ex->fail(PRISM_B200_E_INVALID, "mismatched projection group columns");
     if (!outs[i]) return ex->fail(PRISM_B200_E_INVALID, "null output");
-    total_rows += weights[i]->rows;
+    total_rows += weights[i]->dw.rows;
   }
   cudaSetDevice(ex->device);
   const size_t n = cols;
@@ -401,17 +363,25 @@ int prism_b200_project_f32_group(prism_b200_executor *ex, size_t count,
   CK(ex->y.ensure(total_rows * 4), "output buffer");
   cudaStream_t s = ex->stream;
   CK(cudaMemcpyAsync(ex->x.ptr, x, n * 4, cudaMemcpyHostToDevice, s), "input copy");
-  CK(launch_quantize(ex, static_cast<float *>(ex->x.ptr), n, pinned, ex->act.ptr, s), "quantize");
+  CK(launch_quantize(static_cast<float *>(ex->x.ptr), n, pinned, ex->act.ptr, ex->d_status, s,
+                     false),
+     "quantize");
   size_t off = 0;
   for (size_t i = 0; i < count; ++i) {
     float *y = static_cast<float *>(ex->y.ptr) + off;
-    CK(launch_matvec(ex, weights[i], ex->act.ptr, y, s), "matvec launch");
-    CK(cudaMemcpyAsync(outs[i], y, weights[i]->rows * 4, cudaMemcpyDeviceToHost, s), "output copy");
-    off += weights[i]->rows;
+    CK(project_on(ex, weights[i], ex->act.ptr, y, s), "matvec launch");
+    off += weights[i]->dw.rows;
+  }
+  off = 0;
+  for (size_t i = 0; i < count; ++i) {
+    float *y = static_cast<float *>(ex->y.ptr) + off;
+    CK(cudaMemcpyAsync(outs[i], y, weights[i]->dw.rows * 4, cudaMemcpyDeviceToHost, s),
+       "output copy");
+    off += weights[i]->dw.rows;
   }
   st = finish(ex, s);
   if (st)
-    for (size_t i = 0; i < count; ++i) memset(outs[i], 0, weights[i]->rows * 4);
+    for (size_t i = 0; i < count; ++i) memset(outs[i], 0, weights[i]->dw.rows * 4);
   return st;
 }
 
@@ -428,27 +398,22 @@ int prism_b200_block_dots(prism_b200_executor *ex, const prism_b200_weight *w,
   int st = check_open(ex);
   if (st) return st;
   if ((st = validate_weight(ex, w))) return st;
-  if (!activation || !ints || (w->kind == PRISM_B200_KIND_Q2_K && !ints2))
+  if (!activation || !ints || (w->dw.kind == PRISM_B200_KIND_Q2_K && !ints2))
     return ex->fail(PRISM_B200_E_INVALID, "null buffer");
   cudaSetDevice(ex->device);
-  const size_t abytes = (size_t)w->nb * sizeof(prism_b200_q8k_block);
-  const size_t ibytes = (size_t)w->rows * w->nb * 4;
+  const size_t abytes = (size_t)w->dw.nb * sizeof(prism_b200_q8k_block);
+  const size_t ibytes = (size_t)w->dw.rows * w->dw.nb * 4;
   CK(ex->act.ensure(abytes), "activation buffer");
   CK(ex->ints.ensure(ibytes), "ints buffer");
   CK(ex->ints2.ensure(ibytes), "ints buffer");
   cudaStream_t s = ex->stream;
-  CK(cudaMemcpyAsync(ex->act.ptr, activation, abytes, cudaMemcpyHostToDevice, s), "activation copy");
-  cudaError_t e;
-  if (w->kind == PRISM_B200_KIND_TQ2_0)
-    e = launch_matvec_t<35, kModeInts>(ex, w, ex->act.ptr, nullptr,
-                                       static_cast<int32_t *>(ex->ints.ptr), nullptr, s);
-  else
-    e = launch_matvec_t<10, kModeInts>(ex, w, ex->act.ptr, nullptr,
-                                       static_cast<int32_t *>(ex->ints.ptr),
-                                       static_cast<int32_t *>(ex->ints2.ptr), s);
-  CK(e, "block dots launch");
+  CK(cudaMemcpyAsync(ex->act.ptr, activation, abytes, cudaMemcpyHostToDevice, s),
+     "activation copy");
+  CK(launch_matvec(w->dw, ex->act.ptr, nullptr, static_cast<int32_t *>(ex->ints.ptr),
+                   static_cast<int32_t *>(ex->ints2.ptr), kModeInts, ex->d_status, s, false),
+     "block dots launch");
   CK(cudaMemcpyAsync(ints, ex->ints.ptr, ibytes, cudaMemcpyDeviceToHost, s), "ints copy");
-  if (w->kind == PRISM_B200_KIND_Q2_K)
+  if (w->dw.kind == PRISM_B200_KIND_Q2_K)
     CK(cudaMemcpyAsync(ints2, ex->ints2.ptr, ibytes, cudaMemcpyDeviceToHost, s), "ints copy");
   return finish(ex, s);
 }

@@ -106,6 +106,8 @@ __global__ void __launch_bounds__(256) q8k_quantize_kernel(const float *__restri
                                                            unsigned *status) {
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
+  grid_dependency_wait();  // x may be the previous kernel's output
+  grid_dependents_launch();
   if (warp >= nblocks) return;
   const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)warp * 256 + lane * 8);
   float4 a = src[0], b = src[1];

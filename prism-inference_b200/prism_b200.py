@@ -71,6 +71,8 @@ def load():
         "prism_b200_quantize_q8k": (i32, [vp, vp, sz, i32, vp]),
         "prism_b200_quantize_q8k_device": (i32, [vp, vp, sz, i32, vp, vp]),
         "prism_b200_block_dots": (i32, [vp, vp, vp, vp, vp]),
+        "prism_b200_synth_weights": (i32, [u32, u64, u64, u64, u64, ctypes.c_float,
+                                           ctypes.c_float, vp]),
         "prism_b200_weight_kind": (u32, [vp]),
         "prism_b200_weight_rows": (u64, [vp]),
         "prism_b200_weight_cols": (u64, [vp]),
@@ -91,6 +93,18 @@ def exported_symbols():
     with open(hdr) as f:
         text = f.read()
     return sorted(set(re.findall(r"\b(prism_b200_\w+)\s*\(", text)))
+
+
+def synth_weights(kind, rows, cols, seed, stream=0, scale_lo=0.01, scale_hi=0.05):
+    """Seeded synthetic packed weights (reference byte layout), generated on
+    the host by the library: uint8 array (rows, cols/256*block_bytes)."""
+    bb = BLOCK_BYTES[kind]
+    out = np.empty((rows, cols // 256 * bb), dtype=np.uint8)
+    st = load().prism_b200_synth_weights(kind, rows, cols, seed, stream, scale_lo, scale_hi,
+                                         out.ctypes.data)
+    if st != OK:
+        raise PrismB200Error(st, "invalid synthetic weight request")
+    return out
 
 
 @dataclass

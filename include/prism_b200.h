@@ -173,6 +173,83 @@ int prism_b200_block_dots(prism_b200_executor *ex, const prism_b200_weight *w,
                           const prism_b200_q8k_block *activation,
                           int32_t *ints, int32_t *ints2);
 
+/* ---- Qwen3.5-style hybrid decoder ----------------------------------- */
+/* The reference's Qwen35 graph (reference src/graph.rs:2294 `Qwen35`,
+ * `impl Decoder for Qwen35` src/graph.rs:5392-5580) on the device: every
+ * `full_interval`-th layer is gated full attention over a KV cache, the
+ * others Gated DeltaNet; the output head is tied to token_embd.weight.
+ * Geometry fields mirror the reference's GGUF metadata keys
+ * (src/graph.rs:2966-3056, `qwen35.*`). */
+#define PRISM_B200_KV_F16 0
+#define PRISM_B200_KV_Q8_0 1
+
+typedef struct prism_b200_qwen35_config {
+  uint32_t hidden;          /* qwen35.embedding_length            */
+  uint32_t layers;          /* qwen35.block_count                 */
+  uint32_t heads;           /* qwen35.attention.head_count        */
+  uint32_t kv_heads;        /* qwen35.attention.head_count_kv     */
+  uint32_t head_dim;        /* qwen35.attention.key_length        */
+  uint32_t rope_dim;        /* qwen35.rope.dimension_count        */
+  uint32_t rope_sections[4];/* qwen35.rope.dimension_sections     */
+  float rope_base;          /* qwen35.rope.freq_base              */
+  float eps;                /* qwen35.attention.layer_norm_rms_epsilon */
+  uint32_t ffn;             /* qwen35.feed_forward_length         */
+  uint32_t vocab;           /* rows of token_embd.weight          */
+  uint32_t ssm_state;       /* qwen35.ssm.state_size              */
+  uint32_t ssm_groups;      /* qwen35.ssm.group_count             */
+  uint32_t ssm_values;      /* qwen35.ssm.time_step_rank          */
+  uint32_t conv_kernel;     /* qwen35.ssm.conv_kernel             */
+  uint32_t full_interval;   /* qwen35.full_attention_interval     */
+  uint32_t context;         /* KV capacity in tokens (context_limit) */
+  uint32_t kv_policy;       /* PRISM_B200_KV_F16 or PRISM_B200_KV_Q8_0 */
+  uint32_t weight_kind;     /* PRISM_B200_KIND_TQ2_0 or _Q2_K     */
+} prism_b200_qwen35_config;
+
+typedef struct prism_b200_model prism_b200_model;
+
+int prism_b200_model_create(prism_b200_executor *ex, const prism_b200_qwen35_config *cfg,
+                            prism_b200_model **out);
+void prism_b200_model_destroy(prism_b200_model *m);
+
+/* Bind a tensor by its reference name (src/graph.rs:3112-3238), e.g.
+ * "token_embd.weight", "blk.3.ffn_down.weight".  Packed linear weights use
+ * set_tensor (copied to HBM at once); f32 vectors (norms, ssm_conv1d,
+ * ssm_dt.bias, ssm_a) use set_vector. */
+int prism_b200_model_set_tensor(prism_b200_model *m, const char *name,
+                                const prism_b200_tensor *t);
+int prism_b200_model_set_vector(prism_b200_model *m, const char *name, const float *data,
+                                size_t n);
+
+/* Check every tensor is bound and build the step graphs. */
+int prism_b200_model_finalize(prism_b200_model *m);
+
+/* Clear the KV cache and recurrent state (position 0), as the reference's
+ * Decoder::reset. */
+int prism_b200_model_reset(prism_b200_model *m);
+int64_t prism_b200_model_position(const prism_b200_model *m);
+
+/* One token at the next position (reference Decoder::evaluate_finite_into,
+ * src/graph.rs:5446).  `logits` (host, vocab floats) and `greedy` (the
+ * reference's greedy selection, src/runtime.rs:2630) are optional. */
+int prism_b200_model_evaluate(prism_b200_model *m, uint32_t token, float *logits,
+                              uint32_t *greedy);
+
+/* Ingest `n_prompt` tokens, then greedily generate `n_new` tokens entirely
+ * on the device (reference Runtime::generate loop with greedy sampling,
+ * src/runtime.rs:1944-2031); `out` receives the n_new tokens. */
+int prism_b200_model_generate(prism_b200_model *m, const uint32_t *prompt, size_t n_prompt,
+                              size_t n_new, uint32_t *out);
+
+/* Enqueue `steps` device-driven decode steps on the model's stream without
+ * waiting (each consumes the previous step's greedy token). */
+int prism_b200_model_decode_async(prism_b200_model *m, size_t steps);
+
+/* State readback for parity checks: which = 0 conv history [channels][k-1],
+ * 1 recurrent matrix [values][S][S], 2 keys / 3 values [position][kv*hd]
+ * binary16, 4 hidden [hidden].  Returns the byte count written. */
+int64_t prism_b200_model_read_state(prism_b200_model *m, uint32_t layer, uint32_t which,
+                                    void *out, size_t bytes);
+
 /* ---- synthetic inputs ----------------------------------------------- */
 /* Fill `out` (host, rows*cols/256 blocks in the reference byte layout) with
  * seeded random packed weights: TQ2_0 codes uniform in {-1, 0, +1}, Q2_K

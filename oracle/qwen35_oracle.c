@@ -463,3 +463,15 @@ int po_greedy(const float *logits, size_t n, uint32_t *out) {
   *out = (uint32_t)best;
   return PO_OK;
 }
+
+/* Last layer's scratch activations, for parity debugging:
+ * 5 attended, 6 GDN gate projection, 7 FFN h = up*silu(gate), 8 FFN gate. */
+const float *po_qwen35_scratch(const po_qwen35 *m, int which) {
+  switch (which) {
+    case 5: return m->attended;
+    case 6: return m->zgate;
+    case 7: return m->up;
+    case 8: return m->gate;
+    default: return NULL;
+  }
+}

@@ -75,6 +75,7 @@ const float *po_qwen35_matrix_state(const po_qwen35 *m, int layer);
 const uint16_t *po_qwen35_keys(const po_qwen35 *m, int layer);
 const uint16_t *po_qwen35_values(const po_qwen35 *m, int layer);
 const float *po_qwen35_hidden(const po_qwen35 *m);
+const float *po_qwen35_scratch(const po_qwen35 *m, int which);
 
 /* Greatest finite logit, lowest index on ties (reference src/runtime.rs:2630). */
 int po_greedy(const float *logits, size_t n, uint32_t *out);

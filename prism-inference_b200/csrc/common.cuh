@@ -88,6 +88,22 @@ __device__ __forceinline__ bool is_finite_f(float v) {
   return (__float_as_uint(v) & 0x7f800000u) != 0x7f800000u;
 }
 
+// binary32 transcendentals evaluated in binary64 and rounded once: the
+// correctly rounded result for all but vanishingly rare inputs.  The
+// reference's host libm (expf/logf/sinf/cosf evaluated in binary64
+// internally) returns the same values, so activations feeding the Q8_K
+// quantizer agree bit for bit instead of differing by an ulp, which the
+// quantizer would otherwise amplify into whole-code flips.
+__device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
+__device__ __forceinline__ float log_cr(float x) { return (float)log((double)x); }
+__device__ __forceinline__ float sin_cr(float x) { return (float)sin((double)x); }
+__device__ __forceinline__ float cos_cr(float x) { return (float)cos((double)x); }
+
+// reference src/kernels.rs:3365-3368: silu(v) = v / (1 + exp(-v))
+__device__ __forceinline__ float silu_f(float v) {
+  return __fdiv_rn(v, __fadd_rn(1.0f, exp_cr(-v)));
+}
+
 // ---- byte dot products -----------------------------------------------------
 
 // sum of 4 (unsigned byte of a) * (signed byte of b) + c

@@ -22,81 +22,146 @@ struct DeviceWeight {
   int nb = 0, h = 32, ntiles = 0;
   uint8_t *units = nullptr;
   uint64_t bytes = 0;   // device bytes of the tiled layout
-  int grid = 0;         // persistent CTAs per launch
-  int smem = 0;         // dynamic shared memory per CTA
 };
+
+// The double-buffered tile must also fit the 227 KB shared-memory budget.
+constexpr int kMaxSmem = 232448;
+constexpr int kSmPerSm = 233472;  // shared memory per SM
 
 // Tile height: the largest of 32/16/8 rows that still gives every SM a tile
 // (tiles of 32 rows use one lane per row; 16 and 8 split a row's four
 // 16-byte chunks over 2 or 4 lanes).
-// The double-buffered tile must also fit the 227 KB shared-memory budget.
-constexpr int kMaxSmem = 232448;
 inline int choose_tile_height(uint32_t kind, uint64_t rows, uint64_t cols, int num_sms) {
   int h = 8;
   if ((rows + 31) / 32 >= (uint64_t)2 * num_sms) h = 32;
   else if ((rows + 15) / 16 >= (uint64_t)num_sms) h = 16;
   const int nb = (int)(cols / 256);
-  while (h > 8 && MatvecSmem(nb, h, unit_bytes((int)kind, h)).total() > kMaxSmem) h /= 2;
+  // sized for the up+gate pair (two tiles per buffer), the largest case
+  while (h > 8 && MatvecSmem(nb, h, unit_bytes((int)kind, h), 2 * nb).total() > kMaxSmem) h /= 2;
   return h;
 }
 
-template <int KIND, int H, int MODE>
-inline void *matvec_fn() {
-  return reinterpret_cast<void *>(matvec_kernel<KIND, H, MODE, true>);
+inline int packed_block_bytes(uint32_t kind) {
+  return kind == 35 ? 66 : kind == 10 ? 84 : 0;
 }
 
-inline void *matvec_kernel_ptr(uint32_t kind, int h, int mode) {
-#define PRISM_MV(K, HH)                                                            \
-  if (kind == K && h == HH) return mode == kModeOutput ? matvec_fn<K, HH, kModeOutput>() \
-                                                       : matvec_fn<K, HH, kModeInts>();
-  PRISM_MV(35, 32) PRISM_MV(35, 16) PRISM_MV(35, 8)
-  PRISM_MV(10, 32) PRISM_MV(10, 16) PRISM_MV(10, 8)
-#undef PRISM_MV
-  return nullptr;
-}
-
-// Configure grid and shared memory once per weight (at upload).
-inline cudaError_t configure_weight(DeviceWeight &w, int num_sms) {
-  const int unit = unit_bytes((int)w.kind, w.h);
-  const MatvecSmem L(w.nb, w.h, unit);
-  w.smem = L.total();
-  int max_blocks = 0;
-  for (int mode = 0; mode < 2; ++mode) {
-    void *fn = matvec_kernel_ptr(w.kind, w.h, mode);
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, w.smem);
-    if (e != cudaSuccess) return e;
-    if (mode == 0) {
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&max_blocks, fn, kThreads, w.smem);
-      if (e != cudaSuccess) return e;
+// Every fp16 block scale finite (reference `scale`, src/kernels.rs:152-154).
+inline bool scales_finite(uint32_t kind, const uint8_t *src, size_t nblocks) {
+  const int bb = packed_block_bytes(kind);
+  for (size_t i = 0; i < nblocks; ++i) {
+    const uint8_t *blk = src + i * bb;
+    if (kind == 35) {
+      if ((blk[65] & 0x7c) == 0x7c) return false;
+    } else if ((blk[81] & 0x7c) == 0x7c || (blk[83] & 0x7c) == 0x7c) {
+      return false;
     }
   }
-  if (max_blocks < 1) return cudaErrorInvalidConfiguration;
-  long cap = (long)max_blocks * num_sms;
-  w.grid = (int)(w.ntiles < cap ? w.ntiles : cap);
+  return true;
+}
+
+// Copy reference-layout packed rows to HBM and repack them into the tiled
+// layout (matvec.cuh).  Synchronous on `s`.
+inline cudaError_t upload_tiled(const uint8_t *host, uint32_t kind, uint64_t rows, uint64_t cols,
+                                int num_sms, cudaStream_t s, DeviceWeight &dw) {
+  const int nb = (int)(cols / 256);
+  dw.kind = kind;
+  dw.rows = rows;
+  dw.cols = cols;
+  dw.nb = nb;
+  dw.h = choose_tile_height(kind, rows, cols, num_sms);
+  dw.ntiles = (int)((rows + dw.h - 1) / dw.h);
+  dw.bytes = (uint64_t)dw.ntiles * nb * unit_bytes((int)kind, dw.h);
+  const size_t src_bytes = (size_t)rows * nb * packed_block_bytes(kind);
+  uint8_t *d_src = nullptr;
+  cudaError_t e = cudaMalloc(&dw.units, dw.bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&d_src, src_bytes);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(d_src, host, src_bytes, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) {
+    const long threads = (long)dw.ntiles * nb * dw.h;
+    const unsigned grid = (unsigned)((threads + 255) / 256);
+    const int r = (int)rows;
+#define PRISM_RP(K, HH)                                                               \
+  if (kind == K && dw.h == HH)                                                        \
+    repack_kernel<K, HH><<<grid, 256, 0, s>>>(d_src, r, nb, dw.ntiles, dw.units);
+    PRISM_RP(35, 32) PRISM_RP(35, 16) PRISM_RP(35, 8)
+    PRISM_RP(10, 32) PRISM_RP(10, 16) PRISM_RP(10, 8)
+#undef PRISM_RP
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (d_src) cudaFree(d_src);
+  if (e != cudaSuccess && dw.units) {
+    cudaFree(dw.units);
+    dw.units = nullptr;
+  }
+  return e;
+}
+
+inline MvWeight mv_weight(const DeviceWeight &w, float *y, const float *residual = nullptr) {
+  MvWeight m;
+  m.units = w.units;
+  m.h = w.h;
+  m.ntiles = w.ntiles;
+  m.rows = (int)w.rows;
+  m.y = y;
+  m.residual = residual;
+  return m;
+}
+
+inline void *matvec_kernel_ptr(uint32_t kind, int epi) {
+  if (kind == 35) {
+    if (epi == kEpiStore) return reinterpret_cast<void *>(matvec_kernel<35, kEpiStore>);
+    if (epi == kEpiArgmax) return reinterpret_cast<void *>(matvec_kernel<35, kEpiArgmax>);
+    if (epi == kEpiSwiglu) return reinterpret_cast<void *>(matvec_kernel<35, kEpiSwiglu>);
+    return reinterpret_cast<void *>(matvec_kernel<35, kEpiInts>);
+  }
+  if (epi == kEpiStore) return reinterpret_cast<void *>(matvec_kernel<10, kEpiStore>);
+  if (epi == kEpiArgmax) return reinterpret_cast<void *>(matvec_kernel<10, kEpiArgmax>);
+  if (epi == kEpiSwiglu) return reinterpret_cast<void *>(matvec_kernel<10, kEpiSwiglu>);
+  return reinterpret_cast<void *>(matvec_kernel<10, kEpiInts>);
+}
+
+// Allow the largest dynamic shared memory on every projection variant
+// (once per device).
+inline cudaError_t init_matvec_attributes() {
+  for (uint32_t kind : {35u, 10u})
+    for (int epi = 0; epi < 4; ++epi) {
+      cudaError_t e = cudaFuncSetAttribute(matvec_kernel_ptr(kind, epi),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+      if (e != cudaSuccess) return e;
+    }
   return cudaSuccess;
 }
 
-// Launch one projection.  With `pdl`, the launch may begin while the
+// Launch one projection group.  With `pdl`, the launch may begin while the
 // previous kernel on the stream finishes (programmatic dependent launch):
 // the kernel streams its weights first and waits for the dependency only
 // before reading the activation.
-inline cudaError_t launch_matvec(const DeviceWeight &w, const void *act, float *y,
-                                 int32_t *ints, int32_t *ints2, int mode, unsigned *status,
-                                 cudaStream_t s, bool pdl) {
-  MatvecArgs a;
-  a.w = w.units;
-  a.act = static_cast<const uint8_t *>(act);
-  a.nb = w.nb;
-  a.ntiles = w.ntiles;
-  a.rows = (int)w.rows;
-  a.y = y;
-  a.ints = ints;
-  a.ints2 = ints2;
-  a.status = status;
+inline cudaError_t launch_matvec_group(uint32_t kind, int epi, MvArgs a, int num_sms,
+                                       cudaStream_t s, bool pdl) {
+  int hmax = 8;
+  a.tile_start[0] = 0;
+  for (int g = 0; g < a.count; ++g) {
+    hmax = a.w[g].h > hmax ? a.w[g].h : hmax;
+    a.tile_start[g + 1] = a.tile_start[g] + a.w[g].ntiles;
+  }
+  for (int g = a.count; g < kMaxGroup; ++g) a.tile_start[g + 1] = a.tile_start[a.count];
+  const bool pair = epi == kEpiSwiglu;
+  if (pair && (a.count != 2 || a.w[0].h != a.w[1].h || a.w[0].rows != a.w[1].rows))
+    return cudaErrorInvalidValue;
+  const int upt = pair ? 2 * a.nb : a.nb;
+  const int smem = MatvecSmem(a.nb, hmax, unit_bytes((int)kind, hmax), upt).total();
+  if (smem > kMaxSmem) return cudaErrorInvalidValue;
+  int per_sm = kSmPerSm / (smem + 1024);
+  if (per_sm > 6) per_sm = 6;
+  if (per_sm < 1) per_sm = 1;
+  const int ntiles = pair ? a.w[0].ntiles : a.tile_start[a.count];
+  const long cap = (long)per_sm * num_sms;
+  const int grid = (int)(ntiles < cap ? ntiles : cap);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)w.grid);
+  cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = (size_t)w.smem;
+  cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -104,7 +169,23 @@ inline cudaError_t launch_matvec(const DeviceWeight &w, const void *act, float *
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   void *args[] = {&a};
-  return cudaLaunchKernelExC(&cfg, matvec_kernel_ptr(w.kind, w.h, mode), args);
+  return cudaLaunchKernelExC(&cfg, matvec_kernel_ptr(kind, epi), args);
+}
+
+// Single-weight projection from prepared Q8_K blocks (or block dots).
+inline cudaError_t launch_matvec(const DeviceWeight &w, const void *act, float *y,
+                                 int32_t *ints, int32_t *ints2, int epi, unsigned *status,
+                                 int num_sms, cudaStream_t s, bool pdl) {
+  MvArgs a;
+  a.w[0] = mv_weight(w, y);
+  a.w[0].ints = ints;
+  a.w[0].ints2 = ints2;
+  a.count = 1;
+  a.nb = w.nb;
+  a.prologue = kProQ8K;
+  a.in0 = act;
+  a.status = status;
+  return launch_matvec_group(w.kind, epi, a, num_sms, s, pdl);
 }
 
 inline cudaError_t launch_quantize(const float *x, size_t n, int pinned, void *out,

@@ -1,4 +1,4 @@
-// matvec.cuh -- batch-1 packed ternary / 2-bit projection on sm_100a.
+// matvec.cuh -- batch-1 packed ternary / 2-bit projections on sm_100a.
 //
 // y[r] = sum_b term(r, b): term is the reference's per-block binary32
 // contribution and the sum is the reference's sequential binary32 chain over
@@ -16,15 +16,24 @@
 // layout holds exactly the packed bytes (plus tile padding), so HBM traffic
 // equals the reference's packed size.
 //
-// Execution: persistent CTAs loop over tiles (t = blockIdx.x, += gridDim.x).
-// A tile is streamed into shared memory by 1-D bulk async copies
-// (cp.async.bulk, one mbarrier per unit) two tiles ahead (double buffer), so
-// the next tile's bytes are in flight while the current one is computed.
-// Warp w computes units b = w, w+8, ...: the 32 lanes cover the H rows x 4
-// chunks (L = 32/H lanes per row), weights are lane-private 16-byte shared
-// loads, activations are broadcast 16-byte shared loads, byte products use
-// dp4a and per-row integer partials combine exactly with shuffles.  Terms go
-// to shared memory; then H threads run each row's chain in block order.
+// One launch serves a GROUP of up to four sibling weights that share their
+// input (the reference's project_group_into, src/graph.rs:1869), e.g.
+// attn_qkv + attn_gate + ssm_beta + ssm_alpha.  Persistent CTAs loop over
+// the concatenated tiles (t = blockIdx.x, += gridDim.x).  A tile is streamed
+// into shared memory by 1-D bulk async copies (cp.async.bulk, one mbarrier
+// per unit) two tiles ahead (double buffer).  Warp w computes units
+// b = w, w+8, ...: the 32 lanes cover the H rows x 4 chunks (L = 32/H lanes
+// per row), weights are lane-private 16-byte shared loads, activations are
+// broadcast 16-byte shared loads, byte products use dp4a and per-row integer
+// partials combine exactly with shuffles.  Terms go to shared memory; then
+// H threads run each row's chain in block order.
+//
+// Prologues build the Q8_K activation in shared memory, every CTA the same
+// bytes: from AoS Q8_K blocks, from f32, from RMSNorm(f32) (the reference's
+// normalize-then-prepare, src/kernels.rs:3388-3418 + 463-522), or from
+// SwiGLU(up, gate) (src/graph.rs:121-131).  Epilogues store y, add a
+// residual (src/kernels.rs:2896-2919), or reduce the greedy argmax
+// (src/runtime.rs:2630-2678) with the logits.
 #pragma once
 
 #include "common.cuh"
@@ -34,42 +43,59 @@ namespace prism {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kMaxNb = 64;  // columns <= 16384 per projection
+constexpr int kMaxNb = 64;     // columns <= 16384 per projection
+constexpr int kMaxGroup = 4;   // sibling weights per launch
 
 __host__ __device__ constexpr int unit_bytes(int kind, int h) {
   return (kind == 35 ? 66 : 84) * h;
 }
 
-// Shared-memory layout (dynamic smem), all offsets 16-byte aligned.
+// Shared-memory layout (dynamic smem), all offsets 16-byte aligned.  `h` is
+// the largest tile height in the group (tile buffers are sized for it);
+// `upt` is the units per tile (nb, or 2*nb for the up+gate pair).
 struct MatvecSmem {
-  int nb, h, unit;
-  __host__ __device__ MatvecSmem(int nb_, int h_, int unit_) : nb(nb_), h(h_), unit(unit_) {}
+  int nb, h, unit, upt;
+  __host__ __device__ MatvecSmem(int nb_, int h_, int unit_, int upt_)
+      : nb(nb_), h(h_), unit(unit_), upt(upt_) {}
   __host__ __device__ int act_values() const { return 0; }
   __host__ __device__ int act_scale() const { return nb * 256; }
   __host__ __device__ int act_sums() const { return act_scale() + nb * 4; }
   __host__ __device__ int act_asum() const { return act_sums() + nb * 32; }
-  __host__ __device__ int terms() const { return (act_asum() + nb * 4 + 15) / 16 * 16; }
-  __host__ __device__ int bars() const { return (terms() + nb * h * 4 + 15) / 16 * 16; }
-  __host__ __device__ int bufs() const { return (bars() + 2 * nb * 8 + 127) / 128 * 128; }
-  __host__ __device__ int tile_bytes() const { return nb * unit; }
+  __host__ __device__ int red() const { return (act_asum() + nb * 4 + 15) / 16 * 16; }
+  __host__ __device__ int terms() const { return red() + kWarps * 16; }
+  __host__ __device__ int bars() const { return (terms() + upt * h * 4 + 15) / 16 * 16; }
+  __host__ __device__ int bufs() const { return (bars() + 2 * upt * 8 + 127) / 128 * 128; }
+  __host__ __device__ int tile_bytes() const { return upt * unit; }
   __host__ __device__ int total() const { return bufs() + 2 * tile_bytes(); }
 };
 
-enum MatvecMode : int {
-  kModeOutput = 0,  // y = W x
-  kModeInts = 1,    // exact per-block integer dots to ints / ints2
+enum Prologue : int { kProQ8K = 0, kProF32 = 1, kProRmsNorm = 2 };
+// kEpiSwiglu: w[0] = ffn_up, w[1] = ffn_gate (same geometry); each tile of
+// rows is projected through both and y = up * silu(gate) is stored in
+// w[0].y (reference src/graph.rs:121-131 SwiGLU).
+enum Epilogue : int { kEpiStore = 0, kEpiArgmax = 1, kEpiInts = 2, kEpiSwiglu = 3 };
+
+struct MvWeight {
+  const uint8_t *units = nullptr;
+  int h = 32, ntiles = 0, rows = 0;
+  float *y = nullptr;               // output rows (kEpiStore / kEpiArgmax logits)
+  const float *residual = nullptr;  // y[r] = residual[r] + chain (may alias y)
+  int32_t *ints = nullptr;          // kEpiInts: rows*nb block dots
+  int32_t *ints2 = nullptr;         // kEpiInts, Q2_K min sums
 };
 
-struct MatvecArgs {
-  const uint8_t *w;      // tiled units
-  const uint8_t *act;    // nb AoS Q8_K blocks (4-byte aligned)
-  int nb;                // blocks per row
-  int ntiles;            // H-row tiles
-  int rows;              // true rows
-  float *y;              // rows floats (kModeOutput)
-  int32_t *ints;         // rows*nb (kModeInts)
-  int32_t *ints2;        // rows*nb (kModeInts, Q2_K min sums)
-  unsigned *status;
+struct MvArgs {
+  MvWeight w[kMaxGroup];
+  int count = 1;
+  int nb = 0;
+  int tile_start[kMaxGroup + 1] = {0, 0, 0, 0, 0};
+  int prologue = kProQ8K;
+  const void *in0 = nullptr;        // Q8_K AoS | f32 x | f32 x
+  const float *norm_w = nullptr;    // kProRmsNorm weight
+  float eps = 0.0f;
+  int pinned = 0;                   // pinned Q8_K rounding
+  unsigned long long *argmax_key = nullptr;
+  unsigned *status = nullptr;
 };
 
 __device__ __forceinline__ unsigned byte_of(const uint4 &v, int g) {
@@ -137,7 +163,6 @@ __device__ __forceinline__ int q2k_lane_partial(const uint8_t *unit, const int8_
       acc = dp4a_us(wq.y & m, a.y, acc);
       acc = dp4a_us(wq.z & m, a.z, acc);
       acc = dp4a_us(wq.w & m, a.w, acc);
-      // group g = 8*(c/2) + 2*j + (c%2); c is lane dependent when L > 1
       const int g = 8 * (c >> 1) + 2 * j + (c & 1);
       is += (int)(byte_of(sc, g) & 15u) * (acc >> (2 * j));
     }
@@ -153,10 +178,61 @@ __device__ __forceinline__ int row_allreduce(int v) {
   return v;
 }
 
-// Stage the Q8_K activation (AoS, 4-byte aligned) into shared memory as
-// values[nb][256] | scale[nb] | sums[nb][16] | asum[nb].
-__device__ __forceinline__ void stage_activation(const uint8_t *act, const MatvecSmem &L,
-                                                 uint8_t *smem, unsigned *status) {
+// One unit of one weight: this lane's row gets its block's term and the
+// exact integer dots (dot, dot2 = Q2_K min sum).
+template <int KIND, int H>
+__device__ __forceinline__ void unit_terms(const uint8_t *unit, const int8_t *av, int asum,
+                                           const int16_t *gs, float s, int lane, int &dot,
+                                           int &dot2, float &term) {
+  const int r = lane % H;
+  if (KIND == 35) {
+    dot = row_allreduce<H>(tq2_lane_partial<H>(unit, av, lane)) - asum;
+    dot2 = 0;
+    const float d = half_bits_to_float(reinterpret_cast<const uint16_t *>(unit + 64 * H)[r]);
+    term = __fmul_rn((float)dot, __fmul_rn(d, s));
+  } else {
+    const uint4 sc = reinterpret_cast<const uint4 *>(unit + 64 * H)[r];
+    dot = row_allreduce<H>(q2k_lane_partial<H>(unit, av, sc, lane));
+    int ms = 0;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) ms += (int)gs[g] * (int)(byte_of(sc, g) >> 4);
+    dot2 = ms;
+    const uint16_t *dd = reinterpret_cast<const uint16_t *>(unit + 80 * H);
+    const float d = half_bits_to_float(dd[r]);
+    const float dmin = half_bits_to_float(dd[H + r]);
+    const float t1 = __fmul_rn(__fmul_rn(s, d), (float)dot);
+    const float t2 = __fmul_rn(__fmul_rn(s, dmin), (float)ms);
+    term = __fsub_rn(t1, t2);
+  }
+}
+
+// ---- prologues ----------------------------------------------------------
+
+// Store one quantized block (lane holds q[8] of values 8l..8l+7) into the
+// structure-of-arrays activation layout in shared memory.
+__device__ __forceinline__ void store_q8k_soa(const MatvecSmem &L, uint8_t *smem, int b,
+                                              int lane, float scale, const int8_t (&q)[8],
+                                              int pair_sum) {
+  int8_t *values = reinterpret_cast<int8_t *>(smem + L.act_values()) + b * 256;
+  uint32_t w0 = (uint32_t)(uint8_t)q[0] | ((uint32_t)(uint8_t)q[1] << 8) |
+                ((uint32_t)(uint8_t)q[2] << 16) | ((uint32_t)(uint8_t)q[3] << 24);
+  uint32_t w1 = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) |
+                ((uint32_t)(uint8_t)q[6] << 16) | ((uint32_t)(uint8_t)q[7] << 24);
+  reinterpret_cast<uint2 *>(values)[lane] = make_uint2(w0, w1);
+  if ((lane & 1) == 0)
+    reinterpret_cast<int16_t *>(smem + L.act_sums())[b * 16 + (lane >> 1)] = (int16_t)pair_sum;
+  int tot = pair_sum;
+#pragma unroll
+  for (int off = 2; off < 32; off <<= 1) tot += __shfl_xor_sync(0xffffffffu, tot, off);
+  if (lane == 0) {
+    reinterpret_cast<float *>(smem + L.act_scale())[b] = scale;
+    reinterpret_cast<int *>(smem + L.act_asum())[b] = tot;
+  }
+}
+
+// Stage AoS Q8_K blocks (4-byte aligned) into the SoA layout.
+__device__ __forceinline__ void stage_q8k_aos(const uint8_t *act, const MatvecSmem &L,
+                                              uint8_t *smem, unsigned *status) {
   const int nb = L.nb;
   int8_t *values = reinterpret_cast<int8_t *>(smem + L.act_values());
   float *scale = reinterpret_cast<float *>(smem + L.act_scale());
@@ -176,7 +252,7 @@ __device__ __forceinline__ void stage_activation(const uint8_t *act, const Matve
     }
   }
   __syncthreads();
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int b = warp; b < nb; b += blockDim.x >> 5) {
     const int32_t *vw = reinterpret_cast<const int32_t *>(values + b * 256);
     int s = __dp4a(vw[lane], 0x01010101, 0) + __dp4a(vw[lane + 32], 0x01010101, 0);
@@ -187,31 +263,127 @@ __device__ __forceinline__ void stage_activation(const uint8_t *act, const Matve
       if (!is_finite_f(scale[b])) report(status, kStatusNonfinite);
     }
   }
-  __syncthreads();
 }
 
-// Issue the bulk copies of tile t into buffer `buf` (one mbarrier per unit).
-__device__ __forceinline__ void issue_tile(const uint8_t *w, long t, int nb, int unit,
-                                           uint8_t *buf, uint64_t *bars) {
-  const uint8_t *src = w + t * (long)nb * unit;
+// Sum of squares of x[0..n) in binary64 (reference rms_norm_scale_inner,
+// src/kernels.rs:3823-3878), block-wide, deterministic order.
+__device__ __forceinline__ double block_sumsq_f64(const float *x, int n, double *red) {
+  double s = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = x[i];
+    s += (double)__fmul_rn(v, v);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  double t = 0.0;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+  __syncthreads();
+  return t;
+}
+
+// Build the Q8_K activation in shared memory from an f32 vector:
+//   kProF32:     x
+//   kProRmsNorm: (x * scale) * w, scale = 1/sqrt(mean(x^2) + eps)
+__device__ __forceinline__ void stage_from_f32(const MvArgs &a, const MatvecSmem &L,
+                                               uint8_t *smem) {
+  const int nb = L.nb, n = nb * 256;
+  const float *x = static_cast<const float *>(a.in0);
+  float scale = 1.0f;
+  if (a.prologue == kProRmsNorm) {
+    double *red = reinterpret_cast<double *>(smem + L.red());
+    const double sum = block_sumsq_f64(x, n, red);
+    const float mean = (float)(sum / (double)n);
+    scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+    if (!is_finite_f(scale) || !(scale > 0.0f)) {
+      if (threadIdx.x == 0) report(a.status, kStatusNonfinite);
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int b = warp; b < nb; b += blockDim.x >> 5) {
+    const int base = b * 256 + lane * 8;
+    float v[8];
+    const float4 x0 = *reinterpret_cast<const float4 *>(x + base);
+    const float4 x1 = *reinterpret_cast<const float4 *>(x + base + 4);
+    v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+    v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+    if (a.prologue == kProRmsNorm) {
+      const float4 w0 = *reinterpret_cast<const float4 *>(a.norm_w + base);
+      const float4 w1 = *reinterpret_cast<const float4 *>(a.norm_w + base + 4);
+      const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], scale), w[i]);
+    }
+    float qscale;
+    int8_t q[8];
+    int pair_sum;
+    unsigned st = q8k_quantize_regs(v, lane, a.pinned != 0, qscale, q, pair_sum);
+    if (st && lane == 0) report(a.status, st);
+    store_q8k_soa(L, smem, b, lane, qscale, q, pair_sum);
+  }
+}
+
+// Issue the bulk copies of one tile into buffer `buf` (one mbarrier per unit).
+__device__ __forceinline__ void issue_tile(const uint8_t *src, int nb, int unit, uint8_t *buf,
+                                           uint64_t *bars) {
   for (int b = threadIdx.x; b < nb; b += blockDim.x) {
     mbar_arrive_expect_tx(&bars[b], unit);
     bulk_g2s(buf + b * unit, src + (long)b * unit, unit, &bars[b]);
   }
 }
 
-template <int KIND, int H, int MODE, bool PDL>
-__global__ void __launch_bounds__(kThreads) matvec_kernel(MatvecArgs args) {
-  constexpr int UNIT = unit_bytes(KIND, H);
+__device__ __forceinline__ int group_of(const MvArgs &a, int t) {
+  int g = 0;
+#pragma unroll
+  for (int i = 1; i < kMaxGroup; ++i)
+    if (i < a.count && t >= a.tile_start[i]) g = i;
+  return g;
+}
+
+template <int EPI>
+__device__ __forceinline__ void issue_group_tile(const MvArgs &a, int kind, int t, uint8_t *buf,
+                                                 uint64_t *bars) {
+  if (EPI == kEpiSwiglu) {
+    // units [0, nb) from ffn_up tile t, [nb, 2nb) from ffn_gate tile t
+    const int unit = unit_bytes(kind, a.w[0].h);
+    issue_tile(a.w[0].units + (long)t * a.nb * unit, a.nb, unit, buf, bars);
+    issue_tile(a.w[1].units + (long)t * a.nb * unit, a.nb, unit, buf + a.nb * unit,
+               bars + a.nb);
+    return;
+  }
+  const int g = group_of(a, t);
+  const MvWeight &w = a.w[g];
+  const int unit = unit_bytes(kind, w.h);
+  const int lt = t - a.tile_start[g];
+  issue_tile(w.units + (long)lt * a.nb * unit, a.nb, unit, buf, bars);
+}
+
+// Sortable key of a finite float (larger value -> larger key), with the
+// lowest index winning ties: the reference's greedy selection order.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int index) {
+  unsigned u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (unsigned)index);
+}
+
+template <int KIND, int EPI>
+__global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int nb = args.nb;
-  const MatvecSmem L(nb, H, UNIT);
+  constexpr bool PAIR = EPI == kEpiSwiglu;
+  const int upt = PAIR ? 2 * nb : nb;
+  int hmax = 8;
+  for (int g = 0; g < args.count; ++g) hmax = max(hmax, args.w[g].h);
+  const MatvecSmem L(nb, hmax, unit_bytes(KIND, hmax), upt);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars());  // [2][nb]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars());  // [2][upt]
   uint8_t *bufs = smem + L.bufs();                                  // [2][tile]
-  float *terms = reinterpret_cast<float *>(smem + L.terms());       // [nb][H]
+  float *terms = reinterpret_cast<float *>(smem + L.terms());       // [upt][H]
+  const int ntiles = PAIR ? args.w[0].ntiles : args.tile_start[args.count];
 
-  for (int i = threadIdx.x; i < 2 * nb; i += blockDim.x) {
+  for (int i = threadIdx.x; i < 2 * upt; i += blockDim.x) {
     mbar_init(&bars[i], 1);
     mbar_init_fence();
   }
@@ -219,94 +391,112 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MatvecArgs args) {
   // Weights never depend on the previous kernel: stream the first two tiles
   // before waiting on the grid dependency.
   const int t0 = blockIdx.x;
-  if (t0 < args.ntiles) issue_tile(args.w, t0, nb, UNIT, bufs, bars);
-  if (t0 + (int)gridDim.x < args.ntiles)
-    issue_tile(args.w, t0 + gridDim.x, nb, UNIT, bufs + L.tile_bytes(), bars + nb);
-  if (PDL) grid_dependency_wait();
-  stage_activation(args.act, L, smem, args.status);
-  if (PDL) grid_dependents_launch();
+  if (t0 < ntiles) issue_group_tile<EPI>(args, KIND, t0, bufs, bars);
+  if (t0 + (int)gridDim.x < ntiles)
+    issue_group_tile<EPI>(args, KIND, t0 + gridDim.x, bufs + L.tile_bytes(), bars + upt);
+  grid_dependency_wait();
+  if (args.prologue == kProQ8K)
+    stage_q8k_aos(static_cast<const uint8_t *>(args.in0), L, smem, args.status);
+  else
+    stage_from_f32(args, L, smem);
+  __syncthreads();
+  grid_dependents_launch();
 
   const int8_t *values = reinterpret_cast<const int8_t *>(smem + L.act_values());
   const float *ascale = reinterpret_cast<const float *>(smem + L.act_scale());
   const int16_t *asums = reinterpret_cast<const int16_t *>(smem + L.act_sums());
   const int *aasum = reinterpret_cast<const int *>(smem + L.act_asum());
-  const int r = lane % H;
+  unsigned long long best = 0ull;
 
   bool ok = true;
   int it = 0;
-  for (int t = t0; t < args.ntiles; t += gridDim.x, ++it) {
+  for (int t = t0; t < ntiles; t += gridDim.x, ++it) {
     const int k = it & 1;
     const unsigned parity = (unsigned)(it >> 1) & 1u;
     uint8_t *buf = bufs + k * L.tile_bytes();
-    uint64_t *bk = bars + k * nb;
-    const int row = t * H + r;
-    for (int b = warp; b < nb; b += kWarps) {
-      if (!mbar_wait_bounded(&bk[b], parity, args.status)) {
+    uint64_t *bk = bars + k * upt;
+    const int g = PAIR ? 0 : group_of(args, t);
+    const MvWeight &w = args.w[g];
+    const int H = w.h;
+    const int unit = unit_bytes(KIND, H);
+    const int lt = t - (PAIR ? 0 : args.tile_start[g]);
+    const int r = lane % H;
+    const int row = lt * H + r;
+    for (int u = warp; u < upt; u += kWarps) {
+      if (!mbar_wait_bounded(&bk[u], parity, args.status)) {
         ok = false;
         break;
       }
-      const uint8_t *unit = buf + b * UNIT;
+      const int b = PAIR && u >= nb ? u - nb : u;  // activation block
+      const uint8_t *up = buf + u * unit;
       const int8_t *av = values + b * 256;
-      const float s = ascale[b];
-      int dot, dot2 = 0;
+      int dot, dot2;
       float term;
-      if (KIND == 35) {
-        dot = row_allreduce<H>(tq2_lane_partial<H>(unit, av, lane)) - aasum[b];
-        const float d = half_bits_to_float(reinterpret_cast<const uint16_t *>(unit + 64 * H)[r]);
-        term = __fmul_rn((float)dot, __fmul_rn(d, s));
-      } else {
-        const uint4 sc = reinterpret_cast<const uint4 *>(unit + 64 * H)[r];
-        dot = row_allreduce<H>(q2k_lane_partial<H>(unit, av, sc, lane));
-        const int16_t *gs = asums + b * 16;
-        int ms = 0;
-#pragma unroll
-        for (int g = 0; g < 16; ++g) ms += (int)gs[g] * (int)(byte_of(sc, g) >> 4);
-        dot2 = ms;
-        const uint16_t *dd = reinterpret_cast<const uint16_t *>(unit + 80 * H);
-        const float d = half_bits_to_float(dd[r]);
-        const float dmin = half_bits_to_float(dd[H + r]);
-        const float t1 = __fmul_rn(__fmul_rn(s, d), (float)dot);
-        const float t2 = __fmul_rn(__fmul_rn(s, dmin), (float)ms);
-        term = __fsub_rn(t1, t2);
-      }
+      if (H == 32)
+        unit_terms<KIND, 32>(up, av, aasum[b], asums + b * 16, ascale[b], lane, dot, dot2, term);
+      else if (H == 16)
+        unit_terms<KIND, 16>(up, av, aasum[b], asums + b * 16, ascale[b], lane, dot, dot2, term);
+      else
+        unit_terms<KIND, 8>(up, av, aasum[b], asums + b * 16, ascale[b], lane, dot, dot2, term);
       if (lane < H) {
-        if (MODE == kModeInts) {
-          if (row < args.rows) {
-            args.ints[(size_t)row * nb + b] = dot;
-            if (KIND == 10) args.ints2[(size_t)row * nb + b] = dot2;
+        if (EPI == kEpiInts) {
+          if (row < w.rows) {
+            w.ints[(size_t)row * nb + b] = dot;
+            if (KIND == 10) w.ints2[(size_t)row * nb + b] = dot2;
           }
         } else {
-          terms[b * H + r] = term;
+          terms[u * H + r] = term;
         }
       }
     }
     if (!__syncthreads_and(ok)) break;
-    if (MODE == kModeOutput && threadIdx.x < H) {
+    if (EPI != kEpiInts && threadIdx.x < H) {
       // the reference's chain: sum = 0; sum += term_b for b in order
       float sum = 0.0f;
       for (int b = 0; b < nb; ++b) sum = __fadd_rn(sum, terms[b * H + threadIdx.x]);
-      const int orow = t * H + threadIdx.x;
-      if (orow < args.rows) {
+      const int orow = lt * H + threadIdx.x;
+      if (PAIR) {
+        float gsum = 0.0f;
+        for (int b = nb; b < 2 * nb; ++b) gsum = __fadd_rn(gsum, terms[b * H + threadIdx.x]);
+        if (orow < w.rows) {
+          const float h = __fmul_rn(sum, silu_f(gsum));
+          if (!is_finite_f(sum) || !is_finite_f(gsum)) report(args.status, kStatusNonfinite);
+          w.y[orow] = h;
+        }
+      } else if (orow < w.rows) {
+        if (w.residual) sum = __fadd_rn(w.residual[orow], sum);
         if (!is_finite_f(sum)) report(args.status, kStatusNonfinite);
-        args.y[orow] = sum;
+        if (w.y) w.y[orow] = sum;
+        if (EPI == kEpiArgmax) {
+          const unsigned long long key = argmax_key(sum, orow);
+          best = key > best ? key : best;
+        }
       }
     }
     __syncthreads();
     // refill this buffer with the tile two steps ahead
     const int tn = t + 2 * gridDim.x;
-    if (tn < args.ntiles) {
+    if (tn < ntiles) {
       fence_proxy_async_smem();
-      issue_tile(args.w, tn, nb, UNIT, buf, bk);
+      issue_group_tile<EPI>(args, KIND, tn, buf, bk);
     }
+  }
+  if (EPI == kEpiArgmax) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+      best = o > best ? o : best;
+    }
+    if (lane == 0 && best) atomicMax(args.argmax_key, best);
   }
   if (!ok) {
     // a wait expired: drain every armed copy (bounded) before exiting
     for (int j = 0; j < 2; ++j) {
       const int tj = t0 + (it + j) * gridDim.x;
-      if (tj >= args.ntiles) break;
+      if (tj >= ntiles) break;
       const int kj = (it + j) & 1;
-      for (int b = threadIdx.x; b < nb; b += blockDim.x)
-        mbar_wait_bounded(&bars[kj * nb + b], (unsigned)((it + j) >> 1) & 1u, args.status);
+      for (int u = threadIdx.x; u < upt; u += blockDim.x)
+        mbar_wait_bounded(&bars[kj * upt + u], (unsigned)((it + j) >> 1) & 1u, args.status);
     }
   }
 }

@@ -1,0 +1,678 @@
+// model.cuh -- C ABI of the Qwen3.5-style hybrid decoder on the device.
+//
+// Included once by prism_b200.cu (one translation unit owns every kernel).
+// One decode step is a fixed sequence of launches on the model's stream,
+// captured once into a CUDA graph and replayed per token.  All step state
+// (position, token history, greedy key) lives in device memory, so a graph
+// replay needs no host input and consecutive replays generate greedily
+// without returning to the host.  Launches use programmatic dependent
+// launch, so each projection streams its weights while the previous kernel
+// finishes.
+#pragma once
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "executor.cuh"
+#include "model_kernels.cuh"
+
+namespace prism {
+
+struct ModelLayer {
+  bool full = false;
+  DeviceWeight gate, up, down;
+  DeviceWeight q, k, v, o;                   // full attention
+  DeviceWeight qkv, z, beta, alpha, out;     // Gated DeltaNet
+  float *attn_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+  float *conv_w = nullptr, *dt_bias = nullptr, *ssm_a = nullptr, *ssm_norm = nullptr;
+  float *conv_state = nullptr;   // 2 x [channels][k-1]
+  float *matrix = nullptr;       // [values][S][S]
+  uint16_t *kc = nullptr, *vc = nullptr;  // [context][kv*hd]
+};
+
+}  // namespace prism
+
+struct prism_b200_model {
+  prism_b200_executor *ex = nullptr;
+  prism_b200_qwen35_config cfg{};
+  std::vector<prism::ModelLayer> L;
+  prism::DeviceWeight embd;
+  float *out_norm = nullptr;
+  // activations
+  float *hidden = nullptr, *mixed = nullptr, *zgate = nullptr, *beta = nullptr, *alpha = nullptr;
+  float *attended = nullptr, *projected = nullptr, *key = nullptr, *value = nullptr;
+  float *up = nullptr, *gatef = nullptr, *logits = nullptr;
+  // step state
+  int *d_position = nullptr;
+  uint32_t *d_tokens = nullptr;
+  int *d_prompt_end = nullptr;
+  unsigned long long *d_argmax = nullptr;
+  int64_t position = 0;
+  cudaStream_t stream = nullptr;
+  cudaGraphExec_t g_ingest = nullptr, g_decode = nullptr;
+  std::map<std::string, bool> bound;
+  std::vector<void *> allocations;
+  bool finalized = false;
+
+  int key_width() const { return (int)(cfg.ssm_state * cfg.ssm_groups); }
+  int value_width() const { return (int)(cfg.ssm_state * cfg.ssm_values); }
+  int channels() const { return 2 * key_width() + value_width(); }
+  int kvw() const { return (int)(cfg.kv_heads * cfg.head_dim); }
+  bool is_full(int l) const { return ((l + 1) % (int)cfg.full_interval) == 0; }
+};
+
+namespace prism {
+
+template <typename T>
+cudaError_t model_alloc(prism_b200_model *m, T **p, size_t count) {
+  void *v = nullptr;
+  cudaError_t e = cudaMalloc(&v, count * sizeof(T) < 16 ? 16 : count * sizeof(T));
+  if (e != cudaSuccess) return e;
+  e = cudaMemset(v, 0, count * sizeof(T) < 16 ? 16 : count * sizeof(T));
+  m->allocations.push_back(v);
+  *p = static_cast<T *>(v);
+  return e;
+}
+
+inline cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                     cudaLaunchAttribute *attr, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cfg;
+}
+
+inline StepState step_state(prism_b200_model *m) {
+  StepState st;
+  st.position = m->d_position;
+  st.tokens = m->d_tokens;
+  st.prompt_end = m->d_prompt_end;
+  st.argmax = m->d_argmax;
+  return st;
+}
+
+// Enqueue one decode step.  With `head`, the step ends with the tied LM head,
+// the greedy key and (past the prompt) the next input token.
+inline cudaError_t enqueue_step(prism_b200_model *m, bool head) {
+  prism_b200_executor *ex = m->ex;
+  const auto &c = m->cfg;
+  const bool pdl = ex->pdl;
+  const int sms = ex->num_sms;
+  cudaStream_t s = m->stream;
+  unsigned *status = ex->d_status;
+  cudaLaunchAttribute attr[1];
+  cudaError_t e;
+  {
+    const int n = (int)c.hidden;
+    cudaLaunchConfig_t cfg = pdl_config(dim3((n + 255) / 256), dim3(256), 0, s, attr, pdl);
+    const uint8_t *units = m->embd.units;
+    const int h = m->embd.h, nb = m->embd.nb, vocab = (int)c.vocab;
+    float *hidden = m->hidden;
+    e = c.weight_kind == 35
+            ? cudaLaunchKernelEx(&cfg, embed_kernel<35>, units, h, nb, vocab, step_state(m),
+                                 hidden, n, status)
+            : cudaLaunchKernelEx(&cfg, embed_kernel<10>, units, h, nb, vocab, step_state(m),
+                                 hidden, n, status);
+    if (e != cudaSuccess) return e;
+  }
+  const uint32_t kind = c.weight_kind;
+  for (size_t l = 0; l < m->L.size(); ++l) {
+    ModelLayer &Ly = m->L[l];
+    MvArgs a;
+    a.prologue = kProRmsNorm;
+    a.in0 = m->hidden;
+    a.norm_w = Ly.attn_norm;
+    a.eps = c.eps;
+    a.status = status;
+    a.nb = (int)(c.hidden / 256);
+    if (Ly.full) {
+      a.count = 3;
+      a.w[0] = mv_weight(Ly.q, m->projected);
+      a.w[1] = mv_weight(Ly.k, m->key);
+      a.w[2] = mv_weight(Ly.v, m->value);
+      if ((e = launch_matvec_group(kind, kEpiStore, a, sms, s, pdl)) != cudaSuccess) return e;
+      AttnArgs aa;
+      aa.heads = (int)c.heads;
+      aa.kv_heads = (int)c.kv_heads;
+      aa.hd = (int)c.head_dim;
+      aa.rope_dim = (int)c.rope_dim;
+      for (int j = 0; j < 3; ++j) aa.sections[j] = (int)c.rope_sections[j];
+      aa.eps = c.eps;
+      aa.theta_scale = powf(c.rope_base, -2.0f / (float)c.rope_dim);
+      aa.projected = m->projected;
+      aa.key_in = m->key;
+      aa.value_in = m->value;
+      aa.q_norm = Ly.q_norm;
+      aa.k_norm = Ly.k_norm;
+      aa.kcache = Ly.kc;
+      aa.vcache = Ly.vc;
+      aa.position = m->d_position;
+      aa.attended = m->attended;
+      aa.status = status;
+      const size_t smem = (size_t)(4 * c.head_dim + 64 + c.context + 1) * sizeof(float);
+      cudaLaunchConfig_t cfg =
+          pdl_config(dim3(c.heads), dim3(kAttnThreads), smem, s, attr, pdl);
+      if ((e = cudaLaunchKernelEx(&cfg, attention_decode_kernel, aa)) != cudaSuccess) return e;
+      MvArgs o;
+      o.prologue = kProF32;
+      o.in0 = m->attended;
+      o.status = status;
+      o.nb = (int)(c.heads * c.head_dim / 256);
+      o.count = 1;
+      o.w[0] = mv_weight(Ly.o, m->hidden, m->hidden);
+      if ((e = launch_matvec_group(kind, kEpiStore, o, sms, s, pdl)) != cudaSuccess) return e;
+    } else {
+      a.count = 4;
+      a.w[0] = mv_weight(Ly.qkv, m->mixed);
+      a.w[1] = mv_weight(Ly.z, m->zgate);
+      a.w[2] = mv_weight(Ly.beta, m->beta);
+      a.w[3] = mv_weight(Ly.alpha, m->alpha);
+      if ((e = launch_matvec_group(kind, kEpiStore, a, sms, s, pdl)) != cudaSuccess) return e;
+      GdnArgs g;
+      g.S = (int)c.ssm_state;
+      g.groups = (int)c.ssm_groups;
+      g.values = (int)c.ssm_values;
+      g.conv_k = (int)c.conv_kernel;
+      g.eps = c.eps;
+      g.mixed = m->mixed;
+      g.zgate = m->zgate;
+      g.beta_in = m->beta;
+      g.alpha_in = m->alpha;
+      g.in_stride = g.z_stride = g.ab_stride = 0;
+      g.conv_w = Ly.conv_w;
+      g.dt_bias = Ly.dt_bias;
+      g.ssm_a = Ly.ssm_a;
+      g.norm_w = Ly.ssm_norm;
+      g.conv_state = Ly.conv_state;
+      g.conv_buf_stride = (long)m->channels() * (c.conv_kernel - 1);
+      g.conv_stride = 0;
+      g.state = Ly.matrix;
+      g.state_stride = 0;
+      g.attended = m->attended;
+      g.out_stride = 0;
+      g.position = m->d_position;
+      g.status = status;
+      cudaLaunchConfig_t cfg =
+          pdl_config(dim3(c.ssm_values, 1), dim3(kGdnThreads), 0, s, attr, pdl);
+      if ((e = cudaLaunchKernelEx(&cfg, gdn_decode_kernel, g)) != cudaSuccess) return e;
+      MvArgs o;
+      o.prologue = kProF32;
+      o.in0 = m->attended;
+      o.status = status;
+      o.nb = m->value_width() / 256;
+      o.count = 1;
+      o.w[0] = mv_weight(Ly.out, m->hidden, m->hidden);
+      if ((e = launch_matvec_group(kind, kEpiStore, o, sms, s, pdl)) != cudaSuccess) return e;
+    }
+    MvArgs f;
+    f.prologue = kProRmsNorm;
+    f.in0 = m->hidden;
+    f.norm_w = Ly.post_norm;
+    f.eps = c.eps;
+    f.status = status;
+    f.nb = (int)(c.hidden / 256);
+    f.count = 2;
+    f.w[0] = mv_weight(Ly.up, m->up);  // receives up * silu(gate)
+    f.w[1] = mv_weight(Ly.gate, nullptr);
+    if ((e = launch_matvec_group(kind, kEpiSwiglu, f, sms, s, pdl)) != cudaSuccess) return e;
+    MvArgs d;
+    d.prologue = kProF32;
+    d.in0 = m->up;
+    d.status = status;
+    d.nb = (int)(c.ffn / 256);
+    d.count = 1;
+    d.w[0] = mv_weight(Ly.down, m->hidden, m->hidden);
+    if ((e = launch_matvec_group(kind, kEpiStore, d, sms, s, pdl)) != cudaSuccess) return e;
+  }
+  if (head) {
+    MvArgs h;
+    h.prologue = kProRmsNorm;
+    h.in0 = m->hidden;
+    h.norm_w = m->out_norm;
+    h.eps = c.eps;
+    h.status = status;
+    h.nb = (int)(c.hidden / 256);
+    h.count = 1;
+    h.w[0] = mv_weight(m->embd, m->logits);
+    h.argmax_key = m->d_argmax;
+    if ((e = launch_matvec_group(kind, kEpiArgmax, h, sms, s, pdl)) != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = pdl_config(dim3(1), dim3(32), 0, s, attr, pdl);
+  return cudaLaunchKernelEx(&cfg, finish_step_kernel, step_state(m), head ? 1 : 0);
+}
+
+inline cudaError_t capture_step(prism_b200_model *m, bool head, cudaGraphExec_t *out) {
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return e;
+  cudaError_t e2 = enqueue_step(m, head);
+  e = cudaStreamEndCapture(m->stream, &graph);
+  if (e2 != cudaSuccess) e = e2;
+  if (e == cudaSuccess) e = cudaGraphInstantiate(out, graph, 0);
+  if (graph) cudaGraphDestroy(graph);
+  return e;
+}
+
+// Parse "blk.N.suffix" -> (N, suffix); returns -1 for global names.
+inline int parse_layer(const char *name, std::string &suffix) {
+  std::string s(name);
+  if (s.rfind("blk.", 0) != 0) {
+    suffix = s;
+    return -1;
+  }
+  size_t dot = s.find('.', 4);
+  if (dot == std::string::npos) return -2;
+  int l = atoi(s.substr(4, dot - 4).c_str());
+  suffix = s.substr(dot + 1);
+  return l;
+}
+
+}  // namespace prism
+
+extern "C" {
+
+int prism_b200_model_create(prism_b200_executor *ex, const prism_b200_qwen35_config *cfg,
+                            prism_b200_model **out) {
+  using namespace prism;
+  if (!ex || !cfg || !out) return PRISM_B200_E_INVALID;
+  *out = nullptr;
+  const auto &c = *cfg;
+  const bool ok =
+      c.hidden % 256 == 0 && c.hidden > 0 && c.layers > 0 && c.heads > 0 && c.kv_heads > 0 &&
+      c.heads % c.kv_heads == 0 && c.head_dim == 256 && c.rope_dim <= c.head_dim &&
+      c.rope_dim % 2 == 0 && c.rope_dim <= 64 && c.ffn % 256 == 0 && c.ffn > 0 && c.vocab > 0 &&
+      c.ssm_state == 128 && c.ssm_groups > 0 && c.ssm_values % c.ssm_groups == 0 &&
+      (c.ssm_state * c.ssm_values) % 256 == 0 && c.conv_kernel >= 1 && c.conv_kernel <= 8 &&
+      c.full_interval > 0 && c.context > 0 && c.context <= (1u << 20) && c.eps > 0.0f &&
+      c.rope_base > 0.0f && c.kv_policy == PRISM_B200_KV_F16 &&
+      (c.weight_kind == PRISM_B200_KIND_TQ2_0 || c.weight_kind == PRISM_B200_KIND_Q2_K) &&
+      c.hidden / 256 <= (uint32_t)kMaxNb && c.ffn / 256 <= (uint32_t)kMaxNb &&
+      c.heads * c.head_dim / 256 <= (uint32_t)kMaxNb;
+  if (!ok) return ex->fail(PRISM_B200_E_UNSUPPORTED, "unsupported Qwen35 geometry");
+  cudaSetDevice(ex->device);
+  auto *m = new prism_b200_model();
+  m->ex = ex;
+  m->cfg = c;
+  m->L.resize(c.layers);
+  cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+  const size_t big = std::max<size_t>({c.hidden, c.ffn, (size_t)c.heads * c.head_dim * 2,
+                                       (size_t)m->channels(), (size_t)m->value_width()});
+#define A(p, n) \
+  if (e == cudaSuccess) e = model_alloc(m, &(p), (n))
+  A(m->hidden, c.hidden);
+  A(m->mixed, m->channels());
+  A(m->zgate, m->value_width());
+  A(m->beta, c.ssm_values);
+  A(m->alpha, c.ssm_values);
+  A(m->attended, big);
+  A(m->projected, (size_t)c.heads * c.head_dim * 2);
+  A(m->key, m->kvw());
+  A(m->value, m->kvw());
+  A(m->up, c.ffn);
+  A(m->gatef, c.ffn);
+  A(m->logits, c.vocab);
+  A(m->d_position, 1);
+  A(m->d_tokens, (size_t)c.context + 1);
+  A(m->d_prompt_end, 1);
+  A(m->d_argmax, 1);
+  A(m->out_norm, c.hidden);
+  for (uint32_t l = 0; l < c.layers; ++l) {
+    ModelLayer &Ly = m->L[l];
+    Ly.full = m->is_full((int)l);
+    A(Ly.attn_norm, c.hidden);
+    A(Ly.post_norm, c.hidden);
+    if (Ly.full) {
+      A(Ly.q_norm, c.head_dim);
+      A(Ly.k_norm, c.head_dim);
+      A(Ly.kc, (size_t)c.context * m->kvw());
+      A(Ly.vc, (size_t)c.context * m->kvw());
+    } else {
+      A(Ly.conv_w, (size_t)m->channels() * c.conv_kernel);
+      A(Ly.dt_bias, c.ssm_values);
+      A(Ly.ssm_a, c.ssm_values);
+      A(Ly.ssm_norm, c.ssm_state);
+      A(Ly.conv_state, (size_t)2 * m->channels() * (c.conv_kernel - 1));
+      A(Ly.matrix, (size_t)c.ssm_values * c.ssm_state * c.ssm_state);
+    }
+  }
+#undef A
+  if (e != cudaSuccess) {
+    prism_b200_model_destroy(m);
+    return cuda_fail(ex, e, "model allocation");
+  }
+  *out = m;
+  return PRISM_B200_OK;
+}
+
+void prism_b200_model_destroy(prism_b200_model *m) {
+  if (!m) return;
+  cudaSetDevice(m->ex->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  if (m->g_ingest) cudaGraphExecDestroy(m->g_ingest);
+  if (m->g_decode) cudaGraphExecDestroy(m->g_decode);
+  auto free_w = [](prism::DeviceWeight &w) {
+    if (w.units) cudaFree(w.units);
+    w.units = nullptr;
+  };
+  free_w(m->embd);
+  for (auto &Ly : m->L) {
+    for (auto *w : {&Ly.gate, &Ly.up, &Ly.down, &Ly.q, &Ly.k, &Ly.v, &Ly.o, &Ly.qkv, &Ly.z,
+                    &Ly.beta, &Ly.alpha, &Ly.out})
+      free_w(*w);
+  }
+  for (void *p : m->allocations) cudaFree(p);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+int prism_b200_model_set_tensor(prism_b200_model *m, const char *name,
+                                const prism_b200_tensor *t) {
+  using namespace prism;
+  if (!m || !name || !t || !t->data) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = m->ex;
+  const auto &c = m->cfg;
+  std::string suffix;
+  const int l = parse_layer(name, suffix);
+  DeviceWeight *dst = nullptr;
+  uint64_t rows = 0, cols = 0;
+  if (l == -1 && suffix == "token_embd.weight") {
+    dst = &m->embd;
+    rows = c.vocab;
+    cols = c.hidden;
+  } else if (l >= 0 && l < (int)c.layers) {
+    ModelLayer &Ly = m->L[l];
+    const uint64_t hd = c.head_dim;
+    struct Slot {
+      const char *n;
+      DeviceWeight *w;
+      uint64_t rows, cols;
+      bool full;
+    } slots[] = {
+        {"ffn_gate.weight", &Ly.gate, c.ffn, c.hidden, Ly.full},
+        {"ffn_up.weight", &Ly.up, c.ffn, c.hidden, Ly.full},
+        {"ffn_down.weight", &Ly.down, c.hidden, c.ffn, Ly.full},
+        {"attn_q.weight", &Ly.q, c.heads * hd * 2, c.hidden, true},
+        {"attn_k.weight", &Ly.k, c.kv_heads * hd, c.hidden, true},
+        {"attn_v.weight", &Ly.v, c.kv_heads * hd, c.hidden, true},
+        {"attn_output.weight", &Ly.o, c.hidden, c.heads * hd, true},
+        {"attn_qkv.weight", &Ly.qkv, (uint64_t)m->channels(), c.hidden, false},
+        {"attn_gate.weight", &Ly.z, (uint64_t)m->value_width(), c.hidden, false},
+        {"ssm_beta.weight", &Ly.beta, c.ssm_values, c.hidden, false},
+        {"ssm_alpha.weight", &Ly.alpha, c.ssm_values, c.hidden, false},
+        {"ssm_out.weight", &Ly.out, c.hidden, (uint64_t)m->value_width(), false},
+    };
+    for (auto &sl : slots)
+      if (suffix == sl.n && sl.full == Ly.full) {
+        dst = sl.w;
+        rows = sl.rows;
+        cols = sl.cols;
+      }
+  }
+  if (!dst) return ex->fail(PRISM_B200_E_INVALID, "unknown or misplaced tensor %s", name);
+  if (t->kind != c.weight_kind || t->rows != rows || t->cols != cols)
+    return ex->fail(PRISM_B200_E_INVALID, "tensor %s: kind %u %llux%llu, expected %u %llux%llu",
+                    name, t->kind, (unsigned long long)t->cols, (unsigned long long)t->rows,
+                    c.weight_kind, (unsigned long long)cols, (unsigned long long)rows);
+  const uint8_t *src = static_cast<const uint8_t *>(t->data);
+  if (!scales_finite(t->kind, src, (size_t)rows * (cols / 256)))
+    return ex->fail(PRISM_B200_E_NONFINITE, "tensor %s has a nonfinite block scale", name);
+  cudaSetDevice(ex->device);
+  if (dst->units) cudaFree(dst->units);
+  dst->units = nullptr;
+  cudaError_t e = upload_tiled(src, t->kind, rows, cols, ex->num_sms, m->stream, *dst);
+  if (e != cudaSuccess) return cuda_fail(ex, e, "tensor upload");
+  m->bound[name] = true;
+  m->finalized = false;
+  return PRISM_B200_OK;
+}
+
+int prism_b200_model_set_vector(prism_b200_model *m, const char *name, const float *data,
+                                size_t n) {
+  using namespace prism;
+  if (!m || !name || !data) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = m->ex;
+  const auto &c = m->cfg;
+  std::string suffix;
+  const int l = parse_layer(name, suffix);
+  float *dst = nullptr;
+  size_t want = 0;
+  if (l == -1 && suffix == "output_norm.weight") {
+    dst = m->out_norm;
+    want = c.hidden;
+  } else if (l >= 0 && l < (int)c.layers) {
+    ModelLayer &Ly = m->L[l];
+    struct Slot {
+      const char *n;
+      float *p;
+      size_t size;
+    } slots[] = {
+        {"attn_norm.weight", Ly.attn_norm, c.hidden},
+        {"post_attention_norm.weight", Ly.post_norm, c.hidden},
+        {"attn_q_norm.weight", Ly.q_norm, c.head_dim},
+        {"attn_k_norm.weight", Ly.k_norm, c.head_dim},
+        {"ssm_conv1d.weight", Ly.conv_w, (size_t)m->channels() * c.conv_kernel},
+        {"ssm_dt.bias", Ly.dt_bias, c.ssm_values},
+        {"ssm_a", Ly.ssm_a, c.ssm_values},
+        {"ssm_norm.weight", Ly.ssm_norm, c.ssm_state},
+    };
+    for (auto &sl : slots)
+      if (suffix == sl.n && sl.p) {
+        dst = sl.p;
+        want = sl.size;
+      }
+  }
+  if (!dst) return ex->fail(PRISM_B200_E_INVALID, "unknown or misplaced vector %s", name);
+  if (n != want) return ex->fail(PRISM_B200_E_INVALID, "vector %s has %zu values, expected %zu",
+                                 name, n, want);
+  for (size_t i = 0; i < n; ++i)
+    if (!std::isfinite(data[i]))
+      return ex->fail(PRISM_B200_E_NONFINITE, "vector %s is not finite", name);
+  if (suffix == "ssm_a")
+    for (size_t i = 0; i < n; ++i)
+      if (data[i] > 0.0f)
+        return ex->fail(PRISM_B200_E_INVALID, "recurrent decay ssm_a must be nonpositive");
+  cudaSetDevice(ex->device);
+  cudaError_t e = cudaMemcpy(dst, data, n * sizeof(float), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(ex, e, "vector upload");
+  m->bound[name] = true;
+  return PRISM_B200_OK;
+}
+
+int prism_b200_model_finalize(prism_b200_model *m) {
+  using namespace prism;
+  if (!m) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = m->ex;
+  std::vector<std::string> need = {"token_embd.weight", "output_norm.weight"};
+  for (uint32_t l = 0; l < m->cfg.layers; ++l) {
+    const std::string p = "blk." + std::to_string(l) + ".";
+    for (const char *s : {"attn_norm.weight", "post_attention_norm.weight", "ffn_gate.weight",
+                          "ffn_up.weight", "ffn_down.weight"})
+      need.push_back(p + s);
+    if (m->L[l].full) {
+      for (const char *s : {"attn_q.weight", "attn_k.weight", "attn_v.weight",
+                            "attn_output.weight", "attn_q_norm.weight", "attn_k_norm.weight"})
+        need.push_back(p + s);
+    } else {
+      for (const char *s : {"attn_qkv.weight", "attn_gate.weight", "ssm_beta.weight",
+                            "ssm_alpha.weight", "ssm_out.weight", "ssm_conv1d.weight",
+                            "ssm_dt.bias", "ssm_a", "ssm_norm.weight"})
+        need.push_back(p + s);
+    }
+  }
+  for (auto &n : need)
+    if (!m->bound.count(n)) return ex->fail(PRISM_B200_E_INVALID, "tensor %s is not bound", n.c_str());
+  cudaSetDevice(ex->device);
+  if (m->g_ingest) cudaGraphExecDestroy(m->g_ingest);
+  if (m->g_decode) cudaGraphExecDestroy(m->g_decode);
+  m->g_ingest = m->g_decode = nullptr;
+  cudaError_t e = capture_step(m, false, &m->g_ingest);
+  if (e == cudaSuccess) e = capture_step(m, true, &m->g_decode);
+  if (e != cudaSuccess) return cuda_fail(ex, e, "step graph capture");
+  m->finalized = true;
+  return prism_b200_model_reset(m);
+}
+
+int prism_b200_model_reset(prism_b200_model *m) {
+  using namespace prism;
+  if (!m) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = m->ex;
+  cudaSetDevice(ex->device);
+  const auto &c = m->cfg;
+  cudaStream_t s = m->stream;
+  for (auto &Ly : m->L) {
+    if (Ly.full) {
+      CK(cudaMemsetAsync(Ly.kc, 0, (size_t)c.context * m->kvw() * 2, s), "reset");
+      CK(cudaMemsetAsync(Ly.vc, 0, (size_t)c.context * m->kvw() * 2, s), "reset");
+    } else {
+      CK(cudaMemsetAsync(Ly.conv_state, 0, (size_t)2 * m->channels() * (c.conv_kernel - 1) * 4, s),
+         "reset");
+      CK(cudaMemsetAsync(Ly.matrix, 0, (size_t)c.ssm_values * c.ssm_state * c.ssm_state * 4, s),
+         "reset");
+    }
+  }
+  CK(cudaMemsetAsync(m->d_position, 0, 4, s), "reset");
+  CK(cudaMemsetAsync(m->d_tokens, 0, ((size_t)c.context + 1) * 4, s), "reset");
+  CK(cudaStreamSynchronize(s), "reset");
+  m->position = 0;
+  return PRISM_B200_OK;
+}
+
+int64_t prism_b200_model_position(const prism_b200_model *m) { return m ? m->position : -1; }
+
+static int model_finish(prism_b200_model *m) {
+  prism_b200_executor *ex = m->ex;
+  CK(cudaMemcpyAsync(ex->h_status, ex->d_status, sizeof(unsigned), cudaMemcpyDeviceToHost,
+                     m->stream),
+     "status readback");
+  CK(cudaStreamSynchronize(m->stream), "model step");
+  if (*ex->h_status) {
+    ex->faulted = true;
+    return ex->fail(status_to_code(*ex->h_status), "device reported status 0x%x",
+                    *ex->h_status);
+  }
+  return PRISM_B200_OK;
+}
+
+int prism_b200_model_evaluate(prism_b200_model *m, uint32_t token, float *logits,
+                              uint32_t *greedy) {
+  if (!m) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = m->ex;
+  int st = check_open(ex);
+  if (st) return st;
+  if (!m->finalized) return ex->fail(PRISM_B200_E_INVALID, "model is not finalized");
+  if (token >= m->cfg.vocab || m->position >= (int64_t)m->cfg.context)
+    return ex->fail(PRISM_B200_E_INVALID,
+                    "token is outside the vocabulary or context is exhausted");
+  cudaSetDevice(ex->device);
+  cudaStream_t s = m->stream;
+  const int never = 0x7fffffff;
+  CK(cudaMemcpyAsync(m->d_tokens + m->position, &token, 4, cudaMemcpyHostToDevice, s), "token");
+  CK(cudaMemcpyAsync(m->d_prompt_end, &never, 4, cudaMemcpyHostToDevice, s), "token");
+  CK(cudaGraphLaunch(m->g_decode, s), "decode step");
+  unsigned long long key = 0;
+  CK(cudaMemcpyAsync(&key, m->d_argmax, 8, cudaMemcpyDeviceToHost, s), "greedy");
+  if (logits)
+    CK(cudaMemcpyAsync(logits, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, s),
+       "logits");
+  st = model_finish(m);
+  if (st) {
+    if (logits) memset(logits, 0, (size_t)m->cfg.vocab * 4);
+    return st;
+  }
+  m->position += 1;
+  if (greedy) *greedy = 0xffffffffu - (uint32_t)(key & 0xffffffffull);
+  return PRISM_B200_OK;
+}
+
+int prism_b200_model_decode_async(prism_b200_model *m, size_t steps) {
+  if (!m) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = m->ex;
+  if (!m->finalized) return ex->fail(PRISM_B200_E_INVALID, "model is not finalized");
+  if (m->position + (int64_t)steps > (int64_t)m->cfg.context)
+    return ex->fail(PRISM_B200_E_INVALID, "context is exhausted");
+  cudaSetDevice(ex->device);
+  for (size_t i = 0; i < steps; ++i) CK(cudaGraphLaunch(m->g_decode, m->stream), "decode step");
+  m->position += (int64_t)steps;
+  return PRISM_B200_OK;
+}
+
+int prism_b200_model_generate(prism_b200_model *m, const uint32_t *prompt, size_t n_prompt,
+                              size_t n_new, uint32_t *out) {
+  if (!m) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = m->ex;
+  int st = check_open(ex);
+  if (st) return st;
+  if (!m->finalized) return ex->fail(PRISM_B200_E_INVALID, "model is not finalized");
+  if (!prompt || n_prompt == 0 || (n_new && !out))
+    return ex->fail(PRISM_B200_E_INVALID, "generation needs a prompt");
+  if (m->position + (int64_t)n_prompt + (int64_t)n_new > (int64_t)m->cfg.context)
+    return ex->fail(PRISM_B200_E_INVALID, "context is exhausted");
+  for (size_t i = 0; i < n_prompt; ++i)
+    if (prompt[i] >= m->cfg.vocab)
+      return ex->fail(PRISM_B200_E_INVALID, "prompt token outside the vocabulary");
+  cudaSetDevice(ex->device);
+  cudaStream_t s = m->stream;
+  const int end = (int)(m->position + (int64_t)n_prompt);
+  CK(cudaMemcpyAsync(m->d_tokens + m->position, prompt, n_prompt * 4, cudaMemcpyHostToDevice, s),
+     "prompt");
+  CK(cudaMemcpyAsync(m->d_prompt_end, &end, 4, cudaMemcpyHostToDevice, s), "prompt");
+  for (size_t i = 0; i + 1 < n_prompt; ++i) CK(cudaGraphLaunch(m->g_ingest, s), "ingest step");
+  const size_t decode_steps = n_new ? n_new : 1;
+  for (size_t i = 0; i < decode_steps; ++i) CK(cudaGraphLaunch(m->g_decode, s), "decode step");
+  if (n_new)
+    CK(cudaMemcpyAsync(out, m->d_tokens + end, n_new * 4, cudaMemcpyDeviceToHost, s), "tokens");
+  st = model_finish(m);
+  if (st) return st;
+  m->position += (int64_t)(n_prompt - 1 + decode_steps);
+  return PRISM_B200_OK;
+}
+
+int64_t prism_b200_model_read_state(prism_b200_model *m, uint32_t layer, uint32_t which,
+                                    void *out, size_t bytes) {
+  if (!m || !out) return -PRISM_B200_E_INVALID;
+  const auto &c = m->cfg;
+  const void *src = nullptr;
+  size_t n = 0;
+  if (which == 4) {
+    src = m->hidden;
+    n = (size_t)c.hidden * 4;
+  } else if (which >= 5 && which <= 9) {
+    // the last layer's activations: 5 attended, 6 gate projection (GDN),
+    // 7 ffn up projection, 8 ffn gate projection, 9 logits
+    const size_t sizes[5] = {(size_t)std::max(m->value_width(), (int)(c.heads * c.head_dim)),
+                             (size_t)m->value_width(), c.ffn, c.ffn, c.vocab};
+    const void *ptrs[5] = {m->attended, m->zgate, m->up, m->gatef, m->logits};
+    src = ptrs[which - 5];
+    n = sizes[which - 5] * 4;
+  } else if (layer < c.layers) {
+    const prism::ModelLayer &Ly = m->L[layer];
+    const size_t hist = (size_t)m->channels() * (c.conv_kernel - 1);
+    if (which == 0 && !Ly.full) {
+      // the buffer written by the last step: parity of the current position
+      src = Ly.conv_state + (m->position & 1) * hist;
+      n = hist * 4;
+    } else if (which == 1 && !Ly.full) {
+      src = Ly.matrix;
+      n = (size_t)c.ssm_values * c.ssm_state * c.ssm_state * 4;
+    } else if ((which == 2 || which == 3) && Ly.full) {
+      src = which == 2 ? Ly.kc : Ly.vc;
+      n = (size_t)m->position * m->kvw() * 2;
+    }
+  }
+  if (!src) return -PRISM_B200_E_INVALID;
+  if (bytes < n) return -PRISM_B200_E_INVALID;
+  cudaSetDevice(m->ex->device);
+  if (cudaMemcpyAsync(out, src, n, cudaMemcpyDeviceToHost, m->stream) != cudaSuccess ||
+      cudaStreamSynchronize(m->stream) != cudaSuccess)
+    return -PRISM_B200_E_DEVICE;
+  return (int64_t)n;
+}
+
+}  // extern "C"

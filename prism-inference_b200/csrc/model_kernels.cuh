@@ -1,0 +1,415 @@
+// model_kernels.cuh -- decode-step kernels of the Qwen3.5-style hybrid model.
+//
+// Arithmetic follows the reference's Source contract: binary32 products,
+// binary64 accumulation where the reference sums in binary64 (float_dot,
+// f16_dot, RMS and L2 sums, softmax totals, value sums), separate multiply
+// and add.  Parallel binary64 reductions reorder the sums; their binary32
+// roundings agree with the reference's sequential sums except in rare
+// boundary cases.  Transcendentals (exp, log, sin, cos, pow) are CUDA's,
+// within a few ulp of the host libm the reference uses.
+#pragma once
+
+#include "common.cuh"
+#include "matvec.cuh"
+
+namespace prism {
+
+// ---- small helpers ---------------------------------------------------------
+
+__device__ __forceinline__ double warp_sum_f64(double v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max_f32(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+
+// Block-wide binary64 sum (all threads call; red has >= warps doubles).
+__device__ __forceinline__ double block_sum_f64(double v, double *red) {
+  v = warp_sum_f64(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+  return t;
+}
+
+__device__ __forceinline__ float block_max_f32(float v, float *red) {
+  v = warp_max_f32(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) t = fmaxf(t, red[w]);
+  return t;
+}
+
+__device__ __forceinline__ float sigmoid_f(float v) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cr(-v)));
+}
+
+// reference src/graph.rs:6357-6384 recurrent_decay
+__device__ __forceinline__ float recurrent_decay_f(float alpha, float time_bias, float a,
+                                                   unsigned *status) {
+  if (!is_finite_f(alpha) || !is_finite_f(time_bias) || !is_finite_f(a) || a > 0.0f) {
+    report(status, kStatusNonfinite);
+    return 0.0f;
+  }
+  if (a == 0.0f) return 1.0f;
+  const float linear = __fadd_rn(alpha, time_bias);
+  if (linear >= 88.0f) {
+    if (!is_finite_f(linear)) return 0.0f;
+    return exp_cr(__fmul_rn(linear, a));
+  }
+  const float softplus = linear > 20.0f ? linear : log_cr(__fadd_rn(1.0f, exp_cr(linear)));
+  return exp_cr(__fmul_rn(softplus, a));
+}
+
+// ---- embedding row ---------------------------------------------------------
+
+// Decode row `token` of a tiled TQ2_0 / Q2_K weight (the tied embedding):
+// reference src/kernels/tquants.rs:258-268 / src/kernels/kquants.rs:146-160.
+// Element i of a block: byte (i/128)*32 + i%32, shift 2*((i%128)/32).
+template <int KIND>
+__device__ __forceinline__ float decode_tiled(const uint8_t *units, int h, int nb, int row,
+                                              int i) {
+  const int t = row / h, r = row % h, b = i >> 8, e = i & 255;
+  const uint8_t *unit = units + ((long)t * nb + b) * unit_bytes(KIND, h);
+  const int byte = (e >> 7) * 32 + (e & 31), shift = 2 * ((e & 127) >> 5);
+  const int c = byte >> 4, off = byte & 15;
+  const int code = (unit[(c * h + r) * 16 + off] >> shift) & 3;
+  if (KIND == 35) {
+    const float d = half_bits_to_float(reinterpret_cast<const uint16_t *>(unit + 64 * h)[r]);
+    return __fmul_rn((float)(code - 1), d);
+  }
+  const uint8_t sc = unit[64 * h + r * 16 + (e >> 4)];
+  const uint16_t *dd = reinterpret_cast<const uint16_t *>(unit + 80 * h);
+  const float d = half_bits_to_float(dd[r]), dmin = half_bits_to_float(dd[h + r]);
+  const float t1 = __fmul_rn(__fmul_rn(d, (float)(sc & 15)), (float)code);
+  return __fsub_rn(t1, __fmul_rn(dmin, (float)(sc >> 4)));
+}
+
+struct StepState {
+  int *position;                 // tokens processed so far
+  uint32_t *tokens;              // [context + 1] token per position
+  int *prompt_end;               // first position produced by greedy selection
+  unsigned long long *argmax;    // greedy key of the current step
+};
+
+template <int KIND>
+__global__ void embed_kernel(const uint8_t *units, int h, int nb, int vocab, StepState st,
+                             float *hidden, int n, unsigned *status) {
+  grid_dependency_wait();
+  grid_dependents_launch();
+  const int pos = *st.position;
+  const uint32_t token = st.tokens[pos];
+  if (blockIdx.x == 0 && threadIdx.x == 0) *st.argmax = 0ull;
+  if (token >= (uint32_t)vocab) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) report(status, kStatusInvalid);
+    return;
+  }
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    hidden[i] = decode_tiled<KIND>(units, h, nb, (int)token, i);
+}
+
+// Advance the position; past the prompt, the greedy token becomes the next
+// input (reference src/runtime.rs:1944-2031 generate loop, greedy selection).
+__global__ void finish_step_kernel(StepState st, int write_greedy) {
+  grid_dependency_wait();
+  if (threadIdx.x != 0) return;
+  const int pos = *st.position + 1;
+  if (write_greedy && pos >= *st.prompt_end) {
+    const unsigned long long key = *st.argmax;
+    st.tokens[pos] = 0xffffffffu - (unsigned)(key & 0xffffffffull);
+  }
+  *st.position = pos;
+}
+
+// ---- Gated DeltaNet decode step ------------------------------------------
+
+struct GdnArgs {
+  int S;             // state size (key dim = value dim per head)
+  int groups;        // key heads
+  int values;        // value heads
+  int conv_k;        // convolution kernel (history = conv_k - 1)
+  float eps;
+  // per-sequence inputs (batch stride in elements)
+  const float *mixed;      // [conv channels] qkv projection, before conv
+  const float *zgate;      // [values*S]
+  const float *beta_in;    // [values]
+  const float *alpha_in;   // [values]
+  long in_stride, z_stride, ab_stride;
+  const float *conv_w;     // [channels][conv_k]
+  const float *dt_bias, *ssm_a, *norm_w;
+  float *conv_state;       // two buffers of [batch][channels][conv_k-1], by position parity
+  long conv_buf_stride;    // elements between the two buffers
+  long conv_stride;        // per sequence
+  float *state;            // [batch][values][S][S], updated in place
+  long state_stride;
+  float *attended;         // [batch][values*S]
+  long out_stride;
+  const int *position;     // selects the conv-state buffer (nullptr: buffer 0 -> 1)
+  unsigned *status;
+};
+
+// One CTA per (value head, sequence); 512 threads; S == 128.
+// reference src/graph.rs:5029-5181 (conv, SiLU, L2 of q/k) and
+// src/graph.rs:5191-5343 with gdn_step_row_from (src/graph.rs:801-822).
+constexpr int kGdnThreads = 512;
+
+__global__ void __launch_bounds__(kGdnThreads) gdn_decode_kernel(GdnArgs a) {
+  constexpr int S = 128;
+  __shared__ __align__(16) float q[S], k[S], v[S], o[S];
+  __shared__ double red[kGdnThreads / 32];
+  __shared__ float sdecay, sbeta;
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int kh = h % a.groups;
+  const int kw = a.groups * S;
+  const int hist = a.conv_k - 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  grid_dependency_wait();
+  grid_dependents_launch();
+  const float *mixed = a.mixed + b * a.in_stride;
+  const int parity = a.position ? (*a.position & 1) : 0;
+  const float *hist_in = a.conv_state + parity * a.conv_buf_stride + b * a.conv_stride;
+  float *hist_out = a.conv_state + (parity ^ 1) * a.conv_buf_stride + b * a.conv_stride;
+
+  // 1. depthwise causal convolution + SiLU of this head's q, k, v channels
+  if (threadIdx.x < 3 * S) {
+    const int part = threadIdx.x / S, j = threadIdx.x % S;
+    const int ch = part == 0 ? kh * S + j : part == 1 ? kw + kh * S + j : 2 * kw + h * S + j;
+    const float projected = mixed[ch];
+    const float *hj = hist_in + (long)ch * hist;
+    const float *cj = a.conv_w + (long)ch * a.conv_k;
+    float sum = 0.0f;
+    for (int i = 0; i < hist; ++i) sum = __fadd_rn(sum, __fmul_rn(hj[i], cj[i]));
+    sum = __fadd_rn(sum, __fmul_rn(projected, cj[hist]));
+    const float act = silu_f(sum);
+    (part == 0 ? q : part == 1 ? k : v)[j] = act;
+    // the history of shared q/k channels is written by their first value head
+    if (part == 2 || h == kh) {
+      float *nj = hist_out + (long)ch * hist;
+      for (int i = 0; i + 1 < hist; ++i) nj[i] = hj[i + 1];
+      if (hist > 0) nj[hist - 1] = projected;
+    }
+  }
+  if (threadIdx.x == 0) {
+    sdecay = recurrent_decay_f(a.alpha_in[b * a.ab_stride + h], a.dt_bias[h], a.ssm_a[h],
+                               a.status);
+    sbeta = sigmoid_f(a.beta_in[b * a.ab_stride + h]);
+  }
+  __syncthreads();
+  // 2. L2 normalisation of q and k (reference src/kernels.rs:3333-3352)
+  {
+    const float xq = threadIdx.x < S ? q[threadIdx.x] : 0.0f;
+    const float xk = threadIdx.x < S ? k[threadIdx.x] : 0.0f;
+    const double sq = block_sum_f64(threadIdx.x < S ? (double)__fmul_rn(xq, xq) : 0.0, red);
+    const double sk = block_sum_f64(threadIdx.x < S ? (double)__fmul_rn(xk, xk) : 0.0, red);
+    const float scq = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sq), a.eps));
+    const float sck = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sk), a.eps));
+    __syncthreads();
+    if (threadIdx.x < S) {
+      q[threadIdx.x] = __fmul_rn(xq, scq);
+      k[threadIdx.x] = __fmul_rn(xk, sck);
+    }
+  }
+  __syncthreads();
+  // 3. state rows: S = decay*prev; dk = S.k; delta = (v-dk)*beta;
+  //    S += delta*k; o = (S.q)/sqrt(S)
+  const float decay = sdecay, beta = sbeta;
+  const float oscale = __fdiv_rn(1.0f, __fsqrt_rn((float)S));
+  const float4 kk = reinterpret_cast<const float4 *>(k)[lane];
+  const float4 qq = reinterpret_cast<const float4 *>(q)[lane];
+  float *state = a.state + b * a.state_stride + (long)h * S * S;
+  constexpr int RPW = S / (kGdnThreads / 32);  // rows per warp (8)
+  float4 srow[RPW];
+#pragma unroll
+  for (int i = 0; i < RPW; ++i)
+    srow[i] = reinterpret_cast<const float4 *>(state + (long)(warp * RPW + i) * S)[lane];
+  bool finite = true;
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const int r = warp * RPW + i;
+    float4 s = srow[i];
+    s.x = __fmul_rn(decay, s.x);
+    s.y = __fmul_rn(decay, s.y);
+    s.z = __fmul_rn(decay, s.z);
+    s.w = __fmul_rn(decay, s.w);
+    double dk = (double)__fmul_rn(s.x, kk.x) + (double)__fmul_rn(s.y, kk.y) +
+                (double)__fmul_rn(s.z, kk.z) + (double)__fmul_rn(s.w, kk.w);
+    dk = warp_sum_f64(dk);
+    const float delta = __fmul_rn(__fsub_rn(v[r], (float)dk), beta);
+    s.x = __fadd_rn(s.x, __fmul_rn(delta, kk.x));
+    s.y = __fadd_rn(s.y, __fmul_rn(delta, kk.y));
+    s.z = __fadd_rn(s.z, __fmul_rn(delta, kk.z));
+    s.w = __fadd_rn(s.w, __fmul_rn(delta, kk.w));
+    finite &= is_finite_f(s.x) && is_finite_f(s.y) && is_finite_f(s.z) && is_finite_f(s.w);
+    double dq = (double)__fmul_rn(s.x, qq.x) + (double)__fmul_rn(s.y, qq.y) +
+                (double)__fmul_rn(s.z, qq.z) + (double)__fmul_rn(s.w, qq.w);
+    dq = warp_sum_f64(dq);
+    reinterpret_cast<float4 *>(state + (long)r * S)[lane] = s;
+    if (lane == 0) o[r] = __fmul_rn((float)dq, oscale);
+  }
+  if (!__all_sync(0xffffffffu, finite) && lane == 0) report(a.status, kStatusNonfinite);
+  __syncthreads();
+  // 4. RMSNorm(o) * w * SiLU(z) (reference src/kernels.rs:3589-3625, Source)
+  const float ov = threadIdx.x < S ? o[threadIdx.x] : 0.0f;
+  const double ss = block_sum_f64(threadIdx.x < S ? (double)__fmul_rn(ov, ov) : 0.0, red);
+  const float mean = (float)(ss / (double)S);
+  const float nscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+  if (threadIdx.x < S) {
+    const float z = a.zgate[b * a.z_stride + h * S + threadIdx.x];
+    const float normed = __fmul_rn(__fmul_rn(ov, nscale), a.norm_w[threadIdx.x]);
+    a.attended[b * a.out_stride + h * S + threadIdx.x] = __fmul_rn(normed, silu_f(z));
+  }
+}
+
+// ---- gated full attention over a binary16 KV cache -------------------------
+
+struct AttnArgs {
+  int heads, kv_heads, hd, rope_dim;
+  int sections[3];          // mRoPE sections (text positions: t, h, w equal)
+  float eps, theta_scale;
+  const float *projected;   // [heads][2][hd]: query then gate per head
+  const float *key_in;      // [kv_heads*hd]
+  const float *value_in;    // [kv_heads*hd]
+  const float *q_norm, *k_norm;
+  uint16_t *kcache, *vcache;  // [context][kv_heads*hd] binary16 bits
+  const int *position;
+  float *attended;          // [heads*hd]
+  unsigned *status;
+};
+
+constexpr int kAttnThreads = 256;
+
+// RMSNorm(x)*w, RoPE on the first rope_dim dims, binary16 rounding
+// (reference src/kernels.rs:3679-3750, Source).  One value per thread
+// (hd == blockDim.x); cs holds the (cos, sin) pairs.
+__device__ __forceinline__ float norm_rope_round(const float *x, const float *w, float eps,
+                                                 int hd, int rope, const float *cs, float *buf,
+                                                 double *red) {
+  const int i = threadIdx.x;
+  const float xi = x[i];
+  const double ss = block_sum_f64((double)__fmul_rn(xi, xi), red);
+  const float mean = (float)(ss / (double)hd);
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  buf[i] = __fmul_rn(__fmul_rn(xi, scale), w[i]);
+  __syncthreads();
+  float out = buf[i];
+  const int half = rope / 2;
+  if (i < half) {
+    const float first = buf[i], second = buf[i + half];
+    out = __fsub_rn(__fmul_rn(first, cs[2 * i]), __fmul_rn(second, cs[2 * i + 1]));
+  } else if (i < rope) {
+    const int j = i - half;
+    const float first = buf[j], second = buf[i];
+    out = __fadd_rn(__fmul_rn(first, cs[2 * j + 1]), __fmul_rn(second, cs[2 * j]));
+  }
+  __syncthreads();
+  return round_f16(out);
+}
+
+// One CTA per query head; hd == 256 == blockDim.x.  Scores over the cached
+// positions use binary16 keys (reference f16_dot), the current position the
+// binary32 rounded key (float_dot); softmax_round_f16; binary64 value sums;
+// sigmoid gate (reference src/graph.rs:4470-4950).
+__global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  const int hd = a.hd;
+  float *q = sm;                 // [hd]
+  float *kc = q + hd;            // [hd]
+  float *vc = kc + hd;           // [hd]
+  float *buf = vc + hd;          // [hd]
+  float *cs = buf + hd;          // [rope]
+  float *scores = cs + 64;       // [pos+1]
+  __shared__ double red[kAttnThreads / 32];
+  __shared__ float fred[kAttnThreads / 32];
+  const int h = blockIdx.x;
+  const int group = a.heads / a.kv_heads;
+  const int kvh = h / group;
+  const int kvw = a.kv_heads * hd;
+  const int i = threadIdx.x;
+  const int warp = i >> 5, lane = i & 31;
+  grid_dependency_wait();
+  grid_dependents_launch();
+  const int pos = *a.position;
+  if (i == 0) {
+    // reference src/graph.rs:6406-6437: angles p * theta_scale^i by repeated
+    // binary32 multiplication; text positions give the three sections the
+    // same angle, and indices past 3*section use the fourth (zero) position
+    float theta = (float)pos;
+    for (int j = 0; j < a.rope_dim / 2; ++j) {
+      const float angle = j < 3 * a.sections[j % 3] ? theta : 0.0f;
+      cs[2 * j] = cos_cr(angle);
+      cs[2 * j + 1] = sin_cr(angle);
+      theta = __fmul_rn(theta, a.theta_scale);
+    }
+  }
+  __syncthreads();
+  q[i] = norm_rope_round(a.projected + (long)h * 2 * hd, a.q_norm, a.eps, hd, a.rope_dim, cs,
+                         buf, red);
+  kc[i] = norm_rope_round(a.key_in + (long)kvh * hd, a.k_norm, a.eps, hd, a.rope_dim, cs, buf,
+                          red);
+  vc[i] = round_f16(a.value_in[kvh * hd + i]);
+  if (h % group == 0) {
+    a.kcache[(long)pos * kvw + kvh * hd + i] = float_to_half_bits(kc[i]);
+    a.vcache[(long)pos * kvw + kvh * hd + i] = float_to_half_bits(vc[i]);
+  }
+  __syncthreads();
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+  // scores: warp per position, lane owns 8 dims (one 16-byte key load)
+  const float4 q0 = reinterpret_cast<const float4 *>(q)[lane * 2];
+  const float4 q1 = reinterpret_cast<const float4 *>(q)[lane * 2 + 1];
+  for (int p = warp; p < pos; p += kAttnThreads / 32) {
+    const uint4 kv = *reinterpret_cast<const uint4 *>(a.kcache + (long)p * kvw + kvh * hd + lane * 8);
+    const uint16_t *kh = reinterpret_cast<const uint16_t *>(&kv);
+    double s = (double)__fmul_rn(q0.x, half_bits_to_float(kh[0])) +
+               (double)__fmul_rn(q0.y, half_bits_to_float(kh[1])) +
+               (double)__fmul_rn(q0.z, half_bits_to_float(kh[2])) +
+               (double)__fmul_rn(q0.w, half_bits_to_float(kh[3])) +
+               (double)__fmul_rn(q1.x, half_bits_to_float(kh[4])) +
+               (double)__fmul_rn(q1.y, half_bits_to_float(kh[5])) +
+               (double)__fmul_rn(q1.z, half_bits_to_float(kh[6])) +
+               (double)__fmul_rn(q1.w, half_bits_to_float(kh[7]));
+    s = warp_sum_f64(s);
+    if (lane == 0) scores[p] = __fmul_rn((float)s, scale);
+  }
+  {
+    const double s = block_sum_f64((double)__fmul_rn(q[i], kc[i]), red);
+    if (i == 0) scores[pos] = __fmul_rn((float)s, scale);
+  }
+  __syncthreads();
+  // softmax_round_f16 (reference src/kernels.rs:4431-4466)
+  float m = -INFINITY;
+  for (int p = i; p <= pos; p += kAttnThreads) m = fmaxf(m, scores[p]);
+  m = block_max_f32(m, fred);
+  double tot = 0.0;
+  for (int p = i; p <= pos; p += kAttnThreads) {
+    const float e = exp_cr(__fsub_rn(scores[p], m));
+    scores[p] = e;
+    tot += (double)e;
+  }
+  tot = block_sum_f64(tot, red);
+  const float inv = (float)(1.0 / tot);
+  if (!is_finite_f(m) && i == 0) report(a.status, kStatusNonfinite);
+  __syncthreads();
+  for (int p = i; p <= pos; p += kAttnThreads) scores[p] = round_f16(__fmul_rn(scores[p], inv));
+  __syncthreads();
+  // values: one dimension per thread, binary64 sum in position order
+  double acc = -0.0;
+  const uint16_t *vcol = a.vcache + kvh * hd + i;
+  for (int p = 0; p < pos; ++p)
+    acc += (double)__fmul_rn(scores[p], half_bits_to_float(vcol[(long)p * kvw]));
+  const float out = (float)(acc + (double)__fmul_rn(scores[pos], vc[i]));
+  const float g = a.projected[(long)(2 * h + 1) * hd + i];
+  a.attended[(long)h * hd + i] = __fmul_rn(out, sigmoid_f(g));
+}
+
+}  // namespace prism

@@ -6,6 +6,8 @@
 // kernels on the executor's stream, and for host-pointer variants waits
 // and reads the device status word.  There is no CPU fallback: when a
 // kernel cannot run, the call fails.
+#include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <vector>
 
@@ -81,7 +83,8 @@ int validate_weight(prism_b200_executor *ex, const prism_b200_weight *w) {
 
 cudaError_t project_on(prism_b200_executor *ex, const prism_b200_weight *w, const void *act,
                        float *y, cudaStream_t s) {
-  return launch_matvec(w->dw, act, y, nullptr, nullptr, kModeOutput, ex->d_status, s, ex->pdl);
+  return launch_matvec(w->dw, act, y, nullptr, nullptr, kEpiStore, ex->d_status, ex->num_sms, s,
+                       ex->pdl);
 }
 
 }  // namespace
@@ -104,7 +107,8 @@ int prism_b200_executor_create(int device, prism_b200_executor **out) {
   // PRISM_B200_PDL=0 turns programmatic dependent launch off (A/B timing)
   const char *pdl = getenv("PRISM_B200_PDL");
   ex->pdl = !(pdl && pdl[0] == '0');
-  if (cudaStreamCreateWithFlags(&ex->stream, cudaStreamNonBlocking) != cudaSuccess ||
+  if (init_matvec_attributes() != cudaSuccess ||
+      cudaStreamCreateWithFlags(&ex->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&ex->d_status, 64) != cudaSuccess ||
       cudaHostAlloc(reinterpret_cast<void **>(&ex->h_status), 64, cudaHostAllocDefault) !=
           cudaSuccess ||
@@ -193,54 +197,15 @@ int prism_b200_weight_upload(prism_b200_executor *ex, const prism_b200_tensor *t
   if (!geometry_ok(t))
     return ex->fail(PRISM_B200_E_UNSUPPORTED, "unsupported kind %u or geometry %llux%llu",
                     t->kind, (unsigned long long)t->cols, (unsigned long long)t->rows);
-  const int bb = block_bytes(t->kind);
-  const int nb = (int)(t->cols / 256);
-  const size_t nblocks = (size_t)t->rows * nb;
+  const size_t nblocks = (size_t)t->rows * (t->cols / 256);
   const uint8_t *src = static_cast<const uint8_t *>(t->data);
-  // reference `scale` (src/kernels.rs:152-154): every fp16 scale finite
-  for (size_t i = 0; i < nblocks; ++i) {
-    const uint8_t *blk = src + i * bb;
-    if (t->kind == PRISM_B200_KIND_TQ2_0) {
-      if ((blk[65] & 0x7c) == 0x7c)
-        return ex->fail(PRISM_B200_E_NONFINITE, "nonfinite TQ2_0 scale");
-    } else if ((blk[81] & 0x7c) == 0x7c || (blk[83] & 0x7c) == 0x7c) {
-      return ex->fail(PRISM_B200_E_NONFINITE, "nonfinite Q2_K scale");
-    }
-  }
+  if (!scales_finite(t->kind, src, nblocks))
+    return ex->fail(PRISM_B200_E_NONFINITE, "nonfinite fp16 block scale");
   cudaSetDevice(ex->device);
   auto *w = new prism_b200_weight();
   w->ex = ex;
-  DeviceWeight &dw = w->dw;
-  dw.kind = t->kind;
-  dw.rows = t->rows;
-  dw.cols = t->cols;
-  dw.nb = nb;
-  dw.h = choose_tile_height(t->kind, t->rows, t->cols, ex->num_sms);
-  dw.ntiles = (int)((t->rows + dw.h - 1) / dw.h);
-  dw.bytes = (uint64_t)dw.ntiles * nb * unit_bytes((int)t->kind, dw.h);
-  uint8_t *d_src = nullptr;
-  const size_t src_bytes = nblocks * bb;
-  cudaError_t e = configure_weight(dw, ex->num_sms);
-  if (e == cudaSuccess) e = cudaMalloc(&dw.units, dw.bytes);
-  if (e == cudaSuccess) e = cudaMalloc(&d_src, src_bytes);
-  if (e == cudaSuccess)
-    e = cudaMemcpyAsync(d_src, src, src_bytes, cudaMemcpyHostToDevice, ex->stream);
-  if (e == cudaSuccess) {
-    long threads = (long)dw.ntiles * nb * dw.h;
-    unsigned grid = (unsigned)((threads + 255) / 256);
-    const int rows = (int)t->rows;
-#define PRISM_RP(K, HH)                                                                   \
-  if (dw.kind == K && dw.h == HH)                                                         \
-    repack_kernel<K, HH><<<grid, 256, 0, ex->stream>>>(d_src, rows, nb, dw.ntiles, dw.units);
-    PRISM_RP(35, 32) PRISM_RP(35, 16) PRISM_RP(35, 8)
-    PRISM_RP(10, 32) PRISM_RP(10, 16) PRISM_RP(10, 8)
-#undef PRISM_RP
-    e = cudaGetLastError();
-  }
-  if (e == cudaSuccess) e = cudaStreamSynchronize(ex->stream);
-  if (d_src) cudaFree(d_src);
+  cudaError_t e = upload_tiled(src, t->kind, t->rows, t->cols, ex->num_sms, ex->stream, w->dw);
   if (e != cudaSuccess) {
-    if (dw.units) cudaFree(dw.units);
     delete w;
     return cuda_fail(ex, e, "weight upload");
   }
@@ -410,7 +375,8 @@ int prism_b200_block_dots(prism_b200_executor *ex, const prism_b200_weight *w,
   CK(cudaMemcpyAsync(ex->act.ptr, activation, abytes, cudaMemcpyHostToDevice, s),
      "activation copy");
   CK(launch_matvec(w->dw, ex->act.ptr, nullptr, static_cast<int32_t *>(ex->ints.ptr),
-                   static_cast<int32_t *>(ex->ints2.ptr), kModeInts, ex->d_status, s, false),
+                   static_cast<int32_t *>(ex->ints2.ptr), kEpiInts, ex->d_status, ex->num_sms, s,
+                   false),
      "block dots launch");
   CK(cudaMemcpyAsync(ints, ex->ints.ptr, ibytes, cudaMemcpyDeviceToHost, s), "ints copy");
   if (w->dw.kind == PRISM_B200_KIND_Q2_K)
@@ -419,3 +385,6 @@ int prism_b200_block_dots(prism_b200_executor *ex, const prism_b200_weight *w,
 }
 
 }  // extern "C"
+
+// The model entry points share this translation unit's kernels and helpers.
+#include "model.cuh"

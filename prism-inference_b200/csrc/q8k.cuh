@@ -14,12 +14,13 @@ namespace prism {
 
 constexpr int kQ8KBytes = 292;  // f32 scale, 256 x i8, 16 x i16
 
-// Quantize one 256-value block held 8-per-lane in v[] (lane-major order).
-// Writes the AoS block at `out` (4-byte aligned).  Returns status bits.
-__device__ __forceinline__ unsigned q8k_block_from_regs(const float (&v)[8], int lane,
-                                                        bool pinned, uint8_t *out) {
+// Quantize one block held 8-per-lane in v[].  Outputs the block scale, this
+// lane's 8 codes and the sum of the 16-value group this lane shares with
+// lane^1.  Returns status bits (nonfinite input, range violation).
+__device__ __forceinline__ unsigned q8k_quantize_regs(const float (&v)[8], int lane,
+                                                      bool pinned, float &scale,
+                                                      int8_t (&q)[8], int &pair_sum) {
   unsigned st = 0;
-  // local first-max in index order
   float best = 0.0f;
   int best_idx = 0x7fffffff;
   bool finite = true;
@@ -31,7 +32,7 @@ __device__ __forceinline__ unsigned q8k_block_from_regs(const float (&v)[8], int
       best_idx = lane * 8 + i;
     }
   }
-  // warp reduction: larger magnitude wins, ties go to the smaller index
+  // larger magnitude wins, ties go to the smaller index
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) {
     float ob = __shfl_xor_sync(0xffffffffu, best, off);
@@ -44,14 +45,13 @@ __device__ __forceinline__ unsigned q8k_block_from_regs(const float (&v)[8], int
   }
   finite = __all_sync(0xffffffffu, finite);
   if (!finite) st |= kStatusNonfinite;
-  float maximum = best;  // +0.0 when every value is zero
-  int8_t q[8];
-  float scale = 0.0f;
+  const float maximum = best;  // +0.0 when every value is zero
+  scale = 0.0f;
   if (maximum == 0.0f || !finite) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) q[i] = 0;
   } else {
-    float iscale = __fdiv_rn(-127.0f, maximum);
+    const float iscale = __fdiv_rn(-127.0f, maximum);
     if (!is_finite_f(iscale)) {
       st |= kStatusInvalid;
 #pragma unroll
@@ -70,8 +70,7 @@ __device__ __forceinline__ unsigned q8k_block_from_regs(const float (&v)[8], int
             qi = 0;
           }
         } else {
-          float r = rintf(__fmul_rn(v[i], iscale));
-          r = fminf(r, 127.0f);
+          float r = fminf(rintf(__fmul_rn(v[i], iscale)), 127.0f);
           if (!(r >= -127.0f && r <= 127.0f)) {
             st |= kStatusInvalid;
             r = 0.0f;
@@ -82,11 +81,22 @@ __device__ __forceinline__ unsigned q8k_block_from_regs(const float (&v)[8], int
       }
     }
   }
-  // group sums: group g = lanes 2g, 2g+1
   int s = 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) s += q[i];
   s += __shfl_xor_sync(0xffffffffu, s, 1);
+  pair_sum = s;
+  return st;
+}
+
+// Quantize one block held 8-per-lane and write the AoS block at `out`
+// (4-byte aligned).  Returns status bits.
+__device__ __forceinline__ unsigned q8k_block_from_regs(const float (&v)[8], int lane,
+                                                        bool pinned, uint8_t *out) {
+  float scale;
+  int8_t q[8];
+  int s;
+  const unsigned st = q8k_quantize_regs(v, lane, pinned, scale, q, s);
   if (lane == 0) *reinterpret_cast<float *>(out) = scale;
   uint32_t w0 = (uint32_t)(uint8_t)q[0] | ((uint32_t)(uint8_t)q[1] << 8) |
                 ((uint32_t)(uint8_t)q[2] << 16) | ((uint32_t)(uint8_t)q[3] << 24);

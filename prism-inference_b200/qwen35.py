@@ -131,3 +131,127 @@ def synthetic_weights(cfg, seed=0):
 def prompt_tokens(cfg, n=512, seed=1):
     """Random prompt of n token ids uniform in [0, vocab)."""
     return np.random.default_rng(seed).integers(0, cfg.vocab, n).astype(np.uint32)
+
+
+class _CConfig(__import__("ctypes").Structure):
+    import ctypes as _c
+    _fields_ = [("hidden", _c.c_uint32), ("layers", _c.c_uint32), ("heads", _c.c_uint32),
+                ("kv_heads", _c.c_uint32), ("head_dim", _c.c_uint32), ("rope_dim", _c.c_uint32),
+                ("rope_sections", _c.c_uint32 * 4), ("rope_base", _c.c_float), ("eps", _c.c_float),
+                ("ffn", _c.c_uint32), ("vocab", _c.c_uint32), ("ssm_state", _c.c_uint32),
+                ("ssm_groups", _c.c_uint32), ("ssm_values", _c.c_uint32),
+                ("conv_kernel", _c.c_uint32), ("full_interval", _c.c_uint32),
+                ("context", _c.c_uint32), ("kv_policy", _c.c_uint32), ("weight_kind", _c.c_uint32)]
+
+
+KV_F16, KV_Q8_0 = 0, 1
+
+
+def _declare_model(L):
+    import ctypes as c
+    vp, i32, sz, u32 = c.c_void_p, c.c_int, c.c_size_t, c.c_uint32
+    for name, res, args in [
+        ("prism_b200_model_create", i32, [vp, vp, c.POINTER(vp)]),
+        ("prism_b200_model_destroy", None, [vp]),
+        ("prism_b200_model_set_tensor", i32, [vp, c.c_char_p, vp]),
+        ("prism_b200_model_set_vector", i32, [vp, c.c_char_p, vp, sz]),
+        ("prism_b200_model_finalize", i32, [vp]),
+        ("prism_b200_model_reset", i32, [vp]),
+        ("prism_b200_model_position", c.c_int64, [vp]),
+        ("prism_b200_model_evaluate", i32, [vp, u32, vp, vp]),
+        ("prism_b200_model_generate", i32, [vp, vp, sz, sz, vp]),
+        ("prism_b200_model_decode_async", i32, [vp, sz]),
+        ("prism_b200_model_read_state", c.c_int64, [vp, u32, u32, vp, sz]),
+    ]:
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+
+
+class Qwen35Model:
+    """The hybrid decoder on the device, through the C ABI.  Mirrors the
+    reference's Decoder surface: reset, evaluate (one token -> logits),
+    generate (prompt ingestion + greedy decode)."""
+
+    def __init__(self, executor, cfg, kv_policy=KV_F16):
+        import ctypes as c
+        L = pb.load()
+        _declare_model(L)
+        self.L, self.ex, self.cfg = L, executor, cfg
+        cc = _CConfig()
+        for f, _ in _CConfig._fields_:
+            if f == "rope_sections":
+                cc.rope_sections = (c.c_uint32 * 4)(*cfg.rope_sections)
+            elif f == "kv_policy":
+                cc.kv_policy = kv_policy
+            else:
+                setattr(cc, f, getattr(cfg, f))
+        self._cc = cc
+        h = c.c_void_p()
+        executor._check(L.prism_b200_model_create(executor.h, c.byref(cc), c.byref(h)))
+        self.h = h
+
+    def close(self):
+        if self.h:
+            self.L.prism_b200_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def load(self, weights):
+        import ctypes as c
+        for name, arr in weights.items():
+            if arr.dtype == np.uint8:
+                rows = arr.shape[0]
+                cols = arr.shape[1] // pb.BLOCK_BYTES[self.cfg.weight_kind] * 256
+                t = pb.Tensor(self.cfg.weight_kind, cols, rows, arr)._c()
+                st = self.L.prism_b200_model_set_tensor(self.h, name.encode(), c.byref(t))
+            else:
+                a = np.ascontiguousarray(arr, np.float32).reshape(-1)
+                st = self.L.prism_b200_model_set_vector(self.h, name.encode(), a.ctypes.data, a.size)
+            self.ex._check(st)
+        self.ex._check(self.L.prism_b200_model_finalize(self.h))
+
+    def reset(self):
+        self.ex._check(self.L.prism_b200_model_reset(self.h))
+
+    @property
+    def position(self):
+        return self.L.prism_b200_model_position(self.h)
+
+    def evaluate(self, token, logits=True):
+        import ctypes as c
+        out = np.zeros(self.cfg.vocab, np.float32) if logits else None
+        g = np.zeros(1, np.uint32)
+        self.ex._check(self.L.prism_b200_model_evaluate(
+            self.h, int(token), out.ctypes.data if logits else None, g.ctypes.data))
+        return out, int(g[0])
+
+    def generate(self, prompt, n_new):
+        prompt = np.ascontiguousarray(prompt, np.uint32)
+        out = np.zeros(max(n_new, 1), np.uint32)
+        self.ex._check(self.L.prism_b200_model_generate(self.h, prompt.ctypes.data, prompt.size,
+                                                        n_new, out.ctypes.data))
+        return out[:n_new]
+
+    def decode_async(self, steps):
+        self.ex._check(self.L.prism_b200_model_decode_async(self.h, steps))
+
+    def read_state(self, layer, which):
+        """which: 0 conv, 1 matrix, 2 keys, 3 values, 4 hidden."""
+        c = self.cfg
+        shapes = {0: ((c.conv_channels, c.conv_kernel - 1), np.float32),
+                  1: ((c.ssm_values, c.ssm_state, c.ssm_state), np.float32),
+                  2: ((self.position, c.kv_heads * c.head_dim), np.uint16),
+                  3: ((self.position, c.kv_heads * c.head_dim), np.uint16),
+                  4: ((c.hidden,), np.float32)}
+        shape, dt = shapes[which]
+        out = np.zeros(shape, dt)
+        n = self.L.prism_b200_model_read_state(self.h, layer, which, out.ctypes.data, out.nbytes)
+        if n < 0:
+            raise pb.PrismB200Error(-n, "state readback failed")
+        return out

@@ -244,9 +244,30 @@ int prism_b200_model_generate(prism_b200_model *m, const uint32_t *prompt, size_
  * waiting (each consumes the previous step's greedy token). */
 int prism_b200_model_decode_async(prism_b200_model *m, size_t steps);
 
+/* set_prompt places `n` prompt tokens at the next positions of the token
+ * history; ingest_async then enqueues, without waiting, `n` ingestion steps
+ * (no LM head, the reference's Decoder::ingest, src/lib.rs:229-247).  Decode
+ * steps past the prompt consume the previous step's greedy token. */
+int prism_b200_model_set_prompt(prism_b200_model *m, const uint32_t *tokens, size_t n);
+int prism_b200_model_ingest_async(prism_b200_model *m, size_t n);
+
+/* The model's own stream (a cudaStream_t). */
+void *prism_b200_model_stream(const prism_b200_model *m);
+
+/* Run one decode step (device-driven input, as decode_async) with CUDA
+ * events between phases and report per-layer attention and FFN wall time,
+ * the LM head and the whole step, in milliseconds (reference
+ * src/graph/timing.rs TokenTimings).  Each array holds `layers` floats;
+ * any pointer may be NULL.  The timed step runs without programmatic
+ * dependent launch, so its total exceeds a graph step's. */
+int prism_b200_model_step_timings(prism_b200_model *m, float *attention_ms, float *ffn_ms,
+                                  float *head_ms, float *total_ms);
+
 /* State readback for parity checks: which = 0 conv history [channels][k-1],
  * 1 recurrent matrix [values][S][S], 2 keys / 3 values [position][kv*hd]
- * binary16, 4 hidden [hidden].  Returns the byte count written. */
+ * binary16, 4 hidden [hidden]; the last layer's activations: 5 attended,
+ * 6 GDN gate projection, 7 FFN up*silu(gate), 9 logits.  Returns the byte
+ * count written, or minus a status code. */
 int64_t prism_b200_model_read_state(prism_b200_model *m, uint32_t layer, uint32_t which,
                                     void *out, size_t bytes);
 

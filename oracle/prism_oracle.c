@@ -8,8 +8,14 @@
  *
  * Compile with -ffp-contract=off: every multiply and add below is a separate
  * binary32 (or binary64) rounding, exactly as the reference's Rust source
- * (which never contracts) performs them.  libm expf/logf/sqrtf are the same
- * functions the reference's f32::exp/ln/sqrt lower to on x86-64 Linux.
+ * (which never contracts) performs them.
+ *
+ * Transcendentals: the reference calls f32::exp/ln/sin/cos, whose last-ulp
+ * results depend on the host libm (glibc on Linux, the UCRT on Windows).
+ * This restatement defines them as the correctly rounded binary32 value,
+ * evaluated in binary64 and rounded once (po_expf etc.); the device kernels
+ * use the same definition, so the two agree bit for bit.  A platform libm
+ * differs from it only in rare last-ulp cases.
  */
 #include "prism_oracle.h"
 
@@ -470,11 +476,17 @@ float po_f16_dot(const float *a, const uint16_t *b, size_t n) {
   return (float)acc;
 }
 
+/* Correctly rounded binary32 transcendentals (see the file header). */
+float po_expf(float x) { return (float)exp((double)x); }
+float po_logf(float x) { return (float)log((double)x); }
+float po_sinf(float x) { return (float)sin((double)x); }
+float po_cosf(float x) { return (float)cos((double)x); }
+
 /* reference src/kernels.rs:3365-3368 */
-float po_silu(float v) { return v / (1.0f + expf(-v)); }
+float po_silu(float v) { return v / (1.0f + po_expf(-v)); }
 
 /* reference src/graph.rs:6349-6351 */
-float po_sigmoid(float v) { return 1.0f / (1.0f + expf(-v)); }
+float po_sigmoid(float v) { return 1.0f / (1.0f + po_expf(-v)); }
 
 /* reference src/graph.rs:6357-6384 recurrent_decay */
 int po_recurrent_decay(float alpha, float time_bias, float decay_weight,
@@ -492,11 +504,11 @@ int po_recurrent_decay(float alpha, float time_bias, float decay_weight,
       *out = 0.0f;
       return PO_OK;
     }
-    *out = expf(linear * decay_weight);
+    *out = po_expf(linear * decay_weight);
     return PO_OK;
   }
-  float softplus = linear > 20.0f ? linear : logf(1.0f + expf(linear));
-  *out = expf(softplus * decay_weight);
+  float softplus = linear > 20.0f ? linear : po_logf(1.0f + po_expf(linear));
+  *out = po_expf(softplus * decay_weight);
   return PO_OK;
 }
 
@@ -567,7 +579,7 @@ int po_softmax_round_f16(float *v, size_t n) {
     if (isnan(v[i]) || v[i] == INFINITY) return PO_E_INVALID;
   double total = 0.0;
   for (size_t i = 0; i < n; ++i) {
-    v[i] = expf(v[i] - maximum);
+    v[i] = po_expf(v[i] - maximum);
     total += (double)v[i];
   }
   float inverse = (float)(1.0 / total);

@@ -83,6 +83,10 @@ int po_block_bytes(uint32_t kind);
 /* ---- float primitives (Source contract) ----------------------------- */
 float po_float_dot(const float *a, const float *b, size_t n);
 float po_f16_dot(const float *a, const uint16_t *b, size_t n);
+float po_expf(float x);
+float po_logf(float x);
+float po_sinf(float x);
+float po_cosf(float x);
 float po_silu(float v);
 float po_sigmoid(float v);
 int po_recurrent_decay(float alpha, float time_bias, float decay_weight,

@@ -160,8 +160,8 @@ void po_rope_frequencies(const po_qwen35_config *cfg, int position, float *cos_s
   for (int i = 0; i < cfg->rope_dim / 2; ++i) {
     int sector = i % 3;
     float angle = i < 3 * cfg->rope_sections[sector] ? thetas[sector] : thetas[3];
-    cos_sin[2 * i] = cosf(angle);
-    cos_sin[2 * i + 1] = sinf(angle);
+    cos_sin[2 * i] = po_cosf(angle);
+    cos_sin[2 * i + 1] = po_sinf(angle);
     for (int t = 0; t < 4; ++t) thetas[t] = thetas[t] * theta_scale;
   }
 }
@@ -224,7 +224,7 @@ static int full_attention(po_qwen35 *m, int l, int threads) {
       for (int p = 0; p < npos; ++p)
         sum += (double)(m->scores[p] * po_half_to_float(m->vals[l][(size_t)p * kvw + off + d]));
       float v = (float)(sum + (double)(m->scores[npos] * m->value[off + d]));
-      out[d] = v * (1.0f / (1.0f + expf(-g[d])));
+      out[d] = v * (1.0f / (1.0f + po_expf(-g[d])));
     }
   }
   const void *wo[1] = {W(m, l, PO_W_O)};

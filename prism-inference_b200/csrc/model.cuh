@@ -100,10 +100,19 @@ inline StepState step_state(prism_b200_model *m) {
 
 // Enqueue one decode step.  With `head`, the step ends with the tied LM head,
 // the greedy key and (past the prompt) the next input token.
-inline cudaError_t enqueue_step(prism_b200_model *m, bool head) {
+// `ev` (optional, 2*layers + 4 events) brackets the phases for per-layer
+// timing: ev[0] start, ev[1] after the embedding, ev[2+2l] after layer l's
+// attention, ev[3+2l] after its FFN, ev[2+2L] after the head, ev[3+2L] end.
+// Timed steps run without programmatic dependent launch.
+inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev = nullptr) {
   prism_b200_executor *ex = m->ex;
   const auto &c = m->cfg;
-  const bool pdl = ex->pdl;
+  const bool pdl = ex->pdl && !ev;
+  const int nl = (int)m->L.size();
+  auto mark = [&](int i) {
+    if (ev) cudaEventRecord(ev[i], m->stream);
+  };
+  mark(0);
   const int sms = ex->num_sms;
   cudaStream_t s = m->stream;
   unsigned *status = ex->d_status;
@@ -122,6 +131,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head) {
                                  hidden, n, status);
     if (e != cudaSuccess) return e;
   }
+  mark(1);
   const uint32_t kind = c.weight_kind;
   for (size_t l = 0; l < m->L.size(); ++l) {
     ModelLayer &Ly = m->L[l];
@@ -156,9 +166,16 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head) {
       aa.position = m->d_position;
       aa.attended = m->attended;
       aa.status = status;
-      const size_t smem = (size_t)(4 * c.head_dim + 64 + c.context + 1) * sizeof(float);
-      cudaLaunchConfig_t cfg =
-          pdl_config(dim3(c.heads), dim3(kAttnThreads), smem, s, attr, pdl);
+      // one 8-CTA cluster per query head (split over the cached positions)
+      const size_t smem = attn_smem_bytes((int)c.head_dim, (int)c.context);
+      cudaLaunchAttribute cattr[2];
+      cudaLaunchConfig_t cfg = pdl_config(dim3(c.heads * kAttnSplit), dim3(kAttnThreads), smem,
+                                          s, cattr, pdl);
+      cattr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+      cattr[cfg.numAttrs].val.clusterDim.x = kAttnSplit;
+      cattr[cfg.numAttrs].val.clusterDim.y = 1;
+      cattr[cfg.numAttrs].val.clusterDim.z = 1;
+      cfg.numAttrs += 1;
       if ((e = cudaLaunchKernelEx(&cfg, attention_decode_kernel, aa)) != cudaSuccess) return e;
       MvArgs o;
       o.prologue = kProF32;
@@ -211,6 +228,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head) {
       o.w[0] = mv_weight(Ly.out, m->hidden, m->hidden);
       if ((e = launch_matvec_group(kind, kEpiStore, o, sms, s, pdl)) != cudaSuccess) return e;
     }
+    mark(2 + 2 * (int)l);
     MvArgs f;
     f.prologue = kProRmsNorm;
     f.in0 = m->hidden;
@@ -230,6 +248,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head) {
     d.count = 1;
     d.w[0] = mv_weight(Ly.down, m->hidden, m->hidden);
     if ((e = launch_matvec_group(kind, kEpiStore, d, sms, s, pdl)) != cudaSuccess) return e;
+    mark(3 + 2 * (int)l);
   }
   if (head) {
     MvArgs h;
@@ -244,8 +263,11 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head) {
     h.argmax_key = m->d_argmax;
     if ((e = launch_matvec_group(kind, kEpiArgmax, h, sms, s, pdl)) != cudaSuccess) return e;
   }
+  mark(2 + 2 * nl);
   cudaLaunchConfig_t cfg = pdl_config(dim3(1), dim3(32), 0, s, attr, pdl);
-  return cudaLaunchKernelEx(&cfg, finish_step_kernel, step_state(m), head ? 1 : 0);
+  e = cudaLaunchKernelEx(&cfg, finish_step_kernel, step_state(m), head ? 1 : 0);
+  mark(3 + 2 * nl);
+  return e;
 }
 
 inline cudaError_t capture_step(prism_b200_model *m, bool head, cudaGraphExec_t *out) {
@@ -603,6 +625,39 @@ int prism_b200_model_decode_async(prism_b200_model *m, size_t steps) {
   return PRISM_B200_OK;
 }
 
+void *prism_b200_model_stream(const prism_b200_model *m) {
+  return m ? reinterpret_cast<void *>(m->stream) : nullptr;
+}
+
+int prism_b200_model_set_prompt(prism_b200_model *m, const uint32_t *tokens, size_t n) {
+  if (!m || !tokens || n == 0) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = m->ex;
+  if (m->position + (int64_t)n > (int64_t)m->cfg.context)
+    return ex->fail(PRISM_B200_E_INVALID, "context is exhausted");
+  for (size_t i = 0; i < n; ++i)
+    if (tokens[i] >= m->cfg.vocab)
+      return ex->fail(PRISM_B200_E_INVALID, "prompt token outside the vocabulary");
+  cudaSetDevice(ex->device);
+  const int end = (int)(m->position + (int64_t)n);
+  CK(cudaMemcpyAsync(m->d_tokens + m->position, tokens, n * 4, cudaMemcpyHostToDevice, m->stream),
+     "prompt");
+  CK(cudaMemcpyAsync(m->d_prompt_end, &end, 4, cudaMemcpyHostToDevice, m->stream), "prompt");
+  CK(cudaStreamSynchronize(m->stream), "prompt");
+  return PRISM_B200_OK;
+}
+
+int prism_b200_model_ingest_async(prism_b200_model *m, size_t n) {
+  if (!m) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = m->ex;
+  if (!m->finalized) return ex->fail(PRISM_B200_E_INVALID, "model is not finalized");
+  if (m->position + (int64_t)n > (int64_t)m->cfg.context)
+    return ex->fail(PRISM_B200_E_INVALID, "context is exhausted");
+  cudaSetDevice(ex->device);
+  for (size_t i = 0; i < n; ++i) CK(cudaGraphLaunch(m->g_ingest, m->stream), "ingest step");
+  m->position += (int64_t)n;
+  return PRISM_B200_OK;
+}
+
 int prism_b200_model_generate(prism_b200_model *m, const uint32_t *prompt, size_t n_prompt,
                               size_t n_new, uint32_t *out) {
   if (!m) return PRISM_B200_E_INVALID;
@@ -631,6 +686,42 @@ int prism_b200_model_generate(prism_b200_model *m, const uint32_t *prompt, size_
   st = model_finish(m);
   if (st) return st;
   m->position += (int64_t)(n_prompt - 1 + decode_steps);
+  return PRISM_B200_OK;
+}
+
+int prism_b200_model_step_timings(prism_b200_model *m, float *attention_ms, float *ffn_ms,
+                                  float *head_ms, float *total_ms) {
+  if (!m) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = m->ex;
+  int st = check_open(ex);
+  if (st) return st;
+  if (!m->finalized) return ex->fail(PRISM_B200_E_INVALID, "model is not finalized");
+  if (m->position >= (int64_t)m->cfg.context)
+    return ex->fail(PRISM_B200_E_INVALID, "context is exhausted");
+  cudaSetDevice(ex->device);
+  const int nl = (int)m->L.size();
+  std::vector<cudaEvent_t> ev((size_t)(2 * nl + 4));
+  for (auto &e : ev) CK(cudaEventCreate(&e), "event");
+  cudaError_t e = prism::enqueue_step(m, true, ev.data());
+  if (e == cudaSuccess) e = cudaEventSynchronize(ev.back());
+  if (e == cudaSuccess) {
+    auto span = [&](int a, int b) {
+      float ms = 0.0f;
+      cudaEventElapsedTime(&ms, ev[a], ev[b]);
+      return ms;
+    };
+    for (int l = 0; l < nl; ++l) {
+      if (attention_ms) attention_ms[l] = span(1 + 2 * l, 2 + 2 * l);
+      if (ffn_ms) ffn_ms[l] = span(2 + 2 * l, 3 + 2 * l);
+    }
+    if (head_ms) *head_ms = span(1 + 2 * nl, 2 + 2 * nl);
+    if (total_ms) *total_ms = span(0, 3 + 2 * nl);
+  }
+  for (auto &x : ev) cudaEventDestroy(x);
+  if (e != cudaSuccess) return cuda_fail(ex, e, "timed step");
+  st = model_finish(m);
+  if (st) return st;
+  m->position += 1;
   return PRISM_B200_OK;
 }
 

@@ -9,6 +9,8 @@
 // within a few ulp of the host libm the reference uses.
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "matvec.cuh"
 
@@ -316,22 +318,47 @@ __device__ __forceinline__ float norm_rope_round(const float *x, const float *w,
   return round_f16(out);
 }
 
-// One CTA per query head; hd == 256 == blockDim.x.  Scores over the cached
-// positions use binary16 keys (reference f16_dot), the current position the
-// binary32 rounded key (float_dot); softmax_round_f16; binary64 value sums;
-// sigmoid gate (reference src/graph.rs:4470-4950).
+// Attention decode for one query head split over a cluster of kAttnSplit
+// CTAs (one per SM): CTA r scores and accumulates its contiguous share of
+// the cached positions; the softmax maximum, the binary64 total and the
+// binary64 value partial sums are combined through distributed shared
+// memory in rank (= position) order.  hd == 256 == blockDim.x.
+//
+// Arithmetic (reference src/graph.rs:4470-4950, Source): q and the current
+// k are RMS-normed, RoPE'd and rounded to binary16; past scores are f16_dot
+// (binary32 products, binary64 sum) x 1/sqrt(hd), the current score a
+// float_dot; softmax_round_f16 (binary64 total, probabilities rounded to
+// binary16); values are binary64 sums of binary32 products, rounded once;
+// the output is gated by sigmoid(gate).
+constexpr int kAttnSplit = 8;
+
+__host__ __device__ constexpr int attn_chunk_cap(int context) {
+  return (context + kAttnSplit - 1) / kAttnSplit + 1;
+}
+
+__host__ __device__ constexpr size_t attn_smem_bytes(int hd, int context) {
+  return ((size_t)(4 * hd + 64 + attn_chunk_cap(context)) * 4 + 15) / 16 * 16 +
+         (size_t)hd * 8;
+}
+
 __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs a) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(16) float sm[];
   const int hd = a.hd;
   float *q = sm;                 // [hd]
   float *kc = q + hd;            // [hd]
   float *vc = kc + hd;           // [hd]
   float *buf = vc + hd;          // [hd]
-  float *cs = buf + hd;          // [rope]
-  float *scores = cs + 64;       // [pos+1]
+  float *cs = buf + hd;          // [64]: (cos, sin) pairs
+  float *scores = cs + 64;       // [chunk]
+  double *partial;               // [hd], after the chunk's scores
   __shared__ double red[kAttnThreads / 32];
   __shared__ float fred[kAttnThreads / 32];
-  const int h = blockIdx.x;
+  __shared__ float s_max, s_cur;
+  __shared__ double s_tot;
+  const int rank = (int)cluster.block_rank();
+  const int h = blockIdx.x / kAttnSplit;
   const int group = a.heads / a.kv_heads;
   const int kvh = h / group;
   const int kvw = a.kv_heads * hd;
@@ -340,17 +367,20 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
   grid_dependency_wait();
   grid_dependents_launch();
   const int pos = *a.position;
-  if (i == 0) {
-    // reference src/graph.rs:6406-6437: angles p * theta_scale^i by repeated
-    // binary32 multiplication; text positions give the three sections the
-    // same angle, and indices past 3*section use the fourth (zero) position
+  // chunk of past positions owned by this CTA
+  const int per = (pos + kAttnSplit - 1) / kAttnSplit;
+  const int lo = min(pos, rank * per), hi = min(pos, lo + per);
+  partial = reinterpret_cast<double *>(reinterpret_cast<uint8_t *>(sm) +
+                                       ((size_t)(4 * hd + 64 + per + 1) * 4 + 15) / 16 * 16);
+  if (i < a.rope_dim / 2) {
+    // reference src/graph.rs:6406-6437: angle_j = p * theta_scale^j by j
+    // repeated binary32 multiplications; text positions give the three
+    // sections the same angle, and indices past 3*section use position 0
     float theta = (float)pos;
-    for (int j = 0; j < a.rope_dim / 2; ++j) {
-      const float angle = j < 3 * a.sections[j % 3] ? theta : 0.0f;
-      cs[2 * j] = cos_cr(angle);
-      cs[2 * j + 1] = sin_cr(angle);
-      theta = __fmul_rn(theta, a.theta_scale);
-    }
+    for (int j = 0; j < i; ++j) theta = __fmul_rn(theta, a.theta_scale);
+    const float angle = i < 3 * a.sections[i % 3] ? theta : 0.0f;
+    cs[2 * i] = cos_cr(angle);
+    cs[2 * i + 1] = sin_cr(angle);
   }
   __syncthreads();
   q[i] = norm_rope_round(a.projected + (long)h * 2 * hd, a.q_norm, a.eps, hd, a.rope_dim, cs,
@@ -358,17 +388,18 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
   kc[i] = norm_rope_round(a.key_in + (long)kvh * hd, a.k_norm, a.eps, hd, a.rope_dim, cs, buf,
                           red);
   vc[i] = round_f16(a.value_in[kvh * hd + i]);
-  if (h % group == 0) {
+  if (rank == 0 && h % group == 0) {
     a.kcache[(long)pos * kvw + kvh * hd + i] = float_to_half_bits(kc[i]);
     a.vcache[(long)pos * kvw + kvh * hd + i] = float_to_half_bits(vc[i]);
   }
   __syncthreads();
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
-  // scores: warp per position, lane owns 8 dims (one 16-byte key load)
+  // scores of this chunk: warp per position, lane owns 8 dims (16-byte load)
   const float4 q0 = reinterpret_cast<const float4 *>(q)[lane * 2];
   const float4 q1 = reinterpret_cast<const float4 *>(q)[lane * 2 + 1];
-  for (int p = warp; p < pos; p += kAttnThreads / 32) {
-    const uint4 kv = *reinterpret_cast<const uint4 *>(a.kcache + (long)p * kvw + kvh * hd + lane * 8);
+  for (int p = lo + warp; p < hi; p += kAttnThreads / 32) {
+    const uint4 kv =
+        *reinterpret_cast<const uint4 *>(a.kcache + (long)p * kvw + kvh * hd + lane * 8);
     const uint16_t *kh = reinterpret_cast<const uint16_t *>(&kv);
     double s = (double)__fmul_rn(q0.x, half_bits_to_float(kh[0])) +
                (double)__fmul_rn(q0.y, half_bits_to_float(kh[1])) +
@@ -379,37 +410,68 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
                (double)__fmul_rn(q1.z, half_bits_to_float(kh[6])) +
                (double)__fmul_rn(q1.w, half_bits_to_float(kh[7]));
     s = warp_sum_f64(s);
-    if (lane == 0) scores[p] = __fmul_rn((float)s, scale);
+    if (lane == 0) scores[p - lo] = __fmul_rn((float)s, scale);
   }
   {
+    // the current position's score (every CTA computes the same value)
     const double s = block_sum_f64((double)__fmul_rn(q[i], kc[i]), red);
-    if (i == 0) scores[pos] = __fmul_rn((float)s, scale);
+    if (i == 0) s_cur = __fmul_rn((float)s, scale);
   }
   __syncthreads();
-  // softmax_round_f16 (reference src/kernels.rs:4431-4466)
   float m = -INFINITY;
-  for (int p = i; p <= pos; p += kAttnThreads) m = fmaxf(m, scores[p]);
+  for (int p = i; p < hi - lo; p += kAttnThreads) m = fmaxf(m, scores[p]);
   m = block_max_f32(m, fred);
+  if (i == 0) s_max = m;
+  cluster.sync();
+  // global maximum over every chunk and the current position
+  float M = s_cur;
+  for (int r = 0; r < kAttnSplit; ++r) M = fmaxf(M, *cluster.map_shared_rank(&s_max, r));
   double tot = 0.0;
-  for (int p = i; p <= pos; p += kAttnThreads) {
-    const float e = exp_cr(__fsub_rn(scores[p], m));
+  for (int p = i; p < hi - lo; p += kAttnThreads) {
+    const float e = exp_cr(__fsub_rn(scores[p], M));
     scores[p] = e;
     tot += (double)e;
   }
   tot = block_sum_f64(tot, red);
-  const float inv = (float)(1.0 / tot);
-  if (!is_finite_f(m) && i == 0) report(a.status, kStatusNonfinite);
+  if (i == 0) s_tot = tot;
+  cluster.sync();
+  double total = 0.0;
+  for (int r = 0; r < kAttnSplit; ++r) total += *cluster.map_shared_rank(&s_tot, r);
+  const float e_cur = exp_cr(__fsub_rn(s_cur, M));
+  total += (double)e_cur;
+  const float inv = (float)(1.0 / total);
+  if (!is_finite_f(M) && i == 0 && rank == 0) report(a.status, kStatusNonfinite);
+  const float p_cur = round_f16(__fmul_rn(e_cur, inv));
+  for (int p = i; p < hi - lo; p += kAttnThreads) scores[p] = round_f16(__fmul_rn(scores[p], inv));
   __syncthreads();
-  for (int p = i; p <= pos; p += kAttnThreads) scores[p] = round_f16(__fmul_rn(scores[p], inv));
-  __syncthreads();
-  // values: one dimension per thread, binary64 sum in position order
-  double acc = -0.0;
-  const uint16_t *vcol = a.vcache + kvh * hd + i;
-  for (int p = 0; p < pos; ++p)
-    acc += (double)__fmul_rn(scores[p], half_bits_to_float(vcol[(long)p * kvw]));
-  const float out = (float)(acc + (double)__fmul_rn(scores[pos], vc[i]));
-  const float g = a.projected[(long)(2 * h + 1) * hd + i];
-  a.attended[(long)h * hd + i] = __fmul_rn(out, sigmoid_f(g));
+  // value partial sums of this chunk: one dimension per thread, position order
+  {
+    double acc = -0.0;
+    const uint16_t *vcol = a.vcache + kvh * hd + i;
+    int p = lo;
+    for (; p + 4 <= hi; p += 4) {
+      const uint16_t v0 = vcol[(long)p * kvw], v1 = vcol[(long)(p + 1) * kvw];
+      const uint16_t v2 = vcol[(long)(p + 2) * kvw], v3 = vcol[(long)(p + 3) * kvw];
+      acc += (double)__fmul_rn(scores[p - lo], half_bits_to_float(v0));
+      acc += (double)__fmul_rn(scores[p + 1 - lo], half_bits_to_float(v1));
+      acc += (double)__fmul_rn(scores[p + 2 - lo], half_bits_to_float(v2));
+      acc += (double)__fmul_rn(scores[p + 3 - lo], half_bits_to_float(v3));
+    }
+    for (; p < hi; ++p) acc += (double)__fmul_rn(scores[p - lo], half_bits_to_float(vcol[(long)p * kvw]));
+    partial[i] = acc;
+  }
+  cluster.sync();
+  // CTA r finalises dimensions [r*hd/S, (r+1)*hd/S)
+  const int dims = hd / kAttnSplit;
+  if (i < dims) {
+    const int d = rank * dims + i;
+    double sum = -0.0;
+    for (int r = 0; r < kAttnSplit; ++r) sum += cluster.map_shared_rank(partial, r)[d];
+    const float out = (float)(sum + (double)__fmul_rn(p_cur, vc[d]));
+    const float g = a.projected[(long)(2 * h + 1) * hd + d];
+    a.attended[(long)h * hd + d] = __fmul_rn(out, sigmoid_f(g));
+  }
+  cluster.sync();  // peers' shared memory stays live until every read is done
 }
 
 }  // namespace prism

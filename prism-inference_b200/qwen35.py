@@ -255,3 +255,46 @@ class Qwen35Model:
         if n < 0:
             raise pb.PrismB200Error(-n, "state readback failed")
         return out
+
+    def step_timings(self):
+        """One device-driven decode step with per-phase CUDA events:
+        (attention_ms[layers], ffn_ms[layers], head_ms, total_ms)."""
+        import ctypes as c
+        L = self.L
+        if not getattr(L, "_timings_declared", False):
+            L.prism_b200_model_step_timings.restype = c.c_int
+            L.prism_b200_model_step_timings.argtypes = [c.c_void_p] * 5
+            L._timings_declared = True
+        att = np.zeros(self.cfg.layers, np.float32)
+        ffn = np.zeros(self.cfg.layers, np.float32)
+        head = np.zeros(1, np.float32)
+        tot = np.zeros(1, np.float32)
+        self.ex._check(L.prism_b200_model_step_timings(self.h, att.ctypes.data, ffn.ctypes.data,
+                                                       head.ctypes.data, tot.ctypes.data))
+        return att, ffn, float(head[0]), float(tot[0])
+
+    def stream(self):
+        """The model's cudaStream_t (an integer handle)."""
+        import ctypes as c
+        L = self.L
+        if not getattr(L, "_mstream_declared", False):
+            L.prism_b200_model_stream.restype = c.c_void_p
+            L.prism_b200_model_stream.argtypes = [c.c_void_p]
+            L._mstream_declared = True
+        return L.prism_b200_model_stream(self.h)
+
+    def set_prompt(self, tokens):
+        import ctypes as c
+        L = self.L
+        if not getattr(L, "_prompt_declared", False):
+            L.prism_b200_model_set_prompt.restype = c.c_int
+            L.prism_b200_model_set_prompt.argtypes = [c.c_void_p, c.c_void_p, c.c_size_t]
+            L.prism_b200_model_ingest_async.restype = c.c_int
+            L.prism_b200_model_ingest_async.argtypes = [c.c_void_p, c.c_size_t]
+            L._prompt_declared = True
+        t = np.ascontiguousarray(tokens, np.uint32)
+        self.ex._check(L.prism_b200_model_set_prompt(self.h, t.ctypes.data, t.size))
+
+    def ingest_async(self, n):
+        self.set_prompt  # declarations
+        self.ex._check(self.L.prism_b200_model_ingest_async(self.h, n))

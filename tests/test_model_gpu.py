@@ -1,10 +1,12 @@
 """GPU parity of the Qwen35 decode step against the CPU oracle.
 
-Projections are bit-exact given identical inputs; the floating-point steps
+Projections are bit-exact given identical inputs.  The floating-point steps
 around them (RMS/L2 norms with binary64 sums, RoPE, softmax, SiLU, sigmoid,
-decay) use CUDA's exp/log/sin/cos, which differ from the host libm by a few
-ulp, so hidden states, logits and recurrent state are compared within a
-stated tolerance:
+decay) evaluate exp/log/sin/cos in binary64 and round once, matching the
+host libm the reference uses; binary64 sums are reordered by the parallel
+reductions.  Observed differences are zero, but a rare rounding-boundary
+case is allowed for, so hidden states, logits and recurrent state are
+compared within a stated tolerance:
 
     |gpu - ref| <= ATOL + RTOL * |ref|   with RTOL = 1e-4, ATOL = 1e-4
 
@@ -89,7 +91,7 @@ def test_config1_geometry_first_tokens():
     few tokens against the oracle."""
     cfg = qwen35.CONFIG1
     ex, gm, om, _ = _pair(cfg, seed=0)
-    toks = qwen35.prompt_tokens(cfg, 3, seed=1)
+    toks = qwen35.prompt_tokens(cfg, 10, seed=1)
     for i, t in enumerate(toks):
         lg, greedy = gm.evaluate(t)
         lr = om.step(t, threads=16)

@@ -408,6 +408,112 @@ def run_matvec(args):
         print(json.dumps(line), flush=True)
 
 
+def run_gdn(args):
+    """the Gated DeltaNet kernels alone.  16 heads, d = 128,
+    fp32 state; decode = one recurrent step for B in {1, 16, 64} (HBM bound:
+    the state is read and written); prefill = 4096 tokens in chunks of 64
+    (binary32 compute bound)."""
+    import torch
+    import prism_b200 as pb
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ex = pb.ProjectionExecutor(local)
+    H, D = 16, 128
+    peak, peak_src = peaks()
+    rng = np.random.default_rng(0)
+
+    def make(batch, T):
+        q = torch.randn(batch, T, H, D, device=dev)
+        k = torch.randn(batch, T, H, D, device=dev)
+        q /= q.norm(dim=-1, keepdim=True)
+        k /= k.norm(dim=-1, keepdim=True)
+        v = torch.randn(batch, T, H, D, device=dev)
+        decay = torch.exp(-torch.nn.functional.softplus(torch.randn(batch, T, H, device=dev)))
+        beta = torch.sigmoid(torch.randn(batch, T, H, device=dev))
+        state = torch.zeros(batch, H, D, D, device=dev)
+        out = torch.zeros(batch, T, H, D, device=dev)
+        return q, k, v, decay, beta, state, out
+
+    s = torch.cuda.Stream(device=dev)
+    decode = {}
+    for batch in (1, 16, 64):
+        # rotate over enough state copies that every step misses L2
+        copies = max(2, int(300e6 // (batch * H * D * D * 4)) + 1)
+        sets = [make(batch, 1) for _ in range(copies)]
+        def step(i):
+            q, k, v, g, b, st, o = sets[i % copies]
+            pb.gdn_decode_device(ex, batch, H, H, st.data_ptr(), q.data_ptr(), k.data_ptr(),
+                                 v.data_ptr(), g.data_ptr(), b.data_ptr(), o.data_ptr(),
+                                 stream=s.cuda_stream)
+        for i in range(args.warmup):
+            step(i)
+        K = 50
+        g_ = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_, stream=s):
+            for i in range(K):
+                step(i)
+        with torch.cuda.stream(s):
+            g_.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        with torch.cuda.stream(s):
+            g_.replay()
+        e1.record(s)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / K
+        nbytes = 2 * batch * H * D * D * 4 + batch * H * D * 4 * 4 + batch * H * 8
+        decode["B%d" % batch] = {"us_per_step": us, "gbs": nbytes / us / 1e3,
+                                 "frac": nbytes / us / 1e3 / peak, "bytes": nbytes}
+        del g_, sets
+    ex.sync()
+    prefill = {}
+    T = 4096
+    for batch in (1, 16):
+        q, k, v, g, b, st, o = make(batch, T)
+        def run():
+            pb.gdn_prefill_device(ex, batch, T, H, H, 64, st.data_ptr(), q.data_ptr(),
+                                  k.data_ptr(), v.data_ptr(), g.data_ptr(), b.data_ptr(),
+                                  o.data_ptr(), stream=s.cuda_stream)
+        run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(3):
+            run()
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 3
+        # algorithmic flops of the recurrence: 3 d^2 MACs per token per head
+        # (S.k, S.q, rank-1 update) = 6 d^2 T H flops per sequence
+        flops = 6.0 * D * D * T * H * batch
+        prefill["B%d" % batch] = {"ms": ms, "tflops": flops / (ms / 1e3) / 1e12,
+                                  "tokens_per_s": batch * T / (ms / 1e3)}
+        del q, k, v, g, b, st, o
+    ex.sync()
+    ex.close()
+    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+    line = {
+        "metric": "Gated DeltaNet decode step GB/s (B=64) and chunked prefill TFLOP/s",
+        "value": decode["B64"]["gbs"], "unit": "GB/s", "n_gpus": world, "steps": 50,
+        "warmup": args.warmup, "ms_per_step": decode["B64"]["us_per_step"] / 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (configs[2] distributions)",
+        "config": {"workload": "configs[2]: 16 heads, d_k = d_v = 128, fp32 state; decode "
+                               "B in {1,16,64}; prefill T=4096 chunk 64",
+                   "l2": "decode rotates state copies > 300 MB"},
+        "decode": decode, "prefill": prefill,
+        "roofline": {"bound": "hbm", "achieved": decode["B64"]["gbs"], "peak": peak,
+                     "unit": "GB/s", "frac": decode["B64"]["frac"], "peak_source": peak_src,
+                     "kernel": "gdn_step_kernel (B=64)",
+                     "prefill_fp32_peak_tflops_nominal": fp32_peak},
+        "gpu_launches": 50,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_reference(args):
     world, rank, local = dist_setup(args.gpus)
     if rank != 0:
@@ -453,7 +559,7 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "matvec"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "matvec", "gdn"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-matvec", action="store_true", help="skip the configs[0] sub-benchmark")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens (profiling runs)")
@@ -462,6 +568,8 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "gdn":
+        run_gdn(args)
     elif args.workload == "matvec":
         run_matvec(args)
     else:

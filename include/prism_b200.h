@@ -173,6 +173,31 @@ int prism_b200_block_dots(prism_b200_executor *ex, const prism_b200_weight *w,
                           const prism_b200_q8k_block *activation,
                           int32_t *ints, int32_t *ints2);
 
+/* ---- Gated DeltaNet recurrence --------------------------------------- */
+/* For each sequence b < batch and value head h < heads (key head
+ * h % key_heads), with state rows r = value channels:
+ *   S_r <- decay*S_r; delta_r = (v_r - S_r.k)*beta; S_r += delta_r*k;
+ *   out_r = (S_r.q)/sqrt(d)
+ * (reference src/graph.rs:801-822 gdn_step_row_from, 5191-5343; batched as
+ * src/backend/gdn.rs:24-300 with the gate given as its decay).  DEVICE
+ * pointers, f32, d == 128:
+ *   state [batch][heads][d][d] (updated in place)
+ *   q, k  [batch][tokens][key_heads][d];  v, out [batch][tokens][heads][d]
+ *   decay, beta [batch][tokens][heads]
+ * decode_device runs one step (tokens = 1) with the reference's binary32
+ * products summed in binary64; prefill_device runs `tokens` steps in chunks
+ * of `chunk` (1..64) tokens with the chunkwise (WY) form of the reference's
+ * src/graph/prefill_gdn.rs:223-456, in binary32, within 1e-3 + 1e-3*|ref|
+ * of the sequential recurrence (the reference's stated chunkwise bound). */
+int prism_b200_gdn_decode_device(prism_b200_executor *ex, int batch, int heads, int key_heads,
+                                 int d, float *state, const float *q, const float *k,
+                                 const float *v, const float *decay, const float *beta,
+                                 float *out, void *stream);
+int prism_b200_gdn_prefill_device(prism_b200_executor *ex, int batch, int tokens, int heads,
+                                  int key_heads, int d, int chunk, float *state, const float *q,
+                                  const float *k, const float *v, const float *decay,
+                                  const float *beta, float *out, void *stream);
+
 /* ---- Qwen3.5-style hybrid decoder ----------------------------------- */
 /* The reference's Qwen35 graph (reference src/graph.rs:2294 `Qwen35`,
  * `impl Decoder for Qwen35` src/graph.rs:5392-5580) on the device: every

@@ -188,6 +188,22 @@ inline cudaError_t launch_matvec(const DeviceWeight &w, const void *act, float *
   return launch_matvec_group(w.kind, epi, a, num_sms, s, pdl);
 }
 
+// Launch configuration with optional programmatic dependent launch; `attr`
+// must have room for the caller's extra attributes after index 0.
+inline cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                     cudaLaunchAttribute *attr, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cfg;
+}
+
 inline cudaError_t launch_quantize(const float *x, size_t n, int pinned, void *out,
                                    unsigned *status, cudaStream_t s, bool pdl) {
   int nblocks = (int)(n / 256);
@@ -239,6 +255,7 @@ struct prism_b200_executor {
   std::string identity;
   std::string last_error;
   DeviceBuffer act, x, y, ints, ints2;
+  DeviceBuffer gdn_scratch;       // chunked GDN prefill: per-chunk M, CQ, cum, P
   std::set<prism_b200_weight *> weights;
 
   int fail(int code, const char *fmt, ...) {

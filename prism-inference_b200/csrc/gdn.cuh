@@ -1,0 +1,338 @@
+// gdn.cuh -- Gated DeltaNet recurrence kernels (decode step and chunked
+// prefill) for batches of sequences.
+//
+// Per value head h (key head h % key_heads), state rows r (value channels):
+//   S_r <- decay * S_r;  delta_r = (v_r - S_r.k) * beta;  S_r += delta_r k;
+//   o_r = (S_r . q) / sqrt(d)
+// (reference src/graph.rs:801-822 gdn_step_row_from and 5191-5343; batched
+// form of src/backend/gdn.rs:24-300 with the gate given as the decay).
+//
+// Layouts (f32, device):  state [batch][heads][d][d] (row r = value channel)
+//   q, k [batch][T][key_heads][d];  v, out [batch][T][heads][d];
+//   decay, beta [batch][T][heads].  Decode is T = 1.
+#pragma once
+
+#include "common.cuh"
+
+namespace prism {
+
+struct GdnBatchArgs {
+  int batch, T, heads, key_heads;
+  float *state;
+  const float *q, *k, *v, *decay, *beta;
+  float *out;
+  unsigned *status;
+};
+
+__device__ __forceinline__ double gdn_warp_sum(double v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// ---- decode: one recurrent step ------------------------------------------
+// grid (split, heads, batch); each CTA owns 128/split consecutive state rows
+// of one (sequence, head); a warp updates one row at a time with binary32
+// products summed in binary64 (the reference's float_dot), unfused updates.
+constexpr int kGdnStepThreads = 256;
+
+__global__ void __launch_bounds__(kGdnStepThreads) gdn_step_kernel(GdnBatchArgs a) {
+  constexpr int D = 128;
+  const int split = gridDim.x;
+  const int rows = D / split;
+  const int r0 = blockIdx.x * rows;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kh = h % a.key_heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  grid_dependency_wait();
+  grid_dependents_launch();
+  const long qk = ((long)b * a.key_heads + kh) * D;
+  const long hv = ((long)b * a.heads + h) * D;
+  const float4 kk = reinterpret_cast<const float4 *>(a.k + qk)[lane];
+  const float4 qq = reinterpret_cast<const float4 *>(a.q + qk)[lane];
+  const float decay = a.decay[(long)b * a.heads + h];
+  const float beta = a.beta[(long)b * a.heads + h];
+  const float oscale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
+  float *state = a.state + ((long)b * a.heads + h) * D * D;
+  bool finite = true;
+  for (int r = r0 + warp; r < r0 + rows; r += kGdnStepThreads / 32) {
+    float4 s = reinterpret_cast<const float4 *>(state + (long)r * D)[lane];
+    s.x = __fmul_rn(decay, s.x);
+    s.y = __fmul_rn(decay, s.y);
+    s.z = __fmul_rn(decay, s.z);
+    s.w = __fmul_rn(decay, s.w);
+    double dk = (double)__fmul_rn(s.x, kk.x) + (double)__fmul_rn(s.y, kk.y) +
+                (double)__fmul_rn(s.z, kk.z) + (double)__fmul_rn(s.w, kk.w);
+    dk = gdn_warp_sum(dk);
+    const float delta = __fmul_rn(__fsub_rn(a.v[hv + r], (float)dk), beta);
+    s.x = __fadd_rn(s.x, __fmul_rn(delta, kk.x));
+    s.y = __fadd_rn(s.y, __fmul_rn(delta, kk.y));
+    s.z = __fadd_rn(s.z, __fmul_rn(delta, kk.z));
+    s.w = __fadd_rn(s.w, __fmul_rn(delta, kk.w));
+    finite &= is_finite_f(s.x) && is_finite_f(s.y) && is_finite_f(s.z) && is_finite_f(s.w);
+    double dq = (double)__fmul_rn(s.x, qq.x) + (double)__fmul_rn(s.y, qq.y) +
+                (double)__fmul_rn(s.z, qq.z) + (double)__fmul_rn(s.w, qq.w);
+    dq = gdn_warp_sum(dq);
+    reinterpret_cast<float4 *>(state + (long)r * D)[lane] = s;
+    if (lane == 0) a.out[hv + r] = __fmul_rn((float)dq, oscale);
+  }
+  if (!__all_sync(0xffffffffu, finite) && lane == 0) report(a.status, kStatusNonfinite);
+}
+
+// ---- chunked prefill --------------------------------------------------------
+//
+// The chunkwise form of the recurrence (reference src/graph/prefill_gdn.rs:
+// 223-456, generalised to 64-token chunks).  For a chunk of C tokens:
+//   cum_t  = prod_{s<=t} decay_s,   P[t][j] = prod_{j<s<=t} decay_s
+//   CK[t][j] = P[t][j] (k_j . k_t)  (j < t),  CQ[t][j] = P[t][j] (k_j . q_t)  (j <= t)
+// and per state row r the deltas solve the unit lower-triangular system
+//   delta_t + beta_t sum_{j<t} CK[t][j] delta_j = beta_t (v_rt - cum_t S_r.k_t),
+// i.e. delta_r = M (v_r - cum o S_r K^T) with M = (I + diag(beta) CK)^-1 diag(beta).
+//   o_rt    = (cum_t S_r.q_t + sum_{j<=t} CQ[t][j] delta_rj) / sqrt(d)
+//   S_r    <- cum_{C-1} S_r + sum_j P[C-1][j] delta_rj k_j
+// A prep kernel (one CTA per chunk) writes M, CQ, cum and P[C-1] to scratch;
+// a scan kernel (one CTA per state-row group) walks the chunks in order with
+// the state rows resident in shared memory.  binary32 throughout: the
+// reference's own chunkwise form is checked against its sequential
+// recurrence within 1e-3 + 1e-3 |ref| (docs/cpu-tiled-prefill.md:173-189).
+
+constexpr int kChunk = 64;
+constexpr int kGdnD = 128;
+// shared-memory row strides: +4 floats keeps 16-byte loads of consecutive
+// rows in distinct bank groups, +1 does the same for scalar column walks
+constexpr int kKS = kGdnD + 4;
+constexpr int kMS = kChunk + 1;
+// scratch floats per (sequence, head, chunk): M, CQ, cum, P[C-1]
+constexpr int kChunkScratch = 2 * kChunk * kChunk + 2 * kChunk;
+
+struct GdnPrefillArgs {
+  GdnBatchArgs g;
+  int chunk;          // tokens per chunk (<= 64)
+  int nchunks;        // ceil(T / chunk)
+  float *scratch;     // [batch][heads][nchunks][kChunkScratch]
+};
+
+constexpr int kPrepThreads = 256;
+
+// grid (nchunks, heads, batch)
+__global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefillArgs p) {
+  constexpr int D = kGdnD, C = kChunk;
+  extern __shared__ __align__(16) float sm[];
+  float *K = sm;                 // [C][kKS]
+  float *Q = K + C * kKS;        // [C][kKS]
+  float *P = Q + C * kKS;        // [C][C+1]  decay products (padded)
+  float *Bm = P + C * (C + 1);   // [C][C+1]  beta * CK, then T
+  float *cum = Bm + C * (C + 1); // [C]
+  float *dec = cum + C;          // [C]
+  float *bet = dec + C;          // [C]
+  const GdnBatchArgs &a = p.g;
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kh = h % a.key_heads;
+  const int t0 = c * p.chunk;
+  const int n = min(p.chunk, a.T - t0);
+  grid_dependency_wait();
+  grid_dependents_launch();
+  for (int i = threadIdx.x; i < C * D / 4; i += blockDim.x) {
+    const int t = i / (D / 4), col = i % (D / 4);
+    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
+    if (t < n) {
+      const long off = (((long)b * a.T + t0 + t) * a.key_heads + kh) * D;
+      kv = reinterpret_cast<const float4 *>(a.k + off)[col];
+      qv = reinterpret_cast<const float4 *>(a.q + off)[col];
+    }
+    reinterpret_cast<float4 *>(K + t * kKS)[col] = kv;
+    reinterpret_cast<float4 *>(Q + t * kKS)[col] = qv;
+  }
+  for (int t = threadIdx.x; t < C; t += blockDim.x) {
+    const long off = ((long)b * a.T + t0 + t) * a.heads + h;
+    dec[t] = t < n ? a.decay[off] : 1.0f;
+    bet[t] = t < n ? a.beta[off] : 0.0f;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float d = 1.0f;
+    for (int t = 0; t < C; ++t) {
+      d = __fmul_rn(d, dec[t]);
+      cum[t] = d;
+    }
+  }
+  // P[t][j] = P[t][j+1] * decay_{j+1}, P[t][t] = 1 (reference order)
+  for (int t = threadIdx.x; t < C; t += blockDim.x) {
+    P[t * (C + 1) + t] = 1.0f;
+    for (int j = t - 1; j >= 0; --j)
+      P[t * (C + 1) + j] = __fmul_rn(P[t * (C + 1) + j + 1], dec[j + 1]);
+    for (int j = t + 1; j < C; ++j) P[t * (C + 1) + j] = 0.0f;
+  }
+  __syncthreads();
+  // CK (strict lower) scaled by beta_t into Bm, CQ (lower) to scratch
+  float *scr = p.scratch + (((long)b * a.heads + h) * p.nchunks + c) * kChunkScratch;
+  float *Mout = scr, *CQout = scr + C * C, *cumout = scr + 2 * C * C, *plast = cumout + C;
+  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
+    const int t = i / C, j = i % C;
+    float ck = 0.0f, cq = 0.0f;
+    if (j <= t && t < n) {
+      float dkk = 0.0f, dkq = 0.0f;
+      const float4 *kj = reinterpret_cast<const float4 *>(K + j * kKS);
+      const float4 *kt = reinterpret_cast<const float4 *>(K + t * kKS);
+      const float4 *qt = reinterpret_cast<const float4 *>(Q + t * kKS);
+#pragma unroll 4
+      for (int x = 0; x < D / 4; ++x) {
+        const float4 u = kj[x], w = kt[x], z = qt[x];
+        dkk = fmaf(u.x, w.x, fmaf(u.y, w.y, fmaf(u.z, w.z, fmaf(u.w, w.w, dkk))));
+        dkq = fmaf(u.x, z.x, fmaf(u.y, z.y, fmaf(u.z, z.z, fmaf(u.w, z.w, dkq))));
+      }
+      const float pr = P[t * (C + 1) + j];
+      cq = pr * dkq;
+      if (j < t) ck = pr * dkk;
+    }
+    Bm[t * (C + 1) + j] = bet[t] * ck;
+    CQout[i] = cq;
+  }
+  __syncthreads();
+  // T = (I + Bm)^-1 (unit lower triangular), one column per thread:
+  // T[t][j] = -sum_{k=j}^{t-1} Bm[t][k] T[k][j]; then M = T diag(beta)
+  for (int j = threadIdx.x; j < C; j += blockDim.x) {
+    float col[C];
+#pragma unroll
+    for (int t = 0; t < C; ++t) col[t] = 0.0f;
+    col[j] = 1.0f;
+    for (int t = j + 1; t < C; ++t) {
+      float s = 0.0f;
+      for (int k = j; k < t; ++k) s = fmaf(Bm[t * (C + 1) + k], col[k], s);
+      col[t] = -s;
+    }
+    for (int t = 0; t < C; ++t) Mout[t * C + j] = col[t] * bet[j];
+  }
+  for (int t = threadIdx.x; t < C; t += blockDim.x) {
+    cumout[t] = cum[t];
+    plast[t] = P[(n - 1) * (C + 1) + t];
+  }
+}
+
+__host__ __device__ constexpr size_t gdn_prep_smem() {
+  return (size_t)(2 * kChunk * kKS + 2 * kChunk * (kChunk + 1) + 3 * kChunk) * 4;
+}
+
+// Scan over the chunks of one (sequence, head) for R state rows.
+// grid (128/R, heads, batch), 256 threads.
+constexpr int kScanThreads = 256;
+
+template <int R>
+__host__ __device__ constexpr size_t gdn_scan_smem() {
+  // S[R][D] K,Q[C][kKS] M[C][kMS] CQ[C][C] V[C][R] KD,QD,DL[R][C+1] cum plast
+  return (size_t)(R * kGdnD + 2 * kChunk * kKS + kChunk * kMS + kChunk * kChunk + kChunk * R +
+                  3 * R * (kChunk + 1) + 2 * kChunk) * 4;
+}
+
+template <int R>
+__global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefillArgs p) {
+  constexpr int D = kGdnD, C = kChunk, CP = kChunk + 1;
+  extern __shared__ __align__(16) float sm[];
+  float *S = sm;                 // [R][D]
+  float *K = S + R * D;          // [C][kKS]
+  float *Q = K + C * kKS;        // [C][kKS]
+  float *M = Q + C * kKS;        // [C][kMS]
+  float *CQ = M + C * kMS;       // [C][C]
+  float *V = CQ + C * C;         // [C][R]
+  float *KD = V + C * R;         // [R][C+1]
+  float *QD = KD + R * CP;       // [R][C+1]
+  float *DL = QD + R * CP;       // [R][C+1]  deltas
+  float *cum = DL + R * CP;      // [C]
+  float *plast = cum + C;        // [C]
+  const GdnBatchArgs &a = p.g;
+  const int g = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kh = h % a.key_heads;
+  const int r0 = g * R;
+  const int tid = threadIdx.x;
+  grid_dependency_wait();
+  grid_dependents_launch();
+  float *state = a.state + ((long)b * a.heads + h) * D * D + (long)r0 * D;
+  for (int i = tid; i < R * D / 4; i += blockDim.x)
+    reinterpret_cast<float4 *>(S)[i] = reinterpret_cast<const float4 *>(state)[i];
+  const float oscale = 1.0f / sqrtf((float)D);
+  bool finite = true;
+  for (int c = 0; c < p.nchunks; ++c) {
+    const int t0 = c * p.chunk;
+    const int n = min(p.chunk, a.T - t0);
+    const float *scr = p.scratch + (((long)b * a.heads + h) * p.nchunks + c) * kChunkScratch;
+    __syncthreads();
+    for (int i = tid; i < C * D / 4; i += blockDim.x) {
+      const int t = i / (D / 4), col = i % (D / 4);
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
+      if (t < n) {
+        const long off = (((long)b * a.T + t0 + t) * a.key_heads + kh) * D;
+        kv = reinterpret_cast<const float4 *>(a.k + off)[col];
+        qv = reinterpret_cast<const float4 *>(a.q + off)[col];
+      }
+      reinterpret_cast<float4 *>(K + t * kKS)[col] = kv;
+      reinterpret_cast<float4 *>(Q + t * kKS)[col] = qv;
+    }
+    for (int i = tid; i < C * C / 4; i += blockDim.x)
+      reinterpret_cast<float4 *>(CQ)[i] = reinterpret_cast<const float4 *>(scr + C * C)[i];
+    for (int i = tid; i < C * C; i += blockDim.x) M[(i / C) * kMS + i % C] = scr[i];
+    for (int i = tid; i < C * R; i += blockDim.x) {
+      const int t = i / R, r = i % R;
+      V[i] = t < n ? a.v[(((long)b * a.T + t0 + t) * a.heads + h) * D + r0 + r] : 0.0f;
+    }
+    for (int t = tid; t < C; t += blockDim.x) {
+      cum[t] = scr[2 * C * C + t];
+      plast[t] = scr[2 * C * C + C + t];
+    }
+    __syncthreads();
+    // KD[r][t] = S_r . k_t, QD[r][t] = S_r . q_t
+    for (int i = tid; i < R * C; i += blockDim.x) {
+      const int r = i / C, t = i % C;
+      const float4 *sr = reinterpret_cast<const float4 *>(S + r * D);
+      const float4 *kt = reinterpret_cast<const float4 *>(K + t * kKS);
+      const float4 *qt = reinterpret_cast<const float4 *>(Q + t * kKS);
+      float dk = 0.0f, dq = 0.0f;
+#pragma unroll 4
+      for (int x = 0; x < D / 4; ++x) {
+        const float4 s = sr[x], u = kt[x], w = qt[x];
+        dk = fmaf(s.x, u.x, fmaf(s.y, u.y, fmaf(s.z, u.z, fmaf(s.w, u.w, dk))));
+        dq = fmaf(s.x, w.x, fmaf(s.y, w.y, fmaf(s.z, w.z, fmaf(s.w, w.w, dq))));
+      }
+      KD[r * CP + t] = dk;
+      QD[r * CP + t] = dq;
+    }
+    __syncthreads();
+    // W[r][t] = v_rt - cum_t KD[r][t]  (in place into KD)
+    for (int i = tid; i < R * C; i += blockDim.x) {
+      const int r = i / C, t = i % C;
+      KD[r * CP + t] = V[t * R + r] - cum[t] * KD[r * CP + t];
+    }
+    __syncthreads();
+    // delta[r][t] = sum_{j<=t} M[t][j] W[r][j]
+    for (int i = tid; i < R * C; i += blockDim.x) {
+      const int r = i / C, t = i % C;
+      float s = 0.0f;
+      for (int j = 0; j <= t; ++j) s = fmaf(M[t * kMS + j], KD[r * CP + j], s);
+      DL[r * CP + t] = t < n ? s : 0.0f;
+    }
+    __syncthreads();
+    // o[r][t] = (cum_t QD[r][t] + sum_{j<=t} CQ[t][j] delta[r][j]) / sqrt(d)
+    for (int i = tid; i < R * C; i += blockDim.x) {
+      const int t = i / R, r = i % R;  // r fastest: coalesced output stores
+      if (t < n) {
+        float s = cum[t] * QD[r * CP + t];
+        for (int j = 0; j <= t; ++j) s = fmaf(CQ[t * C + j], DL[r * CP + j], s);
+        a.out[(((long)b * a.T + t0 + t) * a.heads + h) * D + r0 + r] = s * oscale;
+      }
+    }
+    // S_r <- cum_last S_r + sum_j plast_j delta_rj k_j
+    const float last = cum[n - 1];
+    for (int i = tid; i < R * D; i += blockDim.x) {
+      const int r = i / D, x = i % D;
+      float s = last * S[i];
+      for (int j = 0; j < n; ++j) s = fmaf(plast[j] * DL[r * CP + j], K[j * kKS + x], s);
+      finite &= is_finite_f(s);
+      S[i] = s;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < R * D / 4; i += blockDim.x)
+    reinterpret_cast<float4 *>(state)[i] = reinterpret_cast<const float4 *>(S)[i];
+  if (!__syncthreads_and(finite) && tid == 0) report(a.status, kStatusNonfinite);
+}
+
+}  // namespace prism

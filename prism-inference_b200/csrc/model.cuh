@@ -75,20 +75,6 @@ cudaError_t model_alloc(prism_b200_model *m, T **p, size_t count) {
   return e;
 }
 
-inline cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-                                     cudaLaunchAttribute *attr, bool pdl) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cfg;
-}
-
 inline StepState step_state(prism_b200_model *m) {
   StepState st;
   st.position = m->d_position;

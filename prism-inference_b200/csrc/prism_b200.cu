@@ -13,6 +13,7 @@
 
 #include "common.cuh"
 #include "executor.cuh"
+#include "gdn.cuh"
 
 using namespace prism;
 
@@ -134,6 +135,7 @@ void prism_b200_executor_destroy(prism_b200_executor *ex) {
   ex->y.release();
   ex->ints.release();
   ex->ints2.release();
+  ex->gdn_scratch.release();
   if (ex->d_status) cudaFree(ex->d_status);
   if (ex->h_status) cudaFreeHost(ex->h_status);
   if (ex->stream) cudaStreamDestroy(ex->stream);
@@ -382,6 +384,113 @@ int prism_b200_block_dots(prism_b200_executor *ex, const prism_b200_weight *w,
   if (w->dw.kind == PRISM_B200_KIND_Q2_K)
     CK(cudaMemcpyAsync(ints2, ex->ints2.ptr, ibytes, cudaMemcpyDeviceToHost, s), "ints copy");
   return finish(ex, s);
+}
+
+// ---- Gated DeltaNet recurrence ---------------------------------------------
+
+static int gdn_check(prism_b200_executor *ex, int batch, int tokens, int heads, int key_heads,
+                     int d, const void *const *ptrs, int n) {
+  if (batch <= 0 || tokens <= 0 || heads <= 0 || key_heads <= 0 || heads % key_heads ||
+      batch > 65535 || heads > 65535)
+    return ex->fail(PRISM_B200_E_INVALID, "invalid GDN geometry");
+  if (d != kGdnD) return ex->fail(PRISM_B200_E_UNSUPPORTED, "GDN head width must be 128");
+  for (int i = 0; i < n; ++i)
+    if (!ptrs[i] || reinterpret_cast<uintptr_t>(ptrs[i]) % 16)
+      return ex->fail(PRISM_B200_E_INVALID, "GDN buffers must be 16-byte aligned device memory");
+  return PRISM_B200_OK;
+}
+
+extern "C" int prism_b200_gdn_decode_device(prism_b200_executor *ex, int batch, int heads,
+                                            int key_heads, int d, float *state, const float *q,
+                                            const float *k, const float *v, const float *decay,
+                                            const float *beta, float *out, void *stream) {
+  int st = check_open(ex);
+  if (st) return st;
+  const void *ptrs[] = {state, q, k, v, out};
+  if ((st = gdn_check(ex, batch, 1, heads, key_heads, d, ptrs, 5))) return st;
+  if (!decay || !beta) return ex->fail(PRISM_B200_E_INVALID, "null gate buffer");
+  cudaSetDevice(ex->device);
+  GdnBatchArgs a;
+  a.batch = batch;
+  a.T = 1;
+  a.heads = heads;
+  a.key_heads = key_heads;
+  a.state = state;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.decay = decay;
+  a.beta = beta;
+  a.out = out;
+  a.status = ex->d_status;
+  // split each head's 128 rows so that the grid covers every SM twice
+  int split = 1;
+  while (split < 16 && (long)batch * heads * split < 2L * ex->num_sms) split *= 2;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_config(dim3(split, heads, batch), dim3(kGdnStepThreads), 0,
+                                      pick(ex, stream), attr, ex->pdl);
+  CK(cudaLaunchKernelEx(&cfg, gdn_step_kernel, a), "GDN decode launch");
+  return PRISM_B200_OK;
+}
+
+extern "C" int prism_b200_gdn_prefill_device(prism_b200_executor *ex, int batch, int tokens,
+                                             int heads, int key_heads, int d, int chunk,
+                                             float *state, const float *q, const float *k,
+                                             const float *v, const float *decay,
+                                             const float *beta, float *out, void *stream) {
+  int st = check_open(ex);
+  if (st) return st;
+  const void *ptrs[] = {state, q, k, v, out};
+  if ((st = gdn_check(ex, batch, tokens, heads, key_heads, d, ptrs, 5))) return st;
+  if (!decay || !beta) return ex->fail(PRISM_B200_E_INVALID, "null gate buffer");
+  if (chunk < 1 || chunk > kChunk)
+    return ex->fail(PRISM_B200_E_INVALID, "GDN chunk must be 1..%d tokens", kChunk);
+  cudaSetDevice(ex->device);
+  GdnPrefillArgs p;
+  p.g.batch = batch;
+  p.g.T = tokens;
+  p.g.heads = heads;
+  p.g.key_heads = key_heads;
+  p.g.state = state;
+  p.g.q = q;
+  p.g.k = k;
+  p.g.v = v;
+  p.g.decay = decay;
+  p.g.beta = beta;
+  p.g.out = out;
+  p.g.status = ex->d_status;
+  p.chunk = chunk;
+  p.nchunks = (tokens + chunk - 1) / chunk;
+  const size_t scratch = (size_t)batch * heads * p.nchunks * kChunkScratch * sizeof(float);
+  CK(ex->gdn_scratch.ensure(scratch), "GDN scratch");
+  p.scratch = static_cast<float *>(ex->gdn_scratch.ptr);
+  cudaStream_t s = pick(ex, stream);
+  cudaLaunchAttribute attr[1];
+  const size_t prep_smem = gdn_prep_smem();
+  CK(cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          (int)prep_smem),
+     "GDN prep attribute");
+  cudaLaunchConfig_t cfg = pdl_config(dim3(p.nchunks, heads, batch), dim3(kPrepThreads),
+                                      prep_smem, s, attr, ex->pdl);
+  CK(cudaLaunchKernelEx(&cfg, gdn_chunk_prep_kernel, p), "GDN prep launch");
+  // 16 rows per CTA while few (sequence, head) pairs exist, else 64
+  const bool wide = (long)batch * heads * 2 >= ex->num_sms;
+  if (wide) {
+    const size_t smem = gdn_scan_smem<64>();
+    CK(cudaFuncSetAttribute(gdn_chunk_scan_kernel<64>,
+                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+       "GDN scan attribute");
+    cfg = pdl_config(dim3(kGdnD / 64, heads, batch), dim3(kScanThreads), smem, s, attr, ex->pdl);
+    CK(cudaLaunchKernelEx(&cfg, gdn_chunk_scan_kernel<64>, p), "GDN scan launch");
+  } else {
+    const size_t smem = gdn_scan_smem<16>();
+    CK(cudaFuncSetAttribute(gdn_chunk_scan_kernel<16>,
+                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+       "GDN scan attribute");
+    cfg = pdl_config(dim3(kGdnD / 16, heads, batch), dim3(kScanThreads), smem, s, attr, ex->pdl);
+    CK(cudaLaunchKernelEx(&cfg, gdn_chunk_scan_kernel<16>, p), "GDN scan launch");
+  }
+  return PRISM_B200_OK;
 }
 
 }  // extern "C"

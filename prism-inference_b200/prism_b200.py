@@ -277,3 +277,32 @@ class ProjectionExecutor:
         ints2 = np.zeros((w.rows, nb), dtype=np.int32)
         self._check(load().prism_b200_block_dots(self.h, w.handle, _p(act), _p(ints), _p(ints2)))
         return ints if w.kind == KIND_TQ2_0 else (ints, ints2)
+
+
+def _declare_gdn(L):
+    if getattr(L, "_gdn_declared", False):
+        return
+    vp, i32 = ctypes.c_void_p, ctypes.c_int
+    L.prism_b200_gdn_decode_device.restype = i32
+    L.prism_b200_gdn_decode_device.argtypes = [vp, i32, i32, i32, i32] + [vp] * 8
+    L.prism_b200_gdn_prefill_device.restype = i32
+    L.prism_b200_gdn_prefill_device.argtypes = [vp, i32, i32, i32, i32, i32, i32] + [vp] * 8
+    L._gdn_declared = True
+
+
+def gdn_decode_device(ex, batch, heads, key_heads, state, q, k, v, decay, beta, out, stream=None,
+                      d=128):
+    """One Gated DeltaNet step over device buffers (integer pointers)."""
+    L = load()
+    _declare_gdn(L)
+    ex._check(L.prism_b200_gdn_decode_device(ex.h, batch, heads, key_heads, d, state, q, k, v,
+                                             decay, beta, out, stream))
+
+
+def gdn_prefill_device(ex, batch, tokens, heads, key_heads, chunk, state, q, k, v, decay, beta,
+                       out, stream=None, d=128):
+    """Chunked Gated DeltaNet prefill over device buffers."""
+    L = load()
+    _declare_gdn(L)
+    ex._check(L.prism_b200_gdn_prefill_device(ex.h, batch, tokens, heads, key_heads, d, chunk,
+                                              state, q, k, v, decay, beta, out, stream))

@@ -198,6 +198,26 @@ int prism_b200_gdn_prefill_device(prism_b200_executor *ex, int batch, int tokens
                                   const float *k, const float *v, const float *decay,
                                   const float *beta, float *out, void *stream);
 
+/* Same computation and arguments as prism_b200_gdn_prefill_device, but it
+ * never allocates device memory.  This entry point has no counterpart in
+ * the reference.  It is for hosts that cannot let a library allocate:
+ * processes that reserved all device memory up front, and loops that cannot
+ * take the device-wide synchronisation of an allocation.  Its chunk scratch
+ * is a fixed array in the library's device image, of
+ * PRISM_B200_GDN_STATIC_SCRATCH_BYTES; a call needing more
+ * (batch x heads x ceil(tokens/chunk) x 33,280 bytes) fails with
+ * PRISM_B200_E_INVALID before anything is enqueued.  The first call on a
+ * device looks the array's address up (cudaGetSymbolAddress), so make that
+ * first call before any stream capture.  All callers on a device share the
+ * array: calls whose kernels can overlap in time (other streams, other
+ * executors) race and must be serialised by the caller. */
+#define PRISM_B200_GDN_STATIC_SCRATCH_BYTES (32u * 1024u * 1024u)
+int prism_b200_gdn_prefill_device_noalloc(prism_b200_executor *ex, int batch, int tokens,
+                                          int heads, int key_heads, int d, int chunk,
+                                          float *state, const float *q, const float *k,
+                                          const float *v, const float *decay,
+                                          const float *beta, float *out, void *stream);
+
 /* ---- Qwen3.5-style hybrid decoder ----------------------------------- */
 /* The reference's Qwen35 graph (reference src/graph.rs:2294 `Qwen35`,
  * `impl Decoder for Qwen35` src/graph.rs:5392-5580) on the device: every

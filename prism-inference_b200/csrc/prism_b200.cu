@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -494,6 +495,116 @@ extern "C" int prism_b200_gdn_prefill_device(prism_b200_executor *ex, int batch,
 }
 
 }  // extern "C"
+
+// ---- GDN prefill with no device allocation ---------------------------------
+// Some hosts cannot let a library allocate device memory behind their back:
+// a serving process that reserved all of HBM up front for weights and KV
+// pages has none left to give, and a decode loop with a latency budget
+// cannot absorb the device-wide synchronisation that cudaMalloc implies.
+// This variant of prism_b200_gdn_prefill_device keeps its chunk scratch in
+// a fixed module-scope array instead of the executor's growable buffer.  The
+// prep kernel writes every scratch element that the scan kernel reads, so
+// nothing has to start at zero.  The array is shared by every caller on a
+// device: two calls whose kernels overlap in time (different streams, or
+// different executors on one device) race on it.
+namespace {
+
+constexpr size_t kStaticGdnScratchFloats = (size_t)PRISM_B200_GDN_STATIC_SCRATCH_BYTES / 4;
+static_assert(PRISM_B200_GDN_STATIC_SCRATCH_BYTES % 256 == 0, "scratch size");
+
+__device__ __align__(256) float g_static_gdn_scratch[kStaticGdnScratchFloats];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_gdn_mu;
+float *g_static_gdn_ptr[kMaxDevices] = {};
+
+// Device address of the array on `device`, looked up on the first call for
+// that device (with the device current) and cached; null on failure.
+float *static_gdn_scratch(int device, cudaError_t *err) {
+  *err = cudaSuccess;
+  if (device < 0 || device >= kMaxDevices) {
+    *err = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_static_gdn_mu);
+  if (!g_static_gdn_ptr[device]) {
+    void *ptr = nullptr;
+    *err = cudaGetSymbolAddress(&ptr, g_static_gdn_scratch);
+    if (*err != cudaSuccess) return nullptr;
+    g_static_gdn_ptr[device] = static_cast<float *>(ptr);
+  }
+  return g_static_gdn_ptr[device];
+}
+
+}  // namespace
+
+extern "C" int prism_b200_gdn_prefill_device_noalloc(prism_b200_executor *ex, int batch,
+                                                     int tokens, int heads, int key_heads, int d,
+                                                     int chunk, float *state, const float *q,
+                                                     const float *k, const float *v,
+                                                     const float *decay, const float *beta,
+                                                     float *out, void *stream) {
+  int st = check_open(ex);
+  if (st) return st;
+  const void *ptrs[] = {state, q, k, v, out};
+  if ((st = gdn_check(ex, batch, tokens, heads, key_heads, d, ptrs, 5))) return st;
+  if (!decay || !beta) return ex->fail(PRISM_B200_E_INVALID, "null gate buffer");
+  if (chunk < 1 || chunk > kChunk)
+    return ex->fail(PRISM_B200_E_INVALID, "GDN chunk must be 1..%d tokens", kChunk);
+  const long nchunks = (tokens + chunk - 1) / chunk;
+  const size_t need = (size_t)batch * heads * nchunks * kChunkScratch;
+  if (need > kStaticGdnScratchFloats)
+    return ex->fail(PRISM_B200_E_INVALID,
+                    "GDN no-alloc prefill needs %zu scratch bytes (batch %d x heads %d x %ld "
+                    "chunks x %d B); the fixed scratch holds %zu",
+                    need * 4, batch, heads, nchunks, kChunkScratch * 4,
+                    (size_t)PRISM_B200_GDN_STATIC_SCRATCH_BYTES);
+  CK(cudaSetDevice(ex->device), "select device");
+  cudaError_t e;
+  float *scratch = static_gdn_scratch(ex->device, &e);
+  if (!scratch) return cuda_fail(ex, e, "GDN fixed scratch address");
+  GdnPrefillArgs p;
+  p.g.batch = batch;
+  p.g.T = tokens;
+  p.g.heads = heads;
+  p.g.key_heads = key_heads;
+  p.g.state = state;
+  p.g.q = q;
+  p.g.k = k;
+  p.g.v = v;
+  p.g.decay = decay;
+  p.g.beta = beta;
+  p.g.out = out;
+  p.g.status = ex->d_status;
+  p.chunk = chunk;
+  p.nchunks = (int)nchunks;
+  p.scratch = scratch;
+  cudaStream_t s = pick(ex, stream);
+  cudaLaunchAttribute attr[1];
+  const size_t prep_smem = gdn_prep_smem();
+  CK(cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          (int)prep_smem),
+     "GDN prep attribute");
+  cudaLaunchConfig_t cfg = pdl_config(dim3(p.nchunks, heads, batch), dim3(kPrepThreads),
+                                      prep_smem, s, attr, ex->pdl);
+  CK(cudaLaunchKernelEx(&cfg, gdn_chunk_prep_kernel, p), "GDN prep launch");
+  if ((long)batch * heads * 2 >= ex->num_sms) {
+    const size_t smem = gdn_scan_smem<64>();
+    CK(cudaFuncSetAttribute(gdn_chunk_scan_kernel<64>,
+                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+       "GDN scan attribute");
+    cfg = pdl_config(dim3(kGdnD / 64, heads, batch), dim3(kScanThreads), smem, s, attr, ex->pdl);
+    CK(cudaLaunchKernelEx(&cfg, gdn_chunk_scan_kernel<64>, p), "GDN scan launch");
+  } else {
+    const size_t smem = gdn_scan_smem<16>();
+    CK(cudaFuncSetAttribute(gdn_chunk_scan_kernel<16>,
+                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+       "GDN scan attribute");
+    cfg = pdl_config(dim3(kGdnD / 16, heads, batch), dim3(kScanThreads), smem, s, attr, ex->pdl);
+    CK(cudaLaunchKernelEx(&cfg, gdn_chunk_scan_kernel<16>, p), "GDN scan launch");
+  }
+  return PRISM_B200_OK;
+}
 
 // The model entry points share this translation unit's kernels and helpers.
 #include "model.cuh"

@@ -287,6 +287,8 @@ def _declare_gdn(L):
     L.prism_b200_gdn_decode_device.argtypes = [vp, i32, i32, i32, i32] + [vp] * 8
     L.prism_b200_gdn_prefill_device.restype = i32
     L.prism_b200_gdn_prefill_device.argtypes = [vp, i32, i32, i32, i32, i32, i32] + [vp] * 8
+    L.prism_b200_gdn_prefill_device_noalloc.restype = i32
+    L.prism_b200_gdn_prefill_device_noalloc.argtypes = [vp, i32, i32, i32, i32, i32, i32] + [vp] * 8
     L._gdn_declared = True
 
 
@@ -306,3 +308,19 @@ def gdn_prefill_device(ex, batch, tokens, heads, key_heads, chunk, state, q, k, 
     _declare_gdn(L)
     ex._check(L.prism_b200_gdn_prefill_device(ex.h, batch, tokens, heads, key_heads, d, chunk,
                                               state, q, k, v, decay, beta, out, stream))
+
+
+# Size of the fixed scratch of gdn_prefill_device_noalloc (include/prism_b200.h).
+GDN_STATIC_SCRATCH_BYTES = 32 * 1024 * 1024
+
+
+def gdn_prefill_device_noalloc(ex, batch, tokens, heads, key_heads, chunk, state, q, k, v, decay,
+                               beta, out, stream=None, d=128):
+    """gdn_prefill_device without any device allocation: its scratch is a
+    fixed array of GDN_STATIC_SCRATCH_BYTES, shared by all callers on the
+    device (overlapping calls race)."""
+    L = load()
+    _declare_gdn(L)
+    ex._check(L.prism_b200_gdn_prefill_device_noalloc(ex.h, batch, tokens, heads, key_heads, d,
+                                                      chunk, state, q, k, v, decay, beta, out,
+                                                      stream))

@@ -1,0 +1,101 @@
+"""GDN prefill through the no-allocation entry point.
+
+prism_b200_gdn_prefill_device_noalloc must give what
+prism_b200_gdn_prefill_device gives on the same inputs (within the chunkwise
+bound 1e-3 + 1e-3*|ref| used for the prefill tests), on consecutive calls
+that reuse its fixed scratch, and must refuse a call whose scratch would not
+fit before anything is enqueued.  The file name sorts last so that the test
+also runs after every other test in one process.
+"""
+import numpy as np
+import pytest
+import torch
+
+import prism_b200 as pb
+
+pytestmark = pytest.mark.gpu
+
+D = 128
+CHUNK_SCRATCH_BYTES = (2 * 64 * 64 + 128) * 4
+
+
+def inputs(batch, T, heads, key_heads, seed):
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((batch, T, key_heads, D)).astype(np.float32)
+    k = rng.standard_normal((batch, T, key_heads, D)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=-1, keepdims=True)
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = rng.standard_normal((batch, T, heads, D)).astype(np.float32)
+    decay = np.exp(-np.log1p(np.exp(rng.standard_normal((batch, T, heads))))).astype(np.float32)
+    beta = (1.0 / (1.0 + np.exp(-rng.standard_normal((batch, T, heads))))).astype(np.float32)
+    return [torch.from_numpy(a).cuda() for a in (q, k, v, decay, beta)]
+
+
+def close(got, ref):
+    return bool(torch.all((got - ref).abs() <= 1e-3 + 1e-3 * ref.abs()))
+
+
+@pytest.fixture(scope="module")
+def ex():
+    e = pb.ProjectionExecutor(0)
+    yield e
+    e.close()
+
+
+def run(ex, fn, batch, T, heads, key_heads, chunk, state, ins):
+    q, k, v, decay, beta = ins
+    out = torch.zeros((batch, T, heads, D), device="cuda")
+    fn(ex, batch, T, heads, key_heads, chunk, state.data_ptr(), q.data_ptr(), k.data_ptr(),
+       v.data_ptr(), decay.data_ptr(), beta.data_ptr(), out.data_ptr())
+    ex.sync()
+    torch.cuda.synchronize()
+    return out
+
+
+def test_consecutive_calls_match_allocating_entry_point(ex):
+    # two consecutive calls of different geometry: the second reuses the
+    # fixed scratch the first left behind and continues from its state
+    calls = [(2, 200, 4, 4, 64, 11), (2, 300, 4, 2, 37, 12)]
+    g = torch.Generator().manual_seed(5)
+    s_ref = (torch.randn((2, 4, D, D), generator=g) * 0.1).cuda()
+    s_fix = s_ref.clone()
+    for batch, T, heads, key_heads, chunk, seed in calls:
+        ins = inputs(batch, T, heads, key_heads, seed)
+        o_ref = run(ex, pb.gdn_prefill_device, batch, T, heads, key_heads, chunk, s_ref, ins)
+        o_fix = run(ex, pb.gdn_prefill_device_noalloc, batch, T, heads, key_heads, chunk, s_fix,
+                    ins)
+        assert torch.isfinite(o_fix).all()
+        assert close(o_fix, o_ref), (T, chunk)
+        assert close(s_fix, s_ref), (T, chunk)
+
+
+def test_largest_fitting_call_and_refusal_beyond(ex):
+    units = pb.GDN_STATIC_SCRATCH_BYTES // CHUNK_SCRATCH_BYTES   # (sequence, head, chunk) units
+    assert units == 1008
+    # exactly at the limit: one 64-token chunk for `units` heads
+    heads, T = units, 64
+    ins = inputs(1, T, heads, 1, 21)
+    s_ref = (torch.randn((1, heads, D, D), generator=torch.Generator().manual_seed(6)) * 0.1).cuda()
+    s_fix = s_ref.clone()
+    o_ref = run(ex, pb.gdn_prefill_device, 1, T, heads, 1, 64, s_ref, ins)
+    o_fix = run(ex, pb.gdn_prefill_device_noalloc, 1, T, heads, 1, 64, s_fix, ins)
+    assert close(o_fix, o_ref) and close(s_fix, s_ref)
+    del ins, s_ref, o_ref
+    # one head more does not fit: refused on the host, nothing enqueued, the
+    # buffers are sized for the call all the same
+    heads += 1
+    ins = inputs(1, T, heads, 1, 22)
+    state = torch.zeros((1, heads, D, D), device="cuda")
+    before = state.clone()
+    with pytest.raises(pb.PrismB200Error) as err:
+        run(ex, pb.gdn_prefill_device_noalloc, 1, T, heads, 1, 64, state, ins)
+    assert err.value.code == pb.E_INVALID
+    assert "scratch" in str(err.value)
+    assert torch.equal(state, before)
+    # the executor stays usable after the refusal
+    ins = inputs(2, 100, 4, 4, 23)
+    s_ref = torch.zeros((2, 4, D, D), device="cuda")
+    s_fix = s_ref.clone()
+    o_ref = run(ex, pb.gdn_prefill_device, 2, 100, 4, 4, 64, s_ref, ins)
+    o_fix = run(ex, pb.gdn_prefill_device_noalloc, 2, 100, 4, 4, 64, s_fix, ins)
+    assert close(o_fix, o_ref) and close(s_fix, s_ref)

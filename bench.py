@@ -514,6 +514,131 @@ def run_gdn(args):
         print(json.dumps(line), flush=True)
 
 
+GEMM_M = 2048
+GEMM_SHAPES = [(2560, 9216), (9216, 2560)]   # (K, N): gate/up and down
+GEMM_METRIC = "prefill GEMM int-op/s (2048 tokens x Q8_K, TQ2_0 and Q2_K weights)"
+
+
+def int8_peak():
+    """Dense int8 tensor peak: not in MEASURED_PEAKS.json; B200's dense int8
+    rate is twice its dense bf16 rate, so twice the measured bf16 burst."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            bf16 = json.load(f).get("bf16_tflops")
+        if bf16:
+            return 2.0 * float(bf16), "2 x measured bf16 dense burst (MEASURED_PEAKS.json bf16_tflops)"
+    return 2.0 * 1590.0, "2 x fallback bf16 1.59 PFLOP/s"
+
+
+def cpu_gemm_baseline(seconds=15.0):
+    """Oracle per-token tile dots (reference src/kernels/prefill.rs:48-87) on
+    all host cores for a sample of tokens of the gate/up shape."""
+    from oracle import oracle
+    import synth
+    K, N = GEMM_SHAPES[0]
+    w = synth.tq2_weights(N, K, 3)
+    threads = os.cpu_count()
+    n_tok = 8
+    x = np.random.default_rng(4).standard_normal((n_tok, K)).astype(np.float32)
+    oracle.project_tokens(35, w, N, K, x, threads=threads)
+    t0, n = time.perf_counter(), 0
+    while time.perf_counter() - t0 < seconds:
+        oracle.project_tokens(35, w, N, K, x, threads=threads)
+        n += n_tok
+    dt = time.perf_counter() - t0
+    ops = 2.0 * K * N * n
+    return {"value": ops / dt / 1e12, "unit": "Tint-op/s", "cores": threads, "kind": "port",
+            "sample": "%d tokens of the (K=%d, N=%d) TQ2_0 projection in 32-token tiles, %.1f s"
+                      % (n, K, N, dt)}
+
+
+def run_gemm(args):
+    """multi-token projection on the tensor cores.  2048 tokens,
+    (K, N) = (2560, 9216) and (9216, 2560), TQ2_0 and Q2_K weights,
+    activations N(0,1) -> Q8_K on the device, f32 outputs."""
+    import torch
+    import prism_b200 as pb
+    import synth
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ex = pb.ProjectionExecutor(local)
+    s = torch.cuda.Stream(device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)   # > 126 MB L2
+    steps = min(args.steps, 20)
+    results, total_ops, total_ms = {}, 0.0, 0.0
+    launches = 0
+    for kind, name in ((35, "tq2_0"), (10, "q2_k")):
+        for K, N in GEMM_SHAPES:
+            w = synth.tq2_weights(N, K, 3) if kind == 35 else synth.q2k_weights(N, K, 3)
+            wt = ex.upload(pb.Tensor(kind, K, N, w))
+            x = torch.randn(GEMM_M, K, device=dev)
+            y = torch.empty(GEMM_M, N, device=dev)
+            def run():
+                ex.project_f32_tokens_device(wt, GEMM_M, x.data_ptr(), y.data_ptr(),
+                                             stream=s.cuda_stream)
+            for _ in range(args.warmup):
+                run()
+            ex.sync()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(steps)]
+            with torch.cuda.stream(s):
+                for e0, e1 in ev:
+                    flush.zero_()
+                    e0.record(s)
+                    run()
+                    e1.record(s)
+            torch.cuda.synchronize()
+            ex.sync()
+            ms = float(np.mean([e0.elapsed_time(e1) for e0, e1 in ev]))
+            ops = 2.0 * GEMM_M * K * N
+            results["%s_K%d_N%d" % (name, K, N)] = {"ms": ms, "tops": ops / ms / 1e9}
+            total_ops += ops
+            total_ms += ms
+            launches += 2 * steps
+            del wt, x, y
+    # end to end through the host-buffer entry point (gate/up, TQ2_0)
+    K, N = GEMM_SHAPES[0]
+    w = synth.tq2_weights(N, K, 3)
+    t = pb.Tensor(35, K, N, w)
+    xh = np.random.default_rng(4).standard_normal((GEMM_M, K)).astype(np.float32)
+    ex.project_f32_tokens(t, xh)
+    t0 = time.perf_counter()
+    reps = 5
+    for _ in range(reps):
+        ex.project_f32_tokens(t, xh)
+    e2e_s = (time.perf_counter() - t0) / reps
+    ex.close()
+    peak, peak_src = int8_peak()
+    value = total_ops / total_ms / 1e9
+    value = max_over_ranks(value, world, dev) if world > 1 else value
+    top = results["tq2_0_K2560_N9216"]
+    line = {
+        "metric": GEMM_METRIC, "value": value * world, "unit": "Tint-op/s", "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": total_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "i8 x u8 -> i32, f32 chain", "data": "synthetic (configs[3] distributions)",
+        "config": {"workload": "configs[3]: M=2048 tokens, (K,N) in {(2560,9216),(9216,2560)}, "
+                               "TQ2_0 and Q2_K; a step = the four GEMMs",
+                   "l2": "a 256 MB buffer is written between timed launches"},
+        "gemms": results,
+        "roofline": {"bound": "tensor", "achieved": top["tops"], "peak": peak,
+                     "unit": "Tint-op/s", "frac": top["tops"] / peak, "peak_source": peak_src,
+                     "kernel": "gemm_tokens_kernel<35> (K=2560, N=9216) incl. the Q8_K token "
+                               "quantize launch",
+                     "traffic": traffic_from_profiles("gemm_tokens_kernel")},
+        "gpu_launches": launches,
+        "e2e": {"value": 2.0 * GEMM_M * K * N / e2e_s / 1e12, "unit": "Tint-op/s",
+                "h2d_bytes_per_step": GEMM_M * K * 4, "d2h_bytes_per_step": GEMM_M * N * 4,
+                "api": "prism_b200_project_f32_tokens (host buffers), TQ2_0 K=2560 N=9216"},
+    }
+    if rank == 0 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_gemm_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_reference(args):
     world, rank, local = dist_setup(args.gpus)
     if rank != 0:
@@ -559,7 +684,7 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "matvec", "gdn"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "matvec", "gdn", "gemm"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-matvec", action="store_true", help="skip the configs[0] sub-benchmark")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens (profiling runs)")
@@ -570,6 +695,8 @@ def main():
         run_reference(args)
     elif args.workload == "gdn":
         run_gdn(args)
+    elif args.workload == "gemm":
+        run_gemm(args)
     elif args.workload == "matvec":
         run_matvec(args)
     else:

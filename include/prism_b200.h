@@ -156,6 +156,21 @@ int prism_b200_project_f32_group(prism_b200_executor *ex, size_t count,
                                  const float *x, int pinned,
                                  float *const *outs);
 
+/* One projection over a tile of token activations: x is [tokens][cols]
+ * f32, out is [tokens][rows] f32 (reference src/kernels/projection.rs:
+ * 137-153 `project_f32_tokens`, whose default runs `project_f32` per token;
+ * the tiled prefill of src/kernels/prefill.rs:48-87 `dot_quantized_tile_row`
+ * computes the same per-token dots).  Each token is quantized to Q8_K on
+ * the device and every output equals what prism_b200_project_f32 gives for
+ * that token alone, bit for bit.  The integer block dots run on the tensor
+ * cores (tcgen05.mma kind::i8, 128 tokens x 128 rows per tile).
+ * tokens <= 65536; x_dev 16-byte aligned. */
+int prism_b200_project_f32_tokens(prism_b200_executor *ex, const prism_b200_weight *w,
+                                  size_t tokens, const float *x, int pinned, float *out);
+int prism_b200_project_f32_tokens_device(prism_b200_executor *ex, const prism_b200_weight *w,
+                                         size_t tokens, const float *x_dev, int pinned,
+                                         float *out_dev, void *stream);
+
 /* Q8_K activation quantization of n floats (n % 256 == 0)
  * (reference src/kernels.rs:463-522 `q8k_with_input`). */
 int prism_b200_quantize_q8k(prism_b200_executor *ex, const float *x, size_t n,

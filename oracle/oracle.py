@@ -54,6 +54,7 @@ def _declare(L):
         "po_q2k_block_dots": (i32, [vp, vp, sz, vp, vp]),
         "po_q2k_dot": (i32, [vp, vp, sz, vp]),
         "po_matvec": (i32, [u32, vp, sz, sz, vp, vp, i32]),
+        "po_project_tokens": (i32, [u32, vp, sz, sz, vp, sz, i32, vp, i32]),
         "po_float_dot": (f32, [vp, vp, sz]),
         "po_f16_dot": (f32, [vp, vp, sz]),
         "po_silu": (f32, [f32]),
@@ -142,6 +143,16 @@ def matvec(kind, weights, rows, cols, act, threads=1):
     act = np.ascontiguousarray(act, dtype=Q8K_DTYPE)
     y = np.zeros(rows, dtype=np.float32)
     _check(lib().po_matvec(kind, _p(weights), rows, cols, _p(act), _p(y), threads))
+    return y
+
+
+def project_tokens(kind, weights, rows, cols, x, pinned=False, threads=1):
+    """y [tokens][rows]: every token quantized to Q8_K and projected."""
+    weights = np.ascontiguousarray(weights, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, cols)
+    y = np.zeros((x.shape[0], rows), dtype=np.float32)
+    _check(lib().po_project_tokens(kind, _p(weights), rows, cols, _p(x), x.shape[0],
+                                   int(pinned), _p(y), threads))
     return y
 
 

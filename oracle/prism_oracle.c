@@ -451,6 +451,97 @@ int po_matvec(uint32_t kind, const uint8_t *w, size_t rows, size_t cols,
   return st;
 }
 
+/* Multi-token projection: the reference's tiled prefill shares each weight
+ * row across a tile of at most 32 tokens and computes one per-token dot for
+ * each (src/kernels/prefill.rs:26 MAX_TILE_TOKENS, :48-87
+ * dot_quantized_tile_row); tokens are quantized to Q8_K once up front. */
+#define PO_TILE_TOKENS 32
+
+typedef struct {
+  uint32_t kind;
+  const uint8_t *w;
+  size_t row_begin, row_end, nb, rows, tokens;
+  const po_q8k_block *a; /* [tokens][nb] */
+  float *y;              /* [tokens][rows] */
+  int first_error;
+} po_tile_chunk;
+
+static void *po_tile_chunk_run(void *arg) {
+  po_tile_chunk *c = (po_tile_chunk *)arg;
+  size_t rb = (size_t)po_block_bytes(c->kind) * c->nb;
+  c->first_error = PO_OK;
+  for (size_t t0 = 0; t0 < c->tokens; t0 += PO_TILE_TOKENS) {
+    size_t t1 = t0 + PO_TILE_TOKENS < c->tokens ? t0 + PO_TILE_TOKENS : c->tokens;
+    for (size_t r = c->row_begin; r < c->row_end; ++r) {
+      const uint8_t *row = c->w + r * rb;
+      for (size_t t = t0; t < t1; ++t) {
+        const po_q8k_block *a = c->a + t * c->nb;
+        float *out = c->y + t * c->rows + r;
+        int st = c->kind == 35 ? po_tq2_dot(row, a, c->nb, out) : po_q2k_dot(row, a, c->nb, out);
+        if (st != PO_OK) {
+          c->first_error = st;
+          return NULL;
+        }
+      }
+    }
+  }
+  return NULL;
+}
+
+int po_project_tokens(uint32_t kind, const uint8_t *w, size_t rows, size_t cols,
+                      const float *x, size_t tokens, int pinned, float *y, int threads) {
+  if (po_block_bytes(kind) == 0 || cols == 0 || cols % 256 != 0 || rows == 0)
+    return PO_E_INVALID;
+  if (tokens == 0) return PO_OK;
+  size_t nb = cols / 256;
+  po_q8k_block *a = (po_q8k_block *)malloc(tokens * nb * sizeof(po_q8k_block));
+  if (!a) return PO_E_INVALID;
+  int st = PO_OK;
+  for (size_t t = 0; t < tokens && st == PO_OK; ++t)
+    st = po_q8k_quantize(x + t * cols, cols, pinned, a + t * nb);
+  if (st != PO_OK) {
+    free(a);
+    memset(y, 0, tokens * rows * sizeof(float));
+    return st;
+  }
+  if (threads < 1) threads = 1;
+  if ((size_t)threads > rows) threads = (int)rows;
+  size_t chunk = (rows + (size_t)threads - 1) / (size_t)threads;
+  int workers = (int)((rows + chunk - 1) / chunk);
+  po_tile_chunk *cs = (po_tile_chunk *)calloc((size_t)workers, sizeof(po_tile_chunk));
+  pthread_t *ts = (pthread_t *)calloc((size_t)workers, sizeof(pthread_t));
+  if (!cs || !ts) {
+    free(cs);
+    free(ts);
+    free(a);
+    return PO_E_INVALID;
+  }
+  for (int i = 0; i < workers; ++i) {
+    cs[i].kind = kind;
+    cs[i].w = w;
+    cs[i].row_begin = (size_t)i * chunk;
+    cs[i].row_end = cs[i].row_begin + chunk < rows ? cs[i].row_begin + chunk : rows;
+    cs[i].nb = nb;
+    cs[i].rows = rows;
+    cs[i].tokens = tokens;
+    cs[i].a = a;
+    cs[i].y = y;
+  }
+  for (int i = 1; i < workers; ++i) pthread_create(&ts[i], NULL, po_tile_chunk_run, &cs[i]);
+  po_tile_chunk_run(&cs[0]);
+  for (int i = 1; i < workers; ++i) pthread_join(ts[i], NULL);
+  for (int i = 0; i < workers; ++i)
+    if (cs[i].first_error != PO_OK) {
+      st = cs[i].first_error;
+      break;
+    }
+  free(cs);
+  free(ts);
+  free(a);
+  if (st != PO_OK) memset(y, 0, tokens * rows * sizeof(float));
+  return st;
+}
+
 /* ---------------------------------------------------------------------- */
 /* Float primitives (Source contract)                                      */
 /* ---------------------------------------------------------------------- */

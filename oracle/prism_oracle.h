@@ -80,6 +80,13 @@ int po_matvec(uint32_t kind, const uint8_t *w, size_t rows, size_t cols,
               const po_q8k_block *a, float *y, int threads);
 int po_block_bytes(uint32_t kind);
 
+/* Multi-token projection y[t][r] = dot(row r, Q8_K(x[t])) for `tokens`
+ * rows of x [tokens][cols]: each token quantized once, each weight row
+ * shared across tiles of 32 tokens (reference src/kernels/prefill.rs:26,
+ * 48-87), rows split over `threads` workers in contiguous chunks. */
+int po_project_tokens(uint32_t kind, const uint8_t *w, size_t rows, size_t cols,
+                      const float *x, size_t tokens, int pinned, float *y, int threads);
+
 /* ---- float primitives (Source contract) ----------------------------- */
 float po_float_dot(const float *a, const float *b, size_t n);
 float po_f16_dot(const float *a, const uint16_t *b, size_t n);

@@ -256,6 +256,7 @@ struct prism_b200_executor {
   std::string last_error;
   DeviceBuffer act, x, y, ints, ints2;
   DeviceBuffer gdn_scratch;       // chunked GDN prefill: per-chunk M, CQ, cum, P
+  DeviceBuffer tok_x, tok_act, tok_y;  // multi-token projection: inputs, Q8_K tokens, outputs
   std::set<prism_b200_weight *> weights;
 
   int fail(int code, const char *fmt, ...) {

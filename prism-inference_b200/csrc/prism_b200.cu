@@ -15,6 +15,7 @@
 #include "common.cuh"
 #include "executor.cuh"
 #include "gdn.cuh"
+#include "gemm.cuh"
 
 using namespace prism;
 
@@ -137,6 +138,9 @@ void prism_b200_executor_destroy(prism_b200_executor *ex) {
   ex->ints.release();
   ex->ints2.release();
   ex->gdn_scratch.release();
+  ex->tok_x.release();
+  ex->tok_act.release();
+  ex->tok_y.release();
   if (ex->d_status) cudaFree(ex->d_status);
   if (ex->h_status) cudaFreeHost(ex->h_status);
   if (ex->stream) cudaStreamDestroy(ex->stream);
@@ -358,6 +362,61 @@ int prism_b200_project_f32(prism_b200_executor *ex, const prism_b200_weight *w, 
   const prism_b200_weight *ws[1] = {w};
   float *os[1] = {out};
   return prism_b200_project_f32_group(ex, 1, ws, x, pinned, os);
+}
+
+int prism_b200_project_f32_tokens_device(prism_b200_executor *ex, const prism_b200_weight *w,
+                                         size_t tokens, const float *x_dev, int pinned,
+                                         float *out_dev, void *stream) {
+  int st = check_open(ex);
+  if (st) return st;
+  if ((st = validate_weight(ex, w))) return st;
+  if (!tokens) return PRISM_B200_OK;
+  if (!x_dev || !out_dev) return ex->fail(PRISM_B200_E_INVALID, "null device buffer");
+  if (reinterpret_cast<uintptr_t>(x_dev) % 16 || reinterpret_cast<uintptr_t>(out_dev) % 4)
+    return ex->fail(PRISM_B200_E_INVALID, "misaligned token buffers");
+  if (tokens > (size_t)kMaxTokens)
+    return ex->fail(PRISM_B200_E_INVALID, "at most %d tokens per call", kMaxTokens);
+  CK(cudaSetDevice(ex->device), "select device");
+  const DeviceWeight &dw = w->dw;
+  const size_t M = tokens, nb = dw.nb;
+  // Q8_K tokens: codes [M][K] | scale [M][nb] | asum [M][nb] | sums [M][nb][16]
+  const size_t codes = M * nb * 256, meta = M * nb;
+  CK(ex->tok_act.ensure(codes + meta * 4 * 2 + meta * 32), "token activation buffer");
+  uint8_t *base = static_cast<uint8_t *>(ex->tok_act.ptr);
+  TokenQ8K t;
+  t.codes = reinterpret_cast<int8_t *>(base);
+  t.scale = reinterpret_cast<float *>(base + codes);
+  t.asum = reinterpret_cast<int *>(base + codes + meta * 4);
+  t.sums = reinterpret_cast<int16_t *>(base + codes + meta * 8);
+  cudaStream_t s = pick(ex, stream);
+  CK(launch_token_gemm(dw, x_dev, M, pinned, t, out_dev, ex->d_status, s, ex->pdl),
+     "token projection launch");
+  return PRISM_B200_OK;
+}
+
+int prism_b200_project_f32_tokens(prism_b200_executor *ex, const prism_b200_weight *w,
+                                  size_t tokens, const float *x, int pinned, float *out) {
+  int st = check_open(ex);
+  if (st) return st;
+  if ((st = validate_weight(ex, w))) return st;
+  if (!tokens) return PRISM_B200_OK;
+  if (!x || !out) return ex->fail(PRISM_B200_E_INVALID, "null token buffer");
+  if (tokens > (size_t)kMaxTokens)
+    return ex->fail(PRISM_B200_E_INVALID, "at most %d tokens per call", kMaxTokens);
+  CK(cudaSetDevice(ex->device), "select device");
+  const size_t xin = tokens * w->dw.cols * 4, yout = tokens * w->dw.rows * 4;
+  CK(ex->tok_x.ensure(xin), "token input buffer");
+  CK(ex->tok_y.ensure(yout), "token output buffer");
+  cudaStream_t s = ex->stream;
+  CK(cudaMemcpyAsync(ex->tok_x.ptr, x, xin, cudaMemcpyHostToDevice, s), "input copy");
+  if ((st = prism_b200_project_f32_tokens_device(ex, w, tokens,
+                                                 static_cast<float *>(ex->tok_x.ptr), pinned,
+                                                 static_cast<float *>(ex->tok_y.ptr), s)))
+    return st;
+  CK(cudaMemcpyAsync(out, ex->tok_y.ptr, yout, cudaMemcpyDeviceToHost, s), "output copy");
+  st = finish(ex, s);
+  if (st) memset(out, 0, yout);
+  return st;
 }
 
 int prism_b200_block_dots(prism_b200_executor *ex, const prism_b200_weight *w,

@@ -68,6 +68,8 @@ def load():
         "prism_b200_project_device": (i32, [vp, vp, vp, i32, vp, vp]),
         "prism_b200_project_f32": (i32, [vp, vp, vp, i32, vp]),
         "prism_b200_project_f32_group": (i32, [vp, sz, P(vp), vp, i32, P(vp)]),
+        "prism_b200_project_f32_tokens": (i32, [vp, vp, sz, vp, i32, vp]),
+        "prism_b200_project_f32_tokens_device": (i32, [vp, vp, sz, vp, i32, vp, vp]),
         "prism_b200_quantize_q8k": (i32, [vp, vp, sz, i32, vp]),
         "prism_b200_quantize_q8k_device": (i32, [vp, vp, sz, i32, vp, vp]),
         "prism_b200_block_dots": (i32, [vp, vp, vp, vp, vp]),
@@ -248,6 +250,25 @@ class ProjectionExecutor:
         assert out.dtype == np.float32 and out.size == w.rows and out.flags.c_contiguous
         self._check(load().prism_b200_project_f32(self.h, w.handle, _p(x), int(pinned), _p(out)))
         return out
+
+    def project_f32_tokens(self, weight, x, pinned=False):
+        """Y[t] = W x[t] for a tile of tokens x [tokens][cols] (reference
+        src/kernels/projection.rs:137-153), on the tensor cores."""
+        w = self._weight(weight)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim != 2 or x.shape[1] != w.cols:
+            raise PrismB200Error(E_INVALID, "token tile must be [tokens][cols]")
+        out = np.zeros((x.shape[0], w.rows), dtype=np.float32)
+        self._check(load().prism_b200_project_f32_tokens(self.h, w.handle, x.shape[0], _p(x),
+                                                         int(pinned), _p(out)))
+        return out
+
+    def project_f32_tokens_device(self, weight, tokens, x_ptr, out_ptr, pinned=False,
+                                  stream=None):
+        w = self._weight(weight)
+        self._check(load().prism_b200_project_f32_tokens_device(
+            self.h, w.handle, tokens, ctypes.c_void_p(x_ptr), int(pinned),
+            ctypes.c_void_p(out_ptr), ctypes.c_void_p(stream) if stream else None))
 
     def project_f32_group(self, weights, x, pinned=False):
         ws = [self._weight(w) for w in weights]

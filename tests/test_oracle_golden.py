@@ -138,3 +138,22 @@ def test_matvec_threads_bit_equal(oracle):
         assert np.array_equal(y1.view(np.uint32), y5.view(np.uint32))
         for r in (0, 17, 36):
             assert y1[r] == oracle.dot(kind, w[r].reshape(-1), act)
+
+
+def test_project_tokens_equals_per_token_matvec(oracle):
+    rng = np.random.default_rng(8)
+    rows, cols, tokens = 45, 768, 70   # more than two 32-token tiles
+    for kind in (35, 10):
+        bb = oracle.block_bytes(kind)
+        w = rng.integers(0, 256, rows * cols // 256 * bb).astype(np.uint8).reshape(rows, -1, bb)
+        if kind == 35:
+            w[:, :, 64:66] = np.frombuffer(np.float16(0.03).tobytes(), np.uint8)
+        else:
+            w[:, :, 80:82] = np.frombuffer(np.float16(0.02).tobytes(), np.uint8)
+            w[:, :, 82:84] = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
+        x = rng.standard_normal((tokens, cols)).astype(np.float32)
+        for pinned in (False, True):
+            y = oracle.project_tokens(kind, w, rows, cols, x, pinned, threads=4)
+            for t in (0, 31, 32, 69):
+                ref = oracle.matvec(kind, w, rows, cols, oracle.q8k_quantize(x[t], pinned))
+                assert np.array_equal(y[t].view(np.uint32), ref.view(np.uint32))

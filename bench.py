@@ -507,6 +507,7 @@ def run_gdn(args):
         "roofline": {"bound": "hbm", "achieved": decode["B64"]["gbs"], "peak": peak,
                      "unit": "GB/s", "frac": decode["B64"]["frac"], "peak_source": peak_src,
                      "kernel": "gdn_step_kernel (B=64)",
+                     "traffic": traffic_from_profiles("gdn_step_kernel"),
                      "prefill_fp32_peak_tflops_nominal": fp32_peak},
         "gpu_launches": 50,
     }

@@ -379,15 +379,16 @@ int prism_b200_project_f32_tokens_device(prism_b200_executor *ex, const prism_b2
   CK(cudaSetDevice(ex->device), "select device");
   const DeviceWeight &dw = w->dw;
   const size_t M = tokens, nb = dw.nb;
-  // Q8_K tokens: codes [M][K] | scale [M][nb] | asum [M][nb] | sums [M][nb][16]
+  // Q8_K tokens: codes [M][K] | split sums [M][nb][32] | scale [M][nb] |
+  // asum [M][nb]; codes and split start 16-byte aligned (TMA sources)
   const size_t codes = M * nb * 256, meta = M * nb;
-  CK(ex->tok_act.ensure(codes + meta * 4 * 2 + meta * 32), "token activation buffer");
+  CK(ex->tok_act.ensure(codes + meta * 32 + meta * 4 * 2), "token activation buffer");
   uint8_t *base = static_cast<uint8_t *>(ex->tok_act.ptr);
   TokenQ8K t;
   t.codes = reinterpret_cast<int8_t *>(base);
-  t.scale = reinterpret_cast<float *>(base + codes);
-  t.asum = reinterpret_cast<int *>(base + codes + meta * 4);
-  t.sums = reinterpret_cast<int16_t *>(base + codes + meta * 8);
+  t.split = reinterpret_cast<int8_t *>(base + codes);
+  t.scale = reinterpret_cast<float *>(base + codes + meta * 32);
+  t.asum = reinterpret_cast<int *>(base + codes + meta * 36);
   cudaStream_t s = pick(ex, stream);
   CK(launch_token_gemm(dw, x_dev, M, pinned, t, out_dev, ex->d_status, s, ex->pdl),
      "token projection launch");

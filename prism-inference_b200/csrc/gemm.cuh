@@ -7,26 +7,24 @@
 // (the reference's ProjectionTile per-token dots, src/kernels/prefill.rs:
 // 48-87).  The exact int32 block dots of (token m, row n, block b) come from
 // the tensor cores, 128 tokens x 128 rows per CTA tile:
-//   TQ2_0: raw codes c in 0..3 (u8) x Q8_K codes (s8); int = sum(c*a) - sum(a)
+//   TQ2_0: weights c - 1 in -1..2 (s8; code 3 decodes to +2) x Q8_K codes (s8)
 //   Q2_K : isum = sum(sc*q * a) with sc*q in 0..45 (u8), K = 256;
 //          msum = sum_g sums_g * min_g as one more K = 32 product: with
 //          sums_g = 16*hi_g + lo_g (lo in 0..15, hi in -127..127, both s8),
 //          msum = sum_g lo_g*min_g + hi_g*(16*min_g), 16*min_g <= 240 (u8).
 //
-// Pipeline per CTA.  Three load stages, filled by one thread with TMA (the
-// tokens' Q8_K codes, 128 x 256 B, straight into the K-major core-matrix
-// layout: 8 rows x 16 B per core matrix, K-adjacent core matrices 2 KB
-// apart, row-adjacent ones 128 B) and bulk copies (the packed weight units
-// of the 128 rows).  Two unpack stages: all threads expand the 2-bit codes
-// (and for Q2_K the scales and mins) into u8 core matrices, then one thread
-// issues the MMAs into one of two TMEM accumulators and commits to an
-// mbarrier.  The epilogue of block b-1 (tcgen05.ld, then the binary32
-// chain on the CUDA cores; warp w owns TMEM lanes 32(w%4).. = tokens and
-// columns 64(w/4).. = rows) runs while block b's MMAs execute, and block
-// b+2's loads are in flight meanwhile.
+// Pipeline per CTA (warp-specialised, see gemm_tokens_kernel): a load
+// thread stages each block with bulk copies into one of three load stages --
+// the tokens' Q8_K codes (128 x 256 B, stored tile-major by the quantize
+// kernel in the K-major core-matrix layout: 8 rows x 16 B per core matrix,
+// K-adjacent core matrices 2 KB apart, row-adjacent ones 128 B) and the
+// packed weight units of the 128 rows; four warps expand the 2-bit codes
+// into 8-bit core matrices (two unpack stages); one thread issues the MMAs
+// into one of two TMEM accumulators; eight warps read finished accumulators
+// (tcgen05.ld) and extend the binary32 chains on the CUDA cores.  All hand-
+// offs are mbarriers, so loads, unpacking, MMAs and epilogues of successive
+// blocks overlap.
 #pragma once
-
-#include <cuda.h>
 
 #include "common.cuh"
 #include "executor.cuh"
@@ -37,17 +35,25 @@ namespace prism {
 
 constexpr int kGemmM = 128;       // tokens per CTA tile
 constexpr int kGemmN = 128;       // weight rows per CTA tile
-constexpr int kGemmThreads = 256;
+constexpr int kGemmThreads = 448;  // 14 warps, roles below
 constexpr int kGemmLoadStages = 3;
 constexpr int kMaxTokens = 1 << 16;  // tokens per multi-token projection call
 
 // ---- token activations prepared once: Q8_K per (token, block) --------------
+// Codes and split sums are stored tile-major, already in the tensor cores'
+// K-major core-matrix order: for token tile t = m / 128 and block b, one
+// contiguous 32 KB run [16-byte chunk kc][row m % 128][16 B] of codes and
+// one 4 KB run [2][128][16 B] of split sums, so that a single bulk copy
+// stages an operand.
 struct TokenQ8K {
-  int8_t *codes;     // [M][K]
+  int8_t *codes;     // [M/128 padded][nb][16][128][16]
   float *scale;      // [M][nb]
-  int *asum;         // [M][nb]   sum of the block's codes
-  int8_t *split;     // [M][nb][32]  lo_g (16 B) | hi_g (16 B) of the group sums
+  int8_t *split;     // [M/128 padded][nb][2][128][16]  lo_g | hi_g of the group sums
 };
+
+__host__ __device__ inline size_t token_tile(int m, int nb, int b) {
+  return (size_t)(m / 128) * nb + b;
+}
 
 // one warp per (token, block); reference q8k_with_input (src/kernels.rs:463-522)
 __global__ void __launch_bounds__(256) q8k_tokens_kernel(const float *__restrict__ x, int M,
@@ -71,24 +77,22 @@ __global__ void __launch_bounds__(256) q8k_tokens_kernel(const float *__restrict
                 ((uint32_t)(uint8_t)q[2] << 16) | ((uint32_t)(uint8_t)q[3] << 24);
   uint32_t w1 = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) |
                 ((uint32_t)(uint8_t)q[6] << 16) | ((uint32_t)(uint8_t)q[7] << 24);
-  reinterpret_cast<uint2 *>(out.codes + (size_t)m * nb * 256 + b * 256)[lane] = make_uint2(w0, w1);
+  // lane holds codes 8*lane..8*lane+7: chunk kc = lane/2, half lane%2
+  const size_t tile = token_tile(m, nb, b);
+  const int row = m & 127;
+  *reinterpret_cast<uint2 *>(out.codes + tile * 32768 + (lane >> 1) * 2048 + row * 16 +
+                             (lane & 1) * 8) = make_uint2(w0, w1);
   if ((lane & 1) == 0) {
-    // |pair| <= 16 * 128: lo = pair mod 16 in 0..15, hi = floor(pair / 16) in -128..127
-    int8_t *sp = out.split + ((size_t)m * nb + b) * 32;
+    // |pair| <= 16 * 127: lo = pair mod 16 in 0..15, hi = floor(pair / 16) in -127..127
+    int8_t *sp = out.split + tile * 4096 + row * 16;
     sp[lane >> 1] = (int8_t)(pair & 15);
-    sp[16 + (lane >> 1)] = (int8_t)(pair >> 4);
+    sp[2048 + (lane >> 1)] = (int8_t)(pair >> 4);
   }
-  int tot = pair;
-#pragma unroll
-  for (int off = 2; off < 32; off <<= 1) tot += __shfl_xor_sync(0xffffffffu, tot, off);
-  if (lane == 0) {
-    out.scale[(size_t)m * nb + b] = scale;
-    out.asum[(size_t)m * nb + b] = tot;
-  }
+  if (lane == 0) out.scale[(size_t)m * nb + b] = scale;
 }
 
-// ---- tcgen05 / TMA helpers (PTX ISA: tensor memory, matrix and instruction
-// descriptors, bulk tensor copies) ---------------------------------------------
+// ---- tcgen05 helpers (PTX ISA: tensor memory, matrix and instruction
+// descriptors) ----------------------------------------------------------------
 
 // Shared-memory matrix descriptor, K-major, no swizzle: start address,
 // leading-dimension (K-adjacent core matrix) and stride-dimension
@@ -163,27 +167,34 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-// 3-D tiled TMA load into this CTA's shared memory (no multicast)
-__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int c0, int c1,
-                                            int c2, uint64_t *bar) {
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar))
-      : "memory");
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
 struct GemmArgs {
-  CUtensorMap codes_map;  // Q8_K codes viewed as [K/16][M][16 B]
-  CUtensorMap split_map;  // group-sum split viewed as [2 nb][M][16 B]
+  const int8_t *codes;    // tile-major Q8_K codes (TokenQ8K)
+  const int8_t *split;    // tile-major split group sums
   const uint8_t *w;       // tiled weight units (matvec.cuh layout)
   int h, nb, rows, ntiles;
   const float *scale;     // [M][nb]
-  const int *asum;        // [M][nb]
   int M;
   float *y;               // [M][rows]
   unsigned *status;
 };
+
+// Warp roles of the 14-warp CTA.
+constexpr int kWarpUnpack = 1;  // warps 1..4: one weight row per thread
+constexpr int kWarpMma = 5;     // lane 0 issues the MMAs
+constexpr int kWarpEpi = 6;     // warps 6..13: epilogue (token lanes x 64 rows)
 
 // Shared-memory layout of one CTA.
 template <int KIND>
@@ -192,13 +203,15 @@ struct GemmSmem {
   // load stage: A codes 32 KB | A split 4 KB | packed weight units
   static constexpr int kA = 0, kA2 = 32768, kBp = 36864;
   static constexpr int kLoadStage = (kBp + kGemmN * kBlockBytes + 1023) / 1024 * 1024;
-  // unpack stage: B codes 32 KB | B mins 4 KB | d[128] | dmin[128]
+  // unpack stage: B codes 32 KB | B mins 4 KB
   static constexpr int kUnpack = kGemmLoadStages * kLoadStage;
-  static constexpr int kBu = 0, kB2 = 32768, kD = 36864, kDmin = 37376;
-  static constexpr int kUnpackStage = 37888;
-  static constexpr int kBars = kUnpack + 2 * kUnpackStage;  // full[3], done[2], tmem slot
-  static constexpr int kBytes = kBars + 64;
-  static constexpr int kTmemCols = KIND == 35 ? 256 : 512;   // 2 x (isum [+ msum]) x 128
+  static constexpr int kBu = 0, kB2 = 32768;
+  static constexpr int kUnpackStage = 36864;
+  // ring of 4: d[128], dmin[128] of each block's rows (f32)
+  static constexpr int kScales = kUnpack + 2 * kUnpackStage;
+  static constexpr int kBars = kScales + 4096;
+  static constexpr int kBytes = kBars + 256;
+  static constexpr int kTmemCols = KIND == 35 ? 256 : 512;  // 2 x (isum [+ msum]) x 128
 };
 
 // Core-matrix offset (bytes) of (row, 16-byte K chunk) within a 128-row
@@ -207,14 +220,33 @@ __device__ __forceinline__ int core_off(int row, int kc) {
   return kc * 2048 + (row >> 3) * 128 + (row & 7) * 16;
 }
 
+// Warp-specialised CTA (448 threads):
+//   warp 0 lane 0  issues each block's bulk copies once its load stage is
+//                  free (lfree: the MMAs that read it completed);
+//   warps 1..4     unpack a block's weight rows into u8/s8 core matrices once
+//                  the copies landed (full) and the unpack stage is free
+//                  (ufree), then arrive on ufull;
+//   warp 5 lane 0  waits ufull and a drained accumulator (aempty), issues the
+//                  MMAs, publishes the block's scales (dready) and commits
+//                  afull / ufree / lfree;
+//   warps 6..13    wait dready + afull, read TMEM and extend the chains, then
+//                  arrive on aempty.
+// Every wait is bounded; a role that gives up raises the CTA's fail flag and
+// the others stop at their next wait.
 template <int KIND>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tokens_kernel(const __grid_constant__ GemmArgs g) {
   using L = GemmSmem<KIND>;
   extern __shared__ __align__(1024) uint8_t gsm[];
-  uint64_t *full = reinterpret_cast<uint64_t *>(gsm + L::kBars);  // [3]
-  uint64_t *done = full + kGemmLoadStages;                         // [2]
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 2);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(gsm + L::kBars);
+  uint64_t *full = bars, *lfree = bars + 3;                  // [3] each
+  uint64_t *ufull = bars + 6, *ufree = bars + 8;             // [2] each
+  uint64_t *afull = bars + 10, *aempty = bars + 12;          // [2] each
+  uint64_t *dready = bars + 14;                              // [2]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 16);
+  volatile int *fail = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  float *dring = reinterpret_cast<float *>(gsm + L::kScales);  // [4][128]
+  float *mring = dring + 4 * kGemmN;                           // [4][128]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * kGemmN, m0 = blockIdx.y * kGemmM;
@@ -226,8 +258,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_alloc(tmem_slot, L::kTmemCols);
     tmem_relinquish();
   }
-  if (tid == 0) {
-    for (int i = 0; i < kGemmLoadStages + 2; ++i) mbar_init(&full[i], 1);
+  if (tid == 32) {
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&lfree[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ufull[i], 4 * 32);
+      mbar_init(&ufree[i], 1);
+      mbar_init(&afull[i], 1);
+      mbar_init(&aempty[i], 8 * 32);
+      mbar_init(&dready[i], 1);
+    }
+    *fail = 0;
     mbar_init_fence();
   }
   tc_fence_before();
@@ -237,60 +280,76 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   grid_dependency_wait();
   grid_dependents_launch();
 
-  // one thread: TMA the tokens' codes (and split sums), bulk-copy the rows'
-  // packed units of block b into load stage b % 3
-  auto issue_loads = [&](int b) {
-    const int ls = b % kGemmLoadStages;
-    uint8_t *st = gsm + ls * L::kLoadStage;
-    int copies = 0;
-    for (int i = 0; i < tiles; ++i) copies += tile0 + i < g.ntiles;
-    const uint32_t bytes = 32768u + (KIND == 10 ? 4096u : 0u) + (uint32_t)(copies * unit);
-    mbar_arrive_expect_tx(&full[ls], bytes);
-    tma_load_3d(st + L::kA, &g.codes_map, 0, m0, b * 16, &full[ls]);
-    if (KIND == 10) tma_load_3d(st + L::kA2, &g.split_map, 0, m0, b * 2, &full[ls]);
-    for (int i = 0; i < tiles; ++i)
-      if (tile0 + i < g.ntiles)
-        bulk_g2s(st + L::kBp + i * unit, g.w + ((size_t)(tile0 + i) * nb + b) * unit, unit,
-                 &full[ls]);
-  };
+  float acc[64];
+#pragma unroll
+  for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
 
-  // all threads: expand block b's packed units (load stage b % 3) into u8
-  // core matrices (unpack stage b % 2).  Thread t takes row t % 128 and the
-  // packed chunks 2(t/128), 2(t/128)+1; eight consecutive threads write one
-  // 128-byte run, so the stores are conflict-free.
-  auto unpack = [&](int b) {
-    const uint8_t *bp = gsm + (b % kGemmLoadStages) * L::kLoadStage + L::kBp;
-    uint8_t *us = gsm + L::kUnpack + (b & 1) * L::kUnpackStage;
-    const int row = tid & (kGemmN - 1), n = n0 + row;
-    const bool valid = n < g.rows;
-    const uint8_t *u = bp + (row / h) * unit;
-    const int r = row % h;
-    uint4 scv = make_uint4(0u, 0u, 0u, 0u);
-    if (KIND == 10 && valid) scv = *reinterpret_cast<const uint4 *>(u + 64 * h + r * 16);
-#pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {
-      const int c = 2 * (tid >> 7) + cc;
-      uint4 wq = make_uint4(0u, 0u, 0u, 0u);
-      if (valid) wq = *reinterpret_cast<const uint4 *>(u + (c * h + r) * 16);
-      // packed chunk c holds, in bit plane j, the 16 codes of K chunk
-      // kc = (c/2)*8 + 2j + (c%2)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const unsigned mk = 0x03030303u << (2 * j);
-        uint4 o = make_uint4((wq.x & mk) >> (2 * j), (wq.y & mk) >> (2 * j),
-                             (wq.z & mk) >> (2 * j), (wq.w & mk) >> (2 * j));
-        const int kc = (c >> 1) * 8 + 2 * j + (c & 1);
-        if (KIND == 10) {
-          const unsigned sc = byte_of(scv, kc) & 15u;  // sc*q <= 45: no byte carries
-          o.x *= sc;
-          o.y *= sc;
-          o.z *= sc;
-          o.w *= sc;
-        }
-        *reinterpret_cast<uint4 *>(us + L::kBu + core_off(row, kc)) = o;
+  if (warp == 0) {
+    // ---- loads -------------------------------------------------------------
+    if (lane == 0) {
+      int copies = 0;
+      for (int i = 0; i < tiles; ++i) copies += tile0 + i < g.ntiles;
+      const uint32_t bytes = 32768u + (KIND == 10 ? 4096u : 0u) + (uint32_t)(copies * unit);
+      for (int b = 0; b < nb; ++b) {
+        const int ls = b % kGemmLoadStages;
+        if (b >= kGemmLoadStages &&
+            !mbar_wait_bounded(&lfree[ls], (unsigned)(b / kGemmLoadStages - 1) & 1u, g.status))
+          *fail = 1;
+        if (*fail) break;
+        uint8_t *st = gsm + ls * L::kLoadStage;
+        const size_t tile = token_tile(m0, nb, b);
+        mbar_arrive_expect_tx(&full[ls], bytes);
+        bulk_g2s(st + L::kA, g.codes + tile * 32768, 32768u, &full[ls]);
+        if (KIND == 10) bulk_g2s(st + L::kA2, g.split + tile * 4096, 4096u, &full[ls]);
+        for (int i = 0; i < tiles; ++i)
+          if (tile0 + i < g.ntiles)
+            bulk_g2s(st + L::kBp + i * unit, g.w + ((size_t)(tile0 + i) * nb + b) * unit, unit,
+                     &full[ls]);
       }
     }
-    if (tid < kGemmN) {
+  } else if (warp < kWarpMma) {
+    // ---- unpack: thread = weight row ---------------------------------------
+    const int row = tid - 32 * kWarpUnpack, n = n0 + row;
+    const bool valid = n < g.rows;
+    const int r = row % h;
+    for (int b = 0; b < nb; ++b) {
+      const int ls = b % kGemmLoadStages, us = b & 1;
+      bool ok = mbar_wait_bounded(&full[ls], (unsigned)(b / kGemmLoadStages) & 1u, g.status);
+      if (ok && b >= 2) ok = mbar_wait_bounded(&ufree[us], (unsigned)(b / 2 - 1) & 1u, g.status);
+      if (!ok) *fail = 1;
+      if (*fail) break;
+      const uint8_t *u = gsm + ls * L::kLoadStage + L::kBp + (row / h) * unit;
+      uint8_t *ust = gsm + L::kUnpack + us * L::kUnpackStage;
+      uint4 scv = make_uint4(0u, 0u, 0u, 0u);
+      if (KIND == 10 && valid) scv = *reinterpret_cast<const uint4 *>(u + 64 * h + r * 16);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint4 wq = make_uint4(0u, 0u, 0u, 0u);
+        if (valid) wq = *reinterpret_cast<const uint4 *>(u + (c * h + r) * 16);
+        // packed chunk c holds, in bit plane j, the 16 codes of K chunk
+        // kc = (c/2)*8 + 2j + (c%2)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const unsigned mk = 0x03030303u << (2 * j);
+          uint4 o = make_uint4((wq.x & mk) >> (2 * j), (wq.y & mk) >> (2 * j),
+                               (wq.z & mk) >> (2 * j), (wq.w & mk) >> (2 * j));
+          const int kc = (c >> 1) * 8 + 2 * j + (c & 1);
+          if (KIND == 35) {
+            // signed ternary weights: code - 1 per byte (code 3 -> +2)
+            o.x = __vsub4(o.x, 0x01010101u);
+            o.y = __vsub4(o.y, 0x01010101u);
+            o.z = __vsub4(o.z, 0x01010101u);
+            o.w = __vsub4(o.w, 0x01010101u);
+          } else {
+            const unsigned sc = byte_of(scv, kc) & 15u;  // sc*q <= 45: no byte carries
+            o.x *= sc;
+            o.y *= sc;
+            o.z *= sc;
+            o.w *= sc;
+          }
+          *reinterpret_cast<uint4 *>(ust + L::kBu + core_off(row, kc)) = o;
+        }
+      }
       float d = 0.0f, dm = 0.0f;
       if (valid) {
         if (KIND == 35) {
@@ -301,140 +360,119 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           dm = half_bits_to_float(dd[h + r]);
         }
       }
-      reinterpret_cast<float *>(us + L::kD)[row] = d;
-      reinterpret_cast<float *>(us + L::kDmin)[row] = dm;
-    } else if (KIND == 10) {
-      // B mins, K = 32: chunk 0 = min_g, chunk 1 = 16*min_g (g = 0..15)
-      uint4 lo, hi;
-      uint32_t *pl = reinterpret_cast<uint32_t *>(&lo), *ph = reinterpret_cast<uint32_t *>(&hi);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint32_t wv = 0;
-        if (valid) {
-          const uint32_t s4 = q == 0 ? scv.x : q == 1 ? scv.y : q == 2 ? scv.z : scv.w;
-          wv = (s4 >> 4) & 0x0f0f0f0fu;
-        }
-        pl[q] = wv;
-        ph[q] = wv << 4;
+      dring[(b & 3) * kGemmN + row] = d;
+      mring[(b & 3) * kGemmN + row] = dm;
+      if (KIND == 10) {
+        // B mins, K = 32: chunk 0 = min_g, chunk 1 = 16*min_g (g = 0..15)
+        const uint4 lo = make_uint4((scv.x >> 4) & 0x0f0f0f0fu, (scv.y >> 4) & 0x0f0f0f0fu,
+                                    (scv.z >> 4) & 0x0f0f0f0fu, (scv.w >> 4) & 0x0f0f0f0fu);
+        const uint4 hi = make_uint4(lo.x << 4, lo.y << 4, lo.z << 4, lo.w << 4);
+        *reinterpret_cast<uint4 *>(ust + L::kB2 + core_off(row, 0)) = lo;
+        *reinterpret_cast<uint4 *>(ust + L::kB2 + core_off(row, 1)) = hi;
       }
-      *reinterpret_cast<uint4 *>(us + L::kB2 + core_off(row, 0)) = lo;
-      *reinterpret_cast<uint4 *>(us + L::kB2 + core_off(row, 1)) = hi;
+      fence_proxy_async_smem();  // generic stores -> tensor-core (async proxy) reads
+      mbar_arrive(&ufull[us]);
     }
-  };
-
-  auto issue_mma = [&](int b) {
-    const uint8_t *st = gsm + (b % kGemmLoadStages) * L::kLoadStage;
-    const uint8_t *us = gsm + L::kUnpack + (b & 1) * L::kUnpackStage;
-    const uint32_t a = smem_addr(st + L::kA), bsm = smem_addr(us + L::kBu);
-    const uint32_t acc = tmem + (uint32_t)((b & 1) * (L::kTmemCols / 2));
-    constexpr uint32_t idesc = umma_idesc_i8(kGemmM, kGemmN);
+  } else if (warp == kWarpMma) {
+    // ---- MMA issue -----------------------------------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc =
+          umma_idesc_i8(kGemmM, kGemmN) | (KIND == 35 ? (1u << 10) : 0u);  // TQ2_0: B s8
+      constexpr uint32_t idesc_min = umma_idesc_i8(kGemmM, kGemmN);
+      for (int b = 0; b < nb; ++b) {
+        const int ls = b % kGemmLoadStages, us = b & 1;
+        bool ok = mbar_wait_bounded(&ufull[us], (unsigned)(b / 2) & 1u, g.status);
+        if (ok && b >= 2) ok = mbar_wait_bounded(&aempty[us], (unsigned)(b / 2 - 1) & 1u, g.status);
+        if (!ok) *fail = 1;
+        if (*fail) break;
+        mbar_arrive(&dready[us]);  // the block's scales are in place
+        tc_fence_after();
+        const uint32_t a = smem_addr(gsm + ls * L::kLoadStage + L::kA);
+        const uint32_t bsm = smem_addr(gsm + L::kUnpack + us * L::kUnpackStage + L::kBu);
+        const uint32_t accd = tmem + (uint32_t)(us * (L::kTmemCols / 2));
 #pragma unroll
-    for (int k = 0; k < 8; ++k)  // K step k: chunks 2k, 2k+1
-      umma_i8(acc, umma_smem_desc(a + k * 4096, 2048, 128),
-              umma_smem_desc(bsm + k * 4096, 2048, 128), idesc, k > 0 ? 1u : 0u);
-    if (KIND == 10)
-      umma_i8(acc + kGemmN, umma_smem_desc(smem_addr(st + L::kA2), 2048, 128),
-              umma_smem_desc(smem_addr(us + L::kB2), 2048, 128), idesc, 0u);
-    umma_commit(&done[b & 1]);
-  };
-
-  // epilogue state: warp w covers tokens 32(w%4).. and rows 64(w/4)..
-  const int q4 = warp & 3, half = warp >> 2;
-  const int tl = 32 * q4 + lane, m = m0 + tl;
-  const bool mvalid = m < g.M;
-  float acc[64];
-#pragma unroll
-  for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
-  bool failed = false;
-
-  auto epilogue = [&](int b) -> bool {
-    float sa = 0.0f;
-    int asum = 0;
-    if (mvalid) {
-      sa = g.scale[(size_t)m * nb + b];
-      asum = g.asum[(size_t)m * nb + b];
-    }
-    const bool ok = mbar_wait_bounded(&done[b & 1], (unsigned)(b >> 1) & 1u, g.status);
-    if (!__syncthreads_and(ok)) return false;
-    tc_fence_after();
-    const uint8_t *us = gsm + L::kUnpack + (b & 1) * L::kUnpackStage;
-    const float *dsc = reinterpret_cast<const float *>(us + L::kD);
-    const float *dmn = reinterpret_cast<const float *>(us + L::kDmin);
-    const uint32_t base =
-        tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)((b & 1) * (L::kTmemCols / 2));
-#pragma unroll
-    for (int part = 0; part < 2; ++part) {
-      const int col0 = 64 * half + 32 * part;
-      uint32_t r[32];
-      tmem_ld32(base + (uint32_t)col0, r);
-      if (KIND == 35) {
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float term = __fmul_rn((float)((int)r[c] - asum), __fmul_rn(dsc[col0 + c], sa));
-          acc[32 * part + c] = __fadd_rn(acc[32 * part + c], term);
-        }
-      } else {
-        uint32_t ms[32];
-        tmem_ld32(base + (uint32_t)(kGemmN + col0), ms);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float t1 = __fmul_rn(__fmul_rn(sa, dsc[col0 + c]), (float)(int)r[c]);
-          const float t2 = __fmul_rn(__fmul_rn(sa, dmn[col0 + c]), (float)(int)ms[c]);
-          acc[32 * part + c] = __fadd_rn(acc[32 * part + c], __fsub_rn(t1, t2));
-        }
+        for (int k = 0; k < 8; ++k)  // K step k: chunks 2k, 2k+1
+          umma_i8(accd, umma_smem_desc(a + k * 4096, 2048, 128),
+                  umma_smem_desc(bsm + k * 4096, 2048, 128), idesc, k > 0 ? 1u : 0u);
+        if (KIND == 10)
+          umma_i8(accd + kGemmN, umma_smem_desc(a + L::kA2, 2048, 128),
+                  umma_smem_desc(bsm + L::kB2, 2048, 128), idesc_min, 0u);
+        umma_commit(&afull[us]);
+        umma_commit(&ufree[us]);
+        umma_commit(&lfree[ls]);
       }
     }
-    return true;
-  };
-
-  if (tid == 0)
-    for (int b = 0; b < kGemmLoadStages && b < nb; ++b) issue_loads(b);
-  for (int b = 0; b < nb && !failed; ++b) {
-    const bool ok = mbar_wait_bounded(&full[b % kGemmLoadStages],
-                                      (unsigned)(b / kGemmLoadStages) & 1u, g.status);
-    if (ok) unpack(b);
-    fence_proxy_async_smem();  // generic stores -> tensor-core (async proxy) reads
-    tc_fence_before();
-    if (!__syncthreads_and(ok)) {
-      failed = true;
-      break;
-    }
-    if (tid == 0) {
+  } else {
+    // ---- epilogue: thread = token, 64 rows ----------------------------------
+    const int q4 = warp & 3, half = (warp - kWarpEpi) >> 2;
+    const int m = m0 + 32 * q4 + lane;
+    const bool mvalid = m < g.M;
+    float sa_next = mvalid ? g.scale[(size_t)m * nb] : 0.0f;
+    for (int b = 0; b < nb; ++b) {
+      const int us = b & 1;
+      const float sa = sa_next;
+      if (mvalid && b + 1 < nb) sa_next = g.scale[(size_t)m * nb + b + 1];
+      bool ok = mbar_wait_bounded(&dready[us], (unsigned)(b / 2) & 1u, g.status);
+      if (ok) ok = mbar_wait_bounded(&afull[us], (unsigned)(b / 2) & 1u, g.status);
+      if (!ok) *fail = 1;
+      if (*fail) break;
       tc_fence_after();
-      issue_mma(b);
-    }
-    if (b >= 1) {
-      if (!epilogue(b - 1)) {
-        failed = true;
-        break;
+      const float *dsc = dring + (b & 3) * kGemmN + 64 * half;
+      const float *dmn = mring + (b & 3) * kGemmN + 64 * half;
+      const uint32_t base =
+          tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)(us * (L::kTmemCols / 2) + 64 * half);
+#pragma unroll
+      for (int part = 0; part < 4; ++part) {
+        uint32_t rv[16];
+        tmem_ld16(base + (uint32_t)(16 * part), rv);
+        if (KIND == 35) {
+          tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int cc = 16 * part + c;
+            acc[cc] = __fadd_rn(acc[cc], __fmul_rn((float)(int)rv[c], __fmul_rn(dsc[cc], sa)));
+          }
+        } else {
+          uint32_t mv[16];
+          tmem_ld16(base + (uint32_t)(kGemmN + 16 * part), mv);
+          tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int cc = 16 * part + c;
+            const float t1 = __fmul_rn(__fmul_rn(sa, dsc[cc]), (float)(int)rv[c]);
+            const float t2 = __fmul_rn(__fmul_rn(sa, dmn[cc]), (float)(int)mv[c]);
+            acc[cc] = __fadd_rn(acc[cc], __fsub_rn(t1, t2));
+          }
+        }
       }
       tc_fence_before();
-      __syncthreads();  // accumulator (b-1)&1 read; load stage (b-1)%3 consumed
-      if (tid == 0 && b + 2 < nb) issue_loads(b + 2);
+      mbar_arrive(&aempty[us]);
     }
   }
-  if (!failed && !epilogue(nb - 1)) failed = true;
 
-  // outputs: the 128 x 128 tile goes through shared memory (row pitch 129
-  // floats) so that the global stores run along rows
+  // ---- outputs: 128 x 128 tile through shared memory (row pitch 129) ------
   constexpr int kPitch = kGemmN + 1;
   float *otile = reinterpret_cast<float *>(gsm);
   tc_fence_before();
   __syncthreads();
-  if (!failed) {
+  const bool ok = *fail == 0;
+  if (ok && warp >= kWarpEpi) {
+    const int q4 = warp & 3, half = (warp - kWarpEpi) >> 2;
+    const int tl = 32 * q4 + lane;
     bool finite = true;
 #pragma unroll
     for (int c = 0; c < 64; ++c) {
       otile[tl * kPitch + 64 * half + c] = acc[c];
       if (n0 + 64 * half + c < g.rows) finite &= is_finite_f(acc[c]);
     }
-    if (mvalid && !finite) report(g.status, kStatusNonfinite);
+    if (m0 + tl < g.M && !finite) report(g.status, kStatusNonfinite);
   }
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, L::kTmemCols);
-  if (!failed) {
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::kTmemCols);
+  }
+  if (ok) {
     for (int i = tid; i < kGemmM * kGemmN; i += kGemmThreads) {
       const int t = i / kGemmN, c = i % kGemmN;
       const int mm = m0 + t, n = n0 + c;
@@ -444,40 +482,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ---- host side -----------------------------------------------------------
-
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-inline EncodeTiledFn encode_tiled_fn() {
-  static EncodeTiledFn fn = [] {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
-            cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      return (EncodeTiledFn) nullptr;
-    return reinterpret_cast<EncodeTiledFn>(p);
-  }();
-  return fn;
-}
-
-// u8 tensor viewed as [d2][d1][16 B] with byte strides s1 (d1) and s2 (d2);
-// box 16 x box1 x box2.
-inline bool encode_rows16(CUtensorMap *map, const void *base, uint64_t d1, uint64_t d2,
-                          uint64_t s1, uint64_t s2, uint32_t box1, uint32_t box2) {
-  EncodeTiledFn fn = encode_tiled_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[3] = {16, d1, d2};
-  const cuuint64_t strides[2] = {s1, s2};
-  const cuuint32_t box[3] = {16, box1, box2};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
 
 template <int KIND>
 constexpr int gemm_smem_bytes() {
@@ -497,19 +501,14 @@ inline cudaError_t launch_token_gemm(const DeviceWeight &dw, const float *x, siz
   cudaError_t e = cudaLaunchKernelEx(&cfg, q8k_tokens_kernel, x, (int)M, nb, pinned, t, status);
   if (e != cudaSuccess) return e;
   GemmArgs g;
-  memset(&g, 0, sizeof(g));
-  if (!encode_rows16(&g.codes_map, t.codes, M, (uint64_t)nb * 16, (uint64_t)nb * 256, 16,
-                     kGemmM, 16) ||
-      !encode_rows16(&g.split_map, t.split, M, (uint64_t)nb * 2, (uint64_t)nb * 32, 16, kGemmM,
-                     2))
-    return cudaErrorInvalidValue;
+  g.codes = t.codes;
+  g.split = t.split;
   g.w = dw.units;
   g.h = dw.h;
   g.nb = nb;
   g.rows = (int)dw.rows;
   g.ntiles = dw.ntiles;
   g.scale = t.scale;
-  g.asum = t.asum;
   g.M = (int)M;
   g.y = y;
   g.status = status;

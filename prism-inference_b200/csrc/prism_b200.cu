@@ -379,16 +379,17 @@ int prism_b200_project_f32_tokens_device(prism_b200_executor *ex, const prism_b2
   CK(cudaSetDevice(ex->device), "select device");
   const DeviceWeight &dw = w->dw;
   const size_t M = tokens, nb = dw.nb;
-  // Q8_K tokens: codes [M][K] | split sums [M][nb][32] | scale [M][nb] |
-  // asum [M][nb]; codes and split start 16-byte aligned (TMA sources)
-  const size_t codes = M * nb * 256, meta = M * nb;
-  CK(ex->tok_act.ensure(codes + meta * 32 + meta * 4 * 2), "token activation buffer");
+  // Q8_K tokens, tile-major over 128-token tiles: codes | split sums, then
+  // scale [M][nb]; codes and split stay 16-byte aligned (bulk-copy
+  // sources).  Rows of the last tile past M are never stored.
+  const size_t mpad = (M + kGemmM - 1) / kGemmM * kGemmM;
+  const size_t codes = mpad * nb * 256, split = mpad * nb * 32, meta = M * nb;
+  CK(ex->tok_act.ensure(codes + split + meta * 4), "token activation buffer");
   uint8_t *base = static_cast<uint8_t *>(ex->tok_act.ptr);
   TokenQ8K t;
   t.codes = reinterpret_cast<int8_t *>(base);
   t.split = reinterpret_cast<int8_t *>(base + codes);
-  t.scale = reinterpret_cast<float *>(base + codes + meta * 32);
-  t.asum = reinterpret_cast<int *>(base + codes + meta * 36);
+  t.scale = reinterpret_cast<float *>(base + codes + split);
   cudaStream_t s = pick(ex, stream);
   CK(launch_token_gemm(dw, x_dev, M, pinned, t, out_dev, ex->d_status, s, ex->pdl),
      "token projection launch");

@@ -288,6 +288,19 @@ int prism_b200_model_finalize(prism_b200_model *m);
 int prism_b200_model_reset(prism_b200_model *m);
 int64_t prism_b200_model_position(const prism_b200_model *m);
 
+/* 1 when a step runs as one persistent cooperative kernel (weights streamed
+ * across layer boundaries; chosen with PRISM_B200_PERSIST=1 set before
+ * finalize), 0 when it runs as the per-phase kernel sequence.  Both give
+ * the same bits.  No counterpart in the reference. */
+int prism_b200_model_persistent(const prism_b200_model *m);
+
+/* The phase boundaries (globaltimer ns, [start, end] per phase, CTA 0) of
+ * the last prism_b200_model_step_timings step of a persistent model; copies
+ * at most `count` values and returns how many (0 for a non-persistent
+ * model).  Phases: embedding, then per layer three attention-side phases
+ * and the FFN pair, then the LM head.  No counterpart in the reference. */
+int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t count);
+
 /* One token at the next position (reference Decoder::evaluate_finite_into,
  * src/graph.rs:5446).  `logits` (host, vocab floats) and `greedy` (the
  * reference's greedy selection, src/runtime.rs:2630) are optional. */

@@ -158,6 +158,7 @@ def _declare_model(L):
         ("prism_b200_model_finalize", i32, [vp]),
         ("prism_b200_model_reset", i32, [vp]),
         ("prism_b200_model_position", c.c_int64, [vp]),
+        ("prism_b200_model_persistent", i32, [vp]),
         ("prism_b200_model_evaluate", i32, [vp, u32, vp, vp]),
         ("prism_b200_model_generate", i32, [vp, vp, sz, sz, vp]),
         ("prism_b200_model_decode_async", i32, [vp, sz]),
@@ -222,6 +223,11 @@ class Qwen35Model:
     @property
     def position(self):
         return self.L.prism_b200_model_position(self.h)
+
+    @property
+    def persistent(self):
+        """True when each step runs as one persistent cooperative kernel."""
+        return bool(self.L.prism_b200_model_persistent(self.h))
 
     def evaluate(self, token, logits=True):
         import ctypes as c

@@ -294,11 +294,15 @@ int64_t prism_b200_model_position(const prism_b200_model *m);
  * the same bits.  No counterpart in the reference. */
 int prism_b200_model_persistent(const prism_b200_model *m);
 
-/* The phase boundaries (globaltimer ns, [start, end] per phase, CTA 0) of
- * the last prism_b200_model_step_timings step of a persistent model; copies
- * at most `count` values and returns how many (0 for a non-persistent
- * model).  Phases: embedding, then per layer three attention-side phases
- * and the FFN pair, then the LM head.  No counterpart in the reference. */
+/* CTA 0's timeline of the last prism_b200_model_step_timings step of a
+ * persistent model, 8 values per phase: [0] start (barrier passed) and
+ * [7] end (arrival at the next barrier) in globaltimer ns; [5] start,
+ * [1] inputs staged, [2] first tiles resident, [3] their dots done,
+ * [4] their chains done in SM clock cycles (projection phases only).
+ * Copies at most `count` values and returns how many (0 for a
+ * non-persistent model).  Phases: embedding, then per layer three
+ * attention-side phases and the FFN pair, then the LM head.  No counterpart
+ * in the reference. */
 int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t count);
 
 /* One token at the next position (reference Decoder::evaluate_finite_into,

@@ -59,7 +59,7 @@ struct prism_b200_model {
   int nphases = 0, nphases_ingest = 0;
   unsigned *d_sync = nullptr, *d_hsync = nullptr;
   int nhsync = 0;
-  unsigned long long *d_trace = nullptr;  // [2 * phases] of a traced step
+  unsigned long long *d_trace = nullptr;  // [8 * phases] of a traced step
   float *gdn_o = nullptr, *smax = nullptr;
   double *stot = nullptr, *apart = nullptr;
   std::map<std::string, bool> bound;
@@ -429,7 +429,7 @@ inline cudaError_t prepare_persistent(prism_b200_model *m) {
     // a model's layer count, and so its phase count, is fixed at creation
     cudaError_t e = model_alloc(m, &m->d_phases, P.size());
     if (e == cudaSuccess) e = model_alloc(m, &m->d_ptiles, P.size());
-    if (e == cudaSuccess) e = model_alloc(m, &m->d_trace, 2 * P.size());
+    if (e == cudaSuccess) e = model_alloc(m, &m->d_trace, 8 * P.size());
     if (e != cudaSuccess) return e;
   }
   m->nphases = (int)P.size();
@@ -805,7 +805,7 @@ int prism_b200_model_persistent(const prism_b200_model *m) { return m && m->pers
 int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t count) {
   if (!m || !ns) return -PRISM_B200_E_INVALID;
   if (!m->persist) return 0;
-  const size_t n = std::min(count, (size_t)2 * m->nphases);
+  const size_t n = std::min(count, (size_t)8 * m->nphases);
   if (cudaMemcpy(ns, m->d_trace, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
     return -PRISM_B200_E_DEVICE;
   return (int64_t)n;
@@ -946,22 +946,25 @@ int prism_b200_model_step_timings(prism_b200_model *m, float *attention_ms, floa
   if (m->persist) {
     // one traced persistent step: CTA 0's phase boundaries (barrier waits
     // included in the phase that follows them)
-    std::vector<unsigned long long> t((size_t)2 * m->nphases);
+    std::vector<unsigned long long> t((size_t)8 * m->nphases);
     cudaError_t e = prism::launch_persistent(m, true, true);
     if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
     if (e == cudaSuccess)
       e = cudaMemcpy(t.data(), m->d_trace, t.size() * 8, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return cuda_fail(ex, e, "traced step");
-    auto ms = [&](int a, int b) { return (float)((double)(t[b] - t[a]) * 1e-6); };
+    auto end = [&](int q) { return t[(size_t)8 * q + 7]; };
+    auto ms = [](unsigned long long a, unsigned long long b) {
+      return (float)((double)(b - a) * 1e-6);
+    };
     int p = 1;  // phase 0 is the embedding
     for (int l = 0; l < nl; ++l) {
       const int ffn = p + 3;  // three attention-side phases, then the FFN pair
-      if (attention_ms) attention_ms[l] = ms(2 * p - 1, 2 * ffn - 1);
-      if (ffn_ms) ffn_ms[l] = ms(2 * ffn - 1, 2 * (ffn + 2) - 1);
+      if (attention_ms) attention_ms[l] = ms(end(p - 1), end(ffn - 1));
+      if (ffn_ms) ffn_ms[l] = ms(end(ffn - 1), end(ffn + 1));
       p = ffn + 2;
     }
-    if (head_ms) *head_ms = ms(2 * p - 1, 2 * p + 1);
-    if (total_ms) *total_ms = ms(0, 2 * m->nphases - 1);
+    if (head_ms) *head_ms = ms(end(p - 1), end(p));
+    if (total_ms) *total_ms = ms(t[0], end(m->nphases - 1));
     st = model_finish(m);
     if (st) return st;
     m->position += 1;

@@ -39,15 +39,18 @@ constexpr int kPMaxScores = 2048;
 // shared-memory layout
 constexpr int kPActBytes = 19456;                  // MatvecSmem activation area, nb <= 64
 constexpr int kPTermsBytes = 2 * kMaxNb * 32 * 4;  // terms [upt][h]
-constexpr int kPScratchBytes = 8192 + kPMaxScores * 4;
+constexpr int kPScratchBytes = 24576;  // attention: 8 KB + kPMaxScores scores
 constexpr int kPOffAct = kRingBytes;
 constexpr int kPOffTerms = kPOffAct + kPActBytes;
 constexpr int kPOffScratch = kPOffTerms + kPTermsBytes;
 constexpr int kPOffMeta = kPOffScratch + kPScratchBytes;  // bars, ring offsets/lengths, flags
+// terms + scratch form one contiguous work area, used to stage a phase's
+// inputs before the terms are written
+constexpr int kPWorkBytes = kPTermsBytes + kPScratchBytes;
 constexpr int kPOffPlan = kPOffMeta + kRingSlots * 16 + 64;  // the producer's phase plan
-constexpr int kPOffPhase = kPOffPlan + 128;                 // this phase's descriptor
+constexpr int kPOffPhase = kPOffPlan + 128;                 // phase descriptors, double-buffered
 constexpr int kPPhaseBytes = 1024;
-constexpr int kPSmemBytes = kPOffPhase + kPPhaseBytes;
+constexpr int kPSmemBytes = kPOffPhase + 2 * kPPhaseBytes;
 
 enum PhaseType : int { kPhEmbed = 0, kPhMatvec = 1, kPhGdn = 2, kPhAttn = 3 };
 enum PPrologue : int { kPPRms = 0, kPPF32 = 1, kPPGated = 2 };
@@ -110,7 +113,11 @@ struct PersistArgs {
   unsigned *hsync;      // all attention arrival counters (zeroed at step end)
   int nhsync;
   unsigned *status;
-  unsigned long long *trace;  // optional: CTA 0's [start, end] time of each phase
+  // optional, CTA 0's timeline: 8 slots per phase -- [0] start (after the
+  // barrier) and [7] end (arrival at the next barrier) in globaltimer ns;
+  // [5] start, [1] inputs staged, [2] first tiles resident, [3] their dots
+  // done, [4] their chains done in SM clock cycles (projections only)
+  unsigned long long *trace;
 };
 
 // ---- synchronisation -------------------------------------------------------
@@ -199,7 +206,7 @@ template <int KIND>
 __device__ bool grid_barrier(const PersistArgs &pa, unsigned k, Producer &pr, uint8_t *ring,
                              const RingMeta &rm) {
   __syncthreads();
-  if (pa.trace && blockIdx.x == 0 && threadIdx.x == 0) pa.trace[2 * (k - 1) + 1] = global_timer_ns();
+  if (pa.trace && blockIdx.x == 0 && threadIdx.x == 0) pa.trace[8 * (k - 1) + 7] = global_timer_ns();
   if (threadIdx.x == 0) {
     int ok = 1;
     // release: this CTA's writes (ordered by the bar.sync above) before the arrival
@@ -256,11 +263,13 @@ __device__ bool head_barrier(const PersistArgs &pa, unsigned *counter, unsigned 
 // Gated output norm of the GDN heads (the tail of gdn_decode_kernel):
 // y = RMSNorm(o_h) * w * SiLU(z), one warp per head, the binary64 sum of
 // squares in the same order as the 512-thread block sum of that kernel.
-__device__ void gated_heads(const PMatvec &mv, float *out) {
+// o, z, w are shared-memory copies.
+__device__ void gated_heads(const PMatvec &mv, const float *o_all, const float *z_all,
+                            const float *w, float *out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = mv.head_dim;  // 128
   for (int h = warp; h < mv.heads; h += kPWarps) {
-    const float *o = mv.in + (long)h * S;
+    const float *o = o_all + h * S;
     double t = 0.0;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -272,11 +281,35 @@ __device__ void gated_heads(const PMatvec &mv, float *out) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int i = 32 * q + lane;
-      const float normed = __fmul_rn(__fmul_rn(o[i], nscale), mv.norm_w[i]);
-      const float y = __fmul_rn(normed, silu_f(mv.zgate[(long)h * S + i]));
+      const float normed = __fmul_rn(__fmul_rn(o[i], nscale), w[i]);
+      const float y = __fmul_rn(normed, silu_f(z_all[h * S + i]));
       out[h * S + i] = y;
       if (blockIdx.x == 0 && mv.gated_out) mv.gated_out[h * S + i] = y;
     }
+  }
+}
+
+// Copy n floats (n % 4 == 0) from global to shared memory, all threads.
+__device__ __forceinline__ void load_f32(float *dst, const float *src, int n) {
+  for (int i = threadIdx.x * 4; i < n; i += kPThreads * 4)
+    *reinterpret_cast<float4 *>(dst + i) = *reinterpret_cast<const float4 *>(src + i);
+}
+
+// Two units of one tile height at once: independent work for the scheduler
+// to interleave (each unit's dot is a short dependent chain).
+template <int KIND, int H>
+__device__ __forceinline__ void unit_pair(const uint8_t *ua, const int8_t *ava, int asa,
+                                          const int16_t *gsa, float sa_, float *outa,
+                                          const uint8_t *ub, const int8_t *avb, int asb,
+                                          const int16_t *gsb, float sb_, float *outb,
+                                          int lane) {
+  int da, db, d2a, d2b;
+  float ta, tb;
+  unit_terms<KIND, H>(ua, ava, asa, gsa, sa_, lane, da, d2a, ta);
+  unit_terms<KIND, H>(ub, avb, asb, gsb, sb_, lane, db, d2b, tb);
+  if (lane < H) {
+    outa[lane % H] = ta;
+    outb[lane % H] = tb;
   }
 }
 
@@ -301,7 +334,9 @@ __device__ __forceinline__ void unit_dispatch(int H, const uint8_t *unit, const 
 // then every row's chain runs at once (one thread per row).
 template <int KIND>
 __device__ bool run_matvec(const PMatvec &mv, const PersistArgs &pa, uint8_t *smem,
-                           Producer &pr, const RingMeta &rm, int &cons) {
+                           Producer &pr, const RingMeta &rm, int &cons, int phase) {
+  unsigned long long *tr =
+      pa.trace && blockIdx.x == 0 && threadIdx.x == 0 ? pa.trace + 8 * phase : nullptr;
   const int T = mv.ntiles, G = gridDim.x;
   if ((int)blockIdx.x >= T) return true;
   const bool pair = mv.epi == kEpiSwiglu;
@@ -309,7 +344,7 @@ __device__ bool run_matvec(const PMatvec &mv, const PersistArgs &pa, uint8_t *sm
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint8_t *act = smem + kPOffAct;
   float *terms = reinterpret_cast<float *>(smem + kPOffTerms);
-  float *scratch = reinterpret_cast<float *>(smem + kPOffScratch);
+  float *work = terms;  // [kPWorkBytes]: staged inputs, then terms
   const MatvecSmem L(nb, 32, unit_bytes(KIND, 32), upt);
   MvArgs sa;
   sa.nb = nb;
@@ -320,19 +355,33 @@ __device__ bool run_matvec(const PMatvec &mv, const PersistArgs &pa, uint8_t *sm
   sa.prologue = mv.prologue == kPPRms ? kProRmsNorm : kProF32;
   sa.in0 = mv.in;
   const int n = nb * 256;
+  // stage the inputs into shared memory with all loads in flight at once
   if (mv.prologue == kPPGated) {
-    gated_heads(mv, scratch);
+    const int S = mv.head_dim;
+    float *o = work, *z = work + n, *w = work + 2 * n, *y = work + 2 * n + S;
+    if ((3 * n + S) * 4 <= kPWorkBytes) {
+      load_f32(o, mv.in, n);
+      load_f32(z, mv.zgate, n);
+      load_f32(w, mv.norm_w, S);
+      __syncthreads();
+      gated_heads(mv, o, z, w, y);
+      __syncthreads();
+      sa.in0 = y;
+    }
+  } else if (mv.prologue == kPPRms && 2 * n * 4 <= kPWorkBytes) {
+    load_f32(work, mv.in, n);
+    load_f32(work + n, mv.norm_w, n);
     __syncthreads();
-    sa.in0 = scratch;
-  } else if (mv.prologue == kPPRms && n * 4 <= kPScratchBytes) {
-    // one read of x from L2; both passes of the norm then read shared memory
-    for (int i = tid * 4; i < n; i += kPThreads * 4)
-      *reinterpret_cast<float4 *>(scratch + i) = *reinterpret_cast<const float4 *>(mv.in + i);
+    sa.in0 = work;
+    sa.norm_w = work + n;
+  } else if (mv.prologue == kPPF32 && n * 4 <= kPWorkBytes) {
+    load_f32(work, mv.in, n);
     __syncthreads();
-    sa.in0 = scratch;
+    sa.in0 = work;
   }
   stage_from_f32(sa, L, act);
   __syncthreads();
+  if (tr) tr[1] = clock64();
   const int8_t *values = reinterpret_cast<const int8_t *>(act + L.act_values());
   const float *ascale = reinterpret_cast<const float *>(act + L.act_scale());
   const int16_t *asums = reinterpret_cast<const int16_t *>(act + L.act_sums());
@@ -347,10 +396,25 @@ __device__ bool run_matvec(const PMatvec &mv, const PersistArgs &pa, uint8_t *sm
   const int fit = kRingBytes / maxtile - 1;  // one tile's worth lost to wrap padding
   int cap = min(kPWarps, (kPTermsBytes / 4) / (upt * 32));
   cap = mine <= min(cap, fit) ? mine : min(cap, max(1, fit / 2));
+  auto group_of_tile = [&](int t) {
+    int g = 0;
+    if (!pair)
+      for (int i = 1; i < mv.count; ++i)
+        if (t >= mv.tile_start[i]) g = i;
+    return g;
+  };
   unsigned long long best = 0ull;
   for (int k0 = 0; k0 < mine; k0 += cap) {
     const int B = min(cap, mine - k0);
-    if (tid == 0) pump<KIND>(pr, pa, smem, rm);
+    // the chain thread of this batch (warp = tile, lane = row) loads its
+    // residual now, so the load overlaps the dot products
+    const int ck = warp, ct = blockIdx.x + (k0 + ck) * G;
+    const int cg = ck < B ? group_of_tile(ct) : 0;
+    const MvWeight &cw = mv.w[cg];
+    const int corow = (pair ? ct : ct - mv.tile_start[cg]) * cw.h + lane;
+    const bool chain = ck < B && lane < cw.h;
+    if (tid == 0 && pr.issued < cons + B) pump<KIND>(pr, pa, smem, rm);
+    if (tr && k0 == 0) tr[6] = clock64();
     bool arrived = true;
     for (int k = 0; k < B && arrived; ++k)
       arrived = mbar_wait_bounded(&rm.bar[(cons + k) % kRingSlots],
@@ -359,61 +423,80 @@ __device__ bool run_matvec(const PMatvec &mv, const PersistArgs &pa, uint8_t *sm
       if (tid == 0) raise_abort(pa);
       return false;
     }
-    for (int u = warp; u < B * upt; u += kPWarps) {
+    if (tr && k0 == 0) tr[2] = clock64();
+    const int total = B * upt;
+    for (int u = warp; u < total; u += 2 * kPWarps) {
+      const int u2 = u + kPWarps;
       const int k = u / upt, j = u - k * upt;
-      const int t = blockIdx.x + (k0 + k) * G;
-      int g = 0;
-      if (!pair)
-        for (int i = 1; i < mv.count; ++i)
-          if (t >= mv.tile_start[i]) g = i;
+      const int g = group_of_tile(blockIdx.x + (k0 + k) * G);
       const int H = mv.w[g].h;
       const uint8_t *data = smem + rm.off[(cons + k) % kRingSlots];
       const int b = pair && j >= nb ? j - nb : j;
-      unit_dispatch<KIND>(H, data + j * unit_bytes(KIND, H), values + b * 256, aasum[b],
-                          asums + b * 16, ascale[b], lane, terms + k * upt * 32 + j * H);
+      const uint8_t *ua = data + j * unit_bytes(KIND, H);
+      float *oa = terms + k * upt * 32 + j * H;
+      int H2 = -1, b2 = 0;
+      const uint8_t *ub = nullptr;
+      float *ob = nullptr;
+      if (u2 < total) {
+        const int k2 = u2 / upt, j2 = u2 - k2 * upt;
+        const int g2 = group_of_tile(blockIdx.x + (k0 + k2) * G);
+        H2 = mv.w[g2].h;
+        b2 = pair && j2 >= nb ? j2 - nb : j2;
+        ub = smem + rm.off[(cons + k2) % kRingSlots] + j2 * unit_bytes(KIND, H2);
+        ob = terms + k2 * upt * 32 + j2 * H2;
+      }
+      if (H2 == H) {
+        if (H == 32)
+          unit_pair<KIND, 32>(ua, values + b * 256, aasum[b], asums + b * 16, ascale[b], oa, ub,
+                              values + b2 * 256, aasum[b2], asums + b2 * 16, ascale[b2], ob, lane);
+        else if (H == 16)
+          unit_pair<KIND, 16>(ua, values + b * 256, aasum[b], asums + b * 16, ascale[b], oa, ub,
+                              values + b2 * 256, aasum[b2], asums + b2 * 16, ascale[b2], ob, lane);
+        else
+          unit_pair<KIND, 8>(ua, values + b * 256, aasum[b], asums + b * 16, ascale[b], oa, ub,
+                             values + b2 * 256, aasum[b2], asums + b2 * 16, ascale[b2], ob, lane);
+      } else {
+        unit_dispatch<KIND>(H, ua, values + b * 256, aasum[b], asums + b * 16, ascale[b], lane,
+                            oa);
+        if (H2 > 0)
+          unit_dispatch<KIND>(H2, ub, values + b2 * 256, aasum[b2], asums + b2 * 16, ascale[b2],
+                              lane, ob);
+      }
     }
     __syncthreads();
-    {
-      const int k = warp, r = lane;
-      if (k < B) {
-        const int t = blockIdx.x + (k0 + k) * G;
-        int g = 0;
-        if (!pair)
-          for (int i = 1; i < mv.count; ++i)
-            if (t >= mv.tile_start[i]) g = i;
-        const MvWeight &w = mv.w[g];
-        const int H = w.h;
-        const float *tk = terms + k * upt * 32;
-        if (r < H) {
-          // the reference's chain: sum = 0; sum += term_b for b in order
-          float sum = 0.0f;
-          for (int b = 0; b < nb; ++b) sum = __fadd_rn(sum, tk[b * H + r]);
-          const int lt = pair ? t : t - mv.tile_start[g];
-          const int orow = lt * H + r;
-          if (pair) {
-            float gsum = 0.0f;
-            for (int b = nb; b < 2 * nb; ++b) gsum = __fadd_rn(gsum, tk[b * H + r]);
-            if (orow < w.rows) {
-              const float hv = __fmul_rn(sum, silu_f(gsum));
-              if (!is_finite_f(sum) || !is_finite_f(gsum)) report(pa.status, kStatusNonfinite);
-              w.y[orow] = hv;
-            }
-          } else if (orow < w.rows) {
-            if (w.residual) sum = __fadd_rn(w.residual[orow], sum);
-            if (!is_finite_f(sum)) report(pa.status, kStatusNonfinite);
-            if (w.y) w.y[orow] = sum;
-            if (mv.epi == kEpiArgmax) {
-              const unsigned long long key = argmax_key(sum, orow);
-              best = key > best ? key : best;
-            }
-          }
+    if (tr && k0 == 0) tr[3] = clock64();
+    if (chain) {
+      const int H = cw.h, r = lane;
+      const float *tk = terms + ck * upt * 32;
+      // the reference's chain: sum = 0; sum += term_b for b in order
+      float sum = 0.0f;
+      for (int b = 0; b < nb; ++b) sum = __fadd_rn(sum, tk[b * H + r]);
+      if (pair) {
+        float gsum = 0.0f;
+        for (int b = nb; b < 2 * nb; ++b) gsum = __fadd_rn(gsum, tk[b * H + r]);
+        if (corow < cw.rows) {
+          const float hv = __fmul_rn(sum, silu_f(gsum));
+          if (!is_finite_f(sum) || !is_finite_f(gsum)) report(pa.status, kStatusNonfinite);
+          cw.y[corow] = hv;
+        }
+      } else if (corow < cw.rows) {
+        if (cw.residual) sum = __fadd_rn(cw.residual[corow], sum);
+        if (!is_finite_f(sum)) report(pa.status, kStatusNonfinite);
+        if (cw.y) cw.y[corow] = sum;
+        if (mv.epi == kEpiArgmax) {
+          const unsigned long long key = argmax_key(sum, corow);
+          best = key > best ? key : best;
         }
       }
     }
     __syncthreads();  // the batch's ring space is free again
+    if (tr && k0 == 0) tr[4] = clock64();
     if (tid == 0) {
       for (int k = 0; k < B; ++k) pr.tail += rm.len[(cons + k) % kRingSlots];
       pr.consumed += B;
+      // more batches: stream the next one now; otherwise the barrier's
+      // wait loop streams the following phases
+      if (k0 + cap < mine) pump<KIND>(pr, pa, smem, rm);
     }
     cons += B;
   }
@@ -706,26 +789,36 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(Persist
   int cons = 0;
   unsigned barrier = 0;
   bool ok = true;
+  // descriptor p is read into buffer p&1 before the barrier that precedes
+  // phase p, so its load latency hides behind the barrier
+  auto fetch = [&](int p) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(pa.phases + p);
+    uint4 *dst = reinterpret_cast<uint4 *>(smem + kPOffPhase + (p & 1) * kPPhaseBytes);
+    for (int i = threadIdx.x; i < (int)(sizeof(Phase) / 16); i += kPThreads) dst[i] = src[i];
+  };
+  fetch(0);
   for (int p = 0; p < pa.nphases && ok; ++p) {
-    if (p > 0 && !grid_barrier<KIND>(pa, ++barrier, pr, smem, rm)) {
-      ok = false;
-      break;
-    }
-    if (pa.trace && blockIdx.x == 0 && threadIdx.x == 0) pa.trace[2 * p] = global_timer_ns();
-    // one coalesced read of the phase descriptor into shared memory
-    {
-      const uint4 *src = reinterpret_cast<const uint4 *>(pa.phases + p);
-      uint4 *dst = reinterpret_cast<uint4 *>(cur);
-      for (int i = threadIdx.x; i < (int)(sizeof(Phase) / 16); i += kPThreads) dst[i] = src[i];
+    if (p > 0) {
+      fetch(p);
+      if (!grid_barrier<KIND>(pa, ++barrier, pr, smem, rm)) {
+        ok = false;
+        break;
+      }
+    } else {
       __syncthreads();
     }
+    if (pa.trace && blockIdx.x == 0 && threadIdx.x == 0) {
+      pa.trace[8 * p] = global_timer_ns();
+      pa.trace[8 * p + 5] = clock64();
+    }
+    cur = reinterpret_cast<Phase *>(smem + kPOffPhase + (p & 1) * kPPhaseBytes);
     const Phase *ph = cur;
     switch (ph->type) {
       case kPhEmbed:
         run_embed<KIND>(ph->em, pa.st, pos, pa.status);
         break;
       case kPhMatvec:
-        ok = run_matvec<KIND>(ph->mv, pa, smem, pr, rm, cons);
+        ok = run_matvec<KIND>(ph->mv, pa, smem, pr, rm, cons, p);
         break;
       case kPhGdn:
         run_gdn(ph->gdn, pos, smem + kPOffScratch);
@@ -743,7 +836,7 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(Persist
   // the last CTA to finish advances the step and clears the counters
   __syncthreads();
   if (pa.trace && blockIdx.x == 0 && threadIdx.x == 0 && ok)
-    pa.trace[2 * pa.nphases - 1] = global_timer_ns();
+    pa.trace[8 * pa.nphases - 1] = global_timer_ns();
   if (threadIdx.x == 0 && ok) {
     __threadfence();
     const unsigned done = atomicAdd(&pa.sync[1], 1u);

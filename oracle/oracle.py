@@ -192,7 +192,8 @@ class _Cfg(ctypes.Structure):
                 ("vocab", ctypes.c_int32), ("ssm_state", ctypes.c_int32),
                 ("ssm_groups", ctypes.c_int32), ("ssm_values", ctypes.c_int32),
                 ("conv_kernel", ctypes.c_int32), ("full_interval", ctypes.c_int32),
-                ("context", ctypes.c_int32), ("weight_kind", ctypes.c_uint32)]
+                ("context", ctypes.c_int32), ("weight_kind", ctypes.c_uint32),
+                ("kv_policy", ctypes.c_uint32)]
 
 
 W_SLOTS = ["attn_norm.weight", "post_attention_norm.weight", "ffn_gate.weight", "ffn_up.weight",
@@ -225,11 +226,13 @@ def _model_lib():
     return L
 
 
-def make_cfg(cfg):
+def make_cfg(cfg, kv_policy=0):
     c = _Cfg()
     for f, _ in _Cfg._fields_:
         if f == "rope_sections":
             c.rope_sections = (ctypes.c_int32 * 4)(*cfg.rope_sections)
+        elif f == "kv_policy":
+            c.kv_policy = kv_policy
         else:
             setattr(c, f, getattr(cfg, f))
     return c
@@ -238,11 +241,11 @@ def make_cfg(cfg):
 class Qwen35:
     """The reference decode step on the CPU (Source arithmetic)."""
 
-    def __init__(self, cfg, weights):
+    def __init__(self, cfg, weights, kv_policy=0):
         L = _model_lib()
         self.cfg = cfg
         self._keep = {k: np.ascontiguousarray(v) for k, v in weights.items()}
-        self._c = make_cfg(cfg)
+        self._c = make_cfg(cfg, kv_policy)
         g = (ctypes.c_void_p * 2)(self._keep["token_embd.weight"].ctypes.data,
                                   self._keep["output_norm.weight"].ctypes.data)
         n = cfg.layers * len(W_SLOTS)

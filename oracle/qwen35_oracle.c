@@ -185,6 +185,72 @@ static int norm_rope_round(const po_qwen35_config *c, const float *in, const flo
   return PO_OK;
 }
 
+/* Q8_0 record of one KV head's row: scales then codes. */
+static int q8_record(const float *x, int hd, uint8_t *rec) {
+  po_q8_0_block blk[32];
+  int st = po_q8_0_quantize(x, (size_t)hd, blk);
+  if (st) return st;
+  for (int j = 0; j < hd / 32; ++j) {
+    memcpy(rec + 2 * j, &blk[j].d, 2);
+    memcpy(rec + hd / 32 * 2 + 32 * j, blk[j].values, 32);
+  }
+  return PO_OK;
+}
+
+static void q8_dequant(const uint8_t *rec, int hd, float *out) {
+  for (int i = 0; i < hd; ++i) {
+    uint16_t d;
+    memcpy(&d, rec + 2 * (i / 32), 2);
+    out[i] = po_half_to_float(d) * (float)(int8_t)rec[hd / 32 * 2 + i];
+  }
+}
+
+/* The attention of full_attention below over Q8_0 KV records (kv_policy 1):
+ * scores are float_dot(q, dequantized key), values binary64 sums of
+ * binary32 products with the dequantized values; the current position is
+ * quantized first and read back like the history. */
+static int q8_attention(po_qwen35 *m, int l, float scale, int threads) {
+  const po_qwen35_config *c = &m->cfg;
+  const int hd = c->head_dim, rb = PO_KV_Q8_0_RECORD(hd);
+  const int npos = m->position, group = c->heads / c->kv_heads;
+  uint8_t *krec = (uint8_t *)m->keys[l], *vrec = (uint8_t *)m->vals[l];
+  const size_t pstride = (size_t)c->kv_heads * rb;
+  int st;
+  for (int k = 0; k < c->kv_heads; ++k) {
+    if ((st = q8_record(m->key + (size_t)k * hd, hd, krec + npos * pstride + (size_t)k * rb)))
+      return st;
+    if ((st = q8_record(m->value + (size_t)k * hd, hd, vrec + npos * pstride + (size_t)k * rb)))
+      return st;
+  }
+  float kd[1024], vd[1024];
+  for (int h = 0; h < c->heads; ++h) {
+    const int kh = h / group;
+    const float *q = m->query + (size_t)h * hd;
+    for (int p = 0; p <= npos; ++p) {
+      q8_dequant(krec + p * pstride + (size_t)kh * rb, hd, kd);
+      m->scores[p] = po_float_dot(q, kd, (size_t)hd) * scale;
+    }
+    if ((st = po_softmax_round_f16(m->scores, (size_t)npos + 1))) return st;
+    const float *g = m->projected + (size_t)(2 * h + 1) * hd;
+    float *out = m->attended + (size_t)h * hd;
+    double sums[1024];
+    for (int d = 0; d < hd; ++d) sums[d] = -0.0;
+    for (int p = 0; p < npos; ++p) {
+      q8_dequant(vrec + p * pstride + (size_t)kh * rb, hd, vd);
+      for (int d = 0; d < hd; ++d) sums[d] += (double)(m->scores[p] * vd[d]);
+    }
+    q8_dequant(vrec + npos * pstride + (size_t)kh * rb, hd, vd);
+    for (int d = 0; d < hd; ++d) {
+      float v = (float)(sums[d] + (double)(m->scores[npos] * vd[d]));
+      out[d] = v * (1.0f / (1.0f + po_expf(-g[d])));
+    }
+  }
+  const void *wo[1] = {W(m, l, PO_W_O)};
+  int ro[1] = {c->hidden};
+  float *oo[1] = {m->attn_out};
+  return project_group(m, m->attended, c->heads * hd, 1, wo, ro, oo, threads);
+}
+
 /* reference src/graph.rs:4383-4950 full_attention (F16 KV, Source) */
 static int full_attention(po_qwen35 *m, int l, int threads) {
   const po_qwen35_config *c = &m->cfg;
@@ -210,6 +276,7 @@ static int full_attention(po_qwen35 *m, int l, int threads) {
   const float scale = 1.0f / sqrtf((float)hd);
   const int npos = m->position;
   const int group = c->heads / c->kv_heads;
+  if (c->kv_policy == 1) return q8_attention(m, l, scale, threads);
   for (int h = 0; h < c->heads; ++h) {
     const int off = (h / group) * hd;
     const float *q = m->query + (size_t)h * hd;

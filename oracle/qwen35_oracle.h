@@ -23,7 +23,18 @@ typedef struct po_qwen35_config {
   int32_t ffn, vocab, ssm_state, ssm_groups, ssm_values, conv_kernel, full_interval;
   int32_t context;
   uint32_t weight_kind; /* 35 (TQ2_0) or 10 (Q2_K) for every linear weight */
+  uint32_t kv_policy;   /* 0: binary16 K/V; 1: Q8_0 records (see below)      */
 } po_qwen35_config;
+
+/* Q8_0 KV records (kv_policy 1; an addition of this build, not a reference
+ * policy): each cached K or V row of one KV head (head_dim values, already
+ * rounded to binary16 as the binary16 policy stores them) is split into
+ * 32-value blocks coded by the reference's Source Q8_0 codec
+ * (src/kernels.rs:552-617 q8_with_input<false,false,_>); the record is the
+ * head_dim/32 binary16 scales followed by the head_dim codes
+ * (272 bytes for head_dim 256).  Attention reads the dequantized values
+ * scale*code (exact in binary32), for the current position too. */
+#define PO_KV_Q8_0_RECORD(hd) ((hd) / 32 * 2 + (hd))
 
 /* Per-layer weight slots (reference tensor names in comments,
  * src/graph.rs:3112-3238).  Linear weights are packed rows in the reference

@@ -70,6 +70,12 @@ struct prism_b200_model {
   int value_width() const { return (int)(cfg.ssm_state * cfg.ssm_values); }
   int channels() const { return 2 * key_width() + value_width(); }
   int kvw() const { return (int)(cfg.kv_heads * cfg.head_dim); }
+  // bytes of one cached position (all KV heads) of one layer's K or V
+  size_t kv_row_bytes() const {
+    return cfg.kv_policy == PRISM_B200_KV_Q8_0
+               ? (size_t)cfg.kv_heads * prism::q8_0_record_bytes((int)cfg.head_dim)
+               : (size_t)kvw() * 2;
+  }
   bool is_full(int l) const { return ((l + 1) % (int)cfg.full_interval) == 0; }
 };
 
@@ -160,6 +166,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
       aa.k_norm = Ly.k_norm;
       aa.kcache = Ly.kc;
       aa.vcache = Ly.vc;
+      aa.q8 = c.kv_policy == PRISM_B200_KV_Q8_0 ? 1 : 0;
       aa.position = m->d_position;
       aa.attended = m->attended;
       aa.status = status;
@@ -337,6 +344,7 @@ inline std::vector<Phase> build_phases(prism_b200_model *m) {
       aa.k_norm = Ly.k_norm;
       aa.kcache = Ly.kc;
       aa.vcache = Ly.vc;
+      aa.q8 = c.kv_policy == PRISM_B200_KV_Q8_0 ? 1 : 0;
       aa.position = m->d_position;
       aa.attended = m->attended;
       aa.status = status;
@@ -532,7 +540,8 @@ int prism_b200_model_create(prism_b200_executor *ex, const prism_b200_qwen35_con
       c.ssm_state == 128 && c.ssm_groups > 0 && c.ssm_values % c.ssm_groups == 0 &&
       (c.ssm_state * c.ssm_values) % 256 == 0 && c.conv_kernel >= 1 && c.conv_kernel <= 8 &&
       c.full_interval > 0 && c.context > 0 && c.context <= (1u << 20) && c.eps > 0.0f &&
-      c.rope_base > 0.0f && c.kv_policy == PRISM_B200_KV_F16 &&
+      c.rope_base > 0.0f &&
+      (c.kv_policy == PRISM_B200_KV_F16 || c.kv_policy == PRISM_B200_KV_Q8_0) &&
       (c.weight_kind == PRISM_B200_KIND_TQ2_0 || c.weight_kind == PRISM_B200_KIND_Q2_K) &&
       c.hidden / 256 <= (uint32_t)kMaxNb && c.ffn / 256 <= (uint32_t)kMaxNb &&
       c.heads * c.head_dim / 256 <= (uint32_t)kMaxNb;
@@ -581,8 +590,8 @@ int prism_b200_model_create(prism_b200_executor *ex, const prism_b200_qwen35_con
     if (Ly.full) {
       A(Ly.q_norm, c.head_dim);
       A(Ly.k_norm, c.head_dim);
-      A(Ly.kc, (size_t)c.context * m->kvw());
-      A(Ly.vc, (size_t)c.context * m->kvw());
+      A(Ly.kc, ((size_t)c.context * m->kv_row_bytes() + 1) / 2);
+      A(Ly.vc, ((size_t)c.context * m->kv_row_bytes() + 1) / 2);
     } else {
       A(Ly.conv_w, (size_t)m->channels() * c.conv_kernel);
       A(Ly.dt_bias, c.ssm_values);
@@ -780,8 +789,8 @@ int prism_b200_model_reset(prism_b200_model *m) {
   cudaStream_t s = m->stream;
   for (auto &Ly : m->L) {
     if (Ly.full) {
-      CK(cudaMemsetAsync(Ly.kc, 0, (size_t)c.context * m->kvw() * 2, s), "reset");
-      CK(cudaMemsetAsync(Ly.vc, 0, (size_t)c.context * m->kvw() * 2, s), "reset");
+      CK(cudaMemsetAsync(Ly.kc, 0, (size_t)c.context * m->kv_row_bytes(), s), "reset");
+      CK(cudaMemsetAsync(Ly.vc, 0, (size_t)c.context * m->kv_row_bytes(), s), "reset");
     } else {
       CK(cudaMemsetAsync(Ly.conv_state, 0, (size_t)2 * m->channels() * (c.conv_kernel - 1) * 4, s),
          "reset");
@@ -1024,7 +1033,7 @@ int64_t prism_b200_model_read_state(prism_b200_model *m, uint32_t layer, uint32_
       n = (size_t)c.ssm_values * c.ssm_state * c.ssm_state * 4;
     } else if ((which == 2 || which == 3) && Ly.full) {
       src = which == 2 ? Ly.kc : Ly.vc;
-      n = (size_t)m->position * m->kvw() * 2;
+      n = (size_t)m->position * m->kv_row_bytes();
     }
   }
   if (!src) return -PRISM_B200_E_INVALID;

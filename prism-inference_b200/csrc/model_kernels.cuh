@@ -283,7 +283,8 @@ struct AttnArgs {
   const float *key_in;      // [kv_heads*hd]
   const float *value_in;    // [kv_heads*hd]
   const float *q_norm, *k_norm;
-  uint16_t *kcache, *vcache;  // [context][kv_heads*hd] binary16 bits
+  uint16_t *kcache, *vcache;  // [context][kv_heads*hd] binary16 bits, or Q8_0 records
+  int q8;                     // 1: Q8_0 records [context][kv_heads][hd/32 scales | hd codes]
   const int *position;
   float *attended;          // [heads*hd]
   unsigned *status;
@@ -316,6 +317,80 @@ __device__ __forceinline__ float norm_rope_round(const float *x, const float *w,
   }
   __syncthreads();
   return round_f16(out);
+}
+
+// Q8_0 record of one KV head's row (an addition of this build): thread i
+// (i < hd) holds value i; each warp codes one 32-value block with the
+// reference's Source Q8_0 codec (src/kernels.rs:552-617: d = max|x|/127,
+// stored as binary16, codes = round-half-away(x * (1/d))).  Writes the
+// record when `rec` is set and returns the dequantized value scale*code.
+__device__ __forceinline__ float q8_0_roundtrip(float x, uint8_t *rec, int hd,
+                                                unsigned *status) {
+  const int i = threadIdx.x, lane = i & 31;
+  float m = fabsf(x);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  const float d = __fdiv_rn(m, 127.0f);
+  const float inv = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+  const uint16_t hb = float_to_half_bits(d);
+  float r = roundf(__fmul_rn(x, inv));
+  if (!(r >= -127.0f && r <= 127.0f)) {
+    report(status, kStatusInvalid);
+    r = 0.0f;
+  }
+  const int q = (int)r;
+  if (rec) {
+    if (lane == 0) reinterpret_cast<uint16_t *>(rec)[i >> 5] = hb;
+    rec[hd / 32 * 2 + i] = (uint8_t)(int8_t)q;
+  }
+  return __fmul_rn(half_bits_to_float(hb), (float)q);
+}
+
+__host__ __device__ constexpr int q8_0_record_bytes(int hd) { return hd / 32 * 2 + hd; }
+
+// Dequantized value j of a Q8_0 record.
+__device__ __forceinline__ float q8_0_value(const uint8_t *rec, int hd, int j) {
+  const float d = half_bits_to_float(reinterpret_cast<const uint16_t *>(rec)[j >> 5]);
+  return __fmul_rn(d, (float)(int8_t)rec[hd / 32 * 2 + j]);
+}
+
+// Score of position p: lane holds q dims lane*8..lane*8+7; binary32 products
+// summed in binary64 (the binary16 or the Q8_0 key row).
+__device__ __forceinline__ double key_partial(const AttnArgs &a, int p, int kvh,
+                                              const float4 &q0, const float4 &q1, int lane) {
+  const int hd = a.hd;
+  float k[8];
+  if (a.q8) {
+    const int rb = q8_0_record_bytes(hd);
+    const uint8_t *rec = reinterpret_cast<const uint8_t *>(a.kcache) +
+                         ((long)p * a.kv_heads + kvh) * rb;
+    const float d = half_bits_to_float(reinterpret_cast<const uint16_t *>(rec)[lane >> 2]);
+    const uint2 c = *reinterpret_cast<const uint2 *>(rec + hd / 32 * 2 + lane * 8);
+    const int8_t *cb = reinterpret_cast<const int8_t *>(&c);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) k[j] = __fmul_rn(d, (float)cb[j]);
+  } else {
+    const uint4 kv = *reinterpret_cast<const uint4 *>(a.kcache + (long)p * a.kv_heads * hd +
+                                                      kvh * hd + lane * 8);
+    const uint16_t *kh = reinterpret_cast<const uint16_t *>(&kv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) k[j] = half_bits_to_float(kh[j]);
+  }
+  return (double)__fmul_rn(q0.x, k[0]) + (double)__fmul_rn(q0.y, k[1]) +
+         (double)__fmul_rn(q0.z, k[2]) + (double)__fmul_rn(q0.w, k[3]) +
+         (double)__fmul_rn(q1.x, k[4]) + (double)__fmul_rn(q1.y, k[5]) +
+         (double)__fmul_rn(q1.z, k[6]) + (double)__fmul_rn(q1.w, k[7]);
+}
+
+// Value dimension i of position p (binary16 or Q8_0 row).
+__device__ __forceinline__ float value_at(const AttnArgs &a, int p, int kvh, int i) {
+  if (a.q8) {
+    const int rb = q8_0_record_bytes(a.hd);
+    return q8_0_value(reinterpret_cast<const uint8_t *>(a.vcache) +
+                          ((long)p * a.kv_heads + kvh) * rb,
+                      a.hd, i);
+  }
+  return half_bits_to_float(a.vcache[(long)p * a.kv_heads * a.hd + kvh * a.hd + i]);
 }
 
 // Attention decode for one query head split over a cluster of kAttnSplit
@@ -388,7 +463,15 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
   kc[i] = norm_rope_round(a.key_in + (long)kvh * hd, a.k_norm, a.eps, hd, a.rope_dim, cs, buf,
                           red);
   vc[i] = round_f16(a.value_in[kvh * hd + i]);
-  if (rank == 0 && h % group == 0) {
+  const bool writer = rank == 0 && h % group == 0;
+  if (a.q8) {
+    const int rb = q8_0_record_bytes(hd);
+    const long at = ((long)pos * a.kv_heads + kvh) * rb;
+    kc[i] = q8_0_roundtrip(kc[i], writer ? reinterpret_cast<uint8_t *>(a.kcache) + at : nullptr,
+                           hd, a.status);
+    vc[i] = q8_0_roundtrip(vc[i], writer ? reinterpret_cast<uint8_t *>(a.vcache) + at : nullptr,
+                           hd, a.status);
+  } else if (writer) {
     a.kcache[(long)pos * kvw + kvh * hd + i] = float_to_half_bits(kc[i]);
     a.vcache[(long)pos * kvw + kvh * hd + i] = float_to_half_bits(vc[i]);
   }
@@ -398,18 +481,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
   const float4 q0 = reinterpret_cast<const float4 *>(q)[lane * 2];
   const float4 q1 = reinterpret_cast<const float4 *>(q)[lane * 2 + 1];
   for (int p = lo + warp; p < hi; p += kAttnThreads / 32) {
-    const uint4 kv =
-        *reinterpret_cast<const uint4 *>(a.kcache + (long)p * kvw + kvh * hd + lane * 8);
-    const uint16_t *kh = reinterpret_cast<const uint16_t *>(&kv);
-    double s = (double)__fmul_rn(q0.x, half_bits_to_float(kh[0])) +
-               (double)__fmul_rn(q0.y, half_bits_to_float(kh[1])) +
-               (double)__fmul_rn(q0.z, half_bits_to_float(kh[2])) +
-               (double)__fmul_rn(q0.w, half_bits_to_float(kh[3])) +
-               (double)__fmul_rn(q1.x, half_bits_to_float(kh[4])) +
-               (double)__fmul_rn(q1.y, half_bits_to_float(kh[5])) +
-               (double)__fmul_rn(q1.z, half_bits_to_float(kh[6])) +
-               (double)__fmul_rn(q1.w, half_bits_to_float(kh[7]));
-    s = warp_sum_f64(s);
+    const double s = warp_sum_f64(key_partial(a, p, kvh, q0, q1, lane));
     if (lane == 0) scores[p - lo] = __fmul_rn((float)s, scale);
   }
   {
@@ -447,17 +519,16 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
   // value partial sums of this chunk: one dimension per thread, position order
   {
     double acc = -0.0;
-    const uint16_t *vcol = a.vcache + kvh * hd + i;
     int p = lo;
     for (; p + 4 <= hi; p += 4) {
-      const uint16_t v0 = vcol[(long)p * kvw], v1 = vcol[(long)(p + 1) * kvw];
-      const uint16_t v2 = vcol[(long)(p + 2) * kvw], v3 = vcol[(long)(p + 3) * kvw];
-      acc += (double)__fmul_rn(scores[p - lo], half_bits_to_float(v0));
-      acc += (double)__fmul_rn(scores[p + 1 - lo], half_bits_to_float(v1));
-      acc += (double)__fmul_rn(scores[p + 2 - lo], half_bits_to_float(v2));
-      acc += (double)__fmul_rn(scores[p + 3 - lo], half_bits_to_float(v3));
+      const float v0 = value_at(a, p, kvh, i), v1 = value_at(a, p + 1, kvh, i);
+      const float v2 = value_at(a, p + 2, kvh, i), v3 = value_at(a, p + 3, kvh, i);
+      acc += (double)__fmul_rn(scores[p - lo], v0);
+      acc += (double)__fmul_rn(scores[p + 1 - lo], v1);
+      acc += (double)__fmul_rn(scores[p + 2 - lo], v2);
+      acc += (double)__fmul_rn(scores[p + 3 - lo], v3);
     }
-    for (; p < hi; ++p) acc += (double)__fmul_rn(scores[p - lo], half_bits_to_float(vcol[(long)p * kvw]));
+    for (; p < hi; ++p) acc += (double)__fmul_rn(scores[p - lo], value_at(a, p, kvh, i));
     partial[i] = acc;
   }
   cluster.sync();

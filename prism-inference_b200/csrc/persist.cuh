@@ -663,7 +663,14 @@ __device__ bool run_attn(const PAttn &pt, const PersistArgs &pa, int pos, uint8_
     q[i] = qv;
     kc[i] = kv_;
     vc[i] = round_f16(a.value_in[kvh * hd + i]);
-    if (rank == 0 && h % group == 0) {
+    const bool writer = rank == 0 && h % group == 0;
+    if (a.q8) {
+      const long at = ((long)pos * a.kv_heads + kvh) * q8_0_record_bytes(hd);
+      kc[i] = q8_0_roundtrip(kc[i], writer ? reinterpret_cast<uint8_t *>(a.kcache) + at : nullptr,
+                             hd, a.status);
+      vc[i] = q8_0_roundtrip(vc[i], writer ? reinterpret_cast<uint8_t *>(a.vcache) + at : nullptr,
+                             hd, a.status);
+    } else if (writer) {
       a.kcache[(long)pos * kvw + kvh * hd + i] = float_to_half_bits(kc[i]);
       a.vcache[(long)pos * kvw + kvh * hd + i] = float_to_half_bits(vc[i]);
     }
@@ -673,18 +680,7 @@ __device__ bool run_attn(const PAttn &pt, const PersistArgs &pa, int pos, uint8_
   const float4 q0 = reinterpret_cast<const float4 *>(q)[lane * 2];
   const float4 q1 = reinterpret_cast<const float4 *>(q)[lane * 2 + 1];
   for (int p = lo + warp; p < hi; p += kPWarps) {
-    const uint4 kv =
-        *reinterpret_cast<const uint4 *>(a.kcache + (long)p * kvw + kvh * hd + lane * 8);
-    const uint16_t *kh = reinterpret_cast<const uint16_t *>(&kv);
-    double s = (double)__fmul_rn(q0.x, half_bits_to_float(kh[0])) +
-               (double)__fmul_rn(q0.y, half_bits_to_float(kh[1])) +
-               (double)__fmul_rn(q0.z, half_bits_to_float(kh[2])) +
-               (double)__fmul_rn(q0.w, half_bits_to_float(kh[3])) +
-               (double)__fmul_rn(q1.x, half_bits_to_float(kh[4])) +
-               (double)__fmul_rn(q1.y, half_bits_to_float(kh[5])) +
-               (double)__fmul_rn(q1.z, half_bits_to_float(kh[6])) +
-               (double)__fmul_rn(q1.w, half_bits_to_float(kh[7]));
-    s = warp_sum_f64(s);
+    const double s = warp_sum_f64(key_partial(a, p, kvh, q0, q1, lane));
     if (lane == 0) scores[p - lo] = __fmul_rn((float)s, scale);
   }
   {
@@ -724,18 +720,16 @@ __device__ bool run_attn(const PAttn &pt, const PersistArgs &pa, int pos, uint8_
   __syncthreads();
   if (i < hd) {
     double acc = -0.0;
-    const uint16_t *vcol = a.vcache + kvh * hd + i;
     int p = lo;
     for (; p + 4 <= hi; p += 4) {
-      const uint16_t v0 = vcol[(long)p * kvw], v1 = vcol[(long)(p + 1) * kvw];
-      const uint16_t v2 = vcol[(long)(p + 2) * kvw], v3 = vcol[(long)(p + 3) * kvw];
-      acc += (double)__fmul_rn(scores[p - lo], half_bits_to_float(v0));
-      acc += (double)__fmul_rn(scores[p + 1 - lo], half_bits_to_float(v1));
-      acc += (double)__fmul_rn(scores[p + 2 - lo], half_bits_to_float(v2));
-      acc += (double)__fmul_rn(scores[p + 3 - lo], half_bits_to_float(v3));
+      const float v0 = value_at(a, p, kvh, i), v1 = value_at(a, p + 1, kvh, i);
+      const float v2 = value_at(a, p + 2, kvh, i), v3 = value_at(a, p + 3, kvh, i);
+      acc += (double)__fmul_rn(scores[p - lo], v0);
+      acc += (double)__fmul_rn(scores[p + 1 - lo], v1);
+      acc += (double)__fmul_rn(scores[p + 2 - lo], v2);
+      acc += (double)__fmul_rn(scores[p + 3 - lo], v3);
     }
-    for (; p < hi; ++p)
-      acc += (double)__fmul_rn(scores[p - lo], half_bits_to_float(vcol[(long)p * kvw]));
+    for (; p < hi; ++p) acc += (double)__fmul_rn(scores[p - lo], value_at(a, p, kvh, i));
     pt.part[((long)h * kAttnSplit + rank) * hd + i] = acc;
   }
   if (!head_barrier(pa, ctr, 3, flag)) return false;

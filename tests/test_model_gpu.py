@@ -143,3 +143,56 @@ def test_persistent_step_matches_kernel_sequence(cfg_name, monkeypatch):
     for x, y in zip(sa, sb):
         assert np.array_equal(x.view(np.uint32), y.view(np.uint32))
     assert ga == gb
+
+
+def _q8_pair(cfg, seed):
+    from oracle import oracle
+    W = qwen35.synthetic_weights(cfg, seed=seed)
+    ex = pb.ProjectionExecutor(0)
+    gm = qwen35.Qwen35Model(ex, cfg, kv_policy=qwen35.KV_Q8_0)
+    gm.load(W)
+    om = oracle.Qwen35(cfg, W, kv_policy=1)
+    return ex, gm, om
+
+
+def test_q8_0_kv_cache_parity():
+    """Q8_0 KV records (272 B per head and position): the device's records
+    equal the oracle's byte for byte and the logits agree, token by token."""
+    cfg = qwen35.SMALL
+    ex, gm, om = _q8_pair(cfg, seed=31)
+    toks = qwen35.prompt_tokens(cfg, 20, seed=32)
+    rb = cfg.kv_heads * (cfg.head_dim // 32 * 2 + cfg.head_dim)
+    for i, t in enumerate(toks):
+        lg, greedy = gm.evaluate(t)
+        lr = om.step(t, threads=8)
+        ok, err = close(lg, lr)
+        assert ok, "step %d logits max err %g" % (i, err)
+    n = len(toks) * rb
+    for l in range(cfg.layers):
+        if cfg.is_full(l):
+            for which, ref in ((2, om.keys(l)), (3, om.values(l))):
+                got = gm.read_state(l, which).view(np.uint8).reshape(-1)[:n]
+                want = np.ascontiguousarray(ref).view(np.uint8).reshape(-1)[:n]
+                assert np.array_equal(got, want), (l, which)
+    gm.close()
+    ex.close()
+
+
+def test_q8_0_kv_config1_and_persistent(monkeypatch):
+    cfg = qwen35.CONFIG1
+    W = qwen35.synthetic_weights(cfg, seed=8)
+    toks = qwen35.prompt_tokens(cfg, 6, seed=9)
+    from oracle import oracle
+    om = oracle.Qwen35(cfg, W, kv_policy=1)
+    ref = [om.step(t, threads=16) for t in toks]
+    for persist in ("1", "0"):
+        monkeypatch.setenv("PRISM_B200_PERSIST", persist)
+        with pb.ProjectionExecutor(0) as ex:
+            gm = qwen35.Qwen35Model(ex, cfg, kv_policy=qwen35.KV_Q8_0)
+            gm.load(W)
+            assert gm.persistent == (persist == "1")
+            for i, t in enumerate(toks):
+                lg, _ = gm.evaluate(t)
+                ok, err = close(lg, ref[i])
+                assert ok, "persist %s step %d err %g" % (persist, i, err)
+            gm.close()

@@ -348,6 +348,38 @@ int prism_b200_model_step_timings(prism_b200_model *m, float *attention_ms, floa
 int64_t prism_b200_model_read_state(prism_b200_model *m, uint32_t layer, uint32_t which,
                                     void *out, size_t bytes);
 
+/* ---- batched serving -------------------------------------------------- */
+/* Many sequences decoded together over one finalized model's resident
+ * weights (its config, weights and KV policy).  Every step advances each of
+ * the `sequences` by one token: the projections of all their tokens run as
+ * tensor-core GEMMs, Gated DeltaNet and attention per (sequence, head) on
+ * each sequence's own state and KV cache of `context` positions.  Each
+ * sequence gets exactly what decoding it alone gives -- the reference's
+ * weight-sharing batched evaluation contract (reference src/lib.rs:255-275
+ * `evaluate_batch_into`); the reference server keeps one decoder per
+ * sequence (reference server/src/native_backend). */
+typedef struct prism_b200_batch prism_b200_batch;
+int prism_b200_batch_create(prism_b200_model *m, uint32_t sequences, uint32_t context,
+                            prism_b200_batch **out);
+void prism_b200_batch_destroy(prism_b200_batch *b);
+/* Every sequence back to position 0 with empty state. */
+int prism_b200_batch_reset(prism_b200_batch *b);
+/* One step: tokens[sequences] in (host); greedy[sequences] (host, may be
+ * NULL) receives each sequence's greedy next token, which also becomes its
+ * input for prism_b200_batch_decode_async. */
+int prism_b200_batch_step(prism_b200_batch *b, const uint32_t *tokens, uint32_t *greedy);
+/* `steps` greedy steps on the batch's stream, each feeding the previous
+ * step's greedy tokens back in (after at least one prism_b200_batch_step). */
+int prism_b200_batch_decode_async(prism_b200_batch *b, size_t steps);
+void *prism_b200_batch_stream(const prism_b200_batch *b);
+/* Seeded synthetic context for benchmarks: every sequence at `position`
+ * with random KV rows and recurrent/convolution state.  No counterpart in
+ * the reference (it stands in for prompts the benchmark does not ingest). */
+int prism_b200_batch_fill_context(prism_b200_batch *b, uint32_t position, uint64_t seed);
+/* State of one sequence, as prism_b200_model_read_state (which 0..4). */
+int64_t prism_b200_batch_read_state(prism_b200_batch *b, uint32_t seq, uint32_t layer,
+                                    uint32_t which, void *out, size_t bytes);
+
 /* ---- synthetic inputs ----------------------------------------------- */
 /* Fill `out` (host, rows*cols/256 blocks in the reference byte layout) with
  * seeded random packed weights: TQ2_0 codes uniform in {-1, 0, +1}, Q2_K

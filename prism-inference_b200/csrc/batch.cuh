@@ -1,0 +1,556 @@
+// batch.cuh -- batched serving: many sequences decoded together over one
+// model's resident weights.
+//
+// Every step advances each of B sequences by one token.  The projections of
+// all B tokens run as tensor-core GEMMs (gemm.cuh: 128 tokens x 128 rows
+// per CTA, tcgen05.mma kind::i8), so a weight byte is read once per step for
+// the whole batch instead of once per sequence; Gated DeltaNet and attention
+// run per (sequence, head) on each sequence's own state and KV cache.
+// Each sequence's results are those of decoding it alone -- the reference's
+// weight-sharing batched evaluation contract (reference src/lib.rs:255-275
+// `evaluate_batch_into`: "final decoder state matches sequential
+// evaluation"); the server keeps one decoder per sequence
+// (reference server/src/native_backend).  Included once by prism_b200.cu,
+// after model.cuh.
+#pragma once
+
+#include "gemm.cuh"
+
+namespace prism {
+
+struct BatchLayer {
+  float *conv = nullptr;                  // 2 x [B][channels][k-1], by step parity
+  float *matrix = nullptr;                // [B][values][S][S]
+  uint16_t *kc = nullptr, *vc = nullptr;  // [B][context][kv row bytes / 2]
+};
+
+}  // namespace prism
+
+struct prism_b200_batch {
+  prism_b200_model *m = nullptr;
+  int B = 0, context = 0;
+  std::vector<prism::BatchLayer> L;
+  // activations [B][...]
+  float *hidden = nullptr, *xn = nullptr, *mixed = nullptr, *zgate = nullptr, *beta = nullptr,
+        *alpha = nullptr, *attended = nullptr, *projected = nullptr, *key = nullptr,
+        *value = nullptr, *up = nullptr, *gate = nullptr;
+  void *tok = nullptr;  // Q8_K tokens for the GEMMs (largest K)
+  int *d_pos = nullptr, *d_step = nullptr;
+  uint32_t *d_tokens = nullptr;
+  unsigned long long *d_keys = nullptr;
+  cudaStream_t stream = nullptr;
+  cudaGraphExec_t graph = nullptr;
+  std::vector<void *> allocations;
+  int64_t steps = 0;
+  size_t kv_seq_bytes() const { return (size_t)context * m->kv_row_bytes(); }
+};
+
+namespace prism {
+
+template <typename T>
+cudaError_t batch_alloc(prism_b200_batch *b, T **p, size_t count) {
+  void *v = nullptr;
+  const size_t bytes = count * sizeof(T) < 16 ? 16 : count * sizeof(T);
+  cudaError_t e = cudaMalloc(&v, bytes);
+  if (e != cudaSuccess) return e;
+  b->allocations.push_back(v);
+  e = cudaMemset(v, 0, bytes);
+  *p = static_cast<T *>(v);
+  return e;
+}
+
+template <int KIND>
+__global__ void embed_batch_kernel(const uint8_t *units, int h, int nb, int vocab,
+                                   const uint32_t *tokens, float *hidden, int n,
+                                   unsigned *status) {
+  grid_dependency_wait();
+  grid_dependents_launch();
+  const int b = blockIdx.y;
+  const uint32_t token = tokens[b];
+  if (token >= (uint32_t)vocab) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) report(status, kStatusInvalid);
+    return;
+  }
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    hidden[(long)b * n + i] = decode_tiled<KIND>(units, h, nb, (int)token, i);
+}
+
+// RMSNorm of each row (one 256-thread CTA per row): the binary64 sum of
+// squares in block_sumsq_f64's order, then (x * scale) * w -- the values the
+// projection kernels' RMSNorm prologue quantizes.
+__global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float *x, const float *w, int n,
+                                                           float eps, float *out,
+                                                           unsigned *status) {
+  __shared__ double red[8];
+  grid_dependency_wait();
+  grid_dependents_launch();
+  const float *xr = x + (long)blockIdx.x * n;
+  const double sum = block_sumsq_f64(xr, n, red);
+  const float mean = (float)(sum / (double)n);
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  if ((!is_finite_f(scale) || !(scale > 0.0f)) && threadIdx.x == 0) report(status, kStatusNonfinite);
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    out[(long)blockIdx.x * n + i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
+}
+
+// h = up * silu(gate) (reference src/graph.rs:121-131 SwiGLU), in place over up.
+__global__ void swiglu_kernel(float *up, const float *gate, long n, unsigned *status) {
+  grid_dependency_wait();
+  grid_dependents_launch();
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long)gridDim.x * blockDim.x) {
+    const float u = up[i], g = gate[i];
+    if (!is_finite_f(u) || !is_finite_f(g)) report(status, kStatusNonfinite);
+    up[i] = __fmul_rn(u, silu_f(g));
+  }
+}
+
+// Advance every sequence; with `greedy`, its next input is the argmax token.
+__global__ void batch_finish_kernel(unsigned long long *keys, uint32_t *tokens, int *pos, int B,
+                                    int *step, int greedy) {
+  grid_dependency_wait();
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    if (greedy) tokens[b] = 0xffffffffu - (unsigned)(keys[b] & 0xffffffffull);
+    keys[b] = 0ull;
+    pos[b] += 1;
+  }
+  if (threadIdx.x == 0) *step += 1;
+}
+
+// Seeded synthetic context for benchmarks: every sequence at `position`
+// with random KV rows (binary16 in [-1, 1], or Q8_0 records with scales in
+// [2^-8, 2^-6] and codes in [-127, 127]) and small random recurrent and
+// convolution states.  SplitMix64 of (seed, array, element).
+__device__ __forceinline__ uint64_t synth_mix(uint64_t x) {
+  x += 0x9e3779b97f4a7c15ull;
+  x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ull;
+  x = (x ^ (x >> 27)) * 0x94d049bb133111ebull;
+  return x ^ (x >> 31);
+}
+
+__global__ void fill_kv_kernel(uint8_t *kv, long rows, int row_bytes, int hd, int q8,
+                               uint64_t seed) {
+  const long n = rows * row_bytes;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long)gridDim.x * blockDim.x) {
+    const uint64_t r = synth_mix(seed ^ (uint64_t)i);
+    uint8_t v;
+    if (q8) {
+      const int rb = q8_0_record_bytes(hd), o = (int)((i % row_bytes) % rb);
+      if (o < hd / 32 * 2) {
+        // binary16 scale in [2^-8, 2^-6): exponent 7..8, random mantissa
+        const uint16_t half = (uint16_t)((7u + (unsigned)(r & 1)) << 10 | (unsigned)((r >> 8) & 0x3ff));
+        v = (o & 1) ? (uint8_t)(half >> 8) : (uint8_t)(half & 0xff);
+      } else {
+        v = (uint8_t)(int8_t)((int)(r % 255) - 127);
+      }
+    } else {
+      // binary16 in (-1, 1): sign, exponent < 15, random mantissa
+      const uint16_t half = (uint16_t)(((r >> 20) & 1) << 15 | ((r % 15) << 10) | ((r >> 8) & 0x3ff));
+      v = (i & 1) ? (uint8_t)(half >> 8) : (uint8_t)(half & 0xff);
+    }
+    kv[i] = v;
+  }
+}
+
+__global__ void fill_f32_kernel(float *x, long n, float scale, uint64_t seed) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long)gridDim.x * blockDim.x) {
+    const uint64_t r = synth_mix(seed ^ (uint64_t)i);
+    x[i] = scale * ((float)(r >> 40) * (1.0f / 16777216.0f) * 2.0f - 1.0f);
+  }
+}
+
+// Enqueue one step of the whole batch on b->stream.
+inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
+  prism_b200_model *m = b->m;
+  prism_b200_executor *ex = m->ex;
+  const auto &c = m->cfg;
+  const bool pdl = ex->pdl;
+  const int B = b->B;
+  cudaStream_t s = b->stream;
+  unsigned *status = ex->d_status;
+  const uint32_t kind = c.weight_kind;
+  cudaLaunchAttribute attr[2];
+  cudaError_t e;
+  const int H = (int)c.hidden, hnb = H / 256;
+  {
+    cudaLaunchConfig_t cfg = pdl_config(dim3((H + 255) / 256, B), dim3(256), 0, s, attr, pdl);
+    e = kind == 35 ? cudaLaunchKernelEx(&cfg, embed_batch_kernel<35>, m->embd.units, m->embd.h,
+                                        m->embd.nb, (int)c.vocab, (const uint32_t *)b->d_tokens,
+                                        b->hidden, H, status)
+                   : cudaLaunchKernelEx(&cfg, embed_batch_kernel<10>, m->embd.units, m->embd.h,
+                                        m->embd.nb, (int)c.vocab, (const uint32_t *)b->d_tokens,
+                                        b->hidden, H, status);
+    if (e != cudaSuccess) return e;
+  }
+  auto norm = [&](const float *w) {
+    cudaLaunchConfig_t cfg = pdl_config(dim3(B), dim3(256), 0, s, attr, pdl);
+    return cudaLaunchKernelEx(&cfg, rmsnorm_rows_kernel, (const float *)b->hidden, w, H, c.eps,
+                              b->xn, status);
+  };
+  auto quant = [&](const float *x, int nb) {
+    return launch_token_quantize(x, B, nb, 0, token_q8k_carve(b->tok, B, nb), status, s, pdl);
+  };
+  auto mm = [&](const DeviceWeight &w, float *y, const float *residual,
+                unsigned long long *keys) {
+    return launch_token_matmul(w, B, token_q8k_carve(b->tok, B, w.nb), y, residual, keys,
+                               status, s, pdl);
+  };
+#define BK(x)                            \
+  if ((e = (x)) != cudaSuccess) return e
+  for (size_t l = 0; l < m->L.size(); ++l) {
+    ModelLayer &Ly = m->L[l];
+    BatchLayer &Bl = b->L[l];
+    BK(norm(Ly.attn_norm));
+    BK(quant(b->xn, hnb));
+    if (Ly.full) {
+      BK(mm(Ly.q, b->projected, nullptr, nullptr));
+      BK(mm(Ly.k, b->key, nullptr, nullptr));
+      BK(mm(Ly.v, b->value, nullptr, nullptr));
+      AttnArgs aa{};
+      aa.heads = (int)c.heads;
+      aa.kv_heads = (int)c.kv_heads;
+      aa.hd = (int)c.head_dim;
+      aa.rope_dim = (int)c.rope_dim;
+      for (int j = 0; j < 3; ++j) aa.sections[j] = (int)c.rope_sections[j];
+      aa.eps = c.eps;
+      aa.theta_scale = powf(c.rope_base, -2.0f / (float)c.rope_dim);
+      aa.projected = b->projected;
+      aa.key_in = b->key;
+      aa.value_in = b->value;
+      aa.q_norm = Ly.q_norm;
+      aa.k_norm = Ly.k_norm;
+      aa.kcache = Bl.kc;
+      aa.vcache = Bl.vc;
+      aa.q8 = c.kv_policy == PRISM_B200_KV_Q8_0 ? 1 : 0;
+      aa.position = b->d_pos;
+      aa.pos_stride = 1;
+      aa.seq_proj = (long)c.heads * c.head_dim * 2;
+      aa.seq_kv_in = m->kvw();
+      aa.seq_out = (long)c.heads * c.head_dim;
+      aa.seq_cache = (long)(b->kv_seq_bytes() / 2);
+      aa.attended = b->attended;
+      aa.status = status;
+      const size_t smem = attn_smem_bytes((int)c.head_dim, b->context);
+      cudaLaunchConfig_t cfg =
+          pdl_config(dim3(c.heads * kAttnSplit, B), dim3(kAttnThreads), smem, s, attr, pdl);
+      attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+      attr[cfg.numAttrs].val.clusterDim.x = kAttnSplit;
+      attr[cfg.numAttrs].val.clusterDim.y = 1;
+      attr[cfg.numAttrs].val.clusterDim.z = 1;
+      cfg.numAttrs += 1;
+      BK(cudaLaunchKernelEx(&cfg, attention_decode_kernel, aa));
+      BK(quant(b->attended, (int)(c.heads * c.head_dim / 256)));
+      BK(mm(Ly.o, b->hidden, b->hidden, nullptr));
+    } else {
+      BK(mm(Ly.qkv, b->mixed, nullptr, nullptr));
+      BK(mm(Ly.z, b->zgate, nullptr, nullptr));
+      BK(mm(Ly.beta, b->beta, nullptr, nullptr));
+      BK(mm(Ly.alpha, b->alpha, nullptr, nullptr));
+      GdnArgs g{};
+      g.S = (int)c.ssm_state;
+      g.groups = (int)c.ssm_groups;
+      g.values = (int)c.ssm_values;
+      g.conv_k = (int)c.conv_kernel;
+      g.eps = c.eps;
+      g.mixed = b->mixed;
+      g.zgate = b->zgate;
+      g.beta_in = b->beta;
+      g.alpha_in = b->alpha;
+      g.in_stride = m->channels();
+      g.z_stride = m->value_width();
+      g.ab_stride = c.ssm_values;
+      g.conv_w = Ly.conv_w;
+      g.dt_bias = Ly.dt_bias;
+      g.ssm_a = Ly.ssm_a;
+      g.norm_w = Ly.ssm_norm;
+      g.conv_state = Bl.conv;
+      g.conv_stride = (long)m->channels() * (c.conv_kernel - 1);
+      g.conv_buf_stride = g.conv_stride * B;
+      g.state = Bl.matrix;
+      g.state_stride = (long)c.ssm_values * c.ssm_state * c.ssm_state;
+      g.attended = b->attended;
+      g.out_stride = m->value_width();
+      g.position = b->d_step;  // the double-buffered history alternates every step
+      g.status = status;
+      cudaLaunchConfig_t cfg =
+          pdl_config(dim3(c.ssm_values, B), dim3(kGdnThreads), 0, s, attr, pdl);
+      BK(cudaLaunchKernelEx(&cfg, gdn_decode_kernel, g));
+      BK(quant(b->attended, m->value_width() / 256));
+      BK(mm(Ly.out, b->hidden, b->hidden, nullptr));
+    }
+    BK(norm(Ly.post_norm));
+    BK(quant(b->xn, hnb));
+    BK(mm(Ly.up, b->up, nullptr, nullptr));
+    BK(mm(Ly.gate, b->gate, nullptr, nullptr));
+    {
+      const long n = (long)B * c.ffn;
+      cudaLaunchConfig_t cfg =
+          pdl_config(dim3((unsigned)std::min<long>((n + 255) / 256, 4096)), dim3(256), 0, s,
+                     attr, pdl);
+      BK(cudaLaunchKernelEx(&cfg, swiglu_kernel, b->up, (const float *)b->gate, n, status));
+    }
+    BK(quant(b->up, (int)(c.ffn / 256)));
+    BK(mm(Ly.down, b->hidden, b->hidden, nullptr));
+  }
+  if (greedy) {
+    BK(norm(m->out_norm));
+    BK(quant(b->xn, hnb));
+    BK(mm(m->embd, nullptr, nullptr, b->d_keys));
+  }
+  cudaLaunchConfig_t cfg = pdl_config(dim3(1), dim3(256), 0, s, attr, pdl);
+  BK(cudaLaunchKernelEx(&cfg, batch_finish_kernel, b->d_keys, b->d_tokens, b->d_pos, B,
+                        b->d_step, greedy ? 1 : 0));
+#undef BK
+  return cudaSuccess;
+}
+
+}  // namespace prism
+
+extern "C" {
+
+int prism_b200_batch_create(prism_b200_model *m, uint32_t sequences, uint32_t context,
+                            prism_b200_batch **out) {
+  using namespace prism;
+  if (!m || !out) return PRISM_B200_E_INVALID;
+  *out = nullptr;
+  prism_b200_executor *ex = m->ex;
+  int st = check_open(ex);
+  if (st) return st;
+  if (!m->finalized) return ex->fail(PRISM_B200_E_INVALID, "model is not finalized");
+  if (sequences == 0 || sequences > 65535u || context == 0 ||
+      context > (1u << 20))
+    return ex->fail(PRISM_B200_E_INVALID, "batch of %u sequences x %u positions", sequences,
+                    context);
+  if ((context + kAttnSplit - 1) / kAttnSplit + 1 > 16384)
+    return ex->fail(PRISM_B200_E_UNSUPPORTED, "context %u exceeds the attention kernel", context);
+  cudaSetDevice(ex->device);
+  const auto &c = m->cfg;
+  auto *b = new prism_b200_batch();
+  b->m = m;
+  b->B = (int)sequences;
+  b->context = (int)context;
+  b->L.resize(c.layers);
+  const size_t B = sequences;
+  cudaError_t e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+#define A(p, n) \
+  if (e == cudaSuccess) e = batch_alloc(b, &(p), (n))
+  A(b->hidden, B * c.hidden);
+  A(b->xn, B * c.hidden);
+  A(b->mixed, B * m->channels());
+  A(b->zgate, B * m->value_width());
+  A(b->beta, B * c.ssm_values);
+  A(b->alpha, B * c.ssm_values);
+  A(b->attended, B * std::max<size_t>(m->value_width(), (size_t)c.heads * c.head_dim));
+  A(b->projected, B * c.heads * c.head_dim * 2);
+  A(b->key, B * m->kvw());
+  A(b->value, B * m->kvw());
+  A(b->up, B * c.ffn);
+  A(b->gate, B * c.ffn);
+  uint8_t *tokbuf = nullptr;
+  A(tokbuf, token_q8k_bytes(B, (int)std::max<uint32_t>(c.ffn, c.heads * c.head_dim) / 256 + 1));
+  b->tok = tokbuf;
+  A(b->d_pos, B);
+  A(b->d_step, 1);
+  A(b->d_tokens, B);
+  A(b->d_keys, B);
+  for (uint32_t l = 0; l < c.layers; ++l) {
+    BatchLayer &Bl = b->L[l];
+    if (m->L[l].full) {
+      A(Bl.kc, B * b->kv_seq_bytes() / 2);
+      A(Bl.vc, B * b->kv_seq_bytes() / 2);
+    } else {
+      A(Bl.conv, 2 * B * m->channels() * (c.conv_kernel - 1));
+      A(Bl.matrix, B * c.ssm_values * c.ssm_state * c.ssm_state);
+    }
+  }
+#undef A
+  if (e != cudaSuccess) {
+    prism_b200_batch_destroy(b);
+    return cuda_fail(ex, e, "batch allocation");
+  }
+  *out = b;
+  return PRISM_B200_OK;
+}
+
+void prism_b200_batch_destroy(prism_b200_batch *b) {
+  if (!b) return;
+  cudaSetDevice(b->m->ex->device);
+  if (b->stream) cudaStreamSynchronize(b->stream);
+  if (b->graph) cudaGraphExecDestroy(b->graph);
+  for (void *p : b->allocations) cudaFree(p);
+  if (b->stream) cudaStreamDestroy(b->stream);
+  delete b;
+}
+
+int prism_b200_batch_reset(prism_b200_batch *b) {
+  using namespace prism;
+  if (!b) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = b->m->ex;
+  cudaSetDevice(ex->device);
+  const auto &c = b->m->cfg;
+  const size_t B = b->B;
+  cudaStream_t s = b->stream;
+  for (size_t l = 0; l < b->L.size(); ++l) {
+    BatchLayer &Bl = b->L[l];
+    if (b->m->L[l].full) {
+      CK(cudaMemsetAsync(Bl.kc, 0, B * b->kv_seq_bytes(), s), "batch reset");
+      CK(cudaMemsetAsync(Bl.vc, 0, B * b->kv_seq_bytes(), s), "batch reset");
+    } else {
+      CK(cudaMemsetAsync(Bl.conv, 0, 2 * B * b->m->channels() * (c.conv_kernel - 1) * 4, s),
+         "batch reset");
+      CK(cudaMemsetAsync(Bl.matrix, 0, B * c.ssm_values * c.ssm_state * c.ssm_state * 4, s),
+         "batch reset");
+    }
+  }
+  CK(cudaMemsetAsync(b->d_pos, 0, B * 4, s), "batch reset");
+  CK(cudaMemsetAsync(b->d_step, 0, 4, s), "batch reset");
+  CK(cudaMemsetAsync(b->d_keys, 0, B * 8, s), "batch reset");
+  CK(cudaStreamSynchronize(s), "batch reset");
+  b->steps = 0;
+  return PRISM_B200_OK;
+}
+
+static int batch_finish(prism_b200_batch *b) {
+  prism_b200_executor *ex = b->m->ex;
+  CK(cudaMemcpyAsync(ex->h_status, ex->d_status, sizeof(unsigned), cudaMemcpyDeviceToHost,
+                     b->stream),
+     "status readback");
+  CK(cudaStreamSynchronize(b->stream), "batch step");
+  if (*ex->h_status) {
+    ex->faulted = true;
+    return ex->fail(status_to_code(*ex->h_status), "device reported status 0x%x",
+                    *ex->h_status);
+  }
+  return PRISM_B200_OK;
+}
+
+int prism_b200_batch_step(prism_b200_batch *b, const uint32_t *tokens, uint32_t *greedy) {
+  using namespace prism;
+  if (!b || !tokens) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = b->m->ex;
+  int st = check_open(ex);
+  if (st) return st;
+  const auto &c = b->m->cfg;
+  for (int i = 0; i < b->B; ++i)
+    if (tokens[i] >= c.vocab) return ex->fail(PRISM_B200_E_INVALID, "token out of range");
+  if (b->steps >= b->context) return ex->fail(PRISM_B200_E_INVALID, "context is exhausted");
+  cudaSetDevice(ex->device);
+  CK(cudaMemcpyAsync(b->d_tokens, tokens, (size_t)b->B * 4, cudaMemcpyHostToDevice, b->stream),
+     "token copy");
+  if (!b->graph) {
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal), "capture");
+    cudaError_t e2 = enqueue_batch_step(b, true);
+    cudaError_t e = cudaStreamEndCapture(b->stream, &g);
+    if (e2 != cudaSuccess) e = e2;
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&b->graph, g, 0);
+    if (g) cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(ex, e, "batch step capture");
+  }
+  CK(cudaGraphLaunch(b->graph, b->stream), "batch step");
+  if (greedy)
+    CK(cudaMemcpyAsync(greedy, b->d_tokens, (size_t)b->B * 4, cudaMemcpyDeviceToHost, b->stream),
+       "greedy copy");
+  st = batch_finish(b);
+  if (st) return st;
+  b->steps += 1;
+  return PRISM_B200_OK;
+}
+
+int prism_b200_batch_decode_async(prism_b200_batch *b, size_t steps) {
+  if (!b) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = b->m->ex;
+  int st = check_open(ex);
+  if (st) return st;
+  if (!b->graph) return ex->fail(PRISM_B200_E_INVALID, "run one prism_b200_batch_step first");
+  cudaSetDevice(ex->device);
+  for (size_t i = 0; i < steps; ++i) CK(cudaGraphLaunch(b->graph, b->stream), "batch step");
+  b->steps += (int64_t)steps;
+  return PRISM_B200_OK;
+}
+
+void *prism_b200_batch_stream(const prism_b200_batch *b) {
+  return b ? reinterpret_cast<void *>(b->stream) : nullptr;
+}
+
+int prism_b200_batch_fill_context(prism_b200_batch *b, uint32_t position, uint64_t seed) {
+  using namespace prism;
+  if (!b) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = b->m->ex;
+  int st = check_open(ex);
+  if (st) return st;
+  if (position >= (uint32_t)b->context)
+    return ex->fail(PRISM_B200_E_INVALID, "position %u outside the context", position);
+  cudaSetDevice(ex->device);
+  const auto &c = b->m->cfg;
+  cudaStream_t s = b->stream;
+  const size_t B = b->B;
+  for (size_t l = 0; l < b->L.size(); ++l) {
+    BatchLayer &Bl = b->L[l];
+    const uint64_t ls = seed * 1000003ull + l * 7919ull;
+    if (b->m->L[l].full) {
+      const long rows = (long)B * b->context;
+      const int rb = (int)b->m->kv_row_bytes(), q8 = c.kv_policy == PRISM_B200_KV_Q8_0;
+      fill_kv_kernel<<<4096, 256, 0, s>>>(reinterpret_cast<uint8_t *>(Bl.kc), rows, rb,
+                                          (int)c.head_dim, q8, ls * 2 + 1);
+      fill_kv_kernel<<<4096, 256, 0, s>>>(reinterpret_cast<uint8_t *>(Bl.vc), rows, rb,
+                                          (int)c.head_dim, q8, ls * 2 + 2);
+    } else {
+      fill_f32_kernel<<<4096, 256, 0, s>>>(Bl.matrix,
+                                           (long)B * c.ssm_values * c.ssm_state * c.ssm_state,
+                                           0.05f, ls * 2 + 3);
+      fill_f32_kernel<<<1024, 256, 0, s>>>(Bl.conv,
+                                           (long)2 * B * b->m->channels() * (c.conv_kernel - 1),
+                                           0.5f, ls * 2 + 4);
+    }
+  }
+  std::vector<int> pos(B, (int)position);
+  CK(cudaMemcpyAsync(b->d_pos, pos.data(), B * 4, cudaMemcpyHostToDevice, s), "fill");
+  CK(cudaGetLastError(), "fill launch");
+  CK(cudaStreamSynchronize(s), "fill");
+  b->steps = position;
+  return PRISM_B200_OK;
+}
+
+int64_t prism_b200_batch_read_state(prism_b200_batch *b, uint32_t seq, uint32_t layer,
+                                    uint32_t which, void *out, size_t bytes) {
+  if (!b || !out || seq >= (uint32_t)b->B) return -PRISM_B200_E_INVALID;
+  prism_b200_model *m = b->m;
+  const auto &c = m->cfg;
+  const void *src = nullptr;
+  size_t n = 0;
+  if (which == 4) {
+    src = b->hidden + (size_t)seq * c.hidden;
+    n = (size_t)c.hidden * 4;
+  } else if (layer < c.layers) {
+    const prism::BatchLayer &Bl = b->L[layer];
+    const size_t hist = (size_t)m->channels() * (c.conv_kernel - 1);
+    if (which == 0 && !m->L[layer].full) {
+      int step = 0;
+      cudaMemcpy(&step, b->d_step, 4, cudaMemcpyDeviceToHost);
+      src = Bl.conv + ((size_t)(step & 1) * b->B + seq) * hist;
+      n = hist * 4;
+    } else if (which == 1 && !m->L[layer].full) {
+      const size_t per = (size_t)c.ssm_values * c.ssm_state * c.ssm_state;
+      src = Bl.matrix + seq * per;
+      n = per * 4;
+    } else if ((which == 2 || which == 3) && m->L[layer].full) {
+      int pos = 0;
+      cudaMemcpy(&pos, b->d_pos + seq, 4, cudaMemcpyDeviceToHost);
+      const uint8_t *base = reinterpret_cast<const uint8_t *>(which == 2 ? Bl.kc : Bl.vc);
+      src = base + (size_t)seq * b->kv_seq_bytes();
+      n = (size_t)pos * m->kv_row_bytes();
+    }
+  }
+  if (!src) return -PRISM_B200_E_INVALID;
+  if (bytes < n) return -PRISM_B200_E_INVALID;
+  cudaSetDevice(m->ex->device);
+  if (cudaMemcpyAsync(out, src, n, cudaMemcpyDeviceToHost, b->stream) != cudaSuccess ||
+      cudaStreamSynchronize(b->stream) != cudaSuccess)
+    return -PRISM_B200_E_DEVICE;
+  return (int64_t)n;
+}
+
+}  // extern "C"

@@ -187,7 +187,9 @@ struct GemmArgs {
   int h, nb, rows, ntiles;
   const float *scale;     // [M][nb]
   int M;
-  float *y;               // [M][rows]
+  float *y;               // [M][rows], or null
+  const float *residual;  // optional [M][rows]: y = residual + chain (may alias y)
+  unsigned long long *argmax_keys;  // optional [M]: greedy key over each token's rows
   unsigned *status;
 };
 
@@ -460,12 +462,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q4 = warp & 3, half = (warp - kWarpEpi) >> 2;
     const int tl = 32 * q4 + lane;
     bool finite = true;
+    unsigned long long best = 0ull;
 #pragma unroll
     for (int c = 0; c < 64; ++c) {
+      const int n = n0 + 64 * half + c;
       otile[tl * kPitch + 64 * half + c] = acc[c];
-      if (n0 + 64 * half + c < g.rows) finite &= is_finite_f(acc[c]);
+      if (n < g.rows) {
+        finite &= is_finite_f(acc[c]);
+        const unsigned long long key = argmax_key(acc[c], n);
+        best = key > best ? key : best;
+      }
     }
-    if (m0 + tl < g.M && !finite) report(g.status, kStatusNonfinite);
+    if (m0 + tl < g.M) {
+      if (!finite && !g.residual) report(g.status, kStatusNonfinite);
+      if (g.argmax_keys && best) atomicMax(&g.argmax_keys[m0 + tl], best);
+    }
   }
   __syncthreads();
   if (warp == 0) {
@@ -476,7 +487,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int i = tid; i < kGemmM * kGemmN; i += kGemmThreads) {
       const int t = i / kGemmN, c = i % kGemmN;
       const int mm = m0 + t, n = n0 + c;
-      if (mm < g.M && n < g.rows) g.y[(size_t)mm * g.rows + n] = otile[t * kPitch + c];
+      if (mm < g.M && n < g.rows) {
+        float v = otile[t * kPitch + c];
+        if (g.residual) {
+          v = __fadd_rn(g.residual[(size_t)mm * g.rows + n], v);
+          if (!is_finite_f(v)) report(g.status, kStatusNonfinite);
+        }
+        if (g.y) g.y[(size_t)mm * g.rows + n] = v;
+      }
     }
   }
 }
@@ -488,38 +506,72 @@ constexpr int gemm_smem_bytes() {
   return GemmSmem<KIND>::kBytes;
 }
 
-// Quantize M token rows of x [M][cols] to Q8_K, then Y[M][rows] = tokens x W^T
-// on the tensor cores.  Both kernels go on `s` in order.
-inline cudaError_t launch_token_gemm(const DeviceWeight &dw, const float *x, size_t M,
-                                     int pinned, const TokenQ8K &t, float *y, unsigned *status,
-                                     cudaStream_t s, bool pdl) {
-  const int nb = dw.nb;
+// Quantize M token rows of x [M][nb*256] to Q8_K (tile-major, TokenQ8K).
+inline cudaError_t launch_token_quantize(const float *x, size_t M, int nb, int pinned,
+                                         const TokenQ8K &t, unsigned *status, cudaStream_t s,
+                                         bool pdl) {
   cudaLaunchAttribute attr[1];
   const long warps = (long)M * nb;
   cudaLaunchConfig_t cfg =
       pdl_config(dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, s, attr, pdl);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, q8k_tokens_kernel, x, (int)M, nb, pinned, t, status);
-  if (e != cudaSuccess) return e;
+  return cudaLaunchKernelEx(&cfg, q8k_tokens_kernel, x, (int)M, nb, pinned, t, status);
+}
+
+// Y[M][rows] (= residual + chain when residual is set) for quantized tokens
+// t; with argmax_keys, each token's greedy key over the rows.
+inline cudaError_t launch_token_matmul(const DeviceWeight &dw, size_t M, const TokenQ8K &t,
+                                       float *y, const float *residual,
+                                       unsigned long long *argmax_keys, unsigned *status,
+                                       cudaStream_t s, bool pdl) {
   GemmArgs g;
   g.codes = t.codes;
   g.split = t.split;
   g.w = dw.units;
   g.h = dw.h;
-  g.nb = nb;
+  g.nb = dw.nb;
   g.rows = (int)dw.rows;
   g.ntiles = dw.ntiles;
   g.scale = t.scale;
   g.M = (int)M;
   g.y = y;
+  g.residual = residual;
+  g.argmax_keys = argmax_keys;
   g.status = status;
   void (*kernel)(GemmArgs) = dw.kind == 35 ? gemm_tokens_kernel<35> : gemm_tokens_kernel<10>;
   const int smem = dw.kind == 35 ? gemm_smem_bytes<35>() : gemm_smem_bytes<10>();
-  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  cfg = pdl_config(dim3((unsigned)((dw.rows + kGemmN - 1) / kGemmN),
-                        (unsigned)((M + kGemmM - 1) / kGemmM)),
-                   dim3(kGemmThreads), smem, s, attr, pdl);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_config(dim3((unsigned)((dw.rows + kGemmN - 1) / kGemmN),
+                                           (unsigned)((M + kGemmM - 1) / kGemmM)),
+                                      dim3(kGemmThreads), smem, s, attr, pdl);
   return cudaLaunchKernelEx(&cfg, kernel, g);
+}
+
+// Quantize M token rows of x [M][cols] to Q8_K, then Y[M][rows] = tokens x W^T
+// on the tensor cores.  Both kernels go on `s` in order.
+inline cudaError_t launch_token_gemm(const DeviceWeight &dw, const float *x, size_t M,
+                                     int pinned, const TokenQ8K &t, float *y, unsigned *status,
+                                     cudaStream_t s, bool pdl) {
+  cudaError_t e = launch_token_quantize(x, M, dw.nb, pinned, t, status, s, pdl);
+  if (e != cudaSuccess) return e;
+  return launch_token_matmul(dw, M, t, y, nullptr, nullptr, status, s, pdl);
+}
+
+// Bytes of the token activation buffers for M tokens of nb blocks, and the
+// carve of one buffer into them (codes and split stay 16-byte aligned).
+inline size_t token_q8k_bytes(size_t M, int nb) {
+  const size_t mpad = (M + kGemmM - 1) / kGemmM * kGemmM;
+  return mpad * nb * 256 + mpad * nb * 32 + M * nb * 4;
+}
+inline TokenQ8K token_q8k_carve(void *buf, size_t M, int nb) {
+  const size_t mpad = (M + kGemmM - 1) / kGemmM * kGemmM;
+  uint8_t *base = static_cast<uint8_t *>(buf);
+  TokenQ8K t;
+  t.codes = reinterpret_cast<int8_t *>(base);
+  t.split = reinterpret_cast<int8_t *>(base + mpad * nb * 256);
+  t.scale = reinterpret_cast<float *>(base + mpad * nb * 256 + mpad * nb * 32);
+  return t;
 }
 
 }  // namespace prism

@@ -151,7 +151,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
       a.w[1] = mv_weight(Ly.k, m->key);
       a.w[2] = mv_weight(Ly.v, m->value);
       if ((e = launch_matvec_group(kind, kEpiStore, a, sms, s, pdl)) != cudaSuccess) return e;
-      AttnArgs aa;
+      AttnArgs aa{};
       aa.heads = (int)c.heads;
       aa.kv_heads = (int)c.kv_heads;
       aa.hd = (int)c.head_dim;

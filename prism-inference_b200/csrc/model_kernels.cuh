@@ -285,6 +285,9 @@ struct AttnArgs {
   const float *q_norm, *k_norm;
   uint16_t *kcache, *vcache;  // [context][kv_heads*hd] binary16 bits, or Q8_0 records
   int q8;                     // 1: Q8_0 records [context][kv_heads][hd/32 scales | hd codes]
+  // batched decode (grid y = sequence): per-sequence strides, 0 for one sequence
+  long seq_proj, seq_kv_in, seq_out, seq_cache;  // elements of each array's own type
+  int pos_stride;             // 1: position[sequence]; 0: one shared position
   const int *position;
   float *attended;          // [heads*hd]
   unsigned *status;
@@ -416,8 +419,19 @@ __host__ __device__ constexpr size_t attn_smem_bytes(int hd, int context) {
          (size_t)hd * 8;
 }
 
-__global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs args) {
   namespace cg = cooperative_groups;
+  AttnArgs a = args;
+  {
+    const long b = blockIdx.y;  // sequence of a batched step
+    a.projected += b * a.seq_proj;
+    a.key_in += b * a.seq_kv_in;
+    a.value_in += b * a.seq_kv_in;
+    a.attended += b * a.seq_out;
+    a.kcache += b * a.seq_cache;
+    a.vcache += b * a.seq_cache;
+    a.position += b * a.pos_stride;
+  }
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(16) float sm[];
   const int hd = a.hd;

@@ -379,17 +379,9 @@ int prism_b200_project_f32_tokens_device(prism_b200_executor *ex, const prism_b2
   CK(cudaSetDevice(ex->device), "select device");
   const DeviceWeight &dw = w->dw;
   const size_t M = tokens, nb = dw.nb;
-  // Q8_K tokens, tile-major over 128-token tiles: codes | split sums, then
-  // scale [M][nb]; codes and split stay 16-byte aligned (bulk-copy
-  // sources).  Rows of the last tile past M are never stored.
-  const size_t mpad = (M + kGemmM - 1) / kGemmM * kGemmM;
-  const size_t codes = mpad * nb * 256, split = mpad * nb * 32, meta = M * nb;
-  CK(ex->tok_act.ensure(codes + split + meta * 4), "token activation buffer");
-  uint8_t *base = static_cast<uint8_t *>(ex->tok_act.ptr);
-  TokenQ8K t;
-  t.codes = reinterpret_cast<int8_t *>(base);
-  t.split = reinterpret_cast<int8_t *>(base + codes);
-  t.scale = reinterpret_cast<float *>(base + codes + split);
+  // Q8_K tokens, tile-major over 128-token tiles (gemm.cuh token_q8k_carve)
+  CK(ex->tok_act.ensure(token_q8k_bytes(M, (int)nb)), "token activation buffer");
+  const TokenQ8K t = token_q8k_carve(ex->tok_act.ptr, M, (int)nb);
   cudaStream_t s = pick(ex, stream);
   CK(launch_token_gemm(dw, x_dev, M, pinned, t, out_dev, ex->d_status, s, ex->pdl),
      "token projection launch");
@@ -669,3 +661,4 @@ extern "C" int prism_b200_gdn_prefill_device_noalloc(prism_b200_executor *ex, in
 
 // The model entry points share this translation unit's kernels and helpers.
 #include "model.cuh"
+#include "batch.cuh"

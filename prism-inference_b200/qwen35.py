@@ -304,3 +304,79 @@ class Qwen35Model:
     def ingest_async(self, n):
         self.set_prompt  # declarations
         self.ex._check(self.L.prism_b200_model_ingest_async(self.h, n))
+
+
+def _declare_batch(L):
+    import ctypes as c
+    if getattr(L, "_batch_declared", False):
+        return
+    vp, i32, sz, u32, u64 = c.c_void_p, c.c_int, c.c_size_t, c.c_uint32, c.c_uint64
+    for name, res, args in [
+        ("prism_b200_batch_create", i32, [vp, u32, u32, c.POINTER(vp)]),
+        ("prism_b200_batch_destroy", None, [vp]),
+        ("prism_b200_batch_reset", i32, [vp]),
+        ("prism_b200_batch_step", i32, [vp, vp, vp]),
+        ("prism_b200_batch_decode_async", i32, [vp, sz]),
+        ("prism_b200_batch_stream", vp, [vp]),
+        ("prism_b200_batch_fill_context", i32, [vp, u32, u64]),
+        ("prism_b200_batch_read_state", c.c_int64, [vp, u32, u32, u32, vp, sz]),
+    ]:
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    L._batch_declared = True
+
+
+class Qwen35Batch:
+    """Batched serving over a loaded Qwen35Model's weights: `sequences`
+    sequences of up to `context` positions, one token each per step."""
+
+    def __init__(self, model, sequences, context):
+        import ctypes as c
+        self.model, self.B, self.context = model, sequences, context
+        self.L = model.L
+        _declare_batch(self.L)
+        h = c.c_void_p()
+        model.ex._check(self.L.prism_b200_batch_create(model.h, sequences, context, c.byref(h)))
+        self.h = h
+
+    def step(self, tokens):
+        tokens = np.ascontiguousarray(tokens, dtype=np.uint32)
+        assert tokens.size == self.B
+        out = np.zeros(self.B, np.uint32)
+        self.model.ex._check(self.L.prism_b200_batch_step(self.h, tokens.ctypes.data,
+                                                          out.ctypes.data))
+        return out
+
+    def decode_async(self, steps):
+        self.model.ex._check(self.L.prism_b200_batch_decode_async(self.h, steps))
+
+    @property
+    def stream(self):
+        return self.L.prism_b200_batch_stream(self.h)
+
+    def fill_context(self, position, seed=0):
+        self.model.ex._check(self.L.prism_b200_batch_fill_context(self.h, position, seed))
+
+    def reset(self):
+        self.model.ex._check(self.L.prism_b200_batch_reset(self.h))
+
+    def read_state(self, seq, layer, which, nbytes=None):
+        c = self.model.cfg
+        sizes = {0: c.conv_channels * (c.conv_kernel - 1) * 4,
+                 1: c.ssm_values * c.ssm_state * c.ssm_state * 4,
+                 2: self.context * c.kv_heads * c.head_dim * 2,
+                 3: self.context * c.kv_heads * c.head_dim * 2,
+                 4: c.hidden * 4}
+        out = np.zeros(nbytes or sizes[which], np.uint8)
+        n = self.L.prism_b200_batch_read_state(self.h, seq, layer, which, out.ctypes.data,
+                                               out.nbytes)
+        if n < 0:
+            raise pb.PrismB200Error(-n, "batch state readback failed")
+        out = out[:n]
+        return out.view(np.float32) if which in (0, 1, 4) else out
+
+    def close(self):
+        if self.h:
+            self.L.prism_b200_batch_destroy(self.h)
+            self.h = None

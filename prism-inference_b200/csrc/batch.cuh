@@ -15,13 +15,16 @@
 #pragma once
 
 #include "gemm.cuh"
+#include "serve_attn.cuh"
 
 namespace prism {
 
 struct BatchLayer {
   float *conv = nullptr;                  // 2 x [B][channels][k-1], by step parity
   float *matrix = nullptr;                // [B][values][S][S]
-  uint16_t *kc = nullptr, *vc = nullptr;  // [B][context][kv row bytes / 2]
+  // binary16: [B][context][kv heads * hd]; Q8_0 with the serving kernel:
+  // [B][kv head][context][record]
+  uint16_t *kc = nullptr, *vc = nullptr;
 };
 
 }  // namespace prism
@@ -42,6 +45,7 @@ struct prism_b200_batch {
   cudaGraphExec_t graph = nullptr;
   std::vector<void *> allocations;
   int64_t steps = 0;
+  bool serve_attn = false;  // Q8_0 KV through attention_serve_kernel (head-major cache)
   size_t kv_seq_bytes() const { return (size_t)context * m->kv_row_bytes(); }
 };
 
@@ -128,6 +132,7 @@ __device__ __forceinline__ uint64_t synth_mix(uint64_t x) {
   return x ^ (x >> 31);
 }
 
+// q8: 1 plain Q8_0 records, 2 K pages of kServePage interleaved records
 __global__ void fill_kv_kernel(uint8_t *kv, long rows, int row_bytes, int hd, int q8,
                                uint64_t seed) {
   const long n = rows * row_bytes;
@@ -136,8 +141,11 @@ __global__ void fill_kv_kernel(uint8_t *kv, long rows, int row_bytes, int hd, in
     const uint64_t r = synth_mix(seed ^ (uint64_t)i);
     uint8_t v;
     if (q8) {
-      const int rb = q8_0_record_bytes(hd), o = (int)((i % row_bytes) % rb);
-      if (o < hd / 32 * 2) {
+      const int rb = q8_0_record_bytes(hd);
+      const bool scale_byte = q8 == 2 ? (int)(i % ((long)kServePage * rb)) < kServePage * (hd / 32) * 2
+                                      : (int)((i % row_bytes) % rb) < hd / 32 * 2;
+      const int o = (int)(i & 1);
+      if (scale_byte) {
         // binary16 scale in [2^-8, 2^-6): exponent 7..8, random mantissa
         const uint16_t half = (uint16_t)((7u + (unsigned)(r & 1)) << 10 | (unsigned)((r >> 8) & 0x3ff));
         v = (o & 1) ? (uint8_t)(half >> 8) : (uint8_t)(half & 0xff);
@@ -232,15 +240,29 @@ inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
       aa.seq_cache = (long)(b->kv_seq_bytes() / 2);
       aa.attended = b->attended;
       aa.status = status;
-      const size_t smem = attn_smem_bytes((int)c.head_dim, b->context);
-      cudaLaunchConfig_t cfg =
-          pdl_config(dim3(c.heads * kAttnSplit, B), dim3(kAttnThreads), smem, s, attr, pdl);
-      attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
-      attr[cfg.numAttrs].val.clusterDim.x = kAttnSplit;
-      attr[cfg.numAttrs].val.clusterDim.y = 1;
-      attr[cfg.numAttrs].val.clusterDim.z = 1;
-      cfg.numAttrs += 1;
-      BK(cudaLaunchKernelEx(&cfg, attention_decode_kernel, aa));
+      if (b->serve_attn) {
+        // one cluster per (sequence, KV head) over the head-major cache
+        ServeArgs sa{aa, b->context};
+        const size_t smem = serve_smem_bytes((int)c.head_dim, b->context);
+        cudaLaunchConfig_t cfg = pdl_config(dim3(kServeSplit, c.kv_heads, B),
+                                            dim3(kServeThreads), smem, s, attr, pdl);
+        attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+        attr[cfg.numAttrs].val.clusterDim.x = kServeSplit;
+        attr[cfg.numAttrs].val.clusterDim.y = 1;
+        attr[cfg.numAttrs].val.clusterDim.z = 1;
+        cfg.numAttrs += 1;
+        BK(cudaLaunchKernelEx(&cfg, attention_serve_kernel, sa));
+      } else {
+        const size_t smem = attn_smem_bytes((int)c.head_dim, b->context);
+        cudaLaunchConfig_t cfg =
+            pdl_config(dim3(c.heads * kAttnSplit, B), dim3(kAttnThreads), smem, s, attr, pdl);
+        attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+        attr[cfg.numAttrs].val.clusterDim.x = kAttnSplit;
+        attr[cfg.numAttrs].val.clusterDim.y = 1;
+        attr[cfg.numAttrs].val.clusterDim.z = 1;
+        cfg.numAttrs += 1;
+        BK(cudaLaunchKernelEx(&cfg, attention_decode_kernel, aa));
+      }
       BK(quant(b->attended, (int)(c.heads * c.head_dim / 256)));
       BK(mm(Ly.o, b->hidden, b->hidden, nullptr));
     } else {
@@ -331,6 +353,14 @@ int prism_b200_batch_create(prism_b200_model *m, uint32_t sequences, uint32_t co
   b->m = m;
   b->B = (int)sequences;
   b->context = (int)context;
+  b->serve_attn = c.kv_policy == PRISM_B200_KV_Q8_0 && c.heads / c.kv_heads <= (uint32_t)kServeGroup &&
+                  context % kServeChunk == 0 &&
+                  c.head_dim == (uint32_t)kServeThreads &&
+                  serve_smem_bytes((int)c.head_dim, (int)context) <= (size_t)kMaxSmem;
+  if (b->serve_attn &&
+      cudaFuncSetAttribute(attention_serve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)serve_smem_bytes((int)c.head_dim, (int)context)) != cudaSuccess)
+    b->serve_attn = false;
   b->L.resize(c.layers);
   const size_t B = sequences;
   cudaError_t e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
@@ -494,7 +524,8 @@ int prism_b200_batch_fill_context(prism_b200_batch *b, uint32_t position, uint64
       const long rows = (long)B * b->context;
       const int rb = (int)b->m->kv_row_bytes(), q8 = c.kv_policy == PRISM_B200_KV_Q8_0;
       fill_kv_kernel<<<4096, 256, 0, s>>>(reinterpret_cast<uint8_t *>(Bl.kc), rows, rb,
-                                          (int)c.head_dim, q8, ls * 2 + 1);
+                                          (int)c.head_dim, q8 && b->serve_attn ? 2 : q8,
+                                          ls * 2 + 1);
       fill_kv_kernel<<<4096, 256, 0, s>>>(reinterpret_cast<uint8_t *>(Bl.vc), rows, rb,
                                           (int)c.head_dim, q8, ls * 2 + 2);
     } else {
@@ -542,6 +573,32 @@ int64_t prism_b200_batch_read_state(prism_b200_batch *b, uint32_t seq, uint32_t 
       const uint8_t *base = reinterpret_cast<const uint8_t *>(which == 2 ? Bl.kc : Bl.vc);
       src = base + (size_t)seq * b->kv_seq_bytes();
       n = (size_t)pos * m->kv_row_bytes();
+      if (b->serve_attn) {
+        // head-major cache (K in interleaved pages): rebuild [position][kv head][record]
+        if (bytes < n) return -PRISM_B200_E_INVALID;
+        const int hd = (int)c.head_dim, rb = prism::q8_0_record_bytes(hd);
+        std::vector<uint8_t> head((size_t)b->context * rb);
+        uint8_t *dst = static_cast<uint8_t *>(out);
+        cudaSetDevice(m->ex->device);
+        for (uint32_t k = 0; k < c.kv_heads && pos > 0; ++k) {
+          if (cudaMemcpy(head.data(), static_cast<const uint8_t *>(src) + (size_t)k * b->context * rb,
+                         head.size(), cudaMemcpyDeviceToHost) != cudaSuccess)
+            return -PRISM_B200_E_DEVICE;
+          for (int p = 0; p < pos; ++p) {
+            uint8_t *rec = dst + ((size_t)p * c.kv_heads + k) * rb;
+            if (which == 3) {
+              memcpy(rec, head.data() + (size_t)p * rb, rb);
+              continue;
+            }
+            const uint8_t *page = head.data() + (size_t)(p / prism::kServePage) * prism::kServePage * rb;
+            const int slot = p % prism::kServePage;
+            for (int blk = 0; blk < hd / 32; ++blk)
+              memcpy(rec + 2 * blk, page + prism::kpage_scale(hd, blk, slot), 2);
+            for (int d = 0; d < hd; ++d) rec[hd / 32 * 2 + d] = page[prism::kpage_code(hd, d, slot)];
+          }
+        }
+        return (int64_t)n;
+      }
     }
   }
   if (!src) return -PRISM_B200_E_INVALID;

@@ -327,26 +327,33 @@ __device__ __forceinline__ float norm_rope_round(const float *x, const float *w,
 // reference's Source Q8_0 codec (src/kernels.rs:552-617: d = max|x|/127,
 // stored as binary16, codes = round-half-away(x * (1/d))).  Writes the
 // record when `rec` is set and returns the dequantized value scale*code.
-__device__ __forceinline__ float q8_0_roundtrip(float x, uint8_t *rec, int hd,
-                                                unsigned *status) {
-  const int i = threadIdx.x, lane = i & 31;
+__device__ __forceinline__ float q8_0_code(float x, unsigned *status, uint16_t &hb, int &q) {
   float m = fabsf(x);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
   const float d = __fdiv_rn(m, 127.0f);
   const float inv = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
-  const uint16_t hb = float_to_half_bits(d);
+  hb = float_to_half_bits(d);
   float r = roundf(__fmul_rn(x, inv));
   if (!(r >= -127.0f && r <= 127.0f)) {
     report(status, kStatusInvalid);
     r = 0.0f;
   }
-  const int q = (int)r;
+  q = (int)r;
+  return __fmul_rn(half_bits_to_float(hb), (float)q);
+}
+
+__device__ __forceinline__ float q8_0_roundtrip(float x, uint8_t *rec, int hd,
+                                                unsigned *status) {
+  const int i = threadIdx.x;
+  uint16_t hb;
+  int q;
+  const float v = q8_0_code(x, status, hb, q);
   if (rec) {
-    if (lane == 0) reinterpret_cast<uint16_t *>(rec)[i >> 5] = hb;
+    if ((i & 31) == 0) reinterpret_cast<uint16_t *>(rec)[i >> 5] = hb;
     rec[hd / 32 * 2 + i] = (uint8_t)(int8_t)q;
   }
-  return __fmul_rn(half_bits_to_float(hb), (float)q);
+  return v;
 }
 
 __host__ __device__ constexpr int q8_0_record_bytes(int hd) { return hd / 32 * 2 + hd; }

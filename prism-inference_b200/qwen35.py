@@ -69,6 +69,15 @@ class Qwen35Config:
                     ("ssm_out.weight", h, self.value_width)]
         return out
 
+    def linear_bytes(self):
+        """Bytes of every packed weight once, the tied LM head included."""
+        bb = pb.BLOCK_BYTES[self.weight_kind]
+        total = self.vocab * self.hidden // 256 * bb
+        for l in range(self.layers):
+            for _, rows, cols in self.linear_shapes(l):
+                total += rows * cols // 256 * bb
+        return total
+
     def weight_bytes_per_token(self, context=0):
         """Algorithmic HBM bytes of one decode token: every packed weight
         once (LM head included), recurrent state read + write, conv state

@@ -1,7 +1,7 @@
 """Benchmark of the B200 quantized decode hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|matvec]
+                    [--workload decode|matvec|gdn|gemm|serve]
 
 Prints ONE JSON line (rank 0).
 
@@ -18,6 +18,12 @@ state (>> 126 MB L2).
 ``--workload matvec`` is configs[0]: one TQ2_0 projection W 4096 x 4096 of
 N(0,1) x quantized to Q8_K on the device, over 64 rotating device copies
 of W (277 MB > L2).
+
+``--workload gdn`` is configs[2] (GDN decode at B = 1/16/64, chunked
+prefill of 4096 tokens); ``--workload gemm`` is configs[3] (2048-token
+projections on the tensor cores, TQ2_0 and Q2_K, both FFN shapes);
+``--workload serve`` is configs[4] (256 sequences per GPU with 8192-token
+Q8_0 KV contexts, greedy batched decode).
 
 ``--impl reference`` times the reference's CPU arithmetic on the host
 cores -- the C restatement in oracle/, since the Rust reference cannot be

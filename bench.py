@@ -424,6 +424,10 @@ def run_gdn(args):
     world, rank, local = dist_setup(args.gpus)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
     ex = pb.ProjectionExecutor(local)
     H, D = 16, 128
     peak, peak_src = peaks()
@@ -468,7 +472,7 @@ def run_gdn(args):
             g_.replay()
         e1.record(s)
         torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / K
+        us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / K, world, dev)
         nbytes = 2 * batch * H * D * D * 4 + batch * H * D * 4 * 4 + batch * H * 8
         decode["B%d" % batch] = {"us_per_step": us, "gbs": nbytes / us / 1e3,
                                  "frac": nbytes / us / 1e3 / peak, "bytes": nbytes}
@@ -490,7 +494,7 @@ def run_gdn(args):
             run()
         e1.record(s)
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / 3
+        ms = max_over_ranks(e0.elapsed_time(e1) / 3, world, dev)
         # algorithmic flops of the recurrence: 3 d^2 MACs per token per head
         # (S.k, S.q, rank-1 update) = 6 d^2 T H flops per sequence
         flops = 6.0 * D * D * T * H * batch
@@ -502,7 +506,7 @@ def run_gdn(args):
     fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
     line = {
         "metric": "Gated DeltaNet decode step GB/s (B=64) and chunked prefill TFLOP/s",
-        "value": decode["B64"]["gbs"], "unit": "GB/s", "n_gpus": world, "steps": 50,
+        "value": world * decode["B64"]["gbs"], "unit": "GB/s", "n_gpus": world, "steps": 50,
         "warmup": args.warmup, "ms_per_step": decode["B64"]["us_per_step"] / 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (configs[2] distributions)",
@@ -570,6 +574,10 @@ def run_gemm(args):
     world, rank, local = dist_setup(args.gpus)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
     ex = pb.ProjectionExecutor(local)
     s = torch.cuda.Stream(device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)   # > 126 MB L2
@@ -598,7 +606,8 @@ def run_gemm(args):
                     e1.record(s)
             torch.cuda.synchronize()
             ex.sync()
-            ms = float(np.mean([e0.elapsed_time(e1) for e0, e1 in ev]))
+            ms = max_over_ranks(float(np.mean([e0.elapsed_time(e1) for e0, e1 in ev])), world,
+                                dev)
             ops = 2.0 * GEMM_M * K * N
             results["%s_K%d_N%d" % (name, K, N)] = {"ms": ms, "tops": ops / ms / 1e9}
             total_ops += ops
@@ -615,11 +624,10 @@ def run_gemm(args):
     reps = 5
     for _ in range(reps):
         ex.project_f32_tokens(t, xh)
-    e2e_s = (time.perf_counter() - t0) / reps
+    e2e_s = max_over_ranks((time.perf_counter() - t0) / reps, world, dev)
     ex.close()
     peak, peak_src = int8_peak()
-    value = total_ops / total_ms / 1e9
-    value = max_over_ranks(value, world, dev) if world > 1 else value
+    value = total_ops / total_ms / 1e9  # per GPU, from the max-over-ranks times
     top = results["tq2_0_K2560_N9216"]
     line = {
         "metric": GEMM_METRIC, "value": value * world, "unit": "Tint-op/s", "n_gpus": world,
@@ -636,7 +644,7 @@ def run_gemm(args):
                                "quantize launch",
                      "traffic": traffic_from_profiles("gemm_tokens_kernel")},
         "gpu_launches": launches,
-        "e2e": {"value": 2.0 * GEMM_M * K * N / e2e_s / 1e12, "unit": "Tint-op/s",
+        "e2e": {"value": world * 2.0 * GEMM_M * K * N / e2e_s / 1e12, "unit": "Tint-op/s",
                 "h2d_bytes_per_step": GEMM_M * K * 4, "d2h_bytes_per_step": GEMM_M * N * 4,
                 "api": "prism_b200_project_f32_tokens (host buffers), TQ2_0 K=2560 N=9216"},
     }
@@ -824,6 +832,9 @@ def main():
         run_matvec(args)
     else:
         run_decode(args)
+    import torch
+    if torch.distributed.is_available() and torch.distributed.is_initialized():
+        torch.distributed.destroy_process_group()
 
 
 if __name__ == "__main__":

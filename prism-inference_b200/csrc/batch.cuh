@@ -16,6 +16,7 @@
 
 #include "gemm.cuh"
 #include "serve_attn.cuh"
+#include "tp.cuh"
 
 namespace prism {
 
@@ -25,6 +26,13 @@ struct BatchLayer {
   // binary16: [B][context][kv heads * hd]; Q8_0 with the serving kernel:
   // [B][kv head][context][record]
   uint16_t *kc = nullptr, *vc = nullptr;
+};
+
+// The weights one rank multiplies by: the model's own (one rank) or its
+// tensor-parallel slices (tp.cuh), with the per-head vectors of its heads.
+struct ShardLayer {
+  DeviceWeight q, k, v, o, qkv, z, beta, alpha, out, up, gate, down;
+  const float *conv_w = nullptr, *dt_bias = nullptr, *ssm_a = nullptr;
 };
 
 }  // namespace prism
@@ -46,7 +54,16 @@ struct prism_b200_batch {
   std::vector<void *> allocations;
   int64_t steps = 0;
   bool serve_attn = false;  // Q8_0 KV through attention_serve_kernel (head-major cache)
-  size_t kv_seq_bytes() const { return (size_t)context * m->kv_row_bytes(); }
+  // tensor parallelism: this rank's slice; one rank owns everything
+  prism::TpPlan tp;
+  std::vector<prism::ShardLayer> S;
+  prism::DeviceWeight lm;   // output head rows [tp.v0, tp.v1)
+  prism::TpExchange x;
+  int heads = 0, kv_heads = 0, gdn_groups = 0, gdn_heads = 0, ffn = 0;  // this rank's
+  size_t kv_row = 0;        // bytes of one cached position of this rank's KV heads
+  size_t kv_seq_bytes() const { return (size_t)context * kv_row; }
+  int gdn_width() const { return gdn_heads * (int)m->cfg.ssm_state; }
+  int gdn_channels() const { return (2 * gdn_groups + gdn_heads) * (int)m->cfg.ssm_state; }
 };
 
 namespace prism {
@@ -192,33 +209,58 @@ inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
                                         b->hidden, H, status);
     if (e != cudaSuccess) return e;
   }
+  const bool tpx = b->tp.size > 1;
+  // a row-parallel projection's partial waits in an exchange slot until the
+  // next normalisation sums it (tensor parallelism only)
+  int pending = -1, pending_index = 0;
+  const unsigned long long gemm_ctas =
+      (unsigned long long)((H + kGemmN - 1) / kGemmN) * ((B + kGemmM - 1) / kGemmM);
   auto norm = [&](const float *w) {
+    if (pending < 0) {
+      cudaLaunchConfig_t cfg = pdl_config(dim3(B), dim3(256), 0, s, attr, pdl);
+      return cudaLaunchKernelEx(&cfg, rmsnorm_rows_kernel, (const float *)b->hidden, w, H, c.eps,
+                                b->xn, status);
+    }
+    TpWait tw{TpExchange::count(b->x.base, pending), b->x.xstep, (unsigned long long)c.layers,
+              (unsigned long long)pending_index, (unsigned long long)b->tp.size * gemm_ctas};
+    const float *slot = b->x.slot(b->x.base, pending);
+    pending = -1;
     cudaLaunchConfig_t cfg = pdl_config(dim3(B), dim3(256), 0, s, attr, pdl);
-    return cudaLaunchKernelEx(&cfg, rmsnorm_rows_kernel, (const float *)b->hidden, w, H, c.eps,
-                              b->xn, status);
+    return cudaLaunchKernelEx(&cfg, tp_reduce_norm_kernel, slot, b->tp.size, B, H, tw, b->hidden,
+                              w, c.eps, b->xn, status);
   };
   auto quant = [&](const float *x, int nb) {
     return launch_token_quantize(x, B, nb, 0, token_q8k_carve(b->tok, B, nb), status, s, pdl);
   };
   auto mm = [&](const DeviceWeight &w, float *y, const float *residual,
-                unsigned long long *keys) {
+                unsigned long long *keys, int row_base = 0) {
     return launch_token_matmul(w, B, token_q8k_carve(b->tok, B, w.nb), y, residual, keys,
-                               status, s, pdl);
+                               status, s, pdl, nullptr, row_base);
+  };
+  // y = hidden + x W^T over all ranks (row-parallel when sharded)
+  auto mm_residual = [&](const DeviceWeight &w, int slot, int index) {
+    if (!tpx) return mm(w, b->hidden, b->hidden, nullptr);
+    const GemmPush push = b->x.push(b->tp.rank, slot);
+    pending = slot;
+    pending_index = index;
+    return launch_token_matmul(w, B, token_q8k_carve(b->tok, B, w.nb), nullptr, nullptr, nullptr,
+                               status, s, pdl, &push, 0);
   };
 #define BK(x)                            \
   if ((e = (x)) != cudaSuccess) return e
   for (size_t l = 0; l < m->L.size(); ++l) {
     ModelLayer &Ly = m->L[l];
+    ShardLayer &Sh = b->S[l];
     BatchLayer &Bl = b->L[l];
     BK(norm(Ly.attn_norm));
     BK(quant(b->xn, hnb));
     if (Ly.full) {
-      BK(mm(Ly.q, b->projected, nullptr, nullptr));
-      BK(mm(Ly.k, b->key, nullptr, nullptr));
-      BK(mm(Ly.v, b->value, nullptr, nullptr));
+      BK(mm(Sh.q, b->projected, nullptr, nullptr));
+      BK(mm(Sh.k, b->key, nullptr, nullptr));
+      BK(mm(Sh.v, b->value, nullptr, nullptr));
       AttnArgs aa{};
-      aa.heads = (int)c.heads;
-      aa.kv_heads = (int)c.kv_heads;
+      aa.heads = b->heads;
+      aa.kv_heads = b->kv_heads;
       aa.hd = (int)c.head_dim;
       aa.rope_dim = (int)c.rope_dim;
       for (int j = 0; j < 3; ++j) aa.sections[j] = (int)c.rope_sections[j];
@@ -234,9 +276,9 @@ inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
       aa.q8 = c.kv_policy == PRISM_B200_KV_Q8_0 ? 1 : 0;
       aa.position = b->d_pos;
       aa.pos_stride = 1;
-      aa.seq_proj = (long)c.heads * c.head_dim * 2;
-      aa.seq_kv_in = m->kvw();
-      aa.seq_out = (long)c.heads * c.head_dim;
+      aa.seq_proj = (long)b->heads * c.head_dim * 2;
+      aa.seq_kv_in = (long)b->kv_heads * c.head_dim;
+      aa.seq_out = (long)b->heads * c.head_dim;
       aa.seq_cache = (long)(b->kv_seq_bytes() / 2);
       aa.attended = b->attended;
       aa.status = status;
@@ -244,7 +286,7 @@ inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
         // one cluster per (sequence, KV head) over the head-major cache
         ServeArgs sa{aa, b->context};
         const size_t smem = serve_smem_bytes((int)c.head_dim, b->context);
-        cudaLaunchConfig_t cfg = pdl_config(dim3(kServeSplit, c.kv_heads, B),
+        cudaLaunchConfig_t cfg = pdl_config(dim3(kServeSplit, b->kv_heads, B),
                                             dim3(kServeThreads), smem, s, attr, pdl);
         attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
         attr[cfg.numAttrs].val.clusterDim.x = kServeSplit;
@@ -255,7 +297,7 @@ inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
       } else {
         const size_t smem = attn_smem_bytes((int)c.head_dim, b->context);
         cudaLaunchConfig_t cfg =
-            pdl_config(dim3(c.heads * kAttnSplit, B), dim3(kAttnThreads), smem, s, attr, pdl);
+            pdl_config(dim3(b->heads * kAttnSplit, B), dim3(kAttnThreads), smem, s, attr, pdl);
         attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
         attr[cfg.numAttrs].val.clusterDim.x = kAttnSplit;
         attr[cfg.numAttrs].val.clusterDim.y = 1;
@@ -263,67 +305,83 @@ inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
         cfg.numAttrs += 1;
         BK(cudaLaunchKernelEx(&cfg, attention_decode_kernel, aa));
       }
-      BK(quant(b->attended, (int)(c.heads * c.head_dim / 256)));
-      BK(mm(Ly.o, b->hidden, b->hidden, nullptr));
+      BK(quant(b->attended, (int)(b->heads * c.head_dim / 256)));
+      BK(mm_residual(Sh.o, 0, (int)l));
     } else {
-      BK(mm(Ly.qkv, b->mixed, nullptr, nullptr));
-      BK(mm(Ly.z, b->zgate, nullptr, nullptr));
-      BK(mm(Ly.beta, b->beta, nullptr, nullptr));
-      BK(mm(Ly.alpha, b->alpha, nullptr, nullptr));
+      BK(mm(Sh.qkv, b->mixed, nullptr, nullptr));
+      BK(mm(Sh.z, b->zgate, nullptr, nullptr));
+      BK(mm(Sh.beta, b->beta, nullptr, nullptr));
+      BK(mm(Sh.alpha, b->alpha, nullptr, nullptr));
       GdnArgs g{};
       g.S = (int)c.ssm_state;
-      g.groups = (int)c.ssm_groups;
-      g.values = (int)c.ssm_values;
+      g.groups = b->gdn_groups;
+      g.values = b->gdn_heads;
       g.conv_k = (int)c.conv_kernel;
       g.eps = c.eps;
       g.mixed = b->mixed;
       g.zgate = b->zgate;
       g.beta_in = b->beta;
       g.alpha_in = b->alpha;
-      g.in_stride = m->channels();
-      g.z_stride = m->value_width();
-      g.ab_stride = c.ssm_values;
-      g.conv_w = Ly.conv_w;
-      g.dt_bias = Ly.dt_bias;
-      g.ssm_a = Ly.ssm_a;
+      g.in_stride = b->gdn_channels();
+      g.z_stride = b->gdn_width();
+      g.ab_stride = b->gdn_heads;
+      g.conv_w = Sh.conv_w;
+      g.dt_bias = Sh.dt_bias;
+      g.ssm_a = Sh.ssm_a;
       g.norm_w = Ly.ssm_norm;
       g.conv_state = Bl.conv;
-      g.conv_stride = (long)m->channels() * (c.conv_kernel - 1);
+      g.conv_stride = (long)b->gdn_channels() * (c.conv_kernel - 1);
       g.conv_buf_stride = g.conv_stride * B;
       g.state = Bl.matrix;
-      g.state_stride = (long)c.ssm_values * c.ssm_state * c.ssm_state;
+      g.state_stride = (long)b->gdn_heads * c.ssm_state * c.ssm_state;
       g.attended = b->attended;
-      g.out_stride = m->value_width();
+      g.out_stride = b->gdn_width();
       g.position = b->d_step;  // the double-buffered history alternates every step
       g.status = status;
       cudaLaunchConfig_t cfg =
-          pdl_config(dim3(c.ssm_values, B), dim3(kGdnThreads), 0, s, attr, pdl);
+          pdl_config(dim3(b->gdn_heads, B), dim3(kGdnThreads), 0, s, attr, pdl);
       BK(cudaLaunchKernelEx(&cfg, gdn_decode_kernel, g));
-      BK(quant(b->attended, m->value_width() / 256));
-      BK(mm(Ly.out, b->hidden, b->hidden, nullptr));
+      BK(quant(b->attended, b->gdn_width() / 256));
+      BK(mm_residual(Sh.out, 0, (int)l));
     }
     BK(norm(Ly.post_norm));
     BK(quant(b->xn, hnb));
-    BK(mm(Ly.up, b->up, nullptr, nullptr));
-    BK(mm(Ly.gate, b->gate, nullptr, nullptr));
+    BK(mm(Sh.up, b->up, nullptr, nullptr));
+    BK(mm(Sh.gate, b->gate, nullptr, nullptr));
     {
-      const long n = (long)B * c.ffn;
+      const long n = (long)B * b->ffn;
       cudaLaunchConfig_t cfg =
           pdl_config(dim3((unsigned)std::min<long>((n + 255) / 256, 4096)), dim3(256), 0, s,
                      attr, pdl);
       BK(cudaLaunchKernelEx(&cfg, swiglu_kernel, b->up, (const float *)b->gate, n, status));
     }
-    BK(quant(b->up, (int)(c.ffn / 256)));
-    BK(mm(Ly.down, b->hidden, b->hidden, nullptr));
+    BK(quant(b->up, b->ffn / 256));
+    BK(mm_residual(Sh.down, 1, (int)l));
   }
   if (greedy) {
     BK(norm(m->out_norm));
     BK(quant(b->xn, hnb));
-    BK(mm(m->embd, nullptr, nullptr, b->d_keys));
+    BK(mm(b->lm, nullptr, nullptr, b->d_keys, b->tp.v0));
+  } else if (pending >= 0) {
+    BK(norm(nullptr));  // the last exchange still has to reach the hidden state
   }
   cudaLaunchConfig_t cfg = pdl_config(dim3(1), dim3(256), 0, s, attr, pdl);
-  BK(cudaLaunchKernelEx(&cfg, batch_finish_kernel, b->d_keys, b->d_tokens, b->d_pos, B,
-                        b->d_step, greedy ? 1 : 0));
+  if (tpx) {
+    TpKeys kp{};
+    for (int p = 0; p < b->tp.size; ++p) {
+      kp.dst[p] = b->x.keys(b->x.peer[p]) + (size_t)b->tp.rank * B;
+      kp.count[p] = TpExchange::count(b->x.peer[p], 2);
+    }
+    TpWait kw{TpExchange::count(b->x.base, 2), b->x.xstep, 1ull, 0ull,
+              (unsigned long long)b->tp.size};
+    BK(cudaLaunchKernelEx(&cfg, tp_finish_kernel, b->d_keys, kp,
+                          (const unsigned long long *)b->x.keys(b->x.base), b->tp.size, kw,
+                          b->d_tokens, b->d_pos, B, b->d_step, b->x.xstep, greedy ? 1 : 0,
+                          status));
+  } else {
+    BK(cudaLaunchKernelEx(&cfg, batch_finish_kernel, b->d_keys, b->d_tokens, b->d_pos, B,
+                          b->d_step, greedy ? 1 : 0));
+  }
 #undef BK
   return cudaSuccess;
 }
@@ -334,6 +392,11 @@ extern "C" {
 
 int prism_b200_batch_create(prism_b200_model *m, uint32_t sequences, uint32_t context,
                             prism_b200_batch **out) {
+  return prism_b200_batch_create_tp(m, sequences, context, 0, 1, out);
+}
+
+int prism_b200_batch_create_tp(prism_b200_model *m, uint32_t sequences, uint32_t context,
+                               uint32_t tp_rank, uint32_t tp_size, prism_b200_batch **out) {
   using namespace prism;
   if (!m || !out) return PRISM_B200_E_INVALID;
   *out = nullptr;
@@ -347,13 +410,27 @@ int prism_b200_batch_create(prism_b200_model *m, uint32_t sequences, uint32_t co
                     context);
   if ((context + kAttnSplit - 1) / kAttnSplit + 1 > 16384)
     return ex->fail(PRISM_B200_E_UNSUPPORTED, "context %u exceeds the attention kernel", context);
-  cudaSetDevice(ex->device);
   const auto &c = m->cfg;
+  TpPlan plan;
+  if (const char *why = tp_plan(c, (int)tp_rank, (int)tp_size, plan))
+    return ex->fail(tp_size < 1 || tp_size > (uint32_t)kMaxTp || tp_rank >= tp_size
+                        ? PRISM_B200_E_INVALID
+                        : PRISM_B200_E_UNSUPPORTED,
+                    "tensor parallelism %u/%u: %s", tp_rank, tp_size, why);
+  cudaSetDevice(ex->device);
   auto *b = new prism_b200_batch();
   b->m = m;
   b->B = (int)sequences;
   b->context = (int)context;
-  b->serve_attn = c.kv_policy == PRISM_B200_KV_Q8_0 && c.heads / c.kv_heads <= (uint32_t)kServeGroup &&
+  b->tp = plan;
+  const bool tpx = plan.size > 1;
+  b->heads = plan.qh1 - plan.qh0;
+  b->kv_heads = plan.kv1 - plan.kv0;
+  b->gdn_heads = tpx ? plan.gh1 - plan.gh0 : (int)c.ssm_values;
+  b->gdn_groups = tpx ? b->gdn_heads : (int)c.ssm_groups;
+  b->ffn = (plan.fb1 - plan.fb0) * 256;
+  b->kv_row = m->kv_row_bytes() / c.kv_heads * b->kv_heads;
+  b->serve_attn = c.kv_policy == PRISM_B200_KV_Q8_0 && b->heads / b->kv_heads <= kServeGroup &&
                   context % kServeChunk == 0 &&
                   c.head_dim == (uint32_t)kServeThreads &&
                   serve_smem_bytes((int)c.head_dim, (int)context) <= (size_t)kMaxSmem;
@@ -364,20 +441,74 @@ int prism_b200_batch_create(prism_b200_model *m, uint32_t sequences, uint32_t co
   b->L.resize(c.layers);
   const size_t B = sequences;
   cudaError_t e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+  // this rank's weights: the model's own, or gathered slices
+  b->S.resize(c.layers);
+  const int S = (int)c.ssm_state, hd = (int)c.head_dim;
+  for (uint32_t l = 0; l < c.layers && e == cudaSuccess; ++l) {
+    const ModelLayer &Ly = m->L[l];
+    ShardLayer &Sh = b->S[l];
+    if (!tpx) {
+      Sh.q = Ly.q; Sh.k = Ly.k; Sh.v = Ly.v; Sh.o = Ly.o;
+      Sh.qkv = Ly.qkv; Sh.z = Ly.z; Sh.beta = Ly.beta; Sh.alpha = Ly.alpha; Sh.out = Ly.out;
+      Sh.up = Ly.up; Sh.gate = Ly.gate; Sh.down = Ly.down;
+      Sh.conv_w = Ly.conv_w; Sh.dt_bias = Ly.dt_bias; Sh.ssm_a = Ly.ssm_a;
+      continue;
+    }
+    auto gather = [&](const DeviceWeight &w, const std::vector<int> &rows, int b0, int nb,
+                      DeviceWeight &o) {
+      if (e == cudaSuccess)
+        e = tp_gather_weight(w, rows, b0, nb, ex->num_sms, b->allocations, b->stream, o);
+    };
+    if (Ly.full) {
+      // q rows interleave [query(hd) | gate(hd)] per head
+      gather(Ly.q, tp_rows({{plan.qh0 * 2 * hd, plan.qh1 * 2 * hd}}), 0, Ly.q.nb, Sh.q);
+      gather(Ly.k, tp_rows({{plan.kv0 * hd, plan.kv1 * hd}}), 0, Ly.k.nb, Sh.k);
+      gather(Ly.v, tp_rows({{plan.kv0 * hd, plan.kv1 * hd}}), 0, Ly.v.nb, Sh.v);
+      gather(Ly.o, tp_rows({{0, (int)c.hidden}}), plan.qh0 * hd / 256,
+             (plan.qh1 - plan.qh0) * hd / 256, Sh.o);
+    } else {
+      const int kw = (int)c.ssm_groups * S, g0 = plan.gh0 * S, g1 = plan.gh1 * S;
+      gather(Ly.qkv, tp_rows({{g0, g1}, {kw + g0, kw + g1}, {2 * kw + g0, 2 * kw + g1}}), 0,
+             Ly.qkv.nb, Sh.qkv);
+      gather(Ly.z, tp_rows({{g0, g1}}), 0, Ly.z.nb, Sh.z);
+      gather(Ly.beta, tp_rows({{plan.gh0, plan.gh1}}), 0, Ly.beta.nb, Sh.beta);
+      gather(Ly.alpha, tp_rows({{plan.gh0, plan.gh1}}), 0, Ly.alpha.nb, Sh.alpha);
+      gather(Ly.out, tp_rows({{0, (int)c.hidden}}), g0 / 256, (g1 - g0) / 256, Sh.out);
+      // convolution weights of this rank's q, k and v channels
+      float *cw = nullptr;
+      if (e == cudaSuccess) e = batch_alloc(b, &cw, (size_t)3 * (g1 - g0) * c.conv_kernel);
+      for (int part = 0; part < 3 && e == cudaSuccess; ++part)
+        e = cudaMemcpy(cw + (size_t)part * (g1 - g0) * c.conv_kernel,
+                       Ly.conv_w + (size_t)(part * kw + g0) * c.conv_kernel,
+                       (size_t)(g1 - g0) * c.conv_kernel * 4, cudaMemcpyDeviceToDevice);
+      Sh.conv_w = cw;
+      Sh.dt_bias = Ly.dt_bias + plan.gh0;
+      Sh.ssm_a = Ly.ssm_a + plan.gh0;
+    }
+    gather(Ly.up, tp_rows({{plan.fb0 * 256, plan.fb1 * 256}}), 0, Ly.up.nb, Sh.up);
+    gather(Ly.gate, tp_rows({{plan.fb0 * 256, plan.fb1 * 256}}), 0, Ly.gate.nb, Sh.gate);
+    gather(Ly.down, tp_rows({{0, (int)c.hidden}}), plan.fb0, plan.fb1 - plan.fb0, Sh.down);
+  }
+  if (!tpx) {
+    b->lm = m->embd;
+  } else if (e == cudaSuccess) {
+    e = tp_gather_weight(m->embd, tp_rows({{plan.v0, plan.v1}}), 0, m->embd.nb, ex->num_sms,
+                         b->allocations, b->stream, b->lm);
+  }
 #define A(p, n) \
   if (e == cudaSuccess) e = batch_alloc(b, &(p), (n))
   A(b->hidden, B * c.hidden);
   A(b->xn, B * c.hidden);
-  A(b->mixed, B * m->channels());
-  A(b->zgate, B * m->value_width());
-  A(b->beta, B * c.ssm_values);
-  A(b->alpha, B * c.ssm_values);
-  A(b->attended, B * std::max<size_t>(m->value_width(), (size_t)c.heads * c.head_dim));
-  A(b->projected, B * c.heads * c.head_dim * 2);
-  A(b->key, B * m->kvw());
-  A(b->value, B * m->kvw());
-  A(b->up, B * c.ffn);
-  A(b->gate, B * c.ffn);
+  A(b->mixed, B * b->gdn_channels());
+  A(b->zgate, B * b->gdn_width());
+  A(b->beta, B * b->gdn_heads);
+  A(b->alpha, B * b->gdn_heads);
+  A(b->attended, B * std::max<size_t>(b->gdn_width(), (size_t)b->heads * hd));
+  A(b->projected, B * b->heads * hd * 2);
+  A(b->key, B * b->kv_heads * hd);
+  A(b->value, B * b->kv_heads * hd);
+  A(b->up, B * b->ffn);
+  A(b->gate, B * b->ffn);
   uint8_t *tokbuf = nullptr;
   A(tokbuf, token_q8k_bytes(B, (int)std::max<uint32_t>(c.ffn, c.heads * c.head_dim) / 256 + 1));
   b->tok = tokbuf;
@@ -391,11 +522,17 @@ int prism_b200_batch_create(prism_b200_model *m, uint32_t sequences, uint32_t co
       A(Bl.kc, B * b->kv_seq_bytes() / 2);
       A(Bl.vc, B * b->kv_seq_bytes() / 2);
     } else {
-      A(Bl.conv, 2 * B * m->channels() * (c.conv_kernel - 1));
-      A(Bl.matrix, B * c.ssm_values * c.ssm_state * c.ssm_state);
+      A(Bl.conv, 2 * B * b->gdn_channels() * (c.conv_kernel - 1));
+      A(Bl.matrix, B * b->gdn_heads * S * S);
     }
   }
+  if (tpx) {
+    b->x.layout(plan.size, (int)B, (int)c.hidden);
+    A(b->x.base, b->x.bytes);
+    A(b->x.xstep, 1);
+  }
 #undef A
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     prism_b200_batch_destroy(b);
     return cuda_fail(ex, e, "batch allocation");
@@ -404,11 +541,64 @@ int prism_b200_batch_create(prism_b200_model *m, uint32_t sequences, uint32_t co
   return PRISM_B200_OK;
 }
 
+int prism_b200_tp_plan(const prism_b200_qwen35_config *cfg, uint32_t tp_rank, uint32_t tp_size,
+                       int32_t *out) {
+  using namespace prism;
+  if (!cfg || !out) return PRISM_B200_E_INVALID;
+  if (tp_size < 1 || tp_size > (uint32_t)kMaxTp || tp_rank >= tp_size) return PRISM_B200_E_INVALID;
+  TpPlan p;
+  if (tp_plan(*cfg, (int)tp_rank, (int)tp_size, p)) return PRISM_B200_E_UNSUPPORTED;
+  const int32_t v[10] = {p.qh0, p.qh1, p.kv0, p.kv1, p.gh0, p.gh1, p.fb0, p.fb1, p.v0, p.v1};
+  memcpy(out, v, sizeof(v));
+  return PRISM_B200_OK;
+}
+
+int prism_b200_batch_exchange_handle(const prism_b200_batch *b, void *handle) {
+  if (!b || !handle) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = b->m->ex;
+  if (b->tp.size < 2) return ex->fail(PRISM_B200_E_INVALID, "batch is not tensor-parallel");
+  cudaSetDevice(ex->device);
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, b->x.base), "exchange handle");
+  static_assert(sizeof(h) == PRISM_B200_EXCHANGE_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  return PRISM_B200_OK;
+}
+
+int prism_b200_batch_connect(prism_b200_batch *b, const void *handles) {
+  using namespace prism;
+  if (!b || !handles) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = b->m->ex;
+  if (b->tp.size < 2) return ex->fail(PRISM_B200_E_INVALID, "batch is not tensor-parallel");
+  if (b->x.connected) return ex->fail(PRISM_B200_E_INVALID, "batch is already connected");
+  cudaSetDevice(ex->device);
+  const uint8_t *hb = static_cast<const uint8_t *>(handles);
+  for (int p = 0; p < b->tp.size; ++p) {
+    if (p == b->tp.rank) {
+      b->x.peer[p] = b->x.base;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, hb + (size_t)p * sizeof(h), sizeof(h));
+    void *ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess)
+      return ex->fail(PRISM_B200_E_DEVICE, "open rank %d's exchange buffer: %s", p,
+                      cudaGetErrorString(e));
+    b->x.peer[p] = static_cast<uint8_t *>(ptr);
+    b->x.opened[p] = true;
+  }
+  b->x.connected = true;
+  return PRISM_B200_OK;
+}
+
 void prism_b200_batch_destroy(prism_b200_batch *b) {
   if (!b) return;
   cudaSetDevice(b->m->ex->device);
   if (b->stream) cudaStreamSynchronize(b->stream);
   if (b->graph) cudaGraphExecDestroy(b->graph);
+  for (int p = 0; p < prism::kMaxTp; ++p)
+    if (b->x.opened[p]) cudaIpcCloseMemHandle(b->x.peer[p]);
   for (void *p : b->allocations) cudaFree(p);
   if (b->stream) cudaStreamDestroy(b->stream);
   delete b;
@@ -428,9 +618,9 @@ int prism_b200_batch_reset(prism_b200_batch *b) {
       CK(cudaMemsetAsync(Bl.kc, 0, B * b->kv_seq_bytes(), s), "batch reset");
       CK(cudaMemsetAsync(Bl.vc, 0, B * b->kv_seq_bytes(), s), "batch reset");
     } else {
-      CK(cudaMemsetAsync(Bl.conv, 0, 2 * B * b->m->channels() * (c.conv_kernel - 1) * 4, s),
+      CK(cudaMemsetAsync(Bl.conv, 0, 2 * B * b->gdn_channels() * (c.conv_kernel - 1) * 4, s),
          "batch reset");
-      CK(cudaMemsetAsync(Bl.matrix, 0, B * c.ssm_values * c.ssm_state * c.ssm_state * 4, s),
+      CK(cudaMemsetAsync(Bl.matrix, 0, B * b->gdn_heads * c.ssm_state * c.ssm_state * 4, s),
          "batch reset");
     }
   }
@@ -466,6 +656,8 @@ int prism_b200_batch_step(prism_b200_batch *b, const uint32_t *tokens, uint32_t 
   for (int i = 0; i < b->B; ++i)
     if (tokens[i] >= c.vocab) return ex->fail(PRISM_B200_E_INVALID, "token out of range");
   if (b->steps >= b->context) return ex->fail(PRISM_B200_E_INVALID, "context is exhausted");
+  if (b->tp.size > 1 && !b->x.connected)
+    return ex->fail(PRISM_B200_E_INVALID, "connect the tensor-parallel ranks first");
   cudaSetDevice(ex->device);
   CK(cudaMemcpyAsync(b->d_tokens, tokens, (size_t)b->B * 4, cudaMemcpyHostToDevice, b->stream),
      "token copy");
@@ -522,7 +714,7 @@ int prism_b200_batch_fill_context(prism_b200_batch *b, uint32_t position, uint64
     const uint64_t ls = seed * 1000003ull + l * 7919ull;
     if (b->m->L[l].full) {
       const long rows = (long)B * b->context;
-      const int rb = (int)b->m->kv_row_bytes(), q8 = c.kv_policy == PRISM_B200_KV_Q8_0;
+      const int rb = (int)b->kv_row, q8 = c.kv_policy == PRISM_B200_KV_Q8_0;
       fill_kv_kernel<<<4096, 256, 0, s>>>(reinterpret_cast<uint8_t *>(Bl.kc), rows, rb,
                                           (int)c.head_dim, q8 && b->serve_attn ? 2 : q8,
                                           ls * 2 + 1);
@@ -530,10 +722,10 @@ int prism_b200_batch_fill_context(prism_b200_batch *b, uint32_t position, uint64
                                           (int)c.head_dim, q8, ls * 2 + 2);
     } else {
       fill_f32_kernel<<<4096, 256, 0, s>>>(Bl.matrix,
-                                           (long)B * c.ssm_values * c.ssm_state * c.ssm_state,
+                                           (long)B * b->gdn_heads * c.ssm_state * c.ssm_state,
                                            0.05f, ls * 2 + 3);
       fill_f32_kernel<<<1024, 256, 0, s>>>(Bl.conv,
-                                           (long)2 * B * b->m->channels() * (c.conv_kernel - 1),
+                                           (long)2 * B * b->gdn_channels() * (c.conv_kernel - 1),
                                            0.5f, ls * 2 + 4);
     }
   }
@@ -557,14 +749,14 @@ int64_t prism_b200_batch_read_state(prism_b200_batch *b, uint32_t seq, uint32_t 
     n = (size_t)c.hidden * 4;
   } else if (layer < c.layers) {
     const prism::BatchLayer &Bl = b->L[layer];
-    const size_t hist = (size_t)m->channels() * (c.conv_kernel - 1);
+    const size_t hist = (size_t)b->gdn_channels() * (c.conv_kernel - 1);
     if (which == 0 && !m->L[layer].full) {
       int step = 0;
       cudaMemcpy(&step, b->d_step, 4, cudaMemcpyDeviceToHost);
       src = Bl.conv + ((size_t)(step & 1) * b->B + seq) * hist;
       n = hist * 4;
     } else if (which == 1 && !m->L[layer].full) {
-      const size_t per = (size_t)c.ssm_values * c.ssm_state * c.ssm_state;
+      const size_t per = (size_t)b->gdn_heads * c.ssm_state * c.ssm_state;
       src = Bl.matrix + seq * per;
       n = per * 4;
     } else if ((which == 2 || which == 3) && m->L[layer].full) {
@@ -572,7 +764,7 @@ int64_t prism_b200_batch_read_state(prism_b200_batch *b, uint32_t seq, uint32_t 
       cudaMemcpy(&pos, b->d_pos + seq, 4, cudaMemcpyDeviceToHost);
       const uint8_t *base = reinterpret_cast<const uint8_t *>(which == 2 ? Bl.kc : Bl.vc);
       src = base + (size_t)seq * b->kv_seq_bytes();
-      n = (size_t)pos * m->kv_row_bytes();
+      n = (size_t)pos * b->kv_row;
       if (b->serve_attn) {
         // head-major cache (K in interleaved pages): rebuild [position][kv head][record]
         if (bytes < n) return -PRISM_B200_E_INVALID;
@@ -580,12 +772,13 @@ int64_t prism_b200_batch_read_state(prism_b200_batch *b, uint32_t seq, uint32_t 
         std::vector<uint8_t> head((size_t)b->context * rb);
         uint8_t *dst = static_cast<uint8_t *>(out);
         cudaSetDevice(m->ex->device);
-        for (uint32_t k = 0; k < c.kv_heads && pos > 0; ++k) {
+        const uint32_t kvh = (uint32_t)b->kv_heads;
+        for (uint32_t k = 0; k < kvh && pos > 0; ++k) {
           if (cudaMemcpy(head.data(), static_cast<const uint8_t *>(src) + (size_t)k * b->context * rb,
                          head.size(), cudaMemcpyDeviceToHost) != cudaSuccess)
             return -PRISM_B200_E_DEVICE;
           for (int p = 0; p < pos; ++p) {
-            uint8_t *rec = dst + ((size_t)p * c.kv_heads + k) * rb;
+            uint8_t *rec = dst + ((size_t)p * kvh + k) * rb;
             if (which == 3) {
               memcpy(rec, head.data() + (size_t)p * rb, rb);
               continue;

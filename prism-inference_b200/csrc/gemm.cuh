@@ -180,6 +180,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// Tensor-parallel exchange of a row-parallel partial product: instead of
+// storing Y, every CTA stores its tile into each rank's receive slot for
+// this rank (peer memory mapped over NVLink, this rank's own slot included),
+// then adds 1 to each rank's arrival counter for the slot, after a
+// system-scope fence.  The receiving rank sums the slots in rank order.
+constexpr int kMaxTp = 8;
+struct GemmPush {
+  float *dst[kMaxTp];                 // rank p's slot [M][rows] for this rank's partial
+  unsigned long long *count[kMaxTp];  // rank p's arrival counter of the slot
+  int n;                              // ranks (0: no exchange, store Y)
+};
+
 struct GemmArgs {
   const int8_t *codes;    // tile-major Q8_K codes (TokenQ8K)
   const int8_t *split;    // tile-major split group sums
@@ -190,7 +202,9 @@ struct GemmArgs {
   float *y;               // [M][rows], or null
   const float *residual;  // optional [M][rows]: y = residual + chain (may alias y)
   unsigned long long *argmax_keys;  // optional [M]: greedy key over each token's rows
+  int row_base;           // index of row 0 in the argmax key (a vocabulary slice's offset)
   unsigned *status;
+  GemmPush push;
 };
 
 // Warp roles of the 14-warp CTA.
@@ -469,7 +483,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       otile[tl * kPitch + 64 * half + c] = acc[c];
       if (n < g.rows) {
         finite &= is_finite_f(acc[c]);
-        const unsigned long long key = argmax_key(acc[c], n);
+        const unsigned long long key = argmax_key(acc[c], g.row_base + n);
         best = key > best ? key : best;
       }
     }
@@ -483,7 +497,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, L::kTmemCols);
   }
-  if (ok) {
+  if (ok && g.push.n) {
+    // row-parallel partial: coalesced 512-byte rows into every rank's slot
+    for (int i = tid; i < kGemmM * kGemmN; i += kGemmThreads) {
+      const int t = i / kGemmN, c = i % kGemmN;
+      const int mm = m0 + t, n = n0 + c;
+      if (mm < g.M && n < g.rows) {
+        const float v = otile[t * kPitch + c];
+        for (int p = 0; p < g.push.n; ++p) g.push.dst[p][(size_t)mm * g.rows + n] = v;
+      }
+    }
+  } else if (ok) {
     for (int i = tid; i < kGemmM * kGemmN; i += kGemmThreads) {
       const int t = i / kGemmN, c = i % kGemmN;
       const int mm = m0 + t, n = n0 + c;
@@ -496,6 +520,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (g.y) g.y[(size_t)mm * g.rows + n] = v;
       }
     }
+  }
+  if (g.push.n) {
+    // publish: every writer's stores are visible system-wide before the
+    // counters move.  A failed CTA still counts, so that no rank waits out
+    // its limit; its own status word carries the failure.
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0)
+      for (int p = 0; p < g.push.n; ++p) atomicAdd_system(g.push.count[p], 1ull);
   }
 }
 
@@ -522,7 +555,8 @@ inline cudaError_t launch_token_quantize(const float *x, size_t M, int nb, int p
 inline cudaError_t launch_token_matmul(const DeviceWeight &dw, size_t M, const TokenQ8K &t,
                                        float *y, const float *residual,
                                        unsigned long long *argmax_keys, unsigned *status,
-                                       cudaStream_t s, bool pdl) {
+                                       cudaStream_t s, bool pdl, const GemmPush *push = nullptr,
+                                       int row_base = 0) {
   GemmArgs g;
   g.codes = t.codes;
   g.split = t.split;
@@ -536,7 +570,11 @@ inline cudaError_t launch_token_matmul(const DeviceWeight &dw, size_t M, const T
   g.y = y;
   g.residual = residual;
   g.argmax_keys = argmax_keys;
+  g.row_base = 0;
   g.status = status;
+  g.push.n = 0;
+  if (push) g.push = *push;
+  if (row_base) g.row_base = row_base;
   void (*kernel)(GemmArgs) = dw.kind == 35 ? gemm_tokens_kernel<35> : gemm_tokens_kernel<10>;
   const int smem = dw.kind == 35 ? gemm_smem_bytes<35>() : gemm_smem_bytes<10>();
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

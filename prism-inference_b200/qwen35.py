@@ -156,6 +156,38 @@ class _CConfig(__import__("ctypes").Structure):
 KV_F16, KV_Q8_0 = 0, 1
 
 
+def c_config(cfg, kv_policy=KV_F16):
+    """The C ABI's prism_b200_qwen35_config of a Qwen35Config."""
+    import ctypes as c
+    cc = _CConfig()
+    for f, _ in _CConfig._fields_:
+        if f == "rope_sections":
+            cc.rope_sections = (c.c_uint32 * 4)(*cfg.rope_sections)
+        elif f == "kv_policy":
+            cc.kv_policy = kv_policy
+        else:
+            setattr(cc, f, getattr(cfg, f))
+    return cc
+
+
+def tp_plan(cfg, rank, size):
+    """The slice of every linear rank `rank` of a `size`-way tensor-parallel
+    batch owns (host only): dict of [first, end) ranges -- query heads, KV
+    heads, Gated DeltaNet heads, FFN 256-row blocks, vocabulary rows."""
+    import ctypes as c
+    L = pb.load()
+    fn = L.prism_b200_tp_plan
+    fn.restype = c.c_int
+    fn.argtypes = [c.c_void_p, c.c_uint32, c.c_uint32, c.c_void_p]
+    cc = c_config(cfg)
+    out = np.zeros(10, np.int32)
+    st = fn(c.byref(cc), rank, size, out.ctypes.data)
+    if st:
+        raise pb.PrismB200Error(st, "tensor-parallel plan %d/%d" % (rank, size))
+    keys = ["query_heads", "kv_heads", "gdn_heads", "ffn_blocks", "vocab_rows"]
+    return {k: (int(out[2 * i]), int(out[2 * i + 1])) for i, k in enumerate(keys)}
+
+
 def _declare_model(L):
     import ctypes as c
     vp, i32, sz, u32 = c.c_void_p, c.c_int, c.c_size_t, c.c_uint32
@@ -188,14 +220,7 @@ class Qwen35Model:
         L = pb.load()
         _declare_model(L)
         self.L, self.ex, self.cfg = L, executor, cfg
-        cc = _CConfig()
-        for f, _ in _CConfig._fields_:
-            if f == "rope_sections":
-                cc.rope_sections = (c.c_uint32 * 4)(*cfg.rope_sections)
-            elif f == "kv_policy":
-                cc.kv_policy = kv_policy
-            else:
-                setattr(cc, f, getattr(cfg, f))
+        cc = c_config(cfg, kv_policy)
         self._cc = cc
         h = c.c_void_p()
         executor._check(L.prism_b200_model_create(executor.h, c.byref(cc), c.byref(h)))
@@ -329,6 +354,9 @@ def _declare_batch(L):
         ("prism_b200_batch_stream", vp, [vp]),
         ("prism_b200_batch_fill_context", i32, [vp, u32, u64]),
         ("prism_b200_batch_read_state", c.c_int64, [vp, u32, u32, u32, vp, sz]),
+        ("prism_b200_batch_create_tp", i32, [vp, u32, u32, u32, u32, c.POINTER(vp)]),
+        ("prism_b200_batch_exchange_handle", i32, [vp, vp]),
+        ("prism_b200_batch_connect", i32, [vp, vp]),
     ]:
         fn = getattr(L, name)
         fn.restype = res
@@ -336,18 +364,39 @@ def _declare_batch(L):
     L._batch_declared = True
 
 
+EXCHANGE_HANDLE_BYTES = 64
+
+
 class Qwen35Batch:
     """Batched serving over a loaded Qwen35Model's weights: `sequences`
-    sequences of up to `context` positions, one token each per step."""
+    sequences of up to `context` positions, one token each per step.
 
-    def __init__(self, model, sequences, context):
+    With tp_size > 1 this is rank `tp_rank` of a tensor-parallel batch (one
+    process and GPU per rank, all stepping the same tokens): gather every
+    rank's `exchange_handle()` in rank order and pass the list to
+    `connect()` before the first step."""
+
+    def __init__(self, model, sequences, context, tp_rank=0, tp_size=1):
         import ctypes as c
         self.model, self.B, self.context = model, sequences, context
+        self.tp_rank, self.tp_size = tp_rank, tp_size
         self.L = model.L
         _declare_batch(self.L)
         h = c.c_void_p()
-        model.ex._check(self.L.prism_b200_batch_create(model.h, sequences, context, c.byref(h)))
+        model.ex._check(self.L.prism_b200_batch_create_tp(model.h, sequences, context, tp_rank,
+                                                          tp_size, c.byref(h)))
         self.h = h
+
+    def exchange_handle(self):
+        buf = np.zeros(EXCHANGE_HANDLE_BYTES, np.uint8)
+        self.model.ex._check(self.L.prism_b200_batch_exchange_handle(self.h, buf.ctypes.data))
+        return buf.tobytes()
+
+    def connect(self, handles):
+        assert len(handles) == self.tp_size
+        buf = np.frombuffer(b"".join(handles), np.uint8).copy()
+        assert buf.size == EXCHANGE_HANDLE_BYTES * self.tp_size
+        self.model.ex._check(self.L.prism_b200_batch_connect(self.h, buf.ctypes.data))
 
     def step(self, tokens):
         tokens = np.ascontiguousarray(tokens, dtype=np.uint32)

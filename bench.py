@@ -658,24 +658,32 @@ SERVE_B, SERVE_CTX = 256, 8192
 SERVE_METRIC = "batched decode tok/s (256 sequences x 8192-token context, Q8_0 KV)"
 
 
-def serve_step_bytes(cfg, B, position):
-    """Algorithmic bytes of one batched step at `position` (every sequence):
-    weights once, each sequence's Q8_0 K and V rows of the attention layers
-    up to and including the new one, the GDN state read and written, the
-    convolution history read and written."""
+def serve_step_bytes(cfg, B, position, tp=1):
+    """Algorithmic bytes one GPU moves in a batched step at `position` (every
+    sequence): weights once, each sequence's Q8_0 K and V rows of the
+    attention layers up to and including the new one, the GDN state read and
+    written, the convolution history read and written.  Under `tp`-way
+    tensor parallelism a rank holds 1/tp of the weights, GDN heads and
+    channels, and max(kv_heads/tp, 1) KV heads (two ranks share a KV head
+    when tp exceeds the KV heads)."""
     attn = sum(1 for l in range(cfg.layers) if cfg.is_full(l))
     gdn = cfg.layers - attn
     rec = cfg.head_dim // 32 * 2 + cfg.head_dim
-    kv = attn * 2 * cfg.kv_heads * rec * (position + 1) * B
-    state = gdn * 2 * cfg.ssm_values * cfg.ssm_state * cfg.ssm_state * 4 * B
-    conv = gdn * 2 * cfg.conv_channels * (cfg.conv_kernel - 1) * 4 * B
-    return cfg.linear_bytes() + kv + state + conv
+    kv_local = max(cfg.kv_heads // tp, 1)
+    kv = attn * 2 * kv_local * rec * (position + 1) * B
+    state = gdn * 2 * cfg.ssm_values * cfg.ssm_state * cfg.ssm_state * 4 * B // tp
+    conv = gdn * 2 * cfg.conv_channels * (cfg.conv_kernel - 1) * 4 * B // tp
+    return cfg.linear_bytes() // tp + kv + state + conv
 
 
 def run_serve(args):
     """batched serving of 256 sequences with 8192-token random
-    contexts (Q8_0 KV), greedy decode steps.  Sequences are independent, so
-    N ranks serve N disjoint batches of 256 (weak scaling, no exchange)."""
+    contexts (Q8_0 KV), greedy decode steps.  On N ranks, `--parallel tp`
+    (the default, as configs[4] specifies) splits every linear layer, the
+    heads and the KV cache of the same 256 sequences over the ranks and
+    all-reduces the row-parallel projections over NVLink peer memory (strong
+    scaling); `--parallel dp` serves N disjoint batches of 256 instead (weak
+    scaling, no exchange)."""
     import torch
     import prism_b200 as pb
     import qwen35
@@ -693,10 +701,21 @@ def run_serve(args):
     model = qwen35.Qwen35Model(ex, cfg, kv_policy=qwen35.KV_Q8_0)
     model.load(weights)
     SB = args.sequences
-    bt = qwen35.Qwen35Batch(model, SB, SERVE_CTX)
+    tp = world if args.parallel == "tp" else 1
+    tp_mode = qwen35.TP_ALLREDUCE if args.tp_mode == "allreduce" else qwen35.TP_EXACT
+    bt = qwen35.Qwen35Batch(model, SB, SERVE_CTX, tp_rank=rank if tp > 1 else 0, tp_size=tp,
+                            tp_mode=tp_mode)
+    if tp > 1:
+        handles = [None] * world
+        torch.distributed.all_gather_object(handles, bt.exchange_handle())
+        bt.connect(handles)
     start = SERVE_CTX - (K + W + 4)
-    bt.fill_context(start, seed=1 + rank)
-    toks = np.random.default_rng(2 + rank).integers(0, cfg.vocab, SB).astype(np.uint32)
+    # tensor-parallel ranks serve the same sequences: same seeds everywhere
+    seq_seed = 0 if tp > 1 else rank
+    bt.fill_context(start, seed=1 + seq_seed)
+    toks = np.random.default_rng(2 + seq_seed).integers(0, cfg.vocab, SB).astype(np.uint32)
+    if world > 1:
+        torch.distributed.barrier()
     bt.step(toks)  # captures the step graph
     stream = torch.cuda.ExternalStream(bt.stream, device=dev)
     bt.decode_async(W)
@@ -713,9 +732,10 @@ def run_serve(args):
         torch.cuda.synchronize()
     ex.sync()
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
-    tps = world * SB * K / (ms / 1e3)
+    served = SB * (world // tp)   # sequences advanced per step by the whole job
+    tps = served * K / (ms / 1e3)
     mid = start + 1 + W + K // 2
-    step_bytes = serve_step_bytes(cfg, SB, mid)
+    step_bytes = serve_step_bytes(cfg, SB, mid, tp)
     peak, peak_src = peaks()
     achieved = step_bytes / (ms / K / 1e3) / 1e9
     # end to end: host tokens in, greedy tokens out, per step
@@ -725,29 +745,49 @@ def run_serve(args):
     for _ in range(E):
         toks = bt.step(toks)
     e2e_s = (time.perf_counter() - t0) / E
+    if world > 1:
+        torch.distributed.barrier()
     e2e = max_over_ranks(e2e_s, world, dev)
     bt.close()
     model.close()
     ex.close()
     line = {
         "metric": SERVE_METRIC, "value": tps, "unit": "tok/s", "n_gpus": world, "steps": K,
-        "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+        "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+        "scaling": "strong" if tp > 1 else "weak",
         "vs_baseline": None, "dtype": "i8xternary->i32,f32; Q8_0 KV",
         "data": "synthetic (random-init weights, seeded random KV/recurrent context)",
-        "config": {"workload": "configs[4]: %d sequences per GPU, 8192-token context filled "
+        "config": {"workload": "configs[4]: %d sequences%s, 8192-token context filled "
                                "with seeded random Q8_0 KV rows and GDN/conv state, greedy decode "
-                               "from position %d; configs[1] geometry" % (SB, start),
-                   "sequences_per_gpu": SB, "context": SERVE_CTX,
-                   "parallelism": "sequences sharded over ranks (dp%d), no exchange" % world,
+                               "from position %d; configs[1] geometry"
+                               % (SB, " per GPU" if tp == 1 else "", start),
+                   "sequences": served, "context": SERVE_CTX,
+                   "parallelism": (("tp%d exact: column-sharded linears, heads and KV; per "
+                                    "layer 2 all-gathers of quantized head/FFN outputs "
+                                    "(fused into the quantizer) and 2 of hidden rows (fused "
+                                    "into the GEMM epilogue) over NVLink peer memory; "
+                                    "vocabulary-split output head" % tp)
+                                   if args.tp_mode == "exact" else
+                                   ("tp%d all-reduce: column/row-sharded linears, heads and "
+                                    "KV; 2 all-reduces per layer over NVLink peer memory fused "
+                                    "into the GEMM epilogue + next RMSNorm; vocabulary-split "
+                                    "output head" % tp)) if tp > 1 else
+                                  "sequences sharded over ranks (dp%d), no exchange" % world,
                    "l2": "each step reads %.1f GB (> 126 MB L2)" % (step_bytes / 1e9)},
         "clocks": clk.summary(),
-        "gpu_launches": K * (3 + 12 * cfg.layers),
-        "e2e": {"value": world * SB / e2e, "unit": "tok/s", "h2d_bytes_per_step": SB * 4,
+        # embed; per attention layer 15 and per GDN layer 16 kernels (norm,
+        # quantize, projections, attention or GDN, quantize, out-projection,
+        # norm, quantize, up, gate, SwiGLU, quantize, down); norm, quantize,
+        # output head, finish
+        "gpu_launches": K * (1 + sum(15 if cfg.is_full(l) else 16 for l in range(cfg.layers))
+                             + 4),
+        "e2e": {"value": served / e2e, "unit": "tok/s", "h2d_bytes_per_step": SB * 4,
                 "d2h_bytes_per_step": SB * 4,
                 "api": "prism_b200_batch_step per step (host tokens in, greedy tokens out)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_src,
-                     "kernel": "whole batched step (KV + GDN state + weights bytes / step time)",
+                     "kernel": "whole batched step, per GPU (this rank's KV + GDN state + "
+                               "weight bytes / step time)",
                      "algorithmic_bytes_per_step": step_bytes, "traffic": None},
     }
     if rank == 0 and not args.no_cpu:
@@ -815,6 +855,11 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-matvec", action="store_true", help="skip the configs[0] sub-benchmark")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens (profiling runs)")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
+                    help="serve workload on N GPUs: tensor-parallel (default) or sequence-sharded")
+    ap.add_argument("--tp-mode", default="exact", choices=["exact", "allreduce"],
+                    help="serve workload, tensor-parallel: gathered (bit-exact) or all-reduced "
+                         "row-parallel projections")
     ap.add_argument("--sequences", type=int, default=SERVE_B,
                     help="serve workload: sequences per GPU (profiling runs use fewer)")
     args = ap.parse_args()

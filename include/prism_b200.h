@@ -386,31 +386,41 @@ int64_t prism_b200_batch_read_state(prism_b200_batch *b, uint32_t seq, uint32_t 
  * in the reference, which serves on host cores.  Rank `tp_rank` keeps a
  * column slice of every projection feeding a per-head or per-row operation
  * (attention query heads and their KV heads, Gated DeltaNet heads, 256-row
- * blocks of the FFN intermediate) and the matching row slice of attn_output,
- * ssm_out and ffn_down, whose partial sums are all-reduced over NVLink peer
- * memory (fused into the GEMM epilogue and the next RMSNorm, summed in rank
- * order so every rank holds identical hidden states); the output head is
- * split by vocabulary rows.  All ranks pass the same tokens.  Outputs agree
- * with the one-GPU batch within float rounding of the cross-rank sums
- * (relative 1e-4 on hidden states), not bit for bit.
- * Connect before the first step: every rank publishes its exchange handle
- * (prism_b200_batch_exchange_handle), the host gathers them in rank order
- * (tp_size * PRISM_B200_EXCHANGE_HANDLE_BYTES) and every rank passes the
- * gathered array to prism_b200_batch_connect.  The ranks' steps wait on one
- * another (bounded: PRISM_B200_E_TIMEOUT when a rank stops stepping).
- * tp_size 1 is prism_b200_batch_create. */
+ * blocks of the FFN intermediate) and the output head's vocabulary rows.
+ * attn_output, ssm_out and ffn_down, per `tp_mode`:
+ *  - PRISM_B200_TP_EXACT: column-split as well.  Each rank's quantized head
+ *    (FFN) outputs are gathered into every rank over NVLink peer memory,
+ *    and each rank's slice of hidden rows is stored into every rank's
+ *    hidden state (both fused into the producing kernels).  Bit-identical
+ *    to the one-GPU batch and the oracle.
+ *  - PRISM_B200_TP_ALLREDUCE: row-split (input blocks); the partial sums are
+ *    all-reduced over peer memory (fused into the GEMM epilogue and the next
+ *    RMSNorm, summed in rank order: every rank holds identical hidden
+ *    states).  The cross-rank sums round differently from the reference's
+ *    per-row chain, so outputs match the one-GPU batch to float rounding
+ *    only, amplified by the Q8_K quantizers downstream.
+ * All ranks pass the same tokens.  Connect before the first step: every
+ * rank publishes its exchange handle (prism_b200_batch_exchange_handle), the
+ * host gathers them in rank order (tp_size * PRISM_B200_EXCHANGE_HANDLE_BYTES)
+ * and every rank passes the gathered array to prism_b200_batch_connect.  The
+ * ranks' steps wait on one another (bounded: PRISM_B200_E_TIMEOUT when a
+ * rank stops stepping).  tp_size 1 is prism_b200_batch_create. */
 #define PRISM_B200_EXCHANGE_HANDLE_BYTES 64
+#define PRISM_B200_TP_EXACT 0u
+#define PRISM_B200_TP_ALLREDUCE 1u
+int prism_b200_batch_create_tp(prism_b200_model *m, uint32_t sequences, uint32_t context,
+                               uint32_t tp_rank, uint32_t tp_size, uint32_t tp_mode,
+                               prism_b200_batch **out);
+int prism_b200_batch_exchange_handle(const prism_b200_batch *b, void *handle);
+int prism_b200_batch_connect(prism_b200_batch *b, const void *handles);
 /* The slice rank `tp_rank` of `tp_size` owns (host only, no device):
- * out[0..10) = [first, end) of the query heads, the KV heads they read, the
- * Gated DeltaNet heads, the FFN intermediate's 256-row blocks and the
- * output head's vocabulary rows.  PRISM_B200_E_UNSUPPORTED when the
+ * out[0..12) = [first, end) of the query heads, the KV heads they read, the
+ * Gated DeltaNet heads, the FFN intermediate's 256-row blocks, the output
+ * head's vocabulary rows and the hidden rows of attn_output / ssm_out /
+ * ffn_down in the exact form.  PRISM_B200_E_UNSUPPORTED when the
  * geometry does not split `tp_size` ways. */
 int prism_b200_tp_plan(const prism_b200_qwen35_config *cfg, uint32_t tp_rank, uint32_t tp_size,
                        int32_t *out);
-int prism_b200_batch_create_tp(prism_b200_model *m, uint32_t sequences, uint32_t context,
-                               uint32_t tp_rank, uint32_t tp_size, prism_b200_batch **out);
-int prism_b200_batch_exchange_handle(const prism_b200_batch *b, void *handle);
-int prism_b200_batch_connect(prism_b200_batch *b, const void *handles);
 
 /* ---- synthetic inputs ----------------------------------------------- */
 /* Fill `out` (host, rows*cols/256 blocks in the reference byte layout) with

@@ -210,24 +210,42 @@ inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
     if (e != cudaSuccess) return e;
   }
   const bool tpx = b->tp.size > 1;
-  // a row-parallel projection's partial waits in an exchange slot until the
-  // next normalisation sums it (tensor parallelism only)
+  const bool exact = tpx && b->x.mode == kTpExact;
+  const int ranks = b->tp.size;
+  const int hd = (int)c.head_dim;
+  const unsigned long long MH = (unsigned long long)B * H;
+  // Exchanges of this step (tensor parallelism): values delivered to each
+  // counter per step and so far in this step.  A projection that leaves the
+  // heads or the FFN marks its exchange pending; the next normalisation
+  // waits for it (and, all-reduce, sums the partials).
+  unsigned long long gather_step = 0, gather_done = 0, hidden_done = 0;
+  for (size_t l = 0; l < m->L.size(); ++l)
+    gather_step += (unsigned long long)B *
+                   ((m->L[l].full ? c.heads * c.head_dim : (uint32_t)m->value_width()) / 256 +
+                    c.ffn / 256);
   int pending = -1, pending_index = 0;
-  const unsigned long long gemm_ctas =
-      (unsigned long long)((H + kGemmN - 1) / kGemmN) * ((B + kGemmM - 1) / kGemmM);
   auto norm = [&](const float *w) {
     if (pending < 0) {
       cudaLaunchConfig_t cfg = pdl_config(dim3(B), dim3(256), 0, s, attr, pdl);
       return cudaLaunchKernelEx(&cfg, rmsnorm_rows_kernel, (const float *)b->hidden, w, H, c.eps,
                                 b->xn, status);
     }
-    TpWait tw{TpExchange::count(b->x.base, pending), b->x.xstep, (unsigned long long)c.layers,
-              (unsigned long long)pending_index, (unsigned long long)b->tp.size * gemm_ctas};
-    const float *slot = b->x.slot(b->x.base, pending);
+    TpWait tw;
+    const float *slot = nullptr;
+    int nr = 0;
+    if (exact) {
+      tw = TpWait{TpExchange::count(b->x.base, 0), b->x.xstep, 2ull * c.layers * MH, hidden_done};
+    } else {
+      tw = TpWait{TpExchange::count(b->x.base, pending), b->x.xstep,
+                  (unsigned long long)c.layers * ranks * MH,
+                  (unsigned long long)(pending_index + 1) * ranks * MH};
+      slot = b->x.slot(b->x.base, pending);
+      nr = ranks;
+    }
     pending = -1;
     cudaLaunchConfig_t cfg = pdl_config(dim3(B), dim3(256), 0, s, attr, pdl);
-    return cudaLaunchKernelEx(&cfg, tp_reduce_norm_kernel, slot, b->tp.size, B, H, tw, b->hidden,
-                              w, c.eps, b->xn, status);
+    return cudaLaunchKernelEx(&cfg, tp_reduce_norm_kernel, slot, nr, B, H, tw, b->hidden, w,
+                              c.eps, b->xn, status);
   };
   auto quant = [&](const float *x, int nb) {
     return launch_token_quantize(x, B, nb, 0, token_q8k_carve(b->tok, B, nb), status, s, pdl);
@@ -237,14 +255,47 @@ inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
     return launch_token_matmul(w, B, token_q8k_carve(b->tok, B, w.nb), y, residual, keys,
                                status, s, pdl, nullptr, row_base);
   };
-  // y = hidden + x W^T over all ranks (row-parallel when sharded)
-  auto mm_residual = [&](const DeviceWeight &w, int slot, int index) {
-    if (!tpx) return mm(w, b->hidden, b->hidden, nullptr);
-    const GemmPush push = b->x.push(b->tp.rank, slot);
-    pending = slot;
-    pending_index = index;
-    return launch_token_matmul(w, B, token_q8k_carve(b->tok, B, w.nb), nullptr, nullptr, nullptr,
-                               status, s, pdl, &push, 0);
+  // hidden += Q8_K(x) W^T for the projections leaving the heads / the FFN.
+  // x is this rank's [B][nbl * 256] part, blocks b0.. of the full nbt.
+  auto project_out = [&](const DeviceWeight &w, const float *x, int nbl, int b0, int nbt,
+                         int slot, int index) -> cudaError_t {
+    cudaError_t e2;
+    if (!tpx) {
+      if ((e2 = quant(x, nbl)) != cudaSuccess) return e2;
+      return mm(w, b->hidden, b->hidden, nullptr);
+    }
+    if (!exact) {
+      // row-parallel partial into every rank's slot
+      if ((e2 = quant(x, nbl)) != cudaSuccess) return e2;
+      const GemmPush push = b->x.push_partial(b->tp.rank, slot);
+      pending = slot;
+      pending_index = index;
+      return launch_token_matmul(w, B, token_q8k_carve(b->tok, B, w.nb), nullptr, nullptr,
+                                 nullptr, status, s, pdl, &push, 0);
+    }
+    // exact: gather every rank's quantized blocks, then this rank's hidden
+    // rows (with the residual) into every rank's hidden state
+    TpGather gq{};
+    gq.ranks = ranks;
+    for (int p = 0; p < ranks; ++p) {
+      gq.dst[p] = token_q8k_carve(b->x.tok(b->x.peer[p]), B, nbt);
+      gq.count[p] = TpExchange::count(b->x.peer[p], 3);
+    }
+    {
+      const long warps = (long)B * nbl;
+      cudaLaunchConfig_t cfg =
+          pdl_config(dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, s, attr, pdl);
+      if ((e2 = cudaLaunchKernelEx(&cfg, q8k_gather_kernel, x, B, nbl, b0, nbt, gq, status)) !=
+          cudaSuccess)
+        return e2;
+    }
+    gather_done += (unsigned long long)B * nbt;
+    const TpWait gate{TpExchange::count(b->x.base, 3), b->x.xstep, gather_step, gather_done};
+    const GemmPush push = b->x.push_rows(b->tp.hr0);
+    hidden_done += MH;
+    pending = 0;
+    return launch_token_matmul(w, B, token_q8k_carve(b->x.tok(b->x.base), B, nbt), nullptr,
+                               b->hidden, nullptr, status, s, pdl, &push, 0, &gate);
   };
 #define BK(x)                            \
   if ((e = (x)) != cudaSuccess) return e
@@ -305,8 +356,8 @@ inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
         cfg.numAttrs += 1;
         BK(cudaLaunchKernelEx(&cfg, attention_decode_kernel, aa));
       }
-      BK(quant(b->attended, (int)(b->heads * c.head_dim / 256)));
-      BK(mm_residual(Sh.o, 0, (int)l));
+      BK(project_out(Sh.o, b->attended, b->heads * hd / 256, b->tp.qh0 * hd / 256,
+                     (int)(c.heads * c.head_dim / 256), 0, (int)l));
     } else {
       BK(mm(Sh.qkv, b->mixed, nullptr, nullptr));
       BK(mm(Sh.z, b->zgate, nullptr, nullptr));
@@ -341,8 +392,8 @@ inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
       cudaLaunchConfig_t cfg =
           pdl_config(dim3(b->gdn_heads, B), dim3(kGdnThreads), 0, s, attr, pdl);
       BK(cudaLaunchKernelEx(&cfg, gdn_decode_kernel, g));
-      BK(quant(b->attended, b->gdn_width() / 256));
-      BK(mm_residual(Sh.out, 0, (int)l));
+      BK(project_out(Sh.out, b->attended, b->gdn_width() / 256,
+                     b->tp.gh0 * (int)c.ssm_state / 256, m->value_width() / 256, 0, (int)l));
     }
     BK(norm(Ly.post_norm));
     BK(quant(b->xn, hnb));
@@ -355,8 +406,7 @@ inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
                      attr, pdl);
       BK(cudaLaunchKernelEx(&cfg, swiglu_kernel, b->up, (const float *)b->gate, n, status));
     }
-    BK(quant(b->up, b->ffn / 256));
-    BK(mm_residual(Sh.down, 1, (int)l));
+    BK(project_out(Sh.down, b->up, b->ffn / 256, b->tp.fb0, (int)(c.ffn / 256), 1, (int)l));
   }
   if (greedy) {
     BK(norm(m->out_norm));
@@ -372,8 +422,9 @@ inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
       kp.dst[p] = b->x.keys(b->x.peer[p]) + (size_t)b->tp.rank * B;
       kp.count[p] = TpExchange::count(b->x.peer[p], 2);
     }
-    TpWait kw{TpExchange::count(b->x.base, 2), b->x.xstep, 1ull, 0ull,
-              (unsigned long long)b->tp.size};
+    // every rank adds 1 per step
+    const TpWait kw{TpExchange::count(b->x.base, 2), b->x.xstep, (unsigned long long)ranks,
+                    (unsigned long long)ranks};
     BK(cudaLaunchKernelEx(&cfg, tp_finish_kernel, b->d_keys, kp,
                           (const unsigned long long *)b->x.keys(b->x.base), b->tp.size, kw,
                           b->d_tokens, b->d_pos, B, b->d_step, b->x.xstep, greedy ? 1 : 0,
@@ -392,11 +443,12 @@ extern "C" {
 
 int prism_b200_batch_create(prism_b200_model *m, uint32_t sequences, uint32_t context,
                             prism_b200_batch **out) {
-  return prism_b200_batch_create_tp(m, sequences, context, 0, 1, out);
+  return prism_b200_batch_create_tp(m, sequences, context, 0, 1, PRISM_B200_TP_EXACT, out);
 }
 
 int prism_b200_batch_create_tp(prism_b200_model *m, uint32_t sequences, uint32_t context,
-                               uint32_t tp_rank, uint32_t tp_size, prism_b200_batch **out) {
+                               uint32_t tp_rank, uint32_t tp_size, uint32_t tp_mode,
+                               prism_b200_batch **out) {
   using namespace prism;
   if (!m || !out) return PRISM_B200_E_INVALID;
   *out = nullptr;
@@ -411,6 +463,9 @@ int prism_b200_batch_create_tp(prism_b200_model *m, uint32_t sequences, uint32_t
   if ((context + kAttnSplit - 1) / kAttnSplit + 1 > 16384)
     return ex->fail(PRISM_B200_E_UNSUPPORTED, "context %u exceeds the attention kernel", context);
   const auto &c = m->cfg;
+  if (tp_mode != PRISM_B200_TP_EXACT && tp_mode != PRISM_B200_TP_ALLREDUCE)
+    return ex->fail(PRISM_B200_E_INVALID, "tensor-parallel mode %u", tp_mode);
+  const bool allreduce = tp_mode == PRISM_B200_TP_ALLREDUCE;
   TpPlan plan;
   if (const char *why = tp_plan(c, (int)tp_rank, (int)tp_size, plan))
     return ex->fail(tp_size < 1 || tp_size > (uint32_t)kMaxTp || tp_rank >= tp_size
@@ -464,8 +519,11 @@ int prism_b200_batch_create_tp(prism_b200_model *m, uint32_t sequences, uint32_t
       gather(Ly.q, tp_rows({{plan.qh0 * 2 * hd, plan.qh1 * 2 * hd}}), 0, Ly.q.nb, Sh.q);
       gather(Ly.k, tp_rows({{plan.kv0 * hd, plan.kv1 * hd}}), 0, Ly.k.nb, Sh.k);
       gather(Ly.v, tp_rows({{plan.kv0 * hd, plan.kv1 * hd}}), 0, Ly.v.nb, Sh.v);
-      gather(Ly.o, tp_rows({{0, (int)c.hidden}}), plan.qh0 * hd / 256,
-             (plan.qh1 - plan.qh0) * hd / 256, Sh.o);
+      if (allreduce)  // input blocks of this rank's heads
+        gather(Ly.o, tp_rows({{0, (int)c.hidden}}), plan.qh0 * hd / 256,
+               (plan.qh1 - plan.qh0) * hd / 256, Sh.o);
+      else  // this rank's hidden rows over every input block
+        gather(Ly.o, tp_rows({{plan.hr0, plan.hr1}}), 0, Ly.o.nb, Sh.o);
     } else {
       const int kw = (int)c.ssm_groups * S, g0 = plan.gh0 * S, g1 = plan.gh1 * S;
       gather(Ly.qkv, tp_rows({{g0, g1}, {kw + g0, kw + g1}, {2 * kw + g0, 2 * kw + g1}}), 0,
@@ -473,7 +531,10 @@ int prism_b200_batch_create_tp(prism_b200_model *m, uint32_t sequences, uint32_t
       gather(Ly.z, tp_rows({{g0, g1}}), 0, Ly.z.nb, Sh.z);
       gather(Ly.beta, tp_rows({{plan.gh0, plan.gh1}}), 0, Ly.beta.nb, Sh.beta);
       gather(Ly.alpha, tp_rows({{plan.gh0, plan.gh1}}), 0, Ly.alpha.nb, Sh.alpha);
-      gather(Ly.out, tp_rows({{0, (int)c.hidden}}), g0 / 256, (g1 - g0) / 256, Sh.out);
+      if (allreduce)
+        gather(Ly.out, tp_rows({{0, (int)c.hidden}}), g0 / 256, (g1 - g0) / 256, Sh.out);
+      else
+        gather(Ly.out, tp_rows({{plan.hr0, plan.hr1}}), 0, Ly.out.nb, Sh.out);
       // convolution weights of this rank's q, k and v channels
       float *cw = nullptr;
       if (e == cudaSuccess) e = batch_alloc(b, &cw, (size_t)3 * (g1 - g0) * c.conv_kernel);
@@ -487,7 +548,10 @@ int prism_b200_batch_create_tp(prism_b200_model *m, uint32_t sequences, uint32_t
     }
     gather(Ly.up, tp_rows({{plan.fb0 * 256, plan.fb1 * 256}}), 0, Ly.up.nb, Sh.up);
     gather(Ly.gate, tp_rows({{plan.fb0 * 256, plan.fb1 * 256}}), 0, Ly.gate.nb, Sh.gate);
-    gather(Ly.down, tp_rows({{0, (int)c.hidden}}), plan.fb0, plan.fb1 - plan.fb0, Sh.down);
+    if (allreduce)
+      gather(Ly.down, tp_rows({{0, (int)c.hidden}}), plan.fb0, plan.fb1 - plan.fb0, Sh.down);
+    else
+      gather(Ly.down, tp_rows({{plan.hr0, plan.hr1}}), 0, Ly.down.nb, Sh.down);
   }
   if (!tpx) {
     b->lm = m->embd;
@@ -497,7 +561,7 @@ int prism_b200_batch_create_tp(prism_b200_model *m, uint32_t sequences, uint32_t
   }
 #define A(p, n) \
   if (e == cudaSuccess) e = batch_alloc(b, &(p), (n))
-  A(b->hidden, B * c.hidden);
+  if (!tpx || allreduce) A(b->hidden, B * c.hidden);  // exact: in the exchange buffer
   A(b->xn, B * c.hidden);
   A(b->mixed, B * b->gdn_channels());
   A(b->zgate, B * b->gdn_width());
@@ -527,9 +591,12 @@ int prism_b200_batch_create_tp(prism_b200_model *m, uint32_t sequences, uint32_t
     }
   }
   if (tpx) {
-    b->x.layout(plan.size, (int)B, (int)c.hidden);
+    const int tok_nb = (int)std::max<uint32_t>(std::max<uint32_t>(c.ffn, c.heads * c.head_dim),
+                                                (uint32_t)m->value_width()) / 256;
+    b->x.layout(allreduce ? kTpAllReduce : kTpExact, plan.size, (int)B, (int)c.hidden, tok_nb);
     A(b->x.base, b->x.bytes);
     A(b->x.xstep, 1);
+    if (e == cudaSuccess && !allreduce) b->hidden = b->x.hidden(b->x.base);
   }
 #undef A
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -548,7 +615,8 @@ int prism_b200_tp_plan(const prism_b200_qwen35_config *cfg, uint32_t tp_rank, ui
   if (tp_size < 1 || tp_size > (uint32_t)kMaxTp || tp_rank >= tp_size) return PRISM_B200_E_INVALID;
   TpPlan p;
   if (tp_plan(*cfg, (int)tp_rank, (int)tp_size, p)) return PRISM_B200_E_UNSUPPORTED;
-  const int32_t v[10] = {p.qh0, p.qh1, p.kv0, p.kv1, p.gh0, p.gh1, p.fb0, p.fb1, p.v0, p.v1};
+  const int32_t v[12] = {p.qh0, p.qh1, p.kv0, p.kv1, p.gh0, p.gh1,
+                         p.fb0, p.fb1, p.v0,  p.v1,  p.hr0, p.hr1};
   memcpy(out, v, sizeof(v));
   return PRISM_B200_OK;
 }

@@ -55,28 +55,12 @@ __host__ __device__ inline size_t token_tile(int m, int nb, int b) {
   return (size_t)(m / 128) * nb + b;
 }
 
-// one warp per (token, block); reference q8k_with_input (src/kernels.rs:463-522)
-__global__ void __launch_bounds__(256) q8k_tokens_kernel(const float *__restrict__ x, int M,
-                                                         int nb, int pinned, TokenQ8K out,
-                                                         unsigned *status) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  grid_dependency_wait();
-  grid_dependents_launch();
-  if (warp >= M * nb) return;
-  const int m = warp / nb, b = warp % nb;
-  const float *src = x + (size_t)m * nb * 256 + b * 256 + lane * 8;
-  const float4 a = reinterpret_cast<const float4 *>(src)[0];
-  const float4 c = reinterpret_cast<const float4 *>(src)[1];
-  const float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-  float scale;
-  int8_t q[8];
-  int pair;
-  const unsigned st = q8k_quantize_regs(v, lane, pinned != 0, scale, q, pair);
-  if (st && lane == 0) report(status, st);
-  uint32_t w0 = (uint32_t)(uint8_t)q[0] | ((uint32_t)(uint8_t)q[1] << 8) |
-                ((uint32_t)(uint8_t)q[2] << 16) | ((uint32_t)(uint8_t)q[3] << 24);
-  uint32_t w1 = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) |
-                ((uint32_t)(uint8_t)q[6] << 16) | ((uint32_t)(uint8_t)q[7] << 24);
+// Store one quantized (token, block) unit: the lane holds codes
+// 8*lane..8*lane+7 (w0, w1), the pair sum of its 16-group half and, on lane
+// 0, the block scale.
+__device__ __forceinline__ void store_token_unit(const TokenQ8K &out, int nb, int m, int b,
+                                                 int lane, uint32_t w0, uint32_t w1, int pair,
+                                                 float scale) {
   // lane holds codes 8*lane..8*lane+7: chunk kc = lane/2, half lane%2
   const size_t tile = token_tile(m, nb, b);
   const int row = m & 127;
@@ -89,6 +73,41 @@ __global__ void __launch_bounds__(256) q8k_tokens_kernel(const float *__restrict
     sp[2048 + (lane >> 1)] = (int8_t)(pair >> 4);
   }
   if (lane == 0) out.scale[(size_t)m * nb + b] = scale;
+}
+
+// Quantize one (token, block) of x (row stride nb * 256 floats); returns
+// the packed codes in w0/w1 plus the pair sum and scale.
+__device__ __forceinline__ void quantize_token_unit(const float *__restrict__ x, int nb, int m,
+                                                    int b, int lane, int pinned, uint32_t &w0,
+                                                    uint32_t &w1, int &pair, float &scale,
+                                                    unsigned *status) {
+  const float *src = x + (size_t)m * nb * 256 + b * 256 + lane * 8;
+  const float4 a = reinterpret_cast<const float4 *>(src)[0];
+  const float4 c = reinterpret_cast<const float4 *>(src)[1];
+  const float v[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+  int8_t q[8];
+  const unsigned st = q8k_quantize_regs(v, lane, pinned != 0, scale, q, pair);
+  if (st && lane == 0) report(status, st);
+  w0 = (uint32_t)(uint8_t)q[0] | ((uint32_t)(uint8_t)q[1] << 8) |
+       ((uint32_t)(uint8_t)q[2] << 16) | ((uint32_t)(uint8_t)q[3] << 24);
+  w1 = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) |
+       ((uint32_t)(uint8_t)q[6] << 16) | ((uint32_t)(uint8_t)q[7] << 24);
+}
+
+// one warp per (token, block); reference q8k_with_input (src/kernels.rs:463-522)
+__global__ void __launch_bounds__(256) q8k_tokens_kernel(const float *__restrict__ x, int M,
+                                                         int nb, int pinned, TokenQ8K out,
+                                                         unsigned *status) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  grid_dependency_wait();
+  grid_dependents_launch();
+  if (warp >= M * nb) return;
+  const int m = warp / nb, b = warp % nb;
+  uint32_t w0, w1;
+  int pair;
+  float scale;
+  quantize_token_unit(x, nb, m, b, lane, pinned, w0, w1, pair, scale, status);
+  store_token_unit(out, nb, m, b, lane, w0, w1, pair, scale);
 }
 
 // ---- tcgen05 helpers (PTX ISA: tensor memory, matrix and instruction
@@ -180,16 +199,62 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
-// Tensor-parallel exchange of a row-parallel partial product: instead of
-// storing Y, every CTA stores its tile into each rank's receive slot for
-// this rank (peer memory mapped over NVLink, this rank's own slot included),
-// then adds 1 to each rank's arrival counter for the slot, after a
-// system-scope fence.  The receiving rank sums the slots in rank order.
+// ---- tensor-parallel exchanges over peer memory ---------------------------
+// A producer stores its output straight into every rank's buffer (peer
+// memory mapped over NVLink, this rank's own included), then, after a
+// system-scope fence, adds the number of values it delivered to each rank's
+// arrival counter.  Counters only grow: a consumer waits until its counter
+// reaches steps_completed * per_step + offset, where per_step is what one
+// step delivers and offset what this step has delivered up to and including
+// the awaited exchange.
 constexpr int kMaxTp = 8;
+
+struct TpWait {
+  const unsigned long long *count;  // this rank's arrival counter (null: no wait)
+  const unsigned long long *xstep;  // steps completed on this rank
+  unsigned long long per_step, offset;
+};
+
+// Bounded wait (one thread); false when it expired, or when an earlier wait
+// of this executor already did (the step has failed: do not wait again).
+__device__ __forceinline__ bool tp_wait(const TpWait &w, unsigned *status) {
+  if (*reinterpret_cast<volatile unsigned *>(status) & kStatusTimeout) return false;
+  const unsigned long long target = *w.xstep * w.per_step + w.offset;
+  const unsigned long long t0 = global_timer_ns();
+  for (;;) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w.count) : "memory");
+    if (v >= target) break;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      report(status, kStatusTimeout);
+      return false;
+    }
+  }
+  __threadfence_system();
+  return true;
+}
+
+// Publish one CTA's deliveries: all of its stores are visible system-wide
+// before any counter moves.  Called by every thread of the CTA.
+__device__ __forceinline__ void tp_publish(unsigned long long *const *count, int ranks,
+                                           unsigned long long delivered) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < ranks; ++p) atomicAdd_system(count[p], delivered);
+  }
+}
+
+// The GEMM output sent to every rank: element (m, n) of the CTA's tile goes
+// to dst[p][m * ld + col + n] of each rank p -- a row-parallel partial into
+// rank p's receive slot for this rank, or (with the residual added) this
+// rank's rows of the hidden state into rank p's copy.
 struct GemmPush {
-  float *dst[kMaxTp];                 // rank p's slot [M][rows] for this rank's partial
-  unsigned long long *count[kMaxTp];  // rank p's arrival counter of the slot
+  float *dst[kMaxTp];
+  unsigned long long *count[kMaxTp];  // rank p's arrival counter
   int n;                              // ranks (0: no exchange, store Y)
+  int ld, col;
 };
 
 struct GemmArgs {
@@ -205,6 +270,7 @@ struct GemmArgs {
   int row_base;           // index of row 0 in the argmax key (a vocabulary slice's offset)
   unsigned *status;
   GemmPush push;
+  TpWait gate;            // activations gathered from every rank: wait for them first
 };
 
 // Warp roles of the 14-warp CTA.
@@ -295,12 +361,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem = *tmem_slot;
   grid_dependency_wait();
   grid_dependents_launch();
+  if (g.gate.count) {
+    // a gathered activation: every rank's blocks must have landed
+    if (tid == 0 && !tp_wait(g.gate, g.status)) *fail = 1;
+    __syncthreads();
+  }
 
   float acc[64];
 #pragma unroll
   for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
 
-  if (warp == 0) {
+  if (*fail) {
+    // the gathered activations never arrived: no role runs
+  } else if (warp == 0) {
     // ---- loads -------------------------------------------------------------
     if (lane == 0) {
       int copies = 0;
@@ -498,13 +571,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_dealloc(tmem, L::kTmemCols);
   }
   if (ok && g.push.n) {
-    // row-parallel partial: coalesced 512-byte rows into every rank's slot
+    // coalesced 512-byte rows into every rank's buffer
     for (int i = tid; i < kGemmM * kGemmN; i += kGemmThreads) {
       const int t = i / kGemmN, c = i % kGemmN;
       const int mm = m0 + t, n = n0 + c;
       if (mm < g.M && n < g.rows) {
-        const float v = otile[t * kPitch + c];
-        for (int p = 0; p < g.push.n; ++p) g.push.dst[p][(size_t)mm * g.rows + n] = v;
+        const size_t at = (size_t)mm * g.push.ld + g.push.col + n;
+        float v = otile[t * kPitch + c];
+        if (g.residual) {
+          v = __fadd_rn(g.residual[at], v);
+          if (!is_finite_f(v)) report(g.status, kStatusNonfinite);
+        }
+        for (int p = 0; p < g.push.n; ++p) g.push.dst[p][at] = v;
       }
     }
   } else if (ok) {
@@ -522,13 +600,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
   if (g.push.n) {
-    // publish: every writer's stores are visible system-wide before the
-    // counters move.  A failed CTA still counts, so that no rank waits out
-    // its limit; its own status word carries the failure.
-    __threadfence_system();
-    __syncthreads();
-    if (tid == 0)
-      for (int p = 0; p < g.push.n; ++p) atomicAdd_system(g.push.count[p], 1ull);
+    // a failed CTA still counts, so that no rank waits out its limit; its
+    // own status word carries the failure
+    const unsigned long long tm = (unsigned long long)min(kGemmM, g.M - m0);
+    const unsigned long long tn = (unsigned long long)min(kGemmN, g.rows - n0);
+    tp_publish(g.push.count, g.push.n, tm * tn);
   }
 }
 
@@ -556,7 +632,7 @@ inline cudaError_t launch_token_matmul(const DeviceWeight &dw, size_t M, const T
                                        float *y, const float *residual,
                                        unsigned long long *argmax_keys, unsigned *status,
                                        cudaStream_t s, bool pdl, const GemmPush *push = nullptr,
-                                       int row_base = 0) {
+                                       int row_base = 0, const TpWait *gate = nullptr) {
   GemmArgs g;
   g.codes = t.codes;
   g.split = t.split;
@@ -573,7 +649,9 @@ inline cudaError_t launch_token_matmul(const DeviceWeight &dw, size_t M, const T
   g.row_base = 0;
   g.status = status;
   g.push.n = 0;
+  g.gate.count = nullptr;
   if (push) g.push = *push;
+  if (gate) g.gate = *gate;
   if (row_base) g.row_base = row_base;
   void (*kernel)(GemmArgs) = dw.kind == 35 ? gemm_tokens_kernel<35> : gemm_tokens_kernel<10>;
   const int smem = dw.kind == 35 ? gemm_smem_bytes<35>() : gemm_smem_bytes<10>();

@@ -3,27 +3,34 @@
 // A rank owns a column slice (output rows) of every projection that feeds a
 // per-head or per-row operation -- attention q/gate (query heads), k and v
 // (the KV heads those query heads read), the Gated DeltaNet qkv / z / beta /
-// alpha (its heads), FFN up and gate (256-row blocks of the intermediate) --
-// and the matching row slice (input blocks) of the projections that leave
-// them: attn_output, ssm_out and ffn_down.  Those three produce a partial
-// sum of the full hidden vector on every rank, which the ranks all-reduce
-// before the residual add.  The output head is split by vocabulary rows and
-// the greedy token is the maximum of the ranks' (value, index) keys.
+// alpha (its heads), FFN up and gate (256-row blocks of the intermediate)
+// -- and the output head by vocabulary rows; the greedy token is the
+// maximum of the ranks' (value, index) keys.  The projections that leave
+// the heads and the FFN (attn_output, ssm_out, ffn_down) take one of two
+// forms:
 //
-// The all-reduce runs over peer memory, fused into the kernels on either
-// side of it:
-//   * the row-parallel GEMM's epilogue stores its partial tile straight into
-//     every rank's receive slot for this rank (P2P stores over NVLink /
-//     NVSwitch), fences at system scope and bumps each rank's arrival
-//     counter (gemm.cuh GemmPush);
-//   * the next RMSNorm kernel waits (bounded) for its counter, sums the
-//     ranks' partials in rank order, adds the residual and normalises.
-// Every rank therefore sums the same values in the same order and holds
-// bit-identical hidden states.  Two receive slots alternate between the
-// attention/GDN exchange and the FFN exchange: a rank can be at most one
-// exchange ahead of another (its next reduce needs the other's partial), so
-// a slot is never overwritten before every rank has read it.  Counters only
-// grow; an exchange's target is derived from the rank's completed-step count.
+//  * exact (default): column-split too.  Each rank quantizes its heads' (or
+//    FFN rows') output to Q8_K and stores the blocks straight into every
+//    rank's token buffer (fused quantize + all-gather); every rank then
+//    computes its slice of hidden rows over all K blocks and stores
+//    residual + result into every rank's hidden state (fused GEMM epilogue +
+//    all-gather).  Every value is computed exactly as on one GPU, so the
+//    batch is bit-identical to the one-GPU batch and to the oracle.
+//  * all-reduce: row-split (input blocks), as in Megatron-style tensor
+//    parallelism.  Each rank's partial sum of the full hidden vector is
+//    stored into a receive slot of every rank (fused GEMM epilogue); the
+//    next RMSNorm sums the slots in rank order and adds the residual.  All
+//    ranks agree bit for bit, but the cross-rank sums round differently
+//    from the reference's sequential per-row chain, and the Q8_K
+//    quantizers downstream turn those last-place differences into code
+//    flips: outputs match the one-GPU batch only to a tolerance that widens
+//    with depth.
+//
+// Every exchange is a producer storing over NVLink peer memory followed by
+// a bounded counter wait (gemm.cuh TpWait / tp_publish).  The exchanges of a
+// step are totally ordered across ranks (each waits for every rank's
+// previous one), so one buffer per kind (two alternating slots for the
+// all-reduce) is never overwritten before every rank has read it.
 //
 // Buffers are shared between the ranks' processes with CUDA IPC handles,
 // which the host exchanges (one 64-byte handle per rank).
@@ -43,7 +50,10 @@ struct TpPlan {
   int gh0 = 0, gh1 = 0;  // Gated DeltaNet heads (key head == value head)
   int fb0 = 0, fb1 = 0;  // FFN intermediate, in 256-row blocks
   int v0 = 0, v1 = 0;    // vocabulary rows of the output head (128-row tiles)
+  int hr0 = 0, hr1 = 0;  // hidden rows of attn_output / ssm_out / ffn_down (exact form)
 };
+
+enum TpMode : int { kTpExact = 0, kTpAllReduce = 1 };
 
 // Fills `p`; returns nullptr, or why the geometry cannot be split `size` ways.
 inline const char *tp_plan(const prism_b200_qwen35_config &c, int rank, int size, TpPlan &p) {
@@ -57,6 +67,7 @@ inline const char *tp_plan(const prism_b200_qwen35_config &c, int rank, int size
     p.gh1 = (int)c.ssm_values;
     p.fb1 = (int)(c.ffn / 256);
     p.v1 = (int)c.vocab;
+    p.hr1 = (int)c.hidden;
     return nullptr;
   }
   if (c.kv_heads == 0 || c.heads % c.kv_heads) return "query heads not a multiple of KV heads";
@@ -83,6 +94,8 @@ inline const char *tp_plan(const prism_b200_qwen35_config &c, int rank, int size
   if (tiles < size) return "vocabulary smaller than one tile per rank";
   p.v0 = rank * tiles / size * kGemmN;
   p.v1 = std::min<int>((int)c.vocab, (rank + 1) * tiles / size * kGemmN);
+  p.hr0 = (int)((long)rank * c.hidden / size);
+  p.hr1 = (int)((long)(rank + 1) * c.hidden / size);
   return nullptr;
 }
 
@@ -177,74 +190,105 @@ inline cudaError_t tp_gather_weight(const DeviceWeight &src, const std::vector<i
 
 // ---- the exchange ----------------------------------------------------------
 
-// This rank's exchange buffer: 256 B of counters (slot 0, slot 1, keys),
-// two receive slots [ranks][M][hidden] f32, then the greedy keys [ranks][M].
+// This rank's exchange buffer.  Counters (first 256 B): 0 hidden rows
+// (exact) or slot 0 (all-reduce), 1 slot 1, 2 greedy keys, 3 gathered
+// token blocks.  Then the all-reduce slots [2][ranks][M][hidden] f32, the
+// greedy keys [ranks][M], and for the exact form the hidden state [M][hidden]
+// and the gathered Q8_K token buffer.
 struct TpExchange {
   static constexpr size_t kHead = 256;
   uint8_t *base = nullptr;
-  size_t slot_bytes = 0, bytes = 0;
-  int ranks = 1, M = 0, n = 0;
+  int mode = kTpExact, ranks = 1, M = 0, n = 0, tok_nb = 0;
+  size_t slot_bytes = 0, keys_off = 0, hidden_off = 0, tok_off = 0, bytes = 0;
   uint8_t *peer[kMaxTp] = {};  // every rank's buffer as mapped here (own included)
   bool opened[kMaxTp] = {};    // peer[p] came from cudaIpcOpenMemHandle
   bool connected = false;
   unsigned long long *xstep = nullptr;  // steps completed on this rank, never reset
 
-  void layout(int ranks_, int M_, int n_) {
+  static size_t up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+  void layout(int mode_, int ranks_, int M_, int n_, int tok_nb_) {
+    mode = mode_;
     ranks = ranks_;
     M = M_;
     n = n_;
-    slot_bytes = (size_t)ranks * M * n * sizeof(float);
-    bytes = kHead + 2 * slot_bytes + (size_t)ranks * M * 8;
+    tok_nb = tok_nb_;
+    slot_bytes = mode == kTpAllReduce ? (size_t)ranks * M * n * sizeof(float) : 0;
+    keys_off = kHead + 2 * slot_bytes;
+    hidden_off = up(keys_off + (size_t)ranks * M * 8, 256);
+    tok_off = up(hidden_off + (mode == kTpExact ? (size_t)M * n * sizeof(float) : 0), 1024);
+    bytes = tok_off + (mode == kTpExact ? token_q8k_bytes(M, tok_nb) : 0);
   }
   static unsigned long long *count(uint8_t *b, int i) {
     return reinterpret_cast<unsigned long long *>(b) + i;
   }
   float *slot(uint8_t *b, int s) const { return reinterpret_cast<float *>(b + kHead + s * slot_bytes); }
   unsigned long long *keys(uint8_t *b) const {
-    return reinterpret_cast<unsigned long long *>(b + kHead + 2 * slot_bytes);
+    return reinterpret_cast<unsigned long long *>(b + keys_off);
   }
-  // the GEMM push of this rank's partial into slot s of every rank
-  GemmPush push(int rank, int s) const {
+  float *hidden(uint8_t *b) const { return reinterpret_cast<float *>(b + hidden_off); }
+  uint8_t *tok(uint8_t *b) const { return b + tok_off; }
+  // all-reduce: this rank's partial into slot s of every rank
+  GemmPush push_partial(int rank, int s) const {
     GemmPush g{};
     g.n = ranks;
+    g.ld = n;
+    g.col = 0;
     for (int p = 0; p < ranks; ++p) {
       g.dst[p] = slot(peer[p], s) + (size_t)rank * M * n;
       g.count[p] = count(peer[p], s);
     }
     return g;
   }
-};
-
-// An exchange's arrival target: (steps completed * per_step + index + 1) * inc.
-struct TpWait {
-  const unsigned long long *count;
-  const unsigned long long *xstep;
-  unsigned long long per_step, index, inc;
-};
-
-// Bounded wait (one thread) for an exchange; false when it expired or an
-// earlier wait of this step already did (the step has failed: skip).
-__device__ __forceinline__ bool tp_wait(const TpWait &w, unsigned *status) {
-  if (*reinterpret_cast<volatile unsigned *>(status) & kStatusTimeout) return false;
-  const unsigned long long target = (*w.xstep * w.per_step + w.index + 1ull) * w.inc;
-  const unsigned long long t0 = global_timer_ns();
-  for (;;) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w.count) : "memory");
-    if (v >= target) break;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
-      report(status, kStatusTimeout);
-      return false;
+  // exact: this rank's hidden rows [col, col + rows) into every rank's hidden
+  GemmPush push_rows(int col) const {
+    GemmPush g{};
+    g.n = ranks;
+    g.ld = n;
+    g.col = col;
+    for (int p = 0; p < ranks; ++p) {
+      g.dst[p] = hidden(peer[p]);
+      g.count[p] = count(peer[p], 0);
     }
+    return g;
   }
-  __threadfence_system();
-  return true;
+};
+
+// Quantize this rank's blocks of M token rows to Q8_K and store them into
+// every rank's token buffer (fused quantize + all-gather): x is [M][nbl*256],
+// its block b lands at block b0 + b of buffers carved for nbt blocks.  Each
+// CTA then counts its (token, block) units on every rank's counter.
+struct TpGather {
+  TokenQ8K dst[kMaxTp];
+  unsigned long long *count[kMaxTp];
+  int ranks;
+};
+
+__global__ void __launch_bounds__(256) q8k_gather_kernel(const float *__restrict__ x, int M,
+                                                         int nbl, int b0, int nbt, TpGather g,
+                                                         unsigned *status) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  grid_dependency_wait();
+  grid_dependents_launch();
+  const int units = M * nbl;
+  if (warp < units) {
+    const int m = warp / nbl, bl = warp % nbl;
+    uint32_t w0, w1;
+    int pair;
+    float scale;
+    quantize_token_unit(x, nbl, m, bl, lane, 0, w0, w1, pair, scale, status);
+    for (int p = 0; p < g.ranks; ++p)
+      store_token_unit(g.dst[p], nbt, m, b0 + bl, lane, w0, w1, pair, scale);
+  }
+  const int first = blockIdx.x * (blockDim.x >> 5);
+  const int mine = max(0, min((int)(blockDim.x >> 5), units - first));
+  tp_publish(g.count, g.ranks, (unsigned long long)mine);
 }
 
-// All-reduce receive side fused with the next RMSNorm (one 256-thread CTA
-// per token row): hidden = hidden + ((p_0 + p_1) + ... + p_{ranks-1}), then
-// out = (hidden * scale) * w as rmsnorm_rows_kernel computes it.  With
-// w == nullptr only the reduction runs.
+// RMSNorm of each token row after an exchange (one 256-thread CTA per row):
+// wait for the exchange; with ranks > 0 (all-reduce) first
+// hidden += ((p_0 + p_1) + ... + p_{ranks-1}) over the slot's partials;
+// then out = (hidden * scale) * w as rmsnorm_rows_kernel computes it.  With
+// w == nullptr only the wait and the reduction run.
 __global__ void __launch_bounds__(256)
     tp_reduce_norm_kernel(const float *slot, int ranks, int M, int n, TpWait w, float *hidden,
                           const float *nw, float eps, float *out, unsigned *status) {
@@ -256,7 +300,7 @@ __global__ void __launch_bounds__(256)
   __syncthreads();
   const long row = blockIdx.x;
   float *x = hidden + row * n;
-  if (ok) {
+  if (ok && ranks > 0) {
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
       float s = __ldcg(slot + row * n + i);
       for (int p = 1; p < ranks; ++p) s = __fadd_rn(s, __ldcg(slot + ((long)p * M + row) * n + i));
@@ -267,12 +311,26 @@ __global__ void __launch_bounds__(256)
   }
   __syncthreads();
   if (!nw) return;
-  const double sum = block_sumsq_f64(x, n, red);
+  double sum = 0.0;
+  {
+    // block_sumsq_f64's order, over values other ranks may have stored
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const float v = __ldcg(x + i);
+      sum += (double)__fmul_rn(v, v);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    sum = 0.0;
+    for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) sum += red[wi];
+  }
   const float mean = (float)(sum / (double)n);
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
   if ((!is_finite_f(scale) || !(scale > 0.0f)) && threadIdx.x == 0) report(status, kStatusNonfinite);
   for (int i = threadIdx.x; i < n; i += blockDim.x)
-    out[row * n + i] = __fmul_rn(__fmul_rn(x[i], scale), nw[i]);
+    out[row * n + i] = __fmul_rn(__fmul_rn(__ldcg(x + i), scale), nw[i]);
 }
 
 struct TpKeys {
@@ -282,8 +340,8 @@ struct TpKeys {
 
 // End of a tensor-parallel step (one CTA): send this rank's greedy keys
 // (the maximum over its vocabulary slice) to every rank, wait for all of
-// theirs, take the maximum in rank order -- the reference's lowest index
-// among equal maxima, as the key encodes -- and advance every sequence.
+// theirs, take the maximum -- the reference's lowest index among equal
+// maxima, as the key encodes -- and advance every sequence.
 __global__ void tp_finish_kernel(unsigned long long *keys, TpKeys push,
                                  const unsigned long long *recv, int ranks, TpWait w,
                                  uint32_t *tokens, int *pos, int B, int *step,
@@ -295,12 +353,8 @@ __global__ void tp_finish_kernel(unsigned long long *keys, TpKeys push,
     for (int p = 0; p < ranks; ++p) push.dst[p][b] = k;
     keys[b] = 0ull;
   }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int p = 0; p < ranks; ++p) atomicAdd_system(push.count[p], 1ull);
-    ok = tp_wait(w, status);
-  }
+  tp_publish(push.count, ranks, 1ull);
+  if (threadIdx.x == 0) ok = tp_wait(w, status);
   __syncthreads();
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     if (greedy && ok) {

@@ -173,18 +173,19 @@ def c_config(cfg, kv_policy=KV_F16):
 def tp_plan(cfg, rank, size):
     """The slice of every linear rank `rank` of a `size`-way tensor-parallel
     batch owns (host only): dict of [first, end) ranges -- query heads, KV
-    heads, Gated DeltaNet heads, FFN 256-row blocks, vocabulary rows."""
+    heads, Gated DeltaNet heads, FFN 256-row blocks, vocabulary rows, hidden
+    rows of the projections leaving the heads and the FFN (exact form)."""
     import ctypes as c
     L = pb.load()
     fn = L.prism_b200_tp_plan
     fn.restype = c.c_int
     fn.argtypes = [c.c_void_p, c.c_uint32, c.c_uint32, c.c_void_p]
     cc = c_config(cfg)
-    out = np.zeros(10, np.int32)
+    out = np.zeros(12, np.int32)
     st = fn(c.byref(cc), rank, size, out.ctypes.data)
     if st:
         raise pb.PrismB200Error(st, "tensor-parallel plan %d/%d" % (rank, size))
-    keys = ["query_heads", "kv_heads", "gdn_heads", "ffn_blocks", "vocab_rows"]
+    keys = ["query_heads", "kv_heads", "gdn_heads", "ffn_blocks", "vocab_rows", "hidden_rows"]
     return {k: (int(out[2 * i]), int(out[2 * i + 1])) for i, k in enumerate(keys)}
 
 
@@ -354,7 +355,7 @@ def _declare_batch(L):
         ("prism_b200_batch_stream", vp, [vp]),
         ("prism_b200_batch_fill_context", i32, [vp, u32, u64]),
         ("prism_b200_batch_read_state", c.c_int64, [vp, u32, u32, u32, vp, sz]),
-        ("prism_b200_batch_create_tp", i32, [vp, u32, u32, u32, u32, c.POINTER(vp)]),
+        ("prism_b200_batch_create_tp", i32, [vp, u32, u32, u32, u32, u32, c.POINTER(vp)]),
         ("prism_b200_batch_exchange_handle", i32, [vp, vp]),
         ("prism_b200_batch_connect", i32, [vp, vp]),
     ]:
@@ -365,6 +366,7 @@ def _declare_batch(L):
 
 
 EXCHANGE_HANDLE_BYTES = 64
+TP_EXACT, TP_ALLREDUCE = 0, 1
 
 
 class Qwen35Batch:
@@ -374,9 +376,12 @@ class Qwen35Batch:
     With tp_size > 1 this is rank `tp_rank` of a tensor-parallel batch (one
     process and GPU per rank, all stepping the same tokens): gather every
     rank's `exchange_handle()` in rank order and pass the list to
-    `connect()` before the first step."""
+    `connect()` before the first step.  `tp_mode` TP_EXACT gathers the
+    head / FFN outputs and column-splits every projection (bit-identical to
+    one GPU); TP_ALLREDUCE row-splits attn_output / ssm_out / ffn_down and
+    all-reduces their partial sums (matches one GPU to rounding only)."""
 
-    def __init__(self, model, sequences, context, tp_rank=0, tp_size=1):
+    def __init__(self, model, sequences, context, tp_rank=0, tp_size=1, tp_mode=TP_EXACT):
         import ctypes as c
         self.model, self.B, self.context = model, sequences, context
         self.tp_rank, self.tp_size = tp_rank, tp_size
@@ -384,7 +389,7 @@ class Qwen35Batch:
         _declare_batch(self.L)
         h = c.c_void_p()
         model.ex._check(self.L.prism_b200_batch_create_tp(model.h, sequences, context, tp_rank,
-                                                          tp_size, c.byref(h)))
+                                                          tp_size, tp_mode, c.byref(h)))
         self.h = h
 
     def exchange_handle(self):

@@ -90,6 +90,7 @@ def test_tp_plan_partitions_config1(size):
     _assert_partition([p["gdn_heads"] for p in plans], c.ssm_values)
     _assert_partition([p["ffn_blocks"] for p in plans], c.ffn // 256)
     _assert_partition([p["vocab_rows"] for p in plans], c.vocab)
+    _assert_partition([p["hidden_rows"] for p in plans], c.hidden)
     group = c.heads // c.kv_heads
     for p in plans:
         q0, q1 = p["query_heads"]

@@ -1,12 +1,18 @@
 """Tensor-parallel batched serving on 2 GPUs (one process per GPU).
 
-The tensor-parallel step splits attn_output / ssm_out / ffn_down by input
-blocks and all-reduces their partial sums over peer memory, so its hidden
-states differ from the one-GPU batch (which is bit-exact against the oracle)
-by the rounding of the cross-rank sums, propagated through the layers.  The
-tolerance is stated here: every hidden value within 2e-3 * max|hidden| of
-the one-GPU value, and the same greedy tokens.  The ranks hold bit-identical
-hidden states (they sum the same partials in the same order).
+Exact form (the default): every projection is column-split and the head /
+FFN outputs are gathered, so the tensor-parallel batch must equal the
+one-GPU batch (itself bit-exact against the oracle) bit for bit: hidden
+states, greedy tokens.
+
+All-reduce form: attn_output / ssm_out / ffn_down are row-split and their
+partial sums all-reduced, so the first step's hidden states match the
+one-GPU batch to float rounding of the cross-rank sums (stated tolerance:
+every value within 2e-6 * max|hidden|).  Later steps are not compared: the
+Q8_K and Q8_0 quantizers turn last-place differences into code flips that
+the recurrent state carries forward.  In both forms the ranks hold
+bit-identical hidden states (they compute or sum the same values in the
+same order).
 
 The ranks exchange their IPC handles over a gloo process group on
 127.0.0.1; each rank runs on its own GPU (the ranks' kernels wait on one
@@ -20,7 +26,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-HIDDEN_TOL = 2e-3
+ALLREDUCE_FIRST_STEP_TOL = 2e-6
 
 
 def _gpus():
@@ -34,8 +40,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run_batch(qwen35, model, B, context, tokens, tp_rank=0, tp_size=1, dist=None):
-    bt = qwen35.Qwen35Batch(model, B, context, tp_rank=tp_rank, tp_size=tp_size)
+def _run_batch(qwen35, model, B, context, tokens, tp_rank=0, tp_size=1, dist=None, mode=0):
+    bt = qwen35.Qwen35Batch(model, B, context, tp_rank=tp_rank, tp_size=tp_size, tp_mode=mode)
     try:
         if tp_size > 1:
             handles = [None] * tp_size
@@ -53,7 +59,7 @@ def _run_batch(qwen35, model, B, context, tokens, tp_rank=0, tp_size=1, dist=Non
         bt.close()
 
 
-def _rank_main(rank, world, port, cfg, kv, B, context, steps, q):
+def _rank_main(rank, world, port, cfg, kv, B, context, steps, mode, q):
     try:
         import datetime
         import torch.distributed as dist
@@ -65,7 +71,7 @@ def _rank_main(rank, world, port, cfg, kv, B, context, steps, q):
         model = qwen35.Qwen35Model(ex, cfg, kv_policy=kv)
         model.load(qwen35.synthetic_weights(cfg, seed=0))
         tokens = np.random.default_rng(5).integers(0, cfg.vocab, (B, steps)).astype(np.uint32)
-        res = {"tp": _run_batch(qwen35, model, B, context, tokens, rank, world, dist)}
+        res = {"tp": _run_batch(qwen35, model, B, context, tokens, rank, world, dist, mode)}
         if rank == 0:
             res["single"] = _run_batch(qwen35, model, B, context, tokens)
         dist.barrier()
@@ -77,12 +83,13 @@ def _rank_main(rank, world, port, cfg, kv, B, context, steps, q):
         q.put((rank, repr(e)))
 
 
-def _spawn(world, cfg, kv, B, context, steps):
+def _spawn(world, cfg, kv, B, context, steps, mode=0):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, cfg, kv, B, context, steps, q))
+    procs = [ctx.Process(target=_rank_main,
+                         args=(r, world, port, cfg, kv, B, context, steps, mode, q))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -101,37 +108,50 @@ def _spawn(world, cfg, kv, B, context, steps):
     return out
 
 
-def _check(out, world):
+def _ranks_agree(out, world):
     g0, h0 = out[0]["tp"]
     for r in range(1, world):
         g, h = out[r]["tp"]
         assert np.array_equal(g, g0), "ranks disagree on greedy tokens"
         assert np.array_equal(h.view(np.uint32), h0.view(np.uint32)), "ranks' hidden states differ"
+    return g0, h0
+
+
+def _check_exact(out, world):
+    g0, h0 = _ranks_agree(out, world)
     gs, hs = out[0]["single"]
-    err = np.abs(h0 - hs).max(axis=(1, 2))
-    scale = np.abs(hs).max(axis=(1, 2))
-    assert (err <= HIDDEN_TOL * scale).all(), (err / scale).tolist()
+    bad = int((h0.view(np.uint32) != hs.view(np.uint32)).sum())
+    assert bad == 0, "%d hidden values differ from the one-GPU batch" % bad
     assert np.array_equal(g0, gs), (g0, gs)
-    return float((err / scale).max())
 
 
 @pytest.mark.timeout(1200)
 @pytest.mark.parametrize("kv", [0, 1])
-def test_tp2_small_matches_one_gpu(kv):
+def test_tp2_exact_small_bit_identical_to_one_gpu(kv):
     if _gpus() < 2:
         pytest.skip("needs 2 GPUs (one rank per GPU)")
     import qwen35
     cfg = replace(qwen35.SMALL, ssm_groups=4)   # TP needs key heads == value heads
-    out = _spawn(2, cfg, kv, 3, 256, 6)
-    _check(out, 2)
+    _check_exact(_spawn(2, cfg, kv, 3, 256, 6), 2)
 
 
 @pytest.mark.timeout(1800)
-def test_tp2_config1_q8_matches_one_gpu():
+def test_tp2_exact_config1_q8_bit_identical_to_one_gpu():
     if _gpus() < 2:
         pytest.skip("needs 2 GPUs (one rank per GPU)")
     import qwen35
     cfg = replace(qwen35.CONFIG1, context=512)
-    out = _spawn(2, cfg, 1, 2, 512, 4)
-    _check(out, 2)
+    _check_exact(_spawn(2, cfg, 1, 3, 512, 4), 2)
 
+
+@pytest.mark.timeout(1200)
+def test_tp2_allreduce_first_step_within_rounding():
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs (one rank per GPU)")
+    import qwen35
+    cfg = replace(qwen35.CONFIG1, layers=4, context=512)
+    out = _spawn(2, cfg, 1, 3, 512, 1, mode=1)
+    _, h0 = _ranks_agree(out, 2)
+    _, hs = out[0]["single"]
+    err = np.abs(h0[0] - hs[0]).max()
+    assert err <= ALLREDUCE_FIRST_STEP_TOL * np.abs(hs[0]).max(), err / np.abs(hs[0]).max()

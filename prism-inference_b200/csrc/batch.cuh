@@ -346,7 +346,7 @@ inline cudaError_t enqueue_batch_step(prism_b200_batch *b, bool greedy) {
         cfg.numAttrs += 1;
         BK(cudaLaunchKernelEx(&cfg, attention_serve_kernel, sa));
       } else {
-        const size_t smem = attn_smem_bytes((int)c.head_dim, b->context);
+        const size_t smem = attn_launch_smem(aa, b->context);
         cudaLaunchConfig_t cfg =
             pdl_config(dim3(b->heads * kAttnSplit, B), dim3(kAttnThreads), smem, s, attr, pdl);
         attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;

@@ -81,6 +81,21 @@ struct prism_b200_model {
 
 namespace prism {
 
+// Dynamic shared memory of an attention_decode_kernel launch over a cache of
+// `context` positions: with the CTA's K and V rows staged when they fit
+// (sets a.kv_smem_off), else the in-place layout.
+inline size_t attn_launch_smem(AttnArgs &a, int context) {
+  const size_t staged = attn_smem_bytes_staged(a.hd, context, a.q8);
+  if (staged <= (size_t)kMaxSmem &&
+      cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)staged) == cudaSuccess) {
+    a.kv_smem_off = (int)attn_smem_bytes(a.hd, context);
+    return staged;
+  }
+  a.kv_smem_off = 0;
+  return attn_smem_bytes(a.hd, context);
+}
+
 template <typename T>
 cudaError_t model_alloc(prism_b200_model *m, T **p, size_t count) {
   void *v = nullptr;
@@ -171,7 +186,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
       aa.attended = m->attended;
       aa.status = status;
       // one 8-CTA cluster per query head (split over the cached positions)
-      const size_t smem = attn_smem_bytes((int)c.head_dim, (int)c.context);
+      const size_t smem = attn_launch_smem(aa, (int)c.context);
       cudaLaunchAttribute cattr[2];
       cudaLaunchConfig_t cfg = pdl_config(dim3(c.heads * kAttnSplit), dim3(kAttnThreads), smem,
                                           s, cattr, pdl);

@@ -176,6 +176,15 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_decode_kernel(GdnArgs a) {
   const int kw = a.groups * S;
   const int hist = a.conv_k - 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // The state rows were written by this layer's previous step, not by the
+  // kernels this one depends on: load them before the grid dependency, so
+  // their HBM latency overlaps the producer's tail.
+  float *state = a.state + b * a.state_stride + (long)h * S * S;
+  constexpr int RPW = S / (kGdnThreads / 32);  // rows per warp (8)
+  float4 srow[RPW];
+#pragma unroll
+  for (int i = 0; i < RPW; ++i)
+    srow[i] = reinterpret_cast<const float4 *>(state + (long)(warp * RPW + i) * S)[lane];
   grid_dependency_wait();
   grid_dependents_launch();
   const float *mixed = a.mixed + b * a.in_stride;
@@ -229,12 +238,6 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_decode_kernel(GdnArgs a) {
   const float oscale = __fdiv_rn(1.0f, __fsqrt_rn((float)S));
   const float4 kk = reinterpret_cast<const float4 *>(k)[lane];
   const float4 qq = reinterpret_cast<const float4 *>(q)[lane];
-  float *state = a.state + b * a.state_stride + (long)h * S * S;
-  constexpr int RPW = S / (kGdnThreads / 32);  // rows per warp (8)
-  float4 srow[RPW];
-#pragma unroll
-  for (int i = 0; i < RPW; ++i)
-    srow[i] = reinterpret_cast<const float4 *>(state + (long)(warp * RPW + i) * S)[lane];
   bool finite = true;
 #pragma unroll
   for (int i = 0; i < RPW; ++i) {
@@ -291,6 +294,9 @@ struct AttnArgs {
   const int *position;
   float *attended;          // [heads*hd]
   unsigned *status;
+  // > 0: shared-memory offset of the staged K and V rows of a CTA's chunk
+  // (attention_decode_kernel); 0: read them from global memory in place
+  int kv_smem_off;
 };
 
 constexpr int kAttnThreads = 256;
@@ -426,6 +432,46 @@ __host__ __device__ constexpr size_t attn_smem_bytes(int hd, int context) {
          (size_t)hd * 8;
 }
 
+// Bytes of one cached position of one KV head (binary16 row or Q8_0 record).
+__host__ __device__ constexpr int attn_row_bytes(int hd, int q8) {
+  return q8 ? q8_0_record_bytes(hd) : hd * 2;
+}
+
+// Shared memory with the chunk's K and V rows staged (placed after the
+// layout above): the launch uses it when it fits.
+__host__ __device__ constexpr size_t attn_smem_bytes_staged(int hd, int context, int q8) {
+  return attn_smem_bytes(hd, context) +
+         2 * (size_t)attn_chunk_cap(context) * (size_t)attn_row_bytes(hd, q8);
+}
+
+// Score of position p from a staged row (lane holds q dims lane*8..+7).
+__device__ __forceinline__ double key_partial_staged(const uint8_t *row, int hd, int q8,
+                                                     const float4 &q0, const float4 &q1,
+                                                     int lane) {
+  float k[8];
+  if (q8) {
+    const float d = half_bits_to_float(reinterpret_cast<const uint16_t *>(row)[lane >> 2]);
+    const uint2 c = *reinterpret_cast<const uint2 *>(row + hd / 32 * 2 + lane * 8);
+    const int8_t *cb = reinterpret_cast<const int8_t *>(&c);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) k[j] = __fmul_rn(d, (float)cb[j]);
+  } else {
+    const uint4 kv = reinterpret_cast<const uint4 *>(row)[lane];
+    const uint16_t *kh = reinterpret_cast<const uint16_t *>(&kv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) k[j] = half_bits_to_float(kh[j]);
+  }
+  return (double)__fmul_rn(q0.x, k[0]) + (double)__fmul_rn(q0.y, k[1]) +
+         (double)__fmul_rn(q0.z, k[2]) + (double)__fmul_rn(q0.w, k[3]) +
+         (double)__fmul_rn(q1.x, k[4]) + (double)__fmul_rn(q1.y, k[5]) +
+         (double)__fmul_rn(q1.z, k[6]) + (double)__fmul_rn(q1.w, k[7]);
+}
+
+__device__ __forceinline__ float value_staged(const uint8_t *row, int hd, int q8, int i) {
+  if (q8) return q8_0_value(row, hd, i);
+  return half_bits_to_float(reinterpret_cast<const uint16_t *>(row)[i]);
+}
+
 __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs args) {
   namespace cg = cooperative_groups;
   AttnArgs a = args;
@@ -453,6 +499,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
   __shared__ float fred[kAttnThreads / 32];
   __shared__ float s_max, s_cur;
   __shared__ double s_tot;
+  __shared__ __align__(8) uint64_t kvbar[2];
   const int rank = (int)cluster.block_rank();
   const int h = blockIdx.x / kAttnSplit;
   const int group = a.heads / a.kv_heads;
@@ -460,14 +507,43 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
   const int kvw = a.kv_heads * hd;
   const int i = threadIdx.x;
   const int warp = i >> 5, lane = i & 31;
-  grid_dependency_wait();
-  grid_dependents_launch();
+  // The position and the cached rows before it were written by earlier
+  // steps, not by the kernels this one depends on: read the position, build
+  // the RoPE table and start staging this CTA's K and V rows before the grid
+  // dependency, so their latency overlaps the producer's tail.
   const int pos = *a.position;
   // chunk of past positions owned by this CTA
   const int per = (pos + kAttnSplit - 1) / kAttnSplit;
   const int lo = min(pos, rank * per), hi = min(pos, lo + per);
   partial = reinterpret_cast<double *>(reinterpret_cast<uint8_t *>(sm) +
                                        ((size_t)(4 * hd + 64 + per + 1) * 4 + 15) / 16 * 16);
+  const bool staged = a.kv_smem_off > 0;
+  const int rb = attn_row_bytes(hd, a.q8);
+  uint8_t *kbuf = reinterpret_cast<uint8_t *>(sm) + a.kv_smem_off;
+  uint8_t *vbuf = kbuf + (size_t)per * rb;
+  if (staged) {
+    if (i == 0) {
+      mbar_init(&kvbar[0], 1);
+      mbar_init(&kvbar[1], 1);
+      mbar_init_fence();
+    }
+    __syncthreads();
+    if (warp == 0) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&kvbar[0], (unsigned)((hi - lo) * rb));
+        mbar_arrive_expect_tx(&kvbar[1], (unsigned)((hi - lo) * rb));
+      }
+      __syncwarp();
+      for (int p = lo + lane; p < hi; p += 32) {
+        const size_t at = a.q8 ? ((size_t)p * a.kv_heads + kvh) * rb
+                               : ((size_t)p * kvw + (size_t)kvh * hd) * 2;
+        bulk_g2s(kbuf + (size_t)(p - lo) * rb, reinterpret_cast<const uint8_t *>(a.kcache) + at,
+                 (unsigned)rb, &kvbar[0]);
+        bulk_g2s(vbuf + (size_t)(p - lo) * rb, reinterpret_cast<const uint8_t *>(a.vcache) + at,
+                 (unsigned)rb, &kvbar[1]);
+      }
+    }
+  }
   if (i < a.rope_dim / 2) {
     // reference src/graph.rs:6406-6437: angle_j = p * theta_scale^j by j
     // repeated binary32 multiplications; text positions give the three
@@ -478,6 +554,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
     cs[2 * i] = cos_cr(angle);
     cs[2 * i + 1] = sin_cr(angle);
   }
+  grid_dependency_wait();
+  grid_dependents_launch();
   __syncthreads();
   q[i] = norm_rope_round(a.projected + (long)h * 2 * hd, a.q_norm, a.eps, hd, a.rope_dim, cs,
                          buf, red);
@@ -501,9 +579,18 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
   // scores of this chunk: warp per position, lane owns 8 dims (16-byte load)
   const float4 q0 = reinterpret_cast<const float4 *>(q)[lane * 2];
   const float4 q1 = reinterpret_cast<const float4 *>(q)[lane * 2 + 1];
-  for (int p = lo + warp; p < hi; p += kAttnThreads / 32) {
-    const double s = warp_sum_f64(key_partial(a, p, kvh, q0, q1, lane));
-    if (lane == 0) scores[p - lo] = __fmul_rn((float)s, scale);
+  if (staged) {
+    const bool landed = mbar_wait_bounded(&kvbar[0], 0u, a.status);
+    for (int p = lo + warp; p < hi && landed; p += kAttnThreads / 32) {
+      const double s =
+          warp_sum_f64(key_partial_staged(kbuf + (size_t)(p - lo) * rb, hd, a.q8, q0, q1, lane));
+      if (lane == 0) scores[p - lo] = __fmul_rn((float)s, scale);
+    }
+  } else {
+    for (int p = lo + warp; p < hi; p += kAttnThreads / 32) {
+      const double s = warp_sum_f64(key_partial(a, p, kvh, q0, q1, lane));
+      if (lane == 0) scores[p - lo] = __fmul_rn((float)s, scale);
+    }
   }
   {
     // the current position's score (every CTA computes the same value)
@@ -538,7 +625,14 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
   for (int p = i; p < hi - lo; p += kAttnThreads) scores[p] = round_f16(__fmul_rn(scores[p], inv));
   __syncthreads();
   // value partial sums of this chunk: one dimension per thread, position order
-  {
+  if (staged) {
+    double acc = -0.0;
+    if (mbar_wait_bounded(&kvbar[1], 0u, a.status))
+      for (int p = lo; p < hi; ++p)
+        acc += (double)__fmul_rn(scores[p - lo],
+                                 value_staged(vbuf + (size_t)(p - lo) * rb, hd, a.q8, i));
+    partial[i] = acc;
+  } else {
     double acc = -0.0;
     int p = lo;
     for (; p + 4 <= hi; p += 4) {

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <set>
 #include <string>
@@ -137,6 +138,30 @@ inline cudaError_t init_matvec_attributes() {
 // previous kernel on the stream finishes (programmatic dependent launch):
 // the kernel streams its weights first and waits for the dependency only
 // before reading the activation.
+// Projection launch policy.  Default (PRISM_B200_MV_PER_SM unset or 0): as
+// many one-tile CTAs as fit, up to six per SM, two tiles in flight each --
+// measured fastest for batch-1 decode: the integer dots and chains of many
+// small CTAs overlap better than fewer CTAs with deeper tile queues, even
+// though every CTA rebuilds the Q8_K activation.  PRISM_B200_MV_PER_SM=k
+// (1..6) instead aims for k CTAs per SM with all of a CTA's tiles in flight
+// (A/B timing).  PRISM_B200_MV_STAGE=0 reads the f32 input in place instead
+// of staging it in shared memory with one round of loads.
+inline int mv_per_sm() {
+  static const int v = [] {
+    const char *e = getenv("PRISM_B200_MV_PER_SM");
+    const int x = e ? atoi(e) : 0;
+    return x < 0 ? 0 : (x > 6 ? 6 : x);
+  }();
+  return v;
+}
+inline bool mv_stage() {
+  static const bool v = [] {
+    const char *e = getenv("PRISM_B200_MV_STAGE");
+    return !(e && e[0] == '0');
+  }();
+  return v;
+}
+
 inline cudaError_t launch_matvec_group(uint32_t kind, int epi, MvArgs a, int num_sms,
                                        cudaStream_t s, bool pdl) {
   int hmax = 8;
@@ -150,14 +175,50 @@ inline cudaError_t launch_matvec_group(uint32_t kind, int epi, MvArgs a, int num
   if (pair && (a.count != 2 || a.w[0].h != a.w[1].h || a.w[0].rows != a.w[1].rows))
     return cudaErrorInvalidValue;
   const int upt = pair ? 2 * a.nb : a.nb;
-  const int smem = MatvecSmem(a.nb, hmax, unit_bytes((int)kind, hmax), upt).total();
-  if (smem > kMaxSmem) return cudaErrorInvalidValue;
-  int per_sm = kSmPerSm / (smem + 1024);
-  if (per_sm > 6) per_sm = 6;
-  if (per_sm < 1) per_sm = 1;
+  const int unit = unit_bytes((int)kind, hmax);
   const int ntiles = pair ? a.w[0].ntiles : a.tile_start[a.count];
-  const long cap = (long)per_sm * num_sms;
-  const int grid = (int)(ntiles < cap ? ntiles : cap);
+  int grid, smem;
+  const int target = mv_per_sm();
+  if (target == 0) {
+    a.nbuf = 2;
+    const int n = a.nb * 256;
+    const int stage_n = !mv_stage() ? 0 : a.prologue == kProRmsNorm ? 2 * n
+                                        : a.prologue == kProF32     ? n
+                                                                    : 0;
+    // staging must not cost a CTA per SM
+    const int plain = MatvecSmem(a.nb, hmax, unit, upt).total();
+    const int with = MatvecSmem(a.nb, hmax, unit, upt, 2, stage_n).total();
+    const int fit_plain = kSmPerSm / (plain + 1024), fit_with = kSmPerSm / (with + 1024);
+    a.stage = stage_n > 0 && with <= kMaxSmem && (fit_with >= fit_plain || fit_with >= 6);
+    smem = a.stage ? with : plain;
+    if (smem > kMaxSmem) return cudaErrorInvalidValue;
+    int per_sm = kSmPerSm / (smem + 1024);
+    if (per_sm > 6) per_sm = 6;
+    if (per_sm < 1) per_sm = 1;
+    const long cap = (long)per_sm * num_sms;
+    grid = (int)(ntiles < cap ? ntiles : cap);
+  } else {
+    // about `target` CTAs per SM; one tile per CTA when that barely
+    // overfills the SMs.  Each CTA keeps all its tiles in flight when they
+    // fit a budget that leaves room for the next kernel's CTA on the SM
+    // (its weights stream in under this kernel, programmatic dependent
+    // launch), and stages its f32 input in shared memory.
+    const long cap = (long)target * num_sms;
+    const int per_cta = ntiles <= cap + cap / 4 ? 1 : (int)((ntiles + cap - 1) / cap);
+    grid = (ntiles + per_cta - 1) / per_cta;
+    const int n = a.nb * 256;
+    int stage_n = a.prologue == kProRmsNorm ? 2 * n : a.prologue == kProF32 ? n : 0;
+    const int budget = kSmPerSm / (target + 1) - 2048;
+    int nbuf = per_cta;
+    auto size = [&](int nbf, int sn) { return MatvecSmem(a.nb, hmax, unit, upt, nbf, sn).total(); };
+    while (nbuf > 2 && size(nbuf, stage_n) > budget) --nbuf;
+    if (size(nbuf, stage_n) > budget) stage_n = 0;
+    while (nbuf > 1 && size(nbuf, stage_n) > budget) --nbuf;
+    smem = size(nbuf, stage_n);
+    if (smem > kMaxSmem) return cudaErrorInvalidValue;
+    a.nbuf = nbuf;
+    a.stage = stage_n > 0;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kThreads);

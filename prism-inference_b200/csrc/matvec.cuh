@@ -52,11 +52,14 @@ __host__ __device__ constexpr int unit_bytes(int kind, int h) {
 
 // Shared-memory layout (dynamic smem), all offsets 16-byte aligned.  `h` is
 // the largest tile height in the group (tile buffers are sized for it);
-// `upt` is the units per tile (nb, or 2*nb for the up+gate pair).
+// `upt` is the units per tile (nb, or 2*nb for the up+gate pair); `nbuf`
+// tile buffers; `stage_n` floats of staged f32 inputs (x, then the RMSNorm
+// weight), 0 when the prologue reads them in place.
 struct MatvecSmem {
-  int nb, h, unit, upt;
-  __host__ __device__ MatvecSmem(int nb_, int h_, int unit_, int upt_)
-      : nb(nb_), h(h_), unit(unit_), upt(upt_) {}
+  int nb, h, unit, upt, nbuf, stage_n;
+  __host__ __device__ MatvecSmem(int nb_, int h_, int unit_, int upt_, int nbuf_ = 2,
+                                 int stage_n_ = 0)
+      : nb(nb_), h(h_), unit(unit_), upt(upt_), nbuf(nbuf_), stage_n(stage_n_) {}
   __host__ __device__ int act_values() const { return 0; }
   __host__ __device__ int act_scale() const { return nb * 256; }
   __host__ __device__ int act_sums() const { return act_scale() + nb * 4; }
@@ -64,9 +67,10 @@ struct MatvecSmem {
   __host__ __device__ int red() const { return (act_asum() + nb * 4 + 15) / 16 * 16; }
   __host__ __device__ int terms() const { return red() + kWarps * 16; }
   __host__ __device__ int bars() const { return (terms() + upt * h * 4 + 15) / 16 * 16; }
-  __host__ __device__ int bufs() const { return (bars() + 2 * upt * 8 + 127) / 128 * 128; }
+  __host__ __device__ int stage() const { return (bars() + nbuf * upt * 8 + 15) / 16 * 16; }
+  __host__ __device__ int bufs() const { return (stage() + stage_n * 4 + 127) / 128 * 128; }
   __host__ __device__ int tile_bytes() const { return upt * unit; }
-  __host__ __device__ int total() const { return bufs() + 2 * tile_bytes(); }
+  __host__ __device__ int total() const { return bufs() + nbuf * tile_bytes(); }
 };
 
 enum Prologue : int { kProQ8K = 0, kProF32 = 1, kProRmsNorm = 2 };
@@ -96,6 +100,8 @@ struct MvArgs {
   int pinned = 0;                   // pinned Q8_K rounding
   unsigned long long *argmax_key = nullptr;
   unsigned *status = nullptr;
+  int nbuf = 2;                     // tile buffers (tiles in flight per CTA)
+  int stage = 0;                    // 1: stage f32 inputs in shared memory first
 };
 
 __device__ __forceinline__ unsigned byte_of(const uint4 &v, int g) {
@@ -288,9 +294,11 @@ __device__ __forceinline__ double block_sumsq_f64(const float *x, int n, double 
 //   kProF32:     x
 //   kProRmsNorm: (x * scale) * w, scale = 1/sqrt(mean(x^2) + eps)
 __device__ __forceinline__ void stage_from_f32(const MvArgs &a, const MatvecSmem &L,
-                                               uint8_t *smem) {
+                                               uint8_t *smem, const float *x_override = nullptr,
+                                               const float *w_override = nullptr) {
   const int nb = L.nb, n = nb * 256;
-  const float *x = static_cast<const float *>(a.in0);
+  const float *x = x_override ? x_override : static_cast<const float *>(a.in0);
+  const float *norm_w = w_override ? w_override : a.norm_w;
   float scale = 1.0f;
   if (a.prologue == kProRmsNorm) {
     double *red = reinterpret_cast<double *>(smem + L.red());
@@ -310,8 +318,8 @@ __device__ __forceinline__ void stage_from_f32(const MvArgs &a, const MatvecSmem
     v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
     v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
     if (a.prologue == kProRmsNorm) {
-      const float4 w0 = *reinterpret_cast<const float4 *>(a.norm_w + base);
-      const float4 w1 = *reinterpret_cast<const float4 *>(a.norm_w + base + 4);
+      const float4 w0 = *reinterpret_cast<const float4 *>(norm_w + base);
+      const float4 w1 = *reinterpret_cast<const float4 *>(norm_w + base + 4);
       const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], scale), w[i]);
@@ -323,6 +331,14 @@ __device__ __forceinline__ void stage_from_f32(const MvArgs &a, const MatvecSmem
     if (st && lane == 0) report(a.status, st);
     store_q8k_soa(L, smem, b, lane, qscale, q, pair_sum);
   }
+}
+
+// Copy n floats (n % 4 == 0, 16-byte aligned) into shared memory, all
+// threads, every load in flight before the stores.
+__device__ __forceinline__ void load_f32_to_smem(float *dst, const float *src, int n) {
+#pragma unroll 4
+  for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
+    *reinterpret_cast<float4 *>(dst + i) = *reinterpret_cast<const float4 *>(src + i);
 }
 
 // Issue the bulk copies of one tile into buffer `buf` (one mbarrier per unit).
@@ -376,29 +392,43 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
   const int upt = PAIR ? 2 * nb : nb;
   int hmax = 8;
   for (int g = 0; g < args.count; ++g) hmax = max(hmax, args.w[g].h);
-  const MatvecSmem L(nb, hmax, unit_bytes(KIND, hmax), upt);
+  const int nbuf = args.nbuf, n = nb * 256;
+  const bool staged = args.stage && args.prologue != kProQ8K;
+  const MatvecSmem L(nb, hmax, unit_bytes(KIND, hmax), upt, nbuf,
+                     staged ? (args.prologue == kProRmsNorm ? 2 * n : n) : 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars());  // [2][upt]
-  uint8_t *bufs = smem + L.bufs();                                  // [2][tile]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars());  // [nbuf][upt]
+  uint8_t *bufs = smem + L.bufs();                                  // [nbuf][tile]
   float *terms = reinterpret_cast<float *>(smem + L.terms());       // [upt][H]
+  float *xs = reinterpret_cast<float *>(smem + L.stage());          // [n] x, [n] norm weight
   const int ntiles = PAIR ? args.w[0].ntiles : args.tile_start[args.count];
 
-  for (int i = threadIdx.x; i < 2 * upt; i += blockDim.x) {
+  for (int i = threadIdx.x; i < nbuf * upt; i += blockDim.x) {
     mbar_init(&bars[i], 1);
     mbar_init_fence();
   }
   __syncthreads();
-  // Weights never depend on the previous kernel: stream the first two tiles
-  // before waiting on the grid dependency.
+  // Weights never depend on the previous kernel: stream this CTA's first
+  // nbuf tiles, and stage the RMSNorm weight, before waiting on the grid
+  // dependency.
   const int t0 = blockIdx.x;
-  if (t0 < ntiles) issue_group_tile<EPI>(args, KIND, t0, bufs, bars);
-  if (t0 + (int)gridDim.x < ntiles)
-    issue_group_tile<EPI>(args, KIND, t0 + gridDim.x, bufs + L.tile_bytes(), bars + upt);
+  for (int j = 0; j < nbuf; ++j) {
+    const int tj = t0 + j * (int)gridDim.x;
+    if (tj < ntiles) issue_group_tile<EPI>(args, KIND, tj, bufs + j * L.tile_bytes(), bars + j * upt);
+  }
+  if (staged && args.prologue == kProRmsNorm) load_f32_to_smem(xs + n, args.norm_w, n);
   grid_dependency_wait();
-  if (args.prologue == kProQ8K)
+  if (args.prologue == kProQ8K) {
     stage_q8k_aos(static_cast<const uint8_t *>(args.in0), L, smem, args.status);
-  else
+  } else if (staged) {
+    // the input arrives with one round of loads, then the prologue works
+    // from shared memory
+    load_f32_to_smem(xs, static_cast<const float *>(args.in0), n);
+    __syncthreads();
+    stage_from_f32(args, L, smem, xs, xs + n);
+  } else {
     stage_from_f32(args, L, smem);
+  }
   __syncthreads();
   grid_dependents_launch();
 
@@ -411,8 +441,8 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
   bool ok = true;
   int it = 0;
   for (int t = t0; t < ntiles; t += gridDim.x, ++it) {
-    const int k = it & 1;
-    const unsigned parity = (unsigned)(it >> 1) & 1u;
+    const int k = it % nbuf;
+    const unsigned parity = (unsigned)(it / nbuf) & 1u;
     uint8_t *buf = bufs + k * L.tile_bytes();
     uint64_t *bk = bars + k * upt;
     const int g = PAIR ? 0 : group_of(args, t);
@@ -474,8 +504,8 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
       }
     }
     __syncthreads();
-    // refill this buffer with the tile two steps ahead
-    const int tn = t + 2 * gridDim.x;
+    // refill this buffer with the tile nbuf steps ahead
+    const int tn = t + nbuf * (int)gridDim.x;
     if (tn < ntiles) {
       fence_proxy_async_smem();
       issue_group_tile<EPI>(args, KIND, tn, buf, bk);
@@ -491,12 +521,12 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
   }
   if (!ok) {
     // a wait expired: drain every armed copy (bounded) before exiting
-    for (int j = 0; j < 2; ++j) {
-      const int tj = t0 + (it + j) * gridDim.x;
+    for (int j = 0; j < nbuf; ++j) {
+      const int tj = t0 + (it + j) * (int)gridDim.x;
       if (tj >= ntiles) break;
-      const int kj = (it + j) & 1;
+      const int kj = (it + j) % nbuf;
       for (int u = threadIdx.x; u < upt; u += blockDim.x)
-        mbar_wait_bounded(&bars[kj * upt + u], (unsigned)((it + j) >> 1) & 1u, args.status);
+        mbar_wait_bounded(&bars[kj * upt + u], (unsigned)((it + j) / nbuf) & 1u, args.status);
     }
   }
 }

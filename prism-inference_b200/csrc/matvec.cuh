@@ -45,6 +45,7 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxNb = 64;     // columns <= 16384 per projection
 constexpr int kMaxGroup = 4;   // sibling weights per launch
+constexpr int kMaxPrefetch = 8;  // L2 prefetch ranges per launch
 
 __host__ __device__ constexpr int unit_bytes(int kind, int h) {
   return (kind == 35 ? 66 : 84) * h;
@@ -102,6 +103,10 @@ struct MvArgs {
   unsigned *status = nullptr;
   int nbuf = 2;                     // tile buffers (tiles in flight per CTA)
   int stage = 0;                    // 1: stage f32 inputs in shared memory first
+  // L2 prefetch of later kernels' operands (weights, recurrent state): the
+  // grid splits each range; 16-byte aligned, sizes multiples of 16
+  const uint8_t *pf[kMaxPrefetch] = {};
+  unsigned pf_bytes[kMaxPrefetch] = {};
 };
 
 __device__ __forceinline__ unsigned byte_of(const uint4 &v, int g) {
@@ -333,6 +338,23 @@ __device__ __forceinline__ void stage_from_f32(const MvArgs &a, const MatvecSmem
   }
 }
 
+// This CTA's share of the launch's L2 prefetch ranges (one thread), in
+// pieces of at most 32 KB.
+__device__ __forceinline__ void prefetch_l2_share(const MvArgs &a) {
+  for (int r = 0; r < kMaxPrefetch; ++r) {
+    const unsigned bytes = a.pf_bytes[r];
+    if (!bytes) continue;
+    const unsigned chunk = (bytes / gridDim.x + 15u) / 16u * 16u;
+    const unsigned lo = blockIdx.x * chunk;
+    const unsigned hi = min(bytes, lo + chunk);
+    for (unsigned o = lo; o < hi; o += 32768u) {
+      const unsigned len = min(32768u, hi - o);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.pf[r] + o), "r"(len)
+                   : "memory");
+    }
+  }
+}
+
 // Copy n floats (n % 4 == 0, 16-byte aligned) into shared memory, all
 // threads, every load in flight before the stores.
 __device__ __forceinline__ void load_f32_to_smem(float *dst, const float *src, int n) {
@@ -412,6 +434,7 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
   // nbuf tiles, and stage the RMSNorm weight, before waiting on the grid
   // dependency.
   const int t0 = blockIdx.x;
+  if (threadIdx.x == 32) prefetch_l2_share(args);
   for (int j = 0; j < nbuf; ++j) {
     const int tj = t0 + j * (int)gridDim.x;
     if (tj < ntiles) issue_group_tile<EPI>(args, KIND, tj, bufs + j * L.tile_bytes(), bars + j * upt);

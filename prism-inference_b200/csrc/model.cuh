@@ -116,6 +116,60 @@ inline StepState step_state(prism_b200_model *m) {
   return st;
 }
 
+// The step's launches in order (projection groups, Gated DeltaNet,
+// attention; the LM head last with `head`), each with the HBM ranges it
+// reads that no earlier kernel of the step writes: weights and recurrent
+// state.  Projection launches prefetch these into L2 a few launches ahead
+// (kPrefetchAhead), so the weight stream runs under the dependent chain of
+// small kernels instead of inside it; the last launches of a step prefetch
+// the first ones of the next step (the same weights).
+constexpr int kPrefetchAhead = 3;
+constexpr size_t kPrefetchCap = 24u << 20;  // bytes of one range (the LM head's first part)
+
+struct PfItem {
+  std::vector<std::pair<const uint8_t *, size_t>> r;
+  void add(const void *p, size_t bytes) {
+    if (p && bytes) r.emplace_back(static_cast<const uint8_t *>(p), std::min(bytes, kPrefetchCap) / 16 * 16);
+  }
+  void add(const DeviceWeight &w) { add(w.units, w.bytes); }
+};
+
+inline std::vector<PfItem> step_items(prism_b200_model *m, bool head) {
+  const auto &c = m->cfg;
+  std::vector<PfItem> items;
+  for (const ModelLayer &Ly : m->L) {
+    PfItem g, mid, out, ffn, down;
+    if (Ly.full) {
+      g.add(Ly.q);
+      g.add(Ly.k);
+      g.add(Ly.v);
+      out.add(Ly.o);
+    } else {
+      g.add(Ly.qkv);
+      g.add(Ly.z);
+      g.add(Ly.beta);
+      g.add(Ly.alpha);
+      mid.add(Ly.matrix, (size_t)c.ssm_values * c.ssm_state * c.ssm_state * 4);
+      mid.add(Ly.conv_state, (size_t)2 * m->channels() * (c.conv_kernel - 1) * 4);
+      out.add(Ly.out);
+    }
+    ffn.add(Ly.up);
+    ffn.add(Ly.gate);
+    down.add(Ly.down);
+    items.push_back(g);
+    items.push_back(mid);
+    items.push_back(out);
+    items.push_back(ffn);
+    items.push_back(down);
+  }
+  if (head) {
+    PfItem h;
+    h.add(m->embd);
+    items.push_back(h);
+  }
+  return items;
+}
+
 // Enqueue one decode step.  With `head`, the step ends with the tied LM head,
 // the greedy key and (past the prompt) the next input token.
 // `ev` (optional, 2*layers + 4 events) brackets the phases for per-layer
@@ -151,6 +205,32 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
   }
   mark(1);
   const uint32_t kind = c.weight_kind;
+  // L2 prefetch: launch `item` covers the items after `horizon` up to
+  // item + kPrefetchAhead (wrapping into the next step)
+  const std::vector<PfItem> items = step_items(m, head);
+  const int nitems = (int)items.size();
+  int item = 0, horizon = kPrefetchAhead;  // the first items are the previous step's
+  static const bool pf_on = [] {
+    const char *e = getenv("PRISM_B200_PREFETCH");  // 0: off (A/B timing)
+    return !(e && e[0] == '0');
+  }();
+  auto prefetch = [&](MvArgs &a) {
+    if (!pf_on) return;
+    int k = 0;
+    for (; horizon < item + kPrefetchAhead; ++horizon) {
+      for (const auto &r : items[(horizon + 1) % nitems].r)
+        if (k < kMaxPrefetch) {
+          a.pf[k] = r.first;
+          a.pf_bytes[k] = (unsigned)r.second;
+          ++k;
+        }
+    }
+  };
+  auto launch_mv = [&](int epi, MvArgs &a) {
+    prefetch(a);
+    ++item;
+    return launch_matvec_group(kind, epi, a, sms, s, pdl);
+  };
   for (size_t l = 0; l < m->L.size(); ++l) {
     ModelLayer &Ly = m->L[l];
     MvArgs a;
@@ -165,7 +245,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
       a.w[0] = mv_weight(Ly.q, m->projected);
       a.w[1] = mv_weight(Ly.k, m->key);
       a.w[2] = mv_weight(Ly.v, m->value);
-      if ((e = launch_matvec_group(kind, kEpiStore, a, sms, s, pdl)) != cudaSuccess) return e;
+      if ((e = launch_mv(kEpiStore, a)) != cudaSuccess) return e;
       AttnArgs aa{};
       aa.heads = (int)c.heads;
       aa.kv_heads = (int)c.kv_heads;
@@ -196,6 +276,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
       cattr[cfg.numAttrs].val.clusterDim.z = 1;
       cfg.numAttrs += 1;
       if ((e = cudaLaunchKernelEx(&cfg, attention_decode_kernel, aa)) != cudaSuccess) return e;
+      ++item;
       MvArgs o;
       o.prologue = kProF32;
       o.in0 = m->attended;
@@ -203,14 +284,14 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
       o.nb = (int)(c.heads * c.head_dim / 256);
       o.count = 1;
       o.w[0] = mv_weight(Ly.o, m->hidden, m->hidden);
-      if ((e = launch_matvec_group(kind, kEpiStore, o, sms, s, pdl)) != cudaSuccess) return e;
+      if ((e = launch_mv(kEpiStore, o)) != cudaSuccess) return e;
     } else {
       a.count = 4;
       a.w[0] = mv_weight(Ly.qkv, m->mixed);
       a.w[1] = mv_weight(Ly.z, m->zgate);
       a.w[2] = mv_weight(Ly.beta, m->beta);
       a.w[3] = mv_weight(Ly.alpha, m->alpha);
-      if ((e = launch_matvec_group(kind, kEpiStore, a, sms, s, pdl)) != cudaSuccess) return e;
+      if ((e = launch_mv(kEpiStore, a)) != cudaSuccess) return e;
       GdnArgs g;
       g.S = (int)c.ssm_state;
       g.groups = (int)c.ssm_groups;
@@ -238,6 +319,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
       cudaLaunchConfig_t cfg =
           pdl_config(dim3(c.ssm_values, 1), dim3(kGdnThreads), 0, s, attr, pdl);
       if ((e = cudaLaunchKernelEx(&cfg, gdn_decode_kernel, g)) != cudaSuccess) return e;
+      ++item;
       MvArgs o;
       o.prologue = kProF32;
       o.in0 = m->attended;
@@ -245,7 +327,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
       o.nb = m->value_width() / 256;
       o.count = 1;
       o.w[0] = mv_weight(Ly.out, m->hidden, m->hidden);
-      if ((e = launch_matvec_group(kind, kEpiStore, o, sms, s, pdl)) != cudaSuccess) return e;
+      if ((e = launch_mv(kEpiStore, o)) != cudaSuccess) return e;
     }
     mark(2 + 2 * (int)l);
     MvArgs f;
@@ -258,7 +340,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
     f.count = 2;
     f.w[0] = mv_weight(Ly.up, m->up);  // receives up * silu(gate)
     f.w[1] = mv_weight(Ly.gate, nullptr);
-    if ((e = launch_matvec_group(kind, kEpiSwiglu, f, sms, s, pdl)) != cudaSuccess) return e;
+    if ((e = launch_mv(kEpiSwiglu, f)) != cudaSuccess) return e;
     MvArgs d;
     d.prologue = kProF32;
     d.in0 = m->up;
@@ -266,7 +348,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
     d.nb = (int)(c.ffn / 256);
     d.count = 1;
     d.w[0] = mv_weight(Ly.down, m->hidden, m->hidden);
-    if ((e = launch_matvec_group(kind, kEpiStore, d, sms, s, pdl)) != cudaSuccess) return e;
+    if ((e = launch_mv(kEpiStore, d)) != cudaSuccess) return e;
     mark(3 + 2 * (int)l);
   }
   if (head) {
@@ -280,7 +362,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
     h.count = 1;
     h.w[0] = mv_weight(m->embd, m->logits);
     h.argmax_key = m->d_argmax;
-    if ((e = launch_matvec_group(kind, kEpiArgmax, h, sms, s, pdl)) != cudaSuccess) return e;
+    if ((e = launch_mv(kEpiArgmax, h)) != cudaSuccess) return e;
   }
   mark(2 + 2 * nl);
   cudaLaunchConfig_t cfg = pdl_config(dim3(1), dim3(32), 0, s, attr, pdl);

@@ -155,3 +155,17 @@ def test_tp2_allreduce_first_step_within_rounding():
     _, hs = out[0]["single"]
     err = np.abs(h0[0] - hs[0]).max()
     assert err <= ALLREDUCE_FIRST_STEP_TOL * np.abs(hs[0]).max(), err / np.abs(hs[0]).max()
+
+
+@pytest.mark.timeout(1800)
+def test_tp_exact_config1_on_every_gpu():
+    """The widest tensor-parallel split the box offers (8, 4 or 2 ranks): at
+    8 ranks two ranks share each KV head and the FFN blocks split unevenly
+    (36 over 8)."""
+    n = _gpus()
+    world = next((w for w in (8, 4, 2) if w <= n), 0)
+    if world < 2:
+        pytest.skip("needs 2 GPUs (one rank per GPU)")
+    import qwen35
+    cfg = replace(qwen35.CONFIG1, layers=8, context=512)
+    _check_exact(_spawn(world, cfg, 1, 3, 512, 3), world)

@@ -299,10 +299,17 @@ int prism_b200_model_persistent(const prism_b200_model *m);
  * [7] end (arrival at the next barrier) in globaltimer ns; [5] start,
  * [1] inputs staged, [2] first tiles resident, [3] their dots done,
  * [4] their chains done in SM clock cycles (projection phases only).
- * Copies at most `count` values and returns how many (0 for a
- * non-persistent model).  Phases: embedding, then per layer three
- * attention-side phases and the FFN pair, then the LM head.  No counterpart
- * in the reference. */
+ * Phases: embedding, then per layer three attention-side phases and the FFN
+ * pair, then the LM head.
+ * For the kernel-sequence step, with PRISM_B200_TRACE=1 set before the
+ * model is finalized: the last step's per-launch timelines in globaltimer
+ * ns, 8 values per launch (per layer: projection group, GDN or attention,
+ * out-projection, FFN pair, FFN down; then the LM head): CTA 0's [0] entry,
+ * [1] grid dependency passed, [2] input staged, [3] first tile resident,
+ * [4] its dots, [5] its chains, [6] exit, and [7] the last CTA's exit
+ * (projections; GDN and attention stamp [0], [1], [6], [7]).
+ * Copies at most `count` values and returns how many (0 when no timeline
+ * is recorded).  No counterpart in the reference. */
 int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t count);
 
 /* One token at the next position (reference Decoder::evaluate_finite_into,

@@ -32,6 +32,21 @@ __device__ __forceinline__ void report(unsigned *status, unsigned bit) {
   atomicOr(status, bit);
 }
 
+// Optional kernel timelines (globaltimer ns): CTA 0 stamps its progress
+// points; on exit every CTA raises slot 7 to its exit time, so slot 7 ends
+// as the last CTA's exit.
+__device__ __forceinline__ void trace_stamp(unsigned long long *trace, int slot) {
+  if (trace && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+    trace[slot] = global_timer_ns();
+}
+__device__ __forceinline__ void trace_exit(unsigned long long *trace) {
+  if (trace && threadIdx.x == 0) {
+    const unsigned long long t = global_timer_ns();
+    if (blockIdx.x == 0 && blockIdx.y == 0) trace[6] = t;
+    atomicMax(&trace[7], t);
+  }
+}
+
 // ---- binary16 <-> binary32 --------------------------------------------------
 // The hardware conversions: widening is exact for every binary16 value
 // (subnormals included), narrowing rounds to nearest even with overflow to

@@ -194,6 +194,13 @@ inline cudaError_t launch_matvec_group(uint32_t kind, int epi, MvArgs a, int num
     if (smem > kMaxSmem) return cudaErrorInvalidValue;
     int per_sm = kSmPerSm / (smem + 1024);
     if (per_sm > 6) per_sm = 6;
+    // registers cap the resident CTAs too: a grid beyond them runs in a
+    // second wave instead of looping over tiles
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, matvec_kernel_ptr(kind, epi), kThreads,
+                                                      (size_t)smem) == cudaSuccess &&
+        occ > 0 && occ < per_sm)
+      per_sm = occ;
     if (per_sm < 1) per_sm = 1;
     const long cap = (long)per_sm * num_sms;
     grid = (int)(ntiles < cap ? ntiles : cap);

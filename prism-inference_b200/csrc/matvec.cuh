@@ -21,8 +21,8 @@
 // attn_qkv + attn_gate + ssm_beta + ssm_alpha.  Persistent CTAs loop over
 // the concatenated tiles (t = blockIdx.x, += gridDim.x).  A tile is streamed
 // into shared memory by 1-D bulk async copies (cp.async.bulk, one mbarrier
-// per unit) two tiles ahead (double buffer).  Warp w computes units
-// b = w, w+8, ...: the 32 lanes cover the H rows x 4 chunks (L = 32/H lanes
+// per unit) two tiles ahead (double buffer).  Warp w (of 16) computes units
+// b = w, w+16, ...: the 32 lanes cover the H rows x 4 chunks (L = 32/H lanes
 // per row), weights are lane-private 16-byte shared loads, activations are
 // broadcast 16-byte shared loads, byte products use dp4a and per-row integer
 // partials combine exactly with shuffles.  Terms go to shared memory; then
@@ -41,7 +41,7 @@
 
 namespace prism {
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxNb = 64;     // columns <= 16384 per projection
 constexpr int kMaxGroup = 4;   // sibling weights per launch
@@ -107,7 +107,12 @@ struct MvArgs {
   // grid splits each range; 16-byte aligned, sizes multiples of 16
   const uint8_t *pf[kMaxPrefetch] = {};
   unsigned pf_bytes[kMaxPrefetch] = {};
+  // optional timeline (globaltimer ns): CTA 0's [0] entry, [1] past the grid
+  // dependency, [2] input staged, [3] first tile resident, [4] its dots,
+  // [5] its chains, [6] exit; [7] the last CTA's exit
+  unsigned long long *trace = nullptr;
 };
+
 
 __device__ __forceinline__ unsigned byte_of(const uint4 &v, int g) {
   unsigned w = (g < 4) ? v.x : (g < 8) ? v.y : (g < 12) ? v.z : v.w;
@@ -424,6 +429,7 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
   float *terms = reinterpret_cast<float *>(smem + L.terms());       // [upt][H]
   float *xs = reinterpret_cast<float *>(smem + L.stage());          // [n] x, [n] norm weight
   const int ntiles = PAIR ? args.w[0].ntiles : args.tile_start[args.count];
+  trace_stamp(args.trace, 0);
 
   for (int i = threadIdx.x; i < nbuf * upt; i += blockDim.x) {
     mbar_init(&bars[i], 1);
@@ -441,6 +447,7 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
   }
   if (staged && args.prologue == kProRmsNorm) load_f32_to_smem(xs + n, args.norm_w, n);
   grid_dependency_wait();
+  trace_stamp(args.trace, 1);
   if (args.prologue == kProQ8K) {
     stage_q8k_aos(static_cast<const uint8_t *>(args.in0), L, smem, args.status);
   } else if (staged) {
@@ -453,6 +460,7 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
     stage_from_f32(args, L, smem);
   }
   __syncthreads();
+  trace_stamp(args.trace, 2);
   grid_dependents_launch();
 
   const int8_t *values = reinterpret_cast<const int8_t *>(smem + L.act_values());
@@ -480,6 +488,7 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
         ok = false;
         break;
       }
+      if (it == 0 && u == warp) trace_stamp(args.trace, 3);
       const int b = PAIR && u >= nb ? u - nb : u;  // activation block
       const uint8_t *up = buf + u * unit;
       const int8_t *av = values + b * 256;
@@ -503,6 +512,7 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
       }
     }
     if (!__syncthreads_and(ok)) break;
+    if (it == 0) trace_stamp(args.trace, 4);
     if (EPI != kEpiInts && threadIdx.x < H) {
       // the reference's chain: sum = 0; sum += term_b for b in order
       float sum = 0.0f;
@@ -527,6 +537,7 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
       }
     }
     __syncthreads();
+    if (it == 0) trace_stamp(args.trace, 5);
     // refill this buffer with the tile nbuf steps ahead
     const int tn = t + nbuf * (int)gridDim.x;
     if (tn < ntiles) {
@@ -552,6 +563,7 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
         mbar_wait_bounded(&bars[kj * upt + u], (unsigned)((it + j) / nbuf) & 1u, args.status);
     }
   }
+  trace_exit(args.trace);
 }
 
 // ---- upload-time repack: reference row-major blocks -> tiled units ---------

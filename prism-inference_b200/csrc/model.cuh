@@ -60,6 +60,10 @@ struct prism_b200_model {
   unsigned *d_sync = nullptr, *d_hsync = nullptr;
   int nhsync = 0;
   unsigned long long *d_trace = nullptr;  // [8 * phases] of a traced step
+  // per-kernel timelines of the kernel-sequence step (PRISM_B200_TRACE=1 set
+  // before finalize): [8 * launches], projection / GDN / attention launches
+  unsigned long long *d_seqtrace = nullptr;
+  int nseqtrace = 0;
   float *gdn_o = nullptr, *smax = nullptr;
   double *stot = nullptr, *apart = nullptr;
   std::map<std::string, bool> bound;
@@ -226,8 +230,17 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
         }
     }
   };
+  // optional per-launch timelines (not on event-timed steps)
+  auto trace_slot = [&]() -> unsigned long long * {
+    return m->d_seqtrace && !ev && item < m->nseqtrace ? m->d_seqtrace + 8 * item : nullptr;
+  };
+  if (m->d_seqtrace && !ev) {
+    if ((e = cudaMemsetAsync(m->d_seqtrace, 0, (size_t)64 * m->nseqtrace, s)) != cudaSuccess)
+      return e;
+  }
   auto launch_mv = [&](int epi, MvArgs &a) {
     prefetch(a);
+    a.trace = trace_slot();
     ++item;
     return launch_matvec_group(kind, epi, a, sms, s, pdl);
   };
@@ -265,6 +278,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
       aa.position = m->d_position;
       aa.attended = m->attended;
       aa.status = status;
+      aa.trace = trace_slot();
       // one 8-CTA cluster per query head (split over the cached positions)
       const size_t smem = attn_launch_smem(aa, (int)c.context);
       cudaLaunchAttribute cattr[2];
@@ -293,6 +307,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
       a.w[3] = mv_weight(Ly.alpha, m->alpha);
       if ((e = launch_mv(kEpiStore, a)) != cudaSuccess) return e;
       GdnArgs g;
+      g.trace = trace_slot();
       g.S = (int)c.ssm_state;
       g.groups = (int)c.ssm_groups;
       g.values = (int)c.ssm_values;
@@ -678,6 +693,13 @@ int prism_b200_model_create(prism_b200_executor *ex, const prism_b200_qwen35_con
   A(m->stot, (size_t)c.heads * kAttnSplit);
   A(m->apart, (size_t)c.heads * kAttnSplit * c.head_dim);
   A(m->d_sync, 16);
+  {
+    const char *tr = getenv("PRISM_B200_TRACE");
+    if (tr && tr[0] == '1') {
+      m->nseqtrace = 5 * (int)c.layers + 1;
+      A(m->d_seqtrace, (size_t)8 * m->nseqtrace);
+    }
+  }
   A(m->d_hsync, (size_t)(m->nhsync > 0 ? m->nhsync : 1));
   for (uint32_t l = 0; l < c.layers; ++l) {
     ModelLayer &Ly = m->L[l];
@@ -910,7 +932,14 @@ int prism_b200_model_persistent(const prism_b200_model *m) { return m && m->pers
 
 int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t count) {
   if (!m || !ns) return -PRISM_B200_E_INVALID;
-  if (!m->persist) return 0;
+  if (!m->persist) {
+    // the kernel-sequence step's per-launch timelines, when enabled
+    if (!m->d_seqtrace) return 0;
+    const size_t n = std::min(count, (size_t)8 * m->nseqtrace);
+    if (cudaMemcpy(ns, m->d_seqtrace, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
+      return -PRISM_B200_E_DEVICE;
+    return (int64_t)n;
+  }
   const size_t n = std::min(count, (size_t)8 * m->nphases);
   if (cudaMemcpy(ns, m->d_trace, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
     return -PRISM_B200_E_DEVICE;

@@ -159,6 +159,7 @@ struct GdnArgs {
   long out_stride;
   const int *position;     // selects the conv-state buffer (nullptr: buffer 0 -> 1)
   unsigned *status;
+  unsigned long long *trace;  // optional timeline, as MvArgs::trace ([0], [1], [6], [7])
 };
 
 // One CTA per (value head, sequence); 512 threads; S == 128.
@@ -182,10 +183,12 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_decode_kernel(GdnArgs a) {
   float *state = a.state + b * a.state_stride + (long)h * S * S;
   constexpr int RPW = S / (kGdnThreads / 32);  // rows per warp (8)
   float4 srow[RPW];
+  trace_stamp(a.trace, 0);
 #pragma unroll
   for (int i = 0; i < RPW; ++i)
     srow[i] = reinterpret_cast<const float4 *>(state + (long)(warp * RPW + i) * S)[lane];
   grid_dependency_wait();
+  trace_stamp(a.trace, 1);
   grid_dependents_launch();
   const float *mixed = a.mixed + b * a.in_stride;
   const int parity = a.position ? (*a.position & 1) : 0;
@@ -274,6 +277,7 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_decode_kernel(GdnArgs a) {
     const float normed = __fmul_rn(__fmul_rn(ov, nscale), a.norm_w[threadIdx.x]);
     a.attended[b * a.out_stride + h * S + threadIdx.x] = __fmul_rn(normed, silu_f(z));
   }
+  trace_exit(a.trace);
 }
 
 // ---- gated full attention over a binary16 KV cache -------------------------
@@ -297,6 +301,7 @@ struct AttnArgs {
   // > 0: shared-memory offset of the staged K and V rows of a CTA's chunk
   // (attention_decode_kernel); 0: read them from global memory in place
   int kv_smem_off;
+  unsigned long long *trace;  // optional timeline, as MvArgs::trace ([0], [1], [6], [7])
 };
 
 constexpr int kAttnThreads = 256;
@@ -507,6 +512,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
   const int kvw = a.kv_heads * hd;
   const int i = threadIdx.x;
   const int warp = i >> 5, lane = i & 31;
+  trace_stamp(a.trace, 0);
   // The position and the cached rows before it were written by earlier
   // steps, not by the kernels this one depends on: read the position, build
   // the RoPE table and start staging this CTA's K and V rows before the grid
@@ -555,6 +561,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
     cs[2 * i + 1] = sin_cr(angle);
   }
   grid_dependency_wait();
+  trace_stamp(a.trace, 1);
   grid_dependents_launch();
   __syncthreads();
   q[i] = norm_rope_round(a.projected + (long)h * 2 * hd, a.q_norm, a.eps, hd, a.rope_dim, cs,
@@ -658,6 +665,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
     a.attended[(long)h * hd + d] = __fmul_rn(out, sigmoid_f(g));
   }
   cluster.sync();  // peers' shared memory stays live until every read is done
+  trace_exit(a.trace);
 }
 
 }  // namespace prism

@@ -182,14 +182,17 @@ inline cudaError_t launch_matvec_group(uint32_t kind, int epi, MvArgs a, int num
   if (target == 0) {
     a.nbuf = 2;
     const int n = a.nb * 256;
-    const int stage_n = !mv_stage() ? 0 : a.prologue == kProRmsNorm ? 2 * n
-                                        : a.prologue == kProF32     ? n
-                                                                    : 0;
+    const bool gated = a.prologue == kProGated;  // always staged
+    const int stage_n = gated                        ? 2 * n + a.ghd
+                        : !mv_stage()                ? 0
+                        : a.prologue == kProRmsNorm ? 2 * n
+                        : a.prologue == kProF32     ? n
+                                                    : 0;
     // staging must not cost a CTA per SM
     const int plain = MatvecSmem(a.nb, hmax, unit, upt).total();
     const int with = MatvecSmem(a.nb, hmax, unit, upt, 2, stage_n).total();
     const int fit_plain = kSmPerSm / (plain + 1024), fit_with = kSmPerSm / (with + 1024);
-    a.stage = stage_n > 0 && with <= kMaxSmem && (fit_with >= fit_plain || fit_with >= 6);
+    a.stage = gated || (stage_n > 0 && with <= kMaxSmem && (fit_with >= fit_plain || fit_with >= 6));
     smem = a.stage ? with : plain;
     if (smem > kMaxSmem) return cudaErrorInvalidValue;
     int per_sm = kSmPerSm / (smem + 1024);
@@ -214,12 +217,14 @@ inline cudaError_t launch_matvec_group(uint32_t kind, int epi, MvArgs a, int num
     const int per_cta = ntiles <= cap + cap / 4 ? 1 : (int)((ntiles + cap - 1) / cap);
     grid = (ntiles + per_cta - 1) / per_cta;
     const int n = a.nb * 256;
-    int stage_n = a.prologue == kProRmsNorm ? 2 * n : a.prologue == kProF32 ? n : 0;
+    int stage_n = a.prologue == kProGated ? 2 * n + a.ghd
+                  : a.prologue == kProRmsNorm ? 2 * n
+                  : a.prologue == kProF32 ? n : 0;
     const int budget = kSmPerSm / (target + 1) - 2048;
     int nbuf = per_cta;
     auto size = [&](int nbf, int sn) { return MatvecSmem(a.nb, hmax, unit, upt, nbf, sn).total(); };
     while (nbuf > 2 && size(nbuf, stage_n) > budget) --nbuf;
-    if (size(nbuf, stage_n) > budget) stage_n = 0;
+    if (size(nbuf, stage_n) > budget && a.prologue != kProGated) stage_n = 0;
     while (nbuf > 1 && size(nbuf, stage_n) > budget) --nbuf;
     smem = size(nbuf, stage_n);
     if (smem > kMaxSmem) return cudaErrorInvalidValue;

@@ -74,7 +74,10 @@ struct MatvecSmem {
   __host__ __device__ int total() const { return bufs() + nbuf * tile_bytes(); }
 };
 
-enum Prologue : int { kProQ8K = 0, kProF32 = 1, kProRmsNorm = 2 };
+// kProGated: x = RMSNorm(o_h) * w * SiLU(z_h) per head of head_dim values
+// (the Gated DeltaNet output, reference src/kernels.rs:3589-3625 Source),
+// in0 = o, zgate = SiLU(z) (already applied), norm_w = w [head_dim].
+enum Prologue : int { kProQ8K = 0, kProF32 = 1, kProRmsNorm = 2, kProGated = 3 };
 // kEpiSwiglu: w[0] = ffn_up, w[1] = ffn_gate (same geometry); each tile of
 // rows is projected through both and y = up * silu(gate) is stored in
 // w[0].y (reference src/graph.rs:121-131 SwiGLU).
@@ -97,6 +100,8 @@ struct MvArgs {
   int prologue = kProQ8K;
   const void *in0 = nullptr;        // Q8_K AoS | f32 x | f32 x
   const float *norm_w = nullptr;    // kProRmsNorm weight
+  const float *zgate = nullptr;     // kProGated: [heads * head_dim]
+  int gheads = 0, ghd = 0;          // kProGated geometry
   float eps = 0.0f;
   int pinned = 0;                   // pinned Q8_K rounding
   unsigned long long *argmax_key = nullptr;
@@ -360,6 +365,38 @@ __device__ __forceinline__ void prefetch_l2_share(const MvArgs &a) {
   }
 }
 
+// Gated output norm of `heads` heads of S (== 128) values, one warp per
+// head: y = RMSNorm(o_h) * w * g_h with g = SiLU(z) given, the binary64 sum
+// of squares in the order of a 512-thread block sum over the head
+// (gdn_decode_kernel's tail).  y may alias o.
+__device__ __forceinline__ void gated_heads_norm(int heads, int S, float eps, const float *o_all,
+                                                 const float *g_all, const float *w, float *out,
+                                                 float *copy_out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int h = warp; h < heads; h += (int)(blockDim.x >> 5)) {
+    const float *o = o_all + h * S;
+    double t = 0.0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float v = o[32 * q + lane];
+      double sq = (double)__fmul_rn(v, v);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+      t += sq;
+    }
+    const float mean = (float)(t / (double)S);
+    const float nscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = 32 * q + lane;
+      const float normed = __fmul_rn(__fmul_rn(o[i], nscale), w[i]);
+      const float y = __fmul_rn(normed, g_all[h * S + i]);
+      out[h * S + i] = y;
+      if (copy_out) copy_out[h * S + i] = y;
+    }
+  }
+}
+
 // Copy n floats (n % 4 == 0, 16-byte aligned) into shared memory, all
 // threads, every load in flight before the stores.
 __device__ __forceinline__ void load_f32_to_smem(float *dst, const float *src, int n) {
@@ -420,9 +457,13 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
   int hmax = 8;
   for (int g = 0; g < args.count; ++g) hmax = max(hmax, args.w[g].h);
   const int nbuf = args.nbuf, n = nb * 256;
-  const bool staged = args.stage && args.prologue != kProQ8K;
+  const bool gated = args.prologue == kProGated;
+  const bool staged = gated || (args.stage && args.prologue != kProQ8K);
   const MatvecSmem L(nb, hmax, unit_bytes(KIND, hmax), upt, nbuf,
-                     staged ? (args.prologue == kProRmsNorm ? 2 * n : n) : 0);
+                     !staged                          ? 0
+                     : gated                          ? 2 * n + args.ghd
+                     : args.prologue == kProRmsNorm   ? 2 * n
+                                                      : n);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars());  // [nbuf][upt]
   uint8_t *bufs = smem + L.bufs();                                  // [nbuf][tile]
@@ -446,10 +487,20 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
     if (tj < ntiles) issue_group_tile<EPI>(args, KIND, tj, bufs + j * L.tile_bytes(), bars + j * upt);
   }
   if (staged && args.prologue == kProRmsNorm) load_f32_to_smem(xs + n, args.norm_w, n);
+  if (gated) load_f32_to_smem(xs + 2 * n, args.norm_w, args.ghd);
   grid_dependency_wait();
   trace_stamp(args.trace, 1);
   if (args.prologue == kProQ8K) {
     stage_q8k_aos(static_cast<const uint8_t *>(args.in0), L, smem, args.status);
+  } else if (gated) {
+    // o and z in one round of loads, the gated norm in place over o, then
+    // the quantization of the gated vector
+    load_f32_to_smem(xs, static_cast<const float *>(args.in0), n);
+    load_f32_to_smem(xs + n, args.zgate, n);
+    __syncthreads();
+    gated_heads_norm(args.gheads, args.ghd, args.eps, xs, xs + n, xs + 2 * n, xs, nullptr);
+    __syncthreads();
+    stage_from_f32(args, L, smem, xs, nullptr);
   } else if (staged) {
     // the input arrives with one round of loads, then the prologue works
     // from shared memory

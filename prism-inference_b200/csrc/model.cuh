@@ -89,8 +89,12 @@ namespace prism {
 // `context` positions: with the CTA's K and V rows staged when they fit
 // (sets a.kv_smem_off), else the in-place layout.
 inline size_t attn_launch_smem(AttnArgs &a, int context) {
+  static const bool stage_on = [] {
+    const char *e = getenv("PRISM_B200_ATTN_STAGE");  // 0: read rows in place (A/B timing)
+    return !(e && e[0] == '0');
+  }();
   const size_t staged = attn_smem_bytes_staged(a.hd, context, a.q8);
-  if (staged <= (size_t)kMaxSmem &&
+  if (stage_on && staged <= (size_t)kMaxSmem &&
       cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)staged) == cudaSuccess) {
     a.kv_smem_off = (int)attn_smem_bytes(a.hd, context);
@@ -327,17 +331,23 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
       g.conv_stride = 0;
       g.state = Ly.matrix;
       g.state_stride = 0;
-      g.attended = m->attended;
+      g.attended = m->gdn_o;  // pre-norm o; the gated norm is the out-projection's prologue
       g.out_stride = 0;
       g.position = m->d_position;
       g.status = status;
+      // each value head over kGdnSlices CTAs of 16 state rows
       cudaLaunchConfig_t cfg =
-          pdl_config(dim3(c.ssm_values, 1), dim3(kGdnThreads), 0, s, attr, pdl);
-      if ((e = cudaLaunchKernelEx(&cfg, gdn_decode_kernel, g)) != cudaSuccess) return e;
+          pdl_config(dim3(c.ssm_values * kGdnSlices), dim3(kPThreads), 0, s, attr, pdl);
+      if ((e = cudaLaunchKernelEx(&cfg, gdn_slices_kernel, g)) != cudaSuccess) return e;
       ++item;
       MvArgs o;
-      o.prologue = kProF32;
-      o.in0 = m->attended;
+      o.prologue = kProGated;
+      o.in0 = m->gdn_o;
+      o.zgate = m->zgate;  // SiLU(z) after the GDN kernel
+      o.norm_w = Ly.ssm_norm;
+      o.gheads = (int)c.ssm_values;
+      o.ghd = (int)c.ssm_state;
+      o.eps = c.eps;
       o.status = status;
       o.nb = m->value_width() / 256;
       o.count = 1;

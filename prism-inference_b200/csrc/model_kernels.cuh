@@ -442,11 +442,12 @@ __host__ __device__ constexpr int attn_row_bytes(int hd, int q8) {
   return q8 ? q8_0_record_bytes(hd) : hd * 2;
 }
 
-// Shared memory with the chunk's K and V rows staged (placed after the
-// layout above): the launch uses it when it fits.
+// K and V rows stream through two shared-memory buffers of kAttnChunk
+// positions (placed after the layout above): K chunks for the scores, then
+// V chunks for the values.
+constexpr int kAttnChunk = 32;
 __host__ __device__ constexpr size_t attn_smem_bytes_staged(int hd, int context, int q8) {
-  return attn_smem_bytes(hd, context) +
-         2 * (size_t)attn_chunk_cap(context) * (size_t)attn_row_bytes(hd, q8);
+  return attn_smem_bytes(hd, context) + 2 * (size_t)kAttnChunk * (size_t)attn_row_bytes(hd, q8);
 }
 
 // Score of position p from a staged row (lane holds q dims lane*8..+7).
@@ -525,8 +526,27 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
                                        ((size_t)(4 * hd + 64 + per + 1) * 4 + 15) / 16 * 16);
   const bool staged = a.kv_smem_off > 0;
   const int rb = attn_row_bytes(hd, a.q8);
-  uint8_t *kbuf = reinterpret_cast<uint8_t *>(sm) + a.kv_smem_off;
-  uint8_t *vbuf = kbuf + (size_t)per * rb;
+  uint8_t *kvbuf = reinterpret_cast<uint8_t *>(sm) + a.kv_smem_off;  // [2][kAttnChunk][rb]
+  const int nk = (hi - lo + kAttnChunk - 1) / kAttnChunk;  // chunks per pass
+  // chunk g of the pass sequence: K chunks 0..nk-1, then V chunks; warp 0
+  // issues one bulk copy per row (lane = row) into buffer g & 1
+  auto issue = [&](int g) {
+    const bool v = g >= nk;
+    const int p0 = lo + (v ? g - nk : g) * kAttnChunk, count = min(kAttnChunk, hi - p0);
+    uint64_t *bar = &kvbar[g & 1];
+    if (lane == 0) mbar_arrive_expect_tx(bar, (unsigned)(count * rb));
+    __syncwarp();
+    if (lane < count) {
+      const int p = p0 + lane;
+      const size_t at = a.q8 ? ((size_t)p * a.kv_heads + kvh) * rb
+                             : ((size_t)p * kvw + (size_t)kvh * hd) * 2;
+      bulk_g2s(kvbuf + ((size_t)(g & 1) * kAttnChunk + lane) * rb,
+               reinterpret_cast<const uint8_t *>(v ? a.vcache : a.kcache) + at, (unsigned)rb,
+               bar);
+    }
+  };
+  bool landed = true;
+  int issued = 0, waited = 0;  // chunks, identical in every thread
   if (staged) {
     if (i == 0) {
       mbar_init(&kvbar[0], 1);
@@ -534,21 +554,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
       mbar_init_fence();
     }
     __syncthreads();
-    if (warp == 0) {
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&kvbar[0], (unsigned)((hi - lo) * rb));
-        mbar_arrive_expect_tx(&kvbar[1], (unsigned)((hi - lo) * rb));
-      }
-      __syncwarp();
-      for (int p = lo + lane; p < hi; p += 32) {
-        const size_t at = a.q8 ? ((size_t)p * a.kv_heads + kvh) * rb
-                               : ((size_t)p * kvw + (size_t)kvh * hd) * 2;
-        bulk_g2s(kbuf + (size_t)(p - lo) * rb, reinterpret_cast<const uint8_t *>(a.kcache) + at,
-                 (unsigned)rb, &kvbar[0]);
-        bulk_g2s(vbuf + (size_t)(p - lo) * rb, reinterpret_cast<const uint8_t *>(a.vcache) + at,
-                 (unsigned)rb, &kvbar[1]);
-      }
-    }
+    for (int g = 0; g < 2 && g < 2 * nk; ++g, ++issued)
+      if (warp == 0) issue(g);
   }
   if (i < a.rope_dim / 2) {
     // reference src/graph.rs:6406-6437: angle_j = p * theta_scale^j by j
@@ -587,11 +594,26 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
   const float4 q0 = reinterpret_cast<const float4 *>(q)[lane * 2];
   const float4 q1 = reinterpret_cast<const float4 *>(q)[lane * 2 + 1];
   if (staged) {
-    const bool landed = mbar_wait_bounded(&kvbar[0], 0u, a.status);
-    for (int p = lo + warp; p < hi && landed; p += kAttnThreads / 32) {
-      const double s =
-          warp_sum_f64(key_partial_staged(kbuf + (size_t)(p - lo) * rb, hd, a.q8, q0, q1, lane));
-      if (lane == 0) scores[p - lo] = __fmul_rn((float)s, scale);
+    for (int c = 0; c < nk && landed; ++c) {
+      landed = __syncthreads_and(mbar_wait_bounded(&kvbar[c & 1], (unsigned)(c >> 1) & 1u,
+                                                   a.status));
+      if (!landed) break;
+      ++waited;
+      const int p0 = lo + c * kAttnChunk, count = min(kAttnChunk, hi - p0);
+      const uint8_t *rows = kvbuf + (size_t)(c & 1) * kAttnChunk * rb;
+      for (int pp = warp; pp < count; pp += kAttnThreads / 32) {
+        const double s =
+            warp_sum_f64(key_partial_staged(rows + (size_t)pp * rb, hd, a.q8, q0, q1, lane));
+        if (lane == 0) scores[p0 + pp - lo] = __fmul_rn((float)s, scale);
+      }
+      __syncthreads();  // the buffer is free again
+      if (c + 2 < 2 * nk) {
+        if (warp == 0) {
+          fence_proxy_async_smem();
+          issue(c + 2);
+        }
+        ++issued;
+      }
     }
   } else {
     for (int p = lo + warp; p < hi; p += kAttnThreads / 32) {
@@ -634,11 +656,32 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
   // value partial sums of this chunk: one dimension per thread, position order
   if (staged) {
     double acc = -0.0;
-    if (mbar_wait_bounded(&kvbar[1], 0u, a.status))
-      for (int p = lo; p < hi; ++p)
-        acc += (double)__fmul_rn(scores[p - lo],
-                                 value_staged(vbuf + (size_t)(p - lo) * rb, hd, a.q8, i));
+    for (int c = 0; c < nk && landed; ++c) {
+      const int g = nk + c;
+      landed = __syncthreads_and(mbar_wait_bounded(&kvbar[g & 1], (unsigned)(g >> 1) & 1u,
+                                                   a.status));
+      if (!landed) break;
+      ++waited;
+      const int p0 = lo + c * kAttnChunk, count = min(kAttnChunk, hi - p0);
+      const uint8_t *rows = kvbuf + (size_t)(g & 1) * kAttnChunk * rb;
+      for (int pp = 0; pp < count; ++pp)
+        acc += (double)__fmul_rn(scores[p0 + pp - lo],
+                                 value_staged(rows + (size_t)pp * rb, hd, a.q8, i));
+      __syncthreads();
+      if (g + 2 < 2 * nk) {
+        if (warp == 0) {
+          fence_proxy_async_smem();
+          issue(g + 2);
+        }
+        ++issued;
+      }
+    }
     partial[i] = acc;
+    // a chunk that never landed: let the copies still in flight finish
+    // (bounded) before the CTA exits
+    if (issued > waited && i == 0)
+      for (int g = waited; g < issued; ++g)
+        mbar_wait_bounded(&kvbar[g & 1], (unsigned)(g >> 1) & 1u, a.status);
   } else {
     double acc = -0.0;
     int p = lo;

@@ -514,7 +514,8 @@ __device__ bool run_matvec(const PMatvec &mv, const PersistArgs &pa, uint8_t *sm
 // Gated DeltaNet layer, value head h split over kGdnSlices CTAs of 16 state
 // rows (arithmetic of gdn_decode_kernel; the output norm runs in the next
 // projection's prologue).  o (pre-norm) goes to a.attended.
-__device__ void run_gdn(const GdnArgs &a, int pos, uint8_t *scratch) {
+__device__ void run_gdn(const GdnArgs &a, int pos, uint8_t *scratch,
+                        const float4 *preloaded = nullptr) {
   constexpr int S = 128, R = S / kGdnSlices;
   if ((int)blockIdx.x >= a.values * kGdnSlices) return;
   float *q = reinterpret_cast<float *>(scratch);  // [S]
@@ -577,7 +578,7 @@ __device__ void run_gdn(const GdnArgs &a, int pos, uint8_t *scratch) {
     const float4 kk = reinterpret_cast<const float4 *>(k)[lane];
     const float4 qq = reinterpret_cast<const float4 *>(q)[lane];
     float *row = a.state + (long)h * S * S + (long)r * S;
-    float4 s = reinterpret_cast<const float4 *>(row)[lane];
+    float4 s = preloaded ? *preloaded : reinterpret_cast<const float4 *>(row)[lane];
     s.x = __fmul_rn(decay, s.x);
     s.y = __fmul_rn(decay, s.y);
     s.z = __fmul_rn(decay, s.z);
@@ -599,6 +600,34 @@ __device__ void run_gdn(const GdnArgs &a, int pos, uint8_t *scratch) {
     if (lane == 0) a.attended[h * S + r] = __fmul_rn((float)dq, oscale);
     if (!__all_sync(0xffffffffu, finite) && lane == 0) report(a.status, kStatusNonfinite);
   }
+}
+
+// The kernel-sequence step's Gated DeltaNet layer: value head h split over
+// kGdnSlices CTAs of 16 state rows (grid values * kGdnSlices, kPThreads
+// threads), run_gdn's arithmetic.  Pre-norm o goes to a.attended; the gated
+// output norm runs in the out-projection's prologue (kProGated), for which
+// each CTA replaces its 16 z values by SiLU(z) in place.  The state row was
+// written by this layer's previous step: it is loaded before the grid
+// dependency.
+__global__ void __launch_bounds__(kPThreads) gdn_slices_kernel(GdnArgs a) {
+  constexpr int S = 128, R = S / kGdnSlices;
+  __shared__ __align__(16) uint8_t scratch[2048];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x / kGdnSlices, slice = blockIdx.x % kGdnSlices;
+  trace_stamp(a.trace, 0);
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (warp < R && h < a.values)
+    s = reinterpret_cast<const float4 *>(a.state + (long)h * S * S +
+                                         (long)(slice * R + warp) * S)[lane];
+  grid_dependency_wait();
+  trace_stamp(a.trace, 1);
+  grid_dependents_launch();
+  run_gdn(a, *a.position, scratch, &s);
+  if (threadIdx.x < R && h < a.values) {
+    float *z = const_cast<float *>(a.zgate) + (long)h * S + slice * R + threadIdx.x;
+    *z = silu_f(*z);
+  }
+  trace_exit(a.trace);
 }
 
 // RMSNorm(x)*w, RoPE, binary16 rounding over hd (== 256) values; threads at

@@ -67,7 +67,9 @@ struct MatvecSmem {
   __host__ __device__ int act_asum() const { return act_sums() + nb * 32; }
   __host__ __device__ int red() const { return (act_asum() + nb * 4 + 15) / 16 * 16; }
   __host__ __device__ int terms() const { return red() + kWarps * 16; }
-  __host__ __device__ int bars() const { return (terms() + upt * h * 4 + 15) / 16 * 16; }
+  // terms are double-buffered: one tile's chains run while the next tile's
+  // dots fill the other buffer
+  __host__ __device__ int bars() const { return (terms() + 2 * upt * h * 4 + 15) / 16 * 16; }
   __host__ __device__ int stage() const { return (bars() + nbuf * upt * 8 + 15) / 16 * 16; }
   __host__ __device__ int bufs() const { return (stage() + stage_n * 4 + 127) / 128 * 128; }
   __host__ __device__ int tile_bytes() const { return upt * unit; }
@@ -467,7 +469,7 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars());  // [nbuf][upt]
   uint8_t *bufs = smem + L.bufs();                                  // [nbuf][tile]
-  float *terms = reinterpret_cast<float *>(smem + L.terms());       // [upt][H]
+  float *terms2 = reinterpret_cast<float *>(smem + L.terms());      // [2][upt][H]
   float *xs = reinterpret_cast<float *>(smem + L.stage());          // [n] x, [n] norm weight
   const int ntiles = PAIR ? args.w[0].ntiles : args.tile_start[args.count];
   trace_stamp(args.trace, 0);
@@ -534,6 +536,7 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
     const int lt = t - (PAIR ? 0 : args.tile_start[g]);
     const int r = lane % H;
     const int row = lt * H + r;
+    float *terms = terms2 + (it & 1) * upt * hmax;
     for (int u = warp; u < upt; u += kWarps) {
       if (!mbar_wait_bounded(&bk[u], parity, args.status)) {
         ok = false;
@@ -562,8 +565,16 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
         }
       }
     }
+    // the tile's terms are complete and its data consumed: refill the
+    // buffer with the tile nbuf steps ahead, then run the chains (threads
+    // below H) while the other warps go on to the next tile's dots
     if (!__syncthreads_and(ok)) break;
     if (it == 0) trace_stamp(args.trace, 4);
+    const int tn = t + nbuf * (int)gridDim.x;
+    if (tn < ntiles) {
+      fence_proxy_async_smem();
+      issue_group_tile<EPI>(args, KIND, tn, buf, bk);
+    }
     if (EPI != kEpiInts && threadIdx.x < H) {
       // the reference's chain: sum = 0; sum += term_b for b in order
       float sum = 0.0f;
@@ -587,14 +598,7 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(MvArgs args) {
         }
       }
     }
-    __syncthreads();
     if (it == 0) trace_stamp(args.trace, 5);
-    // refill this buffer with the tile nbuf steps ahead
-    const int tn = t + nbuf * (int)gridDim.x;
-    if (tn < ntiles) {
-      fence_proxy_async_smem();
-      issue_group_tile<EPI>(args, KIND, tn, buf, bk);
-    }
   }
   if (EPI == kEpiArgmax) {
 #pragma unroll

@@ -144,8 +144,9 @@ inline cudaError_t init_matvec_attributes() {
 // small CTAs overlap better than fewer CTAs with deeper tile queues, even
 // though every CTA rebuilds the Q8_K activation.  PRISM_B200_MV_PER_SM=k
 // (1..6) instead aims for k CTAs per SM with all of a CTA's tiles in flight
-// (A/B timing).  PRISM_B200_MV_STAGE=0 reads the f32 input in place instead
-// of staging it in shared memory with one round of loads.
+// (A/B timing).  PRISM_B200_MV_STAGE=1 stages the f32 input in shared memory
+// with one round of loads instead of reading it in place (measured neutral;
+// the gated-norm prologue always stages).
 inline int mv_per_sm() {
   static const int v = [] {
     const char *e = getenv("PRISM_B200_MV_PER_SM");
@@ -157,7 +158,7 @@ inline int mv_per_sm() {
 inline bool mv_stage() {
   static const bool v = [] {
     const char *e = getenv("PRISM_B200_MV_STAGE");
-    return !(e && e[0] == '0');
+    return e && e[0] == '1';
   }();
   return v;
 }
@@ -188,23 +189,25 @@ inline cudaError_t launch_matvec_group(uint32_t kind, int epi, MvArgs a, int num
                         : a.prologue == kProRmsNorm ? 2 * n
                         : a.prologue == kProF32     ? n
                                                     : 0;
-    // staging must not cost a CTA per SM
+    // resident CTAs per SM (shared memory and registers): a grid beyond
+    // them runs in a second wave instead of looping over tiles
+    auto resident = [&](int bytes) {
+      int per_sm = kSmPerSm / (bytes + 1024);
+      if (per_sm > 6) per_sm = 6;
+      int occ = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, matvec_kernel_ptr(kind, epi),
+                                                        kThreads, (size_t)bytes) == cudaSuccess &&
+          occ > 0 && occ < per_sm)
+        per_sm = occ;
+      return per_sm < 1 ? 1 : per_sm;
+    };
+    // staging must not cost a resident CTA per SM
     const int plain = MatvecSmem(a.nb, hmax, unit, upt).total();
     const int with = MatvecSmem(a.nb, hmax, unit, upt, 2, stage_n).total();
-    const int fit_plain = kSmPerSm / (plain + 1024), fit_with = kSmPerSm / (with + 1024);
-    a.stage = gated || (stage_n > 0 && with <= kMaxSmem && (fit_with >= fit_plain || fit_with >= 6));
+    a.stage = gated || (stage_n > 0 && with <= kMaxSmem && resident(with) >= resident(plain));
     smem = a.stage ? with : plain;
     if (smem > kMaxSmem) return cudaErrorInvalidValue;
-    int per_sm = kSmPerSm / (smem + 1024);
-    if (per_sm > 6) per_sm = 6;
-    // registers cap the resident CTAs too: a grid beyond them runs in a
-    // second wave instead of looping over tiles
-    int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, matvec_kernel_ptr(kind, epi), kThreads,
-                                                      (size_t)smem) == cudaSuccess &&
-        occ > 0 && occ < per_sm)
-      per_sm = occ;
-    if (per_sm < 1) per_sm = 1;
+    const int per_sm = resident(smem);
     const long cap = (long)per_sm * num_sms;
     grid = (int)(ntiles < cap ? ntiles : cap);
   } else {

@@ -34,6 +34,7 @@ constexpr int kServeChunk = 64;   // positions per streamed chunk
 constexpr int kServeThreads = 256;
 constexpr int kServeGroup = 4;    // largest query-head group
 constexpr int kServePage = 32;    // positions per interleaved K page
+static_assert(kServeThreads == 4 * kServeChunk, "K pass: four lanes per chunk position");
 
 // Byte offsets, inside a K page of `hd`-dimensional rows, of position slot
 // `lane`'s scale of block `blk` and its code of dimension `d`.
@@ -53,10 +54,12 @@ __host__ __device__ constexpr int serve_cap(int context) {
   return (context + kServeSplit - 1) / kServeSplit + 1;
 }
 
-// Shared memory: q[G][hd], kc, vc, buf [hd], cs[64], scores[G][cap] (f32);
-// two chunk buffers; partial[G][hd] (f64); two mbarriers.
+// Shared memory: q[G][hd], kc, vc, buf [hd], cs[64], scores[G][cap],
+// qr[G][4][hd/4] (q regrouped by dimension residue mod 4) (f32); two chunk
+// buffers; partial[G][hd] (f64); two mbarriers.
 __host__ __device__ constexpr size_t serve_offset_chunks(int hd, int context) {
-  return ((size_t)(kServeGroup * hd + 3 * hd + 64 + kServeGroup * serve_cap(context)) * 4 + 127) /
+  return ((size_t)(2 * kServeGroup * hd + 3 * hd + 64 + kServeGroup * serve_cap(context)) * 4 +
+          127) /
          128 * 128;
 }
 __host__ __device__ constexpr size_t serve_offset_partial(int hd, int context) {
@@ -93,6 +96,7 @@ __global__ void __launch_bounds__(kServeThreads) attention_serve_kernel(ServeArg
   float *buf = vc + hd;
   float *cs = buf + hd;                        // [64]
   float *scores = cs + 64;                     // [G][cap]
+  float *qr = scores + kServeGroup * cap;      // [G][4][hd/4]: qr[j][e][w] = q[j][4w+e]
   uint8_t *chunks = ssm + serve_offset_chunks(hd, sa.context);
   double *partial = reinterpret_cast<double *>(ssm + serve_offset_partial(hd, sa.context));
   uint64_t *bars = reinterpret_cast<uint64_t *>(partial + kServeGroup * hd);
@@ -139,9 +143,12 @@ __global__ void __launch_bounds__(kServeThreads) attention_serve_kernel(ServeArg
     cs[2 * i + 1] = sin_cr(angle);
   }
   __syncthreads();
-  for (int j = 0; j < G; ++j)
-    q[j * hd + i] = norm_rope_round(a.projected + (long)(kvh * G + j) * 2 * hd, a.q_norm, a.eps,
-                                    hd, a.rope_dim, cs, buf, red);
+  for (int j = 0; j < G; ++j) {
+    const float qv = norm_rope_round(a.projected + (long)(kvh * G + j) * 2 * hd, a.q_norm, a.eps,
+                                     hd, a.rope_dim, cs, buf, red);
+    q[j * hd + i] = qv;
+    qr[(j * 4 + (i & 3)) * (hd / 4) + (i >> 2)] = qv;
+  }
   kc[i] = norm_rope_round(a.key_in + (long)kvh * hd, a.k_norm, a.eps, hd, a.rope_dim, cs, buf,
                           red);
   vc[i] = round_f16(a.value_in[kvh * hd + i]);
@@ -167,7 +174,11 @@ __global__ void __launch_bounds__(kServeThreads) attention_serve_kernel(ServeArg
     for (int d = 0; d < hd; ++d) s += (double)__fmul_rn(q[i * hd + d], kc[d]);
     s_cur[i] = __fmul_rn((float)s, scale);
   }
-  // K pass: thread t scores position t % 64 of each chunk for head t / 64
+  // K pass: thread t takes position t / 4 of each chunk and dimension
+  // residue e = t % 4 for every head of the group, so that each dequantized
+  // key value serves all G heads; the four residues' binary64 partial sums
+  // (dimensions d = 4w + e in order) meet over the four lanes of the
+  // position as (s0 + s1) + (s2 + s3)
   const int nb32 = hd / 32;
   // A chunk that never lands (bounded wait) stops the passes but not the
   // cluster barriers: every CTA of the cluster reaches each cluster.sync.
@@ -176,33 +187,49 @@ __global__ void __launch_bounds__(kServeThreads) attention_serve_kernel(ServeArg
     ok = __syncthreads_and(ok);
     if (!ok) break;
     const int count = min(kServeChunk, n - c * kServeChunk);
-    const int j = i / kServeChunk, pp = i % kServeChunk;
-    if (j < G && pp < count) {
-      // warp = (head, page): lane `slot` reads consecutive words of the page
+    {
+      const int pp = i >> 2, e = i & 3;
+      // lanes (position, residue): the 4 residues of a position share a
+      // word; 8 positions per warp read consecutive words of the page
       const uint8_t *page = chunks + (c & 1) * kServeChunk * rb + (pp / kServePage) * kServePage * rb;
       const int slot = pp % kServePage;
-      const float4 *qj = reinterpret_cast<const float4 *>(q + j * hd);
-      // four binary64 partial sums (dimensions d = 4w + e by e), combined
-      // pairwise: independent chains for the scheduler, the sums of binary32
-      // products still in binary64
-      double s[4] = {-0.0, -0.0, -0.0, -0.0};
+      double s[kServeGroup];
+#pragma unroll
+      for (int j = 0; j < kServeGroup; ++j) s[j] = -0.0;
       for (int blk = 0; blk < nb32; ++blk) {
         const float d =
             half_bits_to_float(*reinterpret_cast<const uint16_t *>(page + kpage_scale(hd, blk, slot)));
+        float k[8];
 #pragma unroll
         for (int w = 0; w < 8; ++w) {
           const uint32_t word =
               *reinterpret_cast<const uint32_t *>(page + kpage_code(hd, blk * 32 + 4 * w, slot));
-          const float4 qv = qj[blk * 8 + w];
-          const float qq[4] = {qv.x, qv.y, qv.z, qv.w};
+          k[w] = __fmul_rn(d, (float)(int8_t)(word >> (8 * e)));
+        }
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float k = __fmul_rn(d, (float)(int8_t)(word >> (8 * e)));
-            s[e] += (double)__fmul_rn(qq[e], k);
+        for (int j = 0; j < kServeGroup; ++j) {
+          if (j < G) {
+            const float4 *qe = reinterpret_cast<const float4 *>(qr + (j * 4 + e) * (hd / 4) + blk * 8);
+            const float4 qa = qe[0], qb = qe[1];
+            s[j] += (double)__fmul_rn(qa.x, k[0]);
+            s[j] += (double)__fmul_rn(qa.y, k[1]);
+            s[j] += (double)__fmul_rn(qa.z, k[2]);
+            s[j] += (double)__fmul_rn(qa.w, k[3]);
+            s[j] += (double)__fmul_rn(qb.x, k[4]);
+            s[j] += (double)__fmul_rn(qb.y, k[5]);
+            s[j] += (double)__fmul_rn(qb.z, k[6]);
+            s[j] += (double)__fmul_rn(qb.w, k[7]);
           }
         }
       }
-      scores[j * cap + c * kServeChunk + pp] = __fmul_rn((float)((s[0] + s[1]) + (s[2] + s[3])), scale);
+#pragma unroll
+      for (int j = 0; j < kServeGroup; ++j) {
+        const double v1 = __shfl_down_sync(0xffffffffu, s[j], 1);
+        const double v2 = __shfl_down_sync(0xffffffffu, s[j], 2);
+        const double v3 = __shfl_down_sync(0xffffffffu, s[j], 3);
+        if (j < G && e == 0 && pp < count)
+          scores[j * cap + c * kServeChunk + pp] = __fmul_rn((float)((s[j] + v1) + (v2 + v3)), scale);
+      }
     }
     __syncthreads();  // the chunk buffer is free
     if (i == 0 && c + 2 < 2 * nchunks) {

@@ -35,6 +35,7 @@ __device__ __forceinline__ double gdn_warp_sum(double v) {
 // of one (sequence, head); a warp updates one row at a time with binary32
 // products summed in binary64 (the reference's float_dot), unfused updates.
 constexpr int kGdnStepThreads = 256;
+constexpr int kGdnRowBatch = 4;  // state rows a warp loads at once
 
 __global__ void __launch_bounds__(kGdnStepThreads) gdn_step_kernel(GdnBatchArgs a) {
   constexpr int D = 128;
@@ -55,8 +56,20 @@ __global__ void __launch_bounds__(kGdnStepThreads) gdn_step_kernel(GdnBatchArgs 
   const float oscale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
   float *state = a.state + ((long)b * a.heads + h) * D * D;
   bool finite = true;
-  for (int r = r0 + warp; r < r0 + rows; r += kGdnStepThreads / 32) {
-    float4 s = reinterpret_cast<const float4 *>(state + (long)r * D)[lane];
+  // a warp's rows r = r0 + warp + 8i: up to kGdnRowBatch of them are loaded
+  // together, so their HBM latencies overlap
+  constexpr int W = kGdnStepThreads / 32;
+  for (int rb = r0 + warp; rb < r0 + rows; rb += W * kGdnRowBatch) {
+    float4 sr[kGdnRowBatch];
+#pragma unroll
+    for (int i = 0; i < kGdnRowBatch; ++i)
+      if (rb + W * i < r0 + rows)
+        sr[i] = reinterpret_cast<const float4 *>(state + (long)(rb + W * i) * D)[lane];
+#pragma unroll
+    for (int i = 0; i < kGdnRowBatch; ++i) {
+    const int r = rb + W * i;
+    if (r >= r0 + rows) break;
+    float4 s = sr[i];
     s.x = __fmul_rn(decay, s.x);
     s.y = __fmul_rn(decay, s.y);
     s.z = __fmul_rn(decay, s.z);
@@ -75,6 +88,7 @@ __global__ void __launch_bounds__(kGdnStepThreads) gdn_step_kernel(GdnBatchArgs 
     dq = gdn_warp_sum(dq);
     reinterpret_cast<float4 *>(state + (long)r * D)[lane] = s;
     if (lane == 0) a.out[hv + r] = __fmul_rn((float)dq, oscale);
+    }
   }
   if (!__all_sync(0xffffffffu, finite) && lane == 0) report(a.status, kStatusNonfinite);
 }

@@ -477,8 +477,9 @@ extern "C" int prism_b200_gdn_decode_device(prism_b200_executor *ex, int batch, 
   a.beta = beta;
   a.out = out;
   a.status = ex->d_status;
-  // split each head's 128 rows so that the grid covers every SM twice
-  int split = 1;
+  // split each head's 128 rows so that the grid covers every SM twice and a
+  // warp holds at most kGdnRowBatch rows (one round of loads)
+  int split = 128 / (kGdnStepThreads / 32 * kGdnRowBatch);
   while (split < 16 && (long)batch * heads * split < 2L * ex->num_sms) split *= 2;
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_config(dim3(split, heads, batch), dim3(kGdnStepThreads), 0,

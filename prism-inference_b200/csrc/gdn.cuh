@@ -233,8 +233,8 @@ constexpr int kScanThreads = 256;
 
 template <int R>
 __host__ __device__ constexpr size_t gdn_scan_smem() {
-  // S[R][D] K,Q[C][kKS] M[C][kMS] CQ[C][C] V[C][R] KD,QD,DL[R][C+1] cum plast
-  return (size_t)(R * kGdnD + 2 * kChunk * kKS + kChunk * kMS + kChunk * kChunk + kChunk * R +
+  // S[R][D] K,Q[C][kKS] M[C][kMS] CQ[C][kMS] V[C][R] KD,QD,DL[R][C+1] cum plast
+  return (size_t)(R * kGdnD + 2 * kChunk * kKS + 2 * kChunk * kMS + kChunk * R +
                   3 * R * (kChunk + 1) + 2 * kChunk) * 4;
 }
 
@@ -246,8 +246,8 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
   float *K = S + R * D;          // [C][kKS]
   float *Q = K + C * kKS;        // [C][kKS]
   float *M = Q + C * kKS;        // [C][kMS]
-  float *CQ = M + C * kMS;       // [C][C]
-  float *V = CQ + C * C;         // [C][R]
+  float *CQ = M + C * kMS;       // [C][kMS]
+  float *V = CQ + C * kMS;       // [C][R]
   float *KD = V + C * R;         // [R][C+1]
   float *QD = KD + R * CP;       // [R][C+1]
   float *DL = QD + R * CP;       // [R][C+1]  deltas
@@ -281,9 +281,10 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
       reinterpret_cast<float4 *>(K + t * kKS)[col] = kv;
       reinterpret_cast<float4 *>(Q + t * kKS)[col] = qv;
     }
-    for (int i = tid; i < C * C / 4; i += blockDim.x)
-      reinterpret_cast<float4 *>(CQ)[i] = reinterpret_cast<const float4 *>(scr + C * C)[i];
-    for (int i = tid; i < C * C; i += blockDim.x) M[(i / C) * kMS + i % C] = scr[i];
+    for (int i = tid; i < C * C; i += blockDim.x) {
+      M[(i / C) * kMS + i % C] = scr[i];
+      CQ[(i / C) * kMS + i % C] = scr[C * C + i];
+    }
     for (int i = tid; i < C * R; i += blockDim.x) {
       const int t = i / R, r = i % R;
       V[i] = t < n ? a.v[(((long)b * a.T + t0 + t) * a.heads + h) * D + r0 + r] : 0.0f;
@@ -293,54 +294,147 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
       plast[t] = scr[2 * C * C + C + t];
     }
     __syncthreads();
+    // Register tiles: thread (ti, tj) = (tid / 16, tid % 16) owns rows
+    // r = ti + 16a (a < TR) and tokens t = tj + 16b (b < TT); every output
+    // keeps the accumulation order of the one-output-per-thread form.
+    constexpr int TR = R / 16, TT = C / 16;
+    const int ti = tid / 16, tj = tid % 16;
     // KD[r][t] = S_r . k_t, QD[r][t] = S_r . q_t
-    for (int i = tid; i < R * C; i += blockDim.x) {
-      const int r = i / C, t = i % C;
-      const float4 *sr = reinterpret_cast<const float4 *>(S + r * D);
-      const float4 *kt = reinterpret_cast<const float4 *>(K + t * kKS);
-      const float4 *qt = reinterpret_cast<const float4 *>(Q + t * kKS);
-      float dk = 0.0f, dq = 0.0f;
-#pragma unroll 4
+    {
+      float dk[TR][TT], dq[TR][TT];
+#pragma unroll
+      for (int ai = 0; ai < TR; ++ai)
+#pragma unroll
+        for (int bi = 0; bi < TT; ++bi) dk[ai][bi] = dq[ai][bi] = 0.0f;
+#pragma unroll 2
       for (int x = 0; x < D / 4; ++x) {
-        const float4 s = sr[x], u = kt[x], w = qt[x];
-        dk = fmaf(s.x, u.x, fmaf(s.y, u.y, fmaf(s.z, u.z, fmaf(s.w, u.w, dk))));
-        dq = fmaf(s.x, w.x, fmaf(s.y, w.y, fmaf(s.z, w.z, fmaf(s.w, w.w, dq))));
+        float4 sv[TR], kv[TT], qv[TT];
+#pragma unroll
+        for (int ai = 0; ai < TR; ++ai) sv[ai] = reinterpret_cast<const float4 *>(S + (ti + 16 * ai) * D)[x];
+#pragma unroll
+        for (int bi = 0; bi < TT; ++bi) {
+          kv[bi] = reinterpret_cast<const float4 *>(K + (tj + 16 * bi) * kKS)[x];
+          qv[bi] = reinterpret_cast<const float4 *>(Q + (tj + 16 * bi) * kKS)[x];
+        }
+#pragma unroll
+        for (int ai = 0; ai < TR; ++ai)
+#pragma unroll
+          for (int bi = 0; bi < TT; ++bi) {
+            const float4 sr = sv[ai], u = kv[bi], w = qv[bi];
+            dk[ai][bi] = fmaf(sr.x, u.x, fmaf(sr.y, u.y, fmaf(sr.z, u.z, fmaf(sr.w, u.w, dk[ai][bi]))));
+            dq[ai][bi] = fmaf(sr.x, w.x, fmaf(sr.y, w.y, fmaf(sr.z, w.z, fmaf(sr.w, w.w, dq[ai][bi]))));
+          }
       }
-      KD[r * CP + t] = dk;
-      QD[r * CP + t] = dq;
-    }
-    __syncthreads();
-    // W[r][t] = v_rt - cum_t KD[r][t]  (in place into KD)
-    for (int i = tid; i < R * C; i += blockDim.x) {
-      const int r = i / C, t = i % C;
-      KD[r * CP + t] = V[t * R + r] - cum[t] * KD[r * CP + t];
+#pragma unroll
+      for (int ai = 0; ai < TR; ++ai)
+#pragma unroll
+        for (int bi = 0; bi < TT; ++bi) {
+          const int r = ti + 16 * ai, t = tj + 16 * bi;
+          // W[r][t] = v_rt - cum_t KD[r][t]  (into KD)
+          KD[r * CP + t] = V[t * R + r] - cum[t] * dk[ai][bi];
+          QD[r * CP + t] = dq[ai][bi];
+        }
     }
     __syncthreads();
     // delta[r][t] = sum_{j<=t} M[t][j] W[r][j]
-    for (int i = tid; i < R * C; i += blockDim.x) {
-      const int r = i / C, t = i % C;
-      float s = 0.0f;
-      for (int j = 0; j <= t; ++j) s = fmaf(M[t * kMS + j], KD[r * CP + j], s);
-      DL[r * CP + t] = t < n ? s : 0.0f;
+    {
+      float acc[TR][TT];
+#pragma unroll
+      for (int ai = 0; ai < TR; ++ai)
+#pragma unroll
+        for (int bi = 0; bi < TT; ++bi) acc[ai][bi] = 0.0f;
+      const int tmax = tj + 16 * (TT - 1);
+      for (int j = 0; j <= tmax; ++j) {
+        float wv[TR], mv[TT];
+#pragma unroll
+        for (int ai = 0; ai < TR; ++ai) wv[ai] = KD[(ti + 16 * ai) * CP + j];
+#pragma unroll
+        for (int bi = 0; bi < TT; ++bi) mv[bi] = M[(tj + 16 * bi) * kMS + j];
+#pragma unroll
+        for (int bi = 0; bi < TT; ++bi)
+          if (j <= tj + 16 * bi)
+#pragma unroll
+            for (int ai = 0; ai < TR; ++ai) acc[ai][bi] = fmaf(mv[bi], wv[ai], acc[ai][bi]);
+      }
+#pragma unroll
+      for (int ai = 0; ai < TR; ++ai)
+#pragma unroll
+        for (int bi = 0; bi < TT; ++bi) {
+          const int t = tj + 16 * bi;
+          DL[(ti + 16 * ai) * CP + t] = t < n ? acc[ai][bi] : 0.0f;
+        }
     }
     __syncthreads();
-    // o[r][t] = (cum_t QD[r][t] + sum_{j<=t} CQ[t][j] delta[r][j]) / sqrt(d)
+    // o[r][t] = (cum_t QD[r][t] + sum_{j<=t} CQ[t][j] delta[r][j]) / sqrt(d),
+    // staged as [t][r] in the KD area (free now) for coalesced stores
+    {
+      float acc[TR][TT];
+#pragma unroll
+      for (int ai = 0; ai < TR; ++ai)
+#pragma unroll
+        for (int bi = 0; bi < TT; ++bi)
+          acc[ai][bi] = cum[tj + 16 * bi] * QD[(ti + 16 * ai) * CP + tj + 16 * bi];
+      const int tmax = tj + 16 * (TT - 1);
+      for (int j = 0; j <= tmax; ++j) {
+        float dv[TR], cv[TT];
+#pragma unroll
+        for (int ai = 0; ai < TR; ++ai) dv[ai] = DL[(ti + 16 * ai) * CP + j];
+#pragma unroll
+        for (int bi = 0; bi < TT; ++bi) cv[bi] = CQ[(tj + 16 * bi) * kMS + j];
+#pragma unroll
+        for (int bi = 0; bi < TT; ++bi)
+          if (j <= tj + 16 * bi)
+#pragma unroll
+            for (int ai = 0; ai < TR; ++ai) acc[ai][bi] = fmaf(cv[bi], dv[ai], acc[ai][bi]);
+      }
+      float *O = KD;  // [C][R]
+#pragma unroll
+      for (int ai = 0; ai < TR; ++ai)
+#pragma unroll
+        for (int bi = 0; bi < TT; ++bi)
+          O[(tj + 16 * bi) * R + ti + 16 * ai] = acc[ai][bi] * oscale;
+    }
+    __syncthreads();
     for (int i = tid; i < R * C; i += blockDim.x) {
       const int t = i / R, r = i % R;  // r fastest: coalesced output stores
-      if (t < n) {
-        float s = cum[t] * QD[r * CP + t];
-        for (int j = 0; j <= t; ++j) s = fmaf(CQ[t * C + j], DL[r * CP + j], s);
-        a.out[(((long)b * a.T + t0 + t) * a.heads + h) * D + r0 + r] = s * oscale;
-      }
+      if (t < n) a.out[(((long)b * a.T + t0 + t) * a.heads + h) * D + r0 + r] = KD[t * R + r];
     }
-    // S_r <- cum_last S_r + sum_j plast_j delta_rj k_j
-    const float last = cum[n - 1];
-    for (int i = tid; i < R * D; i += blockDim.x) {
-      const int r = i / D, x = i % D;
-      float s = last * S[i];
-      for (int j = 0; j < n; ++j) s = fmaf(plast[j] * DL[r * CP + j], K[j * kKS + x], s);
-      finite &= is_finite_f(s);
-      S[i] = s;
+    // S_r <- cum_last S_r + sum_j plast_j delta_rj k_j; thread (ti, tj)
+    // owns rows r = ti + 16a and columns x = 8 tj .. 8 tj + 7
+    {
+      const float last = cum[n - 1];
+      float acc[TR][8];
+#pragma unroll
+      for (int ai = 0; ai < TR; ++ai) {
+        const float4 s0 = reinterpret_cast<const float4 *>(S + (ti + 16 * ai) * D + 8 * tj)[0];
+        const float4 s1 = reinterpret_cast<const float4 *>(S + (ti + 16 * ai) * D + 8 * tj)[1];
+        acc[ai][0] = last * s0.x; acc[ai][1] = last * s0.y;
+        acc[ai][2] = last * s0.z; acc[ai][3] = last * s0.w;
+        acc[ai][4] = last * s1.x; acc[ai][5] = last * s1.y;
+        acc[ai][6] = last * s1.z; acc[ai][7] = last * s1.w;
+      }
+      for (int j = 0; j < n; ++j) {
+        float cf[TR];
+#pragma unroll
+        for (int ai = 0; ai < TR; ++ai) cf[ai] = plast[j] * DL[(ti + 16 * ai) * CP + j];
+        const float4 k0 = reinterpret_cast<const float4 *>(K + j * kKS + 8 * tj)[0];
+        const float4 k1 = reinterpret_cast<const float4 *>(K + j * kKS + 8 * tj)[1];
+        const float kx[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+        for (int ai = 0; ai < TR; ++ai)
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) acc[ai][c8] = fmaf(cf[ai], kx[c8], acc[ai][c8]);
+      }
+      __syncthreads();  // every thread has read S before it is overwritten
+#pragma unroll
+      for (int ai = 0; ai < TR; ++ai) {
+        float *sr = S + (ti + 16 * ai) * D + 8 * tj;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          finite &= is_finite_f(acc[ai][c8]);
+          sr[c8] = acc[ai][c8];
+        }
+      }
     }
   }
   __syncthreads();

@@ -181,45 +181,66 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefill
   // CK (strict lower) scaled by beta_t into Bm, CQ (lower) to scratch
   float *scr = p.scratch + (((long)b * a.heads + h) * p.nchunks + c) * kChunkScratch;
   float *Mout = scr, *CQout = scr + C * C, *cumout = scr + 2 * C * C, *plast = cumout + C;
-  for (int i = threadIdx.x; i < C * C; i += blockDim.x) {
-    const int t = i / C, j = i % C;
-    float ck = 0.0f, cq = 0.0f;
-    if (j <= t && t < n) {
-      float dkk = 0.0f, dkq = 0.0f;
-      const float4 *kj = reinterpret_cast<const float4 *>(K + j * kKS);
-      const float4 *kt = reinterpret_cast<const float4 *>(K + t * kKS);
-      const float4 *qt = reinterpret_cast<const float4 *>(Q + t * kKS);
-#pragma unroll 4
-      for (int x = 0; x < D / 4; ++x) {
-        const float4 u = kj[x], w = kt[x], z = qt[x];
-        dkk = fmaf(u.x, w.x, fmaf(u.y, w.y, fmaf(u.z, w.z, fmaf(u.w, w.w, dkk))));
-        dkq = fmaf(u.x, z.x, fmaf(u.y, z.y, fmaf(u.z, z.z, fmaf(u.w, z.w, dkq))));
-      }
-      const float pr = P[t * (C + 1) + j];
-      cq = pr * dkq;
-      if (j < t) ck = pr * dkk;
-    }
-    Bm[t * (C + 1) + j] = bet[t] * ck;
-    CQout[i] = cq;
-  }
-  __syncthreads();
-  // T = (I + Bm)^-1 (unit lower triangular), one column per thread:
-  // T[t][j] = -sum_{k=j}^{t-1} Bm[t][k] T[k][j]; then M = T diag(beta)
-  for (int j = threadIdx.x; j < C; j += blockDim.x) {
-    float col[C];
+  {
+    // register tiles: thread (ti, tj) owns t = ti + 16a, j = tj + 16b; the
+    // dots keep the one-output-per-thread accumulation order
+    constexpr int TA = 4;
+    const int ti = threadIdx.x / 16, tj = threadIdx.x % 16;
+    float dkk[TA][TA], dkq[TA][TA];
 #pragma unroll
-    for (int t = 0; t < C; ++t) col[t] = 0.0f;
-    col[j] = 1.0f;
-    for (int t = j + 1; t < C; ++t) {
-      float s = 0.0f;
-      for (int k = j; k < t; ++k) s = fmaf(Bm[t * (C + 1) + k], col[k], s);
-      col[t] = -s;
+    for (int ai = 0; ai < TA; ++ai)
+#pragma unroll
+      for (int bi = 0; bi < TA; ++bi) dkk[ai][bi] = dkq[ai][bi] = 0.0f;
+#pragma unroll 2
+    for (int x = 0; x < D / 4; ++x) {
+      float4 kt[TA], qt[TA], kj[TA];
+#pragma unroll
+      for (int ai = 0; ai < TA; ++ai) {
+        kt[ai] = reinterpret_cast<const float4 *>(K + (ti + 16 * ai) * kKS)[x];
+        qt[ai] = reinterpret_cast<const float4 *>(Q + (ti + 16 * ai) * kKS)[x];
+        kj[ai] = reinterpret_cast<const float4 *>(K + (tj + 16 * ai) * kKS)[x];
+      }
+#pragma unroll
+      for (int ai = 0; ai < TA; ++ai)
+#pragma unroll
+        for (int bi = 0; bi < TA; ++bi) {
+          const float4 u = kj[bi], w = kt[ai], z = qt[ai];
+          dkk[ai][bi] = fmaf(u.x, w.x, fmaf(u.y, w.y, fmaf(u.z, w.z, fmaf(u.w, w.w, dkk[ai][bi]))));
+          dkq[ai][bi] = fmaf(u.x, z.x, fmaf(u.y, z.y, fmaf(u.z, z.z, fmaf(u.w, z.w, dkq[ai][bi]))));
+        }
     }
-    for (int t = 0; t < C; ++t) Mout[t * C + j] = col[t] * bet[j];
+#pragma unroll
+    for (int ai = 0; ai < TA; ++ai)
+#pragma unroll
+      for (int bi = 0; bi < TA; ++bi) {
+        const int t = ti + 16 * ai, j = tj + 16 * bi;
+        float ck = 0.0f, cq = 0.0f;
+        if (j <= t && t < n) {
+          const float pr = P[t * (C + 1) + j];
+          cq = pr * dkq[ai][bi];
+          if (j < t) ck = pr * dkk[ai][bi];
+        }
+        Bm[t * (C + 1) + j] = bet[t] * ck;
+        CQout[t * C + j] = cq;
+      }
   }
   for (int t = threadIdx.x; t < C; t += blockDim.x) {
     cumout[t] = cum[t];
     plast[t] = P[(n - 1) * (C + 1) + t];
+  }
+  __syncthreads();
+  // T = (I + Bm)^-1 (unit lower triangular), one column per thread, the
+  // column kept in shared memory over P (no longer needed):
+  // T[t][j] = -sum_{k=j}^{t-1} Bm[t][k] T[k][j]; then M = T diag(beta)
+  float *T = P;  // [C][C+1]
+  for (int j = threadIdx.x; j < C; j += blockDim.x) {
+    for (int t = 0; t <= j; ++t) T[t * (C + 1) + j] = t == j ? 1.0f : 0.0f;
+    for (int t = j + 1; t < C; ++t) {
+      float s = 0.0f;
+      for (int k = j; k < t; ++k) s = fmaf(Bm[t * (C + 1) + k], T[k * (C + 1) + j], s);
+      T[t * (C + 1) + j] = -s;
+    }
+    for (int t = 0; t < C; ++t) Mout[t * C + j] = T[t * (C + 1) + j] * bet[j];
   }
 }
 

@@ -251,17 +251,29 @@ def run_decode(args):
     prompt = qwen35.prompt_tokens(cfg, PROMPT, seed=1)
     stream = torch.cuda.ExternalStream(model.stream(), device=dev)
 
-    # prefill: ingest the 512-token prompt (no LM head), device-timed
-    model.set_prompt(prompt)
-    torch.cuda.synchronize()
-    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    p0.record(stream)
-    model.ingest_async(PROMPT - 1)
-    p1.record(stream)
-    torch.cuda.synchronize()
-    ex.sync()
-    prefill_ms = max_over_ranks(p0.elapsed_time(p1), world, dev)
+    # prefill: ingest the first PROMPT-1 prompt tokens (no LM head),
+    # device-timed, as sequential decode-path steps and as one batched pass
+    # (prism_b200_model_prefill_async; same resulting state)
+    def timed_ingest(batched):
+        model.reset()
+        model.set_prompt(prompt)
+        torch.cuda.synchronize()
+        q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        q0.record(stream)
+        if batched:
+            model.prefill_async(PROMPT - 1)
+        else:
+            model.ingest_async(PROMPT - 1)
+        q1.record(stream)
+        torch.cuda.synchronize()
+        ex.sync()
+        return max_over_ranks(q0.elapsed_time(q1), world, dev)
+
+    seq_ms = timed_ingest(False)
+    timed_ingest(True)  # first pass allocates the prompt buffers
+    prefill_ms = timed_ingest(True)
     prefill_tps = world * (PROMPT - 1) / (prefill_ms / 1e3)
+    prefill_seq_tps = world * (PROMPT - 1) / (seq_ms / 1e3)
 
     # decode: the first step consumes the last prompt token
     model.decode_async(W)
@@ -292,7 +304,7 @@ def run_decode(args):
     # end to end through the public API: host token in, greedy token out
     model.reset()
     model.set_prompt(prompt)
-    model.ingest_async(PROMPT - 1)
+    model.prefill_async(PROMPT - 1)
     tok = int(prompt[-1])
     for _ in range(W):
         _, tok = model.evaluate(tok, logits=False)
@@ -346,7 +358,14 @@ def run_decode(args):
                      "bytes_per_token": bytes_per_token},
         },
         "prefill": {"value": prefill_tps, "unit": "tok/s",
-                    "note": "prompt ingestion as sequential decode-path steps (no LM head)"},
+                    "tokens": PROMPT - 1, "ms": prefill_ms,
+                    "note": "batched prompt ingestion (prism_b200_model_prefill_async: "
+                            "tensor-core projections over the prompt, exact sequential "
+                            "GDN recurrence, causal attention per token; no LM head); "
+                            "state bit-identical to sequential ingestion",
+                    "sequential": {"value": prefill_seq_tps, "unit": "tok/s", "ms": seq_ms,
+                                   "note": "the same prompt as one-token decode-path "
+                                           "ingestion steps"}},
         "matvec": {"metric": MATVEC_METRIC, "value": mv_step, "unit": "GB/s",
                    "kernel_gbs": mv_kern, "us_per_launch": mv_us, "frac": mv_kern / peak,
                    "bit_exact": mv_parity,
@@ -654,6 +673,125 @@ def run_gemm(args):
         print(json.dumps(line), flush=True)
 
 
+PREFILL_TOKENS = 4096
+PREFILL_METRIC = "prefill tok/s (batch 1, 4096-token prompt)"
+
+
+def prefill_launches(cfg, tokens, chunk=512):
+    """Kernels of one prism_b200_model_prefill_async call: per 512-token pass
+    the positions, the embedding and the final position update, then per
+    layer norm + quantize + projections + the mixer's kernels + FFN."""
+    gdn = 2 + 4 + 4 + 2 + 1      # norm, quant, 4 GEMMs, inputs, scan, history, gated, quant, out
+    att = 2 + 3 + 2 + 1 + 1      # norm, quant, q/k/v GEMMs, kv rows, attention, quant, o
+    ffn = 2 + 2 + 1 + 1 + 1      # norm, quant, up/gate, swiglu, quant, down
+    per_pass = 3 + sum((att if cfg.is_full(l) else gdn) + ffn for l in range(cfg.layers))
+    return per_pass * ((tokens + chunk - 1) // chunk)
+
+
+def projection_ops(cfg):
+    """Integer multiply-adds x 2 of every projection of one token (no LM head)."""
+    total = 0
+    for l in range(cfg.layers):
+        for _, rows, cols in cfg.linear_shapes(l):
+            total += 2 * rows * cols
+    return total
+
+
+def run_prefill(args):
+    """Batched prompt ingestion of the configs[1] model: a step is one
+    prefill_async of a PREFILL_TOKENS-token prompt from position 0 (the
+    model is reset and the prompt placed outside the timed region)."""
+    import dataclasses
+    import torch
+    import prism_b200 as pb
+    import qwen35
+
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+    P = args.prefill_tokens
+    cfg = dataclasses.replace(qwen35.CONFIG1, context=P + 8)
+    K, W = min(args.steps, 10), args.warmup
+    weights = qwen35.synthetic_weights(cfg, seed=0)
+    ex = pb.ProjectionExecutor(local)
+    model = qwen35.Qwen35Model(ex, cfg)
+    model.load(weights)
+    prompt = qwen35.prompt_tokens(cfg, P, seed=1)
+    stream = torch.cuda.ExternalStream(model.stream(), device=dev)
+
+    def one(timed):
+        model.reset()
+        model.set_prompt(prompt)
+        torch.cuda.synchronize()
+        q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        q0.record(stream)
+        model.prefill_async(P)
+        q1.record(stream)
+        torch.cuda.synchronize()
+        ex.sync()
+        return q0.elapsed_time(q1)
+
+    for _ in range(W):
+        one(False)
+    if world > 1:
+        torch.distributed.barrier()
+    with Clocks(local) as clk:
+        times = [one(True) for _ in range(K)]
+    ms = max_over_ranks(float(np.sum(times)), world, dev)
+    tps = world * K * P / (ms / 1e3)
+
+    # end to end through the reference-facing block call (host tokens in,
+    # device status out, 256-token blocks as Decoder::ingest_block takes)
+    model.reset()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for b0 in range(0, P, 256):
+        model.ingest_block(prompt[b0:b0 + 256])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    model.close()
+    ex.close()
+
+    peak, peak_src = int8_peak()
+    ops = projection_ops(cfg) * P
+    achieved = ops / (ms / K / 1e3) / 1e12
+    line = {
+        "metric": PREFILL_METRIC, "value": tps, "unit": "tok/s", "n_gpus": world,
+        "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "i8xternary->i32,f32",
+        "data": "synthetic (random-init weights, random prompt; no public dataset)",
+        "config": {"workload": "configs[1] model (hidden 2560, 32 layers, TQ2_0 seed 0): "
+                               "batched ingestion of a %d-token random prompt (seed 1) from "
+                               "position 0, 512-token passes, no LM head" % P,
+                   "l2": "each pass streams the ~1 GB of weights (> 126 MB L2)"},
+        "clocks": clk.summary(),
+        "gpu_launches": K * prefill_launches(cfg, P),
+        "e2e": {"value": world * P / (e2e_ms / 1e3), "unit": "tok/s",
+                "h2d_bytes_per_step": 4 * P, "d2h_bytes_per_step": 4 * ((P + 255) // 256),
+                "api": "prism_b200_model_ingest_block, 256-token blocks (host tokens in, "
+                       "status out per block)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                     "unit": "Tint-op/s", "frac": achieved / peak, "peak_source": peak_src,
+                     "kernel": "all projections of the pass (gemm_tokens_kernel), their "
+                               "int-ops over the whole pass time (a lower bound on the GEMM "
+                               "kernels' own rate)",
+                     "algorithmic_ops_per_step": ops, "traffic": None},
+    }
+    if rank == 0 and not args.no_cpu:
+        cb, _ = cpu_decode_baseline(weights, cfg, prompt, seconds=15.0)
+        cb["sample"] = "sequential ingestion (the reference's Decoder::ingest per token): " + \
+            cb["sample"]
+        line["cpu_baseline"] = cb
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 SERVE_B, SERVE_CTX = 256, 8192
 SERVE_METRIC = "batched decode tok/s (256 sequences x 8192-token context, Q8_0 KV)"
 
@@ -820,6 +958,9 @@ def run_reference(args):
         prompt = qwen35.prompt_tokens(cfg, PROMPT, seed=1)
         cb, _ = cpu_decode_baseline(weights, cfg, prompt, seconds=30.0)
         metric, unit = DECODE_METRIC, "tok/s"
+        if args.workload == "prefill":
+            # the reference ingests a prompt token by token (Decoder::ingest)
+            metric = PREFILL_METRIC
     line = {
         "impl": "reference", "metric": metric, "value": cb["value"], "unit": unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -851,10 +992,13 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "matvec", "gdn", "gemm", "serve"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "matvec", "gdn", "gemm", "serve",
+                                                                "prefill"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-matvec", action="store_true", help="skip the configs[0] sub-benchmark")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens (profiling runs)")
+    ap.add_argument("--prefill-tokens", type=int, default=PREFILL_TOKENS,
+                    help="prefill workload: prompt tokens (profiling runs use fewer)")
     ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
                     help="serve workload on N GPUs: tensor-parallel (default) or sequence-sharded")
     ap.add_argument("--tp-mode", default="exact", choices=["exact", "allreduce"],
@@ -875,6 +1019,8 @@ def main():
         run_serve(args)
     elif args.workload == "matvec":
         run_matvec(args)
+    elif args.workload == "prefill":
+        run_prefill(args)
     else:
         run_decode(args)
     import torch

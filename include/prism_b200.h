@@ -335,6 +335,22 @@ int prism_b200_model_decode_async(prism_b200_model *m, size_t steps);
 int prism_b200_model_set_prompt(prism_b200_model *m, const uint32_t *tokens, size_t n);
 int prism_b200_model_ingest_async(prism_b200_model *m, size_t n);
 
+/* Batched prompt ingestion (replaces Decoder::ingest_block, src/lib.rs:229-247,
+ * and its tiled override, src/graph.rs:5459-5461).  prefill_async enqueues,
+ * without waiting, the ingestion of the `n` tokens that set_prompt placed at
+ * the next positions: every layer processes up to 512 tokens at once
+ * (tensor-core projections over the tokens, the Gated DeltaNet recurrence
+ * token after token with its state on chip, causal attention of each token
+ * over its prefix).  The KV rows, recurrent and convolution state and
+ * position it leaves are bit for bit those of `n` ingest steps.
+ * ingest_block is the reference's synchronous form: it rejects an empty
+ * block, one longer than PRISM_B200_MAX_PREFILL_BLOCK_TOKENS or a token
+ * outside the vocabulary before changing any state, then places, ingests and
+ * waits, returning the device status. */
+#define PRISM_B200_MAX_PREFILL_BLOCK_TOKENS 256u
+int prism_b200_model_prefill_async(prism_b200_model *m, size_t n);
+int prism_b200_model_ingest_block(prism_b200_model *m, const uint32_t *tokens, size_t n);
+
 /* The model's own stream (a cudaStream_t). */
 void *prism_b200_model_stream(const prism_b200_model *m);
 

@@ -32,6 +32,18 @@ struct ModelLayer {
   uint16_t *kc = nullptr, *vc = nullptr;  // [context][kv*hd]
 };
 
+// Activations of the batched prompt pass (prefill.cuh), [kPrefillChunk]
+// tokens each, allocated on its first use.
+struct PrefillBuffers {
+  float *hidden = nullptr, *xn = nullptr, *mixed = nullptr, *zgate = nullptr, *beta = nullptr,
+        *alpha = nullptr, *o_pre = nullptr, *attended = nullptr, *projected = nullptr,
+        *key = nullptr, *value = nullptr, *up = nullptr, *gate = nullptr, *act = nullptr,
+        *db = nullptr;
+  void *tok = nullptr;  // Q8_K tokens of the widest projection input
+  int *pos = nullptr;   // position of each token
+  bool ready = false;
+};
+
 }  // namespace prism
 
 struct prism_b200_model {
@@ -66,6 +78,7 @@ struct prism_b200_model {
   int nseqtrace = 0;
   float *gdn_o = nullptr, *smax = nullptr;
   double *stot = nullptr, *apart = nullptr;
+  prism::PrefillBuffers pre;
   std::map<std::string, bool> bound;
   std::vector<void *> allocations;
   bool finalized = false;

@@ -302,6 +302,7 @@ struct AttnArgs {
   // (attention_decode_kernel); 0: read them from global memory in place
   int kv_smem_off;
   unsigned long long *trace;  // optional timeline, as MvArgs::trace ([0], [1], [6], [7])
+  int no_write;  // 1: the token's K/V rows are already in the cache (batched prefill)
 };
 
 constexpr int kAttnThreads = 256;
@@ -576,7 +577,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(AttnArgs
   kc[i] = norm_rope_round(a.key_in + (long)kvh * hd, a.k_norm, a.eps, hd, a.rope_dim, cs, buf,
                           red);
   vc[i] = round_f16(a.value_in[kvh * hd + i]);
-  const bool writer = rank == 0 && h % group == 0;
+  const bool writer = rank == 0 && h % group == 0 && !a.no_write;
   if (a.q8) {
     const int rb = q8_0_record_bytes(hd);
     const long at = ((long)pos * a.kv_heads + kvh) * rb;

@@ -1,0 +1,460 @@
+// prefill.cuh -- batched prompt ingestion of one sequence.
+//
+// The reference ingests a prompt token by token through the decoder
+// (src/lib.rs:229-247 Decoder::ingest) or through its tiled prefill
+// (src/graph/prefill.rs), which shares each weight row across a tile of
+// tokens.  Here all the prompt's tokens go through every layer together:
+//   * projections are tensor-core GEMMs over the T tokens (gemm.cuh), with
+//     the same per-row binary32 chains as the decode matvecs;
+//   * each Gated DeltaNet layer forms every token's convolution, q/k norms,
+//     decay and beta at once (gdn_token_inputs_kernel), then runs the exact
+//     recurrence over the tokens with each state row held in one warp's
+//     registers for the whole prompt (gdn_rows_scan_kernel) -- the decode
+//     kernel's arithmetic, token after token;
+//   * each attention layer first writes the T new K/V rows to the cache
+//     (kv_rows_kernel), then every token attends over its own prefix
+//     (attention_decode_kernel with one grid row per token, no writes).
+// The state left behind -- KV rows, recurrent state, convolution history,
+// position -- is bit for bit what T decode-path ingestion steps leave.
+// Included once by prism_b200.cu, after batch.cuh.
+#pragma once
+
+#include "batch.cuh"
+
+namespace prism {
+
+constexpr int kPrefillChunk = 512;  // tokens per batched pass
+
+// ---- Gated DeltaNet over the prompt's tokens --------------------------------
+//
+// The decode step's per-token work splits into what does not depend on the
+// recurrent state -- convolution + SiLU of every channel, L2 normalisation of
+// the q and k groups, decay and beta of every head -- done for all tokens at
+// once (gdn_token_inputs_kernel), and the state recurrence proper, a chain
+// over the tokens for each state row (gdn_rows_scan_kernel).
+
+struct GdnTokensArgs {
+  int S, groups, values, conv_k, T, channels;
+  float eps;
+  const float *mixed;               // [T][channels] qkv projections, before conv
+  const float *beta_in, *alpha_in;  // [T][values]
+  const float *conv_w, *dt_bias, *ssm_a;
+  const float *hist_in;             // [channels][k-1] history before token 0
+  float *act;                       // [T][channels] conv + SiLU, q and k L2-normalised
+  float *db;                        // [T][values][2] decay, beta
+  float *state;                     // [values][S][S], updated in place
+  float *o_pre;                     // [T][values * S] pre-norm outputs
+  unsigned *status;
+};
+
+constexpr int kScanRows = 4;  // state rows (warps) per CTA of the scan
+
+// grid (T, 2 * groups + values), S (= 128) threads: block y < groups is q
+// group y, y < 2 * groups k group y - groups, else v head y - 2 * groups
+// (whose thread 0 also forms the head's decay and beta).  run_gdn's
+// arithmetic: taps in order, SiLU, then the binary64 sum of squares as a
+// warp butterfly per 32 values with the partials added in warp order.
+__global__ void __launch_bounds__(128) gdn_token_inputs_kernel(GdnTokensArgs a) {
+  constexpr int S = 128;
+  __shared__ double red[S / 32];
+  const int t = blockIdx.x, y = blockIdx.y, j = threadIdx.x;
+  const int kw = a.groups * S, hist = a.conv_k - 1;
+  const int part = y < a.groups ? 0 : y < 2 * a.groups ? 1 : 2;
+  const int ch = part == 0 ? y * S + j : part == 1 ? kw + (y - a.groups) * S + j
+                                                   : 2 * kw + (y - 2 * a.groups) * S + j;
+  const float *cj = a.conv_w + (long)ch * a.conv_k;
+  float sum = 0.0f;
+  for (int i = 0; i < hist; ++i) {
+    const int tt = t - hist + i;  // the token whose input is tap i
+    const float hv = tt >= 0 ? a.mixed[(long)tt * a.channels + ch]
+                             : a.hist_in[(long)ch * hist + (t + i)];
+    sum = __fadd_rn(sum, __fmul_rn(hv, cj[i]));
+  }
+  sum = __fadd_rn(sum, __fmul_rn(a.mixed[(long)t * a.channels + ch], cj[hist]));
+  float act = silu_f(sum);
+  if (part < 2) {
+    const double w = warp_sum_f64((double)__fmul_rn(act, act));
+    if ((j & 31) == 0) red[j >> 5] = w;
+    __syncthreads();
+    double tot = 0.0;
+    for (int i = 0; i < S / 32; ++i) tot += red[i];
+    act = __fmul_rn(act, __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)tot), a.eps)));
+  } else if (j == 0) {
+    const int h = y - 2 * a.groups;
+    a.db[((long)t * a.values + h) * 2] =
+        recurrent_decay_f(a.alpha_in[(long)t * a.values + h], a.dt_bias[h], a.ssm_a[h], a.status);
+    a.db[((long)t * a.values + h) * 2 + 1] = sigmoid_f(a.beta_in[(long)t * a.values + h]);
+  }
+  a.act[(long)t * a.channels + ch] = act;
+}
+
+// One warp per state row r of value head h (grid values * S / kScanRows,
+// kScanRows warps): the row stays in registers for the whole prompt, lane l
+// owning columns 4l .. 4l+3.  Per token, run_gdn's row arithmetic in its
+// order: decay, s.k (binary64 partials, warp butterfly), delta, update,
+// s.q.  The next token's inputs are loaded kDepth tokens ahead, and the
+// butterfly of token t's s.q runs beside token t+1's s.k.
+__global__ void __launch_bounds__(32 * kScanRows) gdn_rows_scan_kernel(GdnTokensArgs a) {
+  constexpr int S = 128, kDepth = 4;
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kScanRows + (threadIdx.x >> 5);  // h * S + r
+  if (row >= a.values * S) return;
+  const int h = row / S, kh = h % a.groups, kw = a.groups * S;
+  float *srow = a.state + (long)row * S;
+  float4 s = reinterpret_cast<const float4 *>(srow)[lane];
+  const float oscale = __fdiv_rn(1.0f, __fsqrt_rn((float)S));
+  const float *qbase = a.act + kh * S + 4 * lane;
+  const float *kbase = a.act + kw + kh * S + 4 * lane;
+  const float *vbase = a.act + 2 * kw + row;
+  const float *dbase = a.db + 2 * h;
+  float4 K[kDepth], Q[kDepth];
+  float V[kDepth], DC[kDepth], BT[kDepth];
+  auto load = [&](int u, int t) {
+    const long o = (long)t * a.channels;
+    K[u] = *reinterpret_cast<const float4 *>(kbase + o);
+    Q[u] = *reinterpret_cast<const float4 *>(qbase + o);
+    V[u] = vbase[o];
+    DC[u] = dbase[(long)t * a.values * 2];
+    BT[u] = dbase[(long)t * a.values * 2 + 1];
+  };
+#pragma unroll
+  for (int u = 0; u < kDepth; ++u)
+    if (u < a.T) load(u, u);
+  bool finite = true;
+  double dqp = 0.0;  // s.q partial of the previous token
+  for (int t0 = 0; t0 < a.T; t0 += kDepth) {
+#pragma unroll
+    for (int u = 0; u < kDepth; ++u) {
+      const int t = t0 + u;
+      if (t < a.T) {
+        const float4 kk = K[u], qq = Q[u];
+        const float vv = V[u], decay = DC[u], beta = BT[u];
+        if (t + kDepth < a.T) load(u, t + kDepth);
+        s.x = __fmul_rn(decay, s.x);
+        s.y = __fmul_rn(decay, s.y);
+        s.z = __fmul_rn(decay, s.z);
+        s.w = __fmul_rn(decay, s.w);
+        double dk = (double)__fmul_rn(s.x, kk.x) + (double)__fmul_rn(s.y, kk.y) +
+                    (double)__fmul_rn(s.z, kk.z) + (double)__fmul_rn(s.w, kk.w);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          dk += __shfl_xor_sync(0xffffffffu, dk, off);
+          dqp += __shfl_xor_sync(0xffffffffu, dqp, off);
+        }
+        if (t > 0 && lane == 0)
+          a.o_pre[(long)(t - 1) * a.values * S + row] = __fmul_rn((float)dqp, oscale);
+        const float delta = __fmul_rn(__fsub_rn(vv, (float)dk), beta);
+        s.x = __fadd_rn(s.x, __fmul_rn(delta, kk.x));
+        s.y = __fadd_rn(s.y, __fmul_rn(delta, kk.y));
+        s.z = __fadd_rn(s.z, __fmul_rn(delta, kk.z));
+        s.w = __fadd_rn(s.w, __fmul_rn(delta, kk.w));
+        finite &= is_finite_f(s.x) && is_finite_f(s.y) && is_finite_f(s.z) && is_finite_f(s.w);
+        dqp = (double)__fmul_rn(s.x, qq.x) + (double)__fmul_rn(s.y, qq.y) +
+              (double)__fmul_rn(s.z, qq.z) + (double)__fmul_rn(s.w, qq.w);
+      }
+    }
+  }
+  if (a.T > 0) {
+    dqp = warp_sum_f64(dqp);
+    if (lane == 0) a.o_pre[(long)(a.T - 1) * a.values * S + row] = __fmul_rn((float)dqp, oscale);
+  }
+  reinterpret_cast<float4 *>(srow)[lane] = s;
+  if (!__all_sync(0xffffffffu, finite) && lane == 0) report(a.status, kStatusNonfinite);
+}
+
+// Convolution history after the prompt: each channel's last k-1 inputs
+// (from the prompt's projections, or the history before it when the prompt
+// is shorter).  One thread per channel; out may alias in (every read of a
+// channel precedes its writes, in the same thread).
+__global__ void conv_history_kernel(const float *mixed, const float *hist_in, float *hist_out,
+                                    int channels, int hist, int T) {
+  const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+  if (ch >= channels || hist <= 0 || hist > 8) return;
+  float nv[8];
+  for (int i = 0; i < hist; ++i) {
+    const int tt = T - hist + i;
+    nv[i] = tt >= 0 ? mixed[(long)tt * channels + ch] : hist_in[(long)ch * hist + (T + i)];
+  }
+  for (int i = 0; i < hist; ++i) hist_out[(long)ch * hist + i] = nv[i];
+}
+
+// y = RMSNorm(o_h) * w * SiLU(z_h) per (token, head), a warp per head: the
+// binary64 sum of squares as the decode out-projection's gated prologue
+// forms it (four 32-value butterfly sums, added in order).  grid (T), up to
+// 32 warps per CTA.
+__global__ void gated_rows_kernel(const float *o_pre, const float *zgate, const float *norm_w,
+                                  int values, int S, float eps, float *out) {
+  const int t = blockIdx.x, lane = threadIdx.x & 31;
+  for (int h = threadIdx.x >> 5; h < values; h += (int)(blockDim.x >> 5)) {
+    const long base = ((long)t * values + h) * S;
+    const float *o = o_pre + base;
+    double tot = 0.0;
+    for (int qd = 0; qd < S / 32; ++qd) {
+      const float val = o[32 * qd + lane];
+      tot += warp_sum_f64((double)__fmul_rn(val, val));
+    }
+    const float mean = (float)(tot / (double)S);
+    const float nscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    for (int qd = 0; qd < S / 32; ++qd) {
+      const int i = 32 * qd + lane;
+      const float normed = __fmul_rn(__fmul_rn(o[i], nscale), norm_w[i]);
+      out[base + i] = __fmul_rn(normed, silu_f(zgate[base + i]));
+    }
+  }
+}
+
+// ---- attention: the prompt's K/V rows ---------------------------------------
+
+// The K and V cache rows of tokens p0 .. p0+T-1, as attention_decode_kernel's
+// writer CTA produces them (RMSNorm, RoPE and binary16 rounding of k; binary16
+// rounding of v; binary16 bits or Q8_0 records).  grid (kv_heads, T), hd
+// threads.
+__global__ void __launch_bounds__(kAttnThreads) kv_rows_kernel(AttnArgs a, int p0) {
+  __shared__ __align__(16) float cs[64];
+  __shared__ float buf[kAttnThreads];
+  __shared__ double red[kAttnThreads / 32];
+  const int kvh = blockIdx.x, t = blockIdx.y, i = threadIdx.x;
+  const int hd = a.hd, kvw = a.kv_heads * hd;
+  const int pos = p0 + t;
+  if (i < a.rope_dim / 2) {
+    float theta = (float)pos;
+    for (int j = 0; j < i; ++j) theta = __fmul_rn(theta, a.theta_scale);
+    const float angle = i < 3 * a.sections[i % 3] ? theta : 0.0f;
+    cs[2 * i] = cos_cr(angle);
+    cs[2 * i + 1] = sin_cr(angle);
+  }
+  __syncthreads();
+  float kc = norm_rope_round(a.key_in + (long)t * kvw + (long)kvh * hd, a.k_norm, a.eps, hd,
+                             a.rope_dim, cs, buf, red);
+  float vc = round_f16(a.value_in[(long)t * kvw + kvh * hd + i]);
+  if (a.q8) {
+    const int rb = q8_0_record_bytes(hd);
+    const long at = ((long)pos * a.kv_heads + kvh) * rb;
+    q8_0_roundtrip(kc, reinterpret_cast<uint8_t *>(a.kcache) + at, hd, a.status);
+    q8_0_roundtrip(vc, reinterpret_cast<uint8_t *>(a.vcache) + at, hd, a.status);
+  } else {
+    a.kcache[(long)pos * kvw + kvh * hd + i] = float_to_half_bits(kc);
+    a.vcache[(long)pos * kvw + kvh * hd + i] = float_to_half_bits(vc);
+  }
+}
+
+__global__ void fill_positions_kernel(int *pos, int p0, int T, int *model_position) {
+  for (int t = threadIdx.x; t < T; t += blockDim.x) pos[t] = p0 + t;
+  if (threadIdx.x == 0 && model_position) *model_position = p0 + T;
+}
+
+}  // namespace prism
+
+namespace prism {
+
+inline cudaError_t prefill_alloc(prism_b200_model *m) {
+  PrefillBuffers &pb = m->pre;
+  if (pb.ready) return cudaSuccess;
+  const auto &c = m->cfg;
+  const size_t T = kPrefillChunk;
+  cudaError_t e = cudaSuccess;
+  auto A = [&](auto **p, size_t count) {
+    if (e == cudaSuccess) e = model_alloc(m, p, count);
+  };
+  A(&pb.hidden, T * c.hidden);
+  A(&pb.xn, T * c.hidden);
+  A(&pb.mixed, T * m->channels());
+  A(&pb.zgate, T * m->value_width());
+  A(&pb.beta, T * c.ssm_values);
+  A(&pb.alpha, T * c.ssm_values);
+  A(&pb.o_pre, T * m->value_width());
+  A(&pb.act, T * m->channels());
+  A(&pb.db, T * c.ssm_values * 2);
+  A(&pb.attended, T * std::max<size_t>(m->value_width(), (size_t)c.heads * c.head_dim));
+  A(&pb.projected, T * c.heads * c.head_dim * 2);
+  A(&pb.key, T * m->kvw());
+  A(&pb.value, T * m->kvw());
+  A(&pb.up, T * c.ffn);
+  A(&pb.gate, T * c.ffn);
+  const size_t widest = std::max({(size_t)c.hidden, (size_t)c.ffn, (size_t)c.heads * c.head_dim,
+                                  (size_t)m->value_width()});
+  uint8_t *tok = nullptr;
+  A(&tok, token_q8k_bytes(T, (int)(widest / 256)));
+  pb.tok = tok;
+  A(&pb.pos, T);
+  pb.ready = e == cudaSuccess;
+  return e;
+}
+
+// Enqueue the batched pass of the T prompt tokens at positions p0 .. p0+T-1
+// (already in m->d_tokens) on the model's stream; no LM head.
+inline cudaError_t enqueue_prefill(prism_b200_model *m, int p0, int T) {
+  PrefillBuffers &pb = m->pre;
+  const auto &c = m->cfg;
+  prism_b200_executor *ex = m->ex;
+  cudaStream_t s = m->stream;
+  unsigned *status = ex->d_status;
+  const int H = (int)c.hidden, hnb = H / 256, hd = (int)c.head_dim, S = (int)c.ssm_state;
+  cudaError_t e;
+#define PK(x)                            \
+  if ((e = (x)) != cudaSuccess) return e
+  fill_positions_kernel<<<1, 256, 0, s>>>(pb.pos, p0, T, nullptr);
+  PK(cudaGetLastError());
+  if (c.weight_kind == 35)
+    embed_batch_kernel<35><<<dim3((H + 255) / 256, T), 256, 0, s>>>(
+        m->embd.units, m->embd.h, m->embd.nb, (int)c.vocab, m->d_tokens + p0, pb.hidden, H,
+        status);
+  else
+    embed_batch_kernel<10><<<dim3((H + 255) / 256, T), 256, 0, s>>>(
+        m->embd.units, m->embd.h, m->embd.nb, (int)c.vocab, m->d_tokens + p0, pb.hidden, H,
+        status);
+  PK(cudaGetLastError());
+  auto norm = [&](const float *w) {
+    rmsnorm_rows_kernel<<<T, 256, 0, s>>>(pb.hidden, w, H, c.eps, pb.xn, status);
+    return cudaGetLastError();
+  };
+  auto quant = [&](const float *x, int nb) {
+    return launch_token_quantize(x, T, nb, 0, token_q8k_carve(pb.tok, T, nb), status, s, false);
+  };
+  auto mm = [&](const DeviceWeight &w, float *y, const float *residual) {
+    return launch_token_matmul(w, T, token_q8k_carve(pb.tok, T, w.nb), y, residual, nullptr,
+                               status, s, false);
+  };
+  for (size_t l = 0; l < m->L.size(); ++l) {
+    ModelLayer &Ly = m->L[l];
+    PK(norm(Ly.attn_norm));
+    PK(quant(pb.xn, hnb));
+    if (Ly.full) {
+      PK(mm(Ly.q, pb.projected, nullptr));
+      PK(mm(Ly.k, pb.key, nullptr));
+      PK(mm(Ly.v, pb.value, nullptr));
+      AttnArgs aa{};
+      aa.heads = (int)c.heads;
+      aa.kv_heads = (int)c.kv_heads;
+      aa.hd = hd;
+      aa.rope_dim = (int)c.rope_dim;
+      for (int j = 0; j < 3; ++j) aa.sections[j] = (int)c.rope_sections[j];
+      aa.eps = c.eps;
+      aa.theta_scale = powf(c.rope_base, -2.0f / (float)c.rope_dim);
+      aa.projected = pb.projected;
+      aa.key_in = pb.key;
+      aa.value_in = pb.value;
+      aa.q_norm = Ly.q_norm;
+      aa.k_norm = Ly.k_norm;
+      aa.kcache = Ly.kc;
+      aa.vcache = Ly.vc;
+      aa.q8 = c.kv_policy == PRISM_B200_KV_Q8_0 ? 1 : 0;
+      aa.position = pb.pos;
+      aa.pos_stride = 1;
+      aa.seq_proj = (long)c.heads * hd * 2;
+      aa.seq_kv_in = m->kvw();
+      aa.seq_out = (long)c.heads * hd;
+      aa.seq_cache = 0;  // one sequence: every token reads the same cache
+      aa.no_write = 1;   // kv_rows_kernel wrote the rows
+      aa.attended = pb.attended;
+      aa.status = status;
+      kv_rows_kernel<<<dim3(c.kv_heads, T), kAttnThreads, 0, s>>>(aa, p0);
+      PK(cudaGetLastError());
+      const size_t smem = attn_launch_smem(aa, (int)c.context);
+      cudaLaunchAttribute cattr[2];
+      cudaLaunchConfig_t cfg =
+          pdl_config(dim3(c.heads * kAttnSplit, T), dim3(kAttnThreads), smem, s, cattr, false);
+      cattr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+      cattr[cfg.numAttrs].val.clusterDim.x = kAttnSplit;
+      cattr[cfg.numAttrs].val.clusterDim.y = 1;
+      cattr[cfg.numAttrs].val.clusterDim.z = 1;
+      cfg.numAttrs += 1;
+      PK(cudaLaunchKernelEx(&cfg, attention_decode_kernel, aa));
+      PK(quant(pb.attended, (int)(c.heads * c.head_dim / 256)));
+      PK(mm(Ly.o, pb.hidden, pb.hidden));
+    } else {
+      PK(mm(Ly.qkv, pb.mixed, nullptr));
+      PK(mm(Ly.z, pb.zgate, nullptr));
+      PK(mm(Ly.beta, pb.beta, nullptr));
+      PK(mm(Ly.alpha, pb.alpha, nullptr));
+      const long hist_stride = (long)m->channels() * (c.conv_kernel - 1);
+      const float *hist_in = Ly.conv_state + (p0 & 1) * hist_stride;
+      float *hist_out = Ly.conv_state + ((p0 + T) & 1) * hist_stride;
+      GdnTokensArgs g{};
+      g.S = S;
+      g.groups = (int)c.ssm_groups;
+      g.values = (int)c.ssm_values;
+      g.conv_k = (int)c.conv_kernel;
+      g.T = T;
+      g.channels = m->channels();
+      g.eps = c.eps;
+      g.mixed = pb.mixed;
+      g.beta_in = pb.beta;
+      g.alpha_in = pb.alpha;
+      g.conv_w = Ly.conv_w;
+      g.dt_bias = Ly.dt_bias;
+      g.ssm_a = Ly.ssm_a;
+      g.hist_in = hist_in;
+      g.act = pb.act;
+      g.db = pb.db;
+      g.state = Ly.matrix;
+      g.o_pre = pb.o_pre;
+      g.status = status;
+      gdn_token_inputs_kernel<<<dim3(T, 2 * c.ssm_groups + c.ssm_values), 128, 0, s>>>(g);
+      PK(cudaGetLastError());
+      gdn_rows_scan_kernel<<<c.ssm_values * S / kScanRows, 32 * kScanRows, 0, s>>>(g);
+      PK(cudaGetLastError());
+      conv_history_kernel<<<(m->channels() + 255) / 256, 256, 0, s>>>(
+          pb.mixed, hist_in, hist_out, m->channels(), (int)c.conv_kernel - 1, T);
+      PK(cudaGetLastError());
+      gated_rows_kernel<<<T, std::min<uint32_t>(c.ssm_values, 32) * 32, 0, s>>>(pb.o_pre, pb.zgate, Ly.ssm_norm,
+                                                          (int)c.ssm_values, S, c.eps,
+                                                          pb.attended);
+      PK(cudaGetLastError());
+      PK(quant(pb.attended, m->value_width() / 256));
+      PK(mm(Ly.out, pb.hidden, pb.hidden));
+    }
+    PK(norm(Ly.post_norm));
+    PK(quant(pb.xn, hnb));
+    PK(mm(Ly.up, pb.up, nullptr));
+    PK(mm(Ly.gate, pb.gate, nullptr));
+    {
+      const long n = (long)T * c.ffn;
+      swiglu_kernel<<<(unsigned)std::min<long>((n + 255) / 256, 4096), 256, 0, s>>>(
+          pb.up, pb.gate, n, status);
+      PK(cudaGetLastError());
+    }
+    PK(quant(pb.up, (int)(c.ffn / 256)));
+    PK(mm(Ly.down, pb.hidden, pb.hidden));
+  }
+  fill_positions_kernel<<<1, 256, 0, s>>>(pb.pos, p0, T, m->d_position);
+  PK(cudaGetLastError());
+#undef PK
+  return cudaSuccess;
+}
+
+}  // namespace prism
+
+int prism_b200_model_prefill_async(prism_b200_model *m, size_t n) {
+  using namespace prism;
+  if (!m) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = m->ex;
+  int st = check_open(ex);
+  if (st) return st;
+  if (!m->finalized) return ex->fail(PRISM_B200_E_INVALID, "model is not finalized");
+  if (n == 0) return ex->fail(PRISM_B200_E_INVALID, "prefill needs at least one token");
+  if (m->position + (int64_t)n > (int64_t)m->cfg.context)
+    return ex->fail(PRISM_B200_E_INVALID, "context is exhausted");
+  cudaSetDevice(ex->device);
+  CK(prefill_alloc(m), "prefill buffers");
+  for (size_t done = 0; done < n; done += kPrefillChunk) {
+    const int T = (int)std::min<size_t>(kPrefillChunk, n - done);
+    CK(enqueue_prefill(m, (int)(m->position + (int64_t)done), T), "prefill");
+  }
+  m->position += (int64_t)n;
+  return PRISM_B200_OK;
+}
+
+int prism_b200_model_ingest_block(prism_b200_model *m, const uint32_t *tokens, size_t n) {
+  if (!m) return PRISM_B200_E_INVALID;
+  prism_b200_executor *ex = m->ex;
+  int st = check_open(ex);
+  if (st) return st;
+  if (!tokens || n == 0 || n > PRISM_B200_MAX_PREFILL_BLOCK_TOKENS)
+    return ex->fail(PRISM_B200_E_INVALID, "invalid prefill block bounds");
+  st = prism_b200_model_set_prompt(m, tokens, n);
+  if (st) return st;
+  st = prism_b200_model_prefill_async(m, n);
+  if (st) return st;
+  return model_finish(m);
+}

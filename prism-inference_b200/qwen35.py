@@ -332,13 +332,31 @@ class Qwen35Model:
             L.prism_b200_model_set_prompt.argtypes = [c.c_void_p, c.c_void_p, c.c_size_t]
             L.prism_b200_model_ingest_async.restype = c.c_int
             L.prism_b200_model_ingest_async.argtypes = [c.c_void_p, c.c_size_t]
+            L.prism_b200_model_prefill_async.restype = c.c_int
+            L.prism_b200_model_prefill_async.argtypes = [c.c_void_p, c.c_size_t]
+            L.prism_b200_model_ingest_block.restype = c.c_int
+            L.prism_b200_model_ingest_block.argtypes = [c.c_void_p, c.c_void_p, c.c_size_t]
             L._prompt_declared = True
         t = np.ascontiguousarray(tokens, np.uint32)
         self.ex._check(L.prism_b200_model_set_prompt(self.h, t.ctypes.data, t.size))
 
     def ingest_async(self, n):
+        """Enqueue n one-token ingestion steps of the tokens set_prompt placed."""
         self.set_prompt  # declarations
         self.ex._check(self.L.prism_b200_model_ingest_async(self.h, n))
+
+    def prefill_async(self, n):
+        """Enqueue the batched ingestion of the n tokens set_prompt placed
+        (same resulting state as ingest_async(n))."""
+        self.set_prompt  # declarations
+        self.ex._check(self.L.prism_b200_model_prefill_async(self.h, n))
+
+    def ingest_block(self, tokens):
+        """Decoder::ingest_block: place, ingest and wait (at most
+        MAX_PREFILL_BLOCK_TOKENS tokens)."""
+        self.set_prompt  # declarations
+        t = np.ascontiguousarray(tokens, np.uint32)
+        self.ex._check(self.L.prism_b200_model_ingest_block(self.h, t.ctypes.data, t.size))
 
 
 def _declare_batch(L):

@@ -39,6 +39,7 @@ struct PrefillBuffers {
         *alpha = nullptr, *o_pre = nullptr, *attended = nullptr, *projected = nullptr,
         *key = nullptr, *value = nullptr, *up = nullptr, *gate = nullptr, *act = nullptr,
         *db = nullptr;
+  float *qrows = nullptr, *scur = nullptr, *scratch = nullptr;  // batched attention
   void *tok = nullptr;  // Q8_K tokens of the widest projection input
   int *pos = nullptr;   // position of each token
   bool ready = false;

@@ -238,6 +238,479 @@ __global__ void __launch_bounds__(kAttnThreads) kv_rows_kernel(AttnArgs a, int p
   }
 }
 
+// ---- attention over the prompt ----------------------------------------------
+//
+// Token t of the prompt (position pos = p0 + t) attends over positions
+// 0 .. pos-1 of the cache and its own row.  attention_decode_kernel's
+// arithmetic for it is fixed by its 8-CTA split: scores are binary64 sums of
+// binary32 products, 8 dimensions per lane then a warp butterfly; the
+// softmax maximum is global, the exponentials' binary64 total is formed per
+// CTA (rank r of 8 owns positions [r*per, (r+1)*per), per = ceil(pos/8)) as
+// a 256-thread block sum and the ranks' totals are added in rank order; the
+// probabilities are rounded to binary16; each rank's value sums run over its
+// positions in order from -0.0 and are added in rank order.
+// attention_prefill_kernel reproduces exactly that for kPfQueries (token,
+// head) queries per CTA that share one KV head's rows, staged once per CTA:
+//   * binary16 KV: a query and a key are binary16 values, so their binary32
+//     product is exact (22 significant bits, no underflow) and equals the
+//     binary64 product: each score is a chain of binary64 FMAs on operands
+//     converted once, in the same leaf order and reduction tree;
+//   * Q8_0 KV: dequantized keys carry up to 18 bits, so the binary32
+//     product rounds: the products are formed in binary32 and widened.
+
+constexpr int kPfQueries = 16;  // (token, head) queries per CTA
+constexpr int kPfChunk = 32;    // positions per staged chunk
+constexpr int kPfThreads = 256; // one thread per head dimension in the value pass
+
+struct PrefillAttnArgs {
+  AttnArgs a;       // geometry, norms, caches; projected/attended strides per token
+  int p0, T, G, TQ; // first position, tokens, heads per KV head, tokens per CTA
+  int context;      // scratch positions per query
+  const float *qrows;  // [T][heads][hd] normalised, rotated, binary16-rounded queries
+  const float *scur;   // [T][heads] score of each token's own row
+  float *scratch;      // [CTAs][kPfQueries][context] scores, then probabilities
+};
+
+// Queries and own-row scores (attention_decode_kernel's prologue): grid
+// (heads, T), hd (= kAttnThreads) threads.  Runs after kv_rows_kernel.
+__global__ void __launch_bounds__(kAttnThreads) query_rows_kernel(AttnArgs a, int p0,
+                                                                  float *qrows, float *scur) {
+  __shared__ __align__(16) float cs[64];
+  __shared__ float buf[kAttnThreads];
+  __shared__ double red[kAttnThreads / 32];
+  const int h = blockIdx.x, t = blockIdx.y, i = threadIdx.x;
+  const int hd = a.hd, kvw = a.kv_heads * hd, kvh = h / (a.heads / a.kv_heads);
+  const int pos = p0 + t;
+  if (i < a.rope_dim / 2) {
+    float theta = (float)pos;
+    for (int j = 0; j < i; ++j) theta = __fmul_rn(theta, a.theta_scale);
+    const float angle = i < 3 * a.sections[i % 3] ? theta : 0.0f;
+    cs[2 * i] = cos_cr(angle);
+    cs[2 * i + 1] = sin_cr(angle);
+  }
+  __syncthreads();
+  const float q = norm_rope_round(a.projected + (long)t * a.seq_proj + (long)h * 2 * hd, a.q_norm,
+                                  a.eps, hd, a.rope_dim, cs, buf, red);
+  float kc;
+  if (a.q8) {
+    const int rb = q8_0_record_bytes(hd);
+    kc = q8_0_value(reinterpret_cast<const uint8_t *>(a.kcache) + ((long)pos * a.kv_heads + kvh) * rb,
+                    hd, i);
+  } else {
+    kc = half_bits_to_float(a.kcache[(long)pos * kvw + kvh * hd + i]);
+  }
+  const double s = block_sum_f64((double)__fmul_rn(q, kc), red);
+  qrows[((long)t * a.heads + h) * hd + i] = q;
+  if (i == 0) scur[(long)t * a.heads + h] = __fmul_rn((float)s, __fdiv_rn(1.0f, __fsqrt_rn((float)hd)));
+}
+
+// Exact binary16 -> binary64 widening from the bit fields (normal numbers
+// and zeros; the rare subnormal, infinite or NaN input goes through
+// binary32).
+__device__ __forceinline__ double f16_bits_to_f64(uint16_t hb) {
+  const uint32_t e = (hb >> 10) & 31u, m = hb & 1023u, sgn = (uint32_t)(hb >> 15) << 31;
+  if (e - 1u < 30u) return __hiloint2double((int)(sgn | ((e + 1008u) << 20) | (m << 10)), 0);
+  if ((hb & 0x7fffu) == 0) return __hiloint2double((int)sgn, 0);
+  return (double)half_bits_to_float(hb);
+}
+
+// Staged operand type and product chain of each KV format.  Rows arrive as
+// raw cache bytes (bulk copies) and are widened once per CTA.
+template <bool Q8>
+struct PfOps {
+  using T = double;
+  static constexpr int kRowBytes = 512;  // 256 binary16 values
+  __device__ static T widen_row(const uint8_t *row, int d) {
+    return f16_bits_to_f64(reinterpret_cast<const uint16_t *>(row)[d]);
+  }
+  __device__ static T widen(float x) { return (double)x; }
+  // first term, next term of a binary64 chain of (exact) binary32 products
+  __device__ static double first(T x, T y) { return x * y; }
+  __device__ static double next(T x, T y, double acc) { return fma(x, y, acc); }
+};
+
+template <>
+struct PfOps<true> {
+  using T = float;
+  static constexpr int kRowBytes = q8_0_record_bytes(256);
+  __device__ static T widen_row(const uint8_t *row, int d) { return q8_0_value(row, 256, d); }
+  __device__ static T widen(float x) { return x; }
+  __device__ static double first(T x, T y) { return (double)__fmul_rn(x, y); }
+  __device__ static double next(T x, T y, double acc) { return acc + (double)__fmul_rn(x, y); }
+};
+
+template <bool Q8>
+constexpr size_t prefill_attn_smem() {
+  using T = typename PfOps<Q8>::T;
+  return (size_t)256 * kPfQueries * sizeof(T)                 // queries [hd][Q]
+         + (size_t)256 * (kPfChunk + 1) * sizeof(T)           // keys [hd][chunk+1] / values [chunk][hd]
+         + (size_t)8 * kPfQueries * kPfChunk * 8              // score partial trees [8][Q][chunk]
+         + (size_t)kPfChunk * kPfQueries * sizeof(T)          // probabilities [chunk][Q]
+         + (size_t)2 * kPfChunk * PfOps<Q8>::kRowBytes;       // raw rows, two buffers
+}
+
+// The warp butterfly's sum of 32 lane values v[0..31] (lane l adds lane
+// l^16, then l^8, ...), evaluated by one thread.
+__device__ __forceinline__ double butterfly_sum32(const double (&v)[32]) {
+  double s16[16], s8[8], s4[4];
+#pragma unroll
+  for (int b = 0; b < 16; ++b) s16[b] = v[b] + v[b + 16];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) s8[b] = s16[b] + s16[b + 8];
+#pragma unroll
+  for (int b = 0; b < 4; ++b) s4[b] = s8[b] + s8[b + 4];
+  return (s4[0] + s4[2]) + (s4[1] + s4[3]);
+}
+
+// grid (kv_heads, ceil(T / TQ)), kPfThreads threads; hd == 256, G * TQ <=
+// kPfQueries.  Query qi = tl * G + g is token t0 + tl, head kvh * G + g.
+// The K rows and then the V rows of positions 0 .. (last query's position)
+// stream through two raw buffers in chunks of kPfChunk (bulk copies, one per
+// row, issued two chunks ahead).
+template <bool Q8>
+__global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(PrefillAttnArgs pa) {
+  using Ops = PfOps<Q8>;
+  using T = typename Ops::T;
+  constexpr int HD = 256, QN = kPfQueries, CH = kPfChunk, RB = Ops::kRowBytes;
+  extern __shared__ __align__(128) uint8_t smem[];
+  T *qT = reinterpret_cast<T *>(smem);                            // [HD][QN]
+  T *rows = qT + HD * QN;                                         // [HD][CH+1] / [CH][HD]
+  double *Rs = reinterpret_cast<double *>(rows + HD * (CH + 1));  // [8][QN][CH]
+  T *pd = reinterpret_cast<T *>(Rs + 8 * QN * CH);                // [CH][QN]
+  uint8_t *raw = reinterpret_cast<uint8_t *>(pd + CH * QN);       // [2][CH][RB]
+  double *W = Rs;  // softmax group totals [QN][8][8], between the passes
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ int qpos[QN], qvalid[QN];
+  __shared__ float qmax[QN], qM[QN], qinv[QN], qpcur[QN];
+  __shared__ unsigned qmask[QN];
+  __shared__ int qcnt[QN];
+  const AttnArgs &a = pa.a;
+  const int kvh = blockIdx.x, t0 = blockIdx.y * pa.TQ, G = pa.G;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int cta = blockIdx.y * gridDim.x + blockIdx.x;
+  float *S = pa.scratch + (long)cta * QN * pa.context;
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+  if (tid < QN) {
+    const int tl = tid / G, t = t0 + tl;
+    const bool v = tid < G * pa.TQ && t < pa.T;
+    qvalid[tid] = v;
+    qpos[tid] = v ? pa.p0 + t : 0;
+  }
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    mbar_init_fence();
+  }
+  // queries, transposed: qT[d][qi]
+  for (int k = tid; k < HD * QN; k += kPfThreads) {
+    const int qi = k / HD, d = k % HD, t = t0 + qi / G;
+    const bool v = qi < G * pa.TQ && t < pa.T;
+    const int h = kvh * G + qi % G;
+    qT[d * QN + qi] = Ops::widen(v ? pa.qrows[((long)t * a.heads + h) * HD + d] : 0.0f);
+  }
+  __syncthreads();
+  int plast = 0;
+  for (int qi = 0; qi < QN; ++qi) plast = max(plast, qpos[qi]);
+  const int nk = (plast + CH - 1) / CH;  // chunks per pass
+  // chunk g of the sequence: K chunks 0..nk-1, then V chunks
+  auto issue = [&](int g) {
+    const bool v = g >= nk;
+    const int c0 = (v ? g - nk : g) * CH, count = min(CH, plast - c0);
+    uint64_t *bar = &bars[g & 1];
+    if (lane == 0) mbar_arrive_expect_tx(bar, (unsigned)(count * RB));
+    __syncwarp();
+    if (lane < count) {
+      const long p = c0 + lane;
+      const uint8_t *src =
+          Q8 ? reinterpret_cast<const uint8_t *>(v ? a.vcache : a.kcache) + (p * a.kv_heads + kvh) * RB
+             : reinterpret_cast<const uint8_t *>((v ? a.vcache : a.kcache) + p * a.kv_heads * HD + kvh * HD);
+      bulk_g2s(raw + ((g & 1) * CH + lane) * RB, src, (unsigned)RB, bar);
+    }
+  };
+  bool landed = true;
+  int issued = 0, waited = 0;
+  for (int g = 0; g < 2 && g < 2 * nk; ++g, ++issued)
+    if (warp == 0) issue(g);
+
+  // ---- scores ----
+  const int qg = lane >> 3, pg = lane & 7;
+  float runmax = -INFINITY;
+  for (int c = 0; c < nk && landed; ++c) {
+    const int c0 = c * CH, cn = min(CH, plast - c0), g = c;
+    landed = __syncthreads_and(mbar_wait_bounded(&bars[g & 1], (unsigned)(g >> 1) & 1u, a.status));
+    if (!landed) break;
+    ++waited;
+    {
+      const uint8_t *rb = raw + (g & 1) * CH * RB;
+      for (int pp = 0; pp < CH; ++pp)
+        rows[tid * (CH + 1) + pp] = pp < cn ? Ops::widen_row(rb + pp * RB, tid) : Ops::widen(0.0f);
+    }
+    __syncthreads();
+    if (g + 2 < 2 * nk) {
+      if (warp == 0) {
+        fence_proxy_async_smem();
+        issue(g + 2);
+      }
+      ++issued;
+    }
+    // partial tree R(b, 8) = (P_b + P_b+16) + (P_b+8 + P_b+24) of leaves
+    // (8-dimension chains) b = warp, for queries 4qg.. and positions pg+8i
+    double A[4][4], B[4][4], C[4][4];
+    auto leaf = [&](int l, double (&P)[4][4]) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int d = 8 * l + j;
+        T qv[4], kv[4];
+        if constexpr (Q8) {
+          const float4 q4 = *reinterpret_cast<const float4 *>(qT + d * QN + 4 * qg);
+          qv[0] = q4.x, qv[1] = q4.y, qv[2] = q4.z, qv[3] = q4.w;
+        } else {
+          const double2 qa = *reinterpret_cast<const double2 *>(qT + d * QN + 4 * qg);
+          const double2 qb = *reinterpret_cast<const double2 *>(qT + d * QN + 4 * qg + 2);
+          qv[0] = qa.x, qv[1] = qa.y, qv[2] = qb.x, qv[3] = qb.y;
+        }
+#pragma unroll
+        for (int y = 0; y < 4; ++y) kv[y] = rows[d * (CH + 1) + pg + 8 * y];
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+#pragma unroll
+          for (int y = 0; y < 4; ++y)
+            P[x][y] = j == 0 ? Ops::first(qv[x], kv[y]) : Ops::next(qv[x], kv[y], P[x][y]);
+      }
+    };
+    leaf(warp, A);
+    leaf(warp + 16, B);
+#pragma unroll
+    for (int x = 0; x < 4; ++x)
+#pragma unroll
+      for (int y = 0; y < 4; ++y) A[x][y] = A[x][y] + B[x][y];
+    leaf(warp + 8, B);
+    leaf(warp + 24, C);
+#pragma unroll
+    for (int x = 0; x < 4; ++x)
+#pragma unroll
+      for (int y = 0; y < 4; ++y)
+        Rs[(warp * QN + 4 * qg + x) * CH + pg + 8 * y] = A[x][y] + (B[x][y] + C[x][y]);
+    __syncthreads();
+    // the rest of the butterfly: ((R0+R4)+(R2+R6)) + ((R1+R5)+(R3+R7))
+    {
+      const int qi = tid >> 4;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int pp = (tid & 15) * 2 + e, p = c0 + pp;
+        if (pp < cn && p < qpos[qi]) {
+          const double *r = Rs + qi * CH + pp;
+          constexpr int st = QN * CH;
+          const double s = ((r[0] + r[4 * st]) + (r[2 * st] + r[6 * st])) +
+                           ((r[st] + r[5 * st]) + (r[3 * st] + r[7 * st]));
+          const float sc = __fmul_rn((float)s, scale);
+          S[(long)qi * pa.context + p] = sc;
+          runmax = fmaxf(runmax, sc);
+        }
+      }
+    }
+    __syncthreads();  // Rs and rows are rewritten by the next chunk
+  }
+  // maximum of each query's scores: the 16 threads tid>>4 == qi
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1)
+    runmax = fmaxf(runmax, __shfl_xor_sync(0xffffffffu, runmax, off));
+  if ((tid & 15) == 0) {
+    const int qi = tid >> 4;
+    qmax[qi] = runmax;
+    qM[qi] = qvalid[qi]
+                 ? fmaxf(pa.scur[(long)(t0 + qi / G) * a.heads + kvh * G + qi % G], runmax)
+                 : 0.0f;
+  }
+  __syncthreads();
+
+  // ---- softmax ----
+  // exponentials, 16 threads per query
+  {
+    const int qi = tid >> 4, pos = qpos[qi];
+    const float M = qM[qi];
+    float *Sq = S + (long)qi * pa.context;
+#pragma unroll 8
+    for (int p = tid & 15; p < pos; p += 16) Sq[p] = exp_cr(__fsub_rn(Sq[p], M));
+  }
+  __syncthreads();
+  // per (query, rank, warp of 32 virtual threads): the block sum's warp
+  // butterfly over each virtual thread's strided binary64 total
+  for (int k = tid; k < QN * 64; k += kPfThreads) {
+    const int qi = k >> 6, r = (k >> 3) & 7, w = k & 7, pos = qpos[qi];
+    const int per = (pos + 7) / 8, lo = min(pos, r * per), hi = min(pos, lo + per);
+    const float *Sq = S + (long)qi * pa.context;
+    const int base = lo + 32 * w;
+    double v[32];
+    if (base < hi) {
+      // virtual thread l's first term (0.0 + e is e; no term leaves 0.0),
+      // every load in flight at once; later terms only when per > 256
+      float e0[32];
+#pragma unroll
+      for (int l = 0; l < 32; ++l) e0[l] = base + l < hi ? Sq[base + l] : 0.0f;
+#pragma unroll
+      for (int l = 0; l < 32; ++l) v[l] = (double)e0[l];
+      if (base + 256 < hi) {
+#pragma unroll
+        for (int l = 0; l < 32; ++l)
+          for (int idx = base + 256 + l; idx < hi; idx += 256) v[l] += (double)Sq[idx];
+      }
+      W[k] = butterfly_sum32(v);
+    } else {
+      W[k] = 0.0;
+    }
+  }
+  __syncthreads();
+  if (tid < QN && qvalid[tid]) {
+    const int qi = tid, pos = qpos[qi], per = (pos + 7) / 8;
+    double total = 0.0;
+    for (int r = 0; r < 8; ++r) {
+      if (min(pos, r * per) >= min(pos, min(pos, r * per) + per)) continue;  // empty rank
+      double tr = 0.0;
+      for (int w = 0; w < 8; ++w) tr += W[qi * 64 + r * 8 + w];
+      total += tr;
+    }
+    const float M = qM[qi];
+    const float e_cur = exp_cr(__fsub_rn(pa.scur[(long)(t0 + qi / G) * a.heads + kvh * G + qi % G], M));
+    total += (double)e_cur;
+    const float inv = (float)(1.0 / total);
+    qinv[qi] = inv;
+    qpcur[qi] = round_f16(__fmul_rn(e_cur, inv));
+    if (!is_finite_f(M)) report(a.status, kStatusNonfinite);
+  }
+  __syncthreads();
+  {
+    const int qi = tid >> 4, pos = qvalid[qi] ? qpos[qi] : 0;
+    const float inv = qinv[qi];
+    float *Sq = S + (long)qi * pa.context;
+#pragma unroll 8
+    for (int p = tid & 15; p < pos; p += 16) Sq[p] = round_f16(__fmul_rn(Sq[p], inv));
+  }
+  __syncthreads();
+
+  // ---- values: thread d = tid, every query ----
+  // Each chunk is cut at the union of the queries' rank boundaries (and of
+  // the ends of their position ranges); within a segment every query's
+  // chain runs without a test, and at a cut the queries whose rank ends
+  // there fold their partial into the rank-ordered total.
+  double acc[QN], tot[QN];
+#pragma unroll
+  for (int qi = 0; qi < QN; ++qi) {
+    acc[qi] = -0.0;
+    tot[qi] = -0.0;
+  }
+  // this thread's two probabilities of the next chunk, loaded a chunk ahead
+  float pnext[2];
+  auto load_p = [&](int c0) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int k = tid + e * kPfThreads, pp = k / QN, qi = k % QN, p = c0 + pp;
+      pnext[e] = p < plast && p < qpos[qi] ? S[(long)qi * pa.context + p] : 0.0f;
+    }
+  };
+  load_p(0);
+  for (int c = 0; c < nk && landed; ++c) {
+    const int c0 = c * CH, cn = min(CH, plast - c0), g = nk + c;
+    landed = __syncthreads_and(mbar_wait_bounded(&bars[g & 1], (unsigned)(g >> 1) & 1u, a.status));
+    if (!landed) break;
+    ++waited;
+    {
+      const uint8_t *rb = raw + (g & 1) * CH * RB;
+      for (int pp = 0; pp < cn; ++pp) rows[pp * HD + tid] = Ops::widen_row(rb + pp * RB, tid);
+    }
+#pragma unroll
+    for (int e = 0; e < 2; ++e) pd[tid + e * kPfThreads] = Ops::widen(pnext[e]);
+    if (tid < QN) {
+      // rank boundaries of query tid inside the chunk, and its positions
+      // (a query past the prompt's end runs unchecked on zero
+      // probabilities; its sums are never stored)
+      const int pos = qpos[tid], per = (pos + 7) / 8;
+      const int cnt = qvalid[tid] ? max(0, min(cn, pos - c0)) : cn;
+      unsigned m = 0;
+      if (qvalid[tid] && cnt > 0) {
+        int b = (c0 + per - 1) / per * per;  // first multiple of per at or after c0
+        if (b == 0) b = per;
+        for (; b < c0 + cnt; b += per) m |= 1u << (b - c0);
+      }
+      qmask[tid] = m;
+      qcnt[tid] = cnt;
+    }
+    __syncthreads();
+    if (g + 2 < 2 * nk) {
+      if (warp == 0) {
+        fence_proxy_async_smem();
+        issue(g + 2);
+      }
+      ++issued;
+    }
+    if (c + 1 < nk) load_p(c0 + CH);
+    unsigned cuts = 0;
+    bool full = true;
+#pragma unroll
+    for (int qi = 0; qi < QN; ++qi) {
+      cuts |= qmask[qi];
+      if (qcnt[qi] < cn) {
+        full = false;
+        if (qcnt[qi] > 0) cuts |= 1u << qcnt[qi];
+      }
+    }
+    int pp = 0;
+    while (pp < cn) {
+      if ((cuts >> pp) & 1u) {
+#pragma unroll
+        for (int qi = 0; qi < QN; ++qi)
+          if ((qmask[qi] >> pp) & 1u) {
+            tot[qi] += acc[qi];
+            acc[qi] = -0.0;
+          }
+      }
+      const unsigned above = pp < 31 ? cuts & ~((2u << pp) - 1u) : 0u;
+      const int end = above ? min(cn, __ffs(above) - 1) : cn;
+      if (full) {
+        for (; pp < end; ++pp) {
+          const T vv = rows[pp * HD + tid];
+          const T *pr = pd + pp * QN;
+#pragma unroll
+          for (int qi = 0; qi < QN; ++qi) acc[qi] = Ops::next(pr[qi], vv, acc[qi]);
+        }
+      } else {
+        // the chunk where some queries' positions end: the active set is
+        // constant within the segment
+        bool act[QN];
+#pragma unroll
+        for (int qi = 0; qi < QN; ++qi) act[qi] = pp < qcnt[qi];
+        for (; pp < end; ++pp) {
+          const T vv = rows[pp * HD + tid];
+          const T *pr = pd + pp * QN;
+#pragma unroll
+          for (int qi = 0; qi < QN; ++qi)
+            if (act[qi]) acc[qi] = Ops::next(pr[qi], vv, acc[qi]);
+        }
+      }
+    }
+    __syncthreads();  // rows, pd and the masks are rewritten by the next chunk
+  }
+  // a chunk that never landed: let the copies still in flight finish
+  // (bounded) before the CTA exits
+  if (issued > waited && tid == 0)
+    for (int g = waited; g < issued; ++g)
+      mbar_wait_bounded(&bars[g & 1], (unsigned)(g >> 1) & 1u, a.status);
+#pragma unroll
+  for (int qi = 0; qi < QN; ++qi) {
+    if (!qvalid[qi]) continue;
+    const int pos = qpos[qi], h = kvh * G + qi % G, t = t0 + qi / G;
+    double sum = tot[qi] + acc[qi];
+    const float vc =
+        Q8 ? q8_0_value(reinterpret_cast<const uint8_t *>(a.vcache) + ((long)pos * a.kv_heads + kvh) * RB,
+                        HD, tid)
+           : half_bits_to_float(a.vcache[(long)pos * a.kv_heads * HD + kvh * HD + tid]);
+    sum += (double)__fmul_rn(qpcur[qi], vc);
+    const float out = (float)sum;
+    const float gt = a.projected[(long)t * a.seq_proj + (long)(2 * h + 1) * HD + tid];
+    a.attended[(long)t * a.seq_out + (long)h * HD + tid] = __fmul_rn(out, sigmoid_f(gt));
+  }
+}
+
 __global__ void fill_positions_kernel(int *pos, int p0, int T, int *model_position) {
   for (int t = threadIdx.x; t < T; t += blockDim.x) pos[t] = p0 + t;
   if (threadIdx.x == 0 && model_position) *model_position = p0 + T;
@@ -246,6 +719,13 @@ __global__ void fill_positions_kernel(int *pos, int p0, int T, int *model_positi
 }  // namespace prism
 
 namespace prism {
+
+// The batched attention kernel's geometry: one thread per head dimension
+// (256) and whole KV groups in a CTA's kPfQueries queries.
+inline bool prefill_attn_geometry(const prism_b200_qwen35_config &c) {
+  const uint32_t G = c.kv_heads ? c.heads / c.kv_heads : 0;
+  return c.head_dim == 256 && G >= 1 && G <= (uint32_t)kPfQueries && c.heads == G * c.kv_heads;
+}
 
 inline cudaError_t prefill_alloc(prism_b200_model *m) {
   PrefillBuffers &pb = m->pre;
@@ -277,6 +757,20 @@ inline cudaError_t prefill_alloc(prism_b200_model *m) {
   A(&tok, token_q8k_bytes(T, (int)(widest / 256)));
   pb.tok = tok;
   A(&pb.pos, T);
+  if (prefill_attn_geometry(c)) {
+    const size_t TQ = kPfQueries / (c.heads / c.kv_heads);
+    A(&pb.qrows, T * c.heads * c.head_dim);
+    A(&pb.scur, T * c.heads);
+    A(&pb.scratch, (size_t)c.kv_heads * ((T + TQ - 1) / TQ) * kPfQueries * c.context);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_prefill_kernel<false>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)prefill_attn_smem<false>());
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_prefill_kernel<true>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)prefill_attn_smem<true>());
+  }
   pb.ready = e == cudaSuccess;
   return e;
 }
@@ -350,16 +844,30 @@ inline cudaError_t enqueue_prefill(prism_b200_model *m, int p0, int T) {
       aa.status = status;
       kv_rows_kernel<<<dim3(c.kv_heads, T), kAttnThreads, 0, s>>>(aa, p0);
       PK(cudaGetLastError());
-      const size_t smem = attn_launch_smem(aa, (int)c.context);
-      cudaLaunchAttribute cattr[2];
-      cudaLaunchConfig_t cfg =
-          pdl_config(dim3(c.heads * kAttnSplit, T), dim3(kAttnThreads), smem, s, cattr, false);
-      cattr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
-      cattr[cfg.numAttrs].val.clusterDim.x = kAttnSplit;
-      cattr[cfg.numAttrs].val.clusterDim.y = 1;
-      cattr[cfg.numAttrs].val.clusterDim.z = 1;
-      cfg.numAttrs += 1;
-      PK(cudaLaunchKernelEx(&cfg, attention_decode_kernel, aa));
+      if (prefill_attn_geometry(c)) {
+        const int G = (int)(c.heads / c.kv_heads), TQ = kPfQueries / G;
+        query_rows_kernel<<<dim3(c.heads, T), kAttnThreads, 0, s>>>(aa, p0, pb.qrows, pb.scur);
+        PK(cudaGetLastError());
+        PrefillAttnArgs pa{aa, p0, T, G, TQ, (int)c.context, pb.qrows, pb.scur, pb.scratch};
+        const dim3 grid(c.kv_heads, (T + TQ - 1) / TQ);
+        if (aa.q8)
+          attention_prefill_kernel<true><<<grid, kPfThreads, prefill_attn_smem<true>(), s>>>(pa);
+        else
+          attention_prefill_kernel<false><<<grid, kPfThreads, prefill_attn_smem<false>(), s>>>(pa);
+        PK(cudaGetLastError());
+      } else {
+        // other geometries: attention_decode_kernel, one grid row per token
+        const size_t smem = attn_launch_smem(aa, (int)c.context);
+        cudaLaunchAttribute cattr[2];
+        cudaLaunchConfig_t cfg =
+            pdl_config(dim3(c.heads * kAttnSplit, T), dim3(kAttnThreads), smem, s, cattr, false);
+        cattr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+        cattr[cfg.numAttrs].val.clusterDim.x = kAttnSplit;
+        cattr[cfg.numAttrs].val.clusterDim.y = 1;
+        cattr[cfg.numAttrs].val.clusterDim.z = 1;
+        cfg.numAttrs += 1;
+        PK(cudaLaunchKernelEx(&cfg, attention_decode_kernel, aa));
+      }
       PK(quant(pb.attended, (int)(c.heads * c.head_dim / 256)));
       PK(mm(Ly.o, pb.hidden, pb.hidden));
     } else {

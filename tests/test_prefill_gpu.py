@@ -93,9 +93,11 @@ def test_single_token_prefill():
     _check(qwen35.SMALL, 0, [1, 1, 2], seed=65)
 
 
-def test_config1_geometry_prefill():
+@pytest.mark.parametrize("kv_policy", [0, 1])
+def test_config1_geometry_prefill(kv_policy):
+    # 4 query heads per KV head: 4 tokens per attention CTA
     cfg = dataclasses.replace(qwen35.CONFIG1, layers=8)
-    _check(cfg, 1, [45, 20], seed=67)
+    _check(cfg, kv_policy, [45, 20], seed=67)
 
 
 def test_ingest_block_bounds_and_parity():

@@ -677,12 +677,12 @@ PREFILL_TOKENS = 4096
 PREFILL_METRIC = "prefill tok/s (batch 1, 4096-token prompt)"
 
 
-def prefill_launches(cfg, tokens, chunk=512):
-    """Kernels of one prism_b200_model_prefill_async call: per 512-token pass
+def prefill_launches(cfg, tokens, chunk=2048):
+    """Kernels of one prism_b200_model_prefill_async call: per 2048-token pass
     the positions, the embedding and the final position update, then per
     layer norm + quantize + projections + the mixer's kernels + FFN."""
     gdn = 2 + 4 + 4 + 2 + 1      # norm, quant, 4 GEMMs, inputs, scan, history, gated, quant, out
-    att = 2 + 3 + 2 + 1 + 1      # norm, quant, q/k/v GEMMs, kv rows, attention, quant, o
+    att = 2 + 3 + 3 + 1 + 1      # norm, quant, q/k/v GEMMs, kv rows, query rows, attention, quant, o
     ffn = 2 + 2 + 1 + 1 + 1      # norm, quant, up/gate, swiglu, quant, down
     per_pass = 3 + sum((att if cfg.is_full(l) else gdn) + ffn for l in range(cfg.layers))
     return per_pass * ((tokens + chunk - 1) // chunk)
@@ -768,7 +768,7 @@ def run_prefill(args):
         "data": "synthetic (random-init weights, random prompt; no public dataset)",
         "config": {"workload": "configs[1] model (hidden 2560, 32 layers, TQ2_0 seed 0): "
                                "batched ingestion of a %d-token random prompt (seed 1) from "
-                               "position 0, 512-token passes, no LM head" % P,
+                               "position 0, 2048-token passes, no LM head" % P,
                    "l2": "each pass streams the ~1 GB of weights (> 126 MB L2)"},
         "clocks": clk.summary(),
         "gpu_launches": K * prefill_launches(cfg, P),

@@ -338,7 +338,7 @@ int prism_b200_model_ingest_async(prism_b200_model *m, size_t n);
 /* Batched prompt ingestion (replaces Decoder::ingest_block, src/lib.rs:229-247,
  * and its tiled override, src/graph.rs:5459-5461).  prefill_async enqueues,
  * without waiting, the ingestion of the `n` tokens that set_prompt placed at
- * the next positions: every layer processes up to 512 tokens at once
+ * the next positions: every layer processes up to 2048 tokens at once
  * (tensor-core projections over the tokens, the Gated DeltaNet recurrence
  * token after token with its state on chip, causal attention of each token
  * over its prefix).  The KV rows, recurrent and convolution state and

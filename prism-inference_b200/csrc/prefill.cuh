@@ -23,7 +23,7 @@
 
 namespace prism {
 
-constexpr int kPrefillChunk = 512;  // tokens per batched pass
+constexpr int kPrefillChunk = 2048;  // tokens per batched pass
 
 // ---- Gated DeltaNet over the prompt's tokens --------------------------------
 //
@@ -47,7 +47,7 @@ struct GdnTokensArgs {
   unsigned *status;
 };
 
-constexpr int kScanRows = 4;  // state rows (warps) per CTA of the scan
+constexpr int kScanRows = 16;  // state rows (warps) per CTA of the scan
 
 // grid (T, 2 * groups + values), S (= 128) threads: block y < groups is q
 // group y, y < 2 * groups k group y - groups, else v head y - 2 * groups
@@ -88,75 +88,119 @@ __global__ void __launch_bounds__(128) gdn_token_inputs_kernel(GdnTokensArgs a) 
   a.act[(long)t * a.channels + ch] = act;
 }
 
-// One warp per state row r of value head h (grid values * S / kScanRows,
-// kScanRows warps): the row stays in registers for the whole prompt, lane l
-// owning columns 4l .. 4l+3.  Per token, run_gdn's row arithmetic in its
-// order: decay, s.k (binary64 partials, warp butterfly), delta, update,
-// s.q.  The next token's inputs are loaded kDepth tokens ahead, and the
-// butterfly of token t's s.q runs beside token t+1's s.k.
-__global__ void __launch_bounds__(32 * kScanRows) gdn_rows_scan_kernel(GdnTokensArgs a) {
-  constexpr int S = 128, kDepth = 4;
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kScanRows + (threadIdx.x >> 5);  // h * S + r
-  if (row >= a.values * S) return;
-  const int h = row / S, kh = h % a.groups, kw = a.groups * S;
+// One warp per state row of value head h, kScanRows rows of one head per
+// CTA (grid values * S / kScanRows, 32 * kScanRows threads): each row stays
+// in its warp's registers for the whole prompt, lane l owning columns
+// 4l .. 4l+3.  Per token, run_gdn's row arithmetic in its order: decay, s.k
+// (binary64 partials, warp butterfly), delta, update, s.q.  The tokens'
+// q, k, v, decay and beta come through shared memory in chunks of
+// kScanTokens, loaded cooperatively a chunk ahead; within a chunk the
+// butterfly of token t's s.q runs beside token t+1's s.k.  Outputs leave
+// once per chunk, coalesced.
+constexpr int kScanTokens = 32;
+
+constexpr size_t gdn_scan_smem() {
+  return (size_t)2 * kScanTokens * (2 * 128 + 2 * kScanRows + 2) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(32 * kScanRows, 1) gdn_rows_scan_kernel(GdnTokensArgs a) {
+  constexpr int S = 128, R = kScanRows, TC = kScanTokens, NT = 32 * R;
+  extern __shared__ __align__(128) uint8_t smem[];
+  float *qs = reinterpret_cast<float *>(smem);  // [2][TC][S]
+  float *ks = qs + 2 * TC * S;                  // [2][TC][S]
+  float *vs = ks + 2 * TC * S;                  // [2][TC][R]
+  float *os = vs + 2 * TC * R;                  // [2][TC][R]
+  float *ds = os + 2 * TC * R;                  // [2][TC][2] decay, beta
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row0 = blockIdx.x * R, row = row0 + warp;  // h * S + r
+  if (row0 >= a.values * S) return;
+  const int h = row0 / S, kh = h % a.groups, kw = a.groups * S;
   float *srow = a.state + (long)row * S;
   float4 s = reinterpret_cast<const float4 *>(srow)[lane];
   const float oscale = __fdiv_rn(1.0f, __fsqrt_rn((float)S));
-  const float *qbase = a.act + kh * S + 4 * lane;
-  const float *kbase = a.act + kw + kh * S + 4 * lane;
-  const float *vbase = a.act + 2 * kw + row;
-  const float *dbase = a.db + 2 * h;
-  float4 K[kDepth], Q[kDepth];
-  float V[kDepth], DC[kDepth], BT[kDepth];
-  auto load = [&](int u, int t) {
-    const long o = (long)t * a.channels;
-    K[u] = *reinterpret_cast<const float4 *>(kbase + o);
-    Q[u] = *reinterpret_cast<const float4 *>(qbase + o);
-    V[u] = vbase[o];
-    DC[u] = dbase[(long)t * a.values * 2];
-    BT[u] = dbase[(long)t * a.values * 2 + 1];
-  };
+  const int nc = (a.T + TC - 1) / TC;
+  // cooperative chunk loads: q and k as float4 (TC * S / 4 each), v as
+  // float4 (TC * R / 4), decay and beta (TC pairs)
+  constexpr int QV = TC * S / 4, VV = TC * R / 4;
+  static_assert(QV % NT == 0, "q/k chunk split");
+  float4 rq[QV / NT], rk[QV / NT], rv = make_float4(0.f, 0.f, 0.f, 0.f);
+  float2 rd = make_float2(0.f, 0.f);
+  auto load = [&](int c) {
+    const int tb = c * TC;
 #pragma unroll
-  for (int u = 0; u < kDepth; ++u)
-    if (u < a.T) load(u, u);
-  bool finite = true;
-  double dqp = 0.0;  // s.q partial of the previous token
-  for (int t0 = 0; t0 < a.T; t0 += kDepth) {
-#pragma unroll
-    for (int u = 0; u < kDepth; ++u) {
-      const int t = t0 + u;
-      if (t < a.T) {
-        const float4 kk = K[u], qq = Q[u];
-        const float vv = V[u], decay = DC[u], beta = BT[u];
-        if (t + kDepth < a.T) load(u, t + kDepth);
-        s.x = __fmul_rn(decay, s.x);
-        s.y = __fmul_rn(decay, s.y);
-        s.z = __fmul_rn(decay, s.z);
-        s.w = __fmul_rn(decay, s.w);
-        double dk = (double)__fmul_rn(s.x, kk.x) + (double)__fmul_rn(s.y, kk.y) +
-                    (double)__fmul_rn(s.z, kk.z) + (double)__fmul_rn(s.w, kk.w);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-          dk += __shfl_xor_sync(0xffffffffu, dk, off);
-          dqp += __shfl_xor_sync(0xffffffffu, dqp, off);
-        }
-        if (t > 0 && lane == 0)
-          a.o_pre[(long)(t - 1) * a.values * S + row] = __fmul_rn((float)dqp, oscale);
-        const float delta = __fmul_rn(__fsub_rn(vv, (float)dk), beta);
-        s.x = __fadd_rn(s.x, __fmul_rn(delta, kk.x));
-        s.y = __fadd_rn(s.y, __fmul_rn(delta, kk.y));
-        s.z = __fadd_rn(s.z, __fmul_rn(delta, kk.z));
-        s.w = __fadd_rn(s.w, __fmul_rn(delta, kk.w));
-        finite &= is_finite_f(s.x) && is_finite_f(s.y) && is_finite_f(s.z) && is_finite_f(s.w);
-        dqp = (double)__fmul_rn(s.x, qq.x) + (double)__fmul_rn(s.y, qq.y) +
-              (double)__fmul_rn(s.z, qq.z) + (double)__fmul_rn(s.w, qq.w);
-      }
+    for (int i = 0; i < QV / NT; ++i) {
+      const int e = tid + i * NT, t = tb + e / (S / 4), j = 4 * (e % (S / 4));
+      const long o = (long)t * a.channels;
+      rq[i] = t < a.T ? *reinterpret_cast<const float4 *>(a.act + o + kh * S + j)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      rk[i] = t < a.T ? *reinterpret_cast<const float4 *>(a.act + o + kw + kh * S + j)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-  }
-  if (a.T > 0) {
-    dqp = warp_sum_f64(dqp);
-    if (lane == 0) a.o_pre[(long)(a.T - 1) * a.values * S + row] = __fmul_rn((float)dqp, oscale);
+    if (tid < VV) {
+      const int t = tb + tid / (R / 4), j = 4 * (tid % (R / 4));
+      rv = t < a.T ? *reinterpret_cast<const float4 *>(a.act + (long)t * a.channels + 2 * kw + row0 + j)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (tid < TC) {
+      const int t = tb + tid;
+      rd = t < a.T ? *reinterpret_cast<const float2 *>(a.db + ((long)t * a.values + h) * 2)
+                   : make_float2(0.f, 0.f);
+    }
+  };
+  auto store = [&](int b) {
+#pragma unroll
+    for (int i = 0; i < QV / NT; ++i) {
+      const int e = tid + i * NT;
+      reinterpret_cast<float4 *>(qs + b * TC * S)[e] = rq[i];
+      reinterpret_cast<float4 *>(ks + b * TC * S)[e] = rk[i];
+    }
+    if (tid < VV) reinterpret_cast<float4 *>(vs + b * TC * R)[tid] = rv;
+    if (tid < TC) reinterpret_cast<float2 *>(ds + b * TC * 2)[tid] = rd;
+  };
+  load(0);
+  store(0);
+  __syncthreads();
+  bool finite = true;
+  for (int c = 0; c < nc; ++c) {
+    const int b = c & 1, tb = c * TC, tn = min(TC, a.T - tb);
+    if (c + 1 < nc) load(c + 1);  // in flight during this chunk's recurrence
+    const float *qb = qs + b * TC * S, *kb = ks + b * TC * S;
+    const float *vb = vs + b * TC * R, *db = ds + b * TC * 2;
+    float *ob = os + b * TC * R;
+    double dqp = 0.0;  // s.q partial of the previous token
+    for (int tt = 0; tt < tn; ++tt) {
+      const float4 kk = reinterpret_cast<const float4 *>(kb + tt * S)[lane];
+      const float4 qq = reinterpret_cast<const float4 *>(qb + tt * S)[lane];
+      const float vv = vb[tt * R + warp], decay = db[2 * tt], beta = db[2 * tt + 1];
+      s.x = __fmul_rn(decay, s.x);
+      s.y = __fmul_rn(decay, s.y);
+      s.z = __fmul_rn(decay, s.z);
+      s.w = __fmul_rn(decay, s.w);
+      double dk = (double)__fmul_rn(s.x, kk.x) + (double)__fmul_rn(s.y, kk.y) +
+                  (double)__fmul_rn(s.z, kk.z) + (double)__fmul_rn(s.w, kk.w);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        dk += __shfl_xor_sync(0xffffffffu, dk, off);
+        dqp += __shfl_xor_sync(0xffffffffu, dqp, off);
+      }
+      if (tt > 0 && lane == 0) ob[(tt - 1) * R + warp] = __fmul_rn((float)dqp, oscale);
+      const float delta = __fmul_rn(__fsub_rn(vv, (float)dk), beta);
+      s.x = __fadd_rn(s.x, __fmul_rn(delta, kk.x));
+      s.y = __fadd_rn(s.y, __fmul_rn(delta, kk.y));
+      s.z = __fadd_rn(s.z, __fmul_rn(delta, kk.z));
+      s.w = __fadd_rn(s.w, __fmul_rn(delta, kk.w));
+      finite &= is_finite_f(s.x) && is_finite_f(s.y) && is_finite_f(s.z) && is_finite_f(s.w);
+      dqp = (double)__fmul_rn(s.x, qq.x) + (double)__fmul_rn(s.y, qq.y) +
+            (double)__fmul_rn(s.z, qq.z) + (double)__fmul_rn(s.w, qq.w);
+    }
+    if (tn > 0) {
+      dqp = warp_sum_f64(dqp);
+      if (lane == 0) ob[(tn - 1) * R + warp] = __fmul_rn((float)dqp, oscale);
+    }
+    if (c + 1 < nc) store(b ^ 1);
+    __syncthreads();  // the next chunk's inputs and this chunk's outputs are complete
+    for (int e = tid; e < tn * R; e += NT)
+      a.o_pre[(long)(tb + e / R) * a.values * S + row0 + e % R] = ob[e];
   }
   reinterpret_cast<float4 *>(srow)[lane] = s;
   if (!__all_sync(0xffffffffu, finite) && lane == 0) report(a.status, kStatusNonfinite);
@@ -757,6 +801,9 @@ inline cudaError_t prefill_alloc(prism_b200_model *m) {
   A(&tok, token_q8k_bytes(T, (int)(widest / 256)));
   pb.tok = tok;
   A(&pb.pos, T);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gdn_rows_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)gdn_scan_smem());
   if (prefill_attn_geometry(c)) {
     const size_t TQ = kPfQueries / (c.heads / c.kv_heads);
     A(&pb.qrows, T * c.heads * c.head_dim);
@@ -900,7 +947,7 @@ inline cudaError_t enqueue_prefill(prism_b200_model *m, int p0, int T) {
       g.status = status;
       gdn_token_inputs_kernel<<<dim3(T, 2 * c.ssm_groups + c.ssm_values), 128, 0, s>>>(g);
       PK(cudaGetLastError());
-      gdn_rows_scan_kernel<<<c.ssm_values * S / kScanRows, 32 * kScanRows, 0, s>>>(g);
+      gdn_rows_scan_kernel<<<c.ssm_values * S / kScanRows, 32 * kScanRows, gdn_scan_smem(), s>>>(g);
       PK(cudaGetLastError());
       conv_history_kernel<<<(m->channels() + 255) / 256, 256, 0, s>>>(
           pb.mixed, hist_in, hist_out, m->channels(), (int)c.conv_kernel - 1, T);

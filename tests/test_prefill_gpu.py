@@ -84,9 +84,9 @@ def test_small_prefill_matches_ingestion(kv_policy):
 
 
 def test_prefill_spanning_chunks():
-    # 600 tokens: a 512-token pass, then 88 more over the first pass's rows
-    cfg = dataclasses.replace(qwen35.SMALL, context=1100)
-    _check(cfg, 1, [600, 3], seed=63)
+    # 2100 tokens: a 2048-token pass, then 52 more over the first pass's rows
+    cfg = dataclasses.replace(qwen35.SMALL, context=2200)
+    _check(cfg, 1, [2100, 3], seed=63)
 
 
 def test_single_token_prefill():

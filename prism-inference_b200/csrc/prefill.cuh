@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(kAttnThreads) kv_rows_kernel(AttnArgs a, int p
 
 constexpr int kPfQueries = 16;  // (token, head) queries per CTA
 constexpr int kPfChunk = 32;    // positions per staged chunk
-constexpr int kPfThreads = 256; // one thread per head dimension in the value pass
+constexpr int kPfThreads = 512; // two threads per head dimension in the value pass
 
 struct PrefillAttnArgs {
   AttnArgs a;       // geometry, norms, caches; projected/attended strides per token
@@ -410,7 +410,9 @@ __device__ __forceinline__ double butterfly_sum32(const double (&v)[32]) {
 // kPfQueries.  Query qi = tl * G + g is token t0 + tl, head kvh * G + g.
 // The K rows and then the V rows of positions 0 .. (last query's position)
 // stream through two raw buffers in chunks of kPfChunk (bulk copies, one per
-// row, issued two chunks ahead).
+// row, issued two chunks ahead).  16 warps: the score pass splits the leaf
+// groups and the query halves, the value pass the dimensions and the query
+// halves.
 template <bool Q8>
 __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(PrefillAttnArgs pa) {
   using Ops = PfOps<Q8>;
@@ -477,7 +479,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
     if (warp == 0) issue(g);
 
   // ---- scores ----
-  const int qg = lane >> 3, pg = lane & 7;
+  // warp w: leaf group w & 7, queries 8 (w >> 3) + 2 qg + x, positions pg + 8 y
+  const int lg = warp & 7, q0 = 8 * (warp >> 3) + 2 * (lane >> 3), pg = lane & 7;
   float runmax = -INFINITY;
   for (int c = 0; c < nk && landed; ++c) {
     const int c0 = c * CH, cn = min(CH, plast - c0), g = c;
@@ -486,8 +489,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
     ++waited;
     {
       const uint8_t *rb = raw + (g & 1) * CH * RB;
-      for (int pp = 0; pp < CH; ++pp)
-        rows[tid * (CH + 1) + pp] = pp < cn ? Ops::widen_row(rb + pp * RB, tid) : Ops::widen(0.0f);
+      const int d = tid & (HD - 1), p1 = (tid / HD) * (CH / 2);
+      for (int pp = p1; pp < p1 + CH / 2; ++pp)
+        rows[d * (CH + 1) + pp] = pp < cn ? Ops::widen_row(rb + pp * RB, d) : Ops::widen(0.0f);
     }
     __syncthreads();
     if (g + 2 < 2 * nk) {
@@ -498,50 +502,49 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
       ++issued;
     }
     // partial tree R(b, 8) = (P_b + P_b+16) + (P_b+8 + P_b+24) of leaves
-    // (8-dimension chains) b = warp, for queries 4qg.. and positions pg+8i
-    double A[4][4], B[4][4], C[4][4];
-    auto leaf = [&](int l, double (&P)[4][4]) {
+    // (8-dimension chains) b = lg, for queries q0, q0+1 and positions pg+8y
+    double A[2][4], B[2][4], C[2][4];
+    auto leaf = [&](int l, double (&P)[2][4]) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int d = 8 * l + j;
-        T qv[4], kv[4];
+        T qv[2], kv[4];
         if constexpr (Q8) {
-          const float4 q4 = *reinterpret_cast<const float4 *>(qT + d * QN + 4 * qg);
-          qv[0] = q4.x, qv[1] = q4.y, qv[2] = q4.z, qv[3] = q4.w;
+          const float2 q2 = *reinterpret_cast<const float2 *>(qT + d * QN + q0);
+          qv[0] = q2.x, qv[1] = q2.y;
         } else {
-          const double2 qa = *reinterpret_cast<const double2 *>(qT + d * QN + 4 * qg);
-          const double2 qb = *reinterpret_cast<const double2 *>(qT + d * QN + 4 * qg + 2);
-          qv[0] = qa.x, qv[1] = qa.y, qv[2] = qb.x, qv[3] = qb.y;
+          const double2 q2 = *reinterpret_cast<const double2 *>(qT + d * QN + q0);
+          qv[0] = q2.x, qv[1] = q2.y;
         }
 #pragma unroll
         for (int y = 0; y < 4; ++y) kv[y] = rows[d * (CH + 1) + pg + 8 * y];
 #pragma unroll
-        for (int x = 0; x < 4; ++x)
+        for (int x = 0; x < 2; ++x)
 #pragma unroll
           for (int y = 0; y < 4; ++y)
             P[x][y] = j == 0 ? Ops::first(qv[x], kv[y]) : Ops::next(qv[x], kv[y], P[x][y]);
       }
     };
-    leaf(warp, A);
-    leaf(warp + 16, B);
+    leaf(lg, A);
+    leaf(lg + 16, B);
 #pragma unroll
-    for (int x = 0; x < 4; ++x)
+    for (int x = 0; x < 2; ++x)
 #pragma unroll
       for (int y = 0; y < 4; ++y) A[x][y] = A[x][y] + B[x][y];
-    leaf(warp + 8, B);
-    leaf(warp + 24, C);
+    leaf(lg + 8, B);
+    leaf(lg + 24, C);
 #pragma unroll
-    for (int x = 0; x < 4; ++x)
+    for (int x = 0; x < 2; ++x)
 #pragma unroll
       for (int y = 0; y < 4; ++y)
-        Rs[(warp * QN + 4 * qg + x) * CH + pg + 8 * y] = A[x][y] + (B[x][y] + C[x][y]);
+        Rs[(lg * QN + q0 + x) * CH + pg + 8 * y] = A[x][y] + (B[x][y] + C[x][y]);
     __syncthreads();
-    // the rest of the butterfly: ((R0+R4)+(R2+R6)) + ((R1+R5)+(R3+R7))
+    // the rest of the butterfly: ((R0+R4)+(R2+R6)) + ((R1+R5)+(R3+R7)), one
+    // (query, position) per thread
     {
-      const int qi = tid >> 4;
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int pp = (tid & 15) * 2 + e, p = c0 + pp;
+      const int qi = tid >> 5;
+      {
+        const int pp = tid & 31, p = c0 + pp;
         if (pp < cn && p < qpos[qi]) {
           const double *r = Rs + qi * CH + pp;
           constexpr int st = QN * CH;
@@ -555,12 +558,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
     }
     __syncthreads();  // Rs and rows are rewritten by the next chunk
   }
-  // maximum of each query's scores: the 16 threads tid>>4 == qi
+  // maximum of each query's scores: warp qi
 #pragma unroll
-  for (int off = 8; off > 0; off >>= 1)
+  for (int off = 16; off > 0; off >>= 1)
     runmax = fmaxf(runmax, __shfl_xor_sync(0xffffffffu, runmax, off));
-  if ((tid & 15) == 0) {
-    const int qi = tid >> 4;
+  if (lane == 0) {
+    const int qi = warp;
     qmax[qi] = runmax;
     qM[qi] = qvalid[qi]
                  ? fmaxf(pa.scur[(long)(t0 + qi / G) * a.heads + kvh * G + qi % G], runmax)
@@ -569,13 +572,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
   __syncthreads();
 
   // ---- softmax ----
-  // exponentials, 16 threads per query
+  // exponentials, a warp per query
   {
-    const int qi = tid >> 4, pos = qpos[qi];
+    const int qi = warp, pos = qpos[qi];
     const float M = qM[qi];
     float *Sq = S + (long)qi * pa.context;
 #pragma unroll 8
-    for (int p = tid & 15; p < pos; p += 16) Sq[p] = exp_cr(__fsub_rn(Sq[p], M));
+    for (int p = lane; p < pos; p += 32) Sq[p] = exp_cr(__fsub_rn(Sq[p], M));
   }
   __syncthreads();
   // per (query, rank, warp of 32 virtual threads): the block sum's warp
@@ -624,33 +627,33 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
   }
   __syncthreads();
   {
-    const int qi = tid >> 4, pos = qvalid[qi] ? qpos[qi] : 0;
+    const int qi = warp, pos = qvalid[qi] ? qpos[qi] : 0;
     const float inv = qinv[qi];
     float *Sq = S + (long)qi * pa.context;
 #pragma unroll 8
-    for (int p = tid & 15; p < pos; p += 16) Sq[p] = round_f16(__fmul_rn(Sq[p], inv));
+    for (int p = lane; p < pos; p += 32) Sq[p] = round_f16(__fmul_rn(Sq[p], inv));
   }
   __syncthreads();
 
-  // ---- values: thread d = tid, every query ----
+  // ---- values: thread (d, qh) = (tid % 256, tid / 256), queries 8qh.. ----
   // Each chunk is cut at the union of the queries' rank boundaries (and of
   // the ends of their position ranges); within a segment every query's
   // chain runs without a test, and at a cut the queries whose rank ends
   // there fold their partial into the rank-ordered total.
-  double acc[QN], tot[QN];
+  constexpr int QH = QN / 2;
+  const int d = tid & (HD - 1), qh = tid / HD, qb = QH * qh;
+  double acc[QH], tot[QH];
 #pragma unroll
-  for (int qi = 0; qi < QN; ++qi) {
-    acc[qi] = -0.0;
-    tot[qi] = -0.0;
+  for (int x = 0; x < QH; ++x) {
+    acc[x] = -0.0;
+    tot[x] = -0.0;
   }
-  // this thread's two probabilities of the next chunk, loaded a chunk ahead
-  float pnext[2];
+  // this thread's probability of the next chunk, loaded a chunk ahead
+  static_assert(CH * QN == kPfThreads, "one probability per thread");
+  float pnext;
   auto load_p = [&](int c0) {
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int k = tid + e * kPfThreads, pp = k / QN, qi = k % QN, p = c0 + pp;
-      pnext[e] = p < plast && p < qpos[qi] ? S[(long)qi * pa.context + p] : 0.0f;
-    }
+    const int pp = tid / QN, qi = tid % QN, p = c0 + pp;
+    pnext = p < plast && p < qpos[qi] ? S[(long)qi * pa.context + p] : 0.0f;
   };
   load_p(0);
   for (int c = 0; c < nk && landed; ++c) {
@@ -660,10 +663,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
     ++waited;
     {
       const uint8_t *rb = raw + (g & 1) * CH * RB;
-      for (int pp = 0; pp < cn; ++pp) rows[pp * HD + tid] = Ops::widen_row(rb + pp * RB, tid);
+      const int p1 = qh * (CH / 2), p2 = min(cn, p1 + CH / 2);
+      for (int pp = p1; pp < p2; ++pp) rows[pp * HD + d] = Ops::widen_row(rb + pp * RB, d);
     }
-#pragma unroll
-    for (int e = 0; e < 2; ++e) pd[tid + e * kPfThreads] = Ops::widen(pnext[e]);
+    pd[tid] = Ops::widen(pnext);
     if (tid < QN) {
       // rank boundaries of query tid inside the chunk, and its positions
       // (a query past the prompt's end runs unchecked on zero
@@ -702,33 +705,33 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
     while (pp < cn) {
       if ((cuts >> pp) & 1u) {
 #pragma unroll
-        for (int qi = 0; qi < QN; ++qi)
-          if ((qmask[qi] >> pp) & 1u) {
-            tot[qi] += acc[qi];
-            acc[qi] = -0.0;
+        for (int x = 0; x < QH; ++x)
+          if ((qmask[qb + x] >> pp) & 1u) {
+            tot[x] += acc[x];
+            acc[x] = -0.0;
           }
       }
       const unsigned above = pp < 31 ? cuts & ~((2u << pp) - 1u) : 0u;
       const int end = above ? min(cn, __ffs(above) - 1) : cn;
       if (full) {
         for (; pp < end; ++pp) {
-          const T vv = rows[pp * HD + tid];
-          const T *pr = pd + pp * QN;
+          const T vv = rows[pp * HD + d];
+          const T *pr = pd + pp * QN + qb;
 #pragma unroll
-          for (int qi = 0; qi < QN; ++qi) acc[qi] = Ops::next(pr[qi], vv, acc[qi]);
+          for (int x = 0; x < QH; ++x) acc[x] = Ops::next(pr[x], vv, acc[x]);
         }
       } else {
         // the chunk where some queries' positions end: the active set is
         // constant within the segment
-        bool act[QN];
+        bool act[QH];
 #pragma unroll
-        for (int qi = 0; qi < QN; ++qi) act[qi] = pp < qcnt[qi];
+        for (int x = 0; x < QH; ++x) act[x] = pp < qcnt[qb + x];
         for (; pp < end; ++pp) {
-          const T vv = rows[pp * HD + tid];
-          const T *pr = pd + pp * QN;
+          const T vv = rows[pp * HD + d];
+          const T *pr = pd + pp * QN + qb;
 #pragma unroll
-          for (int qi = 0; qi < QN; ++qi)
-            if (act[qi]) acc[qi] = Ops::next(pr[qi], vv, acc[qi]);
+          for (int x = 0; x < QH; ++x)
+            if (act[x]) acc[x] = Ops::next(pr[x], vv, acc[x]);
         }
       }
     }
@@ -740,18 +743,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
     for (int g = waited; g < issued; ++g)
       mbar_wait_bounded(&bars[g & 1], (unsigned)(g >> 1) & 1u, a.status);
 #pragma unroll
-  for (int qi = 0; qi < QN; ++qi) {
+  for (int x = 0; x < QH; ++x) {
+    const int qi = qb + x;
     if (!qvalid[qi]) continue;
     const int pos = qpos[qi], h = kvh * G + qi % G, t = t0 + qi / G;
-    double sum = tot[qi] + acc[qi];
+    double sum = tot[x] + acc[x];
     const float vc =
         Q8 ? q8_0_value(reinterpret_cast<const uint8_t *>(a.vcache) + ((long)pos * a.kv_heads + kvh) * RB,
-                        HD, tid)
-           : half_bits_to_float(a.vcache[(long)pos * a.kv_heads * HD + kvh * HD + tid]);
+                        HD, d)
+           : half_bits_to_float(a.vcache[(long)pos * a.kv_heads * HD + kvh * HD + d]);
     sum += (double)__fmul_rn(qpcur[qi], vc);
     const float out = (float)sum;
-    const float gt = a.projected[(long)t * a.seq_proj + (long)(2 * h + 1) * HD + tid];
-    a.attended[(long)t * a.seq_out + (long)h * HD + tid] = __fmul_rn(out, sigmoid_f(gt));
+    const float gt = a.projected[(long)t * a.seq_proj + (long)(2 * h + 1) * HD + d];
+    a.attended[(long)t * a.seq_out + (long)h * HD + d] = __fmul_rn(out, sigmoid_f(gt));
   }
 }
 

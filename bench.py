@@ -561,6 +561,95 @@ def int8_peak():
     return 2.0 * 1590.0, "2 x fallback bf16 1.59 PFLOP/s"
 
 
+def run_gemm_tp(args, world, rank, local, dev):
+    """configs[3] on N GPUs, partitioned as the FFN it belongs to: the
+    2048-token FFN chain (gate and up K=2560 -> N=9216, SwiGLU, down
+    9216 -> 2560, TQ2_0) with gate/up column-parallel and down row-parallel,
+    its partial sums all-reduced over NVLink peer memory from the down GEMM's
+    epilogue (prism_b200_ffn_*).  A step is one chain call; the value is the
+    three GEMMs' int-ops per step over the max-over-ranks device time (total
+    work fixed: strong scaling)."""
+    import torch
+    import prism_b200 as pb
+    import synth
+    K, N = GEMM_SHAPES[0]
+    ex = pb.ProjectionExecutor(local)
+    tens = [pb.Tensor(35, K, N, synth.tq2_weights(N, K, 3)),
+            pb.Tensor(35, K, N, synth.tq2_weights(N, K, 4)),
+            pb.Tensor(35, N, K, synth.tq2_weights(K, N, 5))]
+    f = pb.FfnChain(ex, *tens, max_tokens=GEMM_M, tp_rank=rank, tp_size=world)
+    handles = [None] * world
+    torch.distributed.all_gather_object(handles, f.exchange_handle())
+    f.connect(handles)
+    x = torch.randn(GEMM_M, K, device=dev)
+    r = torch.randn(GEMM_M, K, device=dev)
+    y = torch.empty(GEMM_M, K, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)   # > 126 MB L2
+    s = torch.cuda.ExternalStream(ex.stream(), device=dev)
+    steps = min(args.steps, 20)
+
+    def run():
+        f.device(GEMM_M, x.data_ptr(), r.data_ptr(), y.data_ptr())
+
+    for _ in range(args.warmup):
+        run()
+    ex.sync()
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    with Clocks(local) as clk:
+        for e0, e1 in ev:
+            with torch.cuda.stream(s):
+                flush.zero_()
+            e0.record(s)
+            run()
+            e1.record(s)
+        torch.cuda.synchronize()
+    ex.sync()
+    ms = max_over_ranks(float(np.mean([e0.elapsed_time(e1) for e0, e1 in ev])), world, dev)
+    ops = 3 * 2.0 * GEMM_M * K * N
+    # end to end through the host-buffer call (tokens and residual in, rows out)
+    xh = np.random.default_rng(6).standard_normal((GEMM_M, K)).astype(np.float32)
+    rh = np.random.default_rng(7).standard_normal((GEMM_M, K)).astype(np.float32)
+    f(xh, rh)
+    torch.distributed.barrier()
+    t0 = time.perf_counter()
+    reps = 5
+    for _ in range(reps):
+        f(xh, rh)
+    e2e_s = max_over_ranks((time.perf_counter() - t0) / reps, world, dev)
+    torch.distributed.barrier()
+    f.close()
+    ex.close()
+    peak, peak_src = int8_peak()
+    line = {
+        "metric": GEMM_METRIC, "value": ops / ms / 1e9, "unit": "Tint-op/s", "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "i8 x u8 -> i32, f32 chain",
+        "data": "synthetic (configs[3] distributions)",
+        "config": {"workload": "configs[3] as a tensor-parallel FFN chain: M=2048 tokens, "
+                               "gate/up K=2560 N=9216 column-parallel, down K=9216 N=2560 "
+                               "row-parallel, TQ2_0, residual added; a step = one chain",
+                   "parallelism": "tp%d, all-reduce fused into the down GEMM epilogue "
+                                  "(peer stores) and the reduce kernel" % world,
+                   "l2": "a 256 MB buffer is written between timed steps"},
+        "clocks": clk.summary(),
+        "gpu_launches": steps * 7,
+        "e2e": {"value": ops / e2e_s / 1e12, "unit": "Tint-op/s",
+                "h2d_bytes_per_step": 2 * GEMM_M * K * 4, "d2h_bytes_per_step": GEMM_M * K * 4,
+                "api": "prism_b200_ffn_chain_tokens (host buffers), every rank"},
+        "roofline": {"bound": "tensor", "achieved": ops / world / ms / 1e9, "peak": peak,
+                     "unit": "Tint-op/s", "frac": ops / world / ms / 1e9 / peak,
+                     "peak_source": peak_src,
+                     "kernel": "per GPU: the rank's three GEMMs, quantizations, SwiGLU and "
+                               "the all-reduce over the chain's device time",
+                     "traffic": None},
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def cpu_gemm_baseline(seconds=15.0):
     """Oracle per-token tile dots (reference src/kernels/prefill.rs:48-87) on
     all host cores for a sample of tokens of the gate/up shape."""
@@ -597,6 +686,8 @@ def run_gemm(args):
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=dev)
+        if args.parallel == "tp":
+            return run_gemm_tp(args, world, rank, local, dev)
     ex = pb.ProjectionExecutor(local)
     s = torch.cuda.Stream(device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)   # > 126 MB L2

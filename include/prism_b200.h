@@ -171,6 +171,40 @@ int prism_b200_project_f32_tokens_device(prism_b200_executor *ex, const prism_b2
                                          size_t tokens, const float *x_dev, int pinned,
                                          float *out_dev, void *stream);
 
+/* ---- FFN chain over tokens, one GPU or tensor-parallel ---------------- */
+
+/* The full intra-layer FFN chain over a tile of token activations
+ * (reference src/kernels/projection.rs:261-350
+ * `project_f32_ffn_chain_tokens`, without a Hadamard block):
+ *   out[m] = residual[m] + down(Q8_K(SwiGLU(gate(Q8_K(x_m)), up(Q8_K(x_m)))))
+ * with SwiGLU(g, u) = u * silu(g) and `residual` optional.  gate and up are
+ * [F][H] and down [H][F] resident weights of one kind.
+ *
+ * prism_b200_ffn_create prepares the chain for at most `max_tokens` tokens
+ * per call.  With tp_size == 1 it computes every row on this GPU, bit for bit
+ * the sequential chain.  With tp_size N > 1 this is rank `tp_rank` of N (one
+ * process and GPU each): it keeps gate/up rows [r*F/N, (r+1)*F/N) and the
+ * matching input blocks of down (F % (256 N) == 0), and the down projection's
+ * partial sums are all-reduced over NVLink peer memory in rank order (within
+ * a few binary32 ulps of the one-GPU chain).  Tensor-parallel ranks exchange
+ * their 64-byte handles (prism_b200_ffn_exchange_handle, gathered in rank
+ * order) and connect before the first call; every rank then calls with the
+ * same token counts in the same order, like a collective.  A rank that stops
+ * calling makes the others' waits expire (PRISM_B200_E_TIMEOUT). */
+typedef struct prism_b200_ffn prism_b200_ffn;
+int prism_b200_ffn_create(prism_b200_executor *ex, const prism_b200_weight *gate,
+                          const prism_b200_weight *up, const prism_b200_weight *down,
+                          uint32_t max_tokens, uint32_t tp_rank, uint32_t tp_size,
+                          prism_b200_ffn **out);
+void prism_b200_ffn_destroy(prism_b200_ffn *f);
+int prism_b200_ffn_exchange_handle(const prism_b200_ffn *f, void *handle);
+int prism_b200_ffn_connect(prism_b200_ffn *f, const void *handles);
+int prism_b200_ffn_chain_tokens(prism_b200_ffn *f, size_t tokens, const float *x,
+                                const float *residual, int pinned, float *out);
+int prism_b200_ffn_chain_tokens_device(prism_b200_ffn *f, size_t tokens, const float *x_dev,
+                                       const float *residual_dev, int pinned, float *out_dev,
+                                       void *stream);
+
 /* Q8_K activation quantization of n floats (n % 256 == 0)
  * (reference src/kernels.rs:463-522 `q8k_with_input`). */
 int prism_b200_quantize_q8k(prism_b200_executor *ex, const float *x, size_t n,

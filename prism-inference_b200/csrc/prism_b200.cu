@@ -664,3 +664,4 @@ extern "C" int prism_b200_gdn_prefill_device_noalloc(prism_b200_executor *ex, in
 #include "model.cuh"
 #include "batch.cuh"
 #include "prefill.cuh"
+#include "tp_ffn.cuh"

@@ -79,6 +79,12 @@ def load():
         "prism_b200_weight_rows": (u64, [vp]),
         "prism_b200_weight_cols": (u64, [vp]),
         "prism_b200_weight_device_bytes": (u64, [vp]),
+        "prism_b200_ffn_create": (i32, [vp, vp, vp, vp, u32, u32, u32, P(vp)]),
+        "prism_b200_ffn_destroy": (None, [vp]),
+        "prism_b200_ffn_exchange_handle": (i32, [vp, vp]),
+        "prism_b200_ffn_connect": (i32, [vp, vp]),
+        "prism_b200_ffn_chain_tokens": (i32, [vp, sz, vp, vp, i32, vp]),
+        "prism_b200_ffn_chain_tokens_device": (i32, [vp, sz, vp, vp, i32, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -345,3 +351,56 @@ def gdn_prefill_device_noalloc(ex, batch, tokens, heads, key_heads, chunk, state
     ex._check(L.prism_b200_gdn_prefill_device_noalloc(ex.h, batch, tokens, heads, key_heads, d,
                                                       chunk, state, q, k, v, decay, beta, out,
                                                       stream))
+
+
+FFN_EXCHANGE_HANDLE_BYTES = 64
+
+
+class FfnChain:
+    """The FFN chain over token tiles (reference src/kernels/projection.rs:
+    261-350 project_f32_ffn_chain_tokens, no Hadamard): out = residual +
+    down(SwiGLU(gate(x), up(x))) for [tokens][H] activations.
+
+    tp_size > 1 makes this rank `tp_rank` of a tensor-parallel chain (one
+    process and GPU per rank): gather every rank's `exchange_handle()` in rank
+    order, pass the list to `connect()`, then call with the same token counts
+    on every rank."""
+
+    def __init__(self, executor, gate, up, down, max_tokens, tp_rank=0, tp_size=1):
+        self.ex = executor
+        ws = [executor._weight(w) for w in (gate, up, down)]
+        self.H, self.F = ws[0].cols, ws[0].rows
+        self.h = ctypes.c_void_p()
+        executor._check(load().prism_b200_ffn_create(
+            executor.h, ws[0].handle, ws[1].handle, ws[2].handle, max_tokens, tp_rank, tp_size,
+            ctypes.byref(self.h)))
+
+    def exchange_handle(self):
+        buf = ctypes.create_string_buffer(FFN_EXCHANGE_HANDLE_BYTES)
+        self.ex._check(load().prism_b200_ffn_exchange_handle(self.h, buf))
+        return buf.raw
+
+    def connect(self, handles):
+        blob = b"".join(handles)
+        self.ex._check(load().prism_b200_ffn_connect(self.h, blob))
+
+    def __call__(self, x, residual=None, pinned=False):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim != 2 or x.shape[1] != self.H:
+            raise PrismB200Error(E_INVALID, "token tile must be [tokens][hidden]")
+        r = None if residual is None else np.ascontiguousarray(residual, dtype=np.float32)
+        out = np.zeros_like(x)
+        self.ex._check(load().prism_b200_ffn_chain_tokens(
+            self.h, x.shape[0], _p(x), _p(r) if r is not None else None, int(pinned), _p(out)))
+        return out
+
+    def device(self, tokens, x_ptr, residual_ptr, out_ptr, pinned=False, stream=None):
+        self.ex._check(load().prism_b200_ffn_chain_tokens_device(
+            self.h, tokens, ctypes.c_void_p(x_ptr),
+            ctypes.c_void_p(residual_ptr) if residual_ptr else None, int(pinned),
+            ctypes.c_void_p(out_ptr), ctypes.c_void_p(stream) if stream else None))
+
+    def close(self):
+        if self.h:
+            load().prism_b200_ffn_destroy(self.h)
+            self.h = None

@@ -387,7 +387,7 @@ template <bool Q8>
 constexpr size_t prefill_attn_smem() {
   using T = typename PfOps<Q8>::T;
   return (size_t)256 * kPfQueries * sizeof(T)                 // queries [hd][Q]
-         + (size_t)256 * (kPfChunk + 1) * sizeof(T)           // keys [hd][chunk+1] / values [chunk][hd]
+         + (size_t)256 * (kPfChunk + 2) * sizeof(T)           // keys [hd][chunk+2] / values [chunk][hd]
          + (size_t)8 * kPfQueries * kPfChunk * 8              // score partial trees [8][Q][chunk]
          + (size_t)kPfChunk * kPfQueries * sizeof(T)          // probabilities [chunk][Q]
          + (size_t)2 * kPfChunk * PfOps<Q8>::kRowBytes;       // raw rows, two buffers
@@ -418,10 +418,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
   using Ops = PfOps<Q8>;
   using T = typename Ops::T;
   constexpr int HD = 256, QN = kPfQueries, CH = kPfChunk, RB = Ops::kRowBytes;
+  constexpr int CP = CH + 2;  // key row pitch: pairs stay 16-byte aligned
   extern __shared__ __align__(128) uint8_t smem[];
   T *qT = reinterpret_cast<T *>(smem);                            // [HD][QN]
-  T *rows = qT + HD * QN;                                         // [HD][CH+1] / [CH][HD]
-  double *Rs = reinterpret_cast<double *>(rows + HD * (CH + 1));  // [8][QN][CH]
+  T *rows = qT + HD * QN;                                         // [HD][CP] / [CH][HD]
+  double *Rs = reinterpret_cast<double *>(rows + HD * CP);       // [8][QN][CH]
   T *pd = reinterpret_cast<T *>(Rs + 8 * QN * CH);                // [CH][QN]
   uint8_t *raw = reinterpret_cast<uint8_t *>(pd + CH * QN);       // [2][CH][RB]
   double *W = Rs;  // softmax group totals [QN][8][8], between the passes
@@ -491,7 +492,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
       const uint8_t *rb = raw + (g & 1) * CH * RB;
       const int d = tid & (HD - 1), p1 = (tid / HD) * (CH / 2);
       for (int pp = p1; pp < p1 + CH / 2; ++pp)
-        rows[d * (CH + 1) + pp] = pp < cn ? Ops::widen_row(rb + pp * RB, d) : Ops::widen(0.0f);
+        rows[d * CP + pp] = pp < cn ? Ops::widen_row(rb + pp * RB, d) : Ops::widen(0.0f);
     }
     __syncthreads();
     if (g + 2 < 2 * nk) {
@@ -517,7 +518,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
           qv[0] = q2.x, qv[1] = q2.y;
         }
 #pragma unroll
-        for (int y = 0; y < 4; ++y) kv[y] = rows[d * (CH + 1) + pg + 8 * y];
+        for (int y = 0; y < 4; y += 2) {
+          // positions 2pg, 2pg+1 and 2pg+16, 2pg+17: one pair load each
+          const T *kp = rows + d * CP + 2 * pg + 8 * y;
+          if constexpr (Q8) {
+            const float2 k2 = *reinterpret_cast<const float2 *>(kp);
+            kv[y] = k2.x, kv[y + 1] = k2.y;
+          } else {
+            const double2 k2 = *reinterpret_cast<const double2 *>(kp);
+            kv[y] = k2.x, kv[y + 1] = k2.y;
+          }
+        }
 #pragma unroll
         for (int x = 0; x < 2; ++x)
 #pragma unroll
@@ -537,7 +548,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
     for (int x = 0; x < 2; ++x)
 #pragma unroll
       for (int y = 0; y < 4; ++y)
-        Rs[(lg * QN + q0 + x) * CH + pg + 8 * y] = A[x][y] + (B[x][y] + C[x][y]);
+        Rs[(lg * QN + q0 + x) * CH + 2 * pg + (y & 1) + 16 * (y >> 1)] =
+            A[x][y] + (B[x][y] + C[x][y]);
     __syncthreads();
     // the rest of the butterfly: ((R0+R4)+(R2+R6)) + ((R1+R5)+(R3+R7)), one
     // (query, position) per thread
@@ -642,6 +654,22 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
   // there fold their partial into the rank-ordered total.
   constexpr int QH = QN / 2;
   const int d = tid & (HD - 1), qh = tid / HD, qb = QH * qh;
+  // this half's QH probabilities of one position, in 16-byte loads
+  auto load_probs = [](const T *src, T (&dst)[QH]) {
+    if constexpr (Q8) {
+#pragma unroll
+      for (int x = 0; x < QH; x += 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(src + x);
+        dst[x] = v.x, dst[x + 1] = v.y, dst[x + 2] = v.z, dst[x + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int x = 0; x < QH; x += 2) {
+        const double2 v = *reinterpret_cast<const double2 *>(src + x);
+        dst[x] = v.x, dst[x + 1] = v.y;
+      }
+    }
+  };
   double acc[QH], tot[QH];
 #pragma unroll
   for (int x = 0; x < QH; ++x) {
@@ -716,7 +744,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
       if (full) {
         for (; pp < end; ++pp) {
           const T vv = rows[pp * HD + d];
-          const T *pr = pd + pp * QN + qb;
+          T pr[QH];
+          load_probs(pd + pp * QN + qb, pr);
 #pragma unroll
           for (int x = 0; x < QH; ++x) acc[x] = Ops::next(pr[x], vv, acc[x]);
         }
@@ -728,7 +757,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) attention_prefill_kernel(Prefil
         for (int x = 0; x < QH; ++x) act[x] = pp < qcnt[qb + x];
         for (; pp < end; ++pp) {
           const T vv = rows[pp * HD + d];
-          const T *pr = pd + pp * QN + qb;
+          T pr[QH];
+          load_probs(pd + pp * QN + qb, pr);
 #pragma unroll
           for (int x = 0; x < QH; ++x)
             if (act[x]) acc[x] = Ops::next(pr[x], vv, acc[x]);

@@ -94,13 +94,28 @@ __global__ void __launch_bounds__(128) gdn_token_inputs_kernel(GdnTokensArgs a) 
 // 4l .. 4l+3.  Per token, run_gdn's row arithmetic in its order: decay, s.k
 // (binary64 partials, warp butterfly), delta, update, s.q.  The tokens'
 // q, k, v, decay and beta come through shared memory in chunks of
-// kScanTokens, loaded cooperatively a chunk ahead; within a chunk the
-// butterfly of token t's s.q runs beside token t+1's s.k.  Outputs leave
+// kScanTokens, loaded cooperatively a chunk ahead.  s.q only feeds the
+// output, so its lane partials wait in shared memory and at the chunk's end
+// lane t forms token t's sum in the butterfly's association.  Outputs leave
 // once per chunk, coalesced.
 constexpr int kScanTokens = 32;
 
+// The warp butterfly's sum of 32 lane values v[0..31] (lane l adds lane
+// l^16, then l^8, ...), evaluated by one thread.
+__device__ __forceinline__ double butterfly_sum32(const double (&v)[32]) {
+  double s16[16], s8[8], s4[4];
+#pragma unroll
+  for (int b = 0; b < 16; ++b) s16[b] = v[b] + v[b + 16];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) s8[b] = s16[b] + s16[b + 8];
+#pragma unroll
+  for (int b = 0; b < 4; ++b) s4[b] = s8[b] + s8[b + 4];
+  return (s4[0] + s4[2]) + (s4[1] + s4[3]);
+}
+
 constexpr size_t gdn_scan_smem() {
-  return (size_t)2 * kScanTokens * (2 * 128 + 2 * kScanRows + 2) * sizeof(float);
+  return (size_t)2 * kScanTokens * (2 * 128 + 2 * kScanRows + 2) * sizeof(float)  // inputs, outputs
+         + (size_t)kScanRows * kScanTokens * 33 * sizeof(double);  // s.q lane partials
 }
 
 __global__ void __launch_bounds__(32 * kScanRows, 1) gdn_rows_scan_kernel(GdnTokensArgs a) {
@@ -111,6 +126,8 @@ __global__ void __launch_bounds__(32 * kScanRows, 1) gdn_rows_scan_kernel(GdnTok
   float *vs = ks + 2 * TC * S;                  // [2][TC][R]
   float *os = vs + 2 * TC * R;                  // [2][TC][R]
   float *ds = os + 2 * TC * R;                  // [2][TC][2] decay, beta
+  // [R][TC][33]: each token's s.q lane partials, reduced at the chunk's end
+  double *dqs = reinterpret_cast<double *>(ds + 2 * TC * 2);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row0 = blockIdx.x * R, row = row0 + warp;  // h * S + r
   if (row0 >= a.values * S) return;
@@ -160,14 +177,13 @@ __global__ void __launch_bounds__(32 * kScanRows, 1) gdn_rows_scan_kernel(GdnTok
   load(0);
   store(0);
   __syncthreads();
-  bool finite = true;
+  double *dqw = dqs + (size_t)warp * TC * 33;
   for (int c = 0; c < nc; ++c) {
     const int b = c & 1, tb = c * TC, tn = min(TC, a.T - tb);
     if (c + 1 < nc) load(c + 1);  // in flight during this chunk's recurrence
     const float *qb = qs + b * TC * S, *kb = ks + b * TC * S;
     const float *vb = vs + b * TC * R, *db = ds + b * TC * 2;
     float *ob = os + b * TC * R;
-    double dqp = 0.0;  // s.q partial of the previous token
     for (int tt = 0; tt < tn; ++tt) {
       const float4 kk = reinterpret_cast<const float4 *>(kb + tt * S)[lane];
       const float4 qq = reinterpret_cast<const float4 *>(qb + tt * S)[lane];
@@ -178,31 +194,35 @@ __global__ void __launch_bounds__(32 * kScanRows, 1) gdn_rows_scan_kernel(GdnTok
       s.w = __fmul_rn(decay, s.w);
       double dk = (double)__fmul_rn(s.x, kk.x) + (double)__fmul_rn(s.y, kk.y) +
                   (double)__fmul_rn(s.z, kk.z) + (double)__fmul_rn(s.w, kk.w);
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        dk += __shfl_xor_sync(0xffffffffu, dk, off);
-        dqp += __shfl_xor_sync(0xffffffffu, dqp, off);
-      }
-      if (tt > 0 && lane == 0) ob[(tt - 1) * R + warp] = __fmul_rn((float)dqp, oscale);
+      dk = warp_sum_f64(dk);
       const float delta = __fmul_rn(__fsub_rn(vv, (float)dk), beta);
       s.x = __fadd_rn(s.x, __fmul_rn(delta, kk.x));
       s.y = __fadd_rn(s.y, __fmul_rn(delta, kk.y));
       s.z = __fadd_rn(s.z, __fmul_rn(delta, kk.z));
       s.w = __fadd_rn(s.w, __fmul_rn(delta, kk.w));
-      finite &= is_finite_f(s.x) && is_finite_f(s.y) && is_finite_f(s.z) && is_finite_f(s.w);
-      dqp = (double)__fmul_rn(s.x, qq.x) + (double)__fmul_rn(s.y, qq.y) +
-            (double)__fmul_rn(s.z, qq.z) + (double)__fmul_rn(s.w, qq.w);
+      dqw[tt * 33 + lane] = (double)__fmul_rn(s.x, qq.x) + (double)__fmul_rn(s.y, qq.y) +
+                            (double)__fmul_rn(s.z, qq.z) + (double)__fmul_rn(s.w, qq.w);
     }
-    if (tn > 0) {
-      dqp = warp_sum_f64(dqp);
-      if (lane == 0) ob[(tn - 1) * R + warp] = __fmul_rn((float)dqp, oscale);
+    __syncwarp();
+    // lane tt reduces token tt's s.q partials in the butterfly's association
+    if (lane < tn) {
+      double v[32];
+#pragma unroll
+      for (int l = 0; l < 32; ++l) v[l] = dqw[lane * 33 + l];
+      ob[lane * R + warp] = __fmul_rn((float)butterfly_sum32(v), oscale);
     }
+    __syncwarp();
     if (c + 1 < nc) store(b ^ 1);
     __syncthreads();  // the next chunk's inputs and this chunk's outputs are complete
     for (int e = tid; e < tn * R; e += NT)
       a.o_pre[(long)(tb + e / R) * a.values * S + row0 + e % R] = ob[e];
   }
   reinterpret_cast<float4 *>(srow)[lane] = s;
+  // A non-finite state element stays non-finite at every later token (decay
+  // times inf or NaN is inf or NaN, and adding to inf or NaN never gives a
+  // finite value), so the final state's check equals the decode kernel's
+  // check after every token.
+  const bool finite = is_finite_f(s.x) && is_finite_f(s.y) && is_finite_f(s.z) && is_finite_f(s.w);
   if (!__all_sync(0xffffffffu, finite) && lane == 0) report(a.status, kStatusNonfinite);
 }
 
@@ -393,18 +413,6 @@ constexpr size_t prefill_attn_smem() {
          + (size_t)2 * kPfChunk * PfOps<Q8>::kRowBytes;       // raw rows, two buffers
 }
 
-// The warp butterfly's sum of 32 lane values v[0..31] (lane l adds lane
-// l^16, then l^8, ...), evaluated by one thread.
-__device__ __forceinline__ double butterfly_sum32(const double (&v)[32]) {
-  double s16[16], s8[8], s4[4];
-#pragma unroll
-  for (int b = 0; b < 16; ++b) s16[b] = v[b] + v[b + 16];
-#pragma unroll
-  for (int b = 0; b < 8; ++b) s8[b] = s16[b] + s16[b + 8];
-#pragma unroll
-  for (int b = 0; b < 4; ++b) s4[b] = s8[b] + s8[b + 4];
-  return (s4[0] + s4[2]) + (s4[1] + s4[3]);
-}
 
 // grid (kv_heads, ceil(T / TQ)), kPfThreads threads; hd == 256, G * TQ <=
 // kPfQueries.  Query qi = tl * G + g is token t0 + tl, head kvh * G + g.

@@ -433,6 +433,33 @@ def run_matvec(args):
         print(json.dumps(line), flush=True)
 
 
+GDN_METRIC = "Gated DeltaNet decode step GB/s (B=64) and chunked prefill TFLOP/s"
+
+
+def cpu_gdn_baseline(seconds=10.0):
+    """The oracle's sequential GDN head step (reference src/graph.rs:801-822)
+    over the configs[2] heads, one host thread: state bytes read and written
+    per second."""
+    from oracle import oracle
+    d = 128
+    rng = np.random.default_rng(3)
+    st = rng.standard_normal((d, d)).astype(np.float32) * 0.1
+    q = rng.standard_normal(d).astype(np.float32)
+    k = rng.standard_normal(d).astype(np.float32)
+    q /= np.linalg.norm(q)
+    k /= np.linalg.norm(k)
+    v = rng.standard_normal(d).astype(np.float32)
+    oracle.gdn_head_step(st, q, k, v, 0.9, 0.5)
+    t0, n = time.perf_counter(), 0
+    while time.perf_counter() - t0 < seconds:
+        st, _ = oracle.gdn_head_step(st, q, k, v, 0.9, 0.5)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n * 2 * d * d * 4 / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": "%d head steps (128 x 128 fp32 state read and written), %.1f s, one "
+                      "thread" % (n, dt)}
+
+
 def run_gdn(args):
     """the Gated DeltaNet kernels alone.  16 heads, d = 128,
     fp32 state; decode = one recurrent step for B in {1, 16, 64} (HBM bound:
@@ -524,7 +551,7 @@ def run_gdn(args):
     ex.close()
     fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
     line = {
-        "metric": "Gated DeltaNet decode step GB/s (B=64) and chunked prefill TFLOP/s",
+        "metric": GDN_METRIC,
         "value": world * decode["B64"]["gbs"], "unit": "GB/s", "n_gpus": world, "steps": 50,
         "warmup": args.warmup, "ms_per_step": decode["B64"]["us_per_step"] / 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -1042,6 +1069,12 @@ def run_reference(args):
     if args.workload == "matvec":
         cb = cpu_matvec_baseline(seconds=20.0)
         metric, unit = MATVEC_METRIC, "GB/s"
+    elif args.workload == "gemm":
+        cb = cpu_gemm_baseline(seconds=20.0)
+        metric, unit = GEMM_METRIC, "Tint-op/s"
+    elif args.workload == "gdn":
+        cb = cpu_gdn_baseline(seconds=20.0)
+        metric, unit = GDN_METRIC, "GB/s"
     else:
         import qwen35
         cfg = qwen35.CONFIG1
@@ -1052,12 +1085,24 @@ def run_reference(args):
         if args.workload == "prefill":
             # the reference ingests a prompt token by token (Decoder::ingest)
             metric = PREFILL_METRIC
+        elif args.workload == "serve":
+            # the reference serves each sequence with its own decoder
+            metric = SERVE_METRIC
+            cb["sample"] = "per-sequence decode, contexts near position 0: " + cb["sample"]
+    if unit == "tok/s":
+        ms_per_step = 1e3 / cb["value"]
+    elif unit == "Tint-op/s":
+        ms_per_step = 2.0 * GEMM_M * GEMM_SHAPES[0][0] * GEMM_SHAPES[0][1] / (cb["value"] * 1e9)
+    elif args.workload == "gdn":
+        ms_per_step = 64 * 16 * 2 * 128 * 128 * 4 / (cb["value"] * 1e9) * 1e3
+    else:
+        ms_per_step = MV_BYTES / (cb["value"] * 1e9) * 1e3
     line = {
         "impl": "reference", "metric": metric, "value": cb["value"], "unit": unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": (1e3 / cb["value"]) if unit == "tok/s" else MV_BYTES / (cb["value"] * 1e9) * 1e3,
+        "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "i8xternary->i32,f32", "data": "synthetic",
+        "dtype": "f32" if args.workload == "gdn" else "i8xternary->i32,f32", "data": "synthetic",
         "config": {"workload": "same as the ours arm, on the host cores",
                    "note": "the Rust reference cannot be built here (no cargo/rustc); the "
                            "oracle/ C restatement of its Source arithmetic is timed"},

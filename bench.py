@@ -799,7 +799,7 @@ def prefill_launches(cfg, tokens, chunk=2048):
     """Kernels of one prism_b200_model_prefill_async call: per 2048-token pass
     the positions, the embedding and the final position update, then per
     layer norm + quantize + projections + the mixer's kernels + FFN."""
-    gdn = 2 + 4 + 4 + 2 + 1      # norm, quant, 4 GEMMs, inputs, scan, history, gated, quant, out
+    gdn = 2 + 4 + 4 + 2          # norm, quant, 4 GEMMs, inputs, scan, history, gated, quant, out
     att = 2 + 3 + 3 + 1 + 1      # norm, quant, q/k/v GEMMs, kv rows, query rows, attention, quant, o
     ffn = 2 + 2 + 1 + 1 + 1      # norm, quant, up/gate, swiglu, quant, down
     per_pass = 3 + sum((att if cfg.is_full(l) else gdn) + ffn for l in range(cfg.layers))

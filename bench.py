@@ -131,25 +131,73 @@ def max_over_ranks(value, world, dev):
 
 # ---- CPU baselines (oracle restatement of the reference arithmetic) -------
 
-def cpu_decode_baseline(weights, cfg, tokens, seconds=15.0, threads=None):
+def cpu_decode_baseline(weights, cfg, tokens, seconds=15.0, threads=None, logits=True):
     """The reference's decode step on the host cores: the oracle decodes
-    prompt tokens from position 0 for about `seconds`."""
+    prompt tokens from position 0 for about `seconds` (the ingestion rate
+    when `logits` is False: Decoder::ingest computes no LM head)."""
     from oracle import oracle
     threads = threads or os.cpu_count()
     om = oracle.Qwen35(cfg, weights)
-    om.step(tokens[0], threads=threads)  # warm
+    om.step(tokens[0], logits=logits, threads=threads)  # warm
     n, t0 = 0, time.perf_counter()
-    logits = []
+    out = []
     while time.perf_counter() - t0 < seconds and n + 1 < len(tokens):
-        logits.append(om.step(tokens[n + 1], threads=threads))
+        out.append(om.step(tokens[n + 1], logits=logits, threads=threads))
         n += 1
     dt = time.perf_counter() - t0
     om.close()
     return ({"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
-             "sample": "%d decode steps of the oracle Qwen35 at positions 1..%d (the context "
-                       "cost at position ~512 adds <3%% to a token's work), %.1f s, projections "
-                       "row-chunked over %d threads as reference RowParallelism" % (n, n, dt, threads)},
-            logits)
+             "sample": "%d %s steps of the oracle Qwen35 at positions 1..%d, %.1f s, "
+                       "projections row-chunked over %d threads as reference RowParallelism"
+                       % (n, "decode" if logits else "ingestion (no LM head)", n, dt, threads)},
+            out)
+
+
+def device_state(model, cfg):
+    """The model's position and every layer's cached / recurrent state, in
+    the oracle's layouts (Qwen35.load_state)."""
+    states = {}
+    for l in range(cfg.layers):
+        if cfg.is_full(l):
+            states[(l, 2)] = model.read_state(l, 2)
+            states[(l, 3)] = model.read_state(l, 3)
+        else:
+            states[(l, 0)] = model.read_state(l, 0)
+            states[(l, 1)] = model.read_state(l, 1)
+    return model.position, states
+
+
+def cpu_decode_continued(weights, cfg, position, states, tokens, seconds=15.0, threads=None):
+    """The reference's decode step on the host cores at the benchmarked
+    positions: the oracle continues from a state at `position` (the device's
+    state after the same prompt) and decodes `tokens` for about `seconds`.
+    Returns (cpu_baseline, logits of every step it computed)."""
+    from oracle import oracle
+    threads = threads or os.cpu_count()
+    om = oracle.Qwen35(cfg, weights)
+    om.load_state(position, states)
+    out = [om.step(tokens[0], threads=threads)]  # first step untimed
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds and n + 1 < len(tokens):
+        out.append(om.step(tokens[n + 1], threads=threads))
+        n += 1
+    dt = time.perf_counter() - t0
+    om.close()
+    return ({"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+             "sample": "%d decode steps of the oracle Qwen35 at positions %d..%d (continuing "
+                       "from the device's state after the %d-token prompt), %.1f s, "
+                       "projections row-chunked over %d threads as reference RowParallelism"
+                       % (n, position + 1, position + n, position, dt, threads)},
+            out)
+
+
+def oracle_weights(cfg, seed=0):
+    """The configuration's random-init weights built on the host by the
+    oracle's generator (the same bytes as the library's; the reference arm
+    never maps the product library)."""
+    from oracle import oracle
+    import qwen35
+    return qwen35.synthetic_weights(cfg, seed=seed, generator=oracle.synth_weights)
 
 
 def cpu_matvec_baseline(seconds=10.0, threads=None):
@@ -353,6 +401,7 @@ def run_decode(args):
                       "without PDL",
             "algorithmic_bytes_per_launch": ffn_bytes,
             "traffic": traffic_from_profiles("ffn_layer"),
+            "traffic_source": TRAFFIC_SOURCE,
             "step": {"achieved": bytes_per_token / (ms_per_token / 1e3) / 1e9,
                      "frac": bytes_per_token / (ms_per_token / 1e3) / 1e9 / peak,
                      "bytes_per_token": bytes_per_token},
@@ -376,17 +425,29 @@ def run_decode(args):
         "build_s": t_build,
     }
     if rank == 0 and not args.no_cpu:
-        cb, cpu_logits = cpu_decode_baseline(weights, cfg, prompt, seconds=15.0)
-        line["cpu_baseline"] = cb
-        # parity spot check: the same tokens through the device model
+        # the oracle continues from the device's state after the prompt, so
+        # it decodes the benchmarked positions; every step it computes is
+        # also compared with the device's logits for the same token
+        cont = [int(prompt[-1])] + [int(t) for t in qwen35.prompt_tokens(cfg, 400, seed=2)]
         model.reset()
-        errs = []
-        for i, lr in enumerate(cpu_logits[:4]):
-            if i == 0:
-                model.evaluate(prompt[0], logits=False)
-            lg, _ = model.evaluate(prompt[i + 1])
-            errs.append(float(np.max(np.abs(lg - lr))))
-        line["parity"] = {"logits_max_abs_err_first_steps": errs}
+        model.set_prompt(prompt)
+        model.prefill_async(PROMPT - 1)
+        ex.sync()
+        position, states = device_state(model, cfg)
+        cb, cpu_logits = cpu_decode_continued(weights, cfg, position, states, cont, seconds=15.0)
+        line["cpu_baseline"] = cb
+        bit_equal, max_err = 0, 0.0
+        for i, lr in enumerate(cpu_logits):
+            lg, _ = model.evaluate(cont[i])
+            bit_equal += int(np.array_equal(lg.view(np.uint32), lr.view(np.uint32)))
+            max_err = max(max_err, float(np.max(np.abs(lg - lr))))
+        line["parity"] = {"steps_compared": len(cpu_logits),
+                          "positions": [position, position + len(cpu_logits) - 1],
+                          "logits_bit_identical_steps": bit_equal,
+                          "logits_max_abs_err": max_err,
+                          "note": "device vs oracle logits at every step the CPU leg "
+                                  "decoded, both continuing from the device's state after "
+                                  "the prompt"}
     model.close()
     ex.close()
     if world > 1:
@@ -422,7 +483,8 @@ def run_matvec(args):
         "roofline": {"bound": "hbm", "achieved": kern_gbs, "peak": peak, "unit": "GB/s",
                      "frac": kern_gbs / peak, "peak_source": peak_src,
                      "kernel": "matvec_kernel<35,kEpiStore>", "us_per_launch": us,
-                     "traffic": traffic_from_profiles("matvec_tq2_4096")},
+                     "traffic": traffic_from_profiles("matvec_tq2_4096"),
+                     "traffic_source": TRAFFIC_SOURCE},
     }
     if rank == 0 and not args.no_cpu:
         line["cpu_baseline"] = cpu_matvec_baseline()
@@ -564,6 +626,7 @@ def run_gdn(args):
                      "unit": "GB/s", "frac": decode["B64"]["frac"], "peak_source": peak_src,
                      "kernel": "gdn_step_kernel (B=64)",
                      "traffic": traffic_from_profiles("gdn_step_kernel"),
+                     "traffic_source": TRAFFIC_SOURCE,
                      "prefill_fp32_peak_tflops_nominal": fp32_peak},
         "gpu_launches": 50,
     }
@@ -779,7 +842,8 @@ def run_gemm(args):
                      "unit": "Tint-op/s", "frac": top["tops"] / peak, "peak_source": peak_src,
                      "kernel": "gemm_tokens_kernel<35> (K=2560, N=9216) incl. the Q8_K token "
                                "quantize launch",
-                     "traffic": traffic_from_profiles("gemm_tokens_kernel")},
+                     "traffic": traffic_from_profiles("gemm_tokens_kernel"),
+                     "traffic_source": TRAFFIC_SOURCE},
         "gpu_launches": launches,
         "e2e": {"value": world * 2.0 * GEMM_M * K * N / e2e_s / 1e12, "unit": "Tint-op/s",
                 "h2d_bytes_per_step": GEMM_M * K * 4, "d2h_bytes_per_step": GEMM_M * N * 4,
@@ -1077,18 +1141,46 @@ def run_reference(args):
         metric, unit = GDN_METRIC, "GB/s"
     else:
         import qwen35
+        from oracle import oracle
         cfg = qwen35.CONFIG1
-        weights = qwen35.synthetic_weights(cfg, seed=0)
+        weights = oracle_weights(cfg, seed=0)
         prompt = qwen35.prompt_tokens(cfg, PROMPT, seed=1)
-        cb, _ = cpu_decode_baseline(weights, cfg, prompt, seconds=30.0)
+        threads = os.cpu_count()
         metric, unit = DECODE_METRIC, "tok/s"
         if args.workload == "prefill":
             # the reference ingests a prompt token by token (Decoder::ingest)
+            cb, _ = cpu_decode_baseline(weights, cfg, prompt, seconds=30.0, logits=False)
             metric = PREFILL_METRIC
-        elif args.workload == "serve":
-            # the reference serves each sequence with its own decoder
-            metric = SERVE_METRIC
-            cb["sample"] = "per-sequence decode, contexts near position 0: " + cb["sample"]
+            cb["sample"] = "sequential ingestion from position 0: " + cb["sample"]
+        else:
+            # the benchmarked positions: ingest the same prompt (untimed),
+            # then W warm-up and up to K timed decode steps (at most ~30 s)
+            om = oracle.Qwen35(cfg, weights)
+            t_ing = time.perf_counter()
+            for t in prompt[:-1]:
+                om.step(int(t), logits=False, threads=threads)
+            t_ing = time.perf_counter() - t_ing
+            cont = [int(prompt[-1])] + [int(t) for t in qwen35.prompt_tokens(cfg, 600, seed=2)]
+            for i in range(args.warmup):
+                om.step(cont[i], threads=threads)
+            n, t0 = 0, time.perf_counter()
+            while n < args.steps and time.perf_counter() - t0 < 30.0:
+                om.step(cont[args.warmup + n], threads=threads)
+                n += 1
+            dt = time.perf_counter() - t0
+            om.close()
+            cb = {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+                  "sample": "%d decode steps of the oracle Qwen35 at positions %d..%d after "
+                            "ingesting the %d-token prompt (%.0f s, untimed), %.1f s, "
+                            "projections row-chunked over %d threads as reference "
+                            "RowParallelism" % (n, PROMPT - 1 + args.warmup,
+                                                PROMPT - 2 + args.warmup + n, PROMPT - 1,
+                                                t_ing, dt, threads)}
+            if args.workload == "serve":
+                # the reference serves each sequence with its own decoder
+                metric = SERVE_METRIC
+                cb["sample"] = ("per-sequence decode at context ~%d (the 8192-token "
+                                "attention cost is not included): " % PROMPT) + cb["sample"]
     if unit == "tok/s":
         ms_per_step = 1e3 / cb["value"]
     elif unit == "Tint-op/s":
@@ -1108,8 +1200,24 @@ def run_reference(args):
                            "oracle/ C restatement of its Source arithmetic is timed"},
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "product_library_mapped": product_library_mapped(),
     }
     print(json.dumps(line), flush=True)
+
+
+def product_library_mapped():
+    """Whether this process mapped libprism_b200.so (the reference arm must
+    not)."""
+    try:
+        with open("/proc/self/maps") as f:
+            return "libprism_b200" in f.read()
+    except OSError:
+        return None
+
+
+TRAFFIC_SOURCE = ("profiles/traffic.json: dram__bytes_read.sum + dram__bytes_write.sum per "
+                  "launch from a committed ncu capture of the same kernel, not measured in "
+                  "this run")
 
 
 def traffic_from_profiles(key):

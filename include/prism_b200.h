@@ -6,7 +6,7 @@
  * executor seam, `trait Pq2ProjectionExecutor`
  * (reference src/kernels/projection.rs:16-350), or a CPU kernel the seam
  * does not cover yet (cited per function).  A Rust host crate binds these
- * symbols with `extern "C"` declarations (INTEGRATION.md shows the stub).
+ * symbols with `extern "C"` declarations.
  *
  * Conventions
  *  - Plain C types only; no CUDA or framework types.  `stream` arguments

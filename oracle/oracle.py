@@ -218,6 +218,11 @@ def _model_lib():
             ("po_gdn_head_prefill_exact", i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, vp]),
             ("po_gdn_head_prefill_chunked", i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
             ("po_rope_frequencies", None, [vp, i32, vp]),
+            ("po_qwen35_load_state", i32, [vp, i32, i32, vp, ctypes.c_size_t]),
+            ("po_qwen35_set_position", i32, [vp, ctypes.c_int32]),
+            ("po_synth_weights", i32, [ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint64,
+                                       ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
+                                       ctypes.c_float, vp]),
         ]:
             fn = getattr(L, name)
             fn.restype = res
@@ -279,6 +284,15 @@ class Qwen35:
         _check(st)
         return out
 
+    def load_state(self, position, states):
+        """Continue from a state produced elsewhere: `states` maps
+        (layer, which) -> array (which: 0 conv, 1 matrix, 2 keys, 3 values,
+        the layouts of conv_state / matrix_state / keys / values)."""
+        for (layer, which), arr in states.items():
+            a = np.ascontiguousarray(arr)
+            _check(self.L.po_qwen35_load_state(self.h, layer, which, _p(a), a.nbytes))
+        _check(self.L.po_qwen35_set_position(self.h, int(position)))
+
     def hidden(self):
         p = self.L.po_qwen35_hidden(self.h)
         return np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_float)),
@@ -309,6 +323,16 @@ class Qwen35:
         n = self.position
         return np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_uint16)),
                                      (c.context, c.kv_heads * c.head_dim))[:n].copy()
+
+
+def synth_weights(kind, rows, cols, seed, stream=0, scale_lo=0.01, scale_hi=0.05):
+    """Seeded synthetic packed weights on the host (the product library's
+    generator restated): uint8 (rows, cols/256*block) in the reference byte
+    layout."""
+    out = np.empty((rows, cols // 256 * block_bytes(kind)), np.uint8)
+    _check(_model_lib().po_synth_weights(kind, rows, cols, seed, stream, scale_lo, scale_hi,
+                                         _p(out)))
+    return out
 
 
 def greedy(logits):

@@ -47,6 +47,13 @@ typedef struct po_q8_0_block {
   int8_t values[32];
 } po_q8_0_block;
 
+/* ---- seeded synthetic weights (synth_inputs.c) ------------------------ */
+/* rows x cols/256 packed blocks of kind 35 (TQ2_0) or 10 (Q2_K) in the
+ * reference byte layout, the same bytes as the product library's seeded
+ * generator for the same (seed, stream, lo, hi). */
+int po_synth_weights(uint32_t kind, uint64_t rows, uint64_t cols, uint64_t seed,
+                     uint64_t stream, float lo, float hi, uint8_t *out);
+
 /* ---- binary16 ------------------------------------------------------- */
 float po_half_to_float(uint16_t h);
 uint16_t po_float_to_half(float f);

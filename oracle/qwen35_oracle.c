@@ -139,6 +139,33 @@ const uint16_t *po_qwen35_keys(const po_qwen35 *m, int l) { return m->keys[l]; }
 const uint16_t *po_qwen35_values(const po_qwen35 *m, int l) { return m->vals[l]; }
 const float *po_qwen35_hidden(const po_qwen35 *m) { return m->hidden; }
 
+int po_qwen35_load_state(po_qwen35 *m, int layer, int which, const void *src, size_t bytes) {
+  const po_qwen35_config *c = &m->cfg;
+  if (layer < 0 || layer >= c->layers || !src) return PO_E_INVALID;
+  const int full = po_qwen35_is_full_layer(c, layer);
+  void *dst = NULL;
+  size_t cap = 0;
+  if (which == 0 && !full) {
+    dst = m->conv[layer];
+    cap = (size_t)conv_channels(c) * (c->conv_kernel - 1) * 4;
+  } else if (which == 1 && !full) {
+    dst = m->matrix[layer];
+    cap = (size_t)c->ssm_values * c->ssm_state * c->ssm_state * 4;
+  } else if ((which == 2 || which == 3) && full) {
+    dst = which == 2 ? (void *)m->keys[layer] : (void *)m->vals[layer];
+    cap = (size_t)c->context * c->kv_heads * c->head_dim * 2;
+  }
+  if (!dst || bytes > cap) return PO_E_INVALID;
+  memcpy(dst, src, bytes);
+  return PO_OK;
+}
+
+int po_qwen35_set_position(po_qwen35 *m, int32_t position) {
+  if (position < 0 || position >= m->cfg.context) return PO_E_INVALID;
+  m->position = position;
+  return PO_OK;
+}
+
 /* Q8_K-quantize x once, then project each weight (sibling group). */
 static int project_group(po_qwen35 *m, const float *x, int cols, int n, const void *const *ws,
                          const int *rows, float *const *outs, int threads) {

@@ -88,6 +88,14 @@ const uint16_t *po_qwen35_values(const po_qwen35 *m, int layer);
 const float *po_qwen35_hidden(const po_qwen35 *m);
 const float *po_qwen35_scratch(const po_qwen35 *m, int which);
 
+/* Overwrite one layer's recurrent or cached state with `bytes` bytes from
+ * src (which: 0 conv [channels][k-1], 1 matrix [values][S][S], 2 keys,
+ * 3 values -- the first `bytes` of the [context] cache rows), and set the
+ * position: a checker continues decoding from a state produced elsewhere.
+ * Returns PO_E_INVALID for a layer of the wrong kind or an oversize copy. */
+int po_qwen35_load_state(po_qwen35 *m, int layer, int which, const void *src, size_t bytes);
+int po_qwen35_set_position(po_qwen35 *m, int32_t position);
+
 /* Greatest finite logit, lowest index on ties (reference src/runtime.rs:2630). */
 int po_greedy(const float *logits, size_t n, uint32_t *out);
 

@@ -106,15 +106,18 @@ def _stream(name):
     return zlib.crc32(name.encode())
 
 
-def synthetic_weights(cfg, seed=0):
+def synthetic_weights(cfg, seed=0, generator=None):
     """Random-init weights of the architecture: dict name -> array.  Packed
     linear weights are uint8 (rows, cols/256*block) in the reference layout;
-    norms have gain 1.0; ssm_a = -1, ssm_dt.bias = 0; conv1d ~ U(-0.5, 0.5)."""
+    norms have gain 1.0; ssm_a = -1, ssm_dt.bias = 0; conv1d ~ U(-0.5, 0.5).
+    `generator(kind, rows, cols, seed, stream)` makes the packed weights
+    (default: the library's seeded generator, prism_b200_synth_weights)."""
     W = {}
     kind = cfg.weight_kind
+    gen = generator or pb.synth_weights
 
     def packed(name, rows, cols):
-        W[name] = pb.synth_weights(kind, rows, cols, seed, _stream(name))
+        W[name] = gen(kind, rows, cols, seed, _stream(name))
 
     packed("token_embd.weight", cfg.vocab, cfg.hidden)
     W["output_norm.weight"] = np.ones(cfg.hidden, np.float32)

@@ -40,3 +40,16 @@ def test_supports_is_geometry_only():
     ok = prism_b200.Tensor(35, 4096, 4096, __import__("numpy").zeros(1, "u1"))
     # supports() needs no device: a NULL executor is simply "not eligible"
     assert L.prism_b200_executor_supports(None, ctypes.byref(ok._c())) == 0
+
+
+@pytest.mark.parametrize("kind", [35, 10])
+def test_host_generator_matches_library_generator(kind):
+    """The benchmark's reference arm builds its weights with the oracle's
+    restatement of the seeded generator, so it never maps the product
+    library; both must give the same bytes."""
+    import numpy as np
+    from oracle import oracle
+    for rows, cols, seed, stream in [(7, 512, 0, 0), (33, 2560, 5, 123456), (3, 9216, 1, 7)]:
+        a = oracle.synth_weights(kind, rows, cols, seed, stream)
+        b = prism_b200.synth_weights(kind, rows, cols, seed, stream)
+        assert np.array_equal(a, b), (rows, cols, seed, stream)

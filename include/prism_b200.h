@@ -322,11 +322,20 @@ int prism_b200_model_finalize(prism_b200_model *m);
 int prism_b200_model_reset(prism_b200_model *m);
 int64_t prism_b200_model_position(const prism_b200_model *m);
 
-/* 1 when a step runs as one persistent cooperative kernel (weights streamed
- * across layer boundaries; chosen with PRISM_B200_PERSIST=1 set before
- * finalize), 0 when it runs as the per-phase kernel sequence.  Both give
- * the same bits.  No counterpart in the reference. */
+/* 1 when a step runs as one persistent cooperative kernel (the dataflow
+ * step, or the barrier-synchronised one), 0 when it runs as the per-phase
+ * kernel sequence.  All give the same bits.  No counterpart in the
+ * reference. */
 int prism_b200_model_persistent(const prism_b200_model *m);
+
+/* How a decode step runs, chosen at finalize from PRISM_B200_STEP
+ * ("flow", "seq" or "persist"): 2 = the dataflow kernel (one cooperative
+ * launch per token; activations carry a per-step tag that their consumers
+ * poll, weights stream through a shared-memory ring ahead of the compute),
+ * 1 = the barrier-synchronised persistent kernel, 0 = the per-phase kernel
+ * sequence in a CUDA graph.  -1 for a NULL model.  No counterpart in the
+ * reference. */
+int prism_b200_model_step_mode(const prism_b200_model *m);
 
 /* CTA 0's timeline of the last prism_b200_model_step_timings step of a
  * persistent model, 8 values per phase: [0] start (barrier passed) and
@@ -342,6 +351,10 @@ int prism_b200_model_persistent(const prism_b200_model *m);
  * [1] grid dependency passed, [2] input staged, [3] first tile resident,
  * [4] its dots, [5] its chains, [6] exit, and [7] the last CTA's exit
  * (projections; GDN and attention stamp [0], [1], [6], [7]).
+ * For the dataflow step (mode 2): CTA 0's globaltimer stamps of the last
+ * prism_b200_model_step_timings step, 8 values per phase in the same phase
+ * order: [0] phase start (descriptor resident), [1] input staged
+ * (projections), [7] phase end.
  * Copies at most `count` values and returns how many (0 when no timeline
  * is recorded).  No counterpart in the reference. */
 int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t count);

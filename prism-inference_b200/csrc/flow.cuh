@@ -1,0 +1,1133 @@
+// flow.cuh -- the Qwen3.5-style decode step as one persistent dataflow kernel.
+//
+// One cooperative launch per token: one CTA per SM, 16 compute warps plus one
+// weight-streaming warp.  The step is a host-built list of phases
+// (embedding; per layer the attention side and the FFN pair; the LM head).
+//
+// Synchronisation is carried by the data.  Every activation that crosses CTAs
+// is a 64-bit word: binary32 value in the low half, a 32-bit tag in the high
+// half.  The tag is (step epoch << 8) | k, where k is the index of the phase
+// that wrote the word, so a reader that knows which phase produces its input
+// polls those words until every one carries the expected tag and then uses
+// the value it already holds.  There is no grid barrier, no counter and no
+// fence between phases: a consumer waits for exactly the words it reads
+// (a Gated DeltaNet head for its own q/k/v channels, a projection for the
+// whole input vector), one L2 round trip after the last producer's store.
+// Words are stored and loaded with .relaxed.gpu operations, so each 64-bit
+// word is observed whole.  A buffer is rewritten only after every reader of
+// its previous contents is done: a phase's readers finish reading before the
+// phase's own outputs exist, and the next writer of a buffer transitively
+// needs those outputs.
+//
+// The weights never wait for data: the streaming warp walks the same phase
+// list and copies this CTA's weight tiles, phase after phase, into a
+// shared-memory ring with bulk copies, as far ahead as the ring allows.  Each
+// projection phase gives a CTA a contiguous range of tiles, so its copies are
+// contiguous in HBM.  The compute warps stage the Q8_K activation, run the
+// unit dots on resident tiles, release the tiles' ring space, then run each
+// row's chain.
+//
+// The arithmetic is that of the per-kernel path (matvec.cuh,
+// model_kernels.cuh, gdn_slices_kernel): the same unit dots, binary32 chains,
+// binary64 reductions in the same order and the same transcendentals, so the
+// two paths give identical bits.
+//
+// Every wait is bounded (kWaitLimitNs).  A CTA that gives up raises the
+// step's abort word and the timeout status, and every other wait checks the
+// abort word, so the whole grid leaves within one wait limit.  Failures are
+// made CTA-uniform by a vote before anyone acts on them; copies in flight
+// are drained (bounded) before a CTA exits.
+#pragma once
+
+#include "common.cuh"
+#include "matvec.cuh"
+#include "model_kernels.cuh"
+#include "persist.cuh"
+
+namespace prism {
+
+constexpr int kFWarps = 16;                 // compute warps
+constexpr int kFThreads = kFWarps * 32;     // compute threads (named barrier 1)
+constexpr int kFBlock = kFThreads + 32;     // + the weight-streaming warp
+constexpr int kFRing = 150 * 1024;          // weight ring
+constexpr int kFSlots = 64;                 // pieces in flight
+constexpr int kFMaxNb = 48;                 // input blocks per projection (12288 values)
+constexpr int kFActBytes = (kFMaxNb * (256 + 4 + 32 + 4) + 127) / 128 * 128;
+constexpr int kFWorkBytes = 58 * 1024;      // staging, terms, GDN / attention scratch
+constexpr int kFDescBytes = 1024;
+constexpr int kFChunk = 32;                 // attention: positions per K/V chunk
+constexpr int kFMaxScores = 1024;           // attention: positions per CTA
+// shared-memory layout
+constexpr int kFOffAct = kFRing;
+constexpr int kFOffWork = kFOffAct + kFActBytes;
+constexpr int kFOffDesc = kFOffWork + kFWorkBytes;           // [2] phase descriptors
+constexpr int kFOffBars = kFOffDesc + 2 * kFDescBytes;       // ring [kFSlots], desc [2], kv [4]
+constexpr int kFOffMeta = kFOffBars + (kFSlots + 8) * 8;     // off/len [kFSlots], counters
+constexpr int kFOffRed = kFOffMeta + kFSlots * 8 + 64;       // double [16] + float [16]
+constexpr int kFSmemBytes = kFOffRed + 16 * 8 + 16 * 4 + 64;
+static_assert(kFSmemBytes <= 232448, "flow kernel shared memory");
+
+enum FPhaseType : int { kFEmbed = 0, kFProj = 1, kFGdn = 2, kFAttn = 3 };
+enum FPrologue : int { kFRms = 0, kFF32 = 1, kFGated = 2 };
+
+// A projection phase: a group of weights sharing one input.
+struct FProj {
+  int count, nb, epi, prologue;
+  int tile_start[kMaxGroup + 1];
+  int ntiles;                        // tiles of the phase (the SwiGLU pair: per weight)
+  int h[kMaxGroup], rows[kMaxGroup];
+  const uint8_t *units[kMaxGroup];
+  uint64_t *out[kMaxGroup];          // tagged outputs (the pair: up * silu(gate) in out[0])
+  float *plain[kMaxGroup];           // optional plain binary32 copies of the outputs
+  const uint64_t *in;                // tagged input vector [nb * 256]
+  int in_k;
+  const uint64_t *zs;                // kFGated: SiLU(z) [heads * head_dim], tagged
+  int zs_k;
+  const float *norm_w;               // kFRms: [nb * 256]; kFGated: [head_dim]
+  const uint64_t *res;               // residual rows (tagged), or null
+  int res_k;
+  int heads, head_dim;               // kFGated geometry
+  float eps;
+  unsigned long long *argmax_key;    // kEpiArgmax
+};
+
+// A Gated DeltaNet layer: value head h over kGdnSlices CTAs of 16 state rows.
+struct FGdn {
+  const uint64_t *mixed, *z, *beta, *alpha;  // the projection phase's outputs
+  int in_k;
+  const float *conv_w, *dt_bias, *ssm_a;
+  float *conv_state;                 // two buffers by position parity
+  long conv_buf_stride;
+  float *state;                      // [values][S][S]
+  uint64_t *o, *zs;                  // pre-norm output, SiLU(z): [values * S], tagged
+  int S, groups, values, conv_k;
+  float eps;
+};
+
+// Gated full attention: query head h over kAttnSplit CTAs (positions split).
+struct FAttn {
+  const uint64_t *proj, *key, *value;  // [heads][2][hd] query|gate, [kv*hd], [kv*hd]
+  int in_k;
+  const float *q_norm, *k_norm;
+  uint8_t *kcache, *vcache;          // binary16 rows [context][kv*hd] or Q8_0 records
+  int q8;
+  int heads, kv_heads, hd, rope_dim;
+  int sections[3];
+  float eps, theta_scale;
+  uint64_t *smax, *stot, *part;      // exchanges between the split's CTAs, tagged
+  uint64_t *out;                     // [heads * hd] gated output, tagged
+};
+
+struct FEmbed {
+  const uint8_t *units;
+  int h, nb, vocab, n;
+  uint64_t *hidden;
+  float *plain;
+};
+
+struct alignas(16) FPhase {
+  int type, k;
+  FProj pr;
+  FGdn gd;
+  FAttn at;
+  FEmbed em;
+};
+static_assert(sizeof(FPhase) <= kFDescBytes && sizeof(FPhase) % 16 == 0, "phase descriptor");
+
+struct FlowArgs {
+  const FPhase *phases;
+  int nphases;
+  StepState st;
+  int write_greedy;
+  unsigned *sync;        // [0] finished CTAs, [1] abort word, [2] step epoch
+  unsigned *status;
+  unsigned long long *trace;  // optional: [8 * phase] CTA 0's globaltimer stamps
+};
+
+// ---- small helpers -------------------------------------------------------------
+
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+
+// Barrier of the compute warps that also ANDs a predicate over them.
+__device__ __forceinline__ bool csync_and(bool p) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred a, b;\n\tsetp.ne.s32 a, %1, 0;\n\t"
+      "bar.red.and.pred b, 1, 512, a;\n\tselp.s32 %0, 1, 0, b;\n\t}"
+      : "=r"(r)
+      : "r"((int)p)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ uint64_t ld_word(const uint64_t *p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_word(uint64_t *p, uint64_t v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t tagged(float v, uint32_t tag) {
+  return ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
+}
+__device__ __forceinline__ uint64_t tagged_u(uint32_t v, uint32_t tag) {
+  return ((uint64_t)tag << 32) | (uint64_t)v;
+}
+__device__ __forceinline__ bool has_tag(uint64_t w, uint32_t tag) {
+  return (uint32_t)(w >> 32) == tag;
+}
+__device__ __forceinline__ float word_value(uint64_t w) { return __uint_as_float((uint32_t)w); }
+__device__ __forceinline__ double word_pair_value(uint64_t lo, uint64_t hi) {
+  return __longlong_as_double((long long)(((uint64_t)(uint32_t)hi << 32) | (uint32_t)lo));
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_cta(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_cta(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
+}
+
+struct FlowCtl {
+  unsigned *status;
+  unsigned *abort;
+};
+
+__device__ __forceinline__ bool flow_aborted(const FlowCtl &c) {
+  return *reinterpret_cast<volatile const unsigned *>(c.abort) != 0u;
+}
+
+__device__ __forceinline__ void flow_raise(const FlowCtl &c) {
+  report(c.status, kStatusTimeout);
+  atomicExch(c.abort, 1u);
+}
+
+// Called after a poll round that found a word not yet written: keeps the
+// wait bounded (kWaitLimitNs) and leaves early when another CTA aborted.
+struct Spin {
+  unsigned long long t0 = 0;
+  int rounds = 0;
+  __device__ __forceinline__ bool again(const FlowCtl &c) {
+    if (rounds++ == 0) {
+      t0 = global_timer_ns();
+      return true;
+    }
+    if ((rounds & 31) == 0) {
+      if (flow_aborted(c)) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        flow_raise(c);
+        return false;
+      }
+    }
+    return true;
+  }
+};
+
+// Wait for one word; returns false on timeout / abort.
+__device__ __forceinline__ bool wait_word(const uint64_t *p, uint32_t tag, uint64_t &w,
+                                          const FlowCtl &c) {
+  w = ld_word(p);
+  Spin sp;
+  while (!has_tag(w, tag)) {
+    if (!sp.again(c)) return false;
+    w = ld_word(p);
+  }
+  return true;
+}
+
+// Wait for the n (<= N) words p[i0 + j*stride]; their values into v[j].
+template <int N>
+__device__ __forceinline__ bool wait_words(const uint64_t *p, int i0, int stride, int n,
+                                           uint32_t tag, float (&v)[N], const FlowCtl &c) {
+  uint64_t w[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) w[j] = j < n ? ld_word(p + i0 + j * stride) : tagged_u(0u, tag);
+  Spin sp;
+  for (;;) {
+    bool all = true;
+#pragma unroll
+    for (int j = 0; j < N; ++j) all &= has_tag(w[j], tag);
+    if (all) break;
+    if (!sp.again(c)) return false;
+#pragma unroll
+    for (int j = 0; j < N; ++j)
+      if (j < n && !has_tag(w[j], tag)) w[j] = ld_word(p + i0 + j * stride);
+  }
+#pragma unroll
+  for (int j = 0; j < N; ++j) v[j] = word_value(w[j]);
+  return true;
+}
+
+// Binary64 sum over the compute warps in block_sum_f64's order for a
+// 512-thread block; red holds >= 16 doubles.
+__device__ __forceinline__ double fsum_f64(double v, double *red) {
+  v = warp_sum_f64(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  csync();
+  if (lane == 0) red[warp] = v;
+  csync();
+  double t = 0.0;
+  for (int w = 0; w < kFWarps; ++w) t += red[w];
+  return t;
+}
+
+__device__ __forceinline__ float fmax_f32(float v, float *red) {
+  v = warp_max_f32(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  csync();
+  if (lane == 0) red[warp] = v;
+  csync();
+  float t = red[0];
+  for (int w = 1; w < kFWarps; ++w) t = fmaxf(t, red[w]);
+  return t;
+}
+
+// This CTA's contiguous share [t0, t1) of T units of work.
+__device__ __forceinline__ void flow_range(int T, int &t0, int &t1) {
+  t0 = (int)((long)blockIdx.x * T / gridDim.x);
+  t1 = (int)((long)(blockIdx.x + 1) * T / gridDim.x);
+}
+
+__device__ __forceinline__ int flow_group(const FProj &p, int t) {
+  int g = 0;
+#pragma unroll
+  for (int i = 1; i < kMaxGroup; ++i)
+    if (i < p.count && t >= p.tile_start[i]) g = i;
+  return g;
+}
+
+// Ring bytes of tile t of a projection phase (the pair: both weights' tiles).
+template <int KIND>
+__device__ __forceinline__ uint32_t piece_bytes(const FProj &p, int t) {
+  const bool pair = p.epi == kEpiSwiglu;
+  const int g = pair ? 0 : flow_group(p, t);
+  const uint32_t part = (uint32_t)p.nb * unit_bytes(KIND, p.h[g]);
+  return pair ? 2 * part : part;
+}
+
+// ---- ring state ------------------------------------------------------------------
+
+struct FRing {
+  uint8_t *data;
+  uint64_t *bar;      // [kFSlots] piece arrivals
+  uint32_t *off;      // [kFSlots] data offset of the piece
+  uint32_t *len;      // [kFSlots] bytes the piece holds (padding + data)
+  uint32_t *tail;     // bytes released by the consumer (monotonic)
+  uint32_t *released; // pieces released by the consumer
+  uint32_t *issued;   // pieces issued by the producer (written at its exit)
+  uint32_t *kvuse;    // [4] completed uses of the attention K/V barriers
+};
+
+// The weight-streaming warp (lane 0): every projection phase's tiles of this
+// CTA in phase order, each tile (the pair: both weights' tiles) as one
+// piece, as ring space frees up.
+template <int KIND>
+__device__ void flow_producer(const FlowArgs &fa, const FRing &rg, const FlowCtl &c) {
+  uint32_t head = 0, issued = 0;
+  bool ok = true;
+  for (int p = 0; p < fa.nphases && ok; ++p) {
+    const FPhase &ph = fa.phases[p];
+    if (ph.type != kFProj) continue;
+    const FProj &pr = ph.pr;
+    const bool pair = pr.epi == kEpiSwiglu;
+    int t0, t1;
+    flow_range(pr.ntiles, t0, t1);
+    for (int t = t0; t < t1 && ok; ++t) {
+      const int g = pair ? 0 : flow_group(pr, t);
+      const int lt = pair ? t : t - pr.tile_start[g];
+      const uint32_t part = (uint32_t)pr.nb * unit_bytes(KIND, pr.h[g]);
+      const uint32_t bytes = pair ? 2 * part : part;
+      uint32_t off = head % (uint32_t)kFRing;
+      const uint32_t pad = off + bytes > (uint32_t)kFRing ? (uint32_t)kFRing - off : 0u;
+      // wait for room: ring bytes and a free slot
+      Spin sp;
+      for (;;) {
+        const uint32_t tail = ld_acquire_cta(rg.tail);
+        const uint32_t rel = ld_acquire_cta(rg.released);
+        if (head + pad + bytes - tail <= (uint32_t)kFRing && issued - rel < (uint32_t)kFSlots)
+          break;
+        if (!sp.again(c)) {
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+      if (!ok) break;
+      fence_proxy_async_smem();  // released space was read through the generic proxy
+      head += pad;
+      off = head % (uint32_t)kFRing;
+      const int slot = (int)(issued % kFSlots);
+      rg.off[slot] = off;
+      rg.len[slot] = pad + bytes;
+      mbar_arrive_expect_tx(&rg.bar[slot], bytes);
+      bulk_g2s(rg.data + off, pr.units[g] + (size_t)lt * part, part, &rg.bar[slot]);
+      if (pair)
+        bulk_g2s(rg.data + off + part, pr.units[1] + (size_t)lt * part, part, &rg.bar[slot]);
+      head += bytes;
+      ++issued;
+    }
+  }
+  *rg.issued = issued;
+}
+
+// ---- input staging -----------------------------------------------------------------
+
+// Load the tagged input vector of n values into xs (shared), thread i taking
+// indices i, i+512, ...; with `sumsq` also this thread's binary64 sum of
+// squares in block_sumsq_f64's order.
+__device__ __forceinline__ bool stage_words(const uint64_t *in, int n, uint32_t tag, float *xs,
+                                            bool sumsq, double &s, const FlowCtl &c) {
+  constexpr int kMax = kFMaxNb * 256 / kFThreads;  // 24
+  float v[kMax];
+  const int i = threadIdx.x;
+  const int cnt = i < n ? (n - i + kFThreads - 1) / kFThreads : 0;
+  if (!wait_words<kMax>(in, i, kFThreads, cnt, tag, v, c)) return false;
+  s = 0.0;
+#pragma unroll
+  for (int j = 0; j < kMax; ++j)
+    if (j < cnt) {
+      xs[i + j * kFThreads] = v[j];
+      if (sumsq) s += (double)__fmul_rn(v[j], v[j]);
+    }
+  return true;
+}
+
+// Quantize xs[0, nb*256) into the Q8_K SoA activation at act (stage_from_f32's
+// quantization, a block per warp), after RMSNorm scaling when `rms`.
+// nw0/nw1: this lane's norm weights of block `warp`, loaded ahead of time.
+__device__ __forceinline__ void quantize_staged(const float *xs, int nb, float scale,
+                                                const float *norm_w, bool rms, uint8_t *act,
+                                                unsigned *status, float4 nw0, float4 nw1) {
+  const MatvecSmem L(nb, 32, 0, nb);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int b = warp; b < nb; b += kFWarps) {
+    const int base = b * 256 + lane * 8;
+    float v[8];
+    const float4 x0 = *reinterpret_cast<const float4 *>(xs + base);
+    const float4 x1 = *reinterpret_cast<const float4 *>(xs + base + 4);
+    v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+    v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+    if (rms) {
+      const float4 w0 = b == warp ? nw0 : *reinterpret_cast<const float4 *>(norm_w + base);
+      const float4 w1 = b == warp ? nw1 : *reinterpret_cast<const float4 *>(norm_w + base + 4);
+      const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], scale), w[j]);
+    }
+    float qscale;
+    int8_t q[8];
+    int pair_sum;
+    const unsigned st = q8k_quantize_regs(v, lane, false, qscale, q, pair_sum);
+    if (st && lane == 0) report(status, st);
+    store_q8k_soa(L, act, b, lane, qscale, q, pair_sum);
+  }
+}
+
+// ---- phases ------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t flow_tag(uint32_t ep, int k) { return (ep << 8) | (uint32_t)k; }
+
+template <int KIND>
+__device__ void flow_embed(const FEmbed &e, const StepState &st, int pos, uint32_t tag,
+                           unsigned *status) {
+  const uint32_t token = st.tokens[pos];
+  const bool valid = token < (uint32_t)e.vocab;
+  if (!valid && blockIdx.x == 0 && threadIdx.x == 0) report(status, kStatusInvalid);
+  int i0, i1;
+  flow_range(e.n, i0, i1);
+  for (int i = i0 + (int)threadIdx.x; i < i1; i += kFThreads) {
+    const float v = valid ? decode_tiled<KIND>(e.units, e.h, e.nb, (int)token, i) : 0.0f;
+    st_word(e.hidden + i, tagged(v, tag));
+    if (e.plain) e.plain[i] = v;
+  }
+}
+
+// A projection phase.  `cons` is the number of ring pieces consumed so far
+// (the same in every compute thread).
+template <int KIND>
+__device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32_t ep,
+                          uint32_t tag, int &cons, const FlowCtl &c, unsigned long long *tr) {
+  int t0, t1;
+  flow_range(p.ntiles, t0, t1);
+  if (t0 >= t1) return true;
+  const bool pair = p.epi == kEpiSwiglu;
+  const int nb = p.nb, n = nb * 256, upt = pair ? 2 * nb : nb;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint8_t *act = smem + kFOffAct;
+  float *work = reinterpret_cast<float *>(smem + kFOffWork);
+  double *red = reinterpret_cast<double *>(smem + kFOffRed);
+
+  // 1. the Q8_K activation
+  if (p.prologue == kFGated) {
+    // o and SiLU(z) per head, the gated norm into y (one warp per head,
+    // gated_heads_norm's order), then the quantization of y
+    const int S = p.head_dim;  // 128
+    float *y = work;
+    const uint32_t itag = flow_tag(ep, p.in_k), ztag = flow_tag(ep, p.zs_k);
+    float nw[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) nw[q] = p.norm_w[32 * q + lane];
+    bool ok = true;
+    for (int h = warp; h < p.heads && ok; h += kFWarps) {
+      float o[4], g[4];
+      ok = wait_words<4>(p.in, h * S + lane, 32, 4, itag, o, c) &&
+           wait_words<4>(p.zs, h * S + lane, 32, 4, ztag, g, c);
+      if (!ok) break;
+      double t = 0.0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) t += warp_sum_f64((double)__fmul_rn(o[q], o[q]));
+      const float mean = (float)(t / (double)S);
+      const float nscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float normed = __fmul_rn(__fmul_rn(o[q], nscale), nw[q]);
+        y[h * S + 32 * q + lane] = __fmul_rn(normed, g[q]);
+      }
+    }
+    if (!csync_and(ok)) return false;
+    quantize_staged(y, nb, 1.0f, nullptr, false, act, c.status, float4(), float4());
+  } else {
+    float *xs = work;
+    double s = 0.0;
+    const bool rms = p.prologue == kFRms;
+    // the norm weights do not depend on this step: load them first
+    float4 nw0 = float4(), nw1 = float4();
+    if (rms && warp < nb) {
+      nw0 = *reinterpret_cast<const float4 *>(p.norm_w + warp * 256 + lane * 8);
+      nw1 = *reinterpret_cast<const float4 *>(p.norm_w + warp * 256 + lane * 8 + 4);
+    }
+    const bool ok = stage_words(p.in, n, flow_tag(ep, p.in_k), xs, rms, s, c);
+    if (!csync_and(ok)) return false;
+    float scale = 1.0f;
+    if (rms) {
+      // block_sumsq_f64: per-thread sums, warp butterfly, warps in order
+      const double sum = fsum_f64(s, red);
+      const float mean = (float)(sum / (double)n);
+      scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+      if ((!is_finite_f(scale) || !(scale > 0.0f)) && tid == 0) report(c.status, kStatusNonfinite);
+    }
+    quantize_staged(xs, nb, scale, p.norm_w, rms, act, c.status, nw0, nw1);
+  }
+  csync();
+  if (tr) tr[1] = global_timer_ns();
+
+  const MatvecSmem L(nb, 32, 0, nb);
+  const int8_t *values = reinterpret_cast<const int8_t *>(act + L.act_values());
+  const float *ascale = reinterpret_cast<const float *>(act + L.act_scale());
+  const int16_t *asums = reinterpret_cast<const int16_t *>(act + L.act_sums());
+  const int *aasum = reinterpret_cast<const int *>(act + L.act_asum());
+  float *terms = work;  // [batch tiles][upt][32]
+
+  // 2. batches of this CTA's tiles: all of them when the ring holds them
+  // together (they streamed during earlier phases), otherwise batches that
+  // leave room for the next batch to stream in
+  const int mine = t1 - t0;
+  uint32_t maxpiece = 0, total = 0;
+  for (int t = t0; t < t1; ++t) {
+    const uint32_t b = piece_bytes<KIND>(p, t);
+    maxpiece = max(maxpiece, b);
+    total += b;
+  }
+  const int term_cap = (kFWorkBytes / 4) / (upt * 32);
+  int cap = total + maxpiece <= (uint32_t)kFRing
+                ? mine
+                : (int)(((uint32_t)kFRing - maxpiece) / maxpiece / 2);
+  cap = max(1, min(cap, min(term_cap, kFWarps)));  // one chain warp per tile
+  unsigned long long best = 0ull;
+  for (int k0 = 0; k0 < mine; k0 += cap) {
+    const int B = min(cap, mine - k0);
+    // the chain thread of a tile row (warp = tile in the batch, lane = row)
+    // starts its residual load now, so the load overlaps the dots
+    const int ck = warp;
+    const int ct = t0 + k0 + ck;
+    const int cg = ck < B ? (pair ? 0 : flow_group(p, ct)) : 0;
+    const int ch = p.h[cg];
+    const int corow = (pair ? ct : ct - p.tile_start[cg]) * ch + lane;
+    const bool chain = ck < B && lane < ch && corow < p.rows[cg];
+    uint64_t resw = 0;
+    const uint32_t rtag = flow_tag(ep, p.res_k);
+    if (chain && p.res && !pair) resw = ld_word(p.res + corow);
+    bool arrived = true;
+    for (int k = 0; k < B && arrived; ++k)
+      arrived = mbar_wait_bounded(&rg.bar[(cons + k) % kFSlots],
+                                  (unsigned)((cons + k) / kFSlots) & 1u, c.status);
+    if (!csync_and(arrived)) {
+      if (tid == 0) flow_raise(c);
+      return false;
+    }
+    const int tot = B * upt;
+    for (int u = warp; u < tot; u += kFWarps) {
+      const int k = u / upt, j = u - k * upt;
+      const int t = t0 + k0 + k;
+      const int g = pair ? 0 : flow_group(p, t);
+      const int H = p.h[g];
+      const uint8_t *ud = rg.data + rg.off[(cons + k) % kFSlots] + j * unit_bytes(KIND, H);
+      const int b = pair && j >= nb ? j - nb : j;
+      float *out = terms + (k * upt + j) * 32;
+      int dot, dot2;
+      float term;
+      if (H == 32)
+        unit_terms<KIND, 32>(ud, values + b * 256, aasum[b], asums + b * 16, ascale[b], lane, dot,
+                             dot2, term);
+      else if (H == 16)
+        unit_terms<KIND, 16>(ud, values + b * 256, aasum[b], asums + b * 16, ascale[b], lane, dot,
+                             dot2, term);
+      else
+        unit_terms<KIND, 8>(ud, values + b * 256, aasum[b], asums + b * 16, ascale[b], lane, dot,
+                            dot2, term);
+      if (lane < H) out[lane] = term;
+    }
+    csync();
+    if (tid == 0) {
+      // the batch's ring space is free again
+      uint32_t rel = 0;
+      for (int k = 0; k < B; ++k) rel += rg.len[(cons + k) % kFSlots];
+      st_release_cta(rg.tail, *rg.tail + rel);
+      st_release_cta(rg.released, (uint32_t)(cons + B));
+    }
+    cons += B;
+    bool ok = true;
+    if (chain) {
+      const float *tk = terms + ck * upt * 32;
+      // the reference's chain: sum = 0; sum += term_b for b in order
+      float sum = 0.0f;
+      for (int b = 0; b < nb; ++b) sum = __fadd_rn(sum, tk[b * 32 + lane]);
+      const int r = corow;
+      if (pair) {
+        float gsum = 0.0f;
+        for (int b = nb; b < 2 * nb; ++b) gsum = __fadd_rn(gsum, tk[b * 32 + lane]);
+        const float hv = __fmul_rn(sum, silu_f(gsum));
+        if (!is_finite_f(sum) || !is_finite_f(gsum)) report(c.status, kStatusNonfinite);
+        st_word(p.out[0] + r, tagged(hv, tag));
+        if (p.plain[0]) p.plain[0][r] = hv;
+      } else {
+        if (p.res) {
+          if (!has_tag(resw, rtag)) ok = wait_word(p.res + r, rtag, resw, c);
+          sum = __fadd_rn(word_value(resw), sum);
+        }
+        if (!is_finite_f(sum)) report(c.status, kStatusNonfinite);
+        if (p.out[cg]) st_word(p.out[cg] + r, tagged(sum, tag));
+        if (p.plain[cg]) p.plain[cg][r] = sum;
+        if (p.epi == kEpiArgmax) {
+          const unsigned long long key = argmax_key(sum, r);
+          best = key > best ? key : best;
+        }
+      }
+    }
+    // the terms buffer is reused by the next batch
+    if (!csync_and(ok)) return false;
+  }
+  if (p.epi == kEpiArgmax) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+      best = o > best ? o : best;
+    }
+    if (lane == 0 && best) atomicMax(p.argmax_key, best);
+  }
+  return true;
+}
+
+// Gated DeltaNet layer: value head h over kGdnSlices CTAs of 16 state rows
+// (run_gdn's arithmetic).  Writes the pre-norm output and SiLU(z) of its
+// rows; the gated output norm runs in the out-projection's prologue.
+__device__ bool flow_gdn(const FGdn &a, int pos, uint8_t *smem, uint32_t ep, uint32_t tag,
+                         const FlowCtl &c) {
+  constexpr int S = 128, R = S / kGdnSlices;
+  if ((int)blockIdx.x >= a.values * kGdnSlices) return true;
+  float *q = reinterpret_cast<float *>(smem + kFOffWork);  // [S]
+  float *k = q + S;                                        // [S]
+  float *v = k + S;                                        // [R]
+  float *sdb = v + R;                                      // decay, beta
+  double *red = reinterpret_cast<double *>(smem + kFOffRed);
+  const int h = blockIdx.x / kGdnSlices, slice = blockIdx.x % kGdnSlices, r0 = slice * R;
+  const int kh = h % a.groups, kw = a.groups * S, hist = a.conv_k - 1;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int parity = pos & 1;
+  const float *hist_in = a.conv_state + parity * a.conv_buf_stride;
+  float *hist_out = a.conv_state + (parity ^ 1) * a.conv_buf_stride;
+  const uint32_t itag = flow_tag(ep, a.in_k);
+  // this slice's state rows (written by the previous step): before the inputs
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  float *row = a.state + (long)h * S * S + (long)(r0 + warp) * S;
+  if (warp < R) s = reinterpret_cast<const float4 *>(row)[lane];
+  // 1. convolution + SiLU of the head's q, k channels and this slice's v
+  bool ok = true;
+  if (tid < 2 * S + R) {
+    const int part = tid < S ? 0 : tid < 2 * S ? 1 : 2;
+    const int j = part < 2 ? tid - part * S : r0 + (tid - 2 * S);
+    const int ch = part == 0 ? kh * S + j : part == 1 ? kw + kh * S + j : 2 * kw + h * S + j;
+    const float *hj = hist_in + (long)ch * hist;
+    const float *cj = a.conv_w + (long)ch * a.conv_k;
+    float hv[8];
+    for (int i = 0; i < hist; ++i) hv[i] = hj[i];
+    uint64_t w;
+    ok = wait_word(a.mixed + ch, itag, w, c);
+    const float projected = word_value(w);
+    float sum = 0.0f;
+    for (int i = 0; i < hist; ++i) sum = __fadd_rn(sum, __fmul_rn(hv[i], cj[i]));
+    sum = __fadd_rn(sum, __fmul_rn(projected, cj[hist]));
+    const float act = silu_f(sum);
+    if (part == 0) q[j] = act;
+    else if (part == 1) k[j] = act;
+    else v[j - r0] = act;
+    if (ok && (part == 2 || (h == kh && slice == 0))) {
+      float *nj = hist_out + (long)ch * hist;
+      for (int i = 0; i + 1 < hist; ++i) nj[i] = hv[i + 1];
+      if (hist > 0) nj[hist - 1] = projected;
+    }
+  } else if (tid == 2 * S + R) {
+    uint64_t wa = 0, wb = 0;
+    ok = wait_word(a.alpha + h, itag, wa, c) && wait_word(a.beta + h, itag, wb, c);
+    sdb[0] = recurrent_decay_f(word_value(wa), a.dt_bias[h], a.ssm_a[h], c.status);
+    sdb[1] = sigmoid_f(word_value(wb));
+  } else if (tid >= 2 * S + R + 32 && tid < 2 * S + R + 32 + R) {
+    // SiLU(z) of this slice's rows, for the out-projection's gated norm
+    const int i = h * S + r0 + (tid - (2 * S + R + 32));
+    uint64_t wz;
+    ok = wait_word(a.z + i, itag, wz, c);
+    if (ok) st_word(a.zs + i, tagged(silu_f(word_value(wz)), tag));
+  }
+  if (!csync_and(ok)) return false;
+  // 2. L2 normalisation of q and k (the kernel's block-sum order)
+  {
+    const float xq = tid < S ? q[tid] : 0.0f;
+    const float xk = tid < S ? k[tid] : 0.0f;
+    const double sq = fsum_f64(tid < S ? (double)__fmul_rn(xq, xq) : 0.0, red);
+    const double sk = fsum_f64(tid < S ? (double)__fmul_rn(xk, xk) : 0.0, red);
+    const float scq = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sq), a.eps));
+    const float sck = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sk), a.eps));
+    csync();
+    if (tid < S) {
+      q[tid] = __fmul_rn(xq, scq);
+      k[tid] = __fmul_rn(xk, sck);
+    }
+  }
+  csync();
+  // 3. this slice's state rows, one per warp
+  const float decay = sdb[0], beta = sdb[1];
+  const float oscale = __fdiv_rn(1.0f, __fsqrt_rn((float)S));
+  if (warp < R) {
+    const float4 kk = reinterpret_cast<const float4 *>(k)[lane];
+    const float4 qq = reinterpret_cast<const float4 *>(q)[lane];
+    s.x = __fmul_rn(decay, s.x);
+    s.y = __fmul_rn(decay, s.y);
+    s.z = __fmul_rn(decay, s.z);
+    s.w = __fmul_rn(decay, s.w);
+    double dk = (double)__fmul_rn(s.x, kk.x) + (double)__fmul_rn(s.y, kk.y) +
+                (double)__fmul_rn(s.z, kk.z) + (double)__fmul_rn(s.w, kk.w);
+    dk = warp_sum_f64(dk);
+    const float delta = __fmul_rn(__fsub_rn(v[warp], (float)dk), beta);
+    s.x = __fadd_rn(s.x, __fmul_rn(delta, kk.x));
+    s.y = __fadd_rn(s.y, __fmul_rn(delta, kk.y));
+    s.z = __fadd_rn(s.z, __fmul_rn(delta, kk.z));
+    s.w = __fadd_rn(s.w, __fmul_rn(delta, kk.w));
+    const bool finite =
+        is_finite_f(s.x) && is_finite_f(s.y) && is_finite_f(s.z) && is_finite_f(s.w);
+    double dq = (double)__fmul_rn(s.x, qq.x) + (double)__fmul_rn(s.y, qq.y) +
+                (double)__fmul_rn(s.z, qq.z) + (double)__fmul_rn(s.w, qq.w);
+    dq = warp_sum_f64(dq);
+    reinterpret_cast<float4 *>(row)[lane] = s;
+    if (lane == 0) st_word(a.o + h * S + r0 + warp, tagged(__fmul_rn((float)dq, oscale), tag));
+    if (!__all_sync(0xffffffffu, finite) && lane == 0) report(c.status, kStatusNonfinite);
+  }
+  return true;
+}
+
+// RMSNorm(x)*w, RoPE, binary16 rounding over hd (== 256) values held one per
+// thread (threads at or past hd contribute zeros): norm_rope_round's
+// arithmetic over the compute warps.
+__device__ __forceinline__ float flow_norm_rope_round(float xi, const float *w, float eps, int hd,
+                                                      int rope, const float *cs, float *buf,
+                                                      double *red) {
+  const int i = threadIdx.x;
+  const double ss = fsum_f64(i < hd ? (double)__fmul_rn(xi, xi) : 0.0, red);
+  const float mean = (float)(ss / (double)hd);
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+  if (i < hd) buf[i] = __fmul_rn(__fmul_rn(xi, scale), w[i]);
+  csync();
+  float out = i < hd ? buf[i] : 0.0f;
+  const int half = rope / 2;
+  if (i < half) {
+    const float first = buf[i], second = buf[i + half];
+    out = __fsub_rn(__fmul_rn(first, cs[2 * i]), __fmul_rn(second, cs[2 * i + 1]));
+  } else if (i < rope) {
+    const int j = i - half;
+    const float first = buf[j], second = buf[i];
+    out = __fadd_rn(__fmul_rn(first, cs[2 * j + 1]), __fmul_rn(second, cs[2 * j]));
+  }
+  csync();
+  return round_f16(out);
+}
+
+// Attention of query head h split over kAttnSplit CTAs (attention_decode_
+// kernel's arithmetic; hd == 256).  The CTA's cached K and V rows stream
+// through shared-memory chunks by bulk copies issued before its inputs are
+// awaited; the softmax maximum, total and value partial sums are exchanged
+// through tagged words and combined in rank order.
+__device__ bool flow_attn(const FAttn &a, int pos, uint8_t *smem, const FRing &rg, uint32_t ep,
+                          uint32_t tag, const FlowCtl &c) {
+  if ((int)blockIdx.x >= a.heads * kAttnSplit) return true;
+  const int hd = a.hd;
+  uint8_t *work = smem + kFOffWork;
+  float *q = reinterpret_cast<float *>(work);  // [hd]
+  float *kc = q + hd;
+  float *vc = kc + hd;
+  float *buf = vc + hd;
+  float *cs = buf + hd;                        // [64]
+  float *scores = cs + 64;                     // [kFMaxScores]
+  uint8_t *kvbuf = work + (size_t)(4 * hd + 64 + kFMaxScores) * 4;
+  double *red = reinterpret_cast<double *>(smem + kFOffRed);
+  float *fred = reinterpret_cast<float *>(red + 16);
+  uint64_t *kvbar = rg.bar + kFSlots + 2;  // [4]
+  const int rank = blockIdx.x % kAttnSplit, h = blockIdx.x / kAttnSplit;
+  const int group = a.heads / a.kv_heads, kvh = h / group, kvw = a.kv_heads * hd;
+  const int i = threadIdx.x, warp = i >> 5, lane = i & 31;
+  const int per = (pos + kAttnSplit - 1) / kAttnSplit;
+  const int lo = min(pos, rank * per), hi = min(pos, lo + per);
+  const int rb = attn_row_bytes(hd, a.q8);
+  const int nbuf =
+      min(4, (int)((kFWorkBytes - (4 * hd + 64 + kFMaxScores) * 4) / (kFChunk * rb)));
+  const int nk = (hi - lo + kFChunk - 1) / kFChunk;  // chunks per pass
+  const uint32_t itag = flow_tag(ep, a.in_k);
+  // completed uses of each K/V buffer's barrier in earlier attention phases
+  // of this launch: the parity of chunk g's wait is (base + g / nbuf) & 1
+  uint32_t base[4];
+#pragma unroll
+  for (int b = 0; b < 4; ++b) base[b] = rg.kvuse[b];
+  auto par = [&](int g) { return (base[g % nbuf] + (uint32_t)(g / nbuf)) & 1u; };
+  // chunk g of the pass sequence (K chunks, then V chunks) into buffer
+  // g % nbuf: warp 0 issues one bulk copy per row (lane = row)
+  auto issue = [&](int g) {
+    const bool isv = g >= nk;
+    const int p0 = lo + (isv ? g - nk : g) * kFChunk, count = min(kFChunk, hi - p0);
+    uint64_t *bar = &kvbar[g % nbuf];
+    if (lane == 0) mbar_arrive_expect_tx(bar, (unsigned)(count * rb));
+    __syncwarp();
+    if (lane < count) {
+      const int pp = p0 + lane;
+      const size_t at = a.q8 ? ((size_t)pp * a.kv_heads + kvh) * rb
+                             : ((size_t)pp * kvw + (size_t)kvh * hd) * 2;
+      bulk_g2s(kvbuf + ((size_t)(g % nbuf) * kFChunk + lane) * rb,
+               (isv ? a.vcache : a.kcache) + at, (unsigned)rb, bar);
+    }
+  };
+  int issued = min(nbuf, 2 * nk), waited = 0;
+  if (warp == 0) {
+    fence_proxy_async_smem();  // the work area was read through the generic proxy
+    for (int g = 0; g < issued; ++g) issue(g);
+  }
+  if (i < a.rope_dim / 2) {
+    float theta = (float)pos;
+    for (int j = 0; j < i; ++j) theta = __fmul_rn(theta, a.theta_scale);
+    const float angle = i < 3 * a.sections[i % 3] ? theta : 0.0f;
+    cs[2 * i] = cos_cr(angle);
+    cs[2 * i + 1] = sin_cr(angle);
+  }
+  auto drain = [&]() {
+    // copies that were issued but never waited on: let them land (bounded)
+    if (i == 0)
+      for (int g = waited; g < issued; ++g) mbar_wait_bounded(&kvbar[g % nbuf], par(g), c.status);
+  };
+  // inputs: query, current key and value (thread i < hd), the gate of this
+  // CTA's output dimensions (threads hd .. hd + dims)
+  const int dims = hd / kAttnSplit;
+  float xq = 0.f, xk = 0.f, xv = 0.f, gate = 0.f;
+  bool ok = true;
+  if (i < hd) {
+    uint64_t w = 0;
+    ok = wait_word(a.proj + (long)h * 2 * hd + i, itag, w, c);
+    xq = word_value(w);
+    ok = ok && wait_word(a.key + (long)kvh * hd + i, itag, w, c);
+    xk = word_value(w);
+    ok = ok && wait_word(a.value + (long)kvh * hd + i, itag, w, c);
+    xv = word_value(w);
+  } else if (i < hd + dims) {
+    uint64_t w = 0;
+    ok = wait_word(a.proj + (long)(2 * h + 1) * hd + rank * dims + (i - hd), itag, w, c);
+    gate = word_value(w);
+  }
+  if (!csync_and(ok)) {
+    drain();
+    return false;
+  }
+  const float qv = flow_norm_rope_round(xq, a.q_norm, a.eps, hd, a.rope_dim, cs, buf, red);
+  const float kv_ = flow_norm_rope_round(xk, a.k_norm, a.eps, hd, a.rope_dim, cs, buf, red);
+  if (i < hd) {
+    q[i] = qv;
+    kc[i] = kv_;
+    vc[i] = round_f16(xv);
+    // the first CTA of the first query head of the group writes the cache row
+    const bool writer = rank == 0 && h % group == 0;
+    if (a.q8) {
+      const long at = ((long)pos * a.kv_heads + kvh) * q8_0_record_bytes(hd);
+      kc[i] = q8_0_roundtrip(kc[i], writer ? a.kcache + at : nullptr, hd, c.status);
+      vc[i] = q8_0_roundtrip(vc[i], writer ? a.vcache + at : nullptr, hd, c.status);
+    } else if (writer) {
+      reinterpret_cast<uint16_t *>(a.kcache)[(long)pos * kvw + kvh * hd + i] =
+          float_to_half_bits(kc[i]);
+      reinterpret_cast<uint16_t *>(a.vcache)[(long)pos * kvw + kvh * hd + i] =
+          float_to_half_bits(vc[i]);
+    }
+  }
+  csync();
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+  const float4 q0 = reinterpret_cast<const float4 *>(q)[lane * 2];
+  const float4 q1 = reinterpret_cast<const float4 *>(q)[lane * 2 + 1];
+  // scores of the cached positions: warp per position, lane owns 8 dims
+  bool landed = true;
+  for (int chk = 0; chk < nk && landed; ++chk) {
+    landed = csync_and(mbar_wait_bounded(&kvbar[chk % nbuf], par(chk), c.status));
+    if (!landed) break;
+    ++waited;
+    const int p0 = lo + chk * kFChunk, count = min(kFChunk, hi - p0);
+    const uint8_t *rows = kvbuf + (size_t)(chk % nbuf) * kFChunk * rb;
+    for (int pp = warp; pp < count; pp += kFWarps) {
+      const double sc =
+          warp_sum_f64(key_partial_staged(rows + (size_t)pp * rb, hd, a.q8, q0, q1, lane));
+      if (lane == 0) scores[p0 + pp - lo] = __fmul_rn((float)sc, scale);
+    }
+    csync();  // the buffer is free again
+    if (chk + nbuf < 2 * nk) {
+      if (warp == 0) {
+        fence_proxy_async_smem();
+        issue(chk + nbuf);
+      }
+      ++issued;
+    }
+  }
+  if (!landed) {
+    drain();
+    if (i == 0) flow_raise(c);
+    return false;
+  }
+  // the current position's score (every CTA of the head computes it)
+  float s_cur;
+  {
+    const double sc = fsum_f64(i < hd ? (double)__fmul_rn(q[i], kc[i]) : 0.0, red);
+    s_cur = __fmul_rn((float)sc, scale);
+  }
+  float m = -INFINITY;
+  if (i < kAttnThreads)
+    for (int pp = i; pp < hi - lo; pp += kAttnThreads) m = fmaxf(m, scores[pp]);
+  m = fmax_f32(m, fred);
+  uint64_t *smax = a.smax + (long)h * kAttnSplit;
+  if (i == 0) st_word(smax + rank, tagged(m, tag));
+  float M = s_cur;
+  {
+    uint64_t w = 0;
+    ok = i < kAttnSplit ? wait_word(smax + i, tag, w, c) : true;
+    csync();  // fred was read by the maximum
+    if (i < kAttnSplit) fred[i] = word_value(w);
+    if (!csync_and(ok)) {
+      drain();
+      return false;
+    }
+    for (int r = 0; r < kAttnSplit; ++r) M = fmaxf(M, fred[r]);
+  }
+  double tot = 0.0;
+  if (i < kAttnThreads)
+    for (int pp = i; pp < hi - lo; pp += kAttnThreads) {
+      const float e = exp_cr(__fsub_rn(scores[pp], M));
+      scores[pp] = e;
+      tot += (double)e;
+    }
+  tot = fsum_f64(tot, red);
+  uint64_t *stot = a.stot + (long)h * kAttnSplit * 2;
+  if (i == 0) {
+    const unsigned long long bits = (unsigned long long)__double_as_longlong(tot);
+    st_word(stot + 2 * rank, tagged_u((uint32_t)bits, tag));
+    st_word(stot + 2 * rank + 1, tagged_u((uint32_t)(bits >> 32), tag));
+  }
+  double total = 0.0;
+  {
+    uint64_t w0 = 0, w1 = 0;
+    ok = i < kAttnSplit ? wait_word(stot + 2 * i, tag, w0, c) && wait_word(stot + 2 * i + 1, tag, w1, c)
+                        : true;
+    csync();  // red was read by the total
+    if (i < kAttnSplit) red[i] = word_pair_value(w0, w1);
+    if (!csync_and(ok)) {
+      drain();
+      return false;
+    }
+    for (int r = 0; r < kAttnSplit; ++r) total += red[r];
+  }
+  const float e_cur = exp_cr(__fsub_rn(s_cur, M));
+  total += (double)e_cur;
+  const float inv = (float)(1.0 / total);
+  if (!is_finite_f(M) && i == 0 && rank == 0) report(c.status, kStatusNonfinite);
+  const float p_cur = round_f16(__fmul_rn(e_cur, inv));
+  if (i < kAttnThreads)
+    for (int pp = i; pp < hi - lo; pp += kAttnThreads) scores[pp] = round_f16(__fmul_rn(scores[pp], inv));
+  csync();
+  // value partial sums of this CTA's positions: one dimension per thread
+  double acc = -0.0;
+  for (int chk = 0; chk < nk && landed; ++chk) {
+    const int g = nk + chk;
+    landed = csync_and(mbar_wait_bounded(&kvbar[g % nbuf], par(g), c.status));
+    if (!landed) break;
+    ++waited;
+    const int p0 = lo + chk * kFChunk, count = min(kFChunk, hi - p0);
+    const uint8_t *rows = kvbuf + (size_t)(g % nbuf) * kFChunk * rb;
+    if (i < hd)
+      for (int pp = 0; pp < count; ++pp)
+        acc += (double)__fmul_rn(scores[p0 + pp - lo],
+                                 value_staged(rows + (size_t)pp * rb, hd, a.q8, i));
+    csync();
+    if (g + nbuf < 2 * nk) {
+      if (warp == 0) {
+        fence_proxy_async_smem();
+        issue(g + nbuf);
+      }
+      ++issued;
+    }
+  }
+  if (!landed) {
+    drain();
+    if (i == 0) flow_raise(c);
+    return false;
+  }
+  uint64_t *part = a.part + ((long)h * kAttnSplit + rank) * hd * 2;
+  if (i < hd) {
+    const unsigned long long bits = (unsigned long long)__double_as_longlong(acc);
+    st_word(part + 2 * i, tagged_u((uint32_t)bits, tag));
+    st_word(part + 2 * i + 1, tagged_u((uint32_t)(bits >> 32), tag));
+  }
+  // every buffer's barrier completed its uses of this phase
+  if (i == 0)
+    for (int b = 0; b < nbuf; ++b)
+      rg.kvuse[b] = base[b] + (uint32_t)((2 * nk - b + nbuf - 1) / nbuf);
+  // the gate values sit in threads hd .. hd + dims: hand them over
+  if (i >= hd && i < hd + dims) buf[i - hd] = gate;
+  csync();
+  // CTA r finalises dimensions [r*dims, (r+1)*dims), ranks in order
+  ok = true;
+  if (i < dims) {
+    const int d = rank * dims + i;
+    double sum = -0.0;
+    for (int r = 0; r < kAttnSplit && ok; ++r) {
+      const uint64_t *pr = a.part + ((long)h * kAttnSplit + r) * hd * 2 + 2 * d;
+      uint64_t w0 = 0, w1 = 0;
+      ok = wait_word(pr, tag, w0, c) && wait_word(pr + 1, tag, w1, c);
+      sum += word_pair_value(w0, w1);
+    }
+    const float out = (float)(sum + (double)__fmul_rn(p_cur, vc[d]));
+    if (ok) st_word(a.out + (long)h * hd + d, tagged(__fmul_rn(out, sigmoid_f(buf[i])), tag));
+  }
+  return csync_and(ok);
+}
+
+// ---- the kernel --------------------------------------------------------------------
+
+template <int KIND>
+__global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  FRing rg;
+  rg.data = smem;
+  rg.bar = reinterpret_cast<uint64_t *>(smem + kFOffBars);
+  uint64_t *dbar = rg.bar + kFSlots;  // [2] descriptor arrivals; [2..5] attention K/V
+  rg.off = reinterpret_cast<uint32_t *>(smem + kFOffMeta);
+  rg.len = rg.off + kFSlots;
+  rg.tail = rg.len + kFSlots;
+  rg.released = rg.tail + 1;
+  rg.issued = rg.tail + 2;
+  rg.kvuse = rg.tail + 4;
+  const int tid = threadIdx.x;
+  if (tid < kFSlots + 6) mbar_init(&rg.bar[tid], 1);
+  if (tid < 8) rg.tail[tid] = 0u;
+  mbar_init_fence();
+  __syncthreads();
+  FlowCtl c;
+  c.status = fa.status;
+  c.abort = fa.sync + 1;
+  const int pos = *fa.st.position;
+  const uint32_t ep = fa.sync[2];
+  bool ok = true;
+  if (tid >= kFThreads) {
+    // the weight-streaming warp
+    if (tid == kFThreads) flow_producer<KIND>(fa, rg, c);
+  } else {
+    // the compute warps: descriptor p arrives in buffer p & 1 by a bulk copy
+    // issued at the start of phase p - 1
+    auto fetch = [&](int p) {
+      uint8_t *dst = smem + kFOffDesc + (p & 1) * kFDescBytes;
+      mbar_arrive_expect_tx(&dbar[p & 1], (unsigned)sizeof(FPhase));
+      bulk_g2s(dst, fa.phases + p, (unsigned)sizeof(FPhase), &dbar[p & 1]);
+    };
+    if (tid == 0) fetch(0);
+    int cons = 0, fetched = 1, waited = 0;
+    for (int p = 0; p < fa.nphases && ok; ++p) {
+      ok = csync_and(mbar_wait_bounded(&dbar[p & 1], (unsigned)(p >> 1) & 1u, c.status));
+      if (!ok) {
+        if (tid == 0) flow_raise(c);
+        break;
+      }
+      waited = p + 1;
+      if (p + 1 < fa.nphases) {
+        if (tid == 0) {
+          fence_proxy_async_smem();  // buffer (p+1)&1 was read in phase p-1
+          fetch(p + 1);
+        }
+        fetched = p + 2;
+      }
+      const FPhase &ph = *reinterpret_cast<const FPhase *>(smem + kFOffDesc + (p & 1) * kFDescBytes);
+      unsigned long long *tr = fa.trace && blockIdx.x == 0 && tid == 0 ? fa.trace + 8 * p : nullptr;
+      if (tr) tr[0] = global_timer_ns();
+      const uint32_t tag = flow_tag(ep, ph.k);
+      switch (ph.type) {
+        case kFEmbed:
+          flow_embed<KIND>(ph.em, fa.st, pos, tag, c.status);
+          break;
+        case kFProj:
+          ok = flow_proj<KIND>(ph.pr, rg, smem, ep, tag, cons, c, tr);
+          break;
+        case kFGdn:
+          ok = flow_gdn(ph.gd, pos, smem, ep, tag, c);
+          break;
+        default:
+          ok = flow_attn(ph.at, pos, smem, rg, ep, tag, c);
+          break;
+      }
+      ok = csync_and(ok);
+      if (tr) tr[7] = global_timer_ns();
+    }
+    if (!ok && tid == 0 && fetched > waited) {
+      // aborted: the next phase's descriptor copy may still be in flight
+      const int q = fetched - 1;
+      mbar_wait_bounded(&dbar[q & 1], (unsigned)(q >> 1) & 1u, c.status);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // every piece the producer issued was consumed, or is drained here
+    const uint32_t issued = *rg.issued, released = *rg.released;
+    for (uint32_t i = released; i < issued; ++i)
+      mbar_wait_bounded(&rg.bar[i % kFSlots], (i / kFSlots) & 1u, fa.status);
+    // the last CTA to finish advances the step
+    if (ok && !flow_aborted(c)) {
+      __threadfence();
+      const unsigned done = atomicAdd(&fa.sync[0], 1u);
+      if (done == gridDim.x - 1) {
+        __threadfence();
+        const int next = pos + 1;
+        unsigned long long *key = fa.st.argmax;
+        if (fa.write_greedy && next >= *fa.st.prompt_end) {
+          const unsigned long long k = *reinterpret_cast<volatile unsigned long long *>(key);
+          fa.st.tokens[next] = 0xffffffffu - (unsigned)(k & 0xffffffffull);
+        }
+        *key = 0ull;
+        *fa.st.position = next;
+        fa.sync[2] = ep + 1u;
+        fa.sync[0] = 0u;
+        __threadfence();
+      }
+    }
+  }
+}
+
+}  // namespace prism

@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "executor.cuh"
+#include "flow.cuh"
 #include "model_kernels.cuh"
 #include "persist.cuh"
 
@@ -79,6 +80,16 @@ struct prism_b200_model {
   int nseqtrace = 0;
   float *gdn_o = nullptr, *smax = nullptr;
   double *stot = nullptr, *apart = nullptr;
+  // the dataflow step (flow.cuh): phase list, tagged activations, step words
+  bool flow = false;
+  prism::FPhase *d_fphases = nullptr;
+  int nfphases = 0;
+  unsigned *d_fsync = nullptr;  // [0] finished CTAs, [1] abort, [2] step epoch
+  unsigned long long *d_ftrace = nullptr;
+  uint64_t *t_hidden = nullptr, *t_mixed = nullptr, *t_z = nullptr, *t_beta = nullptr,
+           *t_alpha = nullptr, *t_o = nullptr, *t_zs = nullptr, *t_proj = nullptr,
+           *t_key = nullptr, *t_value = nullptr, *t_att = nullptr, *t_up = nullptr,
+           *t_smax = nullptr, *t_stot = nullptr, *t_part = nullptr;
   prism::PrefillBuffers pre;
   std::map<std::string, bool> bound;
   std::vector<void *> allocations;
@@ -98,6 +109,19 @@ struct prism_b200_model {
 };
 
 namespace prism {
+
+// The step mode: PRISM_B200_STEP=flow|seq|persist; without it the kernel
+// sequence, or the barrier-synchronised persistent step with
+// PRISM_B200_PERSIST=1.
+inline int step_mode_request() {
+  const char *e = getenv("PRISM_B200_STEP");
+  if (e && !strcmp(e, "seq")) return 0;
+  if (e && !strcmp(e, "persist")) return 1;
+  if (e && !strcmp(e, "flow")) return 2;
+  const char *p = getenv("PRISM_B200_PERSIST");
+  if (p && p[0] == '1') return 1;
+  return 0;
+}
 
 // Dynamic shared memory of an attention_decode_kernel launch over a cache of
 // `context` positions: with the CTA's K and V rows staged when they fit
@@ -544,8 +568,7 @@ inline std::vector<Phase> build_phases(prism_b200_model *m) {
 // Whether this model and device fit the persistent step's fixed limits.
 inline bool persist_eligible(prism_b200_model *m, const std::vector<Phase> &P) {
   const auto &c = m->cfg;
-  const char *env = getenv("PRISM_B200_PERSIST");
-  if (!env || env[0] != '1') return false;  // opt-in while the kernel sequence is faster
+  if (step_mode_request() != 1) return false;  // opt-in
   const int sms = m->ex->num_sms;
   int coop = 0, optin = 0;
   cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->ex->device);
@@ -633,11 +656,243 @@ inline cudaError_t launch_persistent(prism_b200_model *m, bool head, bool trace 
                                   : cudaLaunchKernelEx(&cfg, decode_persistent_kernel<10>, pa);
 }
 
+// ---- the dataflow step (flow.cuh) ---------------------------------------------
+
+// The step's phases in order; phase k writes its outputs with tag k, and each
+// reader names the phase that wrote its input.  The ingest list stops before
+// the LM head (the last phase).
+inline std::vector<FPhase> build_flow_phases(prism_b200_model *m) {
+  const auto &c = m->cfg;
+  std::vector<FPhase> P;
+  auto proj = [&](int prologue, const uint64_t *in, int in_k, const float *norm_w, int nb,
+                  std::initializer_list<std::pair<const DeviceWeight *, uint64_t *>> ws,
+                  int epi) {
+    FPhase ph;
+    memset(&ph, 0, sizeof(ph));
+    ph.type = kFProj;
+    ph.k = (int)P.size();
+    FProj &pr = ph.pr;
+    pr.prologue = prologue;
+    pr.in = in;
+    pr.in_k = in_k;
+    pr.norm_w = norm_w;
+    pr.eps = c.eps;
+    pr.nb = nb;
+    pr.epi = epi;
+    pr.count = 0;
+    for (const auto &w : ws) {
+      const int g = pr.count++;
+      pr.units[g] = w.first->units;
+      pr.h[g] = w.first->h;
+      pr.rows[g] = (int)w.first->rows;
+      pr.out[g] = w.second;
+      pr.tile_start[g + 1] = pr.tile_start[g] + w.first->ntiles;
+    }
+    for (int g = pr.count; g < kMaxGroup; ++g) pr.tile_start[g + 1] = pr.tile_start[pr.count];
+    pr.ntiles = epi == kEpiSwiglu ? ws.begin()->first->ntiles : pr.tile_start[pr.count];
+    return ph;
+  };
+  int k_hidden = 0;
+  {
+    FPhase ph;
+    memset(&ph, 0, sizeof(ph));
+    ph.type = kFEmbed;
+    ph.k = 0;
+    ph.em.units = m->embd.units;
+    ph.em.h = m->embd.h;
+    ph.em.nb = m->embd.nb;
+    ph.em.vocab = (int)c.vocab;
+    ph.em.n = (int)c.hidden;
+    ph.em.hidden = m->t_hidden;
+    ph.em.plain = m->hidden;
+    P.push_back(ph);
+  }
+  const int hnb = (int)(c.hidden / 256);
+  for (auto &Ly : m->L) {
+    if (Ly.full) {
+      FPhase a1 = proj(kFRms, m->t_hidden, k_hidden, Ly.attn_norm, hnb,
+                       {{&Ly.q, m->t_proj}, {&Ly.k, m->t_key}, {&Ly.v, m->t_value}}, kEpiStore);
+      P.push_back(a1);
+      FPhase ph;
+      memset(&ph, 0, sizeof(ph));
+      ph.type = kFAttn;
+      ph.k = (int)P.size();
+      FAttn &at = ph.at;
+      at.proj = m->t_proj;
+      at.key = m->t_key;
+      at.value = m->t_value;
+      at.in_k = a1.k;
+      at.q_norm = Ly.q_norm;
+      at.k_norm = Ly.k_norm;
+      at.kcache = reinterpret_cast<uint8_t *>(Ly.kc);
+      at.vcache = reinterpret_cast<uint8_t *>(Ly.vc);
+      at.q8 = c.kv_policy == PRISM_B200_KV_Q8_0 ? 1 : 0;
+      at.heads = (int)c.heads;
+      at.kv_heads = (int)c.kv_heads;
+      at.hd = (int)c.head_dim;
+      at.rope_dim = (int)c.rope_dim;
+      for (int j = 0; j < 3; ++j) at.sections[j] = (int)c.rope_sections[j];
+      at.eps = c.eps;
+      at.theta_scale = powf(c.rope_base, -2.0f / (float)c.rope_dim);
+      at.smax = m->t_smax;
+      at.stot = m->t_stot;
+      at.part = m->t_part;
+      at.out = m->t_att;
+      P.push_back(ph);
+      FPhase a3 = proj(kFF32, m->t_att, ph.k, nullptr, (int)(c.heads * c.head_dim / 256),
+                       {{&Ly.o, m->t_hidden}}, kEpiStore);
+      a3.pr.res = m->t_hidden;
+      a3.pr.res_k = k_hidden;
+      a3.pr.plain[0] = m->hidden;
+      P.push_back(a3);
+      k_hidden = a3.k;
+    } else {
+      FPhase g1 = proj(kFRms, m->t_hidden, k_hidden, Ly.attn_norm, hnb,
+                       {{&Ly.qkv, m->t_mixed}, {&Ly.z, m->t_z}, {&Ly.beta, m->t_beta},
+                        {&Ly.alpha, m->t_alpha}},
+                       kEpiStore);
+      P.push_back(g1);
+      FPhase ph;
+      memset(&ph, 0, sizeof(ph));
+      ph.type = kFGdn;
+      ph.k = (int)P.size();
+      FGdn &g = ph.gd;
+      g.mixed = m->t_mixed;
+      g.z = m->t_z;
+      g.beta = m->t_beta;
+      g.alpha = m->t_alpha;
+      g.in_k = g1.k;
+      g.conv_w = Ly.conv_w;
+      g.dt_bias = Ly.dt_bias;
+      g.ssm_a = Ly.ssm_a;
+      g.conv_state = Ly.conv_state;
+      g.conv_buf_stride = (long)m->channels() * (c.conv_kernel - 1);
+      g.state = Ly.matrix;
+      g.o = m->t_o;
+      g.zs = m->t_zs;
+      g.S = (int)c.ssm_state;
+      g.groups = (int)c.ssm_groups;
+      g.values = (int)c.ssm_values;
+      g.conv_k = (int)c.conv_kernel;
+      g.eps = c.eps;
+      P.push_back(ph);
+      FPhase g3 = proj(kFGated, m->t_o, ph.k, Ly.ssm_norm, m->value_width() / 256,
+                       {{&Ly.out, m->t_hidden}}, kEpiStore);
+      g3.pr.zs = m->t_zs;
+      g3.pr.zs_k = ph.k;
+      g3.pr.heads = (int)c.ssm_values;
+      g3.pr.head_dim = (int)c.ssm_state;
+      g3.pr.res = m->t_hidden;
+      g3.pr.res_k = k_hidden;
+      g3.pr.plain[0] = m->hidden;
+      P.push_back(g3);
+      k_hidden = g3.k;
+    }
+    FPhase f1 = proj(kFRms, m->t_hidden, k_hidden, Ly.post_norm, hnb,
+                     {{&Ly.up, m->t_up}, {&Ly.gate, nullptr}}, kEpiSwiglu);
+    P.push_back(f1);
+    FPhase f2 = proj(kFF32, m->t_up, f1.k, nullptr, (int)(c.ffn / 256), {{&Ly.down, m->t_hidden}},
+                     kEpiStore);
+    f2.pr.res = m->t_hidden;
+    f2.pr.res_k = k_hidden;
+    f2.pr.plain[0] = m->hidden;
+    P.push_back(f2);
+    k_hidden = f2.k;
+  }
+  FPhase hd = proj(kFRms, m->t_hidden, k_hidden, m->out_norm, hnb, {{&m->embd, nullptr}},
+                   kEpiArgmax);
+  hd.pr.plain[0] = m->logits;
+  hd.pr.argmax_key = m->d_argmax;
+  P.push_back(hd);
+  return P;
+}
+
+// Whether this model and device fit the dataflow step's fixed limits.
+inline bool flow_eligible(prism_b200_model *m, const std::vector<FPhase> &P) {
+  const auto &c = m->cfg;
+  const int sms = m->ex->num_sms;
+  int coop = 0, optin = 0;
+  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->ex->device);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->ex->device);
+  if (!coop || optin < kFSmemBytes) return false;
+  if ((int)(c.heads * kAttnSplit) > sms || (int)(c.ssm_values * kGdnSlices) > sms) return false;
+  if (c.ssm_state != 128 || c.head_dim != 256 || c.conv_kernel > 8) return false;
+  if ((c.context + kAttnSplit - 1) / kAttnSplit + 1 > (uint32_t)kFMaxScores) return false;
+  if (P.size() > 255) return false;  // the phase index is an 8-bit tag field
+  for (const FPhase &ph : P) {
+    if (ph.type != kFProj) continue;
+    const FProj &pr = ph.pr;
+    if (pr.nb > kFMaxNb) return false;
+    if (pr.epi == kEpiSwiglu && pr.h[0] != pr.h[1]) return false;
+    for (int g = 0; g < pr.count; ++g) {
+      const long piece = (long)pr.nb * unit_bytes((int)c.weight_kind, pr.h[g]) *
+                         (pr.epi == kEpiSwiglu ? 2 : 1);
+      if (piece > kFRing / 3) return false;
+    }
+    // one tile's terms must fit the work area
+    if ((pr.epi == kEpiSwiglu ? 2 : 1) * pr.nb * 32 * 4 > kFWorkBytes) return false;
+  }
+  int blocks = 0;
+  void *k = c.weight_kind == 35 ? (void *)decode_flow_kernel<35> : (void *)decode_flow_kernel<10>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmemBytes) !=
+          cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k, kFBlock, kFSmemBytes) !=
+          cudaSuccess ||
+      blocks < 1)
+    return false;
+  return true;
+}
+
+inline cudaError_t prepare_flow(prism_b200_model *m) {
+  m->flow = false;
+  if (step_mode_request() != 2) return cudaSuccess;
+  std::vector<FPhase> P = build_flow_phases(m);
+  if (!flow_eligible(m, P)) return cudaSuccess;
+  if (!m->d_fphases) {
+    // a model's layer count, and so its phase count, is fixed at creation
+    cudaError_t e = model_alloc(m, &m->d_fphases, P.size());
+    if (e == cudaSuccess) e = model_alloc(m, &m->d_ftrace, 8 * P.size());
+    if (e != cudaSuccess) return e;
+  }
+  m->nfphases = (int)P.size();
+  cudaError_t e = cudaMemcpy(m->d_fphases, P.data(), P.size() * sizeof(FPhase),
+                             cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return e;
+  m->flow = true;
+  return cudaSuccess;
+}
+
+// One cooperative launch: the whole step (with the LM head when `head`).
+inline cudaError_t launch_flow(prism_b200_model *m, bool head, bool trace = false) {
+  FlowArgs fa;
+  fa.phases = m->d_fphases;
+  fa.nphases = head ? m->nfphases : m->nfphases - 1;
+  fa.st = step_state(m);
+  fa.write_greedy = head ? 1 : 0;
+  fa.sync = m->d_fsync;
+  fa.status = m->ex->d_status;
+  fa.trace = trace ? m->d_ftrace : nullptr;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)m->ex->num_sms);
+  cfg.blockDim = dim3(kFBlock);
+  cfg.dynamicSmemBytes = kFSmemBytes;
+  cfg.stream = m->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return m->cfg.weight_kind == 35 ? cudaLaunchKernelEx(&cfg, decode_flow_kernel<35>, fa)
+                                  : cudaLaunchKernelEx(&cfg, decode_flow_kernel<10>, fa);
+}
+
 inline cudaError_t capture_step(prism_b200_model *m, bool head, cudaGraphExec_t *out) {
   cudaGraph_t graph = nullptr;
   cudaError_t e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
   if (e != cudaSuccess) return e;
-  cudaError_t e2 = m->persist ? launch_persistent(m, head) : enqueue_step(m, head);
+  cudaError_t e2 = m->flow      ? launch_flow(m, head)
+                   : m->persist ? launch_persistent(m, head)
+                                : enqueue_step(m, head);
   e = cudaStreamEndCapture(m->stream, &graph);
   if (e2 != cudaSuccess) e = e2;
   if (e == cudaSuccess) e = cudaGraphInstantiate(out, graph, 0);
@@ -717,6 +972,28 @@ int prism_b200_model_create(prism_b200_executor *ex, const prism_b200_qwen35_con
   A(m->stot, (size_t)c.heads * kAttnSplit);
   A(m->apart, (size_t)c.heads * kAttnSplit * c.head_dim);
   A(m->d_sync, 16);
+  A(m->d_fsync, 4);
+  A(m->t_hidden, c.hidden);
+  A(m->t_mixed, m->channels());
+  A(m->t_z, m->value_width());
+  A(m->t_beta, c.ssm_values);
+  A(m->t_alpha, c.ssm_values);
+  A(m->t_o, m->value_width());
+  A(m->t_zs, m->value_width());
+  A(m->t_proj, (size_t)c.heads * c.head_dim * 2);
+  A(m->t_key, m->kvw());
+  A(m->t_value, m->kvw());
+  A(m->t_att, (size_t)c.heads * c.head_dim);
+  A(m->t_up, c.ffn);
+  A(m->t_smax, (size_t)c.heads * kAttnSplit);
+  A(m->t_stot, (size_t)c.heads * kAttnSplit * 2);
+  A(m->t_part, (size_t)c.heads * kAttnSplit * c.head_dim * 2);
+  if (e == cudaSuccess) {
+    // tags carry the step epoch; it starts at 1 so that no zero-filled word
+    // matches, and it only grows (reset keeps it)
+    const unsigned one = 1u;
+    e = cudaMemcpy(m->d_fsync + 2, &one, 4, cudaMemcpyHostToDevice);
+  }
   {
     const char *tr = getenv("PRISM_B200_TRACE");
     if (tr && tr[0] == '1') {
@@ -914,7 +1191,9 @@ int prism_b200_model_finalize(prism_b200_model *m) {
   if (m->g_ingest) cudaGraphExecDestroy(m->g_ingest);
   if (m->g_decode) cudaGraphExecDestroy(m->g_decode);
   m->g_ingest = m->g_decode = nullptr;
-  cudaError_t e = prepare_persistent(m);
+  cudaError_t e = prepare_flow(m);
+  if (e != cudaSuccess) return cuda_fail(ex, e, "dataflow step setup");
+  e = m->flow ? cudaSuccess : prepare_persistent(m);
   if (e != cudaSuccess) return cuda_fail(ex, e, "persistent step setup");
   e = capture_step(m, false, &m->g_ingest);
   if (e == cudaSuccess) e = capture_step(m, true, &m->g_decode);
@@ -942,6 +1221,8 @@ int prism_b200_model_reset(prism_b200_model *m) {
     }
   }
   CK(cudaMemsetAsync(m->d_sync, 0, 16 * 4, s), "reset");
+  CK(cudaMemsetAsync(m->d_fsync, 0, 2 * 4, s), "reset");
+  CK(cudaMemsetAsync(m->d_argmax, 0, 8, s), "reset");
   CK(cudaMemsetAsync(m->d_hsync, 0, (size_t)(m->nhsync > 0 ? m->nhsync : 1) * 4, s), "reset");
   CK(cudaMemsetAsync(m->d_position, 0, 4, s), "reset");
   CK(cudaMemsetAsync(m->d_tokens, 0, ((size_t)c.context + 1) * 4, s), "reset");
@@ -952,10 +1233,22 @@ int prism_b200_model_reset(prism_b200_model *m) {
 
 int64_t prism_b200_model_position(const prism_b200_model *m) { return m ? m->position : -1; }
 
-int prism_b200_model_persistent(const prism_b200_model *m) { return m && m->persist ? 1 : 0; }
+int prism_b200_model_persistent(const prism_b200_model *m) {
+  return m && (m->persist || m->flow) ? 1 : 0;
+}
+
+int prism_b200_model_step_mode(const prism_b200_model *m) {
+  return !m ? -1 : m->flow ? 2 : m->persist ? 1 : 0;
+}
 
 int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t count) {
   if (!m || !ns) return -PRISM_B200_E_INVALID;
+  if (m->flow) {
+    const size_t n = std::min(count, (size_t)8 * m->nfphases);
+    if (cudaMemcpy(ns, m->d_ftrace, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
+      return -PRISM_B200_E_DEVICE;
+    return (int64_t)n;
+  }
   if (!m->persist) {
     // the kernel-sequence step's per-launch timelines, when enabled
     if (!m->d_seqtrace) return 0;
@@ -1102,6 +1395,34 @@ int prism_b200_model_step_timings(prism_b200_model *m, float *attention_ms, floa
     return ex->fail(PRISM_B200_E_INVALID, "context is exhausted");
   cudaSetDevice(ex->device);
   const int nl = (int)m->L.size();
+  if (m->flow) {
+    // one traced dataflow step: CTA 0's phase ends (each phase's input wait
+    // counted in the phase)
+    std::vector<unsigned long long> t((size_t)8 * m->nfphases);
+    cudaError_t e = cudaMemsetAsync(m->d_ftrace, 0, t.size() * 8, m->stream);
+    if (e == cudaSuccess) e = prism::launch_flow(m, true, true);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpy(t.data(), m->d_ftrace, t.size() * 8, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(ex, e, "traced step");
+    auto end = [&](int q) { return t[(size_t)8 * q + 7]; };
+    auto ms = [](unsigned long long a, unsigned long long b) {
+      return (float)((double)(b - a) * 1e-6);
+    };
+    int p = 1;  // phase 0 is the embedding
+    for (int l = 0; l < nl; ++l) {
+      const int ffn = p + 3;  // three attention-side phases, then the FFN pair
+      if (attention_ms) attention_ms[l] = ms(end(p - 1), end(ffn - 1));
+      if (ffn_ms) ffn_ms[l] = ms(end(ffn - 1), end(ffn + 1));
+      p = ffn + 2;
+    }
+    if (head_ms) *head_ms = ms(end(p - 1), end(p));
+    if (total_ms) *total_ms = ms(t[0], end(m->nfphases - 1));
+    st = model_finish(m);
+    if (st) return st;
+    m->position += 1;
+    return PRISM_B200_OK;
+  }
   if (m->persist) {
     // one traced persistent step: CTA 0's phase boundaries (barrier waits
     // included in the phase that follows them)

@@ -140,6 +140,7 @@ struct FlowArgs {
   StepState st;
   int write_greedy;
   unsigned *sync;        // [0] finished CTAs, [1] abort word, [2] step epoch
+  unsigned long long *key;  // the LM head's greedy key while the step runs
   unsigned *status;
   unsigned long long *trace;  // optional: [8 * phase] CTA 0's globaltimer stamps
 };
@@ -477,6 +478,7 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
       float o[4], g[4];
       ok = wait_words<4>(p.in, h * S + lane, 32, 4, itag, o, c) &&
            wait_words<4>(p.zs, h * S + lane, 32, 4, ztag, g, c);
+      ok = __all_sync(0xffffffffu, ok);  // the warp's shuffles below need every lane
       if (!ok) break;
       double t = 0.0;
 #pragma unroll
@@ -1115,12 +1117,12 @@ __global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
       if (done == gridDim.x - 1) {
         __threadfence();
         const int next = pos + 1;
-        unsigned long long *key = fa.st.argmax;
-        if (fa.write_greedy && next >= *fa.st.prompt_end) {
-          const unsigned long long k = *reinterpret_cast<volatile unsigned long long *>(key);
+        // publish the step's greedy key and clear the working one
+        const unsigned long long k = *reinterpret_cast<volatile unsigned long long *>(fa.key);
+        *fa.st.argmax = k;
+        *fa.key = 0ull;
+        if (fa.write_greedy && next >= *fa.st.prompt_end)
           fa.st.tokens[next] = 0xffffffffu - (unsigned)(k & 0xffffffffull);
-        }
-        *key = 0ull;
         *fa.st.position = next;
         fa.sync[2] = ep + 1u;
         fa.sync[0] = 0u;

@@ -85,6 +85,7 @@ struct prism_b200_model {
   prism::FPhase *d_fphases = nullptr;
   int nfphases = 0;
   unsigned *d_fsync = nullptr;  // [0] finished CTAs, [1] abort, [2] step epoch
+  unsigned long long *d_fkey = nullptr;  // greedy key while a dataflow step runs
   unsigned long long *d_ftrace = nullptr;
   uint64_t *t_hidden = nullptr, *t_mixed = nullptr, *t_z = nullptr, *t_beta = nullptr,
            *t_alpha = nullptr, *t_o = nullptr, *t_zs = nullptr, *t_proj = nullptr,
@@ -802,7 +803,7 @@ inline std::vector<FPhase> build_flow_phases(prism_b200_model *m) {
   FPhase hd = proj(kFRms, m->t_hidden, k_hidden, m->out_norm, hnb, {{&m->embd, nullptr}},
                    kEpiArgmax);
   hd.pr.plain[0] = m->logits;
-  hd.pr.argmax_key = m->d_argmax;
+  hd.pr.argmax_key = m->d_fkey;
   P.push_back(hd);
   return P;
 }
@@ -870,6 +871,7 @@ inline cudaError_t launch_flow(prism_b200_model *m, bool head, bool trace = fals
   fa.st = step_state(m);
   fa.write_greedy = head ? 1 : 0;
   fa.sync = m->d_fsync;
+  fa.key = m->d_fkey;
   fa.status = m->ex->d_status;
   fa.trace = trace ? m->d_ftrace : nullptr;
   cudaLaunchConfig_t cfg = {};
@@ -973,6 +975,7 @@ int prism_b200_model_create(prism_b200_executor *ex, const prism_b200_qwen35_con
   A(m->apart, (size_t)c.heads * kAttnSplit * c.head_dim);
   A(m->d_sync, 16);
   A(m->d_fsync, 4);
+  A(m->d_fkey, 1);
   A(m->t_hidden, c.hidden);
   A(m->t_mixed, m->channels());
   A(m->t_z, m->value_width());
@@ -1222,7 +1225,7 @@ int prism_b200_model_reset(prism_b200_model *m) {
   }
   CK(cudaMemsetAsync(m->d_sync, 0, 16 * 4, s), "reset");
   CK(cudaMemsetAsync(m->d_fsync, 0, 2 * 4, s), "reset");
-  CK(cudaMemsetAsync(m->d_argmax, 0, 8, s), "reset");
+  CK(cudaMemsetAsync(m->d_fkey, 0, 8, s), "reset");
   CK(cudaMemsetAsync(m->d_hsync, 0, (size_t)(m->nhsync > 0 ? m->nhsync : 1) * 4, s), "reset");
   CK(cudaMemsetAsync(m->d_position, 0, 4, s), "reset");
   CK(cudaMemsetAsync(m->d_tokens, 0, ((size_t)c.context + 1) * 4, s), "reset");

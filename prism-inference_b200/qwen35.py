@@ -263,6 +263,18 @@ class Qwen35Model:
         return self.L.prism_b200_model_position(self.h)
 
     @property
+    def step_mode(self):
+        """2: the dataflow step kernel, 1: the barrier-synchronised persistent
+        kernel, 0: the per-phase kernel sequence (PRISM_B200_STEP at load)."""
+        import ctypes as c
+        L = self.L
+        if not getattr(L, "_mode_declared", False):
+            L.prism_b200_model_step_mode.restype = c.c_int
+            L.prism_b200_model_step_mode.argtypes = [c.c_void_p]
+            L._mode_declared = True
+        return int(L.prism_b200_model_step_mode(self.h))
+
+    @property
     def persistent(self):
         """True when each step runs as one persistent cooperative kernel."""
         return bool(self.L.prism_b200_model_persistent(self.h))

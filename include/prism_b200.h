@@ -359,6 +359,14 @@ int prism_b200_model_step_mode(const prism_b200_model *m);
  * is recorded).  No counterpart in the reference. */
 int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t count);
 
+/* Dataflow step only: every CTA's globaltimer stamps of the last
+ * prism_b200_model_step_timings step, [phase][CTA][2] (grid = the SM
+ * count): input staged (projection phases, else 0) and phase end, so that a
+ * phase's critical path (its slowest CTA) can be read.  Copies at
+ * most `count` values and returns how many (0 for other step modes).  No
+ * counterpart in the reference. */
+int64_t prism_b200_model_phase_trace_ctas(prism_b200_model *m, uint64_t *ns, size_t count);
+
 /* One token at the next position (reference Decoder::evaluate_finite_into,
  * src/graph.rs:5446).  `logits` (host, vocab floats) and `greedy` (the
  * reference's greedy selection, src/runtime.rs:2630) are optional. */

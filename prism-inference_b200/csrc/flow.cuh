@@ -49,7 +49,7 @@ namespace prism {
 constexpr int kFWarps = 16;                 // compute warps
 constexpr int kFThreads = kFWarps * 32;     // compute threads (named barrier 1)
 constexpr int kFBlock = kFThreads + 32;     // + the weight-streaming warp
-constexpr int kFRing = 150 * 1024;          // weight ring
+constexpr int kFRing = 148 * 1024;          // weight ring
 constexpr int kFSlots = 64;                 // pieces in flight
 constexpr int kFMaxNb = 48;                 // input blocks per projection (12288 values)
 constexpr int kFActBytes = (kFMaxNb * (256 + 4 + 32 + 4) + 127) / 128 * 128;
@@ -60,8 +60,9 @@ constexpr int kFMaxScores = 1024;           // attention: positions per CTA
 // shared-memory layout
 constexpr int kFOffAct = kFRing;
 constexpr int kFOffWork = kFOffAct + kFActBytes;
-constexpr int kFOffDesc = kFOffWork + kFWorkBytes;           // [2] phase descriptors
-constexpr int kFOffBars = kFOffDesc + 2 * kFDescBytes;       // ring [kFSlots], desc [2], kv [4]
+constexpr int kFOffDesc = kFOffWork + kFWorkBytes;           // [kFDescBufs] phase descriptors
+constexpr int kFDescBufs = 4;              // descriptors prefetched kFDescBufs - 1 phases ahead
+constexpr int kFOffBars = kFOffDesc + kFDescBufs * kFDescBytes;  // ring [kFSlots], desc [4], kv [4]
 constexpr int kFOffMeta = kFOffBars + (kFSlots + 8) * 8;     // off/len [kFSlots], counters
 constexpr int kFOffRed = kFOffMeta + kFSlots * 8 + 64;       // double [16] + float [16]
 constexpr int kFSmemBytes = kFOffRed + 16 * 8 + 16 * 4 + 64;
@@ -143,6 +144,7 @@ struct FlowArgs {
   unsigned long long *key;  // the LM head's greedy key while the step runs
   unsigned *status;
   unsigned long long *trace;  // optional: [8 * phase] CTA 0's globaltimer stamps
+  unsigned long long *trace_cta;  // optional: [phase][CTA][2] input staged, phase end
 };
 
 // ---- small helpers -------------------------------------------------------------
@@ -331,15 +333,46 @@ template <int KIND>
 __device__ void flow_producer(const FlowArgs &fa, const FRing &rg, const FlowCtl &c) {
   uint32_t head = 0, issued = 0;
   bool ok = true;
-  for (int p = 0; p < fa.nphases && ok; ++p) {
+  // the phase's plan in registers: the waits below clobber memory, so
+  // fields read through the descriptor would be reloaded from global memory
+  // for every piece; the next phase's plan is loaded while this one issues
+  struct Plan {
+    const uint8_t *units[kMaxGroup];
+    int tile_start[kMaxGroup + 1];
+    int h[kMaxGroup];
+    int type, nb, epi, ntiles, count;
+  };
+  auto load_plan = [&](int p) {
+    Plan q;
     const FPhase &ph = fa.phases[p];
-    if (ph.type != kFProj) continue;
-    const FProj &pr = ph.pr;
+    q.type = ph.type;
+    q.nb = ph.pr.nb;
+    q.epi = ph.pr.epi;
+    q.ntiles = ph.pr.ntiles;
+    q.count = ph.pr.count;
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g) {
+      q.units[g] = ph.pr.units[g];
+      q.h[g] = ph.pr.h[g];
+      q.tile_start[g] = ph.pr.tile_start[g];
+    }
+    q.tile_start[kMaxGroup] = ph.pr.tile_start[kMaxGroup];
+    return q;
+  };
+  Plan next = load_plan(0);
+  for (int p = 0; p < fa.nphases && ok; ++p) {
+    const Plan pr = next;
+    if (p + 1 < fa.nphases) next = load_plan(p + 1);
+    if (pr.type != kFProj) continue;
     const bool pair = pr.epi == kEpiSwiglu;
     int t0, t1;
     flow_range(pr.ntiles, t0, t1);
     for (int t = t0; t < t1 && ok; ++t) {
-      const int g = pair ? 0 : flow_group(pr, t);
+      int g = 0;
+      if (!pair)
+#pragma unroll
+        for (int i = 1; i < kMaxGroup; ++i)
+          if (i < pr.count && t >= pr.tile_start[i]) g = i;
       const int lt = pair ? t : t - pr.tile_start[g];
       const uint32_t part = (uint32_t)pr.nb * unit_bytes(KIND, pr.h[g]);
       const uint32_t bytes = pair ? 2 * part : part;
@@ -452,7 +485,8 @@ __device__ void flow_embed(const FEmbed &e, const StepState &st, int pos, uint32
 // (the same in every compute thread).
 template <int KIND>
 __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32_t ep,
-                          uint32_t tag, int &cons, const FlowCtl &c, unsigned long long *tr) {
+                          uint32_t tag, int &cons, const FlowCtl &c, unsigned long long *tr,
+                          unsigned long long *ts) {
   int t0, t1;
   flow_range(p.ntiles, t0, t1);
   if (t0 >= t1) return true;
@@ -517,6 +551,7 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
   }
   csync();
   if (tr) tr[1] = global_timer_ns();
+  if (ts && tid == 0) *ts = global_timer_ns();
 
   const MatvecSmem L(nb, 32, 0, nb);
   const int8_t *values = reinterpret_cast<const int8_t *>(act + L.act_values());
@@ -562,6 +597,7 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
       if (tid == 0) flow_raise(c);
       return false;
     }
+    if (tr && k0 == 0) tr[2] = global_timer_ns();
     const int tot = B * upt;
     for (int u = warp; u < tot; u += kFWarps) {
       const int k = u / upt, j = u - k * upt;
@@ -585,6 +621,7 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
       if (lane < H) out[lane] = term;
     }
     csync();
+    if (tr && k0 == 0) tr[3] = global_timer_ns();
     if (tid == 0) {
       // the batch's ring space is free again
       uint32_t rel = 0;
@@ -623,6 +660,7 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
     }
     // the terms buffer is reused by the next batch
     if (!csync_and(ok)) return false;
+    if (tr && k0 == 0) tr[4] = global_timer_ns();
   }
   if (p.epi == kEpiArgmax) {
 #pragma unroll
@@ -786,7 +824,7 @@ __device__ bool flow_attn(const FAttn &a, int pos, uint8_t *smem, const FRing &r
   uint8_t *kvbuf = work + (size_t)(4 * hd + 64 + kFMaxScores) * 4;
   double *red = reinterpret_cast<double *>(smem + kFOffRed);
   float *fred = reinterpret_cast<float *>(red + 16);
-  uint64_t *kvbar = rg.bar + kFSlots + 2;  // [4]
+  uint64_t *kvbar = rg.bar + kFSlots + kFDescBufs;  // [4]
   const int rank = blockIdx.x % kAttnSplit, h = blockIdx.x / kAttnSplit;
   const int group = a.heads / a.kv_heads, kvh = h / group, kvw = a.kv_heads * hd;
   const int i = threadIdx.x, warp = i >> 5, lane = i & 31;
@@ -1032,7 +1070,7 @@ __global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
   FRing rg;
   rg.data = smem;
   rg.bar = reinterpret_cast<uint64_t *>(smem + kFOffBars);
-  uint64_t *dbar = rg.bar + kFSlots;  // [2] descriptor arrivals; [2..5] attention K/V
+  uint64_t *dbar = rg.bar + kFSlots;  // [kFDescBufs] descriptor arrivals, then attention K/V [4]
   rg.off = reinterpret_cast<uint32_t *>(smem + kFOffMeta);
   rg.len = rg.off + kFSlots;
   rg.tail = rg.len + kFSlots;
@@ -1040,7 +1078,7 @@ __global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
   rg.issued = rg.tail + 2;
   rg.kvuse = rg.tail + 4;
   const int tid = threadIdx.x;
-  if (tid < kFSlots + 6) mbar_init(&rg.bar[tid], 1);
+  if (tid < kFSlots + kFDescBufs + 4) mbar_init(&rg.bar[tid], 1);
   if (tid < 8) rg.tail[tid] = 0u;
   mbar_init_fence();
   __syncthreads();
@@ -1056,28 +1094,35 @@ __global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
   } else {
     // the compute warps: descriptor p arrives in buffer p & 1 by a bulk copy
     // issued at the start of phase p - 1
+    // the compute warps: descriptor p arrives in buffer p % kFDescBufs by a
+    // bulk copy issued kFDescBufs - 1 phases earlier (its copy queues behind
+    // the weight stream's, so it is issued well ahead)
+    constexpr int D = kFDescBufs;
     auto fetch = [&](int p) {
-      uint8_t *dst = smem + kFOffDesc + (p & 1) * kFDescBytes;
-      mbar_arrive_expect_tx(&dbar[p & 1], (unsigned)sizeof(FPhase));
-      bulk_g2s(dst, fa.phases + p, (unsigned)sizeof(FPhase), &dbar[p & 1]);
+      uint8_t *dst = smem + kFOffDesc + (p % D) * kFDescBytes;
+      mbar_arrive_expect_tx(&dbar[p % D], (unsigned)sizeof(FPhase));
+      bulk_g2s(dst, fa.phases + p, (unsigned)sizeof(FPhase), &dbar[p % D]);
     };
-    if (tid == 0) fetch(0);
-    int cons = 0, fetched = 1, waited = 0;
+    int fetched = min(D - 1, fa.nphases);
+    if (tid == 0)
+      for (int p = 0; p < fetched; ++p) fetch(p);
+    int cons = 0, waited = 0;
     for (int p = 0; p < fa.nphases && ok; ++p) {
-      ok = csync_and(mbar_wait_bounded(&dbar[p & 1], (unsigned)(p >> 1) & 1u, c.status));
+      ok = csync_and(mbar_wait_bounded(&dbar[p % D], (unsigned)(p / D) & 1u, c.status));
       if (!ok) {
         if (tid == 0) flow_raise(c);
         break;
       }
       waited = p + 1;
-      if (p + 1 < fa.nphases) {
+      if (fetched < fa.nphases) {
+        // buffer fetched % D was read in phase p - 1, which every thread left
         if (tid == 0) {
-          fence_proxy_async_smem();  // buffer (p+1)&1 was read in phase p-1
-          fetch(p + 1);
+          fence_proxy_async_smem();
+          fetch(fetched);
         }
-        fetched = p + 2;
+        ++fetched;
       }
-      const FPhase &ph = *reinterpret_cast<const FPhase *>(smem + kFOffDesc + (p & 1) * kFDescBytes);
+      const FPhase &ph = *reinterpret_cast<const FPhase *>(smem + kFOffDesc + (p % D) * kFDescBytes);
       unsigned long long *tr = fa.trace && blockIdx.x == 0 && tid == 0 ? fa.trace + 8 * p : nullptr;
       if (tr) tr[0] = global_timer_ns();
       const uint32_t tag = flow_tag(ep, ph.k);
@@ -1086,7 +1131,9 @@ __global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
           flow_embed<KIND>(ph.em, fa.st, pos, tag, c.status);
           break;
         case kFProj:
-          ok = flow_proj<KIND>(ph.pr, rg, smem, ep, tag, cons, c, tr);
+          ok = flow_proj<KIND>(ph.pr, rg, smem, ep, tag, cons, c, tr,
+                               fa.trace_cta ? fa.trace_cta + ((size_t)p * gridDim.x + blockIdx.x) * 2
+                                            : nullptr);
           break;
         case kFGdn:
           ok = flow_gdn(ph.gd, pos, smem, ep, tag, c);
@@ -1097,11 +1144,13 @@ __global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
       }
       ok = csync_and(ok);
       if (tr) tr[7] = global_timer_ns();
+      if (fa.trace_cta && tid == 0)
+        fa.trace_cta[((size_t)p * gridDim.x + blockIdx.x) * 2 + 1] = global_timer_ns();
     }
-    if (!ok && tid == 0 && fetched > waited) {
-      // aborted: the next phase's descriptor copy may still be in flight
-      const int q = fetched - 1;
-      mbar_wait_bounded(&dbar[q & 1], (unsigned)(q >> 1) & 1u, c.status);
+    if (!ok && tid == 0) {
+      // aborted: descriptor copies may still be in flight
+      for (int q = waited; q < fetched; ++q)
+        mbar_wait_bounded(&dbar[q % D], (unsigned)(q / D) & 1u, c.status);
     }
   }
   __syncthreads();

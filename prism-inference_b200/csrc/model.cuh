@@ -86,7 +86,7 @@ struct prism_b200_model {
   int nfphases = 0;
   unsigned *d_fsync = nullptr;  // [0] finished CTAs, [1] abort, [2] step epoch
   unsigned long long *d_fkey = nullptr;  // greedy key while a dataflow step runs
-  unsigned long long *d_ftrace = nullptr;
+  unsigned long long *d_ftrace = nullptr, *d_ftrace_cta = nullptr;
   uint64_t *t_hidden = nullptr, *t_mixed = nullptr, *t_z = nullptr, *t_beta = nullptr,
            *t_alpha = nullptr, *t_o = nullptr, *t_zs = nullptr, *t_proj = nullptr,
            *t_key = nullptr, *t_value = nullptr, *t_att = nullptr, *t_up = nullptr,
@@ -853,6 +853,8 @@ inline cudaError_t prepare_flow(prism_b200_model *m) {
     // a model's layer count, and so its phase count, is fixed at creation
     cudaError_t e = model_alloc(m, &m->d_fphases, P.size());
     if (e == cudaSuccess) e = model_alloc(m, &m->d_ftrace, 8 * P.size());
+    if (e == cudaSuccess)
+      e = model_alloc(m, &m->d_ftrace_cta, (size_t)2 * m->ex->num_sms * P.size());
     if (e != cudaSuccess) return e;
   }
   m->nfphases = (int)P.size();
@@ -874,6 +876,7 @@ inline cudaError_t launch_flow(prism_b200_model *m, bool head, bool trace = fals
   fa.key = m->d_fkey;
   fa.status = m->ex->d_status;
   fa.trace = trace ? m->d_ftrace : nullptr;
+  fa.trace_cta = trace ? m->d_ftrace_cta : nullptr;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)m->ex->num_sms);
   cfg.blockDim = dim3(kFBlock);
@@ -1238,6 +1241,15 @@ int64_t prism_b200_model_position(const prism_b200_model *m) { return m ? m->pos
 
 int prism_b200_model_persistent(const prism_b200_model *m) {
   return m && (m->persist || m->flow) ? 1 : 0;
+}
+
+int64_t prism_b200_model_phase_trace_ctas(prism_b200_model *m, uint64_t *ns, size_t count) {
+  if (!m || !ns) return -PRISM_B200_E_INVALID;
+  if (!m->flow) return 0;
+  const size_t n = std::min(count, (size_t)2 * m->ex->num_sms * m->nfphases);
+  if (cudaMemcpy(ns, m->d_ftrace_cta, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return -PRISM_B200_E_DEVICE;
+  return (int64_t)n;
 }
 
 int prism_b200_model_step_mode(const prism_b200_model *m) {

@@ -171,6 +171,87 @@ int prism_b200_project_f32_tokens_device(prism_b200_executor *ex, const prism_b2
                                          size_t tokens, const float *x_dev, int pinned,
                                          float *out_dev, void *stream);
 
+/* ---- the rest of the executor trait ------------------------------------ */
+
+/* Remaining submissions of a bounded session (reference
+ * src/kernels/projection.rs:20-28 `operation_capacity`).  This executor has
+ * no bounded session: always -1, the reference's `None` (opaque capacity). */
+int64_t prism_b200_executor_operation_capacity(const prism_b200_executor *ex);
+
+/* Direct F32 activations, one tensor or a sibling group sharing one input
+ * (reference src/kernels/projection.rs:93-96 `supports_f32`, :110-113
+ * `supports_f32_group`): kinds TQ2_0 / Q2_K with the geometry `supports`
+ * accepts; a group of 1..4 tensors of one kind and one column count. */
+int prism_b200_executor_supports_f32(const prism_b200_executor *ex,
+                                     const prism_b200_tensor *tensor);
+int prism_b200_executor_supports_f32_group(const prism_b200_executor *ex, size_t count,
+                                           const prism_b200_tensor *const *tensors);
+
+/* Q8_0 activations (reference src/kernels/projection.rs:62-90
+ * `supports_q8` / `project_q8`), which the reference routes for PTQ1 and
+ * odd-block PQ2 rows only.  TQ2_0 and Q2_K take Q8_K activations, so
+ * supports_q8 returns 0 and project_q8 returns PRISM_B200_E_UNSUPPORTED
+ * (the reference trait's default) with `out` zero-filled; the executor
+ * stays open. */
+int prism_b200_executor_supports_q8(const prism_b200_executor *ex,
+                                    const prism_b200_tensor *tensor);
+int prism_b200_project_q8(prism_b200_executor *ex, const prism_b200_weight *w,
+                          const void *activation, int pinned, float *out);
+
+/* 1: multi-token tiles run natively on the device (reference
+ * src/kernels/projection.rs:270-274 `supports_tile_tokens`). */
+int prism_b200_executor_supports_tile_tokens(const prism_b200_executor *ex);
+
+/* Two or three sibling projections over a tile of tokens sharing one input
+ * (reference src/kernels/projection.rs:158-210 `project_f32_pair_tokens`,
+ * `project_f32_triple_tokens`): x is [tokens][cols], out_k [tokens][rows_k].
+ * The tokens are quantized to Q8_K once and every weight runs on the
+ * tensor cores over them; each token's outputs equal
+ * prism_b200_project_f32_group's for that token, bit for bit.
+ * weights[0..1] / [0..2] share kind and columns; tokens <= 65536. */
+int prism_b200_project_f32_pair_tokens(prism_b200_executor *ex,
+                                       const prism_b200_weight *const *weights, size_t tokens,
+                                       const float *x, int pinned, float *out_a, float *out_b);
+int prism_b200_project_f32_triple_tokens(prism_b200_executor *ex,
+                                         const prism_b200_weight *const *weights, size_t tokens,
+                                         const float *x, int pinned, float *out_a, float *out_b,
+                                         float *out_c);
+
+/* Fused ffn_gate + ffn_up + SwiGLU: out = up(x) * silu(gate(x)) (reference
+ * src/kernels/projection.rs:212-260 `supports_f32_ffn_swiglu`,
+ * `project_f32_ffn_swiglu`, `project_f32_ffn_swiglu_tokens`; SwiGLU as
+ * src/graph.rs:121-131).  gate and up are [F][H] of one kind; out has F
+ * values (per token: [tokens][F]).  One token runs as one projection
+ * kernel over both weights; a token tile as two tensor-core GEMMs and an
+ * elementwise kernel.  Both equal up/gate from prism_b200_project_f32_group
+ * followed by the binary32 SwiGLU, bit for bit. */
+int prism_b200_executor_supports_f32_ffn_swiglu(const prism_b200_executor *ex,
+                                                const prism_b200_tensor *gate,
+                                                const prism_b200_tensor *up);
+int prism_b200_project_f32_ffn_swiglu(prism_b200_executor *ex, const prism_b200_weight *gate,
+                                      const prism_b200_weight *up, const float *x, int pinned,
+                                      float *out);
+int prism_b200_project_f32_ffn_swiglu_tokens(prism_b200_executor *ex,
+                                             const prism_b200_weight *gate,
+                                             const prism_b200_weight *up, size_t tokens,
+                                             const float *x, int pinned, float *out);
+
+/* The full FFN chain for one token (reference src/kernels/projection.rs:
+ * 262-293 `supports_f32_ffn_chain`, `project_f32_ffn_chain`):
+ *   out = residual + down(Q8_K(up(x) * silu(gate(x))))
+ * with `residual` optional (NULL: no add).  gate/up [F][H], down [H][F],
+ * one kind.  `hadamard_block_size` must be 0 (no rotation): a rotated chain
+ * returns PRISM_B200_E_UNSUPPORTED before any submission.  The token-tile
+ * form is prism_b200_ffn_chain_tokens below. */
+int prism_b200_executor_supports_f32_ffn_chain(const prism_b200_executor *ex,
+                                               const prism_b200_tensor *gate,
+                                               const prism_b200_tensor *up,
+                                               const prism_b200_tensor *down);
+int prism_b200_project_f32_ffn_chain(prism_b200_executor *ex, const prism_b200_weight *gate,
+                                     const prism_b200_weight *up, const prism_b200_weight *down,
+                                     const float *x, const float *residual,
+                                     uint32_t hadamard_block_size, int pinned, float *out);
+
 /* ---- FFN chain over tokens, one GPU or tensor-parallel ---------------- */
 
 /* The full intra-layer FFN chain over a tile of token activations

@@ -665,3 +665,4 @@ extern "C" int prism_b200_gdn_prefill_device_noalloc(prism_b200_executor *ex, in
 #include "batch.cuh"
 #include "prefill.cuh"
 #include "tp_ffn.cuh"
+#include "seam.cuh"

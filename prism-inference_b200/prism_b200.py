@@ -85,6 +85,20 @@ def load():
         "prism_b200_ffn_connect": (i32, [vp, vp]),
         "prism_b200_ffn_chain_tokens": (i32, [vp, sz, vp, vp, i32, vp]),
         "prism_b200_ffn_chain_tokens_device": (i32, [vp, sz, vp, vp, i32, vp, vp]),
+        "prism_b200_executor_operation_capacity": (i64, [vp]),
+        "prism_b200_executor_supports_f32": (i32, [vp, P(_Tensor)]),
+        "prism_b200_executor_supports_f32_group": (i32, [vp, sz, P(P(_Tensor))]),
+        "prism_b200_executor_supports_q8": (i32, [vp, P(_Tensor)]),
+        "prism_b200_project_q8": (i32, [vp, vp, vp, i32, vp]),
+        "prism_b200_executor_supports_tile_tokens": (i32, [vp]),
+        "prism_b200_project_f32_pair_tokens": (i32, [vp, P(vp), sz, vp, i32, vp, vp]),
+        "prism_b200_project_f32_triple_tokens": (i32, [vp, P(vp), sz, vp, i32, vp, vp, vp]),
+        "prism_b200_executor_supports_f32_ffn_swiglu": (i32, [vp, P(_Tensor), P(_Tensor)]),
+        "prism_b200_project_f32_ffn_swiglu": (i32, [vp, vp, vp, vp, i32, vp]),
+        "prism_b200_project_f32_ffn_swiglu_tokens": (i32, [vp, vp, vp, sz, vp, i32, vp]),
+        "prism_b200_executor_supports_f32_ffn_chain": (i32, [vp, P(_Tensor), P(_Tensor),
+                                                             P(_Tensor)]),
+        "prism_b200_project_f32_ffn_chain": (i32, [vp, vp, vp, vp, vp, vp, u32, i32, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -213,6 +227,38 @@ class ProjectionExecutor:
         n = load().prism_b200_executor_operation_count(self.h, ctypes.byref(t))
         return None if n < 0 else n
 
+    def operation_capacity(self):
+        """Remaining submissions of a bounded session, None when opaque
+        (reference src/kernels/projection.rs:20-28)."""
+        n = load().prism_b200_executor_operation_capacity(self.h)
+        return None if n < 0 else n
+
+    def supports_f32(self, tensor):
+        t = tensor._c()
+        return bool(load().prism_b200_executor_supports_f32(self.h, ctypes.byref(t)))
+
+    def supports_f32_group(self, tensors):
+        cs = [t._c() for t in tensors]
+        arr = (ctypes.POINTER(_Tensor) * len(cs))(*[ctypes.pointer(c) for c in cs])
+        return bool(load().prism_b200_executor_supports_f32_group(self.h, len(cs), arr))
+
+    def supports_q8(self, tensor):
+        t = tensor._c()
+        return bool(load().prism_b200_executor_supports_q8(self.h, ctypes.byref(t)))
+
+    def supports_tile_tokens(self):
+        return bool(load().prism_b200_executor_supports_tile_tokens(self.h))
+
+    def supports_f32_ffn_swiglu(self, gate, up):
+        g, u = gate._c(), up._c()
+        return bool(load().prism_b200_executor_supports_f32_ffn_swiglu(
+            self.h, ctypes.byref(g), ctypes.byref(u)))
+
+    def supports_f32_ffn_chain(self, gate, up, down):
+        g, u, d = gate._c(), up._c(), down._c()
+        return bool(load().prism_b200_executor_supports_f32_ffn_chain(
+            self.h, ctypes.byref(g), ctypes.byref(u), ctypes.byref(d)))
+
     # -- weights ---------------------------------------------------------
     def upload(self, tensor):
         t = tensor._c()
@@ -284,6 +330,65 @@ class ProjectionExecutor:
         oh = (ctypes.c_void_p * len(ws))(*[o.ctypes.data for o in outs])
         self._check(load().prism_b200_project_f32_group(self.h, len(ws), wh, _p(x), int(pinned), oh))
         return outs
+
+    def project_q8(self, weight, activation, pinned=False):
+        """Q8_0 activations (reference src/kernels/projection.rs:62-90)."""
+        w = self._weight(weight)
+        act = np.ascontiguousarray(activation)
+        out = np.zeros(w.rows, dtype=np.float32)
+        self._check(load().prism_b200_project_q8(self.h, w.handle, _p(act), int(pinned), _p(out)))
+        return out
+
+    def _tokens_group(self, fn, weights, x, pinned):
+        ws = [self._weight(w) for w in weights]
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim != 2 or x.shape[1] != ws[0].cols:
+            raise PrismB200Error(E_INVALID, "token tile must be [tokens][cols]")
+        outs = [np.zeros((x.shape[0], w.rows), dtype=np.float32) for w in ws]
+        wh = (ctypes.c_void_p * len(ws))(*[w.handle.value for w in ws])
+        self._check(fn(self.h, wh, x.shape[0], _p(x), int(pinned), *[_p(o) for o in outs]))
+        return outs
+
+    def project_f32_pair_tokens(self, weights, x, pinned=False):
+        """Two siblings over a token tile (reference projection.rs:158-181)."""
+        assert len(weights) == 2
+        return self._tokens_group(load().prism_b200_project_f32_pair_tokens, weights, x, pinned)
+
+    def project_f32_triple_tokens(self, weights, x, pinned=False):
+        """Three siblings over a token tile (reference projection.rs:183-210)."""
+        assert len(weights) == 3
+        return self._tokens_group(load().prism_b200_project_f32_triple_tokens, weights, x, pinned)
+
+    def project_f32_ffn_swiglu(self, gate, up, x, pinned=False):
+        """up(x) * silu(gate(x)) for one token (reference projection.rs:218-234)."""
+        g, u = self._weight(gate), self._weight(up)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.zeros(u.rows, dtype=np.float32)
+        self._check(load().prism_b200_project_f32_ffn_swiglu(self.h, g.handle, u.handle, _p(x),
+                                                             int(pinned), _p(out)))
+        return out
+
+    def project_f32_ffn_swiglu_tokens(self, gate, up, x, pinned=False):
+        """up(x) * silu(gate(x)) over a token tile (reference projection.rs:236-260)."""
+        g, u = self._weight(gate), self._weight(up)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.zeros((x.shape[0], u.rows), dtype=np.float32)
+        self._check(load().prism_b200_project_f32_ffn_swiglu_tokens(
+            self.h, g.handle, u.handle, x.shape[0], _p(x), int(pinned), _p(out)))
+        return out
+
+    def project_f32_ffn_chain(self, gate, up, down, x, residual=None, hadamard_block_size=0,
+                              pinned=False):
+        """residual + down(SwiGLU(gate(x), up(x))) for one token (reference
+        projection.rs:276-293)."""
+        g, u, d = self._weight(gate), self._weight(up), self._weight(down)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.zeros(d.rows, dtype=np.float32)
+        r = None if residual is None else np.ascontiguousarray(residual, dtype=np.float32)
+        self._check(load().prism_b200_project_f32_ffn_chain(
+            self.h, g.handle, u.handle, d.handle, _p(x), _p(r) if r is not None else None,
+            int(hadamard_block_size), int(pinned), _p(out)))
+        return out
 
     def quantize_q8k(self, x, pinned=False):
         x = np.ascontiguousarray(x, dtype=np.float32)

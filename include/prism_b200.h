@@ -432,18 +432,23 @@ int prism_b200_model_step_mode(const prism_b200_model *m);
  * [1] grid dependency passed, [2] input staged, [3] first tile resident,
  * [4] its dots, [5] its chains, [6] exit, and [7] the last CTA's exit
  * (projections; GDN and attention stamp [0], [1], [6], [7]).
- * For the dataflow step (mode 2): CTA 0's globaltimer stamps of the last
- * prism_b200_model_step_timings step, 8 values per phase in the same phase
- * order: [0] phase start (descriptor resident), [1] input staged
- * (projections), [7] phase end.
+ * For the dataflow step (mode 2): CTA 0's stamps of the last
+ * prism_b200_model_step_timings step, 16 values per phase in the same phase
+ * order, globaltimer ns unless noted: [5] before the descriptor wait,
+ * [0] descriptor resident, [6] next descriptor requested, [1] input staged,
+ * [2] first batch's weights resident, [3] its dots, [4] its chains,
+ * [7] phase end; projections also [8] before the weight wait, [9] after it,
+ * [10] pieces the weight stream was ahead (a count), [11] issue time of the
+ * batch's last piece, [12] pieces in the batch (a count).
  * Copies at most `count` values and returns how many (0 when no timeline
  * is recorded).  No counterpart in the reference. */
 int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t count);
 
 /* Dataflow step only: every CTA's globaltimer stamps of the last
- * prism_b200_model_step_timings step, [phase][CTA][2] (grid = the SM
- * count): input staged (projection phases, else 0) and phase end, so that a
- * phase's critical path (its slowest CTA) can be read.  Copies at
+ * prism_b200_model_step_timings step, [phase][CTA][4] (grid = the SM
+ * count): inputs arrived and input staged (projection phases, else 0),
+ * phase end, and a spare 0, so that a phase's critical path (its slowest
+ * CTA) can be read.  Copies at
  * most `count` values and returns how many (0 for other step modes).  No
  * counterpart in the reference. */
 int64_t prism_b200_model_phase_trace_ctas(prism_b200_model *m, uint64_t *ns, size_t count);

@@ -49,7 +49,7 @@ namespace prism {
 constexpr int kFWarps = 16;                 // compute warps
 constexpr int kFThreads = kFWarps * 32;     // compute threads (named barrier 1)
 constexpr int kFBlock = kFThreads + 32;     // + the weight-streaming warp
-constexpr int kFRing = 148 * 1024;          // weight ring
+constexpr int kFRing = 144 * 1024;          // weight ring
 constexpr int kFSlots = 64;                 // pieces in flight
 constexpr int kFMaxNb = 48;                 // input blocks per projection (12288 values)
 constexpr int kFActBytes = (kFMaxNb * (256 + 4 + 32 + 4) + 127) / 128 * 128;
@@ -57,6 +57,7 @@ constexpr int kFWorkBytes = 58 * 1024;      // staging, terms, GDN / attention s
 constexpr int kFDescBytes = 1024;
 constexpr int kFChunk = 32;                 // attention: positions per K/V chunk
 constexpr int kFMaxScores = 1024;           // attention: positions per CTA
+constexpr int kFPieceMax = 32 * 1024;       // bytes of one weight-stream piece (soft cap)
 // shared-memory layout
 constexpr int kFOffAct = kFRing;
 constexpr int kFOffWork = kFOffAct + kFActBytes;
@@ -65,7 +66,12 @@ constexpr int kFDescBufs = 4;              // descriptors prefetched kFDescBufs 
 constexpr int kFOffBars = kFOffDesc + kFDescBufs * kFDescBytes;  // ring [kFSlots], desc [4], kv [4]
 constexpr int kFOffMeta = kFOffBars + (kFSlots + 8) * 8;     // off/len [kFSlots], counters
 constexpr int kFOffRed = kFOffMeta + kFSlots * 8 + 64;       // double [16] + float [16]
-constexpr int kFSmemBytes = kFOffRed + 16 * 8 + 16 * 4 + 64;
+constexpr int kFOffRes = kFOffRed + 16 * 8 + 16 * 4 + 64;    // u64 [kFThreads] residual words
+constexpr int kFOffTab = kFOffRes + kFThreads * 8;            // batch tile table [4][16] u32
+constexpr int kFOffIssue = kFOffTab + 4 * kFWarps * 4;         // u64 [kFSlots] (traced steps)
+constexpr int kFMaxPieces = 48;                               // weight-stream pieces per phase
+constexpr int kFOffPieces = kFOffIssue + kFSlots * 8;         // count + [4][kFMaxPieces]
+constexpr int kFSmemBytes = kFOffPieces + (4 + 4 * kFMaxPieces) * 4;
 static_assert(kFSmemBytes <= 232448, "flow kernel shared memory");
 
 enum FPhaseType : int { kFEmbed = 0, kFProj = 1, kFGdn = 2, kFAttn = 3 };
@@ -77,6 +83,8 @@ struct FProj {
   int tile_start[kMaxGroup + 1];
   int ntiles;                        // tiles of the phase (the SwiGLU pair: per weight)
   int h[kMaxGroup], rows[kMaxGroup];
+  int part[kMaxGroup];               // bytes of one tile of weight g
+  int most[kMaxGroup];               // tiles per weight-stream piece of weight g
   const uint8_t *units[kMaxGroup];
   uint64_t *out[kMaxGroup];          // tagged outputs (the pair: up * silu(gate) in out[0])
   float *plain[kMaxGroup];           // optional plain binary32 copies of the outputs
@@ -143,8 +151,8 @@ struct FlowArgs {
   unsigned *sync;        // [0] finished CTAs, [1] abort word, [2] step epoch
   unsigned long long *key;  // the LM head's greedy key while the step runs
   unsigned *status;
-  unsigned long long *trace;  // optional: [8 * phase] CTA 0's globaltimer stamps
-  unsigned long long *trace_cta;  // optional: [phase][CTA][2] input staged, phase end
+  unsigned long long *trace;  // optional: [16 * phase] CTA 0's globaltimer stamps
+  unsigned long long *trace_cta;  // optional: [phase][CTA][4] inputs arrived, staged, end
 };
 
 // ---- small helpers -------------------------------------------------------------
@@ -194,6 +202,16 @@ __device__ __forceinline__ uint32_t ld_acquire_cta(const uint32_t *p) {
 }
 __device__ __forceinline__ void st_release_cta(uint32_t *p, uint32_t v) {
   asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
+}
+
+// 8-byte asynchronous copy global -> shared (not a register load, so a
+// barrier does not wait for it); completed by cp_async_wait_all().
+__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 struct FlowCtl {
@@ -304,13 +322,31 @@ __device__ __forceinline__ int flow_group(const FProj &p, int t) {
   return g;
 }
 
-// Ring bytes of tile t of a projection phase (the pair: both weights' tiles).
-template <int KIND>
-__device__ __forceinline__ uint32_t piece_bytes(const FProj &p, int t) {
-  const bool pair = p.epi == kEpiSwiglu;
-  const int g = pair ? 0 : flow_group(p, t);
-  const uint32_t part = (uint32_t)p.nb * unit_bytes(KIND, p.h[g]);
-  return pair ? 2 * part : part;
+// One piece of the weight stream: a run of consecutive tiles of one weight
+// (the pair: the same tiles of up and of gate), at most most[g] tiles
+// (about 32 KB, at least one tile, never more than a batch holds), starting
+// at tile t of this CTA's range [t, t1).  One bulk copy per weight moves it:
+// a copy's fixed cost on the SM's copy engine (about 0.1-0.2 us) makes
+// small copies the stream's limit.
+struct FPiece {
+  int g, lt, nt;     // weight, its first local tile, tiles
+  uint32_t part;     // bytes of one tile of one weight
+  uint32_t bytes;    // ring bytes (the pair: both runs)
+};
+__device__ __forceinline__ FPiece piece_at(int count, const int *tile_start, const int *part,
+                                           const int *most, bool pair, int ntiles, int t, int t1) {
+  FPiece q;
+  q.g = 0;
+  if (!pair)
+#pragma unroll
+    for (int i = 1; i < kMaxGroup; ++i)
+      if (i < count && t >= tile_start[i]) q.g = i;
+  const int end = pair ? ntiles : tile_start[q.g + 1];
+  q.lt = pair ? t : t - tile_start[q.g];
+  q.part = (uint32_t)part[q.g];
+  q.nt = min(min(t1, end) - t, most[q.g]);
+  q.bytes = (uint32_t)q.nt * q.part * (pair ? 2u : 1u);
+  return q;
 }
 
 // ---- ring state ------------------------------------------------------------------
@@ -323,7 +359,11 @@ struct FRing {
   uint32_t *tail;     // bytes released by the consumer (monotonic)
   uint32_t *released; // pieces released by the consumer
   uint32_t *issued;   // pieces issued by the producer (written at its exit)
+  uint32_t *issued_live;  // pieces issued so far (release after each issue)
+  uint32_t *desc_done;    // phases the compute warps finished (release)
+  uint32_t *desc_fetched; // descriptors the fetcher issued
   uint32_t *kvuse;    // [4] completed uses of the attention K/V barriers
+  unsigned long long *issue_ts;  // [kFSlots] issue time of each piece (traced steps)
 };
 
 // The weight-streaming warp (lane 0): every projection phase's tiles of this
@@ -339,21 +379,21 @@ __device__ void flow_producer(const FlowArgs &fa, const FRing &rg, const FlowCtl
   struct Plan {
     const uint8_t *units[kMaxGroup];
     int tile_start[kMaxGroup + 1];
-    int h[kMaxGroup];
-    int type, nb, epi, ntiles, count;
+    int part[kMaxGroup], most[kMaxGroup];
+    int type, epi, ntiles, count;
   };
   auto load_plan = [&](int p) {
     Plan q;
     const FPhase &ph = fa.phases[p];
     q.type = ph.type;
-    q.nb = ph.pr.nb;
     q.epi = ph.pr.epi;
     q.ntiles = ph.pr.ntiles;
     q.count = ph.pr.count;
 #pragma unroll
     for (int g = 0; g < kMaxGroup; ++g) {
       q.units[g] = ph.pr.units[g];
-      q.h[g] = ph.pr.h[g];
+      q.part[g] = ph.pr.part[g];
+      q.most[g] = ph.pr.most[g];
       q.tile_start[g] = ph.pr.tile_start[g];
     }
     q.tile_start[kMaxGroup] = ph.pr.tile_start[kMaxGroup];
@@ -367,15 +407,10 @@ __device__ void flow_producer(const FlowArgs &fa, const FRing &rg, const FlowCtl
     const bool pair = pr.epi == kEpiSwiglu;
     int t0, t1;
     flow_range(pr.ntiles, t0, t1);
-    for (int t = t0; t < t1 && ok; ++t) {
-      int g = 0;
-      if (!pair)
-#pragma unroll
-        for (int i = 1; i < kMaxGroup; ++i)
-          if (i < pr.count && t >= pr.tile_start[i]) g = i;
-      const int lt = pair ? t : t - pr.tile_start[g];
-      const uint32_t part = (uint32_t)pr.nb * unit_bytes(KIND, pr.h[g]);
-      const uint32_t bytes = pair ? 2 * part : part;
+    for (int t = t0; t < t1 && ok;) {
+      const FPiece q = piece_at(pr.count, pr.tile_start, pr.part, pr.most, pair, pr.ntiles, t, t1);
+      t += q.nt;
+      const uint32_t bytes = q.bytes;
       uint32_t off = head % (uint32_t)kFRing;
       const uint32_t pad = off + bytes > (uint32_t)kFRing ? (uint32_t)kFRing - off : 0u;
       // wait for room: ring bytes and a free slot
@@ -398,12 +433,15 @@ __device__ void flow_producer(const FlowArgs &fa, const FRing &rg, const FlowCtl
       const int slot = (int)(issued % kFSlots);
       rg.off[slot] = off;
       rg.len[slot] = pad + bytes;
+      const uint32_t run = (uint32_t)q.nt * q.part;
+      if (fa.trace) rg.issue_ts[slot] = global_timer_ns();
       mbar_arrive_expect_tx(&rg.bar[slot], bytes);
-      bulk_g2s(rg.data + off, pr.units[g] + (size_t)lt * part, part, &rg.bar[slot]);
+      bulk_g2s(rg.data + off, pr.units[q.g] + (size_t)q.lt * q.part, run, &rg.bar[slot]);
       if (pair)
-        bulk_g2s(rg.data + off + part, pr.units[1] + (size_t)lt * part, part, &rg.bar[slot]);
+        bulk_g2s(rg.data + off + run, pr.units[1] + (size_t)q.lt * q.part, run, &rg.bar[slot]);
       head += bytes;
       ++issued;
+      st_release_cta(rg.issued_live, issued);
     }
   }
   *rg.issued = issued;
@@ -431,6 +469,69 @@ __device__ __forceinline__ bool stage_words(const uint64_t *in, int n, uint32_t 
   return true;
 }
 
+// Q8_K of one 256-value block held 8 per lane (lane l: values 8l..8l+7),
+// stored into the SoA activation: the same bits as q8k_quantize_regs +
+// store_q8k_soa (Source rounding), with a shorter dependent chain.  The
+// block maximum, the first value of largest magnitude, comes from a warp
+// max reduction of this lane's first-largest magnitude, a ballot for the
+// first lane holding it and one shuffle of its signed value; the block code
+// sum from a warp add reduction.
+__device__ __forceinline__ unsigned q8k_block_fast(const float (&v)[8], int lane, int b,
+                                                   const MatvecSmem &L, uint8_t *act) {
+  float best = 0.0f;
+  bool finite = true;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    finite &= is_finite_f(v[i]);
+    if (fabsf(v[i]) > fabsf(best)) best = v[i];
+  }
+  const unsigned mag = __float_as_uint(fabsf(best));
+  const unsigned top = __reduce_max_sync(0xffffffffu, mag);
+  const unsigned holders = __ballot_sync(0xffffffffu, mag == top);
+  const float maximum = __shfl_sync(0xffffffffu, best, __ffs(holders) - 1);
+  finite = __all_sync(0xffffffffu, finite);
+  unsigned st = finite ? 0u : kStatusNonfinite;
+  int q[8];
+  float scale = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) q[i] = 0;
+  if (maximum != 0.0f && finite) {
+    const float iscale = __fdiv_rn(-127.0f, maximum);
+    if (!is_finite_f(iscale)) {
+      st |= kStatusInvalid;
+    } else {
+      scale = __fdiv_rn(1.0f, iscale);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float r = fminf(rintf(__fmul_rn(v[i], iscale)), 127.0f);
+        if (!(r >= -127.0f && r <= 127.0f)) {
+          st |= kStatusInvalid;
+          r = 0.0f;
+        }
+        q[i] = (int)r;
+      }
+    }
+  }
+  int own = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) own += q[i];
+  const int pair_sum = own + __shfl_xor_sync(0xffffffffu, own, 1);
+  const int total = __reduce_add_sync(0xffffffffu, own);
+  int8_t *values = reinterpret_cast<int8_t *>(act + L.act_values()) + b * 256;
+  const uint32_t w0 = (uint32_t)(uint8_t)q[0] | ((uint32_t)(uint8_t)q[1] << 8) |
+                      ((uint32_t)(uint8_t)q[2] << 16) | ((uint32_t)(uint8_t)q[3] << 24);
+  const uint32_t w1 = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) |
+                      ((uint32_t)(uint8_t)q[6] << 16) | ((uint32_t)(uint8_t)q[7] << 24);
+  reinterpret_cast<uint2 *>(values)[lane] = make_uint2(w0, w1);
+  if ((lane & 1) == 0)
+    reinterpret_cast<int16_t *>(act + L.act_sums())[b * 16 + (lane >> 1)] = (int16_t)pair_sum;
+  if (lane == 0) {
+    reinterpret_cast<float *>(act + L.act_scale())[b] = scale;
+    reinterpret_cast<int *>(act + L.act_asum())[b] = total;
+  }
+  return st;
+}
+
 // Quantize xs[0, nb*256) into the Q8_K SoA activation at act (stage_from_f32's
 // quantization, a block per warp), after RMSNorm scaling when `rms`.
 // nw0/nw1: this lane's norm weights of block `warp`, loaded ahead of time.
@@ -453,12 +554,8 @@ __device__ __forceinline__ void quantize_staged(const float *xs, int nb, float s
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], scale), w[j]);
     }
-    float qscale;
-    int8_t q[8];
-    int pair_sum;
-    const unsigned st = q8k_quantize_regs(v, lane, false, qscale, q, pair_sum);
+    const unsigned st = q8k_block_fast(v, lane, b, L, act);
     if (st && lane == 0) report(status, st);
-    store_q8k_soa(L, act, b, lane, qscale, q, pair_sum);
   }
 }
 
@@ -486,7 +583,7 @@ __device__ void flow_embed(const FEmbed &e, const StepState &st, int pos, uint32
 template <int KIND>
 __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32_t ep,
                           uint32_t tag, int &cons, const FlowCtl &c, unsigned long long *tr,
-                          unsigned long long *ts) {
+                          unsigned long long *ts, unsigned long long *trace_all) {
   int t0, t1;
   flow_range(p.ntiles, t0, t1);
   if (t0 >= t1) return true;
@@ -496,6 +593,78 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
   uint8_t *act = smem + kFOffAct;
   float *work = reinterpret_cast<float *>(smem + kFOffWork);
   double *red = reinterpret_cast<double *>(smem + kFOffRed);
+  // this CTA's pieces of the phase (the weight stream's order), laid out by
+  // one thread while the others stage the input
+  int *pl_n = reinterpret_cast<int *>(smem + kFOffPieces);
+  int *pl_nt = pl_n + 4, *pl_g = pl_nt + kFMaxPieces, *pl_lt = pl_g + kFMaxPieces;
+  uint32_t *pl_bytes = reinterpret_cast<uint32_t *>(pl_lt + kFMaxPieces);
+  // pl_n[0]: first piece of the current batch, [1] its pieces, [2] its
+  // tiles, [3] pieces in the list
+  uint32_t *tb_off_ = reinterpret_cast<uint32_t *>(smem + kFOffTab);
+  uint32_t byte_cap = 0;
+  // Plan the batch that starts at piece i0 (consumed pieces: cons) and lay
+  // out its tile table: batches are runs of whole pieces, all of them when
+  // the ring holds the phase's pieces together (they streamed during
+  // earlier phases), else runs that leave room for the next batch; at most
+  // one tile per compute warp.  Offsets are known once the stream issued the
+  // pieces; their data is awaited separately.  Last thread only.
+  auto plan = [&](int i0, int cons_at) -> bool {
+    const int n = pl_n[3];
+    int i1 = i0, ntl = 0;
+    uint32_t bb = 0;
+    while (i1 < n) {
+      const int nt = pl_nt[i1];
+      if (i1 > i0 && (ntl + nt > kFWarps || bb + pl_bytes[i1] > byte_cap)) break;
+      ntl += nt;
+      bb += pl_bytes[i1];
+      ++i1;
+    }
+    const int np = i1 - i0;
+    bool ok = true;
+    if (np) {
+      Spin sp;
+      while ((int)(ld_acquire_cta(rg.issued_live) - (uint32_t)cons_at) < np) {
+        if (!sp.again(c)) {
+          ok = false;
+          break;
+        }
+      }
+      int k = 0;
+      for (int i = 0; i < np && ok; ++i) {
+        const uint32_t base = rg.off[(cons_at + i) % kFSlots];  // past any wrap padding
+        const int nt = pl_nt[i0 + i], g = pl_g[i0 + i], lt = pl_lt[i0 + i];
+        const uint32_t part = (uint32_t)p.part[g];
+        for (int j = 0; j < nt; ++j, ++k) {
+          tb_off_[k] = base + (uint32_t)j * part;
+          tb_off_[kFWarps + k] = base + (uint32_t)(nt + j) * part;
+          reinterpret_cast<int *>(tb_off_)[2 * kFWarps + k] = g;
+          reinterpret_cast<int *>(tb_off_)[3 * kFWarps + k] = lt + j;
+        }
+      }
+    }
+    pl_n[0] = i0;
+    pl_n[1] = np;
+    pl_n[2] = ntl;
+    return ok;
+  };
+  bool plan_ok = true;
+  if (tid == kFThreads - 1) {
+    int n = 0;
+    uint32_t total = 0, maxpiece = 0;
+    for (int t = t0; t < t1 && n < kFMaxPieces; ++n) {
+      const FPiece q = piece_at(p.count, p.tile_start, p.part, p.most, pair, p.ntiles, t, t1);
+      pl_nt[n] = q.nt;
+      pl_g[n] = q.g;
+      pl_lt[n] = q.lt;
+      pl_bytes[n] = q.bytes;
+      total += q.bytes;
+      maxpiece = max(maxpiece, q.bytes);
+      t += q.nt;
+    }
+    pl_n[3] = n;
+    byte_cap = total + maxpiece <= (uint32_t)kFRing ? total : ((uint32_t)kFRing - maxpiece) / 2;
+    plan_ok = plan(0, cons);
+  }
 
   // 1. the Q8_K activation
   if (p.prologue == kFGated) {
@@ -526,6 +695,7 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
       }
     }
     if (!csync_and(ok)) return false;
+    if (ts && tid == 0) ts[0] = global_timer_ns();
     quantize_staged(y, nb, 1.0f, nullptr, false, act, c.status, float4(), float4());
   } else {
     float *xs = work;
@@ -539,6 +709,7 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
     }
     const bool ok = stage_words(p.in, n, flow_tag(ep, p.in_k), xs, rms, s, c);
     if (!csync_and(ok)) return false;
+    if (ts && tid == 0) ts[0] = global_timer_ns();
     float scale = 1.0f;
     if (rms) {
       // block_sumsq_f64: per-thread sums, warp butterfly, warps in order
@@ -551,7 +722,7 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
   }
   csync();
   if (tr) tr[1] = global_timer_ns();
-  if (ts && tid == 0) *ts = global_timer_ns();
+  if (ts && tid == 0) ts[1] = global_timer_ns();
 
   const MatvecSmem L(nb, 32, 0, nb);
   const int8_t *values = reinterpret_cast<const int8_t *>(act + L.act_values());
@@ -560,52 +731,54 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
   const int *aasum = reinterpret_cast<const int *>(act + L.act_asum());
   float *terms = work;  // [batch tiles][upt][32]
 
-  // 2. batches of this CTA's tiles: all of them when the ring holds them
-  // together (they streamed during earlier phases), otherwise batches that
-  // leave room for the next batch to stream in
-  const int mine = t1 - t0;
-  uint32_t maxpiece = 0, total = 0;
-  for (int t = t0; t < t1; ++t) {
-    const uint32_t b = piece_bytes<KIND>(p, t);
-    maxpiece = max(maxpiece, b);
-    total += b;
-  }
-  const int term_cap = (kFWorkBytes / 4) / (upt * 32);
-  int cap = total + maxpiece <= (uint32_t)kFRing
-                ? mine
-                : (int)(((uint32_t)kFRing - maxpiece) / maxpiece / 2);
-  cap = max(1, min(cap, min(term_cap, kFWarps)));  // one chain warp per tile
+  // 2. batches of whole pieces (planned by the last thread, see above)
+  uint32_t *tb_off = reinterpret_cast<uint32_t *>(smem + kFOffTab);
+  uint32_t *tb_off2 = tb_off + kFWarps;
+  int *tb_g = reinterpret_cast<int *>(tb_off2 + kFWarps);
+  int *tb_lt = tb_g + kFWarps;
   unsigned long long best = 0ull;
-  for (int k0 = 0; k0 < mine; k0 += cap) {
-    const int B = min(cap, mine - k0);
-    // the chain thread of a tile row (warp = tile in the batch, lane = row)
-    // starts its residual load now, so the load overlaps the dots
-    const int ck = warp;
-    const int ct = t0 + k0 + ck;
-    const int cg = ck < B ? (pair ? 0 : flow_group(p, ct)) : 0;
-    const int ch = p.h[cg];
-    const int corow = (pair ? ct : ct - p.tile_start[cg]) * ch + lane;
-    const bool chain = ck < B && lane < ch && corow < p.rows[cg];
-    uint64_t resw = 0;
-    const uint32_t rtag = flow_tag(ep, p.res_k);
-    if (chain && p.res && !pair) resw = ld_word(p.res + corow);
-    bool arrived = true;
-    for (int k = 0; k < B && arrived; ++k)
-      arrived = mbar_wait_bounded(&rg.bar[(cons + k) % kFSlots],
-                                  (unsigned)((cons + k) / kFSlots) & 1u, c.status);
+  bool first = true;
+  for (;;) {
+    const int np = pl_n[1], ntl = pl_n[2];
+    if (np == 0) break;
+    // the batch's pieces have landed: one thread waits, the vote tells the rest
+    bool arrived = plan_ok;
+    unsigned long long *tw = trace_all && first ? trace_all : nullptr;  // CTA 0, thread 511
+    if (tid == kFThreads - 1) {
+      if (tw) tw[8] = global_timer_ns();
+      for (int i = 0; i < np && arrived; ++i) {
+        const int slot = (cons + i) % kFSlots;
+        arrived = mbar_wait_bounded(&rg.bar[slot], (unsigned)((cons + i) / kFSlots) & 1u, c.status);
+      }
+      if (tw) {
+        tw[9] = global_timer_ns();
+        tw[11] = rg.issue_ts[(cons + np - 1) % kFSlots];
+        tw[12] = np;
+      }
+    }
     if (!csync_and(arrived)) {
       if (tid == 0) flow_raise(c);
       return false;
     }
-    if (tr && k0 == 0) tr[2] = global_timer_ns();
-    const int tot = B * upt;
+    if (tr && first) tr[2] = global_timer_ns();
+    // the chain thread of a tile row (warp = tile in the batch, lane = row);
+    // its residual row comes by an asynchronous copy during the dots (a
+    // register load in flight would hold the barriers until it returns)
+    const int ck = warp;
+    const int cg = ck < ntl ? tb_g[ck] : 0;
+    const int ch = p.h[cg];
+    const int corow = (ck < ntl ? tb_lt[ck] : 0) * ch + lane;
+    const bool chain = ck < ntl && lane < ch && corow < p.rows[cg];
+    uint64_t *resw_s = reinterpret_cast<uint64_t *>(smem + kFOffRes) + tid;
+    const uint32_t rtag = flow_tag(ep, p.res_k);
+    if (chain && p.res && !pair) cp_async8(resw_s, p.res + corow);
+    const int tot = ntl * upt;
     for (int u = warp; u < tot; u += kFWarps) {
       const int k = u / upt, j = u - k * upt;
-      const int t = t0 + k0 + k;
-      const int g = pair ? 0 : flow_group(p, t);
-      const int H = p.h[g];
-      const uint8_t *ud = rg.data + rg.off[(cons + k) % kFSlots] + j * unit_bytes(KIND, H);
-      const int b = pair && j >= nb ? j - nb : j;
+      const int H = p.h[tb_g[k]];
+      const bool second = pair && j >= nb;
+      const int b = second ? j - nb : j;
+      const uint8_t *ud = rg.data + (second ? tb_off2[k] : tb_off[k]) + b * unit_bytes(KIND, H);
       float *out = terms + (k * upt + j) * 32;
       int dot, dot2;
       float term;
@@ -621,15 +794,18 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
       if (lane < H) out[lane] = term;
     }
     csync();
-    if (tr && k0 == 0) tr[3] = global_timer_ns();
+    if (tr && first) tr[3] = global_timer_ns();
     if (tid == 0) {
       // the batch's ring space is free again
       uint32_t rel = 0;
-      for (int k = 0; k < B; ++k) rel += rg.len[(cons + k) % kFSlots];
+      for (int i = 0; i < np; ++i) rel += rg.len[(cons + i) % kFSlots];
       st_release_cta(rg.tail, *rg.tail + rel);
-      st_release_cta(rg.released, (uint32_t)(cons + B));
+      st_release_cta(rg.released, (uint32_t)(cons + np));
     }
-    cons += B;
+    cons += np;
+    // the next batch is planned while the chains run (its table is free:
+    // every thread read this batch's entries before the barrier above)
+    if (tid == kFThreads - 1) plan_ok = plan(pl_n[0] + np, cons);
     bool ok = true;
     if (chain) {
       const float *tk = terms + ck * upt * 32;
@@ -646,6 +822,8 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
         if (p.plain[0]) p.plain[0][r] = hv;
       } else {
         if (p.res) {
+          cp_async_wait_all();
+          uint64_t resw = *resw_s;
           if (!has_tag(resw, rtag)) ok = wait_word(p.res + r, rtag, resw, c);
           sum = __fadd_rn(word_value(resw), sum);
         }
@@ -658,9 +836,10 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
         }
       }
     }
-    // the terms buffer is reused by the next batch
+    // the terms buffer is reused by the next batch; the plan is published
     if (!csync_and(ok)) return false;
-    if (tr && k0 == 0) tr[4] = global_timer_ns();
+    if (tr && first) tr[4] = global_timer_ns();
+    first = false;
   }
   if (p.epi == kEpiArgmax) {
 #pragma unroll
@@ -1076,10 +1255,14 @@ __global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
   rg.tail = rg.len + kFSlots;
   rg.released = rg.tail + 1;
   rg.issued = rg.tail + 2;
+  rg.issued_live = rg.tail + 3;
   rg.kvuse = rg.tail + 4;
+  rg.desc_done = rg.tail + 8;
+  rg.desc_fetched = rg.tail + 9;
+  rg.issue_ts = reinterpret_cast<unsigned long long *>(smem + kFOffIssue);
   const int tid = threadIdx.x;
   if (tid < kFSlots + kFDescBufs + 4) mbar_init(&rg.bar[tid], 1);
-  if (tid < 8) rg.tail[tid] = 0u;
+  if (tid < 16) rg.tail[tid] = 0u;
   mbar_init_fence();
   __syncthreads();
   FlowCtl c;
@@ -1088,43 +1271,48 @@ __global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
   const int pos = *fa.st.position;
   const uint32_t ep = fa.sync[2];
   bool ok = true;
+  constexpr int D = kFDescBufs;
   if (tid >= kFThreads) {
-    // the weight-streaming warp
-    if (tid == kFThreads) flow_producer<KIND>(fa, rg, c);
+    if (tid == kFThreads) {
+      // lane 0 of the streaming warp: the weight stream
+      flow_producer<KIND>(fa, rg, c);
+    } else if (tid == kFThreads + 1) {
+      // lane 1: phase descriptors into D buffers; descriptor q goes into
+      // buffer q % D once the compute warps finished phase q - D
+      Spin sp;
+      for (int q = 0; q < fa.nphases; ++q) {
+        bool room = true;
+        while (q >= D && (int)ld_acquire_cta(rg.desc_done) < q - D + 1) {
+          if (!sp.again(c)) {
+            room = false;
+            break;
+          }
+          __nanosleep(32);
+        }
+        if (!room) break;
+        fence_proxy_async_smem();  // the buffer was read through the generic proxy
+        mbar_arrive_expect_tx(&dbar[q % D], (unsigned)sizeof(FPhase));
+        bulk_g2s(smem + kFOffDesc + (q % D) * kFDescBytes, fa.phases + q, (unsigned)sizeof(FPhase),
+                 &dbar[q % D]);
+        st_release_cta(rg.desc_fetched, (uint32_t)(q + 1));
+      }
+    }
   } else {
-    // the compute warps: descriptor p arrives in buffer p & 1 by a bulk copy
-    // issued at the start of phase p - 1
-    // the compute warps: descriptor p arrives in buffer p % kFDescBufs by a
-    // bulk copy issued kFDescBufs - 1 phases earlier (its copy queues behind
-    // the weight stream's, so it is issued well ahead)
-    constexpr int D = kFDescBufs;
-    auto fetch = [&](int p) {
-      uint8_t *dst = smem + kFOffDesc + (p % D) * kFDescBytes;
-      mbar_arrive_expect_tx(&dbar[p % D], (unsigned)sizeof(FPhase));
-      bulk_g2s(dst, fa.phases + p, (unsigned)sizeof(FPhase), &dbar[p % D]);
-    };
-    int fetched = min(D - 1, fa.nphases);
-    if (tid == 0)
-      for (int p = 0; p < fetched; ++p) fetch(p);
+    // the compute warps: descriptor p arrives in buffer p % D
     int cons = 0, waited = 0;
     for (int p = 0; p < fa.nphases && ok; ++p) {
-      ok = csync_and(mbar_wait_bounded(&dbar[p % D], (unsigned)(p / D) & 1u, c.status));
+      unsigned long long *tr = fa.trace && blockIdx.x == 0 && tid == 0 ? fa.trace + 16 * p : nullptr;
+      if (tr) tr[5] = global_timer_ns();
+      ok = csync_and(tid != kFThreads - 1 ||
+                     mbar_wait_bounded(&dbar[p % D], (unsigned)(p / D) & 1u, c.status));
+      if (tr) tr[0] = global_timer_ns();
       if (!ok) {
         if (tid == 0) flow_raise(c);
         break;
       }
       waited = p + 1;
-      if (fetched < fa.nphases) {
-        // buffer fetched % D was read in phase p - 1, which every thread left
-        if (tid == 0) {
-          fence_proxy_async_smem();
-          fetch(fetched);
-        }
-        ++fetched;
-      }
       const FPhase &ph = *reinterpret_cast<const FPhase *>(smem + kFOffDesc + (p % D) * kFDescBytes);
-      unsigned long long *tr = fa.trace && blockIdx.x == 0 && tid == 0 ? fa.trace + 8 * p : nullptr;
-      if (tr) tr[0] = global_timer_ns();
+      if (tr) tr[6] = global_timer_ns();
       const uint32_t tag = flow_tag(ep, ph.k);
       switch (ph.type) {
         case kFEmbed:
@@ -1132,8 +1320,9 @@ __global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
           break;
         case kFProj:
           ok = flow_proj<KIND>(ph.pr, rg, smem, ep, tag, cons, c, tr,
-                               fa.trace_cta ? fa.trace_cta + ((size_t)p * gridDim.x + blockIdx.x) * 2
-                                            : nullptr);
+                               fa.trace_cta ? fa.trace_cta + ((size_t)p * gridDim.x + blockIdx.x) * 4
+                                            : nullptr,
+                               fa.trace && blockIdx.x == 0 ? fa.trace + 16 * p : nullptr);
           break;
         case kFGdn:
           ok = flow_gdn(ph.gd, pos, smem, ep, tag, c);
@@ -1143,17 +1332,21 @@ __global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
           break;
       }
       ok = csync_and(ok);
+      if (tid == 0) st_release_cta(rg.desc_done, (uint32_t)(p + 1));  // buffer p % D is free
       if (tr) tr[7] = global_timer_ns();
       if (fa.trace_cta && tid == 0)
-        fa.trace_cta[((size_t)p * gridDim.x + blockIdx.x) * 2 + 1] = global_timer_ns();
+        fa.trace_cta[((size_t)p * gridDim.x + blockIdx.x) * 4 + 2] = global_timer_ns();
     }
-    if (!ok && tid == 0) {
-      // aborted: descriptor copies may still be in flight
-      for (int q = waited; q < fetched; ++q)
-        mbar_wait_bounded(&dbar[q % D], (unsigned)(q / D) & 1u, c.status);
-    }
+    if (!ok && tid == 0) st_release_cta(rg.tail + 10, (uint32_t)waited);
   }
+  cp_async_wait_all();  // an aborted phase may leave a residual copy in flight
   __syncthreads();
+  if (tid == 0 && !ok) {
+    // aborted: descriptor copies may still be in flight
+    const uint32_t fetched = *rg.desc_fetched, waited = rg.tail[10];
+    for (uint32_t q = waited; q < fetched; ++q)
+      mbar_wait_bounded(&dbar[q % D], (q / D) & 1u, c.status);
+  }
   if (tid == 0) {
     // every piece the producer issued was consumed, or is drained here
     const uint32_t issued = *rg.issued, released = *rg.released;

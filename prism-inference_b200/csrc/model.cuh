@@ -691,6 +691,16 @@ inline std::vector<FPhase> build_flow_phases(prism_b200_model *m) {
     }
     for (int g = pr.count; g < kMaxGroup; ++g) pr.tile_start[g + 1] = pr.tile_start[pr.count];
     pr.ntiles = epi == kEpiSwiglu ? ws.begin()->first->ntiles : pr.tile_start[pr.count];
+    // weight-stream pieces: runs of about kFPieceMax bytes, one tile at
+    // least, no more tiles than a batch holds (a warp per tile; terms fit)
+    const bool pair = epi == kEpiSwiglu;
+    const int upt = pair ? 2 * nb : nb;
+    const int tiles = std::min(kFWarps, (kFWorkBytes / 4) / (upt * 32));
+    for (int g = 0; g < pr.count; ++g) {
+      pr.part[g] = nb * unit_bytes((int)c.weight_kind, pr.h[g]);
+      const int per = pair ? 2 * pr.part[g] : pr.part[g];
+      pr.most[g] = std::max(1, std::min(tiles, kFPieceMax / per));
+    }
     return ph;
   };
   int k_hidden = 0;
@@ -830,8 +840,9 @@ inline bool flow_eligible(prism_b200_model *m, const std::vector<FPhase> &P) {
                          (pr.epi == kEpiSwiglu ? 2 : 1);
       if (piece > kFRing / 3) return false;
     }
-    // one tile's terms must fit the work area
+    // one tile's terms must fit the work area; a CTA's pieces fit its list
     if ((pr.epi == kEpiSwiglu ? 2 : 1) * pr.nb * 32 * 4 > kFWorkBytes) return false;
+    if ((pr.ntiles + sms - 1) / sms + pr.count > kFMaxPieces) return false;
   }
   int blocks = 0;
   void *k = c.weight_kind == 35 ? (void *)decode_flow_kernel<35> : (void *)decode_flow_kernel<10>;
@@ -852,9 +863,9 @@ inline cudaError_t prepare_flow(prism_b200_model *m) {
   if (!m->d_fphases) {
     // a model's layer count, and so its phase count, is fixed at creation
     cudaError_t e = model_alloc(m, &m->d_fphases, P.size());
-    if (e == cudaSuccess) e = model_alloc(m, &m->d_ftrace, 8 * P.size());
+    if (e == cudaSuccess) e = model_alloc(m, &m->d_ftrace, 16 * P.size());
     if (e == cudaSuccess)
-      e = model_alloc(m, &m->d_ftrace_cta, (size_t)2 * m->ex->num_sms * P.size());
+      e = model_alloc(m, &m->d_ftrace_cta, (size_t)4 * m->ex->num_sms * P.size());
     if (e != cudaSuccess) return e;
   }
   m->nfphases = (int)P.size();
@@ -1246,7 +1257,7 @@ int prism_b200_model_persistent(const prism_b200_model *m) {
 int64_t prism_b200_model_phase_trace_ctas(prism_b200_model *m, uint64_t *ns, size_t count) {
   if (!m || !ns) return -PRISM_B200_E_INVALID;
   if (!m->flow) return 0;
-  const size_t n = std::min(count, (size_t)2 * m->ex->num_sms * m->nfphases);
+  const size_t n = std::min(count, (size_t)4 * m->ex->num_sms * m->nfphases);
   if (cudaMemcpy(ns, m->d_ftrace_cta, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
     return -PRISM_B200_E_DEVICE;
   return (int64_t)n;
@@ -1259,7 +1270,7 @@ int prism_b200_model_step_mode(const prism_b200_model *m) {
 int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t count) {
   if (!m || !ns) return -PRISM_B200_E_INVALID;
   if (m->flow) {
-    const size_t n = std::min(count, (size_t)8 * m->nfphases);
+    const size_t n = std::min(count, (size_t)16 * m->nfphases);
     if (cudaMemcpy(ns, m->d_ftrace, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
       return -PRISM_B200_E_DEVICE;
     return (int64_t)n;
@@ -1413,14 +1424,14 @@ int prism_b200_model_step_timings(prism_b200_model *m, float *attention_ms, floa
   if (m->flow) {
     // one traced dataflow step: CTA 0's phase ends (each phase's input wait
     // counted in the phase)
-    std::vector<unsigned long long> t((size_t)8 * m->nfphases);
+    std::vector<unsigned long long> t((size_t)16 * m->nfphases);
     cudaError_t e = cudaMemsetAsync(m->d_ftrace, 0, t.size() * 8, m->stream);
     if (e == cudaSuccess) e = prism::launch_flow(m, true, true);
     if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
     if (e == cudaSuccess)
       e = cudaMemcpy(t.data(), m->d_ftrace, t.size() * 8, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return cuda_fail(ex, e, "traced step");
-    auto end = [&](int q) { return t[(size_t)8 * q + 7]; };
+    auto end = [&](int q) { return t[(size_t)16 * q + 7]; };
     auto ms = [](unsigned long long a, unsigned long long b) {
       return (float)((double)(b - a) * 1e-6);
     };

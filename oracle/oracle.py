@@ -220,6 +220,13 @@ def _model_lib():
             ("po_rope_frequencies", None, [vp, i32, vp]),
             ("po_qwen35_load_state", i32, [vp, i32, i32, vp, ctypes.c_size_t]),
             ("po_qwen35_set_position", i32, [vp, ctypes.c_int32]),
+            ("po_pinned_gdn_dot", ctypes.c_float, [vp, vp, ctypes.c_size_t]),
+            ("po_pinned_gdn_add_scaled", i32, [vp, vp, ctypes.c_float, ctypes.c_size_t]),
+            ("po_pinned_attention_dot", i32, [vp, vp, ctypes.c_size_t, vp]),
+            ("po_vector_exp", ctypes.c_float, [ctypes.c_float]),
+            ("po_pinned_softmax", i32, [vp, ctypes.c_size_t, i32]),
+            ("po_pinned_rope", i32, [vp, ctypes.c_size_t, i32, i32, vp, i32]),
+            ("po_source_rope", i32, [vp, ctypes.c_size_t, i32, i32, vp]),
             ("po_synth_weights", i32, [ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint64,
                                        ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float,
                                        ctypes.c_float, vp]),
@@ -333,6 +340,52 @@ def synth_weights(kind, rows, cols, seed, stream=0, scale_lo=0.01, scale_hi=0.05
     _check(_model_lib().po_synth_weights(kind, rows, cols, seed, stream, scale_lo, scale_hi,
                                          _p(out)))
     return out
+
+
+# ---- pinned (Swift) variants, for the reference's native captures ----------
+
+def _f32(a):
+    return np.ascontiguousarray(a, np.float32)
+
+
+def pinned_gdn_dot(a, b):
+    a, b = _f32(a), _f32(b)
+    return np.float32(_model_lib().po_pinned_gdn_dot(_p(a), _p(b), a.size))
+
+
+def pinned_gdn_add_scaled(target, inp, scale):
+    t, x = _f32(target).copy(), _f32(inp)
+    _check(_model_lib().po_pinned_gdn_add_scaled(_p(t), _p(x), float(scale), t.size))
+    return t
+
+
+def pinned_attention_dot(values, weights):
+    v, w = _f32(values), _f32(weights)
+    out = np.zeros(1, np.float32)
+    _check(_model_lib().po_pinned_attention_dot(_p(v), _p(w), w.size, _p(out)))
+    return out[0]
+
+
+def vector_exp(x):
+    return np.float32(_model_lib().po_vector_exp(float(np.float32(x))))
+
+
+def pinned_softmax(scores, round_f16=False):
+    s = _f32(scores).copy()
+    _check(_model_lib().po_pinned_softmax(_p(s), s.size, int(round_f16)))
+    return s
+
+
+def pinned_rope(x, cos_sin, head=256, rotary=64, in_place=False):
+    v, cs = _f32(x).copy(), _f32(cos_sin)
+    _check(_model_lib().po_pinned_rope(_p(v), v.size, head, rotary, _p(cs), int(in_place)))
+    return v
+
+
+def source_rope(x, cos_sin, head=256, rotary=64):
+    v, cs = _f32(x).copy(), _f32(cos_sin)
+    _check(_model_lib().po_source_rope(_p(v), v.size, head, rotary, _p(cs)))
+    return v
 
 
 def greedy(logits):

@@ -47,6 +47,18 @@ typedef struct po_q8_0_block {
   int8_t values[32];
 } po_q8_0_block;
 
+/* ---- pinned (Swift) arithmetic variants (pinned_oracle.c) ------------- */
+/* The reference's PinnedSwift GDN dot / scaled update, attention dot,
+ * vector exponential, softmax and RoPE, for checking its native captures. */
+float po_pinned_gdn_dot(const float *a, const float *b, size_t n);
+int po_pinned_gdn_add_scaled(float *target, const float *input, float scale, size_t n);
+int po_pinned_attention_dot(const float *values, const float *weights, size_t n, float *out);
+float po_vector_exp(float value);
+int po_pinned_softmax(float *scores, size_t n, int round_f16);
+/* x: n values, heads of `head`; cos_sin: rotary/2 (cos, sin) pairs. */
+int po_pinned_rope(float *x, size_t n, int head, int rotary, const float *cos_sin, int in_place);
+int po_source_rope(float *x, size_t n, int head, int rotary, const float *cos_sin);
+
 /* ---- seeded synthetic weights (synth_inputs.c) ------------------------ */
 /* rows x cols/256 packed blocks of kind 35 (TQ2_0) or 10 (Q2_K) in the
  * reference byte layout, the same bytes as the product library's seeded

@@ -13,6 +13,16 @@ library serves plus the Q8_K rounding control:
 * ``tests/fixtures/upstream-kquants.json``  -> ``q2_k.json``   (TypeId 10)
 * ``tests/fixtures/swift-q8k-parity.{json,bin}`` -> ``q8k_parity.json``
 
+and the native captures that pin the reference's pinned (Swift) GDN,
+attention and RoPE arithmetic, into ``pinned.json``:
+
+* ``swift-gdn-parity.{json,bin}``   GDN dot and row-update cases
+* ``swift-attention-dot.json``      attention dots and one weighted value
+* ``swift-attention-softmax.json``  masked softmax rows
+* ``swift-attention-rope.json`` + ``swift-rope-basis.json``
+                                    out-of-place RoPE with native cos/sin
+* ``swift-rope-inplace.{json,bin}`` in-place RoPE and one binary16 boundary
+
 Field meaning (hex strings are little-endian byte dumps):
   OutputHex      packed weight blocks
   InputHex       the f32 row the weights were quantized from (optional)
@@ -73,11 +83,81 @@ def main(ref_root):
             for i, c in enumerate(q8k_meta["cases"])
         ],
     }
-    for name, obj in (("tq2_0.json", tq), ("q2_k.json", kq), ("q8k_parity.json", q8k)):
+    pinned = pinned_fixtures(fixtures)
+    for name, obj in (("tq2_0.json", tq), ("q2_k.json", kq), ("q8k_parity.json", q8k),
+                      ("pinned.json", pinned)):
         with open(os.path.join(HERE, name), "w") as f:
             json.dump(obj, f, indent=1)
             f.write("\n")
-        print("wrote", name, len(obj["cases"]), "cases")
+        print("wrote", name, len(obj.get("cases", obj)), "records")
+
+
+def pinned_fixtures(fx):
+    """The pinned-arithmetic captures, as plain u32 bit lists."""
+    import struct
+
+    def words(buf, off, n):
+        return list(struct.unpack_from("<%dI" % n, buf, off)), off + 4 * n
+
+    out = {"source": "reference tests/fixtures swift-* native captures (ggml-cpu sha256 "
+                     "701b354a38b25e5c6dc57a1559f71cd26b2d0f8d69c1576a0e77a59a4273d2ab)"}
+    # GDN: PGDN001\0, u32 dots, u32 rows; dot: width, native, x[w], y[w];
+    # row: width, v, native out, q[w], k[w], state[w], native updated state[w]
+    with open(os.path.join(fx, "swift-gdn-parity.bin"), "rb") as f:
+        b = f.read()
+    assert b[:8] == b"PGDN001\0"
+    (nd, nr), off = words(b, 8, 2)
+    dots, rows = [], []
+    for _ in range(nd):
+        (w, native), off = words(b, off, 2)
+        x, off = words(b, off, w)
+        y, off = words(b, off, w)
+        dots.append({"native": native, "x": x, "y": y})
+    for _ in range(nr):
+        (w, v, native), off = words(b, off, 3)
+        q, off = words(b, off, w)
+        k, off = words(b, off, w)
+        st, off = words(b, off, w)
+        upd, off = words(b, off, w)
+        rows.append({"v": v, "native_out": native, "q": q, "k": k, "state": st,
+                     "native_state": upd})
+    assert off == len(b)
+    out["gdn"] = {"dots": dots, "rows": rows}
+    with open(os.path.join(fx, "swift-attention-dot.json")) as f:
+        d = json.load(f)
+    out["attention_dot"] = {
+        "cases": [{"name": c["name"], "first": c["first_bits"], "second": c["second_bits"],
+                   "native": c["native_bits"]} for c in d["cases"]],
+        "weighted_value": d["weighted_value"]}
+    with open(os.path.join(fx, "swift-attention-softmax.json")) as f:
+        d = json.load(f)
+    out["softmax"] = [{"input": c["input_bits"], "native": c["native_bits"]} for c in d["cases"]]
+    with open(os.path.join(fx, "swift-attention-rope.json")) as f:
+        d = json.load(f)
+    with open(os.path.join(fx, "swift-rope-basis.json")) as f:
+        basis = json.load(f)
+    rope = {"head": d["head"], "rotary": d["rotary_dimensions"], "input": d["input_bits"],
+            "cases": []}
+    for c, k in zip(d["cases"], basis["cases"]):
+        assert c["position"] == k["position"]
+        rope["cases"].append({"position": c["position"], "cos": k["cosine_bits"],
+                              "sin": k["sine_bits"], "native_out_of_place": c["native_bits"]})
+    with open(os.path.join(fx, "swift-rope-inplace.bin"), "rb") as f:
+        b = f.read()
+    assert b[:8] == b"SWROPIP1"
+    (n,), off = words(b, 8, 1)
+    for i in range(n):
+        (pos,), off = words(b, off, 1)
+        nat, off = words(b, off, 64)
+        assert pos == rope["cases"][i]["position"]
+        rope["cases"][i]["native_in_place_first64"] = nat
+    bw, off = words(b, off, 11)
+    assert off == len(b)
+    rope["boundary"] = dict(zip(["position", "pair", "first", "second", "cos", "sin",
+                                 "in_place_0", "in_place_1", "out_of_place_0",
+                                 "out_of_place_1", "half_words"], bw))
+    out["rope"] = rope
+    return out
 
 
 if __name__ == "__main__":

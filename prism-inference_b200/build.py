@@ -14,7 +14,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libprism_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
-SOURCES = ["prism_b200.cu", "synth.cu"]
+SOURCES = ["prism_b200.cu", "synth.cu", "static_scratch.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
          "-Xcompiler", "-Wall", "--expt-relaxed-constexpr", "-fmad=false"]
@@ -44,7 +44,6 @@ def build(force=False, verbose=False):
     if not force and up_to_date():
         return LIB
     cmd = [NVCC] + ARCH + FLAGS + ["-I", os.path.join(ROOT, "include"), "-o", LIB] + sources()
-    cmd += ["-lcuda"] if False else []
     if verbose:
         cmd += ["-Xptxas", "-v"]
         print(" ".join(cmd))

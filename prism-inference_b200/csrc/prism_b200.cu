@@ -556,40 +556,16 @@ extern "C" int prism_b200_gdn_prefill_device(prism_b200_executor *ex, int batch,
 // pages has none left to give, and a decode loop with a latency budget
 // cannot absorb the device-wide synchronisation that cudaMalloc implies.
 // This variant of prism_b200_gdn_prefill_device keeps its chunk scratch in
-// a fixed module-scope array instead of the executor's growable buffer.  The
-// prep kernel writes every scratch element that the scan kernel reads, so
-// nothing has to start at zero.  The array is shared by every caller on a
-// device: two calls whose kernels overlap in time (different streams, or
-// different executors on one device) race on it.
-namespace {
-
-constexpr size_t kStaticGdnScratchFloats = (size_t)PRISM_B200_GDN_STATIC_SCRATCH_BYTES / 4;
-static_assert(PRISM_B200_GDN_STATIC_SCRATCH_BYTES % 256 == 0, "scratch size");
-
-__device__ __align__(256) float g_static_gdn_scratch[kStaticGdnScratchFloats];
-
-constexpr int kMaxDevices = 64;
-std::mutex g_static_gdn_mu;
-float *g_static_gdn_ptr[kMaxDevices] = {};
-
-// Device address of the array on `device`, looked up on the first call for
-// that device (with the device current) and cached; null on failure.
-float *static_gdn_scratch(int device, cudaError_t *err) {
-  *err = cudaSuccess;
-  if (device < 0 || device >= kMaxDevices) {
-    *err = cudaErrorInvalidDevice;
-    return nullptr;
-  }
-  std::lock_guard<std::mutex> lock(g_static_gdn_mu);
-  if (!g_static_gdn_ptr[device]) {
-    void *ptr = nullptr;
-    *err = cudaGetSymbolAddress(&ptr, g_static_gdn_scratch);
-    if (*err != cudaSuccess) return nullptr;
-    g_static_gdn_ptr[device] = static_cast<float *>(ptr);
-  }
-  return g_static_gdn_ptr[device];
+// a fixed module-scope array (static_scratch.cu) instead of the executor's
+// growable buffer.  The prep kernel writes every scratch element that the
+// scan kernel reads, so nothing has to start at zero.  The array is shared
+// by every caller on a device: two calls whose kernels overlap in time
+// (different streams, or different executors on one device) race on it.
+namespace prism_b200_internal {
+float *static_gdn_scratch(int device, cudaError_t *err);
 }
-
+namespace {
+constexpr size_t kStaticGdnScratchFloats = (size_t)PRISM_B200_GDN_STATIC_SCRATCH_BYTES / 4;
 }  // namespace
 
 extern "C" int prism_b200_gdn_prefill_device_noalloc(prism_b200_executor *ex, int batch,
@@ -615,7 +591,7 @@ extern "C" int prism_b200_gdn_prefill_device_noalloc(prism_b200_executor *ex, in
                     (size_t)PRISM_B200_GDN_STATIC_SCRATCH_BYTES);
   CK(cudaSetDevice(ex->device), "select device");
   cudaError_t e;
-  float *scratch = static_gdn_scratch(ex->device, &e);
+  float *scratch = prism_b200_internal::static_gdn_scratch(ex->device, &e);
   if (!scratch) return cuda_fail(ex, e, "GDN fixed scratch address");
   GdnPrefillArgs p;
   p.g.batch = batch;

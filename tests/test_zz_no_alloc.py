@@ -3,8 +3,9 @@
 prism_b200_gdn_prefill_device_noalloc must give what
 prism_b200_gdn_prefill_device gives on the same inputs (within the chunkwise
 bound 1e-3 + 1e-3*|ref| used for the prefill tests), on consecutive calls
-that reuse its fixed scratch, and must refuse a call whose scratch would not
-fit before anything is enqueued.  The file name sorts last so that the test
+that reuse its fixed scratch, must refuse a call whose scratch would not fit
+before anything is enqueued, and must leave a fresh executor's device free
+memory unchanged.  The file name sorts last so that the test
 also runs after every other test in one process.
 """
 import numpy as np
@@ -99,3 +100,38 @@ def test_largest_fitting_call_and_refusal_beyond(ex):
     o_ref = run(ex, pb.gdn_prefill_device, 2, 100, 4, 4, 64, s_ref, ins)
     o_fix = run(ex, pb.gdn_prefill_device_noalloc, 2, 100, 4, 4, 64, s_fix, ins)
     assert close(o_fix, o_ref) and close(s_fix, s_ref)
+
+
+def test_fresh_executor_allocates_no_device_memory(ex):
+    """On a fresh executor the no-allocation prefill leaves the device's free
+    memory unchanged, while the allocating entry point on the same executor
+    then grows its scratch by at least the same chunk scratch -- the control
+    showing that the measure sees an allocation of this size."""
+    heads, T = 1008, 64                      # the largest fitting call
+    ins = inputs(1, T, heads, 1, 31)
+    state = torch.zeros((1, heads, D, D), device="cuda")
+    out = torch.zeros((1, T, heads, D), device="cuda")
+    q, k, v, decay, beta = ins
+
+    def call(e, fn):
+        fn(e, 1, T, heads, 1, 64, state.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+           decay.data_ptr(), beta.data_ptr(), out.data_ptr())
+        e.sync()
+        torch.cuda.synchronize()
+
+    # the module holding the fixed scratch and both kernels are loaded on
+    # this device by a first call from another executor
+    call(ex, pb.gdn_prefill_device_noalloc)
+    fresh = pb.ProjectionExecutor(0)
+    try:
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        call(fresh, pb.gdn_prefill_device_noalloc)
+        call(fresh, pb.gdn_prefill_device_noalloc)
+        free1 = torch.cuda.mem_get_info()[0]
+        assert free1 == free0, free0 - free1
+        call(fresh, pb.gdn_prefill_device)
+        free2 = torch.cuda.mem_get_info()[0]
+        assert free1 - free2 >= heads * CHUNK_SCRATCH_BYTES, free1 - free2
+    finally:
+        fresh.close()

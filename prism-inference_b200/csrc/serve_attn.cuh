@@ -50,9 +50,14 @@ struct ServeArgs {
   int context;  // positions per (sequence, KV head) in the cache
 };
 
+// Scores held per CTA: the largest page-aligned share of the cached
+// positions, ceil(pos / (kServeSplit * kServePage)) * kServePage for
+// pos < context.
 __host__ __device__ constexpr int serve_cap(int context) {
-  return (context + kServeSplit - 1) / kServeSplit + 1;
+  return (context + kServeSplit * kServePage - 1) / (kServeSplit * kServePage) * kServePage;
 }
+static_assert(serve_cap(4224) == 544 && serve_cap(8192) == 1024 && serve_cap(64) == 32,
+              "serve_cap covers the page-aligned shares");
 
 // Shared memory: q[G][hd], kc, vc, buf [hd], cs[64], scores[G][cap],
 // qr[G][4][hd/4] (q regrouped by dimension residue mod 4) (f32); two chunk

@@ -373,6 +373,37 @@ def run_decode(args):
 
     peak, peak_src = peaks()
     achieved_ffn = ffn_bytes / (ffn_ms / 1e3) / 1e9
+    flow = model.step_mode == 2
+    step_gbs = bytes_per_token / (ms_per_token / 1e3) / 1e9
+    if flow:
+        # one kernel is the whole step: its roofline is the step's
+        roofline = {
+            "bound": "hbm", "achieved": step_gbs, "peak": peak, "unit": "GB/s",
+            "frac": step_gbs / peak, "peak_source": peak_src,
+            "kernel": "decode_flow_kernel<35>: the whole decode step as one cooperative "
+                      "launch (weights, recurrent and convolution state, KV rows of the "
+                      "context), event-timed over the decode steps",
+            "algorithmic_bytes_per_launch": bytes_per_token,
+            "traffic": traffic_from_profiles("decode_flow_kernel"),
+            "traffic_source": TRAFFIC_SOURCE,
+            "step": {"achieved": step_gbs, "frac": step_gbs / peak,
+                     "bytes_per_token": bytes_per_token},
+            "ffn_phase_pair": {"achieved": achieved_ffn, "frac": achieved_ffn / peak,
+                               "bytes": ffn_bytes,
+                               "note": "the FFN up+gate and down phases of one layer, median "
+                                       "over layers, from the traced step's phase times"}}
+    else:
+        roofline = {
+            "bound": "hbm", "achieved": achieved_ffn, "peak": peak, "unit": "GB/s",
+            "frac": achieved_ffn / peak, "peak_source": peak_src,
+            "kernel": "FFN of one layer: matvec_kernel<35,kEpiSwiglu> (up+gate) + "
+                      "matvec_kernel<35,kEpiStore> (down), median over layers, event-timed "
+                      "without PDL",
+            "algorithmic_bytes_per_launch": ffn_bytes,
+            "traffic": traffic_from_profiles("ffn_layer"),
+            "traffic_source": TRAFFIC_SOURCE,
+            "step": {"achieved": step_gbs, "frac": step_gbs / peak,
+                     "bytes_per_token": bytes_per_token}}
     line = {
         "metric": DECODE_METRIC, "value": tps, "unit": "tok/s", "n_gpus": world,
         "steps": K, "warmup": W, "ms_per_step": decode_ms / K, "higher_is_better": True,
@@ -386,26 +417,18 @@ def run_decode(args):
             "prompt": PROMPT, "decode_steps": K,
             "l2": "every step streams %.3f GB of weights and state (> 126 MB L2)"
                   % (bytes_per_token / 1e9),
-            "graph": "one CUDA graph per step, programmatic dependent launch between kernels",
+            "graph": ("one CUDA graph per step holding one cooperative kernel: the dataflow "
+                      "step (phases hand tagged activations to each other through global "
+                      "memory, no grid barrier)") if flow else
+                     "one CUDA graph per step, programmatic dependent launch between kernels",
+            "step_mode": "flow" if flow else "sequence",
         },
         "clocks": clk.summary(),
-        "gpu_launches": K * (3 + 5 * cfg.layers),
+        "gpu_launches": K if flow else K * (3 + 5 * cfg.layers),
         "e2e": {"value": e2e_tps, "unit": "tok/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 12,
                 "api": "prism_b200_model_evaluate per token (host token in, greedy token out)"},
-        "roofline": {
-            "bound": "hbm", "achieved": achieved_ffn, "peak": peak, "unit": "GB/s",
-            "frac": achieved_ffn / peak, "peak_source": peak_src,
-            "kernel": "FFN of one layer: matvec_kernel<35,kEpiSwiglu> (up+gate) + "
-                      "matvec_kernel<35,kEpiStore> (down), median over layers, event-timed "
-                      "without PDL",
-            "algorithmic_bytes_per_launch": ffn_bytes,
-            "traffic": traffic_from_profiles("ffn_layer"),
-            "traffic_source": TRAFFIC_SOURCE,
-            "step": {"achieved": bytes_per_token / (ms_per_token / 1e3) / 1e9,
-                     "frac": bytes_per_token / (ms_per_token / 1e3) / 1e9 / peak,
-                     "bytes_per_token": bytes_per_token},
-        },
+        "roofline": roofline,
         "prefill": {"value": prefill_tps, "unit": "tok/s",
                     "tokens": PROMPT - 1, "ms": prefill_ms,
                     "note": "batched prompt ingestion (prism_b200_model_prefill_async: "
@@ -450,6 +473,8 @@ def run_decode(args):
                                   "the prompt"}
     model.close()
     ex.close()
+    if not args.no_serve:
+        line["serve_tp"] = serve_tp_summary(args, world, rank, local, dev)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -975,6 +1000,7 @@ def run_prefill(args):
 
 
 SERVE_B, SERVE_CTX = 256, 8192
+SERVE_TP_STEPS = 8  # steps of the serve_tp sub-object of the decode line
 SERVE_METRIC = "batched decode tok/s (256 sequences x 8192-token context, Q8_0 KV)"
 
 
@@ -996,33 +1022,20 @@ def serve_step_bytes(cfg, B, position, tp=1):
     return cfg.linear_bytes() // tp + kv + state + conv
 
 
-def run_serve(args):
-    """configs[4]: batched serving of 256 sequences with 8192-token random
-    contexts (Q8_0 KV), greedy decode steps.  On N ranks, `--parallel tp`
-    (the default, as configs[4] specifies) splits every linear layer, the
-    heads and the KV cache of the same 256 sequences over the ranks and
-    all-reduces the row-parallel projections over NVLink peer memory (strong
-    scaling); `--parallel dp` serves N disjoint batches of 256 instead (weak
-    scaling, no exchange)."""
+def serve_measure(args, world, rank, local, dev, K, W, tp, tp_mode):
+    """Time the configs[4] batched step on this rank: `tp` ranks split every
+    linear, the heads and the KV of the same sequences (tp == world), or each
+    rank serves its own sequences (tp == 1).  Returns the measured figures;
+    the process group (world > 1) is already up."""
     import torch
     import prism_b200 as pb
     import qwen35
-    world, rank, local = dist_setup(args.gpus)
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                             device_id=dev)
     cfg = replace_ctx(qwen35.CONFIG1, SERVE_CTX)
-    K, W = min(args.steps, 64), args.warmup
     weights = qwen35.synthetic_weights(cfg, seed=0)
     ex = pb.ProjectionExecutor(local)
     model = qwen35.Qwen35Model(ex, cfg, kv_policy=qwen35.KV_Q8_0)
     model.load(weights)
     SB = args.sequences
-    tp = world if args.parallel == "tp" else 1
-    tp_mode = qwen35.TP_ALLREDUCE if args.tp_mode == "allreduce" else qwen35.TP_EXACT
     bt = qwen35.Qwen35Batch(model, SB, SERVE_CTX, tp_rank=rank if tp > 1 else 0, tp_size=tp,
                             tp_mode=tp_mode)
     if tp > 1:
@@ -1053,11 +1066,8 @@ def run_serve(args):
     ex.sync()
     ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
     served = SB * (world // tp)   # sequences advanced per step by the whole job
-    tps = served * K / (ms / 1e3)
     mid = start + 1 + W + K // 2
     step_bytes = serve_step_bytes(cfg, SB, mid, tp)
-    peak, peak_src = peaks()
-    achieved = step_bytes / (ms / K / 1e3) / 1e9
     # end to end: host tokens in, greedy tokens out, per step
     E = 3
     torch.cuda.synchronize()
@@ -1071,38 +1081,72 @@ def run_serve(args):
     bt.close()
     model.close()
     ex.close()
+    return {"cfg": cfg, "weights": weights, "ms": ms, "K": K, "W": W, "served": served,
+            "SB": SB, "start": start, "step_bytes": step_bytes, "e2e_s": e2e,
+            "clocks": clk.summary()}
+
+
+def serve_parallelism(tp, world, tp_mode):
+    if tp == 1:
+        return "sequences sharded over ranks (dp%d), no exchange" % world if world > 1 else \
+            "one GPU"
+    if tp_mode == "exact":
+        return ("tp%d exact: column-sharded linears, heads and KV; per layer 2 all-gathers of "
+                "quantized head/FFN outputs (fused into the quantizer) and 2 of hidden rows "
+                "(fused into the GEMM epilogue) over NVLink peer memory; vocabulary-split "
+                "output head" % tp)
+    return ("tp%d all-reduce: column/row-sharded linears, heads and KV; 2 all-reduces per "
+            "layer over NVLink peer memory fused into the GEMM epilogue + next RMSNorm; "
+            "vocabulary-split output head" % tp)
+
+
+def run_serve(args):
+    """configs[4]: batched serving of 256 sequences with 8192-token random
+    contexts (Q8_0 KV), greedy decode steps.  On N ranks, `--parallel tp`
+    (the default, as configs[4] specifies) splits every linear layer, the
+    heads and the KV cache of the same 256 sequences over the ranks and
+    exchanges the row-parallel outputs over NVLink peer memory (strong
+    scaling); `--parallel dp` serves N disjoint batches of 256 instead (weak
+    scaling, no exchange)."""
+    import torch
+    import qwen35
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+    tp = world if args.parallel == "tp" else 1
+    tp_mode = qwen35.TP_ALLREDUCE if args.tp_mode == "allreduce" else qwen35.TP_EXACT
+    r = serve_measure(args, world, rank, local, dev, min(args.steps, 64), args.warmup, tp,
+                      tp_mode)
+    cfg, K, ms, served, step_bytes = r["cfg"], r["K"], r["ms"], r["served"], r["step_bytes"]
+    tps = served * K / (ms / 1e3)
+    peak, peak_src = peaks()
+    achieved = step_bytes / (ms / K / 1e3) / 1e9
     line = {
         "metric": SERVE_METRIC, "value": tps, "unit": "tok/s", "n_gpus": world, "steps": K,
-        "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+        "warmup": r["W"], "ms_per_step": ms / K, "higher_is_better": True,
         "scaling": "strong" if tp > 1 else "weak",
         "vs_baseline": None, "dtype": "i8xternary->i32,f32; Q8_0 KV",
         "data": "synthetic (random-init weights, seeded random KV/recurrent context)",
         "config": {"workload": "configs[4]: %d sequences%s, 8192-token context filled "
                                "with seeded random Q8_0 KV rows and GDN/conv state, greedy decode "
                                "from position %d; configs[1] geometry"
-                               % (SB, " per GPU" if tp == 1 else "", start),
+                               % (r["SB"], " per GPU" if tp == 1 else "", r["start"]),
                    "sequences": served, "context": SERVE_CTX,
-                   "parallelism": (("tp%d exact: column-sharded linears, heads and KV; per "
-                                    "layer 2 all-gathers of quantized head/FFN outputs "
-                                    "(fused into the quantizer) and 2 of hidden rows (fused "
-                                    "into the GEMM epilogue) over NVLink peer memory; "
-                                    "vocabulary-split output head" % tp)
-                                   if args.tp_mode == "exact" else
-                                   ("tp%d all-reduce: column/row-sharded linears, heads and "
-                                    "KV; 2 all-reduces per layer over NVLink peer memory fused "
-                                    "into the GEMM epilogue + next RMSNorm; vocabulary-split "
-                                    "output head" % tp)) if tp > 1 else
-                                  "sequences sharded over ranks (dp%d), no exchange" % world,
+                   "parallelism": serve_parallelism(tp, world, args.tp_mode),
                    "l2": "each step reads %.1f GB (> 126 MB L2)" % (step_bytes / 1e9)},
-        "clocks": clk.summary(),
+        "clocks": r["clocks"],
         # embed; per attention layer 15 and per GDN layer 16 kernels (norm,
         # quantize, projections, attention or GDN, quantize, out-projection,
         # norm, quantize, up, gate, SwiGLU, quantize, down); norm, quantize,
         # output head, finish
         "gpu_launches": K * (1 + sum(15 if cfg.is_full(l) else 16 for l in range(cfg.layers))
                              + 4),
-        "e2e": {"value": served / e2e, "unit": "tok/s", "h2d_bytes_per_step": SB * 4,
-                "d2h_bytes_per_step": SB * 4,
+        "e2e": {"value": served / r["e2e_s"], "unit": "tok/s", "h2d_bytes_per_step": r["SB"] * 4,
+                "d2h_bytes_per_step": r["SB"] * 4,
                 "api": "prism_b200_batch_step per step (host tokens in, greedy tokens out)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_src,
@@ -1111,14 +1155,38 @@ def run_serve(args):
                      "algorithmic_bytes_per_step": step_bytes, "traffic": None},
     }
     if rank == 0 and not args.no_cpu:
-        cb, _ = cpu_decode_baseline(weights, qwen35.CONFIG1,
+        cb, _ = cpu_decode_baseline(r["weights"], qwen35.CONFIG1,
                                     qwen35.prompt_tokens(qwen35.CONFIG1, 64, seed=1), seconds=15.0)
         cb["sample"] = ("per-sequence oracle decode (the CPU serves sequences one at a time): " +
                         cb["sample"] + "; contexts near position 0, so the 8192-token attention "
                         "cost is not included (favours the CPU)")
         line["cpu_baseline"] = cb
+    if world > 1:
+        torch.distributed.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def serve_tp_summary(args, world, rank, local, dev):
+    """The configs[4] tensor-parallel serving figure at this N (tp == N, the
+    exact exchange form): the sub-object the decode line carries so that a
+    1..8-GPU run of the default workload also measures the serving curve."""
+    import qwen35
+    r = serve_measure(args, world, rank, local, dev, SERVE_TP_STEPS, 3, world, qwen35.TP_EXACT)
+    K, ms, served, step_bytes = r["K"], r["ms"], r["served"], r["step_bytes"]
+    peak, peak_src = peaks()
+    achieved = step_bytes / (ms / K / 1e3) / 1e9
+    return {"metric": SERVE_METRIC, "value": served * K / (ms / 1e3), "unit": "tok/s",
+            "n_gpus": world, "tp": world, "steps": K, "warmup": r["W"], "ms_per_step": ms / K,
+            "scaling": "strong", "sequences": served, "context": SERVE_CTX,
+            "parallelism": serve_parallelism(world, world, "exact"),
+            "roofline": {"bound": "hbm", "achieved_per_gpu": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
+                         "algorithmic_bytes_per_step_per_gpu": step_bytes},
+            "e2e": {"value": served / r["e2e_s"], "unit": "tok/s",
+                    "h2d_bytes_per_step": r["SB"] * 4, "d2h_bytes_per_step": r["SB"] * 4,
+                    "api": "prism_b200_batch_step per step"},
+            "clocks": r["clocks"]}
 
 
 def replace_ctx(cfg, context):
@@ -1240,6 +1308,8 @@ def main():
                                                                 "prefill"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-matvec", action="store_true", help="skip the configs[0] sub-benchmark")
+    ap.add_argument("--no-serve", action="store_true",
+                    help="skip the decode line's serve_tp (configs[4] at tp = N) sub-object")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens (profiling runs)")
     ap.add_argument("--prefill-tokens", type=int, default=PREFILL_TOKENS,
                     help="prefill workload: prompt tokens (profiling runs use fewer)")

@@ -152,10 +152,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
   return ok != 0;
 }
 
+// Non-blocking test of the phase's completion.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait; returns false (and reports) if the phase never completed.
+// A phase that already completed is seen by a non-blocking test.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned parity,
                                                   unsigned *status) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test_wait(bar, parity) || mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   while (!mbar_try_wait(bar, parity)) {
     if (global_timer_ns() - t0 > kWaitLimitNs) {

@@ -55,8 +55,11 @@ constexpr int kFMaxNb = 48;                 // input blocks per projection (1228
 constexpr int kFActBytes = (kFMaxNb * (256 + 4 + 32 + 4) + 127) / 128 * 128;
 constexpr int kFWorkBytes = 58 * 1024;      // staging, terms, GDN / attention scratch
 constexpr int kFDescBytes = 1024;
-constexpr int kFChunk = 32;                 // attention: positions per K/V chunk
-constexpr int kFMaxScores = 1024;           // attention: positions per CTA
+constexpr int kFAttnMaxPos = 2048;          // attention: positions of one head's scores
+constexpr int kFKChunk = 16;                // attention: cached K rows per copy job
+constexpr int kFVDepth = 16;                // attention: V positions per share per copy job
+constexpr int kFAttnSlots = 7;              // attention: 8 KB slots the copy jobs rotate through
+constexpr int kFAttnSlot = 8192;
 constexpr int kFPieceMax = 32 * 1024;       // bytes of one weight-stream piece (soft cap)
 // shared-memory layout
 constexpr int kFOffAct = kFRing;
@@ -65,8 +68,8 @@ constexpr int kFOffDesc = kFOffWork + kFWorkBytes;           // [kFDescBufs] pha
 constexpr int kFDescBufs = 4;              // descriptors prefetched kFDescBufs - 1 phases ahead
 constexpr int kFOffBars = kFOffDesc + kFDescBufs * kFDescBytes;  // ring [kFSlots], desc [4], kv [4]
 constexpr int kFOffMeta = kFOffBars + (kFSlots + 8) * 8;     // off/len [kFSlots], counters
-constexpr int kFOffRed = kFOffMeta + kFSlots * 8 + 64;       // double [16] + float [16]
-constexpr int kFOffRes = kFOffRed + 16 * 8 + 16 * 4 + 64;    // u64 [kFThreads] residual words
+constexpr int kFOffRed = kFOffMeta + kFSlots * 8 + 64;       // double [2][16] + float [16]
+constexpr int kFOffRes = kFOffRed + 2 * 16 * 8 + 16 * 4 + 64;  // u64 [kFThreads] residual words
 constexpr int kFOffTab = kFOffRes + kFThreads * 8;            // batch tile table [4][16] u32
 constexpr int kFOffIssue = kFOffTab + 4 * kFWarps * 4;         // u64 [kFSlots] (traced steps)
 constexpr int kFMaxPieces = 48;                               // weight-stream pieces per phase
@@ -123,7 +126,8 @@ struct FAttn {
   int heads, kv_heads, hd, rope_dim;
   int sections[3];
   float eps, theta_scale;
-  uint64_t *smax, *stot, *part;      // exchanges between the split's CTAs, tagged
+  uint64_t *sc;                      // [heads][ctx] scores of the cached positions, tagged
+  int ctx;
   uint64_t *out;                     // [heads * hd] gated output, tagged
 };
 
@@ -213,6 +217,31 @@ __device__ __forceinline__ void cp_async8(void *dst, const void *src) {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// Wait until at most n of this thread's most recently committed groups are
+// pending (n above 7 waits for more than asked, which is safe).
+__device__ __forceinline__ void cp_async_wait_pending(int n) {
+  switch (n) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+    case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+    case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
+    case 6: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 7;" ::: "memory"); break;
+  }
+}
 
 struct FlowCtl {
   unsigned *status;
@@ -230,6 +259,10 @@ __device__ __forceinline__ void flow_raise(const FlowCtl &c) {
 
 // Called after a poll round that found a word not yet written: keeps the
 // wait bounded (kWaitLimitNs) and leaves early when another CTA aborted.
+// The abort word (a global load, a round trip during which nothing is
+// polled) is consulted only once a wait has lasted kSpinAbortNs, longer
+// than any wait of a step that runs normally.
+constexpr unsigned long long kSpinAbortNs = 20000;
 struct Spin {
   unsigned long long t0 = 0;
   int rounds = 0;
@@ -239,8 +272,9 @@ struct Spin {
       return true;
     }
     if ((rounds & 31) == 0) {
-      if (flow_aborted(c)) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
+      const unsigned long long waited = global_timer_ns() - t0;
+      if (waited > kSpinAbortNs && flow_aborted(c)) return false;
+      if (waited > kWaitLimitNs) {
         flow_raise(c);
         return false;
       }
@@ -258,6 +292,30 @@ __device__ __forceinline__ bool wait_word(const uint64_t *p, uint32_t tag, uint6
     if (!sp.again(c)) return false;
     w = ld_word(p);
   }
+  return true;
+}
+
+// Wait for the words *p[j], j < N, with every load in flight at once;
+// their values into v[j].
+template <int N>
+__device__ __forceinline__ bool wait_each(const uint64_t *const (&p)[N], uint32_t tag,
+                                          float (&v)[N], const FlowCtl &c) {
+  uint64_t w[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) w[j] = ld_word(p[j]);
+  Spin sp;
+  for (;;) {
+    bool all = true;
+#pragma unroll
+    for (int j = 0; j < N; ++j) all &= has_tag(w[j], tag);
+    if (all) break;
+    if (!sp.again(c)) return false;
+#pragma unroll
+    for (int j = 0; j < N; ++j)
+      if (!has_tag(w[j], tag)) w[j] = ld_word(p[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < N; ++j) v[j] = word_value(w[j]);
   return true;
 }
 
@@ -295,6 +353,32 @@ __device__ __forceinline__ double fsum_f64(double v, double *red) {
   double t = 0.0;
   for (int w = 0; w < kFWarps; ++w) t += red[w];
   return t;
+}
+
+// Two binary64 sums over the compute warps at once, each in fsum_f64's
+// order; red holds >= 32 doubles.
+__device__ __forceinline__ void fsum2_f64(double &a, double &b, double *red) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const double x = __shfl_xor_sync(0xffffffffu, a, off);
+    const double y = __shfl_xor_sync(0xffffffffu, b, off);
+    a += x;
+    b += y;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  csync();
+  if (lane == 0) {
+    red[warp] = a;
+    red[16 + warp] = b;
+  }
+  csync();
+  double ta = 0.0, tb = 0.0;
+  for (int w = 0; w < kFWarps; ++w) {
+    ta += red[w];
+    tb += red[16 + w];
+  }
+  a = ta;
+  b = tb;
 }
 
 __device__ __forceinline__ float fmax_f32(float v, float *red) {
@@ -362,7 +446,6 @@ struct FRing {
   uint32_t *issued_live;  // pieces issued so far (release after each issue)
   uint32_t *desc_done;    // phases the compute warps finished (release)
   uint32_t *desc_fetched; // descriptors the fetcher issued
-  uint32_t *kvuse;    // [4] completed uses of the attention K/V barriers
   unsigned long long *issue_ts;  // [kFSlots] issue time of each piece (traced steps)
 };
 
@@ -455,16 +538,29 @@ __device__ void flow_producer(const FlowArgs &fa, const FRing &rg, const FlowCtl
 __device__ __forceinline__ bool stage_words(const uint64_t *in, int n, uint32_t tag, float *xs,
                                             bool sumsq, double &s, const FlowCtl &c) {
   constexpr int kMax = kFMaxNb * 256 / kFThreads;  // 24
-  float v[kMax];
   const int i = threadIdx.x;
   const int cnt = i < n ? (n - i + kFThreads - 1) / kFThreads : 0;
-  if (!wait_words<kMax>(in, i, kFThreads, cnt, tag, v, c)) return false;
+  uint64_t w[kMax];
+#pragma unroll
+  for (int j = 0; j < kMax; ++j) w[j] = j < cnt ? ld_word(in + i + j * kFThreads) : tagged_u(0u, tag);
+  Spin sp;
+  for (;;) {
+    bool all = true;
+#pragma unroll
+    for (int j = 0; j < kMax; ++j) all &= has_tag(w[j], tag);
+    if (all) break;
+    if (!sp.again(c)) return false;
+#pragma unroll
+    for (int j = 0; j < kMax; ++j)
+      if (j < cnt && !has_tag(w[j], tag)) w[j] = ld_word(in + i + j * kFThreads);
+  }
   s = 0.0;
 #pragma unroll
   for (int j = 0; j < kMax; ++j)
     if (j < cnt) {
-      xs[i + j * kFThreads] = v[j];
-      if (sumsq) s += (double)__fmul_rn(v[j], v[j]);
+      const float v = word_value(w[j]);
+      xs[i + j * kFThreads] = v;
+      if (sumsq) s += (double)__fmul_rn(v, v);
     }
   return true;
 }
@@ -679,8 +775,36 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
     bool ok = true;
     for (int h = warp; h < p.heads && ok; h += kFWarps) {
       float o[4], g[4];
-      ok = wait_words<4>(p.in, h * S + lane, 32, 4, itag, o, c) &&
-           wait_words<4>(p.zs, h * S + lane, 32, 4, ztag, g, c);
+      {
+        // the head's outputs and SiLU(z) words, all eight loads in flight
+        uint64_t w[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          w[q] = ld_word(p.in + h * S + 32 * q + lane);
+          w[4 + q] = ld_word(p.zs + h * S + 32 * q + lane);
+        }
+        Spin sp;
+        for (;;) {
+          bool all = true;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) all &= has_tag(w[q], itag) && has_tag(w[4 + q], ztag);
+          if (all) break;
+          if (!sp.again(c)) {
+            ok = false;
+            break;
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (!has_tag(w[q], itag)) w[q] = ld_word(p.in + h * S + 32 * q + lane);
+            if (!has_tag(w[4 + q], ztag)) w[4 + q] = ld_word(p.zs + h * S + 32 * q + lane);
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          o[q] = word_value(w[q]);
+          g[q] = word_value(w[4 + q]);
+        }
+      }
       ok = __all_sync(0xffffffffu, ok);  // the warp's shuffles below need every lane
       if (!ok) break;
       double t = 0.0;
@@ -810,11 +934,14 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
     if (chain) {
       const float *tk = terms + ck * upt * 32;
       // the reference's chain: sum = 0; sum += term_b for b in order
+      // (unrolled so that the loads run ahead of the dependent adds)
       float sum = 0.0f;
+#pragma unroll 8
       for (int b = 0; b < nb; ++b) sum = __fadd_rn(sum, tk[b * 32 + lane]);
       const int r = corow;
       if (pair) {
         float gsum = 0.0f;
+#pragma unroll 8
         for (int b = nb; b < 2 * nb; ++b) gsum = __fadd_rn(gsum, tk[b * 32 + lane]);
         const float hv = __fmul_rn(sum, silu_f(gsum));
         if (!is_finite_f(sum) || !is_finite_f(gsum)) report(c.status, kStatusNonfinite);
@@ -901,10 +1028,11 @@ __device__ bool flow_gdn(const FGdn &a, int pos, uint8_t *smem, uint32_t ep, uin
       if (hist > 0) nj[hist - 1] = projected;
     }
   } else if (tid == 2 * S + R) {
-    uint64_t wa = 0, wb = 0;
-    ok = wait_word(a.alpha + h, itag, wa, c) && wait_word(a.beta + h, itag, wb, c);
-    sdb[0] = recurrent_decay_f(word_value(wa), a.dt_bias[h], a.ssm_a[h], c.status);
-    sdb[1] = sigmoid_f(word_value(wb));
+    const uint64_t *const src[2] = {a.alpha + h, a.beta + h};
+    float x[2];
+    ok = wait_each<2>(src, itag, x, c);
+    sdb[0] = recurrent_decay_f(x[0], a.dt_bias[h], a.ssm_a[h], c.status);
+    sdb[1] = sigmoid_f(x[1]);
   } else if (tid >= 2 * S + R + 32 && tid < 2 * S + R + 32 + R) {
     // SiLU(z) of this slice's rows, for the out-projection's gated norm
     const int i = h * S + r0 + (tid - (2 * S + R + 32));
@@ -958,89 +1086,148 @@ __device__ bool flow_gdn(const FGdn &a, int pos, uint8_t *smem, uint32_t ep, uin
   return true;
 }
 
-// RMSNorm(x)*w, RoPE, binary16 rounding over hd (== 256) values held one per
-// thread (threads at or past hd contribute zeros): norm_rope_round's
-// arithmetic over the compute warps.
-__device__ __forceinline__ float flow_norm_rope_round(float xi, const float *w, float eps, int hd,
-                                                      int rope, const float *cs, float *buf,
-                                                      double *red) {
+// RMSNorm(x)*w, RoPE and binary16 rounding (norm_rope_round's arithmetic)
+// of the query (xq, weights wq) and the current key (xk, wk) over hd
+// (== 256) values held one per thread, threads at or past hd contributing
+// zeros; the two reductions share their barriers.  bq and bk are [hd]
+// scratch.
+__device__ __forceinline__ void flow_norm_rope_round2(float xq, float xk, const float *wq,
+                                                      const float *wk, float eps, int hd,
+                                                      int rope, const float *cs, float *bq,
+                                                      float *bk, double *red, float &oq,
+                                                      float &ok_) {
   const int i = threadIdx.x;
-  const double ss = fsum_f64(i < hd ? (double)__fmul_rn(xi, xi) : 0.0, red);
-  const float mean = (float)(ss / (double)hd);
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-  if (i < hd) buf[i] = __fmul_rn(__fmul_rn(xi, scale), w[i]);
-  csync();
-  float out = i < hd ? buf[i] : 0.0f;
-  const int half = rope / 2;
-  if (i < half) {
-    const float first = buf[i], second = buf[i + half];
-    out = __fsub_rn(__fmul_rn(first, cs[2 * i]), __fmul_rn(second, cs[2 * i + 1]));
-  } else if (i < rope) {
-    const int j = i - half;
-    const float first = buf[j], second = buf[i];
-    out = __fadd_rn(__fmul_rn(first, cs[2 * j + 1]), __fmul_rn(second, cs[2 * j]));
+  double sq = i < hd ? (double)__fmul_rn(xq, xq) : 0.0;
+  double sk = i < hd ? (double)__fmul_rn(xk, xk) : 0.0;
+  fsum2_f64(sq, sk, red);
+  const float scq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(sq / (double)hd), eps)));
+  const float sck = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(sk / (double)hd), eps)));
+  if (i < hd) {
+    bq[i] = __fmul_rn(__fmul_rn(xq, scq), wq[i]);
+    bk[i] = __fmul_rn(__fmul_rn(xk, sck), wk[i]);
   }
   csync();
-  return round_f16(out);
+  float a = i < hd ? bq[i] : 0.0f, b = i < hd ? bk[i] : 0.0f;
+  const int half = rope / 2;
+  if (i < half) {
+    a = __fsub_rn(__fmul_rn(bq[i], cs[2 * i]), __fmul_rn(bq[i + half], cs[2 * i + 1]));
+    b = __fsub_rn(__fmul_rn(bk[i], cs[2 * i]), __fmul_rn(bk[i + half], cs[2 * i + 1]));
+  } else if (i < rope) {
+    const int j = i - half;
+    a = __fadd_rn(__fmul_rn(bq[j], cs[2 * j + 1]), __fmul_rn(bq[i], cs[2 * j]));
+    b = __fadd_rn(__fmul_rn(bk[j], cs[2 * j + 1]), __fmul_rn(bk[i], cs[2 * j]));
+  }
+  csync();
+  oq = round_f16(a);
+  ok_ = round_f16(b);
 }
 
 // Attention of query head h split over kAttnSplit CTAs (attention_decode_
-// kernel's arithmetic; hd == 256).  The CTA's cached K and V rows stream
-// through shared-memory chunks by bulk copies issued before its inputs are
-// awaited; the softmax maximum, total and value partial sums are exchanged
-// through tagged words and combined in rank order.
-__device__ bool flow_attn(const FAttn &a, int pos, uint8_t *smem, const FRing &rg, uint32_t ep,
-                          uint32_t tag, const FlowCtl &c) {
+// kernel's arithmetic and reduction orders; hd == 256).  CTA r scores its
+// share of the cached positions and publishes the scores as tagged words;
+// every CTA of the head then forms the softmax over all positions itself --
+// the maximum, each share's binary64 total in the tree that attention_
+// decode_kernel's block reduction gives it, the shares' totals in rank
+// order -- and CTA r accumulates output dimensions [r*32, r*32 + 32) over
+// every position: each share's binary64 partial sum in position order, the
+// shares in rank order.  The same sums as the kernel with one exchange
+// instead of three.  The K rows of the CTA's share and the V column slices
+// of every position stream through shared memory by 16-byte asynchronous
+// copies issued before the inputs are awaited.
+constexpr int kFAttnHead = 15360;  // q, kc, vc, buf, cs, probabilities, trees, partials, gate
+static_assert((4 * 256 + 64 + kFAttnMaxPos) * 4 + (64 + 8 + 8 * 32) * 8 + 32 * 4 <= kFAttnHead,
+              "attention head area");
+static_assert(kFAttnHead + kFAttnSlots * kFAttnSlot <= kFActBytes + kFWorkBytes,
+              "attention slots fit the activation and work areas");
+static_assert(kFKChunk * 512 <= kFAttnSlot && 8 * kFVDepth * 64 <= kFAttnSlot,
+              "a binary16 K chunk or V chunk fills one slot");
+
+// Two binary64 warp sums in warp_sum_f64's butterfly, interleaved.
+__device__ __forceinline__ void warp_sum2_f64(double &a, double &b) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const double x = __shfl_xor_sync(0xffffffffu, a, off);
+    const double y = __shfl_xor_sync(0xffffffffu, b, off);
+    a += x;
+    b += y;
+  }
+}
+
+__device__ bool flow_attn(const FAttn &a, int pos, uint8_t *smem, uint32_t ep, uint32_t tag,
+                          const FlowCtl &c, unsigned long long *tr) {
   if ((int)blockIdx.x >= a.heads * kAttnSplit) return true;
   const int hd = a.hd;
-  uint8_t *work = smem + kFOffWork;
-  float *q = reinterpret_cast<float *>(work);  // [hd]
+  uint8_t *area = smem + kFOffAct;
+  float *q = reinterpret_cast<float *>(area);  // [hd]
   float *kc = q + hd;
   float *vc = kc + hd;
   float *buf = vc + hd;
   float *cs = buf + hd;                        // [64]
-  float *scores = cs + 64;                     // [kFMaxScores]
-  uint8_t *kvbuf = work + (size_t)(4 * hd + 64 + kFMaxScores) * 4;
+  float *pr = cs + 64;                         // [kFAttnMaxPos] scores, exponentials, probabilities
+  double *tw = reinterpret_cast<double *>(pr + kFAttnMaxPos);  // [share][warp] tree sums
+  double *tot = tw + 64;                       // [share]
+  double *part = tot + 8;                      // [share][32]
+  float *gs = reinterpret_cast<float *>(part + 8 * 32);  // [32] gate
   double *red = reinterpret_cast<double *>(smem + kFOffRed);
-  float *fred = reinterpret_cast<float *>(red + 16);
-  uint64_t *kvbar = rg.bar + kFSlots + kFDescBufs;  // [4]
+  float *fred = reinterpret_cast<float *>(red + 32);
   const int rank = blockIdx.x % kAttnSplit, h = blockIdx.x / kAttnSplit;
   const int group = a.heads / a.kv_heads, kvh = h / group, kvw = a.kv_heads * hd;
   const int i = threadIdx.x, warp = i >> 5, lane = i & 31;
   const int per = (pos + kAttnSplit - 1) / kAttnSplit;
   const int lo = min(pos, rank * per), hi = min(pos, lo + per);
   const int rb = attn_row_bytes(hd, a.q8);
-  const int nbuf =
-      min(4, (int)((kFWorkBytes - (4 * hd + 64 + kFMaxScores) * 4) / (kFChunk * rb)));
-  const int nk = (hi - lo + kFChunk - 1) / kFChunk;  // chunks per pass
-  const uint32_t itag = flow_tag(ep, a.in_k);
-  // completed uses of each K/V buffer's barrier in earlier attention phases
-  // of this launch: the parity of chunk g's wait is (base + g / nbuf) & 1
-  uint32_t base[4];
-#pragma unroll
-  for (int b = 0; b < 4; ++b) base[b] = rg.kvuse[b];
-  auto par = [&](int g) { return (base[g % nbuf] + (uint32_t)(g / nbuf)) & 1u; };
-  // chunk g of the pass sequence (K chunks, then V chunks) into buffer
-  // g % nbuf: warp 0 issues one bulk copy per row (lane = row)
+  const int dims = hd / kAttnSplit;  // 32: one Q8_0 block
+  uint8_t *slots = area + kFAttnHead;  // [kFAttnSlots][kFAttnSlot]
+  const int nk = (hi - lo + kFKChunk - 1) / kFKChunk;  // K jobs of this share
+  const int nv = (per + kFVDepth - 1) / kFVDepth;      // V jobs (every share at once)
+  const int njobs = nk + nv;
+  auto krow = [&](int p) -> const uint8_t * {
+    return a.q8 ? a.kcache + ((size_t)p * a.kv_heads + kvh) * rb
+                : a.kcache + ((size_t)p * kvw + (size_t)kvh * hd) * 2;
+  };
+  // Copy job g (g < nk: K rows of the share; else V chunk g - nk: slot
+  // r * kFVDepth + t holds position lo_r + k * kFVDepth + t of share r,
+  // dimensions [rank*32, rank*32 + 32)) into slot g % kFAttnSlots, as one
+  // cp.async group per thread: job g is group g of the phase.
   auto issue = [&](int g) {
-    const bool isv = g >= nk;
-    const int p0 = lo + (isv ? g - nk : g) * kFChunk, count = min(kFChunk, hi - p0);
-    uint64_t *bar = &kvbar[g % nbuf];
-    if (lane == 0) mbar_arrive_expect_tx(bar, (unsigned)(count * rb));
-    __syncwarp();
-    if (lane < count) {
-      const int pp = p0 + lane;
-      const size_t at = a.q8 ? ((size_t)pp * a.kv_heads + kvh) * rb
-                             : ((size_t)pp * kvw + (size_t)kvh * hd) * 2;
-      bulk_g2s(kvbuf + ((size_t)(g % nbuf) * kFChunk + lane) * rb,
-               (isv ? a.vcache : a.kcache) + at, (unsigned)rb, bar);
+    uint8_t *dst = slots + (size_t)(g % kFAttnSlots) * kFAttnSlot;
+    if (g < nk) {
+      const int p0 = lo + g * kFKChunk, count = min(kFKChunk, hi - p0), cpr = rb / 16;
+      for (int j = i; j < count * cpr; j += kFThreads) {
+        const int row = j / cpr, off = (j - row * cpr) * 16;
+        cp_async16(dst + (size_t)row * rb + off, krow(p0 + row) + off);
+      }
+    } else {
+      const int k = g - nk, cps = a.q8 ? 3 : 4;
+      for (int j = i; j < 8 * kFVDepth * cps; j += kFThreads) {
+        const int slot = j / cps, cp = j - slot * cps;
+        const int r = slot / kFVDepth, t = slot - r * kFVDepth;
+        const int lo_r = min(pos, r * per), hi_r = min(pos, lo_r + per);
+        const int p = lo_r + k * kFVDepth + t;
+        if (p >= hi_r) continue;
+        if (a.q8) {
+          const uint8_t *rec = a.vcache + ((size_t)p * a.kv_heads + kvh) * rb;
+          if (cp < 2)
+            cp_async16(dst + slot * 32 + cp * 16, rec + hd / 32 * 2 + rank * dims + cp * 16);
+          else  // the aligned word holding block `rank`'s scale
+            cp_async4(dst + 8 * kFVDepth * 32 + slot * 4, rec + (rank & ~1) * 2);
+        } else {
+          cp_async16(dst + slot * 64 + cp * 16,
+                     a.vcache + ((size_t)p * kvw + (size_t)kvh * hd + rank * dims) * 2 + cp * 16);
+        }
+      }
+    }
+    cp_async_commit();
+  };
+  // every slot starts filling now; a consumed job's slot takes job g + slots
+  int ng = min(njobs, kFAttnSlots);
+  for (int g = 0; g < ng; ++g) issue(g);
+  auto refill = [&](int g) {
+    if (g + kFAttnSlots < njobs) {
+      issue(g + kFAttnSlots);
+      ++ng;
     }
   };
-  int issued = min(nbuf, 2 * nk), waited = 0;
-  if (warp == 0) {
-    fence_proxy_async_smem();  // the work area was read through the generic proxy
-    for (int g = 0; g < issued; ++g) issue(g);
-  }
   if (i < a.rope_dim / 2) {
     float theta = (float)pos;
     for (int j = 0; j < i; ++j) theta = __fmul_rn(theta, a.theta_scale);
@@ -1048,35 +1235,29 @@ __device__ bool flow_attn(const FAttn &a, int pos, uint8_t *smem, const FRing &r
     cs[2 * i] = cos_cr(angle);
     cs[2 * i + 1] = sin_cr(angle);
   }
-  auto drain = [&]() {
-    // copies that were issued but never waited on: let them land (bounded)
-    if (i == 0)
-      for (int g = waited; g < issued; ++g) mbar_wait_bounded(&kvbar[g % nbuf], par(g), c.status);
-  };
   // inputs: query, current key and value (thread i < hd), the gate of this
   // CTA's output dimensions (threads hd .. hd + dims)
-  const int dims = hd / kAttnSplit;
-  float xq = 0.f, xk = 0.f, xv = 0.f, gate = 0.f;
+  const uint32_t itag = flow_tag(ep, a.in_k);
+  float xq = 0.f, xk = 0.f, xv = 0.f;
   bool ok = true;
   if (i < hd) {
-    uint64_t w = 0;
-    ok = wait_word(a.proj + (long)h * 2 * hd + i, itag, w, c);
-    xq = word_value(w);
-    ok = ok && wait_word(a.key + (long)kvh * hd + i, itag, w, c);
-    xk = word_value(w);
-    ok = ok && wait_word(a.value + (long)kvh * hd + i, itag, w, c);
-    xv = word_value(w);
+    const uint64_t *const src[3] = {a.proj + (long)h * 2 * hd + i, a.key + (long)kvh * hd + i,
+                                    a.value + (long)kvh * hd + i};
+    float x[3];
+    ok = wait_each<3>(src, itag, x, c);
+    xq = x[0];
+    xk = x[1];
+    xv = x[2];
   } else if (i < hd + dims) {
     uint64_t w = 0;
     ok = wait_word(a.proj + (long)(2 * h + 1) * hd + rank * dims + (i - hd), itag, w, c);
-    gate = word_value(w);
+    gs[i - hd] = word_value(w);
   }
-  if (!csync_and(ok)) {
-    drain();
-    return false;
-  }
-  const float qv = flow_norm_rope_round(xq, a.q_norm, a.eps, hd, a.rope_dim, cs, buf, red);
-  const float kv_ = flow_norm_rope_round(xk, a.k_norm, a.eps, hd, a.rope_dim, cs, buf, red);
+  if (!csync_and(ok)) return false;
+  if (tr) tr[1] = global_timer_ns();
+  float qv, kv_;
+  flow_norm_rope_round2(xq, xk, a.q_norm, a.k_norm, a.eps, hd, a.rope_dim, cs, buf, vc, red, qv,
+                        kv_);
   if (i < hd) {
     q[i] = qv;
     kc[i] = kv_;
@@ -1095,150 +1276,148 @@ __device__ bool flow_attn(const FAttn &a, int pos, uint8_t *smem, const FRing &r
     }
   }
   csync();
+  if (tr) tr[2] = global_timer_ns();
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
   const float4 q0 = reinterpret_cast<const float4 *>(q)[lane * 2];
   const float4 q1 = reinterpret_cast<const float4 *>(q)[lane * 2 + 1];
-  // scores of the cached positions: warp per position, lane owns 8 dims
-  bool landed = true;
-  for (int chk = 0; chk < nk && landed; ++chk) {
-    landed = csync_and(mbar_wait_bounded(&kvbar[chk % nbuf], par(chk), c.status));
-    if (!landed) break;
-    ++waited;
-    const int p0 = lo + chk * kFChunk, count = min(kFChunk, hi - p0);
-    const uint8_t *rows = kvbuf + (size_t)(chk % nbuf) * kFChunk * rb;
-    for (int pp = warp; pp < count; pp += kFWarps) {
-      const double sc =
-          warp_sum_f64(key_partial_staged(rows + (size_t)pp * rb, hd, a.q8, q0, q1, lane));
-      if (lane == 0) scores[p0 + pp - lo] = __fmul_rn((float)sc, scale);
-    }
-    csync();  // the buffer is free again
-    if (chk + nbuf < 2 * nk) {
-      if (warp == 0) {
-        fence_proxy_async_smem();
-        issue(chk + nbuf);
+  uint64_t *sc = a.sc + (long)h * a.ctx;
+  // scores of the share: two K jobs at a time, warp per position, lane owns 8 dims
+  for (int g0 = 0; g0 < nk; g0 += 2) {
+    const int g1 = min(g0 + 1, nk - 1);
+    cp_async_wait_pending(ng - 1 - g1);
+    csync();
+    if (tr && g0 == 0) tr[14] = global_timer_ns();
+    const int p0 = lo + g0 * kFKChunk, count = min((g1 - g0 + 1) * kFKChunk, hi - p0);
+    for (int pp = warp; pp < count; pp += 2 * kFWarps) {
+      const bool two = pp + kFWarps < count;
+      auto row = [&](int x) {
+        return slots + (size_t)((g0 + x / kFKChunk) % kFAttnSlots) * kFAttnSlot +
+               (size_t)(x % kFKChunk) * rb;
+      };
+      double s0 = key_partial_staged(row(pp), hd, a.q8, q0, q1, lane);
+      double s1 = two ? key_partial_staged(row(pp + kFWarps), hd, a.q8, q0, q1, lane) : 0.0;
+      warp_sum2_f64(s0, s1);
+      if (lane == 0) {
+        const float v0 = __fmul_rn((float)s0, scale);
+        pr[p0 + pp] = v0;
+        st_word(sc + p0 + pp, tagged(v0, tag));
+        if (two) {
+          const float v1 = __fmul_rn((float)s1, scale);
+          pr[p0 + pp + kFWarps] = v1;
+          st_word(sc + p0 + pp + kFWarps, tagged(v1, tag));
+        }
       }
-      ++issued;
     }
+    csync();  // the slots are free again
+    if (tr && g0 == 0) tr[15] = global_timer_ns();
+    for (int g = g0; g <= g1; ++g) refill(g);
   }
-  if (!landed) {
-    drain();
-    if (i == 0) flow_raise(c);
-    return false;
-  }
+  if (tr) tr[3] = global_timer_ns();
   // the current position's score (every CTA of the head computes it)
   float s_cur;
   {
-    const double sc = fsum_f64(i < hd ? (double)__fmul_rn(q[i], kc[i]) : 0.0, red);
-    s_cur = __fmul_rn((float)sc, scale);
+    const double s = fsum_f64(i < hd ? (double)__fmul_rn(q[i], kc[i]) : 0.0, red);
+    s_cur = __fmul_rn((float)s, scale);
   }
+  // every share's scores: the other CTAs' from their tagged words
+  {
+    float v[kFAttnMaxPos / kFThreads];
+    const int cnt = i < pos ? (pos - i + kFThreads - 1) / kFThreads : 0;
+    ok = wait_words<kFAttnMaxPos / kFThreads>(sc, i, kFThreads, cnt, tag, v, c);
+#pragma unroll
+    for (int j = 0; j < kFAttnMaxPos / kFThreads; ++j)
+      if (j < cnt) pr[i + j * kFThreads] = v[j];
+    if (!csync_and(ok)) return false;
+  }
+  if (tr) tr[4] = global_timer_ns();
   float m = -INFINITY;
-  if (i < kAttnThreads)
-    for (int pp = i; pp < hi - lo; pp += kAttnThreads) m = fmaxf(m, scores[pp]);
-  m = fmax_f32(m, fred);
-  uint64_t *smax = a.smax + (long)h * kAttnSplit;
-  if (i == 0) st_word(smax + rank, tagged(m, tag));
-  float M = s_cur;
+  for (int p = i; p < pos; p += kFThreads) m = fmaxf(m, pr[p]);
+  const float M = fmaxf(s_cur, fmax_f32(m, fred));
+  if (tr) tr[10] = global_timer_ns();
+  for (int p = i; p < pos; p += kFThreads) pr[p] = exp_cr(__fsub_rn(pr[p], M));
+  csync();
+  if (tr) tr[11] = global_timer_ns();
+  // share r's total: thread j < kAttnThreads of attention_decode_kernel sums
+  // positions j, j + kAttnThreads, ... of the share; warps in butterflies;
+  // the eight warps in order
+  // (a warp past the share's positions sums zeros: its tree is +0.0)
   {
-    uint64_t w = 0;
-    ok = i < kAttnSplit ? wait_word(smax + i, tag, w, c) : true;
-    csync();  // fred was read by the maximum
-    if (i < kAttnSplit) fred[i] = word_value(w);
-    if (!csync_and(ok)) {
-      drain();
-      return false;
+    const int wn = min(kAttnThreads / 32, (per + 31) / 32);  // warps with positions
+    for (int t = warp; t < 8 * wn; t += kFWarps) {
+      const int r = t / wn, w = t % wn;
+      const int lo_r = min(pos, r * per), n_r = min(pos, lo_r + per) - lo_r;
+      double y = 0.0;
+      for (int pp = w * 32 + lane; pp < n_r; pp += kAttnThreads) y += (double)pr[lo_r + pp];
+      y = warp_sum_f64(y);
+      if (lane == 0) tw[r * (kAttnThreads / 32) + w] = y;
     }
-    for (int r = 0; r < kAttnSplit; ++r) M = fmaxf(M, fred[r]);
+    if (i < 64 && (i & 7) >= wn) tw[i] = 0.0;
   }
-  double tot = 0.0;
-  if (i < kAttnThreads)
-    for (int pp = i; pp < hi - lo; pp += kAttnThreads) {
-      const float e = exp_cr(__fsub_rn(scores[pp], M));
-      scores[pp] = e;
-      tot += (double)e;
-    }
-  tot = fsum_f64(tot, red);
-  uint64_t *stot = a.stot + (long)h * kAttnSplit * 2;
-  if (i == 0) {
-    const unsigned long long bits = (unsigned long long)__double_as_longlong(tot);
-    st_word(stot + 2 * rank, tagged_u((uint32_t)bits, tag));
-    st_word(stot + 2 * rank + 1, tagged_u((uint32_t)(bits >> 32), tag));
+  csync();
+  if (tr) tr[12] = global_timer_ns();
+  if (i < 8) {
+    double t = 0.0;
+    for (int w = 0; w < kAttnThreads / 32; ++w) t += tw[i * 8 + w];
+    tot[i] = t;
   }
+  csync();
+  if (tr) tr[13] = global_timer_ns();
   double total = 0.0;
-  {
-    uint64_t w0 = 0, w1 = 0;
-    ok = i < kAttnSplit ? wait_word(stot + 2 * i, tag, w0, c) && wait_word(stot + 2 * i + 1, tag, w1, c)
-                        : true;
-    csync();  // red was read by the total
-    if (i < kAttnSplit) red[i] = word_pair_value(w0, w1);
-    if (!csync_and(ok)) {
-      drain();
-      return false;
-    }
-    for (int r = 0; r < kAttnSplit; ++r) total += red[r];
-  }
+  for (int r = 0; r < kAttnSplit; ++r) total += tot[r];
   const float e_cur = exp_cr(__fsub_rn(s_cur, M));
   total += (double)e_cur;
   const float inv = (float)(1.0 / total);
   if (!is_finite_f(M) && i == 0 && rank == 0) report(c.status, kStatusNonfinite);
   const float p_cur = round_f16(__fmul_rn(e_cur, inv));
-  if (i < kAttnThreads)
-    for (int pp = i; pp < hi - lo; pp += kAttnThreads) scores[pp] = round_f16(__fmul_rn(scores[pp], inv));
-  csync();
-  // value partial sums of this CTA's positions: one dimension per thread
+  for (int p = i; p < pos; p += kFThreads) pr[p] = round_f16(__fmul_rn(pr[p], inv));
+  if (tr) tr[8] = global_timer_ns();
+  // values: thread (share r, dimension dl) sums the share's positions in order
+  const int vr = i >> 5, dl = i & 31;
+  const int vlo = min(pos, vr * per), vhi = min(pos, vlo + per);
   double acc = -0.0;
-  for (int chk = 0; chk < nk && landed; ++chk) {
-    const int g = nk + chk;
-    landed = csync_and(mbar_wait_bounded(&kvbar[g % nbuf], par(g), c.status));
-    if (!landed) break;
-    ++waited;
-    const int p0 = lo + chk * kFChunk, count = min(kFChunk, hi - p0);
-    const uint8_t *rows = kvbuf + (size_t)(g % nbuf) * kFChunk * rb;
-    if (i < hd)
-      for (int pp = 0; pp < count; ++pp)
-        acc += (double)__fmul_rn(scores[p0 + pp - lo],
-                                 value_staged(rows + (size_t)pp * rb, hd, a.q8, i));
+  for (int k0 = 0; k0 < nv; k0 += 2) {
+    const int k1 = min(k0 + 1, nv - 1);
+    cp_async_wait_pending(ng - 1 - (nk + k1));
     csync();
-    if (g + nbuf < 2 * nk) {
-      if (warp == 0) {
-        fence_proxy_async_smem();
-        issue(g + nbuf);
+    if (i < kAttnThreads) {
+      for (int k = k0; k <= k1; ++k) {
+        const uint8_t *vb = slots + (size_t)((nk + k) % kFAttnSlots) * kFAttnSlot;
+        const int p0 = vlo + k * kFVDepth, count = min(kFVDepth, vhi - p0);
+        if (a.q8) {
+          const uint32_t *sw = reinterpret_cast<const uint32_t *>(vb + 8 * kFVDepth * 32);
+          for (int t = 0; t < count; ++t) {
+            const int slot = vr * kFVDepth + t;
+            const uint32_t word = sw[slot];
+            const float d = half_bits_to_float((uint16_t)(rank & 1 ? word >> 16 : word));
+            const float v = __fmul_rn(d, (float)(int8_t)vb[slot * 32 + dl]);
+            acc += (double)__fmul_rn(pr[p0 + t], v);
+          }
+        } else {
+          for (int t = 0; t < count; ++t) {
+            const int slot = vr * kFVDepth + t;
+            const float v =
+                half_bits_to_float(reinterpret_cast<const uint16_t *>(vb + slot * 64)[dl]);
+            acc += (double)__fmul_rn(pr[p0 + t], v);
+          }
+        }
       }
-      ++issued;
     }
+    csync();  // the slots are free again
+    for (int k = k0; k <= k1; ++k) refill(nk + k);
   }
-  if (!landed) {
-    drain();
-    if (i == 0) flow_raise(c);
-    return false;
-  }
-  uint64_t *part = a.part + ((long)h * kAttnSplit + rank) * hd * 2;
-  if (i < hd) {
-    const unsigned long long bits = (unsigned long long)__double_as_longlong(acc);
-    st_word(part + 2 * i, tagged_u((uint32_t)bits, tag));
-    st_word(part + 2 * i + 1, tagged_u((uint32_t)(bits >> 32), tag));
-  }
-  // every buffer's barrier completed its uses of this phase
-  if (i == 0)
-    for (int b = 0; b < nbuf; ++b)
-      rg.kvuse[b] = base[b] + (uint32_t)((2 * nk - b + nbuf - 1) / nbuf);
-  // the gate values sit in threads hd .. hd + dims: hand them over
-  if (i >= hd && i < hd + dims) buf[i - hd] = gate;
+  if (i < kAttnThreads) part[vr * 32 + dl] = acc;
   csync();
-  // CTA r finalises dimensions [r*dims, (r+1)*dims), ranks in order
-  ok = true;
+  if (tr) tr[9] = global_timer_ns();
+  // this CTA's output dimensions: the shares in rank order, the current
+  // position, the gate
   if (i < dims) {
     const int d = rank * dims + i;
     double sum = -0.0;
-    for (int r = 0; r < kAttnSplit && ok; ++r) {
-      const uint64_t *pr = a.part + ((long)h * kAttnSplit + r) * hd * 2 + 2 * d;
-      uint64_t w0 = 0, w1 = 0;
-      ok = wait_word(pr, tag, w0, c) && wait_word(pr + 1, tag, w1, c);
-      sum += word_pair_value(w0, w1);
-    }
+    for (int r = 0; r < kAttnSplit; ++r) sum += part[r * 32 + i];
     const float out = (float)(sum + (double)__fmul_rn(p_cur, vc[d]));
-    if (ok) st_word(a.out + (long)h * hd + d, tagged(__fmul_rn(out, sigmoid_f(buf[i])), tag));
+    st_word(a.out + (long)h * hd + d, tagged(__fmul_rn(out, sigmoid_f(gs[i])), tag));
   }
-  return csync_and(ok);
+  return true;
 }
 
 // ---- the kernel --------------------------------------------------------------------
@@ -1249,19 +1428,18 @@ __global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
   FRing rg;
   rg.data = smem;
   rg.bar = reinterpret_cast<uint64_t *>(smem + kFOffBars);
-  uint64_t *dbar = rg.bar + kFSlots;  // [kFDescBufs] descriptor arrivals, then attention K/V [4]
+  uint64_t *dbar = rg.bar + kFSlots;  // [kFDescBufs] descriptor arrivals
   rg.off = reinterpret_cast<uint32_t *>(smem + kFOffMeta);
   rg.len = rg.off + kFSlots;
   rg.tail = rg.len + kFSlots;
   rg.released = rg.tail + 1;
   rg.issued = rg.tail + 2;
   rg.issued_live = rg.tail + 3;
-  rg.kvuse = rg.tail + 4;
   rg.desc_done = rg.tail + 8;
   rg.desc_fetched = rg.tail + 9;
   rg.issue_ts = reinterpret_cast<unsigned long long *>(smem + kFOffIssue);
   const int tid = threadIdx.x;
-  if (tid < kFSlots + kFDescBufs + 4) mbar_init(&rg.bar[tid], 1);
+  if (tid < kFSlots + kFDescBufs) mbar_init(&rg.bar[tid], 1);
   if (tid < 16) rg.tail[tid] = 0u;
   mbar_init_fence();
   __syncthreads();
@@ -1300,16 +1478,12 @@ __global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
   } else {
     // the compute warps: descriptor p arrives in buffer p % D
     int cons = 0, waited = 0;
+    // descriptor p + 1 is awaited (thread 511) inside phase p's closing barrier
+    ok = csync_and(tid != kFThreads - 1 || mbar_wait_bounded(&dbar[0], 0u, c.status));
+    if (!ok && tid == 0) flow_raise(c);
     for (int p = 0; p < fa.nphases && ok; ++p) {
       unsigned long long *tr = fa.trace && blockIdx.x == 0 && tid == 0 ? fa.trace + 16 * p : nullptr;
-      if (tr) tr[5] = global_timer_ns();
-      ok = csync_and(tid != kFThreads - 1 ||
-                     mbar_wait_bounded(&dbar[p % D], (unsigned)(p / D) & 1u, c.status));
-      if (tr) tr[0] = global_timer_ns();
-      if (!ok) {
-        if (tid == 0) flow_raise(c);
-        break;
-      }
+      if (tr) tr[5] = tr[0] = global_timer_ns();
       waited = p + 1;
       const FPhase &ph = *reinterpret_cast<const FPhase *>(smem + kFOffDesc + (p % D) * kFDescBytes);
       if (tr) tr[6] = global_timer_ns();
@@ -1328,10 +1502,14 @@ __global__ void __launch_bounds__(kFBlock, 1) decode_flow_kernel(FlowArgs fa) {
           ok = flow_gdn(ph.gd, pos, smem, ep, tag, c);
           break;
         default:
-          ok = flow_attn(ph.at, pos, smem, rg, ep, tag, c);
+          ok = flow_attn(ph.at, pos, smem, ep, tag, c, tr);
           break;
       }
-      ok = csync_and(ok);
+      const bool next = tid != kFThreads - 1 || p + 1 >= fa.nphases ||
+                        mbar_wait_bounded(&dbar[(p + 1) % D], (unsigned)((p + 1) / D) & 1u,
+                                          c.status);
+      ok = csync_and(ok && next);
+      if (!ok && tid == 0) flow_raise(c);
       if (tid == 0) st_release_cta(rg.desc_done, (uint32_t)(p + 1));  // buffer p % D is free
       if (tr) tr[7] = global_timer_ns();
       if (fa.trace_cta && tid == 0)

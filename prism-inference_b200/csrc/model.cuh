@@ -90,7 +90,7 @@ struct prism_b200_model {
   uint64_t *t_hidden = nullptr, *t_mixed = nullptr, *t_z = nullptr, *t_beta = nullptr,
            *t_alpha = nullptr, *t_o = nullptr, *t_zs = nullptr, *t_proj = nullptr,
            *t_key = nullptr, *t_value = nullptr, *t_att = nullptr, *t_up = nullptr,
-           *t_smax = nullptr, *t_stot = nullptr, *t_part = nullptr;
+           *t_scores = nullptr;
   prism::PrefillBuffers pre;
   std::map<std::string, bool> bound;
   std::vector<void *> allocations;
@@ -745,9 +745,8 @@ inline std::vector<FPhase> build_flow_phases(prism_b200_model *m) {
       for (int j = 0; j < 3; ++j) at.sections[j] = (int)c.rope_sections[j];
       at.eps = c.eps;
       at.theta_scale = powf(c.rope_base, -2.0f / (float)c.rope_dim);
-      at.smax = m->t_smax;
-      at.stot = m->t_stot;
-      at.part = m->t_part;
+      at.sc = m->t_scores;
+      at.ctx = (int)c.context;
       at.out = m->t_att;
       P.push_back(ph);
       FPhase a3 = proj(kFF32, m->t_att, ph.k, nullptr, (int)(c.heads * c.head_dim / 256),
@@ -828,7 +827,7 @@ inline bool flow_eligible(prism_b200_model *m, const std::vector<FPhase> &P) {
   if (!coop || optin < kFSmemBytes) return false;
   if ((int)(c.heads * kAttnSplit) > sms || (int)(c.ssm_values * kGdnSlices) > sms) return false;
   if (c.ssm_state != 128 || c.head_dim != 256 || c.conv_kernel > 8) return false;
-  if ((c.context + kAttnSplit - 1) / kAttnSplit + 1 > (uint32_t)kFMaxScores) return false;
+  if (c.context > (uint32_t)kFAttnMaxPos) return false;
   if (P.size() > 255) return false;  // the phase index is an 8-bit tag field
   for (const FPhase &ph : P) {
     if (ph.type != kFProj) continue;
@@ -1002,9 +1001,7 @@ int prism_b200_model_create(prism_b200_executor *ex, const prism_b200_qwen35_con
   A(m->t_value, m->kvw());
   A(m->t_att, (size_t)c.heads * c.head_dim);
   A(m->t_up, c.ffn);
-  A(m->t_smax, (size_t)c.heads * kAttnSplit);
-  A(m->t_stot, (size_t)c.heads * kAttnSplit * 2);
-  A(m->t_part, (size_t)c.heads * kAttnSplit * c.head_dim * 2);
+  A(m->t_scores, (size_t)c.heads * c.context);
   if (e == cudaSuccess) {
     // tags carry the step epoch; it starts at 1 so that no zero-filled word
     // matches, and it only grows (reset keeps it)

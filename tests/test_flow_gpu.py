@@ -112,3 +112,18 @@ def test_flow_decode_async_and_timings(monkeypatch):
                 assert total + 1e-3 >= float(np.sum(att) + np.sum(ffn))
             gm.close()
     assert outs[0] == outs[1]
+
+
+@pytest.mark.parametrize("kv_policy", [qwen35.KV_F16, qwen35.KV_Q8_0])
+def test_flow_at_the_longest_flow_context(kv_policy, monkeypatch):
+    """The small geometry at a 2048-token context after a 2000-token prompt:
+    each CTA of a head scores about 250 cached rows in eight K chunks and
+    sums every position's values in sixteen V chunks, the most the dataflow
+    attention takes."""
+    import dataclasses
+    cfg = dataclasses.replace(qwen35.SMALL, context=2048)
+    W = qwen35.synthetic_weights(cfg, seed=17)
+    prompt = qwen35.prompt_tokens(cfg, 2000, seed=18)
+    toks = qwen35.prompt_tokens(cfg, 8, seed=19)
+    compare(run("flow", cfg, W, kv_policy, toks, prompt=prompt, gen=4, monkeypatch=monkeypatch),
+            run("seq", cfg, W, kv_policy, toks, prompt=prompt, gen=4, monkeypatch=monkeypatch))

@@ -200,6 +200,72 @@ def oracle_weights(cfg, seed=0):
     return qwen35.synthetic_weights(cfg, seed=seed, generator=oracle.synth_weights)
 
 
+def phase_trace_report(model, cfg, steps=3, out=sys.stderr):
+    """Per-phase critical path of the dataflow step from its globaltimer
+    stamps (prism_b200_model_phase_trace / _phase_trace_ctas), printed as a
+    table: for each phase kind, the time from the previous phase's last CTA
+    to this phase's last CTA (mean over the layers), CTA 0's split of it,
+    and the attention phase's sub-steps.  The stamps add a few stores per
+    phase; the step traced is otherwise the timed one."""
+    import ctypes
+    L = model.L
+    for fn in ("prism_b200_model_phase_trace", "prism_b200_model_phase_trace_ctas"):
+        getattr(L, fn).restype = ctypes.c_int64
+        getattr(L, fn).argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]
+    if model.step_mode != 2:
+        print("phase trace: the dataflow step is not in use", file=out)
+        return
+    totals = []
+    for _ in range(steps):
+        totals.append(model.step_timings()[3])
+    names = ["embed"]
+    for l in range(cfg.layers):
+        names += (["attn_qkv", "attention", "attn_out"] if cfg.is_full(l)
+                  else ["gdn_proj", "gdn_rec", "gdn_out"])
+        names += ["ffn_upgate", "ffn_down"]
+    names += ["lm_head"]
+    P = len(names)
+    buf = np.zeros(16 * P, np.uint64)
+    n = L.prism_b200_model_phase_trace(model.h, buf.ctypes.data, buf.size)
+    t = buf[:n].reshape(-1, 16).astype(np.int64)
+    cb = np.zeros(P * 4 * 1024, np.uint64)
+    n2 = L.prism_b200_model_phase_trace_ctas(model.h, cb.ctypes.data, cb.size)
+    G = n2 // P // 4
+    cc = cb[:P * G * 4].reshape(P, G, 4).astype(np.int64)
+    ca, cs, ce = cc[:, :, 0], cc[:, :, 1], cc[:, :, 2]
+    us = lambda x: x / 1e3
+    print("traced steps: %s ms (one cooperative kernel per step, %d CTAs)"
+          % (", ".join("%.3f" % x for x in totals), G), file=out)
+    print("%-11s %3s %8s | %8s %8s %8s %8s %8s" % ("phase", "n", "crit_us", "arrive", "stage",
+                                                    "wgt", "dots", "chain"), file=out)
+    agg = {}
+    for i, nm in enumerate(names[1:], 1):
+        crit = us(ce[i].max() - ce[i - 1].max())
+        row = [crit]
+        if nm not in ("gdn_rec", "attention"):
+            valid = ca[i] > 0
+            arrive = us(np.median(ca[i][valid] - ce[i - 1].max())) if valid.any() else 0.0
+            c0 = t[i]
+            row += [arrive, us(c0[1] - c0[0]), us(c0[2] - c0[1]), us(c0[3] - c0[2]),
+                    us(c0[4] - c0[3])]
+        agg.setdefault(nm, []).append(row)
+    total = 0.0
+    for nm, rows in agg.items():
+        r = np.mean(np.array(rows), axis=0)
+        total += r[0] * len(rows)
+        cols = " ".join("%8.2f" % x for x in r[1:]) if len(r) > 1 else ""
+        print("%-11s %3d %8.2f | %s" % (nm, len(rows), r[0], cols), file=out)
+    print("critical path sum %.1f us" % total, file=out)
+    att = [i for i, nm in enumerate(names) if nm == "attention"]
+    if att:
+        keys = [(1, "inputs"), (2, "norm+rope"), (3, "K pass"), (4, "scores in"), (10, "max"),
+                (11, "exp"), (12, "trees"), (13, "totals"), (8, "probs"), (9, "V pass"), (7, "end")]
+        steps_ = np.array([[us(t[i, b] - t[i, a]) for (a, _), (b, _) in
+                            zip([(0, "start")] + keys[:-1], keys)] for i in att])
+        print("attention (CTA 0, mean over layers): " + ", ".join(
+            "%s %.2f" % (k[1], v) for k, v in zip(keys, steps_.mean(axis=0))), file=out)
+
+
 def cpu_matvec_baseline(seconds=10.0, threads=None):
     from oracle import oracle
     import synth
@@ -345,6 +411,8 @@ def run_decode(args):
 
     # per-layer phase timings of one more step (events between phases)
     att, ffn, head_ms, total_ms = model.step_timings()
+    if args.phase_trace and rank == 0:
+        phase_trace_report(model, cfg)
     bb = pb.BLOCK_BYTES[cfg.weight_kind]
     ffn_bytes = 3 * cfg.ffn * cfg.hidden // 256 * bb
     ffn_ms = float(np.median(ffn))
@@ -664,9 +732,18 @@ GEMM_SHAPES = [(2560, 9216), (9216, 2560)]   # (K, N): gate/up and down
 GEMM_METRIC = "prefill GEMM int-op/s (2048 tokens x Q8_K, TQ2_0 and Q2_K weights)"
 
 
-def int8_peak():
-    """Dense int8 tensor peak: not in MEASURED_PEAKS.json; B200's dense int8
-    rate is twice its dense bf16 rate, so twice the measured bf16 burst."""
+def int8_peak(ex=None):
+    """Dense int8 tensor peak: measured on this device by the library's
+    tcgen05.mma.kind::i8 microbenchmark (prism_b200_tensor_peak_i8) when an
+    executor is given; otherwise twice the measured bf16 burst (B200's dense
+    int8 rate is twice its dense bf16 rate)."""
+    if ex is not None:
+        try:
+            return ex.tensor_peak_i8(), ("measured: tcgen05.mma.kind::i8 128x256x32 back to back "
+                                         "from shared memory, one CTA per SM "
+                                         "(prism_b200_tensor_peak_i8)")
+        except Exception:
+            pass
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
@@ -736,8 +813,8 @@ def run_gemm_tp(args, world, rank, local, dev):
     e2e_s = max_over_ranks((time.perf_counter() - t0) / reps, world, dev)
     torch.distributed.barrier()
     f.close()
+    peak, peak_src = int8_peak(ex)
     ex.close()
-    peak, peak_src = int8_peak()
     line = {
         "metric": GEMM_METRIC, "value": ops / ms / 1e9, "unit": "Tint-op/s", "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -850,8 +927,8 @@ def run_gemm(args):
     for _ in range(reps):
         ex.project_f32_tokens(t, xh)
     e2e_s = max_over_ranks((time.perf_counter() - t0) / reps, world, dev)
+    peak, peak_src = int8_peak(ex)
     ex.close()
-    peak, peak_src = int8_peak()
     value = total_ops / total_ms / 1e9  # per GPU, from the max-over-ranks times
     top = results["tq2_0_K2560_N9216"]
     line = {
@@ -963,9 +1040,9 @@ def run_prefill(args):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
     model.close()
+    peak, peak_src = int8_peak(ex)
     ex.close()
 
-    peak, peak_src = int8_peak()
     ops = projection_ops(cfg) * P
     achieved = ops / (ms / K / 1e3) / 1e12
     line = {
@@ -1308,6 +1385,8 @@ def main():
                                                                 "prefill"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-matvec", action="store_true", help="skip the configs[0] sub-benchmark")
+    ap.add_argument("--phase-trace", action="store_true",
+                    help="print the dataflow step's per-phase critical path to stderr")
     ap.add_argument("--no-serve", action="store_true",
                     help="skip the decode line's serve_tp (configs[4] at tp = N) sub-object")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens (profiling runs)")

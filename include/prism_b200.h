@@ -51,6 +51,11 @@ extern "C" {
 #define PRISM_B200_KIND_Q2_K 10
 #define PRISM_B200_KIND_Q8_K 15
 #define PRISM_B200_KIND_TQ2_0 35
+/* The reference's own packed ternary formats (reference src/kernels.rs:
+ * 85-86, 178-183): 128 weights per block, PQ2 in 34 bytes (binary16 scale,
+ * then 2-bit codes), PTQ1 in 28 bytes (base-3 digits, then the scale). */
+#define PRISM_B200_KIND_PQ2 142
+#define PRISM_B200_KIND_PTQ1 143
 
 /* Native Q8_K activation block (reference tools/ternary/src/lib.rs:27-39):
  * repr(C), 292 bytes. */
@@ -59,6 +64,15 @@ typedef struct prism_b200_q8k_block {
   int8_t values[256];
   int16_t sums[16];
 } prism_b200_q8k_block;
+
+/* One Q8_0 activation block (the reference's Q8Block, src/kernels.rs:
+ * 524-535): scale (binary16-rounded) and scaled code sum as binary32, then
+ * 32 codes; 40 bytes. */
+typedef struct prism_b200_q8_block {
+  float scale;
+  float sum;
+  int8_t values[32];
+} prism_b200_q8_block;
 
 /* A packed weight tensor in the reference's byte layout
  * (reference src/model.rs:184-196 `Tensor`): `cols` = dimensions[0] (K),
@@ -103,22 +117,27 @@ int prism_b200_executor_reset(prism_b200_executor *ex);
 
 /* Eligibility from geometry alone, before any submission
  * (reference src/kernels/projection.rs:41-46 `supports`).  Returns 1 when
- * the tensor's kind is TQ2_0 or Q2_K and cols is a positive multiple of 256. */
+ * the tensor's kind is TQ2_0 or Q2_K and cols is a positive multiple of 256,
+ * or PQ2 or PTQ1 and cols is a positive multiple of 128. */
 int prism_b200_executor_supports(const prism_b200_executor *ex,
                                  const prism_b200_tensor *tensor);
 
 /* Submission count of one projection (reference
  * src/kernels/projection.rs:28-35 `operation_count`): the number of
- * 32-row x 256-column work units, or -1 when unsupported. */
+ * 32-row x 256-column work units (PQ2 / PTQ1: rows x 128-column blocks),
+ * or -1 when unsupported. */
 int64_t prism_b200_executor_operation_count(const prism_b200_executor *ex,
                                             const prism_b200_tensor *tensor);
 
 /* ---- resident weights ----------------------------------------------- */
 
 /* Validate (finite fp16 scales, exact extents) and upload a weight once;
- * it stays resident in HBM in the executor's tiled layout until released.
- * Mirrors the resident tiles of the reference's DSP executor
- * (reference docs/inference-efficiency.md:266-277). */
+ * it stays resident in HBM until released: TQ2_0 and Q2_K in the executor's
+ * tiled layout, PQ2 and PTQ1 as uploaded.  Mirrors the resident tiles of
+ * the reference's DSP executor (reference docs/inference-efficiency.md:
+ * 266-277).  PQ2 and PTQ1 weights serve prism_b200_project,
+ * _project_device, _project_q8 and _project_f32; the other projections
+ * refuse them with PRISM_B200_E_UNSUPPORTED. */
 int prism_b200_weight_upload(prism_b200_executor *ex,
                              const prism_b200_tensor *tensor,
                              prism_b200_weight **out);
@@ -128,10 +147,12 @@ void prism_b200_weight_release(prism_b200_weight *w);
 
 /* y = W x over already quantized Q8_K activations
  * (reference src/kernels/projection.rs:48-60 `project`; per-row arithmetic
- * of src/kernels/tquants.rs:270-287 and src/kernels/kquants.rs:346-420).
- * `activation` holds cols/256 blocks; `out` receives rows floats.
- * `fused` selects the PQ2 fused multiply-add contract in the reference and
- * has no effect on TQ2_0 / Q2_K, whose reference dots have one order. */
+ * of src/kernels/tquants.rs:270-287, src/kernels/kquants.rs:346-420 and,
+ * for PQ2, src/kernels.rs:941-959).  `activation` holds cols/256 blocks;
+ * `out` receives rows floats.  `fused` selects the PQ2 fused multiply-add
+ * contract and has no effect on TQ2_0 / Q2_K, whose reference dots have one
+ * order.  PTQ1, and PQ2 whose cols is not a multiple of 256, take Q8_0
+ * activations instead: PRISM_B200_E_UNSUPPORTED, `out` zero-filled. */
 int prism_b200_project(prism_b200_executor *ex, const prism_b200_weight *w,
                        const prism_b200_q8k_block *activation, int fused,
                        float *out);
@@ -144,7 +165,9 @@ int prism_b200_project_device(prism_b200_executor *ex,
  * (reference src/kernels.rs:1935-1987 `MatvecScratch::prepare` followed by
  * `PreparedMatvec::matvec_into`; src/kernels/projection.rs:95-107
  * `project_f32`).  `pinned` selects the pinned fused Q8_K rounding
- * (reference src/kernels.rs:421-428); 0 is the Source contract. */
+ * (reference src/kernels.rs:421-428); 0 is the Source contract.  PQ2 and
+ * PTQ1 quantize by their activation contract (Q8_K for PQ2 with a multiple
+ * of 256 columns, else Q8_0) and dot unfused; `pinned` is refused there. */
 int prism_b200_project_f32(prism_b200_executor *ex, const prism_b200_weight *w,
                            const float *x, int pinned, float *out);
 
@@ -189,10 +212,13 @@ int prism_b200_executor_supports_f32_group(const prism_b200_executor *ex, size_t
 
 /* Q8_0 activations (reference src/kernels/projection.rs:62-90
  * `supports_q8` / `project_q8`), which the reference routes for PTQ1 and
- * odd-block PQ2 rows only.  TQ2_0 and Q2_K take Q8_K activations, so
- * supports_q8 returns 0 and project_q8 returns PRISM_B200_E_UNSUPPORTED
- * (the reference trait's default) with `out` zero-filled; the executor
- * stays open. */
+ * odd-block PQ2 rows: `activation` holds cols/32 prism_b200_q8_block; per
+ * 128-weight block the four groups' scale x integer dot are summed in
+ * binary32, then output += scale x sum (src/kernels.rs:1043-1063).  TQ2_0
+ * and Q2_K take Q8_K activations, so supports_q8 returns 0 for them and
+ * project_q8 returns PRISM_B200_E_UNSUPPORTED (the reference trait's
+ * default) with `out` zero-filled; the executor stays open.  `pinned`
+ * (the native PTQ1 lane order) is refused the same way. */
 int prism_b200_executor_supports_q8(const prism_b200_executor *ex,
                                     const prism_b200_tensor *tensor);
 int prism_b200_project_q8(prism_b200_executor *ex, const prism_b200_weight *w,
@@ -407,29 +433,21 @@ int prism_b200_model_finalize(prism_b200_model *m);
 int prism_b200_model_reset(prism_b200_model *m);
 int64_t prism_b200_model_position(const prism_b200_model *m);
 
-/* 1 when a step runs as one persistent cooperative kernel (the dataflow
- * step, or the barrier-synchronised one), 0 when it runs as the per-phase
- * kernel sequence.  All give the same bits.  No counterpart in the
- * reference. */
+/* 1 when a step runs as one cooperative kernel (the dataflow step), 0 when
+ * it runs as the per-phase kernel sequence.  Both give the same bits.  No
+ * counterpart in the reference. */
 int prism_b200_model_persistent(const prism_b200_model *m);
 
-/* How a decode step runs, chosen at finalize from PRISM_B200_STEP
- * ("flow", "seq" or "persist"): 2 = the dataflow kernel (one cooperative
- * launch per token; activations carry a per-step tag that their consumers
- * poll, weights stream through a shared-memory ring ahead of the compute),
- * 1 = the barrier-synchronised persistent kernel, 0 = the per-phase kernel
- * sequence in a CUDA graph.  -1 for a NULL model.  No counterpart in the
+/* How a decode step runs, chosen at finalize: 2 = the dataflow kernel (one
+ * cooperative launch per token; activations carry a per-step tag that their
+ * consumers poll, weights stream through a shared-memory ring ahead of the
+ * compute), the default wherever the model and device are eligible; 0 = the
+ * per-phase kernel sequence in a CUDA graph (PRISM_B200_STEP=seq, or an
+ * ineligible model).  -1 for a NULL model.  No counterpart in the
  * reference. */
 int prism_b200_model_step_mode(const prism_b200_model *m);
 
-/* CTA 0's timeline of the last prism_b200_model_step_timings step of a
- * persistent model, 8 values per phase: [0] start (barrier passed) and
- * [7] end (arrival at the next barrier) in globaltimer ns; [5] start,
- * [1] inputs staged, [2] first tiles resident, [3] their dots done,
- * [4] their chains done in SM clock cycles (projection phases only).
- * Phases: embedding, then per layer three attention-side phases and the FFN
- * pair, then the LM head.
- * For the kernel-sequence step, with PRISM_B200_TRACE=1 set before the
+/* For the kernel-sequence step, with PRISM_B200_TRACE=1 set before the
  * model is finalized: the last step's per-launch timelines in globaltimer
  * ns, 8 values per launch (per layer: projection group, GDN or attention,
  * out-projection, FFN pair, FFN down; then the LM head): CTA 0's [0] entry,
@@ -437,13 +455,17 @@ int prism_b200_model_step_mode(const prism_b200_model *m);
  * [4] its dots, [5] its chains, [6] exit, and [7] the last CTA's exit
  * (projections; GDN and attention stamp [0], [1], [6], [7]).
  * For the dataflow step (mode 2): CTA 0's stamps of the last
- * prism_b200_model_step_timings step, 16 values per phase in the same phase
- * order, globaltimer ns unless noted: [5] before the descriptor wait,
- * [0] descriptor resident, [6] next descriptor requested, [1] input staged,
- * [2] first batch's weights resident, [3] its dots, [4] its chains,
- * [7] phase end; projections also [8] before the weight wait, [9] after it,
- * [10] pieces the weight stream was ahead (a count), [11] issue time of the
- * batch's last piece, [12] pieces in the batch (a count).
+ * prism_b200_model_step_timings step, 16 values per phase (embedding, then
+ * per layer three attention-side phases and the FFN pair, then the LM head),
+ * globaltimer ns unless noted: [5] and [0] phase start, [6] descriptor read,
+ * [7] phase end.  Projections: [1] input staged, [2] first batch's weights
+ * resident, [3] its dots, [4] its chains, [8] before the weight wait, [9]
+ * after it, [11] issue time of the batch's last piece, [12] pieces in the
+ * batch (a count).  Attention: [1] inputs arrived, [2] query and key
+ * normed, rotated and cached, [14] first K rows resident, [15] their
+ * scores, [3] the share's scores, [4] every position's scores resident,
+ * [10] softmax maximum, [11] exponentials, [12] share trees, [13] share
+ * totals, [8] probabilities, [9] value sums.
  * Copies at most `count` values and returns how many (0 when no timeline
  * is recorded).  No counterpart in the reference. */
 int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t count);
@@ -451,10 +473,10 @@ int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t c
 /* Dataflow step only: every CTA's globaltimer stamps of the last
  * prism_b200_model_step_timings step, [phase][CTA][4] (grid = the SM
  * count): inputs arrived and input staged (projection phases, else 0),
- * phase end, and a spare 0, so that a phase's critical path (its slowest
- * CTA) can be read.  Copies at
- * most `count` values and returns how many (0 for other step modes).  No
- * counterpart in the reference. */
+ * phase end, and the end of the phase's first weight-batch planning
+ * (projection phases, else 0), so that a phase's critical path (its slowest
+ * CTA) can be read.  Copies at most `count` values and returns how many (0
+ * for the kernel sequence).  No counterpart in the reference. */
 int64_t prism_b200_model_phase_trace_ctas(prism_b200_model *m, uint64_t *ns, size_t count);
 
 /* One token at the next position (reference Decoder::evaluate_finite_into,
@@ -607,6 +629,12 @@ uint64_t prism_b200_weight_cols(const prism_b200_weight *w);
 /* Bytes the weight occupies in HBM (equal to its packed byte size plus the
  * zero padding of the last 32-row tile). */
 uint64_t prism_b200_weight_device_bytes(const prism_b200_weight *w);
+
+/* Measured dense int8 tensor-core rate of the executor's device, in
+ * Tint-op/s (2 per multiply-add): one CTA per SM issues `iters` back-to-back
+ * tcgen05.mma.kind::i8 of 128x256x32 from shared memory.  No reference
+ * counterpart; the denominator of the prefill GEMM's tensor roofline. */
+int prism_b200_tensor_peak_i8(prism_b200_executor *ex, int iters, double *tops);
 
 #ifdef __cplusplus
 }

@@ -46,6 +46,13 @@ def _declare(L):
         "po_float_to_half": (ctypes.c_uint16, [f32]),
         "po_q8k_quantize": (i32, [vp, sz, i32, vp]),
         "po_q8_0_quantize": (i32, [vp, sz, vp]),
+        "po_pq2_values": (None, [vp, vp]),
+        "po_ptq1_values": (None, [vp, vp]),
+        "po_packed_uses_q8k": (i32, [u32, sz]),
+        "po_pq2_dot_q8k": (i32, [vp, sz, vp, i32, vp]),
+        "po_packed_dot_q8": (i32, [u32, vp, sz, vp, vp]),
+        "po_packed_matvec": (i32, [u32, vp, sz, sz, vp, i32, vp]),
+        "po_packed_row": (i32, [u32, vp, sz, sz, vp]),
         "po_tq2_decode": (i32, [vp, sz, vp]),
         "po_tq2_quantize": (i32, [vp, sz, vp]),
         "po_tq2_block_dots": (i32, [vp, vp, sz, vp]),
@@ -96,6 +103,57 @@ def q8_0_quantize(x):
 
 def block_bytes(kind):
     return {35: 66, 10: 84}[kind]
+
+
+# ---- PQ2 (142) and PTQ1 (143): 128 weights per block --------------------
+PACKED_BLOCK_BYTES = {142: 34, 143: 28}
+
+
+def packed_values(kind, block):
+    """The 128 weights (-1..2) of one PQ2 or PTQ1 block."""
+    b = np.ascontiguousarray(block, dtype=np.uint8)
+    out = np.zeros(128, np.int16)
+    (lib().po_pq2_values if kind == 142 else lib().po_ptq1_values)(_p(b), _p(out))
+    return out
+
+
+def packed_uses_q8k(kind, cols):
+    """The reference's activation contract: Q8_K for PQ2 with a multiple of
+    256 columns, Q8_0 otherwise."""
+    return bool(lib().po_packed_uses_q8k(kind, cols))
+
+
+def pq2_dot_q8k(weights_row, act, fused=False):
+    w = np.ascontiguousarray(weights_row, dtype=np.uint8)
+    a = np.ascontiguousarray(act, dtype=Q8K_DTYPE)
+    out = np.zeros(1, np.float32)
+    _check(lib().po_pq2_dot_q8k(_p(w), w.size // 34, _p(a), int(fused), _p(out)))
+    return out[0]
+
+
+def packed_dot_q8(kind, weights_row, act):
+    w = np.ascontiguousarray(weights_row, dtype=np.uint8)
+    a = np.ascontiguousarray(act, dtype=Q8_0_DTYPE)
+    out = np.zeros(1, np.float32)
+    _check(lib().po_packed_dot_q8(kind, _p(w), w.size // PACKED_BLOCK_BYTES[kind], _p(a), _p(out)))
+    return out[0]
+
+
+def packed_matvec(kind, weights, rows, cols, x, fused=False):
+    """y = W x for a PQ2 or PTQ1 tensor [rows][cols], x quantized by the
+    activation contract of (kind, cols)."""
+    w = np.ascontiguousarray(weights, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.zeros(rows, np.float32)
+    _check(lib().po_packed_matvec(kind, _p(w), rows, cols, _p(x), int(fused), _p(y)))
+    return y
+
+
+def packed_row(kind, weights, cols, r):
+    w = np.ascontiguousarray(weights, dtype=np.uint8)
+    out = np.zeros(cols, np.float32)
+    _check(lib().po_packed_row(kind, _p(w), cols, r, _p(out)))
+    return out
 
 
 def decode(kind, packed):

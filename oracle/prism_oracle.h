@@ -106,6 +106,22 @@ int po_block_bytes(uint32_t kind);
 int po_project_tokens(uint32_t kind, const uint8_t *w, size_t rows, size_t cols,
                       const float *x, size_t tokens, int pinned, float *y, int threads);
 
+/* ---- PQ2 (type 142, 34 B / 128 weights) and PTQ1 (type 143, 28 B) --
+ * (packed_oracle.c).  Decoders give the 128 weights of a block (-1..2);
+ * dots follow the reference's Q8_K and Q8_0 contracts; the matvec
+ * quantizes x by the contract of (kind, cols) and dots every row. */
+void po_pq2_values(const uint8_t *block, int16_t *out);
+void po_ptq1_values(const uint8_t *block, int16_t *out);
+int po_packed_block_bytes(uint32_t kind);
+int po_packed_uses_q8k(uint32_t kind, size_t cols);
+int po_pq2_dot_q8k(const uint8_t *w, size_t nblocks, const po_q8k_block *a, int fused,
+                   float *out);
+int po_packed_dot_q8(uint32_t kind, const uint8_t *w, size_t nblocks, const po_q8_0_block *a,
+                     float *out);
+int po_packed_matvec(uint32_t kind, const uint8_t *w, size_t rows, size_t cols, const float *x,
+                     int fused, float *y);
+int po_packed_row(uint32_t kind, const uint8_t *w, size_t cols, size_t r, float *out);
+
 /* ---- float primitives (Source contract) ----------------------------- */
 float po_float_dot(const float *a, const float *b, size_t n);
 float po_f16_dot(const float *a, const uint16_t *b, size_t n);

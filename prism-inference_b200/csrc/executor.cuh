@@ -23,6 +23,7 @@ struct DeviceWeight {
   int nb = 0, h = 32, ntiles = 0;
   uint8_t *units = nullptr;
   uint64_t bytes = 0;   // device bytes of the tiled layout
+  bool packed = false;  // PQ2 / PTQ1 rows as uploaded (packed.cuh), not tiled
 };
 
 // The double-buffered tile must also fit the 227 KB shared-memory budget.

@@ -42,7 +42,7 @@
 #include "common.cuh"
 #include "matvec.cuh"
 #include "model_kernels.cuh"
-#include "persist.cuh"
+#include "gdn_decode.cuh"
 
 namespace prism {
 
@@ -156,7 +156,7 @@ struct FlowArgs {
   unsigned long long *key;  // the LM head's greedy key while the step runs
   unsigned *status;
   unsigned long long *trace;  // optional: [16 * phase] CTA 0's globaltimer stamps
-  unsigned long long *trace_cta;  // optional: [phase][CTA][4] inputs arrived, staged, end
+  unsigned long long *trace_cta;  // optional: [phase][CTA][4] inputs arrived, staged, end, planned
 };
 
 // ---- small helpers -------------------------------------------------------------
@@ -760,6 +760,7 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
     pl_n[3] = n;
     byte_cap = total + maxpiece <= (uint32_t)kFRing ? total : ((uint32_t)kFRing - maxpiece) / 2;
     plan_ok = plan(0, cons);
+    if (ts) ts[3] = global_timer_ns();
   }
 
   // 1. the Q8_K activation

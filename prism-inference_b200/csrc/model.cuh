@@ -17,7 +17,7 @@
 #include "executor.cuh"
 #include "flow.cuh"
 #include "model_kernels.cuh"
-#include "persist.cuh"
+#include "gdn_decode.cuh"
 
 namespace prism {
 
@@ -66,20 +66,11 @@ struct prism_b200_model {
   int64_t position = 0;
   cudaStream_t stream = nullptr;
   cudaGraphExec_t g_ingest = nullptr, g_decode = nullptr;
-  // persistent step (persist.cuh): phase list, barrier words, exchange buffers
-  bool persist = false;
-  prism::Phase *d_phases = nullptr;
-  prism::PTiles *d_ptiles = nullptr;
-  int nphases = 0, nphases_ingest = 0;
-  unsigned *d_sync = nullptr, *d_hsync = nullptr;
-  int nhsync = 0;
-  unsigned long long *d_trace = nullptr;  // [8 * phases] of a traced step
   // per-kernel timelines of the kernel-sequence step (PRISM_B200_TRACE=1 set
   // before finalize): [8 * launches], projection / GDN / attention launches
   unsigned long long *d_seqtrace = nullptr;
   int nseqtrace = 0;
-  float *gdn_o = nullptr, *smax = nullptr;
-  double *stot = nullptr, *apart = nullptr;
+  float *gdn_o = nullptr;
   // the dataflow step (flow.cuh): phase list, tagged activations, step words
   bool flow = false;
   prism::FPhase *d_fphases = nullptr;
@@ -111,17 +102,12 @@ struct prism_b200_model {
 
 namespace prism {
 
-// The step mode: PRISM_B200_STEP=flow|seq|persist; without it the kernel
-// sequence, or the barrier-synchronised persistent step with
-// PRISM_B200_PERSIST=1.
+// The step mode: the dataflow step (2) where the model and device are
+// eligible, else the kernel sequence (0); PRISM_B200_STEP=seq selects the
+// kernel sequence.
 inline int step_mode_request() {
   const char *e = getenv("PRISM_B200_STEP");
-  if (e && !strcmp(e, "seq")) return 0;
-  if (e && !strcmp(e, "persist")) return 1;
-  if (e && !strcmp(e, "flow")) return 2;
-  const char *p = getenv("PRISM_B200_PERSIST");
-  if (p && p[0] == '1') return 1;
-  return 0;
+  return e && !strcmp(e, "seq") ? 0 : 2;
 }
 
 // Dynamic shared memory of an attention_decode_kernel launch over a cache of
@@ -376,7 +362,7 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
       g.status = status;
       // each value head over kGdnSlices CTAs of 16 state rows
       cudaLaunchConfig_t cfg =
-          pdl_config(dim3(c.ssm_values * kGdnSlices), dim3(kPThreads), 0, s, attr, pdl);
+          pdl_config(dim3(c.ssm_values * kGdnSlices), dim3(kGdnThreads), 0, s, attr, pdl);
       if ((e = cudaLaunchKernelEx(&cfg, gdn_slices_kernel, g)) != cudaSuccess) return e;
       ++item;
       MvArgs o;
@@ -433,228 +419,6 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
   e = cudaLaunchKernelEx(&cfg, finish_step_kernel, step_state(m), head ? 1 : 0);
   mark(3 + 2 * nl);
   return e;
-}
-
-// ---- the persistent step (persist.cuh) ---------------------------------------
-
-// Phase list of one step: embedding; per layer the attention-side phases
-// and the FFN pair; the LM head last (the ingest list stops before it).
-inline std::vector<Phase> build_phases(prism_b200_model *m) {
-  const auto &c = m->cfg;
-  unsigned *status = m->ex->d_status;
-  std::vector<Phase> P;
-  auto blank = [] {
-    Phase ph{};
-    return ph;
-  };
-  auto matvec = [&](int prologue, const float *in, const float *norm_w, int nb,
-                    std::initializer_list<MvWeight> ws, int epi) {
-    Phase ph = blank();
-    ph.type = kPhMatvec;
-    PMatvec &mv = ph.mv;
-    mv.prologue = prologue;
-    mv.in = in;
-    mv.norm_w = norm_w;
-    mv.eps = c.eps;
-    mv.nb = nb;
-    mv.epi = epi;
-    mv.count = 0;
-    mv.tile_start[0] = 0;
-    for (const MvWeight &w : ws) {
-      mv.w[mv.count] = w;
-      mv.tile_start[mv.count + 1] = mv.tile_start[mv.count] + w.ntiles;
-      ++mv.count;
-    }
-    for (int g = mv.count; g < kMaxGroup; ++g) mv.tile_start[g + 1] = mv.tile_start[mv.count];
-    mv.ntiles = epi == kEpiSwiglu ? mv.w[0].ntiles : mv.tile_start[mv.count];
-    return ph;
-  };
-  {
-    Phase ph = blank();
-    ph.type = kPhEmbed;
-    ph.em.units = m->embd.units;
-    ph.em.h = m->embd.h;
-    ph.em.nb = m->embd.nb;
-    ph.em.vocab = (int)c.vocab;
-    ph.em.n = (int)c.hidden;
-    ph.em.hidden = m->hidden;
-    P.push_back(ph);
-  }
-  const int hnb = (int)(c.hidden / 256);
-  int ai = 0;
-  for (auto &Ly : m->L) {
-    if (Ly.full) {
-      P.push_back(matvec(kPPRms, m->hidden, Ly.attn_norm, hnb,
-                         {mv_weight(Ly.q, m->projected), mv_weight(Ly.k, m->key),
-                          mv_weight(Ly.v, m->value)},
-                         kEpiStore));
-      Phase ph = blank();
-      ph.type = kPhAttn;
-      AttnArgs &aa = ph.at.a;
-      aa.heads = (int)c.heads;
-      aa.kv_heads = (int)c.kv_heads;
-      aa.hd = (int)c.head_dim;
-      aa.rope_dim = (int)c.rope_dim;
-      for (int j = 0; j < 3; ++j) aa.sections[j] = (int)c.rope_sections[j];
-      aa.eps = c.eps;
-      aa.theta_scale = powf(c.rope_base, -2.0f / (float)c.rope_dim);
-      aa.projected = m->projected;
-      aa.key_in = m->key;
-      aa.value_in = m->value;
-      aa.q_norm = Ly.q_norm;
-      aa.k_norm = Ly.k_norm;
-      aa.kcache = Ly.kc;
-      aa.vcache = Ly.vc;
-      aa.q8 = c.kv_policy == PRISM_B200_KV_Q8_0 ? 1 : 0;
-      aa.position = m->d_position;
-      aa.attended = m->attended;
-      aa.status = status;
-      ph.at.smax = m->smax;
-      ph.at.stot = m->stot;
-      ph.at.part = m->apart;
-      ph.at.hsync = m->d_hsync + (size_t)ai * c.heads;
-      ++ai;
-      P.push_back(ph);
-      P.push_back(matvec(kPPF32, m->attended, nullptr, (int)(c.heads * c.head_dim / 256),
-                         {mv_weight(Ly.o, m->hidden, m->hidden)}, kEpiStore));
-    } else {
-      P.push_back(matvec(kPPRms, m->hidden, Ly.attn_norm, hnb,
-                         {mv_weight(Ly.qkv, m->mixed), mv_weight(Ly.z, m->zgate),
-                          mv_weight(Ly.beta, m->beta), mv_weight(Ly.alpha, m->alpha)},
-                         kEpiStore));
-      Phase ph = blank();
-      ph.type = kPhGdn;
-      GdnArgs &g = ph.gdn;
-      g.S = (int)c.ssm_state;
-      g.groups = (int)c.ssm_groups;
-      g.values = (int)c.ssm_values;
-      g.conv_k = (int)c.conv_kernel;
-      g.eps = c.eps;
-      g.mixed = m->mixed;
-      g.zgate = m->zgate;
-      g.beta_in = m->beta;
-      g.alpha_in = m->alpha;
-      g.conv_w = Ly.conv_w;
-      g.dt_bias = Ly.dt_bias;
-      g.ssm_a = Ly.ssm_a;
-      g.norm_w = Ly.ssm_norm;
-      g.conv_state = Ly.conv_state;
-      g.conv_buf_stride = (long)m->channels() * (c.conv_kernel - 1);
-      g.state = Ly.matrix;
-      g.attended = m->gdn_o;  // pre-norm output; the next phase applies the gated norm
-      g.position = m->d_position;
-      g.status = status;
-      P.push_back(ph);
-      Phase o = matvec(kPPGated, m->gdn_o, Ly.ssm_norm, m->value_width() / 256,
-                       {mv_weight(Ly.out, m->hidden, m->hidden)}, kEpiStore);
-      o.mv.zgate = m->zgate;
-      o.mv.gated_out = m->attended;
-      o.mv.heads = (int)c.ssm_values;
-      o.mv.head_dim = (int)c.ssm_state;
-      P.push_back(o);
-    }
-    MvWeight upw = mv_weight(Ly.up, m->up);
-    P.push_back(matvec(kPPRms, m->hidden, Ly.post_norm, hnb, {upw, mv_weight(Ly.gate, nullptr)},
-                       kEpiSwiglu));
-    P.push_back(matvec(kPPF32, m->up, nullptr, (int)(c.ffn / 256),
-                       {mv_weight(Ly.down, m->hidden, m->hidden)}, kEpiStore));
-  }
-  Phase hd = matvec(kPPRms, m->hidden, m->out_norm, hnb, {mv_weight(m->embd, m->logits)},
-                    kEpiArgmax);
-  hd.mv.argmax_key = m->d_argmax;
-  P.push_back(hd);
-  return P;
-}
-
-// Whether this model and device fit the persistent step's fixed limits.
-inline bool persist_eligible(prism_b200_model *m, const std::vector<Phase> &P) {
-  const auto &c = m->cfg;
-  if (step_mode_request() != 1) return false;  // opt-in
-  const int sms = m->ex->num_sms;
-  int coop = 0, optin = 0;
-  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->ex->device);
-  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->ex->device);
-  if (!coop || optin < kPSmemBytes) return false;
-  if ((int)(c.heads * kAttnSplit) > sms || (int)(c.ssm_values * kGdnSlices) > sms) return false;
-  if (c.ssm_state != 128 || c.head_dim != 256 || c.ssm_values * c.ssm_state > 2048) return false;
-  if ((c.context + kAttnSplit - 1) / kAttnSplit > (uint32_t)kPMaxScores) return false;
-  for (const Phase &ph : P) {
-    if (ph.type != kPhMatvec) continue;
-    for (int g = 0; g < ph.mv.count; ++g) {
-      const long tile = (long)ph.mv.nb * unit_bytes((int)c.weight_kind, ph.mv.w[g].h) *
-                        (ph.mv.epi == kEpiSwiglu ? 2 : 1);
-      if (tile > kRingBytes / 2) return false;
-    }
-  }
-  return true;
-}
-
-inline cudaError_t prepare_persistent(prism_b200_model *m) {
-  std::vector<Phase> P = build_phases(m);
-  m->persist = persist_eligible(m, P);
-  if (!m->persist) return cudaSuccess;
-  if (!m->d_phases) {
-    // a model's layer count, and so its phase count, is fixed at creation
-    cudaError_t e = model_alloc(m, &m->d_phases, P.size());
-    if (e == cudaSuccess) e = model_alloc(m, &m->d_ptiles, P.size());
-    if (e == cudaSuccess) e = model_alloc(m, &m->d_trace, 8 * P.size());
-    if (e != cudaSuccess) return e;
-  }
-  m->nphases = (int)P.size();
-  m->nphases_ingest = m->nphases - 1;
-  std::vector<PTiles> plan(P.size());
-  for (size_t i = 0; i < P.size(); ++i) {
-    PTiles &t = plan[i];
-    memset(&t, 0, sizeof(t));
-    if (P[i].type != kPhMatvec) continue;
-    const PMatvec &mv = P[i].mv;
-    t.ntiles = mv.ntiles;
-    t.count = mv.count;
-    t.pair = mv.epi == kEpiSwiglu ? 1 : 0;
-    for (int g = 0; g <= kMaxGroup; ++g) t.tile_start[g] = mv.tile_start[g];
-    for (int g = 0; g < mv.count; ++g) {
-      t.units[g] = mv.w[g].units;
-      t.part[g] = mv.nb * unit_bytes((int)m->cfg.weight_kind, mv.w[g].h);
-    }
-  }
-  cudaError_t e = cudaMemcpy(m->d_phases, P.data(), P.size() * sizeof(Phase),
-                             cudaMemcpyHostToDevice);
-  if (e == cudaSuccess)
-    e = cudaMemcpy(m->d_ptiles, plan.data(), plan.size() * sizeof(PTiles),
-                   cudaMemcpyHostToDevice);
-  if (e != cudaSuccess) return e;
-  void *k35 = (void *)decode_persistent_kernel<35>, *k10 = (void *)decode_persistent_kernel<10>;
-  e = cudaFuncSetAttribute(k35, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k10, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
-  return e;
-}
-
-// One cooperative launch: the whole step.
-inline cudaError_t launch_persistent(prism_b200_model *m, bool head, bool trace = false) {
-  PersistArgs pa;
-  pa.phases = m->d_phases;
-  pa.tiles = m->d_ptiles;
-  pa.nphases = head ? m->nphases : m->nphases_ingest;
-  pa.st = step_state(m);
-  pa.write_greedy = head ? 1 : 0;
-  pa.sync = m->d_sync;
-  pa.hsync = m->d_hsync;
-  pa.nhsync = m->nhsync;
-  pa.status = m->ex->d_status;
-  pa.trace = trace ? m->d_trace : nullptr;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)m->ex->num_sms);
-  cfg.blockDim = dim3(kPThreads);
-  cfg.dynamicSmemBytes = kPSmemBytes;
-  cfg.stream = m->stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return m->cfg.weight_kind == 35 ? cudaLaunchKernelEx(&cfg, decode_persistent_kernel<35>, pa)
-                                  : cudaLaunchKernelEx(&cfg, decode_persistent_kernel<10>, pa);
 }
 
 // ---- the dataflow step (flow.cuh) ---------------------------------------------
@@ -905,9 +669,7 @@ inline cudaError_t capture_step(prism_b200_model *m, bool head, cudaGraphExec_t 
   cudaGraph_t graph = nullptr;
   cudaError_t e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
   if (e != cudaSuccess) return e;
-  cudaError_t e2 = m->flow      ? launch_flow(m, head)
-                   : m->persist ? launch_persistent(m, head)
-                                : enqueue_step(m, head);
+  cudaError_t e2 = m->flow ? launch_flow(m, head) : enqueue_step(m, head);
   e = cudaStreamEndCapture(m->stream, &graph);
   if (e2 != cudaSuccess) e = e2;
   if (e == cudaSuccess) e = cudaGraphInstantiate(out, graph, 0);
@@ -979,14 +741,7 @@ int prism_b200_model_create(prism_b200_executor *ex, const prism_b200_qwen35_con
   A(m->d_prompt_end, 1);
   A(m->d_argmax, 1);
   A(m->out_norm, c.hidden);
-  int attn_layers = 0;
-  for (uint32_t l = 0; l < c.layers; ++l) attn_layers += m->is_full((int)l) ? 1 : 0;
-  m->nhsync = attn_layers * (int)c.heads;
   A(m->gdn_o, m->value_width());
-  A(m->smax, (size_t)c.heads * kAttnSplit);
-  A(m->stot, (size_t)c.heads * kAttnSplit);
-  A(m->apart, (size_t)c.heads * kAttnSplit * c.head_dim);
-  A(m->d_sync, 16);
   A(m->d_fsync, 4);
   A(m->d_fkey, 1);
   A(m->t_hidden, c.hidden);
@@ -1015,7 +770,6 @@ int prism_b200_model_create(prism_b200_executor *ex, const prism_b200_qwen35_con
       A(m->d_seqtrace, (size_t)8 * m->nseqtrace);
     }
   }
-  A(m->d_hsync, (size_t)(m->nhsync > 0 ? m->nhsync : 1));
   for (uint32_t l = 0; l < c.layers; ++l) {
     ModelLayer &Ly = m->L[l];
     Ly.full = m->is_full((int)l);
@@ -1207,8 +961,6 @@ int prism_b200_model_finalize(prism_b200_model *m) {
   m->g_ingest = m->g_decode = nullptr;
   cudaError_t e = prepare_flow(m);
   if (e != cudaSuccess) return cuda_fail(ex, e, "dataflow step setup");
-  e = m->flow ? cudaSuccess : prepare_persistent(m);
-  if (e != cudaSuccess) return cuda_fail(ex, e, "persistent step setup");
   e = capture_step(m, false, &m->g_ingest);
   if (e == cudaSuccess) e = capture_step(m, true, &m->g_decode);
   if (e != cudaSuccess) return cuda_fail(ex, e, "step graph capture");
@@ -1234,10 +986,8 @@ int prism_b200_model_reset(prism_b200_model *m) {
          "reset");
     }
   }
-  CK(cudaMemsetAsync(m->d_sync, 0, 16 * 4, s), "reset");
   CK(cudaMemsetAsync(m->d_fsync, 0, 2 * 4, s), "reset");
   CK(cudaMemsetAsync(m->d_fkey, 0, 8, s), "reset");
-  CK(cudaMemsetAsync(m->d_hsync, 0, (size_t)(m->nhsync > 0 ? m->nhsync : 1) * 4, s), "reset");
   CK(cudaMemsetAsync(m->d_position, 0, 4, s), "reset");
   CK(cudaMemsetAsync(m->d_tokens, 0, ((size_t)c.context + 1) * 4, s), "reset");
   CK(cudaStreamSynchronize(s), "reset");
@@ -1247,9 +997,7 @@ int prism_b200_model_reset(prism_b200_model *m) {
 
 int64_t prism_b200_model_position(const prism_b200_model *m) { return m ? m->position : -1; }
 
-int prism_b200_model_persistent(const prism_b200_model *m) {
-  return m && (m->persist || m->flow) ? 1 : 0;
-}
+int prism_b200_model_persistent(const prism_b200_model *m) { return m && m->flow ? 1 : 0; }
 
 int64_t prism_b200_model_phase_trace_ctas(prism_b200_model *m, uint64_t *ns, size_t count) {
   if (!m || !ns) return -PRISM_B200_E_INVALID;
@@ -1261,7 +1009,7 @@ int64_t prism_b200_model_phase_trace_ctas(prism_b200_model *m, uint64_t *ns, siz
 }
 
 int prism_b200_model_step_mode(const prism_b200_model *m) {
-  return !m ? -1 : m->flow ? 2 : m->persist ? 1 : 0;
+  return !m ? -1 : m->flow ? 2 : 0;
 }
 
 int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t count) {
@@ -1272,16 +1020,10 @@ int64_t prism_b200_model_phase_trace(prism_b200_model *m, uint64_t *ns, size_t c
       return -PRISM_B200_E_DEVICE;
     return (int64_t)n;
   }
-  if (!m->persist) {
-    // the kernel-sequence step's per-launch timelines, when enabled
-    if (!m->d_seqtrace) return 0;
-    const size_t n = std::min(count, (size_t)8 * m->nseqtrace);
-    if (cudaMemcpy(ns, m->d_seqtrace, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
-      return -PRISM_B200_E_DEVICE;
-    return (int64_t)n;
-  }
-  const size_t n = std::min(count, (size_t)8 * m->nphases);
-  if (cudaMemcpy(ns, m->d_trace, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
+  // the kernel-sequence step's per-launch timelines, when enabled
+  if (!m->d_seqtrace) return 0;
+  const size_t n = std::min(count, (size_t)8 * m->nseqtrace);
+  if (cudaMemcpy(ns, m->d_seqtrace, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
     return -PRISM_B200_E_DEVICE;
   return (int64_t)n;
 }
@@ -1441,33 +1183,6 @@ int prism_b200_model_step_timings(prism_b200_model *m, float *attention_ms, floa
     }
     if (head_ms) *head_ms = ms(end(p - 1), end(p));
     if (total_ms) *total_ms = ms(t[0], end(m->nfphases - 1));
-    st = model_finish(m);
-    if (st) return st;
-    m->position += 1;
-    return PRISM_B200_OK;
-  }
-  if (m->persist) {
-    // one traced persistent step: CTA 0's phase boundaries (barrier waits
-    // included in the phase that follows them)
-    std::vector<unsigned long long> t((size_t)8 * m->nphases);
-    cudaError_t e = prism::launch_persistent(m, true, true);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
-    if (e == cudaSuccess)
-      e = cudaMemcpy(t.data(), m->d_trace, t.size() * 8, cudaMemcpyDeviceToHost);
-    if (e != cudaSuccess) return cuda_fail(ex, e, "traced step");
-    auto end = [&](int q) { return t[(size_t)8 * q + 7]; };
-    auto ms = [](unsigned long long a, unsigned long long b) {
-      return (float)((double)(b - a) * 1e-6);
-    };
-    int p = 1;  // phase 0 is the embedding
-    for (int l = 0; l < nl; ++l) {
-      const int ffn = p + 3;  // three attention-side phases, then the FFN pair
-      if (attention_ms) attention_ms[l] = ms(end(p - 1), end(ffn - 1));
-      if (ffn_ms) ffn_ms[l] = ms(end(ffn - 1), end(ffn + 1));
-      p = ffn + 2;
-    }
-    if (head_ms) *head_ms = ms(end(p - 1), end(p));
-    if (total_ms) *total_ms = ms(t[0], end(m->nphases - 1));
     st = model_finish(m);
     if (st) return st;
     m->position += 1;

@@ -16,6 +16,7 @@
 #include "executor.cuh"
 #include "gdn.cuh"
 #include "gemm.cuh"
+#include "packed.cuh"
 
 using namespace prism;
 
@@ -51,6 +52,13 @@ bool geometry_ok(const prism_b200_tensor *t) {
          t->cols <= kMaxCols && t->rows > 0 && t->rows <= (1ull << 30);
 }
 
+// PQ2 / PTQ1 tensors: whole 128-weight blocks (reference src/kernels.rs:
+// 88-119 layout, 121-143 dimensions).
+bool packed_geometry_ok(const prism_b200_tensor *t) {
+  return t && pq_block_bytes(t->kind) != 0 && t->cols > 0 && t->cols % 128 == 0 &&
+         t->cols <= kMaxCols && t->rows > 0 && t->rows <= (1ull << 30);
+}
+
 cudaStream_t pick(prism_b200_executor *ex, void *stream) {
   return stream ? reinterpret_cast<cudaStream_t>(stream) : ex->stream;
 }
@@ -78,9 +86,23 @@ int finish(prism_b200_executor *ex, cudaStream_t s) {
   return PRISM_B200_OK;
 }
 
-int validate_weight(prism_b200_executor *ex, const prism_b200_weight *w) {
+// A weight of this executor in either layout.
+int validate_any_weight(prism_b200_executor *ex, const prism_b200_weight *w) {
   if (!w || w->ex != ex || !w->dw.units)
     return ex->fail(PRISM_B200_E_INVALID, "weight does not belong to this executor");
+  return PRISM_B200_OK;
+}
+
+// A tiled (TQ2_0 / Q2_K) weight of this executor: every path but the packed
+// projections (prism_b200_project, _project_device, _project_q8,
+// _project_f32) needs one.
+int validate_weight(prism_b200_executor *ex, const prism_b200_weight *w) {
+  int st = validate_any_weight(ex, w);
+  if (st) return st;
+  if (w->dw.packed)
+    return ex->fail(PRISM_B200_E_UNSUPPORTED,
+                    "PQ2/PTQ1 weights are projected by prism_b200_project, _project_device, "
+                    "_project_q8 and _project_f32 only");
   return PRISM_B200_OK;
 }
 
@@ -88,6 +110,75 @@ cudaError_t project_on(prism_b200_executor *ex, const prism_b200_weight *w, cons
                        float *y, cudaStream_t s) {
   return launch_matvec(w->dw, act, y, nullptr, nullptr, kEpiStore, ex->d_status, ex->num_sms, s,
                        ex->pdl);
+}
+
+// ---- PQ2 / PTQ1 (packed.cuh) ------------------------------------------------
+
+// Whether a packed weight takes Q8_K activations (reference src/kernels.rs:
+// 1663-1674): PQ2 with a multiple of 256 columns; PTQ1 and other PQ2 rows
+// take Q8_0.
+bool packed_q8k(const DeviceWeight &dw) { return dw.kind == 142 && dw.cols % 256 == 0; }
+
+int upload_packed(prism_b200_executor *ex, const prism_b200_tensor *t, prism_b200_weight **out) {
+  const int bb = pq_block_bytes(t->kind);
+  const size_t nb = t->cols / 128, nblocks = (size_t)t->rows * nb;
+  const uint8_t *src = static_cast<const uint8_t *>(t->data);
+  for (size_t i = 0; i < nblocks; ++i) {
+    // every block scale finite (reference scale(), src/kernels.rs:152-154)
+    const uint8_t hi = src[i * bb + (t->kind == 142 ? 1 : 27)];
+    if ((hi & 0x7c) == 0x7c) return ex->fail(PRISM_B200_E_NONFINITE, "nonfinite fp16 block scale");
+  }
+  CK(cudaSetDevice(ex->device), "select device");
+  auto *w = new prism_b200_weight();
+  w->ex = ex;
+  DeviceWeight &dw = w->dw;
+  dw.kind = t->kind;
+  dw.rows = t->rows;
+  dw.cols = t->cols;
+  dw.nb = (int)nb;
+  dw.h = 0;
+  dw.ntiles = 0;
+  dw.packed = true;
+  dw.bytes = nblocks * (size_t)bb;
+  cudaError_t e = cudaMalloc(&dw.units, dw.bytes);
+  if (e == cudaSuccess) e = cudaMemcpy(dw.units, src, dw.bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    if (dw.units) cudaFree(dw.units);
+    delete w;
+    return cuda_fail(ex, e, "weight upload");
+  }
+  ex->weights.insert(w);
+  *out = w;
+  return PRISM_B200_OK;
+}
+
+cudaError_t launch_packed(prism_b200_executor *ex, const DeviceWeight &dw, const void *act,
+                          bool q8k, int fused, float *y, cudaStream_t s) {
+  PackedArgs a;
+  a.w = dw.units;
+  a.kind = dw.kind;
+  a.rows = (long)dw.rows;
+  a.nb = dw.nb;
+  a.act = act;
+  a.q8k = q8k ? 1 : 0;
+  a.fused = fused ? 1 : 0;
+  a.y = y;
+  a.status = ex->d_status;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg =
+      pdl_config(dim3((unsigned)((dw.rows + kPackedWarps - 1) / kPackedWarps)),
+                 dim3(kPackedWarps * 32), 0, s, attr, ex->pdl);
+  return cudaLaunchKernelEx(&cfg, packed_matvec_kernel, a);
+}
+
+cudaError_t launch_q8_0_quantize(prism_b200_executor *ex, const float *x, size_t n, void *out,
+                                 cudaStream_t s) {
+  const long nblocks = (long)(n / 32);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_config(dim3((unsigned)((nblocks * 32 + 255) / 256)), dim3(256), 0,
+                                      s, attr, ex->pdl);
+  return cudaLaunchKernelEx(&cfg, q8_0_quantize_kernel, x, nblocks, static_cast<Q8Act *>(out),
+                            ex->d_status);
 }
 
 }  // namespace
@@ -184,12 +275,13 @@ int prism_b200_executor_reset(prism_b200_executor *ex) {
 
 int prism_b200_executor_supports(const prism_b200_executor *ex,
                                  const prism_b200_tensor *tensor) {
-  return ex && geometry_ok(tensor) ? 1 : 0;
+  return ex && (geometry_ok(tensor) || packed_geometry_ok(tensor)) ? 1 : 0;
 }
 
 int64_t prism_b200_executor_operation_count(const prism_b200_executor *ex,
                                             const prism_b200_tensor *tensor) {
   if (!prism_b200_executor_supports(ex, tensor)) return -1;
+  if (packed_geometry_ok(tensor)) return (int64_t)tensor->rows * (int64_t)(tensor->cols / 128);
   const int h = choose_tile_height(tensor->kind, tensor->rows, tensor->cols, ex->num_sms);
   int64_t tiles = (int64_t)((tensor->rows + h - 1) / h);
   return tiles * (int64_t)(tensor->cols / 256);
@@ -201,6 +293,7 @@ int prism_b200_weight_upload(prism_b200_executor *ex, const prism_b200_tensor *t
   if (st) return st;
   if (!out || !t || !t->data) return ex->fail(PRISM_B200_E_INVALID, "null tensor or output");
   *out = nullptr;
+  if (packed_geometry_ok(t)) return upload_packed(ex, t, out);
   if (!geometry_ok(t))
     return ex->fail(PRISM_B200_E_UNSUPPORTED, "unsupported kind %u or geometry %llux%llu",
                     t->kind, (unsigned long long)t->cols, (unsigned long long)t->rows);
@@ -242,34 +335,51 @@ uint64_t prism_b200_weight_device_bytes(const prism_b200_weight *w) {
 int prism_b200_project_device(prism_b200_executor *ex, const prism_b200_weight *w,
                               const void *activation_dev, int fused, float *out_dev,
                               void *stream) {
-  (void)fused;
   int st = check_open(ex);
   if (st) return st;
-  if ((st = validate_weight(ex, w))) return st;
+  if ((st = validate_any_weight(ex, w))) return st;
+  if (w->dw.packed && !packed_q8k(w->dw))
+    return ex->fail(PRISM_B200_E_UNSUPPORTED,
+                    "kind %u with %llu columns takes Q8_0 activations (prism_b200_project_q8)",
+                    w->dw.kind, (unsigned long long)w->dw.cols);
   if (!activation_dev || !out_dev) return ex->fail(PRISM_B200_E_INVALID, "null device buffer");
   if (reinterpret_cast<uintptr_t>(activation_dev) % 4)
     return ex->fail(PRISM_B200_E_INVALID, "activation must be 4-byte aligned");
   cudaSetDevice(ex->device);
-  CK(project_on(ex, w, activation_dev, out_dev, pick(ex, stream)), "matvec launch");
+  if (w->dw.packed)
+    CK(launch_packed(ex, w->dw, activation_dev, true, fused, out_dev, pick(ex, stream)),
+       "packed matvec launch");
+  else
+    CK(project_on(ex, w, activation_dev, out_dev, pick(ex, stream)), "matvec launch");
   return PRISM_B200_OK;
 }
 
 int prism_b200_project(prism_b200_executor *ex, const prism_b200_weight *w,
                        const prism_b200_q8k_block *activation, int fused, float *out) {
-  (void)fused;
   int st = check_open(ex);
   if (st) return st;
-  if ((st = validate_weight(ex, w))) return st;
+  if ((st = validate_any_weight(ex, w))) return st;
+  if (w->dw.packed && !packed_q8k(w->dw)) {
+    if (out) memset(out, 0, w->dw.rows * sizeof(float));
+    return ex->fail(PRISM_B200_E_UNSUPPORTED,
+                    "kind %u with %llu columns takes Q8_0 activations (prism_b200_project_q8)",
+                    w->dw.kind, (unsigned long long)w->dw.cols);
+  }
   if (!activation || !out) return ex->fail(PRISM_B200_E_INVALID, "null buffer");
   cudaSetDevice(ex->device);
-  const size_t abytes = (size_t)w->dw.nb * sizeof(prism_b200_q8k_block);
+  const size_t abytes =
+      (size_t)(w->dw.packed ? w->dw.cols / 256 : w->dw.nb) * sizeof(prism_b200_q8k_block);
   const size_t ybytes = (size_t)w->dw.rows * sizeof(float);
   CK(ex->act.ensure(abytes), "activation buffer");
   CK(ex->y.ensure(ybytes), "output buffer");
   cudaStream_t s = ex->stream;
   CK(cudaMemcpyAsync(ex->act.ptr, activation, abytes, cudaMemcpyHostToDevice, s),
      "activation copy");
-  CK(project_on(ex, w, ex->act.ptr, static_cast<float *>(ex->y.ptr), s), "matvec launch");
+  if (w->dw.packed)
+    CK(launch_packed(ex, w->dw, ex->act.ptr, true, fused, static_cast<float *>(ex->y.ptr), s),
+       "packed matvec launch");
+  else
+    CK(project_on(ex, w, ex->act.ptr, static_cast<float *>(ex->y.ptr), s), "matvec launch");
   CK(cudaMemcpyAsync(out, ex->y.ptr, ybytes, cudaMemcpyDeviceToHost, s), "output copy");
   st = finish(ex, s);
   if (st) memset(out, 0, ybytes);
@@ -359,6 +469,36 @@ int prism_b200_project_f32_group(prism_b200_executor *ex, size_t count,
 
 int prism_b200_project_f32(prism_b200_executor *ex, const prism_b200_weight *w, const float *x,
                            int pinned, float *out) {
+  if (ex && w && w->ex == ex && w->dw.packed) {
+    // PQ2 / PTQ1: quantized by the tensor's activation contract, unfused
+    int st = check_open(ex);
+    if (st) return st;
+    if (!x || !out) return ex->fail(PRISM_B200_E_INVALID, "null buffer");
+    if (pinned)
+      return ex->fail(PRISM_B200_E_UNSUPPORTED, "pinned accumulation of kind %u", w->dw.kind);
+    const DeviceWeight &dw = w->dw;
+    const bool q8k = packed_q8k(dw);
+    const size_t n = dw.cols;
+    const size_t abytes = q8k ? n / 256 * sizeof(prism_b200_q8k_block) : n / 32 * sizeof(Q8Act);
+    const size_t ybytes = (size_t)dw.rows * sizeof(float);
+    CK(cudaSetDevice(ex->device), "select device");
+    CK(ex->x.ensure(n * sizeof(float)), "input buffer");
+    CK(ex->act.ensure(abytes), "activation buffer");
+    CK(ex->y.ensure(ybytes), "output buffer");
+    cudaStream_t s = ex->stream;
+    float *xd = static_cast<float *>(ex->x.ptr);
+    CK(cudaMemcpyAsync(xd, x, n * sizeof(float), cudaMemcpyHostToDevice, s), "input copy");
+    if (q8k)
+      CK(launch_quantize(xd, n, 0, ex->act.ptr, ex->d_status, s, ex->pdl), "quantize launch");
+    else
+      CK(launch_q8_0_quantize(ex, xd, n, ex->act.ptr, s), "quantize launch");
+    CK(launch_packed(ex, dw, ex->act.ptr, q8k, 0, static_cast<float *>(ex->y.ptr), s),
+       "packed matvec launch");
+    CK(cudaMemcpyAsync(out, ex->y.ptr, ybytes, cudaMemcpyDeviceToHost, s), "output copy");
+    st = finish(ex, s);
+    if (st) memset(out, 0, ybytes);
+    return st;
+  }
   const prism_b200_weight *ws[1] = {w};
   float *os[1] = {out};
   return prism_b200_project_f32_group(ex, 1, ws, x, pinned, os);
@@ -641,4 +781,5 @@ extern "C" int prism_b200_gdn_prefill_device_noalloc(prism_b200_executor *ex, in
 #include "batch.cuh"
 #include "prefill.cuh"
 #include "tp_ffn.cuh"
+#include "peak.cuh"
 #include "seam.cuh"

@@ -127,23 +127,41 @@ int prism_b200_executor_supports_f32_group(const prism_b200_executor *ex, size_t
 
 int prism_b200_executor_supports_q8(const prism_b200_executor *ex,
                                     const prism_b200_tensor *tensor) {
-  // Q8_0 activations serve PTQ1 and odd-block PQ2 rows in the reference;
-  // TQ2_0 and Q2_K take Q8_K activations
-  (void)ex;
-  (void)tensor;
-  return 0;
+  // Q8_0 activations serve PTQ1 and PQ2 rows (the reference routes PQ2 here
+  // when its columns are not a multiple of 256); TQ2_0 and Q2_K take Q8_K
+  return ex && packed_geometry_ok(tensor) ? 1 : 0;
 }
 
 int prism_b200_project_q8(prism_b200_executor *ex, const prism_b200_weight *w,
                           const void *activation, int pinned, float *out) {
-  (void)pinned;
   int st = check_open(ex);
   if (st) return st;
-  if ((st = validate_weight(ex, w))) return st;
-  if (out) memset(out, 0, w->dw.rows * 4);
-  (void)activation;
-  return ex->fail(PRISM_B200_E_UNSUPPORTED,
-                  "kind %u takes Q8_K activations (prism_b200_project), not Q8_0", w->dw.kind);
+  if ((st = validate_any_weight(ex, w))) return st;
+  const DeviceWeight &dw = w->dw;
+  const size_t ybytes = dw.rows * sizeof(float);
+  if (!dw.packed) {
+    if (out) memset(out, 0, ybytes);
+    return ex->fail(PRISM_B200_E_UNSUPPORTED,
+                    "kind %u takes Q8_K activations (prism_b200_project), not Q8_0", dw.kind);
+  }
+  if (pinned) {
+    if (out) memset(out, 0, ybytes);
+    return ex->fail(PRISM_B200_E_UNSUPPORTED, "pinned accumulation of kind %u", dw.kind);
+  }
+  if (!activation || !out) return ex->fail(PRISM_B200_E_INVALID, "null buffer");
+  const size_t abytes = dw.cols / 32 * sizeof(Q8Act);
+  CK(cudaSetDevice(ex->device), "select device");
+  CK(ex->act.ensure(abytes), "activation buffer");
+  CK(ex->y.ensure(ybytes), "output buffer");
+  cudaStream_t s = ex->stream;
+  CK(cudaMemcpyAsync(ex->act.ptr, activation, abytes, cudaMemcpyHostToDevice, s),
+     "activation copy");
+  CK(launch_packed(ex, dw, ex->act.ptr, false, 0, static_cast<float *>(ex->y.ptr), s),
+     "packed matvec launch");
+  CK(cudaMemcpyAsync(out, ex->y.ptr, ybytes, cudaMemcpyDeviceToHost, s), "output copy");
+  st = finish(ex, s);
+  if (st) memset(out, 0, ybytes);
+  return st;
 }
 
 int prism_b200_executor_supports_tile_tokens(const prism_b200_executor *ex) { return ex ? 1 : 0; }
@@ -282,3 +300,34 @@ int prism_b200_project_f32_ffn_chain(prism_b200_executor *ex, const prism_b200_w
 }
 
 }  // extern "C"
+
+// ---- measured dense int8 tensor-core rate ----------------------------------
+// No reference counterpart: the denominator of the GEMM's tensor roofline.
+// One CTA per SM issues `iters` back-to-back kind::i8 MMAs (128x256x32) from
+// shared memory; a warm-up launch precedes the event-timed one.
+extern "C" int prism_b200_tensor_peak_i8(prism_b200_executor *ex, int iters, double *tops) {
+  int st = check_open(ex);
+  if (st) return st;
+  if (!tops || iters < 1 || iters > (1 << 20))
+    return ex->fail(PRISM_B200_E_INVALID, "iters must be 1..2^20 and tops non-null");
+  CK(cudaSetDevice(ex->device), "select device");
+  cudaStream_t s = ex->stream;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  CK(cudaEventCreate(&e0), "event");
+  if (cudaEventCreate(&e1) != cudaSuccess) {
+    cudaEventDestroy(e0);
+    return ex->fail(PRISM_B200_E_DEVICE, "event");
+  }
+  tensor_peak_i8_kernel<<<ex->num_sms, 128, 0, s>>>(iters, ex->d_status);
+  cudaEventRecord(e0, s);
+  tensor_peak_i8_kernel<<<ex->num_sms, 128, 0, s>>>(iters, ex->d_status);
+  cudaEventRecord(e1, s);
+  cudaError_t e = cudaGetLastError();
+  st = e == cudaSuccess ? finish(ex, s) : cuda_fail(ex, e, "tensor peak launch");
+  float ms = 0.0f;
+  if (st == PRISM_B200_OK && cudaEventElapsedTime(&ms, e0, e1) == cudaSuccess && ms > 0.0f)
+    *tops = 2.0 * kPeakM * kPeakN * kPeakK * (double)iters * ex->num_sms / (ms * 1e-3) / 1e12;
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  return st;
+}

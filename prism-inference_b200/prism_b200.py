@@ -21,10 +21,15 @@ LIB_PATH = os.path.join(HERE, "libprism_b200.so")
 OK = 0
 E_INVALID, E_UNSUPPORTED, E_NONFINITE, E_DEVICE, E_TIMEOUT, E_FAULTED = 1, 2, 3, 4, 5, 6
 KIND_Q2_K, KIND_Q8_K, KIND_TQ2_0 = 10, 15, 35
+KIND_PQ2, KIND_PTQ1 = 142, 143   # the reference's own packed ternary formats
 BLOCK_BYTES = {KIND_TQ2_0: 66, KIND_Q2_K: 84}
+PACKED_BLOCK_BYTES = {KIND_PQ2: 34, KIND_PTQ1: 28}   # per 128 weights
 
 Q8K_DTYPE = np.dtype([("scale", "<f4"), ("values", "i1", (256,)), ("sums", "<i2", (16,))])
 assert Q8K_DTYPE.itemsize == 292
+# prism_b200_q8_block: the reference's Q8Block (scale, code sum, 32 codes)
+Q8_DTYPE = np.dtype([("scale", "<f4"), ("sum", "<f4"), ("values", "i1", (32,))])
+assert Q8_DTYPE.itemsize == 40
 
 
 class PrismB200Error(RuntimeError):
@@ -86,6 +91,7 @@ def load():
         "prism_b200_ffn_chain_tokens": (i32, [vp, sz, vp, vp, i32, vp]),
         "prism_b200_ffn_chain_tokens_device": (i32, [vp, sz, vp, vp, i32, vp, vp]),
         "prism_b200_executor_operation_capacity": (i64, [vp]),
+        "prism_b200_tensor_peak_i8": (i32, [vp, i32, P(ctypes.c_double)]),
         "prism_b200_executor_supports_f32": (i32, [vp, P(_Tensor)]),
         "prism_b200_executor_supports_f32_group": (i32, [vp, sz, P(P(_Tensor))]),
         "prism_b200_executor_supports_q8": (i32, [vp, P(_Tensor)]),
@@ -227,6 +233,13 @@ class ProjectionExecutor:
         n = load().prism_b200_executor_operation_count(self.h, ctypes.byref(t))
         return None if n < 0 else n
 
+    def tensor_peak_i8(self, iters=8192):
+        """Measured dense int8 tensor-core rate of this device, Tint-op/s
+        (no reference counterpart: the GEMM roofline's denominator)."""
+        v = ctypes.c_double(0.0)
+        self._check(load().prism_b200_tensor_peak_i8(self.h, iters, ctypes.byref(v)))
+        return v.value
+
     def operation_capacity(self):
         """Remaining submissions of a bounded session, None when opaque
         (reference src/kernels/projection.rs:20-28)."""
@@ -332,9 +345,12 @@ class ProjectionExecutor:
         return outs
 
     def project_q8(self, weight, activation, pinned=False):
-        """Q8_0 activations (reference src/kernels/projection.rs:62-90)."""
+        """Q8_0 activations, cols/32 Q8_DTYPE blocks (reference
+        src/kernels/projection.rs:62-90): PTQ1 and PQ2 weights."""
         w = self._weight(weight)
         act = np.ascontiguousarray(activation)
+        if act.dtype == Q8_DTYPE and act.size * 32 != w.cols:
+            raise PrismB200Error(E_INVALID, "activation extent differs from weight columns")
         out = np.zeros(w.rows, dtype=np.float32)
         self._check(load().prism_b200_project_q8(self.h, w.handle, _p(act), int(pinned), _p(out)))
         return out

@@ -264,8 +264,8 @@ class Qwen35Model:
 
     @property
     def step_mode(self):
-        """2: the dataflow step kernel, 1: the barrier-synchronised persistent
-        kernel, 0: the per-phase kernel sequence (PRISM_B200_STEP at load)."""
+        """2: the dataflow step kernel (the default where eligible), 0: the
+        per-phase kernel sequence (PRISM_B200_STEP=seq at load)."""
         import ctypes as c
         L = self.L
         if not getattr(L, "_mode_declared", False):
@@ -276,7 +276,8 @@ class Qwen35Model:
 
     @property
     def persistent(self):
-        """True when each step runs as one persistent cooperative kernel."""
+        """True when each step runs as one cooperative kernel (the dataflow
+        step)."""
         return bool(self.L.prism_b200_model_persistent(self.h))
 
     def evaluate(self, token, logits=True):

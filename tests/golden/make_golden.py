@@ -84,12 +84,49 @@ def main(ref_root):
         ],
     }
     pinned = pinned_fixtures(fixtures)
+    ptq = ptq_fixture(fixtures)
     for name, obj in (("tq2_0.json", tq), ("q2_k.json", kq), ("q8k_parity.json", q8k),
-                      ("pinned.json", pinned)):
+                      ("pinned.json", pinned), ("ptq_reference.json", ptq)):
         with open(os.path.join(HERE, name), "w") as f:
             json.dump(obj, f, indent=1)
             f.write("\n")
         print("wrote", name, len(obj.get("cases", obj)), "records")
+
+
+def ptq_fixture(fx):
+    """The native C++ PQ2/PTQ codec capture (tests/fixtures/ptq-reference.bin,
+    layout in tools/ternary/tests/fixtures/README.md): binary16 conversions,
+    then per case the same rows as PQ2 blocks and as PTQ blocks."""
+    import struct
+    with open(os.path.join(fx, "ptq-reference.bin"), "rb") as f:
+        buf = f.read()
+    assert hashlib.sha256(buf).hexdigest() == \
+        "de86d0ff0e31037635ae5f607bcb68d4e62ee7cb5d1b5db5e739ef900114fd79"
+    assert buf[:8] == b"PTPAR001"
+    off = 8
+    (nconv,) = struct.unpack_from("<I", buf, off)
+    off += 4
+    conversions = []
+    for _ in range(nconv):
+        h, bits = struct.unpack_from("<HI", buf, off)
+        conversions.append([h, bits])
+        off += 6
+    (ncases,) = struct.unpack_from("<I", buf, off)
+    off += 4
+    cases = []
+    for _ in range(ncases):
+        rows, bpr = struct.unpack_from("<II", buf, off)
+        off += 8
+        n = rows * bpr
+        pq2 = buf[off:off + 34 * n]
+        off += 34 * n
+        ptq = buf[off:off + 28 * n]
+        off += 28 * n
+        cases.append({"rows": rows, "blocks_per_row": bpr, "pq2_hex": pq2.hex(),
+                      "ptq_hex": ptq.hex()})
+    assert off == len(buf)
+    return {"source": "tests/fixtures/ptq-reference.bin (native C++ PQ2/PTQ codec capture)",
+            "half_conversions": conversions, "cases": cases}
 
 
 def pinned_fixtures(fx):

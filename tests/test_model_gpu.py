@@ -113,38 +113,6 @@ def test_model_rejects_bad_tensors():
         gm.close()
 
 
-@pytest.mark.parametrize("cfg_name", ["SMALL", "CONFIG1"])
-def test_persistent_step_matches_kernel_sequence(cfg_name, monkeypatch):
-    """The persistent step (one cooperative kernel per token) and the
-    per-phase kernel sequence give identical logits, hidden state and
-    recurrent state, token by token."""
-    cfg = getattr(qwen35, cfg_name)
-    W = qwen35.synthetic_weights(cfg, seed=5)
-    toks = qwen35.prompt_tokens(cfg, 12, seed=6)
-    runs = []
-    for persist in ("1", "0"):
-        monkeypatch.setenv("PRISM_B200_PERSIST", persist)
-        with pb.ProjectionExecutor(0) as ex:
-            gm = qwen35.Qwen35Model(ex, cfg)
-            gm.load(W)
-            assert gm.persistent == (persist == "1")
-            out = []
-            for t in toks:
-                lg, g = gm.evaluate(t)
-                out.append((lg.copy(), g, gm.read_state(0, 4).copy()))
-            states = [gm.read_state(l, 1).copy() for l in range(cfg.layers) if not cfg.is_full(l)]
-            gen = gm.generate(toks[:4], 6)
-            runs.append((out, states, list(gen)))
-            gm.close()
-    (a, sa, ga), (b, sb, gb) = runs
-    for i, ((la, gi, ha), (lb, gj, hb)) in enumerate(zip(a, b)):
-        assert np.array_equal(la.view(np.uint32), lb.view(np.uint32)), "step %d logits" % i
-        assert gi == gj and np.array_equal(ha.view(np.uint32), hb.view(np.uint32)), i
-    for x, y in zip(sa, sb):
-        assert np.array_equal(x.view(np.uint32), y.view(np.uint32))
-    assert ga == gb
-
-
 def _q8_pair(cfg, seed):
     from oracle import oracle
     W = qwen35.synthetic_weights(cfg, seed=seed)
@@ -178,21 +146,23 @@ def test_q8_0_kv_cache_parity():
     ex.close()
 
 
-def test_q8_0_kv_config1_and_persistent(monkeypatch):
+def test_q8_0_kv_config1_both_step_modes(monkeypatch):
+    """configs[1] with Q8_0 KV against the oracle, through the dataflow step
+    (the default) and through the per-phase kernel sequence."""
     cfg = qwen35.CONFIG1
     W = qwen35.synthetic_weights(cfg, seed=8)
     toks = qwen35.prompt_tokens(cfg, 6, seed=9)
     from oracle import oracle
     om = oracle.Qwen35(cfg, W, kv_policy=1)
     ref = [om.step(t, threads=16) for t in toks]
-    for persist in ("1", "0"):
-        monkeypatch.setenv("PRISM_B200_PERSIST", persist)
+    for mode, want in (("flow", 2), ("seq", 0)):
+        monkeypatch.setenv("PRISM_B200_STEP", mode)
         with pb.ProjectionExecutor(0) as ex:
             gm = qwen35.Qwen35Model(ex, cfg, kv_policy=qwen35.KV_Q8_0)
             gm.load(W)
-            assert gm.persistent == (persist == "1")
+            assert gm.step_mode == want and gm.persistent == (want == 2)
             for i, t in enumerate(toks):
                 lg, _ = gm.evaluate(t)
                 ok, err = close(lg, ref[i])
-                assert ok, "persist %s step %d err %g" % (persist, i, err)
+                assert ok, "%s step %d err %g" % (mode, i, err)
             gm.close()

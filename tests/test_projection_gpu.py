@@ -112,7 +112,10 @@ def test_eligibility_and_operation_count(ex):
     assert ex.supports(pb.Tensor(35, 2560, 9216, z))
     assert ex.supports(pb.Tensor(10, 9216, 2560, z))
     assert not ex.supports(pb.Tensor(35, 2500, 10, z))
-    assert not ex.supports(pb.Tensor(142, 256, 10, z))
+    # the reference's own PQ2 / PTQ1 formats: whole 128-weight blocks
+    assert ex.supports(pb.Tensor(142, 256, 10, z)) and ex.supports(pb.Tensor(143, 384, 10, z))
+    assert not ex.supports(pb.Tensor(142, 200, 10, z))
+    assert not ex.supports(pb.Tensor(34, 256, 10, z))  # TQ1_0 is not built
     # units of (tile of H rows) x (256-column block); H is 8, 16 or 32
     n = ex.operation_count(pb.Tensor(35, 4096, 4096, z))
     assert n in (512 * 16, 256 * 16, 128 * 16)

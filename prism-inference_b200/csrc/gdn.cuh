@@ -249,31 +249,49 @@ __host__ __device__ constexpr size_t gdn_prep_smem() {
 }
 
 // Scan over the chunks of one (sequence, head) for R state rows.
-// grid (128/R, heads, batch), 256 threads.
-constexpr int kScanThreads = 256;
+// grid (128/R, heads, batch), kScanThreads threads: warp w owns state rows
+// w + 16a (a < R/16) and lane l tokens l + 32b (b < 2) of every chunk tile.
+// With R == 16 (the small-batch grid) the next chunk's K, Q and V arrive by
+// asynchronous copies into a second buffer while the current one computes.
+constexpr int kScanThreads = 512;
+
+template <int R>
+__host__ __device__ constexpr bool gdn_scan_prefetch() {
+  return R == 16;
+}
 
 template <int R>
 __host__ __device__ constexpr size_t gdn_scan_smem() {
-  // S[R][D] K,Q[C][kKS] M[C][kMS] CQ[C][kMS] V[C][R] KD,QD,DL[R][C+1] cum plast
-  return (size_t)(R * kGdnD + 2 * kChunk * kKS + 2 * kChunk * kMS + kChunk * R +
-                  3 * R * (kChunk + 1) + 2 * kChunk) * 4;
+  // S[R][D] K,Q[C][kKS] M[C][kMS] CQ[C][kMS] V[C][R] KD,QD,DL[R][C+1] cum plast,
+  // and with prefetch a second K, Q, V
+  return (size_t)(R * kGdnD + (gdn_scan_prefetch<R>() ? 2 : 1) * (2 * kChunk * kKS + kChunk * R) +
+                  2 * kChunk * kMS + 3 * R * (kChunk + 1) + 2 * kChunk) *
+         4;
+}
+
+__device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
 }
 
 template <int R>
 __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefillArgs p) {
   constexpr int D = kGdnD, C = kChunk, CP = kChunk + 1;
+  constexpr bool PF = gdn_scan_prefetch<R>();
+  constexpr int NB = PF ? 2 : 1;
   extern __shared__ __align__(16) float sm[];
-  float *S = sm;                 // [R][D]
-  float *K = S + R * D;          // [C][kKS]
-  float *Q = K + C * kKS;        // [C][kKS]
-  float *M = Q + C * kKS;        // [C][kMS]
-  float *CQ = M + C * kMS;       // [C][kMS]
-  float *V = CQ + C * kMS;       // [C][R]
-  float *KD = V + C * R;         // [R][C+1]
-  float *QD = KD + R * CP;       // [R][C+1]
-  float *DL = QD + R * CP;       // [R][C+1]  deltas
-  float *cum = DL + R * CP;      // [C]
-  float *plast = cum + C;        // [C]
+  float *S = sm;                          // [R][D]
+  float *Kb = S + R * D;                  // [NB][C][kKS]
+  float *Qb = Kb + NB * C * kKS;          // [NB][C][kKS]
+  float *Vb = Qb + NB * C * kKS;          // [NB][C][R]
+  float *M = Vb + NB * C * R;             // [C][kMS]
+  float *CQ = M + C * kMS;                // [C][kMS]
+  float *KD = CQ + C * kMS;               // [R][C+1]
+  float *QD = KD + R * CP;                // [R][C+1]
+  float *DL = QD + R * CP;                // [R][C+1]  deltas
+  float *cum = DL + R * CP;               // [C]
+  float *plast = cum + C;                 // [C]
   const GdnBatchArgs &a = p.g;
   const int g = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kh = h % a.key_heads;
@@ -284,42 +302,60 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
   float *state = a.state + ((long)b * a.heads + h) * D * D + (long)r0 * D;
   for (int i = tid; i < R * D / 4; i += blockDim.x)
     reinterpret_cast<float4 *>(S)[i] = reinterpret_cast<const float4 *>(state)[i];
+  // chunk c's K and Q rows and V slice into buffer `buf` (zeros past the
+  // prompt's end), as asynchronous copies committed as one group
+  auto issue = [&](int c, int buf) {
+    const int t0 = c * p.chunk, n = min(p.chunk, a.T - t0);
+    float *K = Kb + buf * C * kKS, *Q = Qb + buf * C * kKS, *V = Vb + buf * C * R;
+    for (int i = tid; i < C * D / 4; i += blockDim.x) {
+      const int t = i / (D / 4), col = i % (D / 4);
+      const long off = (((long)b * a.T + t0 + min(t, n - 1)) * a.key_heads + kh) * D;
+      cp_async16_zfill(K + t * kKS + 4 * col, a.k + off + 4 * col, t < n);
+      cp_async16_zfill(Q + t * kKS + 4 * col, a.q + off + 4 * col, t < n);
+    }
+    for (int i = tid; i < C * R / 4; i += blockDim.x) {
+      const int t = i / (R / 4), q4 = i % (R / 4);
+      const long off = (((long)b * a.T + t0 + min(t, n - 1)) * a.heads + h) * D + r0;
+      cp_async16_zfill(V + t * R + 4 * q4, a.v + off + 4 * q4, t < n);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (PF && p.nchunks > 0) issue(0, 0);
   const float oscale = 1.0f / sqrtf((float)D);
   bool finite = true;
   for (int c = 0; c < p.nchunks; ++c) {
     const int t0 = c * p.chunk;
     const int n = min(p.chunk, a.T - t0);
+    const int buf = PF ? (c & 1) : 0;
     const float *scr = p.scratch + (((long)b * a.heads + h) * p.nchunks + c) * kChunkScratch;
     __syncthreads();
-    for (int i = tid; i < C * D / 4; i += blockDim.x) {
-      const int t = i / (D / 4), col = i % (D / 4);
-      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
-      if (t < n) {
-        const long off = (((long)b * a.T + t0 + t) * a.key_heads + kh) * D;
-        kv = reinterpret_cast<const float4 *>(a.k + off)[col];
-        qv = reinterpret_cast<const float4 *>(a.q + off)[col];
+    if (PF) {
+      // the next chunk streams into the other buffer during this one
+      if (c + 1 < p.nchunks) {
+        issue(c + 1, buf ^ 1);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
       }
-      reinterpret_cast<float4 *>(K + t * kKS)[col] = kv;
-      reinterpret_cast<float4 *>(Q + t * kKS)[col] = qv;
+    } else {
+      issue(c, 0);
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
+    const float *K = Kb + buf * C * kKS, *Q = Qb + buf * C * kKS, *V = Vb + buf * C * R;
     for (int i = tid; i < C * C; i += blockDim.x) {
       M[(i / C) * kMS + i % C] = scr[i];
       CQ[(i / C) * kMS + i % C] = scr[C * C + i];
-    }
-    for (int i = tid; i < C * R; i += blockDim.x) {
-      const int t = i / R, r = i % R;
-      V[i] = t < n ? a.v[(((long)b * a.T + t0 + t) * a.heads + h) * D + r0 + r] : 0.0f;
     }
     for (int t = tid; t < C; t += blockDim.x) {
       cum[t] = scr[2 * C * C + t];
       plast[t] = scr[2 * C * C + C + t];
     }
     __syncthreads();
-    // Register tiles: thread (ti, tj) = (tid / 16, tid % 16) owns rows
-    // r = ti + 16a (a < TR) and tokens t = tj + 16b (b < TT); every output
-    // keeps the accumulation order of the one-output-per-thread form.
-    constexpr int TR = R / 16, TT = C / 16;
-    const int ti = tid / 16, tj = tid % 16;
+    // Register tiles: warp ti = tid / 32 owns rows r = ti + 16a (a < TR), lane
+    // tj = tid % 32 tokens t = tj + 32b (b < TT); every output keeps the
+    // accumulation order of the one-output-per-thread form.
+    constexpr int TR = R / 16, TT = C / 32;
+    const int ti = tid / 32, tj = tid % 32;
     // KD[r][t] = S_r . k_t, QD[r][t] = S_r . q_t
     {
       float dk[TR][TT], dq[TR][TT];
@@ -334,8 +370,8 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
         for (int ai = 0; ai < TR; ++ai) sv[ai] = reinterpret_cast<const float4 *>(S + (ti + 16 * ai) * D)[x];
 #pragma unroll
         for (int bi = 0; bi < TT; ++bi) {
-          kv[bi] = reinterpret_cast<const float4 *>(K + (tj + 16 * bi) * kKS)[x];
-          qv[bi] = reinterpret_cast<const float4 *>(Q + (tj + 16 * bi) * kKS)[x];
+          kv[bi] = reinterpret_cast<const float4 *>(K + (tj + 32 * bi) * kKS)[x];
+          qv[bi] = reinterpret_cast<const float4 *>(Q + (tj + 32 * bi) * kKS)[x];
         }
 #pragma unroll
         for (int ai = 0; ai < TR; ++ai)
@@ -350,7 +386,7 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
       for (int ai = 0; ai < TR; ++ai)
 #pragma unroll
         for (int bi = 0; bi < TT; ++bi) {
-          const int r = ti + 16 * ai, t = tj + 16 * bi;
+          const int r = ti + 16 * ai, t = tj + 32 * bi;
           // W[r][t] = v_rt - cum_t KD[r][t]  (into KD)
           KD[r * CP + t] = V[t * R + r] - cum[t] * dk[ai][bi];
           QD[r * CP + t] = dq[ai][bi];
@@ -364,16 +400,16 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
       for (int ai = 0; ai < TR; ++ai)
 #pragma unroll
         for (int bi = 0; bi < TT; ++bi) acc[ai][bi] = 0.0f;
-      const int tmax = tj + 16 * (TT - 1);
+      const int tmax = tj + 32 * (TT - 1);
       for (int j = 0; j <= tmax; ++j) {
         float wv[TR], mv[TT];
 #pragma unroll
         for (int ai = 0; ai < TR; ++ai) wv[ai] = KD[(ti + 16 * ai) * CP + j];
 #pragma unroll
-        for (int bi = 0; bi < TT; ++bi) mv[bi] = M[(tj + 16 * bi) * kMS + j];
+        for (int bi = 0; bi < TT; ++bi) mv[bi] = M[(tj + 32 * bi) * kMS + j];
 #pragma unroll
         for (int bi = 0; bi < TT; ++bi)
-          if (j <= tj + 16 * bi)
+          if (j <= tj + 32 * bi)
 #pragma unroll
             for (int ai = 0; ai < TR; ++ai) acc[ai][bi] = fmaf(mv[bi], wv[ai], acc[ai][bi]);
       }
@@ -381,7 +417,7 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
       for (int ai = 0; ai < TR; ++ai)
 #pragma unroll
         for (int bi = 0; bi < TT; ++bi) {
-          const int t = tj + 16 * bi;
+          const int t = tj + 32 * bi;
           DL[(ti + 16 * ai) * CP + t] = t < n ? acc[ai][bi] : 0.0f;
         }
     }
@@ -394,17 +430,17 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
       for (int ai = 0; ai < TR; ++ai)
 #pragma unroll
         for (int bi = 0; bi < TT; ++bi)
-          acc[ai][bi] = cum[tj + 16 * bi] * QD[(ti + 16 * ai) * CP + tj + 16 * bi];
-      const int tmax = tj + 16 * (TT - 1);
+          acc[ai][bi] = cum[tj + 32 * bi] * QD[(ti + 16 * ai) * CP + tj + 32 * bi];
+      const int tmax = tj + 32 * (TT - 1);
       for (int j = 0; j <= tmax; ++j) {
         float dv[TR], cv[TT];
 #pragma unroll
         for (int ai = 0; ai < TR; ++ai) dv[ai] = DL[(ti + 16 * ai) * CP + j];
 #pragma unroll
-        for (int bi = 0; bi < TT; ++bi) cv[bi] = CQ[(tj + 16 * bi) * kMS + j];
+        for (int bi = 0; bi < TT; ++bi) cv[bi] = CQ[(tj + 32 * bi) * kMS + j];
 #pragma unroll
         for (int bi = 0; bi < TT; ++bi)
-          if (j <= tj + 16 * bi)
+          if (j <= tj + 32 * bi)
 #pragma unroll
             for (int ai = 0; ai < TR; ++ai) acc[ai][bi] = fmaf(cv[bi], dv[ai], acc[ai][bi]);
       }
@@ -413,47 +449,43 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
       for (int ai = 0; ai < TR; ++ai)
 #pragma unroll
         for (int bi = 0; bi < TT; ++bi)
-          O[(tj + 16 * bi) * R + ti + 16 * ai] = acc[ai][bi] * oscale;
+          O[(tj + 32 * bi) * R + ti + 16 * ai] = acc[ai][bi] * oscale;
     }
     __syncthreads();
     for (int i = tid; i < R * C; i += blockDim.x) {
       const int t = i / R, r = i % R;  // r fastest: coalesced output stores
       if (t < n) a.out[(((long)b * a.T + t0 + t) * a.heads + h) * D + r0 + r] = KD[t * R + r];
     }
-    // S_r <- cum_last S_r + sum_j plast_j delta_rj k_j; thread (ti, tj)
-    // owns rows r = ti + 16a and columns x = 8 tj .. 8 tj + 7
+    // S_r <- cum_last S_r + sum_j plast_j delta_rj k_j; warp ti owns rows
+    // r = ti + 16a, lane tj columns x = 4 tj .. 4 tj + 3
     {
       const float last = cum[n - 1];
-      float acc[TR][8];
+      float acc[TR][4];
 #pragma unroll
       for (int ai = 0; ai < TR; ++ai) {
-        const float4 s0 = reinterpret_cast<const float4 *>(S + (ti + 16 * ai) * D + 8 * tj)[0];
-        const float4 s1 = reinterpret_cast<const float4 *>(S + (ti + 16 * ai) * D + 8 * tj)[1];
+        const float4 s0 = reinterpret_cast<const float4 *>(S + (ti + 16 * ai) * D + 4 * tj)[0];
         acc[ai][0] = last * s0.x; acc[ai][1] = last * s0.y;
         acc[ai][2] = last * s0.z; acc[ai][3] = last * s0.w;
-        acc[ai][4] = last * s1.x; acc[ai][5] = last * s1.y;
-        acc[ai][6] = last * s1.z; acc[ai][7] = last * s1.w;
       }
       for (int j = 0; j < n; ++j) {
         float cf[TR];
 #pragma unroll
         for (int ai = 0; ai < TR; ++ai) cf[ai] = plast[j] * DL[(ti + 16 * ai) * CP + j];
-        const float4 k0 = reinterpret_cast<const float4 *>(K + j * kKS + 8 * tj)[0];
-        const float4 k1 = reinterpret_cast<const float4 *>(K + j * kKS + 8 * tj)[1];
-        const float kx[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+        const float4 k0 = reinterpret_cast<const float4 *>(K + j * kKS + 4 * tj)[0];
+        const float kx[4] = {k0.x, k0.y, k0.z, k0.w};
 #pragma unroll
         for (int ai = 0; ai < TR; ++ai)
 #pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) acc[ai][c8] = fmaf(cf[ai], kx[c8], acc[ai][c8]);
+          for (int c4 = 0; c4 < 4; ++c4) acc[ai][c4] = fmaf(cf[ai], kx[c4], acc[ai][c4]);
       }
       __syncthreads();  // every thread has read S before it is overwritten
 #pragma unroll
       for (int ai = 0; ai < TR; ++ai) {
-        float *sr = S + (ti + 16 * ai) * D + 8 * tj;
+        float *sr = S + (ti + 16 * ai) * D + 4 * tj;
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          finite &= is_finite_f(acc[ai][c8]);
-          sr[c8] = acc[ai][c8];
+        for (int c4 = 0; c4 < 4; ++c4) {
+          finite &= is_finite_f(acc[ai][c4]);
+          sr[c4] = acc[ai][c4];
         }
       }
     }

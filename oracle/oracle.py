@@ -71,6 +71,17 @@ def _declare(L):
         "po_add_rms_norm": (i32, [vp, vp, vp, sz, f32, vp]),
         "po_l2_norm": (None, [vp, sz, f32]),
         "po_softmax_round_f16": (i32, [vp, sz]),
+        "po_kvq_splitmix": (ctypes.c_uint64, [vp]),
+        "po_kvq_levels": (None, [i32, vp]),
+        "po_kvq_record_bytes": (i32, [i32]),
+        "po_kvq_encode": (i32, [i32, ctypes.c_uint64, i32, vp, vp]),
+        "po_kvq_rotate": (i32, [i32, ctypes.c_uint64, vp, vp]),
+        "po_kvq_inverse": (i32, [i32, ctypes.c_uint64, vp]),
+        "po_kvq_score": (i32, [i32, vp, vp, vp]),
+        "po_kvq_accumulate": (i32, [i32, vp, f32, vp]),
+        "po_kvq_decode": (i32, [i32, ctypes.c_uint64, vp, vp]),
+        "po_kvq_attend_head": (i32, [i32, ctypes.c_uint64, i32, ctypes.c_uint64, vp, vp, vp, sz,
+                                     f32, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -232,6 +243,89 @@ def softmax_round_f16(v):
     v = np.array(v, dtype=np.float32)
     _check(lib().po_softmax_round_f16(_p(v), v.size))
     return v
+
+
+# ---- rotated scalar KV codec (kvq_oracle.c) --------------------------------
+KVQ_KEY_SEED = 0x5357_4946_544b_5631
+KVQ_VALUE_SEED = 0x5357_4946_5456_5631
+# policy -> (key bits, value bits, value version)
+KVQ_POLICIES = {"rsq4": (4, 4, 1), "rsq4vf": (4, 4, 2), "rsq4k3v": (4, 3, 1)}
+
+
+def kvq_levels(bits):
+    out = np.zeros(16, np.float32)
+    lib().po_kvq_levels(8 if bits == 3 else 16, _p(out))
+    return out
+
+
+def kvq_record_bytes(bits):
+    return lib().po_kvq_record_bytes(bits)
+
+
+def kvq_encode(bits, seed, rows, version=1):
+    """Records (n, 100|132) uint8 of rows (n, 256) float32."""
+    rows = np.ascontiguousarray(np.atleast_2d(rows), np.float32)
+    out = np.zeros((rows.shape[0], kvq_record_bytes(bits)), np.uint8)
+    for i in range(rows.shape[0]):
+        _check(lib().po_kvq_encode(bits, seed, version, _p(rows[i]), _p(out[i])))
+    return out
+
+
+def kvq_rotate(bits, seed, row):
+    row = np.ascontiguousarray(row, np.float32)
+    out = np.zeros(256, np.float32)
+    _check(lib().po_kvq_rotate(bits, seed, _p(row), _p(out)))
+    return out
+
+
+def kvq_inverse(bits, seed, row):
+    out = np.array(row, np.float32, copy=True)
+    _check(lib().po_kvq_inverse(bits, seed, _p(out)))
+    return out
+
+
+def kvq_score(bits, rotated_query, record):
+    q = np.ascontiguousarray(rotated_query, np.float32)
+    r = np.ascontiguousarray(record, np.uint8)
+    out = np.zeros(1, np.float32)
+    _check(lib().po_kvq_score(bits, _p(q), _p(r), _p(out)))
+    return out[0]
+
+
+def kvq_accumulate(bits, record, weight, out):
+    """In-place accumulation of weight * record into out (256 float32)."""
+    r = np.ascontiguousarray(record, np.uint8)
+    _check(lib().po_kvq_accumulate(bits, _p(r), float(weight), _p(out)))
+    return out
+
+
+def kvq_decode(bits, seed, records):
+    records = np.ascontiguousarray(np.atleast_2d(records), np.uint8)
+    out = np.zeros((records.shape[0], 256), np.float32)
+    for i in range(records.shape[0]):
+        _check(lib().po_kvq_decode(bits, seed, _p(records[i]), _p(out[i])))
+    return out
+
+
+def kvq_attend(policy, queries, keys, values, heads, kv_heads, attn_scale, gates):
+    """Every query head over n positions of packed K/V records (reference
+    src/graph/quantized_kv.rs attend_head): queries (heads, 256), keys
+    (n, kv_heads, 132), values (n, kv_heads, 100|132), gates (heads, 256)."""
+    kb, vb, _ = KVQ_POLICIES[policy]
+    keys = np.ascontiguousarray(keys, np.uint8)
+    values = np.ascontiguousarray(values, np.uint8)
+    n = keys.shape[0]
+    group = heads // kv_heads
+    out = np.zeros((heads, 256), np.float32)
+    for h in range(heads):
+        kh = h // group
+        k = np.ascontiguousarray(keys[:, kh])
+        v = np.ascontiguousarray(values[:, kh])
+        q = np.ascontiguousarray(queries[h], np.float32)
+        g = np.ascontiguousarray(gates[h], np.float32)
+        _check(lib().po_kvq_attend_head(kb, KVQ_KEY_SEED, vb, KVQ_VALUE_SEED, _p(q), _p(k), _p(v),
+                                        n, float(attn_scale), _p(g), _p(out[h])))
+    return out
 
 
 def recurrent_decay(alpha, time_bias, decay_weight):

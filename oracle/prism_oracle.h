@@ -140,6 +140,20 @@ int po_add_rms_norm(float *values, const float *delta, const float *w,
 void po_l2_norm(float *x, size_t n, float eps);
 int po_softmax_round_f16(float *v, size_t n);
 
+/* ---- rotated scalar KV codec, rsq (kvq_oracle.c) -------------------- */
+uint64_t po_kvq_splitmix(uint64_t *state);
+void po_kvq_levels(int levels, float *out);
+int po_kvq_record_bytes(int bits);
+int po_kvq_encode(int bits, uint64_t seed, int version, const float *input, uint8_t *out);
+int po_kvq_rotate(int bits, uint64_t seed, const float *input, float *out);
+int po_kvq_inverse(int bits, uint64_t seed, float *inout);
+int po_kvq_score(int bits, const float *rotated_query, const uint8_t *rec, float *out);
+int po_kvq_accumulate(int bits, const uint8_t *rec, float weight, float *out);
+int po_kvq_decode(int bits, uint64_t seed, const uint8_t *rec, float *out);
+int po_kvq_attend_head(int kbits, uint64_t kseed, int vbits, uint64_t vseed, const float *query,
+                       const uint8_t *keys, const uint8_t *values, size_t n, float attn_scale,
+                       const float *gate, float *out);
+
 #ifdef __cplusplus
 }
 #endif

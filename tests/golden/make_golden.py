@@ -85,12 +85,54 @@ def main(ref_root):
     }
     pinned = pinned_fixtures(fixtures)
     ptq = ptq_fixture(fixtures)
+    kvq = kvq_fixture(ref_root)
     for name, obj in (("tq2_0.json", tq), ("q2_k.json", kq), ("q8k_parity.json", q8k),
-                      ("pinned.json", pinned), ("ptq_reference.json", ptq)):
+                      ("pinned.json", pinned), ("ptq_reference.json", ptq),
+                      ("kvq_reference.json", kvq)):
         with open(os.path.join(HERE, name), "w") as f:
             json.dump(obj, f, indent=1)
             f.write("\n")
         print("wrote", name, len(obj.get("cases", obj)), "records")
+
+
+def kvq_fixture(ref_root):
+    """The rotated scalar KV codec's published constants and known answers:
+    the binary32 level tables (src/kv_quant/tables.rs), the SplitMix64 words
+    of seed 0 and the little-endian packing goldens (src/kv_quant/tests.rs
+    splitmix_stream_matches_independent_known_words and
+    packing_matches_fixed_little_endian_goldens), read from the source text."""
+    import re
+    import struct
+    src = os.path.join(ref_root, "src", "kv_quant")
+    with open(os.path.join(src, "tables.rs")) as f:
+        tables = f.read()
+    with open(os.path.join(src, "tests.rs")) as f:
+        tests = f.read()
+
+    def table(name):
+        body = tables.split("const %s: [f32; 16] = [" % name)[1].split("];")[0]
+        vals = [float(t.replace("_", "")) for t in re.findall(r"-?[0-9][0-9_.]*", body)]
+        assert len(vals) == 16
+        return [struct.unpack("<I", struct.pack("<f", v))[0] for v in vals]
+
+    def words(fn):
+        body = tests.split("fn %s()" % fn)[1].split("\n}\n")[0]
+        return body
+
+    sm = words("splitmix_stream_matches_independent_known_words")
+    splitmix = [int(w.replace("_", ""), 16) for w in re.findall(r"0x([0-9a-f_]{16,})", sm)]
+    pk = words("packing_matches_fixed_little_endian_goldens")
+    packs = [[int(b, 16) for b in re.findall(r"0x([0-9a-f]{2})", arr)]
+             for arr in re.findall(r"\[(0x[0-9a-f]{2}(?:, 0x[0-9a-f]{2})*)\]", pk)]
+    assert len(splitmix) == 3 and [len(p) for p in packs] == [3, 8]
+    return {
+        "source": "src/kv_quant/tables.rs THREE and FOUR; src/kv_quant/tests.rs known words",
+        "three_bits": table("THREE"),
+        "four_bits": table("FOUR"),
+        "splitmix_seed0": splitmix,
+        "pack3": packs[0],
+        "pack4": packs[1],
+    }
 
 
 def ptq_fixture(fx):

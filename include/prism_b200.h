@@ -387,6 +387,12 @@ int prism_b200_gdn_prefill_device_noalloc(prism_b200_executor *ex, int batch, in
  * (src/graph.rs:2966-3056, `qwen35.*`). */
 #define PRISM_B200_KV_F16 0
 #define PRISM_B200_KV_Q8_0 1
+/* The reference's rotated scalar KV policies (reference src/graph/
+ * quantized_kv.rs:16-84 KvCachePolicy): every full-attention position is
+ * stored as a record of the codec below per KV head, the current one too. */
+#define PRISM_B200_KV_RSQ4 2    /* "rsq4": 4-bit keys and values            */
+#define PRISM_B200_KV_RSQ4VF 3  /* "rsq4vf": values with fitted scales      */
+#define PRISM_B200_KV_RSQ4K3V 4 /* "rsq4k3v": 4-bit keys, 3-bit values      */
 
 typedef struct prism_b200_qwen35_config {
   uint32_t hidden;          /* qwen35.embedding_length            */
@@ -406,7 +412,8 @@ typedef struct prism_b200_qwen35_config {
   uint32_t conv_kernel;     /* qwen35.ssm.conv_kernel             */
   uint32_t full_interval;   /* qwen35.full_attention_interval     */
   uint32_t context;         /* KV capacity in tokens (context_limit) */
-  uint32_t kv_policy;       /* PRISM_B200_KV_F16 or PRISM_B200_KV_Q8_0 */
+  uint32_t kv_policy;       /* PRISM_B200_KV_*; the rotated policies
+                               need context <= 32768                  */
   uint32_t weight_kind;     /* PRISM_B200_KIND_TQ2_0 or _Q2_K     */
 } prism_b200_qwen35_config;
 
@@ -509,8 +516,10 @@ int prism_b200_model_ingest_async(prism_b200_model *m, size_t n);
  * (tensor-core projections over the tokens, the Gated DeltaNet recurrence
  * token after token with its state on chip, causal attention of each token
  * over its prefix).  The KV rows, recurrent and convolution state and
- * position it leaves are bit for bit those of `n` ingest steps.
- * ingest_block is the reference's synchronous form: it rejects an empty
+ * position it leaves are bit for bit those of `n` ingest steps.  Under the
+ * rotated KV policies it runs those `n` ingest steps (the reference's tiled
+ * prefill keeps their records bit for bit, tests/graph/quantized_kv.rs:
+ * 164-260).  ingest_block is the reference's synchronous form: it rejects an empty
  * block, one longer than PRISM_B200_MAX_PREFILL_BLOCK_TOKENS or a token
  * outside the vocabulary before changing any state, then places, ingests and
  * waits, returning the device status. */
@@ -532,7 +541,8 @@ int prism_b200_model_step_timings(prism_b200_model *m, float *attention_ms, floa
 
 /* State readback for parity checks: which = 0 conv history [channels][k-1],
  * 1 recurrent matrix [values][S][S], 2 keys / 3 values [position][kv*hd]
- * binary16, 4 hidden [hidden]; the last layer's activations: 5 attended,
+ * binary16 (Q8_0: [position][kv][272 B]; rotated: [position][kv][132 or
+ * 100 B] records), 4 hidden [hidden]; the last layer's activations: 5 attended,
  * 6 GDN gate projection, 7 FFN up*silu(gate), 9 logits.  Returns the byte
  * count written, or minus a status code. */
 int64_t prism_b200_model_read_state(prism_b200_model *m, uint32_t layer, uint32_t which,
@@ -547,7 +557,8 @@ int64_t prism_b200_model_read_state(prism_b200_model *m, uint32_t layer, uint32_
  * sequence gets exactly what decoding it alone gives -- the reference's
  * weight-sharing batched evaluation contract (reference src/lib.rs:255-275
  * `evaluate_batch_into`); the reference server keeps one decoder per
- * sequence (reference server/src/native_backend). */
+ * sequence (reference server/src/native_backend).  Models under a rotated
+ * KV policy are refused (E_UNSUPPORTED): they decode one sequence. */
 typedef struct prism_b200_batch prism_b200_batch;
 int prism_b200_batch_create(prism_b200_model *m, uint32_t sequences, uint32_t context,
                             prism_b200_batch **out);
@@ -635,6 +646,57 @@ uint64_t prism_b200_weight_device_bytes(const prism_b200_weight *w);
  * tcgen05.mma.kind::i8 of 128x256x32 from shared memory.  No reference
  * counterpart; the denominator of the prefill GEMM's tensor roofline. */
 int prism_b200_tensor_peak_i8(prism_b200_executor *ex, int iters, double *tops);
+
+/* ---- rotated scalar KV codec ("rsq") --------------------------------- */
+/* The reference's packed KV codec (reference src/kv_quant.rs `Quantizer`,
+ * src/kv_quant/scalar.rs, fitted_scale.rs, tables.rs) for 256-channel rows:
+ * a record is the binary32 scale |x|_2 / 16 (version 2: fitted to the codes)
+ * then 256 codes of `bits` (3 or 4) bits, packed little-endian, of the row
+ * normalised and rotated by three seeded sign flips and normalised
+ * Walsh-Hadamard transforms; 100 or 132 bytes.  The policies use the fixed
+ * seeds below (reference src/graph/quantized_kv.rs:80-84). */
+#define PRISM_B200_KVQ_KEY_SEED 0x53574946544b5631ull
+#define PRISM_B200_KVQ_VALUE_SEED 0x5357494654565631ull
+
+/* Record bytes of a codec precision: 100 (3 bits), 132 (4 bits), else 0. */
+int prism_b200_kvq_record_bytes(uint32_t bits);
+
+/* Quantizer::encode of n rows (reference src/kv_quant.rs:515-565): rows
+ * [n][256] binary32, records [n][record bytes].  version 1, or 2 for the
+ * fitted scale (Quantizer::with_fitted_scale).  A nonfinite input or a
+ * nonzero row whose scale underflows returns E_INVALID, an overflow
+ * E_NONFINITE (the device-side status rules above). */
+int prism_b200_kvq_encode(prism_b200_executor *ex, uint32_t bits, uint64_t seed,
+                          uint32_t version, const float *rows, size_t n, uint8_t *records);
+int prism_b200_kvq_encode_device(prism_b200_executor *ex, uint32_t bits, uint64_t seed,
+                                 uint32_t version, const float *rows, size_t n,
+                                 uint8_t *records, void *stream);
+
+/* Quantizer::decode of n records (reference src/kv_quant.rs:812-822):
+ * the reconstruction in the rotated basis, then the inverse rotation.  A
+ * malformed record (negative, -0 or nonfinite scale; nonzero codes with a
+ * zero scale) returns E_INVALID. */
+int prism_b200_kvq_decode(prism_b200_executor *ex, uint32_t bits, uint64_t seed,
+                          const uint8_t *records, size_t n, float *rows);
+
+/* Gated attention of `heads` query heads over `positions` records
+ * (reference src/graph/quantized_kv.rs:1302-1348 attend_head, Source
+ * arithmetic), head h reading KV head h / (heads / kv_heads): the query row
+ * rotated by the key codec, scores in four binary64 lanes times the record
+ * scale times attn_scale, softmax_round_f16 over the positions in order,
+ * the binary32 value scan in the rotated basis, the inverse value rotation,
+ * then times sigmoid(gate).  queries, gates, out: [heads][256] binary32;
+ * keys [positions][kv_heads][132], values [positions][kv_heads][132 | 100]
+ * for `policy` PRISM_B200_KV_RSQ4, _RSQ4VF or _RSQ4K3V.  1..32768
+ * positions. */
+int prism_b200_kvq_attend(prism_b200_executor *ex, uint32_t policy, const float *queries,
+                          const uint8_t *keys, const uint8_t *values, size_t positions,
+                          uint32_t heads, uint32_t kv_heads, float attn_scale, const float *gates,
+                          float *out);
+int prism_b200_kvq_attend_device(prism_b200_executor *ex, uint32_t policy, const float *queries,
+                                 const uint8_t *keys, const uint8_t *values, size_t positions,
+                                 uint32_t heads, uint32_t kv_heads, float attn_scale,
+                                 const float *gates, float *out, void *stream);
 
 #ifdef __cplusplus
 }

@@ -483,6 +483,18 @@ class Qwen35:
         return np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_uint16)),
                                      (c.context, c.kv_heads * c.head_dim))[:n].copy()
 
+    def records(self, layer, value=False):
+        """Rotated scalar KV records (kv_policy 2-4) of the cached positions:
+        uint8 (position, kv_heads, record bytes)."""
+        c = self.cfg
+        kb, vb, _ = KVQ_POLICIES[("rsq4", "rsq4vf", "rsq4k3v")[self._c.kv_policy - 2]]
+        rb = kvq_record_bytes(vb if value else kb)
+        p = (self.L.po_qwen35_values if value else self.L.po_qwen35_keys)(self.h, layer)
+        n = self.position
+        raw = np.ctypeslib.as_array(ctypes.cast(p, ctypes.POINTER(ctypes.c_uint8)),
+                                    (c.context * c.kv_heads * c.head_dim * 2,))
+        return raw[:n * c.kv_heads * rb].reshape(n, c.kv_heads, rb).copy()
+
 
 def synth_weights(kind, rows, cols, seed, stream=0, scale_lo=0.01, scale_hi=0.05):
     """Seeded synthetic packed weights on the host (the product library's

@@ -278,6 +278,55 @@ static int q8_attention(po_qwen35 *m, int l, float scale, int threads) {
   return project_group(m, m->attended, c->heads * hd, 1, wo, ro, oo, threads);
 }
 
+/* The attention of full_attention below over rotated scalar KV records
+ * (kv_policy 2 rsq4, 3 rsq4vf, 4 rsq4k3v; reference src/graph/
+ * quantized_kv.rs:16-84 KvCachePolicy and :629-657 prepare_current): the
+ * current position's normalised key and rounded value are encoded first
+ * (key: 4 bits, the key seed; value: 4 or 3 bits, the value seed, version 2
+ * for rsq4vf) and every position, the current one included, is read back as
+ * a record by attend_head. */
+#define KVQ_KEY_SEED 0x53574946544b5631ull
+#define KVQ_VALUE_SEED 0x5357494654565631ull
+static int kvq_attention(po_qwen35 *m, int l, float scale) {
+  const po_qwen35_config *c = &m->cfg;
+  const int hd = c->head_dim, npos = m->position, group = c->heads / c->kv_heads;
+  const int vbits = c->kv_policy == 4 ? 3 : 4, vversion = c->kv_policy == 3 ? 2 : 1;
+  const int kb = po_kvq_record_bytes(4), vb = po_kvq_record_bytes(vbits);
+  uint8_t *krec = (uint8_t *)m->keys[l], *vrec = (uint8_t *)m->vals[l];
+  int st;
+  for (int k = 0; k < c->kv_heads; ++k) {
+    if ((st = po_kvq_encode(4, KVQ_KEY_SEED, 1, m->key + (size_t)k * hd,
+                            krec + ((size_t)npos * c->kv_heads + k) * kb)))
+      return st;
+    if ((st = po_kvq_encode(vbits, KVQ_VALUE_SEED, vversion, m->value + (size_t)k * hd,
+                            vrec + ((size_t)npos * c->kv_heads + k) * vb)))
+      return st;
+  }
+  /* attend_head takes one KV head's records contiguous: gather them */
+  uint8_t *kk = (uint8_t *)malloc((size_t)(npos + 1) * kb);
+  uint8_t *vv = (uint8_t *)malloc((size_t)(npos + 1) * vb);
+  if (!kk || !vv) {
+    free(kk);
+    free(vv);
+    return PO_E_INVALID;
+  }
+  st = PO_OK;
+  for (int h = 0; h < c->heads && !st; ++h) {
+    const int kh = h / group;
+    if (h % group == 0)
+      for (int p = 0; p <= npos; ++p) {
+        memcpy(kk + (size_t)p * kb, krec + ((size_t)p * c->kv_heads + kh) * kb, (size_t)kb);
+        memcpy(vv + (size_t)p * vb, vrec + ((size_t)p * c->kv_heads + kh) * vb, (size_t)vb);
+      }
+    st = po_kvq_attend_head(4, KVQ_KEY_SEED, vbits, KVQ_VALUE_SEED, m->query + (size_t)h * hd, kk,
+                            vv, (size_t)npos + 1, scale, m->projected + (size_t)(2 * h + 1) * hd,
+                            m->attended + (size_t)h * hd);
+  }
+  free(kk);
+  free(vv);
+  return st;
+}
+
 /* reference src/graph.rs:4383-4950 full_attention (F16 KV, Source) */
 static int full_attention(po_qwen35 *m, int l, int threads) {
   const po_qwen35_config *c = &m->cfg;
@@ -304,6 +353,13 @@ static int full_attention(po_qwen35 *m, int l, int threads) {
   const int npos = m->position;
   const int group = c->heads / c->kv_heads;
   if (c->kv_policy == 1) return q8_attention(m, l, scale, threads);
+  if (c->kv_policy >= 2) {
+    if ((st = kvq_attention(m, l, scale))) return st;
+    const void *wo[1] = {W(m, l, PO_W_O)};
+    int ro[1] = {c->hidden};
+    float *oo[1] = {m->attn_out};
+    return project_group(m, m->attended, c->heads * hd, 1, wo, ro, oo, threads);
+  }
   for (int h = 0; h < c->heads; ++h) {
     const int off = (h / group) * hd;
     const float *q = m->query + (size_t)h * hd;

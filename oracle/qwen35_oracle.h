@@ -23,7 +23,10 @@ typedef struct po_qwen35_config {
   int32_t ffn, vocab, ssm_state, ssm_groups, ssm_values, conv_kernel, full_interval;
   int32_t context;
   uint32_t weight_kind; /* 35 (TQ2_0) or 10 (Q2_K) for every linear weight */
-  uint32_t kv_policy;   /* 0: binary16 K/V; 1: Q8_0 records (see below)      */
+  uint32_t kv_policy;   /* 0: binary16 K/V; 1: Q8_0 records (see below);
+                           2 rsq4, 3 rsq4vf, 4 rsq4k3v: the reference's
+                           rotated scalar records (kvq_oracle.c), keys and
+                           values per position [kv_heads][132 | 100 B]     */
 } po_qwen35_config;
 
 /* Q8_0 KV records (kv_policy 1; an addition of this build, not a reference

@@ -463,6 +463,9 @@ int prism_b200_batch_create_tp(prism_b200_model *m, uint32_t sequences, uint32_t
   if ((context + kAttnSplit - 1) / kAttnSplit + 1 > 16384)
     return ex->fail(PRISM_B200_E_UNSUPPORTED, "context %u exceeds the attention kernel", context);
   const auto &c = m->cfg;
+  if (m->rotated())
+    return ex->fail(PRISM_B200_E_UNSUPPORTED,
+                    "batched serving keeps binary16 or Q8_0 KV, not rotated records");
   if (tp_mode != PRISM_B200_TP_EXACT && tp_mode != PRISM_B200_TP_ALLREDUCE)
     return ex->fail(PRISM_B200_E_INVALID, "tensor-parallel mode %u", tp_mode);
   const bool allreduce = tp_mode == PRISM_B200_TP_ALLREDUCE;

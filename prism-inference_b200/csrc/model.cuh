@@ -17,6 +17,7 @@
 #include "executor.cuh"
 #include "flow.cuh"
 #include "model_kernels.cuh"
+#include "kvq.cuh"
 #include "gdn_decode.cuh"
 
 namespace prism {
@@ -91,8 +92,13 @@ struct prism_b200_model {
   int value_width() const { return (int)(cfg.ssm_state * cfg.ssm_values); }
   int channels() const { return 2 * key_width() + value_width(); }
   int kvw() const { return (int)(cfg.kv_heads * cfg.head_dim); }
+  // the reference's rotated scalar records (rsq4, rsq4vf, rsq4k3v)
+  bool rotated() const { return cfg.kv_policy >= PRISM_B200_KV_RSQ4; }
+  int value_bits() const { return cfg.kv_policy == PRISM_B200_KV_RSQ4K3V ? 3 : 4; }
   // bytes of one cached position (all KV heads) of one layer's K or V
-  size_t kv_row_bytes() const {
+  size_t kv_row_bytes(bool value = false) const {
+    if (rotated())
+      return (size_t)cfg.kv_heads * prism::kvq_record_bytes(value ? value_bits() : 4);
     return cfg.kv_policy == PRISM_B200_KV_Q8_0
                ? (size_t)cfg.kv_heads * prism::q8_0_record_bytes((int)cfg.head_dim)
                : (size_t)kvw() * 2;
@@ -203,6 +209,58 @@ inline std::vector<PfItem> step_items(prism_b200_model *m, bool head) {
   return items;
 }
 
+// The attention of a full layer over rotated scalar records (kv_policy
+// rsq4, rsq4vf, rsq4k3v; reference src/graph/quantized_kv.rs:16-84): the
+// append kernel encodes the current key and value rows at the step's
+// position, then kvq_attend_kernel attends over every record.
+inline cudaError_t launch_kvq_step(prism_b200_model *m, const ModelLayer &Ly, unsigned *status,
+                                   cudaStream_t s, bool pdl) {
+  const auto &c = m->cfg;
+  const int vbits = m->value_bits();
+  static const KvqCodec kc = kvq_codec(4, kKvqKeySeed, 1);
+  const KvqCodec vc = kvq_codec(vbits, kKvqValueSeed, c.kv_policy == PRISM_B200_KV_RSQ4VF ? 2 : 1);
+  const float theta_scale = powf(c.rope_base, -2.0f / (float)c.rope_dim);
+  KvqAppendArgs ap{};
+  ap.kc = kc;
+  ap.vc = vc;
+  ap.kv_heads = (int)c.kv_heads;
+  ap.rope_dim = (int)c.rope_dim;
+  for (int j = 0; j < 3; ++j) ap.sections[j] = (int)c.rope_sections[j];
+  ap.eps = c.eps;
+  ap.theta_scale = theta_scale;
+  ap.key_in = m->key;
+  ap.value_in = m->value;
+  ap.k_norm = Ly.k_norm;
+  ap.kcache = reinterpret_cast<uint8_t *>(Ly.kc);
+  ap.vcache = reinterpret_cast<uint8_t *>(Ly.vc);
+  ap.position = m->d_position;
+  ap.status = status;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_config(dim3(2 * c.kv_heads), dim3(kKvqDim), 0, s, attr, pdl);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kvq_append_kernel, ap);
+  if (e != cudaSuccess) return e;
+  KvqAttnArgs at{};
+  at.kc = kc;
+  at.vc = vc;
+  at.heads = (int)c.heads;
+  at.kv_heads = (int)c.kv_heads;
+  at.projected = m->projected;
+  at.q_norm = Ly.q_norm;
+  at.eps = c.eps;
+  at.theta_scale = theta_scale;
+  at.rope_dim = (int)c.rope_dim;
+  for (int j = 0; j < 3; ++j) at.sections[j] = (int)c.rope_sections[j];
+  at.gate = m->projected + kKvqDim;  // head h's gate row follows its query row
+  at.gate_stride = 2 * kKvqDim;
+  at.keys = ap.kcache;
+  at.values = ap.vcache;
+  at.position = m->d_position;
+  at.attn_scale = 1.0f / 16.0f;  // 1 / sqrt(256)
+  at.out = m->attended;
+  at.status = status;
+  return launch_kvq_attend(at, (int)c.context, s, pdl);
+}
+
 // Enqueue one decode step.  With `head`, the step ends with the tied LM head,
 // the greedy key and (past the prompt) the next input token.
 // `ev` (optional, 2*layers + 4 events) brackets the phases for per-layer
@@ -288,38 +346,45 @@ inline cudaError_t enqueue_step(prism_b200_model *m, bool head, cudaEvent_t *ev 
       a.w[1] = mv_weight(Ly.k, m->key);
       a.w[2] = mv_weight(Ly.v, m->value);
       if ((e = launch_mv(kEpiStore, a)) != cudaSuccess) return e;
-      AttnArgs aa{};
-      aa.heads = (int)c.heads;
-      aa.kv_heads = (int)c.kv_heads;
-      aa.hd = (int)c.head_dim;
-      aa.rope_dim = (int)c.rope_dim;
-      for (int j = 0; j < 3; ++j) aa.sections[j] = (int)c.rope_sections[j];
-      aa.eps = c.eps;
-      aa.theta_scale = powf(c.rope_base, -2.0f / (float)c.rope_dim);
-      aa.projected = m->projected;
-      aa.key_in = m->key;
-      aa.value_in = m->value;
-      aa.q_norm = Ly.q_norm;
-      aa.k_norm = Ly.k_norm;
-      aa.kcache = Ly.kc;
-      aa.vcache = Ly.vc;
-      aa.q8 = c.kv_policy == PRISM_B200_KV_Q8_0 ? 1 : 0;
-      aa.position = m->d_position;
-      aa.attended = m->attended;
-      aa.status = status;
-      aa.trace = trace_slot();
-      // one 8-CTA cluster per query head (split over the cached positions)
-      const size_t smem = attn_launch_smem(aa, (int)c.context);
-      cudaLaunchAttribute cattr[2];
-      cudaLaunchConfig_t cfg = pdl_config(dim3(c.heads * kAttnSplit), dim3(kAttnThreads), smem,
-                                          s, cattr, pdl);
-      cattr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
-      cattr[cfg.numAttrs].val.clusterDim.x = kAttnSplit;
-      cattr[cfg.numAttrs].val.clusterDim.y = 1;
-      cattr[cfg.numAttrs].val.clusterDim.z = 1;
-      cfg.numAttrs += 1;
-      if ((e = cudaLaunchKernelEx(&cfg, attention_decode_kernel, aa)) != cudaSuccess) return e;
-      ++item;
+      if (m->rotated()) {
+        // the reference's rotated scalar records: encode the current K/V
+        // rows, then attend over every record
+        if ((e = launch_kvq_step(m, Ly, status, s, pdl)) != cudaSuccess) return e;
+        ++item;
+      } else {
+        AttnArgs aa{};
+        aa.heads = (int)c.heads;
+        aa.kv_heads = (int)c.kv_heads;
+        aa.hd = (int)c.head_dim;
+        aa.rope_dim = (int)c.rope_dim;
+        for (int j = 0; j < 3; ++j) aa.sections[j] = (int)c.rope_sections[j];
+        aa.eps = c.eps;
+        aa.theta_scale = powf(c.rope_base, -2.0f / (float)c.rope_dim);
+        aa.projected = m->projected;
+        aa.key_in = m->key;
+        aa.value_in = m->value;
+        aa.q_norm = Ly.q_norm;
+        aa.k_norm = Ly.k_norm;
+        aa.kcache = Ly.kc;
+        aa.vcache = Ly.vc;
+        aa.q8 = c.kv_policy == PRISM_B200_KV_Q8_0 ? 1 : 0;
+        aa.position = m->d_position;
+        aa.attended = m->attended;
+        aa.status = status;
+        aa.trace = trace_slot();
+        // one 8-CTA cluster per query head (split over the cached positions)
+        const size_t smem = attn_launch_smem(aa, (int)c.context);
+        cudaLaunchAttribute cattr[2];
+        cudaLaunchConfig_t cfg = pdl_config(dim3(c.heads * kAttnSplit), dim3(kAttnThreads), smem,
+                                            s, cattr, pdl);
+        cattr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+        cattr[cfg.numAttrs].val.clusterDim.x = kAttnSplit;
+        cattr[cfg.numAttrs].val.clusterDim.y = 1;
+        cattr[cfg.numAttrs].val.clusterDim.z = 1;
+        cfg.numAttrs += 1;
+        if ((e = cudaLaunchKernelEx(&cfg, attention_decode_kernel, aa)) != cudaSuccess) return e;
+        ++item;
+      }
       MvArgs o;
       o.prologue = kProF32;
       o.in0 = m->attended;
@@ -592,6 +657,7 @@ inline bool flow_eligible(prism_b200_model *m, const std::vector<FPhase> &P) {
   if ((int)(c.heads * kAttnSplit) > sms || (int)(c.ssm_values * kGdnSlices) > sms) return false;
   if (c.ssm_state != 128 || c.head_dim != 256 || c.conv_kernel > 8) return false;
   if (c.context > (uint32_t)kFAttnMaxPos) return false;
+  if (m->rotated()) return false;  // rotated records: the kernel sequence
   if (P.size() > 255) return false;  // the phase index is an 8-bit tag field
   for (const FPhase &ph : P) {
     if (ph.type != kFProj) continue;
@@ -709,7 +775,8 @@ int prism_b200_model_create(prism_b200_executor *ex, const prism_b200_qwen35_con
       (c.ssm_state * c.ssm_values) % 256 == 0 && c.conv_kernel >= 1 && c.conv_kernel <= 8 &&
       c.full_interval > 0 && c.context > 0 && c.context <= (1u << 20) && c.eps > 0.0f &&
       c.rope_base > 0.0f &&
-      (c.kv_policy == PRISM_B200_KV_F16 || c.kv_policy == PRISM_B200_KV_Q8_0) &&
+      c.kv_policy <= PRISM_B200_KV_RSQ4K3V &&
+      (c.kv_policy < PRISM_B200_KV_RSQ4 || c.context <= (uint32_t)kKvqMaxPos) &&
       (c.weight_kind == PRISM_B200_KIND_TQ2_0 || c.weight_kind == PRISM_B200_KIND_Q2_K) &&
       c.hidden / 256 <= (uint32_t)kMaxNb && c.ffn / 256 <= (uint32_t)kMaxNb &&
       c.heads * c.head_dim / 256 <= (uint32_t)kMaxNb;
@@ -779,7 +846,7 @@ int prism_b200_model_create(prism_b200_executor *ex, const prism_b200_qwen35_con
       A(Ly.q_norm, c.head_dim);
       A(Ly.k_norm, c.head_dim);
       A(Ly.kc, ((size_t)c.context * m->kv_row_bytes() + 1) / 2);
-      A(Ly.vc, ((size_t)c.context * m->kv_row_bytes() + 1) / 2);
+      A(Ly.vc, ((size_t)c.context * m->kv_row_bytes(true) + 1) / 2);
     } else {
       A(Ly.conv_w, (size_t)m->channels() * c.conv_kernel);
       A(Ly.dt_bias, c.ssm_values);
@@ -978,7 +1045,7 @@ int prism_b200_model_reset(prism_b200_model *m) {
   for (auto &Ly : m->L) {
     if (Ly.full) {
       CK(cudaMemsetAsync(Ly.kc, 0, (size_t)c.context * m->kv_row_bytes(), s), "reset");
-      CK(cudaMemsetAsync(Ly.vc, 0, (size_t)c.context * m->kv_row_bytes(), s), "reset");
+      CK(cudaMemsetAsync(Ly.vc, 0, (size_t)c.context * m->kv_row_bytes(true), s), "reset");
     } else {
       CK(cudaMemsetAsync(Ly.conv_state, 0, (size_t)2 * m->channels() * (c.conv_kernel - 1) * 4, s),
          "reset");
@@ -1242,7 +1309,7 @@ int64_t prism_b200_model_read_state(prism_b200_model *m, uint32_t layer, uint32_
       n = (size_t)c.ssm_values * c.ssm_state * c.ssm_state * 4;
     } else if ((which == 2 || which == 3) && Ly.full) {
       src = which == 2 ? Ly.kc : Ly.vc;
-      n = (size_t)m->position * m->kv_row_bytes();
+      n = (size_t)m->position * m->kv_row_bytes(which == 3);
     }
   }
   if (!src) return -PRISM_B200_E_INVALID;

@@ -1032,6 +1032,10 @@ int prism_b200_model_prefill_async(prism_b200_model *m, size_t n) {
   if (n == 0) return ex->fail(PRISM_B200_E_INVALID, "prefill needs at least one token");
   if (m->position + (int64_t)n > (int64_t)m->cfg.context)
     return ex->fail(PRISM_B200_E_INVALID, "context is exhausted");
+  // rotated records: one-token steps (the reference's tiled prefill keeps
+  // the sequential steps' records bit for bit, tests/graph/quantized_kv.rs:
+  // 164-260)
+  if (m->rotated()) return prism_b200_model_ingest_async(m, n);
   cudaSetDevice(ex->device);
   CK(prefill_alloc(m), "prefill buffers");
   for (size_t done = 0; done < n; done += kPrefillChunk) {

@@ -45,6 +45,16 @@ class _Tensor(ctypes.Structure):
 
 _lib = None
 
+# KV policies (include/prism_b200.h): the reference's rotated scalar records
+KV_RSQ4, KV_RSQ4VF, KV_RSQ4K3V = 2, 3, 4
+KVQ_KEY_SEED = 0x5357_4946_544b_5631
+KVQ_VALUE_SEED = 0x5357_4946_5456_5631
+
+
+def kvq_record_bytes(bits):
+    """Record bytes of a codec precision: 100 (3 bits), 132 (4 bits), else 0."""
+    return {3: 100, 4: 132}.get(int(bits), 0)
+
 
 def load():
     """Load the built library; raise if it is missing (no fallback)."""
@@ -92,6 +102,14 @@ def load():
         "prism_b200_ffn_chain_tokens_device": (i32, [vp, sz, vp, vp, i32, vp, vp]),
         "prism_b200_executor_operation_capacity": (i64, [vp]),
         "prism_b200_tensor_peak_i8": (i32, [vp, i32, P(ctypes.c_double)]),
+        "prism_b200_kvq_record_bytes": (i32, [u32]),
+        "prism_b200_kvq_encode": (i32, [vp, u32, u64, u32, vp, sz, vp]),
+        "prism_b200_kvq_encode_device": (i32, [vp, u32, u64, u32, vp, sz, vp, vp]),
+        "prism_b200_kvq_decode": (i32, [vp, u32, u64, vp, sz, vp]),
+        "prism_b200_kvq_attend": (i32, [vp, u32, vp, vp, vp, sz, u32, u32, ctypes.c_float, vp,
+                                        vp]),
+        "prism_b200_kvq_attend_device": (i32, [vp, u32, vp, vp, vp, sz, u32, u32,
+                                               ctypes.c_float, vp, vp, vp]),
         "prism_b200_executor_supports_f32": (i32, [vp, P(_Tensor)]),
         "prism_b200_executor_supports_f32_group": (i32, [vp, sz, P(P(_Tensor))]),
         "prism_b200_executor_supports_q8": (i32, [vp, P(_Tensor)]),
@@ -239,6 +257,58 @@ class ProjectionExecutor:
         v = ctypes.c_double(0.0)
         self._check(load().prism_b200_tensor_peak_i8(self.h, iters, ctypes.byref(v)))
         return v.value
+
+    # -- rotated scalar KV codec (reference src/kv_quant.rs) --------------
+    def kvq_encode(self, bits, seed, rows, version=1):
+        """Quantizer::encode of rows (n, 256) float32 -> records (n, 100|132)."""
+        rows = np.ascontiguousarray(np.atleast_2d(rows), dtype=np.float32)
+        if rows.ndim != 2 or rows.shape[1] != 256:
+            raise PrismB200Error(E_INVALID, "codec rows must be [n][256]")
+        out = np.zeros((rows.shape[0], max(kvq_record_bytes(bits), 1)), np.uint8)
+        self._check(load().prism_b200_kvq_encode(self.h, bits, seed, version, _p(rows),
+                                                 rows.shape[0], _p(out)))
+        return out
+
+    def kvq_encode_device(self, bits, seed, rows_ptr, n, records_ptr, version=1, stream=None):
+        self._check(load().prism_b200_kvq_encode_device(self.h, bits, seed, version, rows_ptr, n,
+                                                        records_ptr, stream))
+
+    def kvq_decode(self, bits, seed, records):
+        """Quantizer::decode of records (n, 100|132) -> rows (n, 256)."""
+        records = np.ascontiguousarray(np.atleast_2d(records), dtype=np.uint8)
+        if records.shape[1] != kvq_record_bytes(bits):
+            raise PrismB200Error(E_INVALID, "records must be [n][record bytes]")
+        out = np.zeros((records.shape[0], 256), np.float32)
+        self._check(load().prism_b200_kvq_decode(self.h, bits, seed, _p(records),
+                                                 records.shape[0], _p(out)))
+        return out
+
+    def kvq_attend(self, policy, queries, keys, values, attn_scale, gates):
+        """Gated attention of every query head over packed K/V records
+        (reference src/graph/quantized_kv.rs attend_head): queries, gates
+        (heads, 256) float32; keys (n, kv_heads, 132), values
+        (n, kv_heads, 132|100) uint8."""
+        queries = np.ascontiguousarray(queries, dtype=np.float32)
+        gates = np.ascontiguousarray(gates, dtype=np.float32)
+        keys = np.ascontiguousarray(keys, dtype=np.uint8)
+        values = np.ascontiguousarray(values, dtype=np.uint8)
+        heads, kv_heads = queries.shape[0], keys.shape[1]
+        vbits = 3 if policy == KV_RSQ4K3V else 4
+        if (queries.shape != (heads, 256) or gates.shape != queries.shape or keys.ndim != 3
+                or keys.shape[2] != 132 or values.shape != keys.shape[:2] +
+                (kvq_record_bytes(vbits),)):
+            raise PrismB200Error(E_INVALID, "attention extents")
+        out = np.zeros((heads, 256), np.float32)
+        self._check(load().prism_b200_kvq_attend(self.h, policy, _p(queries), _p(keys),
+                                                 _p(values), keys.shape[0], heads, kv_heads,
+                                                 float(attn_scale), _p(gates), _p(out)))
+        return out
+
+    def kvq_attend_device(self, policy, queries_ptr, keys_ptr, values_ptr, positions, heads,
+                          kv_heads, attn_scale, gates_ptr, out_ptr, stream=None):
+        self._check(load().prism_b200_kvq_attend_device(
+            self.h, policy, queries_ptr, keys_ptr, values_ptr, positions, heads, kv_heads,
+            float(attn_scale), gates_ptr, out_ptr, stream))
 
     def operation_capacity(self):
         """Remaining submissions of a bounded session, None when opaque

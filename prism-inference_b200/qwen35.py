@@ -157,6 +157,8 @@ class _CConfig(__import__("ctypes").Structure):
 
 
 KV_F16, KV_Q8_0 = 0, 1
+# the reference's rotated scalar policies: rsq4, rsq4vf, rsq4k3v
+KV_RSQ4, KV_RSQ4VF, KV_RSQ4K3V = 2, 3, 4
 
 
 def c_config(cfg, kv_policy=KV_F16):
@@ -309,6 +311,19 @@ class Qwen35Model:
         shape, dt = shapes[which]
         out = np.zeros(shape, dt)
         n = self.L.prism_b200_model_read_state(self.h, layer, which, out.ctypes.data, out.nbytes)
+        if n < 0:
+            raise pb.PrismB200Error(-n, "state readback failed")
+        return out
+
+    def records(self, layer, value=False):
+        """The rotated scalar KV records (kv_policy KV_RSQ4, _RSQ4VF,
+        _RSQ4K3V) of a full layer: uint8 (position, kv_heads, record bytes)."""
+        c = self.cfg
+        bits = 3 if (value and self._cc.kv_policy == KV_RSQ4K3V) else 4
+        rb = pb.kvq_record_bytes(bits)
+        out = np.zeros((self.position, c.kv_heads, rb), np.uint8)
+        n = self.L.prism_b200_model_read_state(self.h, layer, 3 if value else 2,
+                                               out.ctypes.data, out.nbytes)
         if n < 0:
             raise pb.PrismB200Error(-n, "state readback failed")
         return out

@@ -59,3 +59,31 @@ def test_small_model_runs_and_is_deterministic(oracle):
     a2 = [m1.step(t) for t in toks][-1]
     assert np.array_equal(a2, a)
     assert oracle.greedy(np.array([1, 3, 3, 2], np.float32)) == 1
+
+
+@pytest.mark.parametrize("policy", [2, 3, 4])
+def test_small_model_with_rotated_kv_records(oracle, policy):
+    """The rotated scalar KV policies (2 rsq4, 3 rsq4vf, 4 rsq4k3v) store
+    every position as a record that decodes near the binary16 policy's row,
+    and the logits stay near the binary16 policy's (the codec is lossy)."""
+    cfg = qwen35.SMALL
+    W = qwen35.synthetic_weights(cfg, seed=3)
+    exact = oracle.Qwen35(cfg, W)
+    packed = oracle.Qwen35(cfg, W, kv_policy=policy)
+    toks = qwen35.prompt_tokens(cfg, 5, seed=4)
+    for t in toks:
+        a = exact.step(t, threads=2)
+        b = packed.step(t, threads=2)
+        assert np.all(np.isfinite(b))
+    assert np.max(np.abs(a - b)) < 0.1 * max(1.0, np.max(np.abs(a)))
+    kb, vb, _ = oracle.KVQ_POLICIES[("rsq4", "rsq4vf", "rsq4k3v")[policy - 2]]
+    layer = next(l for l in range(cfg.layers) if (l + 1) % cfg.full_interval == 0)
+    keys = packed.records(layer)
+    vals = packed.records(layer, value=True)
+    assert keys.shape == (5, cfg.kv_heads, 132)
+    assert vals.shape == (5, cfg.kv_heads, oracle.kvq_record_bytes(vb))
+    ref_k = exact.keys(layer).view(np.float16).astype(np.float32).reshape(5, cfg.kv_heads, 256)
+    dec = oracle.kvq_decode(kb, oracle.KVQ_KEY_SEED, keys.reshape(-1, 132)).reshape(ref_k.shape)
+    # the first position saw identical inputs under both policies
+    err = np.sum((dec[0] - ref_k[0]) ** 2) / np.sum(ref_k[0] ** 2)
+    assert err < 0.04

@@ -23,7 +23,9 @@ of W (277 MB > L2).
 prefill of 4096 tokens); ``--workload gemm`` is configs[3] (2048-token
 projections on the tensor cores, TQ2_0 and Q2_K, both FFN shapes);
 ``--workload serve`` is configs[4] (256 sequences per GPU with 8192-token
-Q8_0 KV contexts, greedy batched decode).
+Q8_0 KV contexts, greedy batched decode).  ``--workload kvq`` times the
+reference's rotated scalar KV attention (rsq4 / rsq4k3v records) at the
+configs[1] head geometry over 2048-32768 positions, and the codec's encode.
 
 ``--impl reference`` times the reference's CPU arithmetic on the host
 cores -- the C restatement in oracle/, since the Rust reference cannot be
@@ -729,6 +731,154 @@ def run_gdn(args):
 
 GEMM_M = 2048
 GEMM_SHAPES = [(2560, 9216), (9216, 2560)]   # (K, N): gate/up and down
+KVQ_METRIC = "rotated KV attention positions/s (configs[1] heads, rsq4, 8192 positions)"
+KVQ_CONTEXTS = (2048, 8192, 32768)
+
+
+def cpu_kvq_baseline(seconds=10.0, n=2048):
+    """The oracle's attend_head (the reference's scalar Source arithmetic)
+    over n rsq4 positions for the 16 heads of configs[1], one thread."""
+    from oracle import oracle
+    rng = np.random.default_rng(0)
+    k = rng.standard_normal((n * 4, 256)).astype(np.float16).astype(np.float32)
+    v = rng.standard_normal((n * 4, 256)).astype(np.float16).astype(np.float32)
+    keys = oracle.kvq_encode(4, oracle.KVQ_KEY_SEED, k).reshape(n, 4, -1)
+    vals = oracle.kvq_encode(4, oracle.KVQ_VALUE_SEED, v).reshape(n, 4, -1)
+    q = rng.standard_normal((16, 256)).astype(np.float16).astype(np.float32)
+    g = rng.standard_normal((16, 256)).astype(np.float32)
+    reps, t0 = 0, time.perf_counter()
+    while reps < 1 or time.perf_counter() - t0 < seconds:
+        oracle.kvq_attend("rsq4", q, keys, vals, 16, 4, 1 / 16, g)
+        reps += 1
+    dt = time.perf_counter() - t0
+    return {"value": reps * n * 16 / dt, "unit": "positions/s", "cores": 1, "kind": "port",
+            "sample": "%d calls of the oracle's rsq4 attend_head over %d positions x 16 "
+                      "heads (4 KV heads), %.1f s" % (reps, n, dt)}
+
+
+def run_kvq(args):
+    """The reference's rotated scalar KV attention (src/graph/quantized_kv.rs
+    attend_head) on the device at the configs[1] attention geometry: 16
+    query heads over 4 KV heads of 256 channels, 2048 / 8192 / 32768 cached
+    positions, rsq4 (132 B keys and values) and rsq4k3v (100 B values).
+    Record sets rotate so that every launch reads them from HBM; the codec's
+    encode throughput is measured alongside."""
+    import torch
+    import prism_b200 as pb
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ex = pb.ProjectionExecutor(local)
+    peak, peak_src = peaks()
+    H, KV = 16, 4
+    s = torch.cuda.Stream(device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    out = {}
+    for policy, name in ((pb.KV_RSQ4, "rsq4"), (pb.KV_RSQ4K3V, "rsq4k3v")):
+        vbits = 3 if policy == pb.KV_RSQ4K3V else 4
+        vb = pb.kvq_record_bytes(vbits)
+        for n in KVQ_CONTEXTS:
+            per = n * KV * (132 + vb)
+            copies = max(2, int(300e6 // per) + 1)
+            sets = []
+            with torch.cuda.stream(s):  # the rows and their encodes on one stream
+                for c in range(copies):
+                    kr = torch.randn(n * KV, 256, device=dev, generator=g).half().float()
+                    vr = torch.randn(n * KV, 256, device=dev, generator=g).half().float()
+                    keys = torch.empty(n * KV * 132, dtype=torch.uint8, device=dev)
+                    vals = torch.empty(n * KV * vb, dtype=torch.uint8, device=dev)
+                    ex.kvq_encode_device(4, pb.KVQ_KEY_SEED, kr.data_ptr(), n * KV,
+                                         keys.data_ptr(), stream=s.cuda_stream)
+                    ex.kvq_encode_device(vbits, pb.KVQ_VALUE_SEED, vr.data_ptr(), n * KV,
+                                         vals.data_ptr(), stream=s.cuda_stream)
+                    sets.append((keys, vals))
+                    del kr, vr
+            torch.cuda.synchronize()
+            ex.sync()
+            q = torch.randn(H, 256, device=dev, generator=g).half().float()
+            gate = torch.randn(H, 256, device=dev, generator=g)
+            o = torch.empty(H, 256, device=dev)
+            torch.cuda.synchronize()
+
+            def launch(i):
+                keys, vals = sets[i % copies]
+                ex.kvq_attend_device(policy, q.data_ptr(), keys.data_ptr(), vals.data_ptr(), n,
+                                     H, KV, 1 / 16, gate.data_ptr(), o.data_ptr(),
+                                     stream=s.cuda_stream)
+            for i in range(max(args.warmup, 3)):
+                launch(i)
+            K = 20
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=s):
+                for i in range(K):
+                    launch(i)
+            with torch.cuda.stream(s):
+                gr.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with Clocks(local) as clk:
+                e0.record(s)
+                with torch.cuda.stream(s):
+                    gr.replay()
+                e1.record(s)
+                torch.cuda.synchronize()
+            ex.sync()
+            us = e0.elapsed_time(e1) * 1e3 / K
+            out["%s_%d" % (name, n)] = {
+                "us_per_launch": us, "positions_per_s": n * H / (us * 1e-6),
+                "record_bytes": per, "gbs": per / us / 1e3, "hbm_frac": per / us / 1e3 / peak,
+                "clocks": clk.summary()}
+            del gr, sets
+    # encode throughput: 65536 rows of 256 channels, 4-bit, version 1 and 2
+    rows = torch.randn(65536, 256, device=dev, generator=g)
+    recs = torch.empty(65536 * 132, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+    enc = {}
+    for ver in (1, 2):
+        def encode():
+            ex.kvq_encode_device(4, pb.KVQ_KEY_SEED, rows.data_ptr(), 65536, recs.data_ptr(),
+                                 version=ver, stream=s.cuda_stream)
+        encode()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(5):
+            encode()
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 5
+        enc["v%d" % ver] = {"ms": ms, "rows_per_s": 65536 / (ms * 1e-3),
+                            "gbs": 65536 * (1024 + 132) / (ms * 1e-3) / 1e9}
+    ex.sync()
+    ex.close()
+    head = out["rsq4_8192"]
+    cb = None if args.no_cpu else cpu_kvq_baseline(seconds=10.0)
+    line = {
+        "metric": KVQ_METRIC, "value": head["positions_per_s"], "unit": "positions/s",
+        "n_gpus": 1, "steps": 20, "warmup": max(args.warmup, 3),
+        "ms_per_step": head["us_per_launch"] / 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64 scores, f32 values",
+        "data": "synthetic: N(0,1) rows rounded to binary16, encoded on the device",
+        "config": {"workload": "configs[1] attention geometry (16 q / 4 kv heads x 256) over "
+                               "rotated scalar records, one launch per layer-token",
+                   "l2": "record sets rotate over > 300 MB per context"},
+        "attention": out, "encode_65536_rows": enc,
+        "roofline": {"bound": "hbm", "achieved": head["gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": head["hbm_frac"], "peak_source": peak_src,
+                     "kernel": "kvq_attend_kernel (rsq4, 8192 positions)",
+                     "traffic": traffic_from_profiles("kvq_attend_kernel"),
+                     "traffic_source": TRAFFIC_SOURCE,
+                     "note": "latency-bound, not HBM-bound: each CTA's 32 binary32 value "
+                             "chains run in position order (the reference's accumulation "
+                             "contract), fed by the other warps; the binary64 score lanes "
+                             "and the in-order chains set the time (profiles/"
+                             "kvq_attend_rsq4.md)"},
+        "cpu_baseline": cb, "gpu_launches": 20,
+    }
+    print(json.dumps(line), flush=True)
+
+
 GEMM_METRIC = "prefill GEMM int-op/s (2048 tokens x Q8_K, TQ2_0 and Q2_K weights)"
 
 
@@ -1284,6 +1434,9 @@ def run_reference(args):
     elif args.workload == "gdn":
         cb = cpu_gdn_baseline(seconds=20.0)
         metric, unit = GDN_METRIC, "GB/s"
+    elif args.workload == "kvq":
+        cb = cpu_kvq_baseline(seconds=20.0, n=8192)
+        metric, unit = KVQ_METRIC, "positions/s"
     else:
         import qwen35
         from oracle import oracle
@@ -1328,6 +1481,8 @@ def run_reference(args):
                                 "attention cost is not included): " % PROMPT) + cb["sample"]
     if unit == "tok/s":
         ms_per_step = 1e3 / cb["value"]
+    elif unit == "positions/s":
+        ms_per_step = 8192 * 16 / cb["value"] * 1e3
     elif unit == "Tint-op/s":
         ms_per_step = 2.0 * GEMM_M * GEMM_SHAPES[0][0] * GEMM_SHAPES[0][1] / (cb["value"] * 1e9)
     elif args.workload == "gdn":
@@ -1382,7 +1537,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "matvec", "gdn", "gemm", "serve",
-                                                                "prefill"])
+                                                                "prefill", "kvq"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-matvec", action="store_true", help="skip the configs[0] sub-benchmark")
     ap.add_argument("--phase-trace", action="store_true",
@@ -1414,6 +1569,8 @@ def main():
         run_matvec(args)
     elif args.workload == "prefill":
         run_prefill(args)
+    elif args.workload == "kvq":
+        run_kvq(args)
     else:
         run_decode(args)
     import torch

@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "executor.cuh"
+#include "flow.cuh"  // cp_async4, cp_async_commit, cp_async_wait_*
 #include "model_kernels.cuh"
 
 namespace prism {
@@ -35,7 +36,7 @@ namespace prism {
 constexpr int kKvqDim = 256;
 constexpr int kKvqSplit = 8;        // CTAs (one cluster) per query head
 constexpr int kKvqMaxPos = 32768;   // positions one attention launch serves
-constexpr int kKvqChunk = 256;      // value-scan staging chunk, positions
+constexpr int kKvqChunk = 128;      // value-scan staging chunk, positions
 constexpr uint64_t kKvqKeySeed = 0x53574946544b5631ull;    // reference KEY_SEED
 constexpr uint64_t kKvqValueSeed = 0x5357494654565631ull;  // reference VALUE_SEED
 
@@ -111,16 +112,20 @@ __device__ __forceinline__ float kvq_hadamard(float v, float *sh, bool &finite) 
 }
 
 // Quantizer::rotate / forward (reference src/kv_quant.rs:479-488, 831-848).
-__device__ __forceinline__ float kvq_forward(const KvqCodec &c, float v, float *sh, bool &finite) {
+__device__ __forceinline__ float kvq_forward(const KvqCodec &c, float v, float *sh,
+                                             bool &finite) {
   finite = true;
-  for (int p = 0; p < 3 && finite; ++p) v = kvq_hadamard(kvq_sign(c, p, threadIdx.x, v), sh, finite);
+  for (int p = 0; p < 3 && finite; ++p)
+    v = kvq_hadamard(kvq_sign(c, p, threadIdx.x, v), sh, finite);
   return v;
 }
 
 // Quantizer::inverse (reference src/kv_quant.rs:490-525).
-__device__ __forceinline__ float kvq_inverse(const KvqCodec &c, float v, float *sh, bool &finite) {
+__device__ __forceinline__ float kvq_inverse(const KvqCodec &c, float v, float *sh,
+                                             bool &finite) {
   finite = true;
-  for (int p = 2; p >= 0 && finite; --p) v = kvq_sign(c, p, threadIdx.x, kvq_hadamard(v, sh, finite));
+  for (int p = 2; p >= 0 && finite; --p)
+    v = kvq_sign(c, p, threadIdx.x, kvq_hadamard(v, sh, finite));
   return v;
 }
 
@@ -137,7 +142,8 @@ struct KvqEncodeSmem {
 // src/kv_quant/fitted_scale.rs:8-48): thread i holds channel i of the row.
 // Writes the record (when `rec` is set) and returns 0, or returns the status
 // bit of the failure and writes nothing.  Every return is block-uniform.
-__device__ unsigned kvq_encode_row(float x, const KvqCodec &c, uint8_t *rec, KvqEncodeSmem &sm) {
+__device__ unsigned kvq_encode_row(float x, const KvqCodec &c, uint8_t *rec,
+                                   KvqEncodeSmem &sm) {
   const int i = threadIdx.x;
   const int nlev = c.bits == 3 ? 8 : 16;
   sm.row[i] = x;
@@ -359,41 +365,90 @@ struct KvqAttnArgs {
   float attn_scale;
   float *out;                   // [heads][256]
   unsigned *status;
+  // optional timeline (CTA 0): [0] start, [1] query rotated, [2] scores,
+  // [3] scores gathered, [4] softmax total, [5] value scan done, [6]/[7] exit
+  unsigned long long *trace;
 };
 
-// Dynamic shared memory of a kvq_attend_kernel launch serving up to `cap`
-// positions: the score row, then two value staging buffers.
+// Shared memory of kvq_attend_kernel: the score row (`cap` positions,
+// padded to 16 B), then a region the phases take in turn -- two buffers of
+// staged key records during the scores; during the value scan its ring of
+// raw value words (per chunk: the scales, then 16-byte code slices) and two
+// chunks of increments ([position][channel], rows of 36 words).
+constexpr int kKvqKeyChunk = 224;  // key records per staging buffer
+constexpr int kKvqRing = 8;        // raw value chunks: 6 in flight, 1 forming, 1 free
+constexpr int kKvqIncRow = 36;     // words per position row of increments
+constexpr size_t kKvqKeyBytes = (size_t)2 * kKvqKeyChunk * 33 * 4;
+constexpr size_t kKvqRawChunk = (size_t)kKvqChunk * 5 * 4;  // scales + slices
+constexpr size_t kKvqRawBytes = (size_t)kKvqRing * kKvqRawChunk;
+constexpr size_t kKvqIncBytes = (size_t)2 * kKvqChunk * kKvqIncRow * 4;
+constexpr size_t kKvqUnionBytes =
+    kKvqKeyBytes > kKvqRawBytes + kKvqIncBytes ? kKvqKeyBytes : kKvqRawBytes + kKvqIncBytes;
+
+__host__ __device__ constexpr size_t kvq_score_bytes(int cap) {
+  return ((size_t)cap * 4 + 15) / 16 * 16;
+}
 __host__ __device__ constexpr size_t kvq_attend_smem(int cap) {
-  return ((size_t)cap * 4 + 15) / 16 * 16 + 2 * (size_t)kKvqChunk * 5 * 4;
+  return kvq_score_bytes(cap) + kKvqUnionBytes;
 }
 
+// Head h of the cluster's 8 CTAs.  Each CTA scores a contiguous share of the
+// positions (a thread per position over the share's key records, staged by
+// asynchronous copies), the CTAs exchange their maxima, exponentiate their
+// shares and gather every share's exponentials; each then forms the total,
+// the binary16 probabilities and the value chains of its 32 channels, and
+// all 8 rebuild the inverse rotation of the 256.  VB: value code bits.
+template <int VB>
 __global__ void __launch_bounds__(kKvqDim) kvq_attend_kernel(KvqAttnArgs a) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(16) float kvq_dyn[];
-  __shared__ double qd[kKvqDim];
+  __shared__ __align__(16) double qd[kKvqDim];
   __shared__ double levk[16];
   __shared__ float levv[16];
   __shared__ float sh[kKvqDim], cs[64], buf[kKvqDim];
   __shared__ float vout[32];
   __shared__ double red[kKvqDim / 32];
   __shared__ float fred[kKvqDim / 32];
-  __shared__ float s_inv;
+  __shared__ float s_max, s_emin, s_inv;
+  __shared__ double s_sum;
   const int i = threadIdx.x, warp = i >> 5, lane = i & 31;
   const int rank = (int)cluster.block_rank();
   const int h = blockIdx.x / kKvqSplit;
   const int kvh = h / (a.heads / a.kv_heads);
+  trace_stamp(a.trace, 0);
   if (i < 16) {
     levk[i] = (double)kvq_level(4, i);
-    levv[i] = i < (1 << a.vc.bits) ? kvq_level(a.vc.bits, i) : 0.0f;
+    levv[i] = i < (1 << VB) ? kvq_level(VB, i) : 0.0f;
   }
   const int pos = a.position ? *a.position : 0;
   if (a.projected && i < a.rope_dim / 2) kvq_rope_pair(i, pos, a.theta_scale, a.sections, cs);
   grid_dependency_wait();
   grid_dependents_launch();
-  __syncthreads();
   unsigned bad = 0;
   const int n = a.position ? pos + 1 : a.n_fixed;
+  float *scores = kvq_dyn;
+  uint8_t *ureg = reinterpret_cast<uint8_t *>(kvq_dyn) + kvq_score_bytes(n);
+  // this CTA's share: a multiple of 4 positions (16-byte aligned rows)
+  const int share = (n + 4 * kKvqSplit - 1) / (4 * kKvqSplit) * 4;
+  const int lo = min(n, rank * share), hi = min(n, lo + share);
+  const int krb = kvq_record_bytes(4);
+  uint32_t *kst = reinterpret_cast<uint32_t *>(ureg);  // [2][chunk][33]
+  const int nkc = (hi - lo + kKvqKeyChunk - 1) / kKvqKeyChunk;
+  auto kfetch = [&](int c) {  // key records of chunk c into buffer c & 1
+    if (c < nkc) {
+      uint32_t *dst = kst + (size_t)(c & 1) * kKvqKeyChunk * 33;
+      const int p0 = lo + c * kKvqKeyChunk, cnt = min(kKvqKeyChunk, hi - p0);
+      for (int e = i; e < cnt * 33; e += kKvqDim) {
+        const int pp = e / 33, w = e - pp * 33;
+        cp_async4(dst + e, a.keys + ((size_t)(p0 + pp) * a.kv_heads + kvh) * krb + 4 * w);
+      }
+    }
+    cp_async_commit();  // an empty group past the end keeps the count uniform
+  };
+  kfetch(0);
+  kfetch(1);
+  __syncthreads();
   float q;
   if (a.projected)
     q = norm_rope_round(a.projected + (long)h * 2 * kKvqDim, a.q_norm, a.eps, kKvqDim,
@@ -402,130 +457,235 @@ __global__ void __launch_bounds__(kKvqDim) kvq_attend_kernel(KvqAttnArgs a) {
     q = a.query[(long)h * kKvqDim + i];
   bool finite = __syncthreads_and(is_finite_f(q));
   if (!finite) bad |= kStatusInvalid;
-  float rq = kvq_forward(a.kc, finite ? q : 0.0f, sh, finite);
+  const float rq = kvq_forward(a.kc, finite ? q : 0.0f, sh, finite);
   if (!finite) bad |= kStatusNonfinite;
   qd[i] = (double)rq;
-  __syncthreads();
+  trace_stamp(a.trace, 1);
 
-  // scores of this CTA's share of the positions: a position per thread,
-  // four binary64 lanes over the 4-bit codes
-  float *scores = kvq_dyn;
-  const int share = (n + kKvqSplit - 1) / kKvqSplit;
-  const int lo = min(n, rank * share), hi = min(n, lo + share);
-  const int krb = kvq_record_bytes(4);
-  for (int p = lo + i; p < hi; p += kKvqDim) {
-    const uint32_t *rec = reinterpret_cast<const uint32_t *>(
-        a.keys + ((size_t)p * a.kv_heads + kvh) * krb);
-    const uint32_t sbits = __ldg(rec);
-    const float scale = __uint_as_float(sbits);
-    double l0 = 0.0, l1 = 0.0, l2 = 0.0, l3 = 0.0;
-    uint32_t any = 0;
+  // scores of the share, a position per thread: four binary64 lanes, each
+  // adding the exact products q_i * level in channel order
+  for (int c = 0; c < nkc; ++c) {
+    cp_async_wait_pending(1);
+    __syncthreads();  // chunk c's records (and, first, the query) visible
+    const int p0 = lo + c * kKvqKeyChunk, cnt = min(kKvqKeyChunk, hi - p0);
+    if (i < cnt) {
+      const uint32_t *r = kst + (size_t)(c & 1) * kKvqKeyChunk * 33 + i * 33;
+      const uint32_t sbits = r[0];
+      const float scale = __uint_as_float(sbits);
+      double l0 = 0.0, l1 = 0.0, l2 = 0.0, l3 = 0.0;
+      uint32_t any = 0;
 #pragma unroll 4
-    for (int w = 0; w < 32; ++w) {
-      const uint32_t word = __ldg(rec + 1 + w);
-      any |= word;
-      const double *qq = qd + 8 * w;
-      l0 = __fma_rn(qq[0], levk[word & 15u], l0);
-      l1 = __fma_rn(qq[1], levk[(word >> 4) & 15u], l1);
-      l2 = __fma_rn(qq[2], levk[(word >> 8) & 15u], l2);
-      l3 = __fma_rn(qq[3], levk[(word >> 12) & 15u], l3);
-      l0 = __fma_rn(qq[4], levk[(word >> 16) & 15u], l0);
-      l1 = __fma_rn(qq[5], levk[(word >> 20) & 15u], l1);
-      l2 = __fma_rn(qq[6], levk[(word >> 24) & 15u], l2);
-      l3 = __fma_rn(qq[7], levk[word >> 28], l3);
+      for (int w = 0; w < 32; ++w) {
+        const uint32_t word = r[1 + w];
+        any |= word;
+        const double2 *qq = reinterpret_cast<const double2 *>(qd + 8 * w);
+        const double2 q01 = qq[0], q23 = qq[1], q45 = qq[2], q67 = qq[3];
+        l0 = __fma_rn(q01.x, levk[word & 15u], l0);
+        l1 = __fma_rn(q01.y, levk[(word >> 4) & 15u], l1);
+        l2 = __fma_rn(q23.x, levk[(word >> 8) & 15u], l2);
+        l3 = __fma_rn(q23.y, levk[(word >> 12) & 15u], l3);
+        l0 = __fma_rn(q45.x, levk[(word >> 16) & 15u], l0);
+        l1 = __fma_rn(q45.y, levk[(word >> 20) & 15u], l1);
+        l2 = __fma_rn(q67.x, levk[(word >> 24) & 15u], l2);
+        l3 = __fma_rn(q67.y, levk[word >> 28], l3);
+      }
+      float s = 0.0f;
+      if (!kvq_scale_ok(sbits) || (scale == 0.0f && any)) {
+        bad |= kStatusInvalid;
+      } else if (scale != 0.0f) {
+        const float unscaled =
+            __double2float_rn(__dadd_rn(__dadd_rn(__dadd_rn(l0, l1), l2), l3));
+        s = __fmul_rn(unscaled, scale);
+        if (!is_finite_f(unscaled) || !is_finite_f(s)) bad |= kStatusNonfinite;
+      }
+      scores[p0 + i] = __fmul_rn(s, a.attn_scale);
     }
-    float s = 0.0f;
-    if (!kvq_scale_ok(sbits) || (scale == 0.0f && any)) {
-      bad |= kStatusInvalid;
-    } else if (scale != 0.0f) {
-      const float unscaled = __double2float_rn(__dadd_rn(__dadd_rn(__dadd_rn(l0, l1), l2), l3));
-      s = __fmul_rn(unscaled, scale);
-      if (!is_finite_f(unscaled) || !is_finite_f(s)) bad |= kStatusNonfinite;
-    }
-    scores[p] = __fmul_rn(s, a.attn_scale);
+    __syncthreads();  // buffer c & 1 is free again
+    kfetch(c + 2);
   }
-  cluster.sync();
-  // every CTA gathers the other shares
-  for (int r = 0; r < kKvqSplit; ++r) {
-    if (r == rank) continue;
-    const int rlo = min(n, r * share), rhi = min(n, rlo + share);
-    const float *peer = cluster.map_shared_rank(scores, r);
-    for (int p = rlo + i; p < rhi; p += kKvqDim) scores[p] = peer[p];
-  }
-  cluster.sync();  // no CTA rewrites its scores while a peer still reads them
+  cp_async_wait_all();
+  trace_stamp(a.trace, 2);
 
   // softmax_round_f16 (reference src/kernels.rs softmax_round_f16): the
-  // maximum, binary32 exponentials, their binary64 total in position order,
-  // binary16-rounded probabilities
+  // maximum over every share first
   float m = -INFINITY;
-  for (int p = i; p < n; p += kKvqDim) m = fmaxf(m, scores[p]);
+  for (int p = lo + i; p < hi; p += kKvqDim) m = fmaxf(m, scores[p]);
   m = block_max_f32(m, fred);
-  if (!is_finite_f(m)) bad |= kStatusInvalid;
-  for (int p = i; p < n; p += kKvqDim) scores[p] = exp_cr(__fsub_rn(scores[p], m));
-  __syncthreads();
+  if (i == 0) s_max = m;
+  cluster.sync();
+  float M = -INFINITY;
+  for (int r = 0; r < kKvqSplit; ++r) M = fmaxf(M, *cluster.map_shared_rank(&s_max, r));
+  if (!is_finite_f(M)) bad |= kStatusInvalid;
+  // the share's binary32 exponentials, their minimum and binary64 sum
+  float emin = INFINITY;
+  double part = 0.0;
+  for (int p = lo + i; p < hi; p += kKvqDim) {
+    const float e = exp_cr(__fsub_rn(scores[p], M));
+    scores[p] = e;
+    emin = fminf(emin, e);
+    part = __dadd_rn(part, (double)e);
+  }
+  emin = -block_max_f32(-emin, fred);
+  part = block_sum_f64(part, red);
   if (i == 0) {
-    double total = 0.0;
-    int p = 0;
-    for (; p + 4 <= n; p += 4) {
-      const float4 e = *reinterpret_cast<const float4 *>(scores + p);
-      total = __dadd_rn(total, (double)e.x);
-      total = __dadd_rn(total, (double)e.y);
-      total = __dadd_rn(total, (double)e.z);
-      total = __dadd_rn(total, (double)e.w);
+    s_emin = emin;
+    s_sum = part;
+  }
+  cluster.sync();
+  // every share's exponentials into this CTA's row
+  for (int r = 0; r < kKvqSplit; ++r) {
+    if (r == rank) continue;
+    const int rlo = min(n, r * share), rhi = min(n, rlo + share), n4 = (rhi - rlo) / 4;
+    const float *peer = cluster.map_shared_rank(scores, r);
+    for (int k = i; k < n4; k += kKvqDim)
+      reinterpret_cast<float4 *>(scores + rlo)[k] = reinterpret_cast<const float4 *>(peer + rlo)[k];
+    for (int p = rlo + 4 * n4 + i; p < rhi; p += kKvqDim) scores[p] = peer[p];
+  }
+  float gmin = INFINITY;
+  double tree = 0.0;
+  for (int r = 0; r < kKvqSplit; ++r) {
+    gmin = fminf(gmin, *cluster.map_shared_rank(&s_emin, r));
+    tree = __dadd_rn(tree, *cluster.map_shared_rank(&s_sum, r));
+  }
+  cluster.sync();  // every peer has its copy before anything is rewritten
+  trace_stamp(a.trace, 3);
+  // The total in position order.  When every exponential is at least
+  // 2^(ceil(log2 n) - 30), all are multiples of the smallest one's ulp u and
+  // the total stays below 2^53 u: every partial sum, in any order, is exact,
+  // so the shares' tree is the sequential result.  Otherwise one thread adds
+  // them in order.
+  int lg = 0;
+  while ((1 << lg) < n) ++lg;
+  if (i == 0) {
+    double total = tree;
+    if (!(gmin >= ldexpf(1.0f, lg - 30))) {
+      total = 0.0;
+      int p = 0;
+      for (; p + 4 <= n; p += 4) {
+        const float4 e = *reinterpret_cast<const float4 *>(scores + p);
+        total = __dadd_rn(total, (double)e.x);
+        total = __dadd_rn(total, (double)e.y);
+        total = __dadd_rn(total, (double)e.z);
+        total = __dadd_rn(total, (double)e.w);
+      }
+      for (; p < n; ++p) total = __dadd_rn(total, (double)scores[p]);
     }
-    for (; p < n; ++p) total = __dadd_rn(total, (double)scores[p]);
     s_inv = __double2float_rn(__ddiv_rn(1.0, total));
   }
   __syncthreads();
   const float inv = s_inv;
-  for (int p = i; p < n; p += kKvqDim) scores[p] = round_f16(__fmul_rn(scores[p], inv));
+  trace_stamp(a.trace, 4);
 
-  // value scan over this CTA's 32 channels [32 rank, 32 rank + 32): warp 0
-  // runs the chains, the other warps stage the next chunk's scales and code
-  // slices (bits words per position)
-  const int vb = a.vc.bits, vrb = kvq_record_bytes(vb);
-  const int stride = 1 + vb;  // words per staged position
-  uint32_t *stage = reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(kvq_dyn) +
-                                                 ((size_t)n * 4 + 15) / 16 * 16);
+  // value scan over this CTA's 32 channels [32 rank, 32 rank + 32).  Each
+  // channel's binary32 chain runs in warp 0 in position order, one add per
+  // position.  Warps 1-7 feed it: they copy the records' scales and code
+  // slices into a ring by asynchronous copies, six chunks ahead, and form
+  // the next chunk's increments round_f16(e * inv) * scale * level, a
+  // position per thread, as rows of 36 words (the chain's lanes read one
+  // row without bank conflicts, the formers' 16-byte stores spread over the
+  // banks).  A chunk's tail up to a multiple of 8 positions holds +0, which
+  // leaves a chain unchanged (its sum is never -0: it starts at +0 and
+  // x + (-x) is +0).
+  constexpr int kWords = 1 + VB;  // copies per position: the scale, the slice
+  const int vrb = kvq_record_bytes(VB);
+  uint8_t *raw = ureg;                                             // [ring] chunks
+  float *inc = reinterpret_cast<float *>(ureg + kKvqRawBytes);     // [2][chunk][36]
+  constexpr int kLead = kKvqRing - 2;
   const int nchunks = (n + kKvqChunk - 1) / kKvqChunk;
-  auto stage_chunk = [&](int ck, int t0, int nt) {
-    uint32_t *dst = stage + (size_t)(ck & 1) * kKvqChunk * 5;
+  const int pt = i - 32, np = kKvqDim - 32;  // producer index and count
+  auto fetch = [&](int ck) {  // chunk ck into ring slot ck % kKvqRing
+    if (ck < nchunks) {
+      uint32_t *sc = reinterpret_cast<uint32_t *>(raw + (size_t)(ck % kKvqRing) * kKvqRawChunk);
+      uint32_t *sl = sc + kKvqChunk;  // [chunk][4] slice words
+      const int p0 = ck * kKvqChunk, cnt = min(kKvqChunk, n - p0);
+      for (int e = pt; e < cnt * kWords; e += np) {
+        const int pp = e / kWords, w = e - pp * kWords;
+        const uint32_t *rec = reinterpret_cast<const uint32_t *>(
+            a.values + ((size_t)(p0 + pp) * a.kv_heads + kvh) * vrb);
+        if (w == 0)
+          cp_async4(sc + pp, rec);
+        else
+          cp_async4(sl + 4 * pp + (w - 1), rec + 1 + rank * VB + (w - 1));
+      }
+    }
+    cp_async_commit();
+  };
+  auto form = [&](int ck) {  // increments of chunk ck into slot ck & 1
+    const uint32_t *sc =
+        reinterpret_cast<const uint32_t *>(raw + (size_t)(ck % kKvqRing) * kKvqRawChunk);
+    const uint4 *sl = reinterpret_cast<const uint4 *>(sc + kKvqChunk);
+    float *dst = inc + (size_t)(ck & 1) * kKvqChunk * kKvqIncRow;
     const int p0 = ck * kKvqChunk, cnt = min(kKvqChunk, n - p0);
-    for (int e = t0; e < cnt * stride; e += nt) {
-      const int pp = e / stride, w = e % stride;
-      const uint32_t *rec = reinterpret_cast<const uint32_t *>(
-          a.values + ((size_t)(p0 + pp) * a.kv_heads + kvh) * vrb);
-      dst[e] = __ldg(rec + (w == 0 ? 0 : 1 + rank * vb + (w - 1)));
+    const int cnt8 = (cnt + 7) & ~7;
+    for (int pp = pt; pp < cnt8; pp += np) {
+      float4 *row = reinterpret_cast<float4 *>(dst + pp * kKvqIncRow);
+      if (pp >= cnt) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) row[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        continue;
+      }
+      const uint32_t sbits = sc[pp];
+      const float scale = __uint_as_float(sbits);
+      const uint4 wv = sl[pp];
+      const uint64_t lo64 = (uint64_t)wv.x | ((uint64_t)wv.y << 32);
+      const uint64_t hi64 = (uint64_t)wv.z | ((uint64_t)wv.w << 32);
+      const float ws = __fmul_rn(round_f16(__fmul_rn(scores[p0 + pp], inv)), scale);
+      const bool nonzero = (wv.x | wv.y | wv.z | (VB == 4 ? wv.w : 0u)) != 0u;
+      if (!kvq_scale_ok(sbits) || (scale == 0.0f && nonzero)) bad |= kStatusInvalid;
+      if (!is_finite_f(ws)) bad |= kStatusNonfinite;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int bit = VB * (4 * j + k);  // code 4j + k of the slice
+          const uint32_t code =
+              bit < 64 ? (uint32_t)(bit + VB <= 64 ? (lo64 >> bit)
+                                                   : ((lo64 >> bit) | (hi64 << (64 - bit))))
+                       : (uint32_t)(hi64 >> (bit - 64));
+          v[k] = __fmul_rn(ws, levv[code & ((1u << VB) - 1u)]);
+        }
+        row[j] = make_float4(v[0], v[1], v[2], v[3]);
+      }
     }
   };
-  stage_chunk(0, i, kKvqDim);
+  if (warp != 0) {
+    for (int ck = 0; ck <= kLead; ++ck) fetch(ck);
+    cp_async_wait_pending(kLead);  // chunk 0 landed
+  }
   __syncthreads();
-  // the lane's code: bits [vb * lane, vb * lane + vb) of the slice
-  const int cbit = vb * lane, cw = cbit >> 5, cs_ = cbit & 31;
+  if (warp != 0) form(0);
+  __syncthreads();
   float acc = 0.0f;
   for (int ck = 0; ck < nchunks; ++ck) {
-    if (warp != 0) {
-      if (ck + 1 < nchunks) stage_chunk(ck + 1, i - 32, kKvqDim - 32);
-    } else {
-      const uint32_t *src = stage + (size_t)(ck & 1) * kKvqChunk * 5;
-      const int p0 = ck * kKvqChunk, cnt = min(kKvqChunk, n - p0);
-#pragma unroll 4
-      for (int pp = 0; pp < cnt; ++pp) {
-        const uint32_t *e = src + pp * stride;
-        const uint32_t sbits = e[0];
-        const float scale = __uint_as_float(sbits);
-        uint32_t code = e[1 + cw] >> cs_;
-        if (cs_ + vb > 32) code |= e[2 + cw] << (32 - cs_);
-        code &= (1u << vb) - 1u;
-        const uint32_t any = __ballot_sync(0xffffffffu, code != 0);
-        const float ws = __fmul_rn(scores[p0 + pp], scale);
-        if (!kvq_scale_ok(sbits) || (scale == 0.0f && any)) bad |= kStatusInvalid;
-        if (!is_finite_f(ws)) bad |= kStatusNonfinite;
-        acc = __fadd_rn(acc, __fmul_rn(ws, levv[code]));
+    if (warp == 0) {
+      const float *src = inc + (size_t)(ck & 1) * kKvqChunk * kKvqIncRow + lane;
+      const int cnt8 = (min(kKvqChunk, n - ck * kKvqChunk) + 7) & ~7;
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = src[k * kKvqIncRow];
+      for (int pp = 0; pp < cnt8; pp += 8) {
+        const int nx = pp + 8 < cnt8 ? pp + 8 : pp;
+        float w[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) w[k] = src[(nx + k) * kKvqIncRow];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc = __fadd_rn(acc, v[k]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = w[k];
       }
+    } else if (ck + 1 < nchunks) {
+      // chunk ck + 1 is the oldest pending group; the producers' barrier
+      // publishes every thread's copies of it
+      cp_async_wait_pending(kLead - 1);
+      asm volatile("bar.sync 1, %0;" ::"r"(kKvqDim - 32) : "memory");
+      form(ck + 1);
+      fetch(ck + 1 + kLead);  // slot of chunk ck - 1, formed two iterations ago
     }
     __syncthreads();
   }
+  if (warp != 0) cp_async_wait_all();
+  trace_stamp(a.trace, 5);
   if (warp == 0) vout[lane] = acc;
   cluster.sync();
   float v = cluster.map_shared_rank(vout, i >> 5)[i & 31];
@@ -539,13 +699,15 @@ __global__ void __launch_bounds__(kKvqDim) kvq_attend_kernel(KvqAttnArgs a) {
   }
   if (bad) report(a.status, bad);
   cluster.sync();  // peers' shared memory stays live until every read is done
+  trace_exit(a.trace);
 }
 
 // One 8-CTA cluster per query head; `cap` bounds the positions served.
 inline cudaError_t launch_kvq_attend(const KvqAttnArgs &a, int cap, cudaStream_t s, bool pdl) {
   const size_t smem = kvq_attend_smem(cap);
-  cudaError_t e = cudaFuncSetAttribute(kvq_attend_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  auto kern = a.vc.bits == 3 ? kvq_attend_kernel<3> : kvq_attend_kernel<4>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchAttribute cattr[2];
   cudaLaunchConfig_t cfg =
@@ -555,7 +717,7 @@ inline cudaError_t launch_kvq_attend(const KvqAttnArgs &a, int cap, cudaStream_t
   cattr[cfg.numAttrs].val.clusterDim.y = 1;
   cattr[cfg.numAttrs].val.clusterDim.z = 1;
   cfg.numAttrs += 1;
-  return cudaLaunchKernelEx(&cfg, kvq_attend_kernel, a);
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 }  // namespace prism

@@ -71,6 +71,10 @@ def _declare(L):
         "po_add_rms_norm": (i32, [vp, vp, vp, sz, f32, vp]),
         "po_l2_norm": (None, [vp, sz, f32]),
         "po_softmax_round_f16": (i32, [vp, sz]),
+        "po_ext_block_bytes": (i32, [u32]),
+        "po_ext_decode": (i32, [u32, vp, sz, vp]),
+        "po_ext_block_ints": (i32, [u32, vp, vp, sz, vp, vp]),
+        "po_ext_dot": (i32, [u32, vp, vp, sz, vp]),
         "po_kvq_splitmix": (ctypes.c_uint64, [vp]),
         "po_kvq_levels": (None, [i32, vp]),
         "po_kvq_record_bytes": (i32, [i32]),
@@ -112,8 +116,13 @@ def q8_0_quantize(x):
     return out
 
 
+# Q8_K-contract kinds (reference src/kernels.rs:1653-1674): TQ2_0, Q2_K, and
+# TQ1_0, Q3_K, Q4_K, Q5_K, Q6_K (kquant_oracle.c)
+BLOCK_BYTES = {35: 66, 10: 84, 34: 54, 11: 110, 12: 144, 13: 176, 14: 210}
+
+
 def block_bytes(kind):
-    return {35: 66, 10: 84}[kind]
+    return BLOCK_BYTES[kind]
 
 
 # ---- PQ2 (142) and PTQ1 (143): 128 weights per block --------------------
@@ -171,8 +180,11 @@ def decode(kind, packed):
     packed = np.ascontiguousarray(packed, dtype=np.uint8)
     nb = packed.size // block_bytes(kind)
     out = np.zeros(nb * 256, dtype=np.float32)
-    fn = lib().po_tq2_decode if kind == 35 else lib().po_q2k_decode
-    _check(fn(_p(packed), nb, _p(out)))
+    if kind in (35, 10):
+        fn = lib().po_tq2_decode if kind == 35 else lib().po_q2k_decode
+        _check(fn(_p(packed), nb, _p(out)))
+    else:
+        _check(lib().po_ext_decode(kind, _p(packed), nb, _p(out)))
     return out
 
 
@@ -187,8 +199,11 @@ def dot(kind, packed_row, act):
     packed_row = np.ascontiguousarray(packed_row, dtype=np.uint8)
     act = np.ascontiguousarray(act, dtype=Q8K_DTYPE)
     out = np.zeros(1, dtype=np.float32)
-    fn = lib().po_tq2_dot if kind == 35 else lib().po_q2k_dot
-    _check(fn(_p(packed_row), _p(act), act.size, _p(out)))
+    if kind in (35, 10):
+        fn = lib().po_tq2_dot if kind == 35 else lib().po_q2k_dot
+        _check(fn(_p(packed_row), _p(act), act.size, _p(out)))
+    else:
+        _check(lib().po_ext_dot(kind, _p(packed_row), _p(act), act.size, _p(out)))
     return out[0]
 
 
@@ -205,6 +220,18 @@ def block_dots(kind, packed_row, act):
     msum = np.zeros(act.size, dtype=np.int32)
     _check(lib().po_q2k_block_dots(_p(packed_row), _p(act), act.size, _p(isum), _p(msum)))
     return isum, msum
+
+
+def ext_block_ints(kind, packed_row, act):
+    """Exact integer parts per block (kinds 34, 11-14): 8 lane sums
+    (TQ1_0: the block sum in lane 0) and the minimum sum (Q4_K, Q5_K)."""
+    packed_row = np.ascontiguousarray(packed_row, dtype=np.uint8)
+    act = np.ascontiguousarray(act, dtype=Q8K_DTYPE)
+    lanes = np.zeros((act.size, 8), dtype=np.int32)
+    msum = np.zeros(act.size, dtype=np.int32)
+    _check(lib().po_ext_block_ints(kind, _p(packed_row), _p(act), act.size, _p(lanes),
+                                   _p(msum)))
+    return lanes, msum
 
 
 def matvec(kind, weights, rows, cols, act, threads=1):

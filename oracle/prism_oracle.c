@@ -378,7 +378,14 @@ int po_q2k_dot(const uint8_t *w, const po_q8k_block *a, size_t nblocks,
 int po_block_bytes(uint32_t kind) {
   if (kind == 35) return 66;
   if (kind == 10) return 84;
-  return 0;
+  return po_ext_block_bytes(kind);  /* 34, 11-14 */
+}
+
+static int po_row_dot(uint32_t kind, const uint8_t *row, const po_q8k_block *a, size_t nb,
+                      float *y) {
+  if (kind == 35) return po_tq2_dot(row, a, nb, y);
+  if (kind == 10) return po_q2k_dot(row, a, nb, y);
+  return po_ext_dot(kind, row, a, nb, y);
 }
 
 typedef struct {
@@ -397,8 +404,7 @@ static void *po_chunk_run(void *arg) {
   c->first_error = PO_OK;
   for (size_t r = c->row_begin; r < c->row_end; ++r) {
     const uint8_t *row = c->w + r * rb;
-    int st = c->kind == 35 ? po_tq2_dot(row, c->a, c->nb, c->y + r)
-                           : po_q2k_dot(row, c->a, c->nb, c->y + r);
+    int st = po_row_dot(c->kind, row, c->a, c->nb, c->y + r);
     if (st != PO_OK) {
       c->first_error = st;
       c->first_error_row = r;
@@ -477,7 +483,7 @@ static void *po_tile_chunk_run(void *arg) {
       for (size_t t = t0; t < t1; ++t) {
         const po_q8k_block *a = c->a + t * c->nb;
         float *out = c->y + t * c->rows + r;
-        int st = c->kind == 35 ? po_tq2_dot(row, a, c->nb, out) : po_q2k_dot(row, a, c->nb, out);
+        int st = po_row_dot(c->kind, row, a, c->nb, out);
         if (st != PO_OK) {
           c->first_error = st;
           return NULL;

@@ -140,6 +140,14 @@ int po_add_rms_norm(float *values, const float *delta, const float *w,
 void po_l2_norm(float *x, size_t n, float eps);
 int po_softmax_round_f16(float *v, size_t n);
 
+/* ---- TQ1_0 (34) and Q3_K..Q6_K (11-14) (kquant_oracle.c) ------------ */
+int po_ext_block_bytes(uint32_t kind);
+int po_ext_decode(uint32_t kind, const uint8_t *blocks, size_t nblocks, float *out);
+int po_ext_block_ints(uint32_t kind, const uint8_t *w, const po_q8k_block *a, size_t nblocks,
+                      int32_t *lanes, int32_t *msum);
+int po_ext_dot(uint32_t kind, const uint8_t *w, const po_q8k_block *a, size_t nblocks,
+               float *out);
+
 /* ---- rotated scalar KV codec, rsq (kvq_oracle.c) -------------------- */
 uint64_t po_kvq_splitmix(uint64_t *state);
 void po_kvq_levels(int levels, float *out);

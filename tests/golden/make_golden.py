@@ -62,6 +62,9 @@ def main(ref_root):
     fixtures = os.path.join(ref_root, "tests", "fixtures")
     tq = _cases(os.path.join(fixtures, "upstream-tquants.json"), 35)
     kq = _cases(os.path.join(fixtures, "upstream-kquants.json"), 10)
+    more = {"tq1_0.json": _cases(os.path.join(fixtures, "upstream-tquants.json"), 34)}
+    for type_id, name in ((11, "q3_k"), (12, "q4_k"), (13, "q5_k"), (14, "q6_k")):
+        more[name + ".json"] = _cases(os.path.join(fixtures, "upstream-kquants.json"), type_id)
     with open(os.path.join(fixtures, "swift-q8k-parity.json")) as f:
         q8k_meta = json.load(f)
     with open(os.path.join(fixtures, "swift-q8k-parity.bin"), "rb") as f:
@@ -88,7 +91,7 @@ def main(ref_root):
     kvq = kvq_fixture(ref_root)
     for name, obj in (("tq2_0.json", tq), ("q2_k.json", kq), ("q8k_parity.json", q8k),
                       ("pinned.json", pinned), ("ptq_reference.json", ptq),
-                      ("kvq_reference.json", kvq)):
+                      ("kvq_reference.json", kvq)) + tuple(more.items()):
         with open(os.path.join(HERE, name), "w") as f:
             json.dump(obj, f, indent=1)
             f.write("\n")

@@ -23,7 +23,10 @@ def _bytes(h):
     return np.frombuffer(bytes.fromhex(h), dtype=np.uint8)
 
 
-@pytest.mark.parametrize("name,kind", [("tq2_0.json", 35), ("q2_k.json", 10)])
+@pytest.mark.parametrize("name,kind", [("tq2_0.json", 35), ("q2_k.json", 10),
+                                       ("tq1_0.json", 34), ("q3_k.json", 11),
+                                       ("q4_k.json", 12), ("q5_k.json", 13),
+                                       ("q6_k.json", 14)])
 def test_decode_and_generic_dot_match_golden(oracle, name, kind):
     fx = _load(name)
     assert len(fx["cases"]) == 5

@@ -51,6 +51,16 @@ extern "C" {
 #define PRISM_B200_KIND_Q2_K 10
 #define PRISM_B200_KIND_Q8_K 15
 #define PRISM_B200_KIND_TQ2_0 35
+/* The rest of the reference's Q8_K activation contract (reference
+ * src/kernels.rs:1653-1674): TQ1_0 54 B and Q3_K 110, Q4_K 144, Q5_K 176,
+ * Q6_K 210 B per 256 weights, in the upstream ggml byte layouts
+ * (src/kernels/tquants.rs, src/kernels/kquants.rs).  Kept as uploaded and
+ * projected by prism_b200_project, _project_device and _project_f32. */
+#define PRISM_B200_KIND_TQ1_0 34
+#define PRISM_B200_KIND_Q3_K 11
+#define PRISM_B200_KIND_Q4_K 12
+#define PRISM_B200_KIND_Q5_K 13
+#define PRISM_B200_KIND_Q6_K 14
 /* The reference's own packed ternary formats (reference src/kernels.rs:
  * 85-86, 178-183): 128 weights per block, PQ2 in 34 bytes (binary16 scale,
  * then 2-bit codes), PTQ1 in 28 bytes (base-3 digits, then the scale). */
@@ -117,15 +127,16 @@ int prism_b200_executor_reset(prism_b200_executor *ex);
 
 /* Eligibility from geometry alone, before any submission
  * (reference src/kernels/projection.rs:41-46 `supports`).  Returns 1 when
- * the tensor's kind is TQ2_0 or Q2_K and cols is a positive multiple of 256,
- * or PQ2 or PTQ1 and cols is a positive multiple of 128. */
+ * the tensor's kind is TQ2_0, Q2_K, TQ1_0 or Q3_K..Q6_K and cols is a
+ * positive multiple of 256, or PQ2 or PTQ1 and cols is a positive multiple
+ * of 128. */
 int prism_b200_executor_supports(const prism_b200_executor *ex,
                                  const prism_b200_tensor *tensor);
 
 /* Submission count of one projection (reference
  * src/kernels/projection.rs:28-35 `operation_count`): the number of
- * 32-row x 256-column work units (PQ2 / PTQ1: rows x 128-column blocks),
- * or -1 when unsupported. */
+ * 32-row x 256-column work units (PQ2 / PTQ1: rows x 128-column blocks;
+ * TQ1_0, Q3_K..Q6_K: rows x 256-column blocks), or -1 when unsupported. */
 int64_t prism_b200_executor_operation_count(const prism_b200_executor *ex,
                                             const prism_b200_tensor *tensor);
 
@@ -133,11 +144,12 @@ int64_t prism_b200_executor_operation_count(const prism_b200_executor *ex,
 
 /* Validate (finite fp16 scales, exact extents) and upload a weight once;
  * it stays resident in HBM until released: TQ2_0 and Q2_K in the executor's
- * tiled layout, PQ2 and PTQ1 as uploaded.  Mirrors the resident tiles of
- * the reference's DSP executor (reference docs/inference-efficiency.md:
- * 266-277).  PQ2 and PTQ1 weights serve prism_b200_project,
- * _project_device, _project_q8 and _project_f32; the other projections
- * refuse them with PRISM_B200_E_UNSUPPORTED. */
+ * tiled layout, PQ2, PTQ1, TQ1_0 and Q3_K..Q6_K as uploaded.  Mirrors the
+ * resident tiles of the reference's DSP executor (reference
+ * docs/inference-efficiency.md:266-277).  PQ2 and PTQ1 weights serve
+ * prism_b200_project, _project_device, _project_q8 and _project_f32; TQ1_0
+ * and Q3_K..Q6_K the same but _project_q8 (they take Q8_K); the other
+ * projections refuse them with PRISM_B200_E_UNSUPPORTED. */
 int prism_b200_weight_upload(prism_b200_executor *ex,
                              const prism_b200_tensor *tensor,
                              prism_b200_weight **out);

@@ -17,6 +17,7 @@
 #include "gdn.cuh"
 #include "gemm.cuh"
 #include "packed.cuh"
+#include "kquant.cuh"
 
 using namespace prism;
 
@@ -54,10 +55,28 @@ bool geometry_ok(const prism_b200_tensor *t) {
 
 // PQ2 / PTQ1 tensors: whole 128-weight blocks (reference src/kernels.rs:
 // 88-119 layout, 121-143 dimensions).
-bool packed_geometry_ok(const prism_b200_tensor *t) {
+bool pq_geometry_ok(const prism_b200_tensor *t) {
   return t && pq_block_bytes(t->kind) != 0 && t->cols > 0 && t->cols % 128 == 0 &&
          t->cols <= kMaxCols && t->rows > 0 && t->rows <= (1ull << 30);
 }
+
+// TQ1_0 and Q3_K..Q6_K tensors: whole 256-weight blocks.
+bool kquant_geometry_ok(const prism_b200_tensor *t) {
+  return t && kquant_block_bytes(t->kind) != 0 && t->cols > 0 && t->cols % 256 == 0 &&
+         t->cols <= kMaxCols && t->rows > 0 && t->rows <= (1ull << 30);
+}
+
+// Weights kept as uploaded (the reference's block bytes) rather than
+// repacked into row tiles: PQ2, PTQ1, TQ1_0, Q3_K..Q6_K.
+bool packed_geometry_ok(const prism_b200_tensor *t) {
+  return pq_geometry_ok(t) || kquant_geometry_ok(t);
+}
+
+// Bytes and weights of one stored block of a packed kind.
+int stored_block_bytes(uint32_t kind) {
+  return pq_block_bytes(kind) ? pq_block_bytes(kind) : kquant_block_bytes(kind);
+}
+int stored_block_weights(uint32_t kind) { return pq_block_bytes(kind) ? 128 : 256; }
 
 cudaStream_t pick(prism_b200_executor *ex, void *stream) {
   return stream ? reinterpret_cast<cudaStream_t>(stream) : ex->stream;
@@ -117,17 +136,36 @@ cudaError_t project_on(prism_b200_executor *ex, const prism_b200_weight *w, cons
 // Whether a packed weight takes Q8_K activations (reference src/kernels.rs:
 // 1663-1674): PQ2 with a multiple of 256 columns; PTQ1 and other PQ2 rows
 // take Q8_0.
-bool packed_q8k(const DeviceWeight &dw) { return dw.kind == 142 && dw.cols % 256 == 0; }
+bool packed_q8k(const DeviceWeight &dw) {
+  return (dw.kind == 142 && dw.cols % 256 == 0) || kquant_block_bytes(dw.kind) != 0;
+}
+
+// Offsets of the fp16 scales of a stored block (every one must be finite).
+int block_scale_offsets(uint32_t kind, int *off) {
+  switch (kind) {
+    case 142: off[0] = 0; return 1;
+    case 143: off[0] = 26; return 1;
+    case 34: off[0] = 52; return 1;
+    case 11: off[0] = 108; return 1;
+    case 12: case 13: off[0] = 0; off[1] = 2; return 2;
+    case 14: off[0] = 208; return 1;
+    default: return 0;
+  }
+}
 
 int upload_packed(prism_b200_executor *ex, const prism_b200_tensor *t, prism_b200_weight **out) {
-  const int bb = pq_block_bytes(t->kind);
-  const size_t nb = t->cols / 128, nblocks = (size_t)t->rows * nb;
+  const int bb = stored_block_bytes(t->kind);
+  const size_t nb = t->cols / stored_block_weights(t->kind), nblocks = (size_t)t->rows * nb;
   const uint8_t *src = static_cast<const uint8_t *>(t->data);
-  for (size_t i = 0; i < nblocks; ++i) {
-    // every block scale finite (reference scale(), src/kernels.rs:152-154)
-    const uint8_t hi = src[i * bb + (t->kind == 142 ? 1 : 27)];
-    if ((hi & 0x7c) == 0x7c) return ex->fail(PRISM_B200_E_NONFINITE, "nonfinite fp16 block scale");
-  }
+  int offs[2];
+  const int nscales = block_scale_offsets(t->kind, offs);
+  for (size_t i = 0; i < nblocks; ++i)
+    for (int k = 0; k < nscales; ++k) {
+      // every block scale finite (reference scale(), src/kernels.rs:152-154)
+      const uint8_t hi = src[i * bb + offs[k] + 1];
+      if ((hi & 0x7c) == 0x7c)
+        return ex->fail(PRISM_B200_E_NONFINITE, "nonfinite fp16 block scale");
+    }
   CK(cudaSetDevice(ex->device), "select device");
   auto *w = new prism_b200_weight();
   w->ex = ex;
@@ -154,6 +192,20 @@ int upload_packed(prism_b200_executor *ex, const prism_b200_tensor *t, prism_b20
 
 cudaError_t launch_packed(prism_b200_executor *ex, const DeviceWeight &dw, const void *act,
                           bool q8k, int fused, float *y, cudaStream_t s) {
+  if (kquant_block_bytes(dw.kind)) {
+    KquantArgs k;
+    k.w = dw.units;
+    k.kind = dw.kind;
+    k.rows = (long)dw.rows;
+    k.nb = dw.nb;
+    k.act = static_cast<const uint8_t *>(act);
+    k.y = y;
+    k.status = ex->d_status;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_config(dim3((unsigned)((dw.rows + kKqWarps - 1) / kKqWarps)),
+                                        dim3(kKqWarps * 32), 0, s, attr, ex->pdl);
+    return cudaLaunchKernelEx(&cfg, kquant_matvec_kernel, k);
+  }
   PackedArgs a;
   a.w = dw.units;
   a.kind = dw.kind;
@@ -281,7 +333,8 @@ int prism_b200_executor_supports(const prism_b200_executor *ex,
 int64_t prism_b200_executor_operation_count(const prism_b200_executor *ex,
                                             const prism_b200_tensor *tensor) {
   if (!prism_b200_executor_supports(ex, tensor)) return -1;
-  if (packed_geometry_ok(tensor)) return (int64_t)tensor->rows * (int64_t)(tensor->cols / 128);
+  if (packed_geometry_ok(tensor))
+    return (int64_t)tensor->rows * (int64_t)(tensor->cols / stored_block_weights(tensor->kind));
   const int h = choose_tile_height(tensor->kind, tensor->rows, tensor->cols, ex->num_sms);
   int64_t tiles = (int64_t)((tensor->rows + h - 1) / h);
   return tiles * (int64_t)(tensor->cols / 256);

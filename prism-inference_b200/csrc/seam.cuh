@@ -128,8 +128,9 @@ int prism_b200_executor_supports_f32_group(const prism_b200_executor *ex, size_t
 int prism_b200_executor_supports_q8(const prism_b200_executor *ex,
                                     const prism_b200_tensor *tensor) {
   // Q8_0 activations serve PTQ1 and PQ2 rows (the reference routes PQ2 here
-  // when its columns are not a multiple of 256); TQ2_0 and Q2_K take Q8_K
-  return ex && packed_geometry_ok(tensor) ? 1 : 0;
+  // when its columns are not a multiple of 256); TQ2_0, TQ1_0 and the K
+  // quants take Q8_K
+  return ex && pq_geometry_ok(tensor) ? 1 : 0;
 }
 
 int prism_b200_project_q8(prism_b200_executor *ex, const prism_b200_weight *w,
@@ -139,7 +140,7 @@ int prism_b200_project_q8(prism_b200_executor *ex, const prism_b200_weight *w,
   if ((st = validate_any_weight(ex, w))) return st;
   const DeviceWeight &dw = w->dw;
   const size_t ybytes = dw.rows * sizeof(float);
-  if (!dw.packed) {
+  if (!dw.packed || kquant_block_bytes(dw.kind)) {
     if (out) memset(out, 0, ybytes);
     return ex->fail(PRISM_B200_E_UNSUPPORTED,
                     "kind %u takes Q8_K activations (prism_b200_project), not Q8_0", dw.kind);

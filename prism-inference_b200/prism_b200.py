@@ -23,6 +23,9 @@ E_INVALID, E_UNSUPPORTED, E_NONFINITE, E_DEVICE, E_TIMEOUT, E_FAULTED = 1, 2, 3,
 KIND_Q2_K, KIND_Q8_K, KIND_TQ2_0 = 10, 15, 35
 KIND_PQ2, KIND_PTQ1 = 142, 143   # the reference's own packed ternary formats
 BLOCK_BYTES = {KIND_TQ2_0: 66, KIND_Q2_K: 84}
+# the rest of the reference's Q8_K contract, served as uploaded (kquant.cuh)
+KIND_TQ1_0, KIND_Q3_K, KIND_Q4_K, KIND_Q5_K, KIND_Q6_K = 34, 11, 12, 13, 14
+KQUANT_BLOCK_BYTES = {34: 54, 11: 110, 12: 144, 13: 176, 14: 210}   # per 256 weights
 PACKED_BLOCK_BYTES = {KIND_PQ2: 34, KIND_PTQ1: 28}   # per 128 weights
 
 Q8K_DTYPE = np.dtype([("scale", "<f4"), ("values", "i1", (256,)), ("sums", "<i2", (16,))])

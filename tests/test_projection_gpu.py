@@ -115,11 +115,15 @@ def test_eligibility_and_operation_count(ex):
     # the reference's own PQ2 / PTQ1 formats: whole 128-weight blocks
     assert ex.supports(pb.Tensor(142, 256, 10, z)) and ex.supports(pb.Tensor(143, 384, 10, z))
     assert not ex.supports(pb.Tensor(142, 200, 10, z))
-    assert not ex.supports(pb.Tensor(34, 256, 10, z))  # TQ1_0 is not built
+    # TQ1_0 and Q3_K..Q6_K: whole 256-weight blocks, one unit per row and block
+    for kind in (34, 11, 12, 13, 14):
+        assert ex.supports(pb.Tensor(kind, 512, 10, z))
+        assert not ex.supports(pb.Tensor(kind, 384, 10, z))
+        assert ex.operation_count(pb.Tensor(kind, 512, 10, z)) == 20
     # units of (tile of H rows) x (256-column block); H is 8, 16 or 32
     n = ex.operation_count(pb.Tensor(35, 4096, 4096, z))
     assert n in (512 * 16, 256 * 16, 128 * 16)
-    assert ex.operation_count(pb.Tensor(12, 256, 1, z)) is None
+    assert ex.operation_count(pb.Tensor(15, 256, 1, z)) is None  # Q8_K is an activation
 
 
 def test_errors_are_terminal_and_clear_output(oracle):

@@ -332,6 +332,17 @@ int prism_b200_quantize_q8k_device(prism_b200_executor *ex, const float *x_dev,
                                    size_t n, int pinned, void *out_dev,
                                    void *stream);
 
+/* f32 weights -> TQ1_0 (kind 34) or TQ2_0 (kind 35) blocks (reference
+ * src/kernels/tquants.rs:288-336 `quantize`): per 256 values d = max |x|
+ * stored as binary16, level = round-half-away(x * (1/d)) + 1.  `n` is a
+ * positive multiple of 256; `out` receives n/256 blocks of 54 or 66 bytes.
+ * A nonfinite input returns E_INVALID, a block maximum beyond binary16
+ * E_NONFINITE (the device-side status rules above). */
+int prism_b200_quantize_tq(prism_b200_executor *ex, uint32_t kind, const float *x, size_t n,
+                           void *out);
+int prism_b200_quantize_tq_device(prism_b200_executor *ex, uint32_t kind, const float *x_dev,
+                                  size_t n, void *out_dev, void *stream);
+
 /* The exact per-block integer dots of a projection, the parity observable
  * of the int32 contract (reference src/kernels/tquants.rs:220-245
  * `dot_tq2_block`; src/kernels/kquants.rs:162-200 `dot_q2_k_block`).

@@ -236,3 +236,52 @@ int po_ext_dot(uint32_t kind, const uint8_t *w, const po_q8k_block *a, size_t nb
   *out = sum;
   return PO_OK;
 }
+
+/* reference src/kernels/tquants.rs:288-336 quantize, kinds 34 and 35:
+ * d = max |x| stored as binary16, level = round(x * (1 / d)) + 1 (0 when d
+ * is 0), then TQ2_0's 2-bit fields or TQ1_0's base-3 bytes
+ * ceil(code * 256 / 243) (four-digit bytes scaled by 3 first). */
+int po_tq_quantize(uint32_t kind, const float *x, size_t n, uint8_t *out) {
+  const int size = kind == 35 ? 66 : kind == 34 ? 54 : 0;
+  if (!size || n == 0 || n % 256) return PO_E_INVALID;
+  for (size_t i = 0; i < n; ++i)
+    if (!isfinite(x[i])) return PO_E_INVALID;
+  memset(out, 0, n / 256 * (size_t)size);
+  for (size_t b = 0; b < n / 256; ++b) {
+    const float *c = x + b * 256;
+    uint8_t *o = out + b * (size_t)size;
+    float d = 0.0f;
+    for (int i = 0; i < 256; ++i) d = fmaxf(d, fabsf(c[i]));
+    const uint16_t bits = po_float_to_half(d);
+    if (!isfinite(po_half_to_float(bits))) return PO_E_NONFINITE;
+    o[size - 2] = (uint8_t)(bits & 0xff);
+    o[size - 1] = (uint8_t)(bits >> 8);
+    float inverse = 0.0f;
+    if (d != 0.0f) {
+      inverse = 1.0f / d;
+      if (!isfinite(inverse)) return PO_E_NONFINITE;
+    }
+    uint8_t level[256];
+    for (int i = 0; i < 256; ++i) level[i] = (uint8_t)((int)(int16_t)roundf(c[i] * inverse) + 1);
+    if (kind == 35) {
+      for (int i = 0; i < 256; ++i)
+        o[i / 128 * 32 + i % 32] |= (uint8_t)(level[i] << (2 * (i % 128 / 32)));
+      continue;
+    }
+    for (int byte = 0; byte < 52; ++byte) {
+      int first, stride, count;
+      if (byte < 32) {
+        first = byte; stride = 32; count = 5;
+      } else if (byte < 48) {
+        first = 160 + byte - 32; stride = 16; count = 5;
+      } else {
+        first = 240 + byte - 48; stride = 4; count = 4;
+      }
+      unsigned code = 0;
+      for (int k = 0; k < count; ++k) code = code * 3 + level[first + k * stride];
+      if (count == 4) code *= 3;
+      o[byte] = (uint8_t)((code * 256 + 242) / 243);
+    }
+  }
+  return PO_OK;
+}

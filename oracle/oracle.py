@@ -75,6 +75,7 @@ def _declare(L):
         "po_ext_decode": (i32, [u32, vp, sz, vp]),
         "po_ext_block_ints": (i32, [u32, vp, vp, sz, vp, vp]),
         "po_ext_dot": (i32, [u32, vp, vp, sz, vp]),
+        "po_tq_quantize": (i32, [u32, vp, sz, vp]),
         "po_kvq_splitmix": (ctypes.c_uint64, [vp]),
         "po_kvq_levels": (None, [i32, vp]),
         "po_kvq_record_bytes": (i32, [i32]),
@@ -192,6 +193,14 @@ def tq2_quantize(x):
     x = np.ascontiguousarray(x, dtype=np.float32)
     out = np.zeros(x.size // 256 * 66, dtype=np.uint8)
     _check(lib().po_tq2_quantize(_p(x), x.size, _p(out)))
+    return out
+
+
+def tq_quantize(kind, x):
+    """f32 -> TQ1_0 (34) or TQ2_0 (35) blocks (reference tquants::quantize)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.zeros(x.size // 256 * {34: 54, 35: 66}[kind], dtype=np.uint8)
+    _check(lib().po_tq_quantize(kind, _p(x), x.size, _p(out)))
     return out
 
 

@@ -147,6 +147,7 @@ int po_ext_block_ints(uint32_t kind, const uint8_t *w, const po_q8k_block *a, si
                       int32_t *lanes, int32_t *msum);
 int po_ext_dot(uint32_t kind, const uint8_t *w, const po_q8k_block *a, size_t nblocks,
                float *out);
+int po_tq_quantize(uint32_t kind, const float *x, size_t n, uint8_t *out);
 
 /* ---- rotated scalar KV codec, rsq (kvq_oracle.c) -------------------- */
 uint64_t po_kvq_splitmix(uint64_t *state);

@@ -177,4 +177,65 @@ __global__ void __launch_bounds__(kKqWarps * 32) kquant_matvec_kernel(KquantArgs
   }
 }
 
+// f32 rows -> TQ1_0 (34) or TQ2_0 (35) blocks (reference
+// src/kernels/tquants.rs:288-336 quantize): d = max |x| stored as binary16;
+// level = round-half-away(x * (1 / d)) + 1 (0 when d is 0); TQ2_0 ORs the
+// levels into 2-bit fields, TQ1_0 folds five (or four, then times 3) levels
+// per byte in base 3 and stores ceil(code * 256 / 243).  One CTA of 256
+// threads per block, a thread per weight; the caller has checked nothing, so
+// a nonfinite input reports invalid and an overflowing d nonfinite (the
+// block is then left unwritten).
+__global__ void __launch_bounds__(256) tq_quantize_kernel(uint32_t kind, const float *x,
+                                                           uint8_t *out, unsigned *status) {
+  __shared__ uint8_t level[256];
+  __shared__ float red[8];
+  const int i = threadIdx.x;
+  const long b = blockIdx.x;
+  grid_dependency_wait();
+  grid_dependents_launch();
+  const float v = x[b * 256 + i];
+  if (!__syncthreads_and(is_finite_f(v))) {
+    if (i == 0) report(status, kStatusInvalid);
+    return;
+  }
+  float m = fabsf(v);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if ((i & 31) == 0) red[i >> 5] = m;
+  __syncthreads();
+  float d = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) d = fmaxf(d, red[w]);
+  const uint16_t bits = float_to_half_bits(d);
+  const float inverse = d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d);
+  if (!is_finite_f(half_bits_to_float(bits)) || !is_finite_f(inverse)) {
+    if (i == 0) report(status, kStatusNonfinite);
+    return;
+  }
+  level[i] = (uint8_t)((int)roundf(__fmul_rn(v, inverse)) + 1);
+  __syncthreads();
+  const int size = kind == 35 ? 66 : 54;
+  uint8_t *o = out + b * size;
+  if (kind == 35) {
+    if (i < 64) {
+      const int half = i / 32, col = i % 32;
+      unsigned byte = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) byte |= (unsigned)level[half * 128 + col + 32 * k] << (2 * k);
+      o[i] = (uint8_t)byte;
+    }
+  } else if (i < 52) {
+    const int first = i < 32 ? i : i < 48 ? 160 + i - 32 : 240 + i - 48;
+    const int stride = i < 32 ? 32 : i < 48 ? 16 : 4, count = i < 48 ? 5 : 4;
+    unsigned code = 0;
+    for (int k = 0; k < count; ++k) code = code * 3 + level[first + k * stride];
+    if (count == 4) code *= 3;
+    o[i] = (uint8_t)((code * 256 + 242) / 243);
+  }
+  if (i == 0) {
+    o[size - 2] = (uint8_t)(bits & 0xff);
+    o[size - 1] = (uint8_t)(bits >> 8);
+  }
+}
+
 }  // namespace prism

@@ -439,6 +439,60 @@ int prism_b200_project(prism_b200_executor *ex, const prism_b200_weight *w,
   return st;
 }
 
+// ---- f32 -> TQ1_0 / TQ2_0 (reference src/kernels/tquants.rs:288-336) --------
+
+static int tq_quantize_check(prism_b200_executor *ex, uint32_t kind, size_t n) {
+  if (kind != PRISM_B200_KIND_TQ2_0 && kind != PRISM_B200_KIND_TQ1_0)
+    return ex->fail(PRISM_B200_E_UNSUPPORTED, "no quantizer for kind %u", kind);
+  if (n == 0 || n % 256 || n / 256 > 0x7fffffffu)
+    return ex->fail(PRISM_B200_E_INVALID, "quantizer needs complete 256-value blocks");
+  return PRISM_B200_OK;
+}
+
+static cudaError_t launch_tq_quantize(prism_b200_executor *ex, uint32_t kind, const float *x,
+                                      size_t n, uint8_t *out, cudaStream_t s) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_config(dim3((unsigned)(n / 256)), dim3(256), 0, s, attr, ex->pdl);
+  return cudaLaunchKernelEx(&cfg, tq_quantize_kernel, kind, x, out, ex->d_status);
+}
+
+extern "C" int prism_b200_quantize_tq_device(prism_b200_executor *ex, uint32_t kind,
+                                             const float *x_dev, size_t n, void *out_dev,
+                                             void *stream) {
+  int st = check_open(ex);
+  if (st) return st;
+  if ((st = tq_quantize_check(ex, kind, n))) return st;
+  if (!x_dev || !out_dev) return ex->fail(PRISM_B200_E_INVALID, "null device buffer");
+  cudaSetDevice(ex->device);
+  CK(launch_tq_quantize(ex, kind, x_dev, n, static_cast<uint8_t *>(out_dev), pick(ex, stream)),
+     "quantize launch");
+  return PRISM_B200_OK;
+}
+
+extern "C" int prism_b200_quantize_tq(prism_b200_executor *ex, uint32_t kind, const float *x,
+                                      size_t n, void *out) {
+  int st = check_open(ex);
+  if (st) return st;
+  if ((st = tq_quantize_check(ex, kind, n))) return st;
+  if (!x || !out) return ex->fail(PRISM_B200_E_INVALID, "null buffer");
+  const size_t obytes = n / 256 * (kind == PRISM_B200_KIND_TQ2_0 ? 66 : 54);
+  cudaSetDevice(ex->device);
+  CK(ex->x.ensure(n * sizeof(float)), "input buffer");
+  CK(ex->y.ensure(obytes), "output buffer");
+  cudaStream_t s = ex->stream;
+  CK(cudaMemcpyAsync(ex->x.ptr, x, n * sizeof(float), cudaMemcpyHostToDevice, s), "input copy");
+  CK(launch_tq_quantize(ex, kind, static_cast<const float *>(ex->x.ptr), n,
+                        static_cast<uint8_t *>(ex->y.ptr), s),
+     "quantize launch");
+  if ((st = finish(ex, s))) {
+    memset(out, 0, obytes);
+    return st;
+  }
+  CK(cudaMemcpyAsync(out, ex->y.ptr, obytes, cudaMemcpyDeviceToHost, s), "output copy");
+  CK(cudaStreamSynchronize(s), "output copy");
+  return PRISM_B200_OK;
+}
+
 int prism_b200_quantize_q8k_device(prism_b200_executor *ex, const float *x_dev, size_t n,
                                    int pinned, void *out_dev, void *stream) {
   int st = check_open(ex);

@@ -105,6 +105,8 @@ def load():
         "prism_b200_ffn_chain_tokens_device": (i32, [vp, sz, vp, vp, i32, vp, vp]),
         "prism_b200_executor_operation_capacity": (i64, [vp]),
         "prism_b200_tensor_peak_i8": (i32, [vp, i32, P(ctypes.c_double)]),
+        "prism_b200_quantize_tq": (i32, [vp, u32, vp, sz, vp]),
+        "prism_b200_quantize_tq_device": (i32, [vp, u32, vp, sz, vp, vp]),
         "prism_b200_kvq_record_bytes": (i32, [u32]),
         "prism_b200_kvq_encode": (i32, [vp, u32, u64, u32, vp, sz, vp]),
         "prism_b200_kvq_encode_device": (i32, [vp, u32, u64, u32, vp, sz, vp, vp]),
@@ -260,6 +262,14 @@ class ProjectionExecutor:
         v = ctypes.c_double(0.0)
         self._check(load().prism_b200_tensor_peak_i8(self.h, iters, ctypes.byref(v)))
         return v.value
+
+    def quantize_tq(self, kind, x):
+        """f32 weights -> TQ1_0 (34) or TQ2_0 (35) blocks (reference
+        src/kernels/tquants.rs:288-336 quantize)."""
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+        out = np.zeros(x.size // 256 * {34: 54, 35: 66}.get(kind, 1), np.uint8)
+        self._check(load().prism_b200_quantize_tq(self.h, kind, _p(x), x.size, _p(out)))
+        return out
 
     # -- rotated scalar KV codec (reference src/kv_quant.rs) --------------
     def kvq_encode(self, bits, seed, rows, version=1):

@@ -91,3 +91,31 @@ def test_refusals_leave_the_executor_open(ex):
     assert not ex.supports(pb.Tensor(12, 384, 4, rand_rows(12, 4, 256, 1)))  # cols % 256
     got = ex.project_f32(t, x)
     assert np.array_equal(bits(got), bits(oracle.matvec(12, w, 64, 512, oracle.q8k_quantize(x))))
+
+
+@pytest.mark.parametrize("kind,name", [(35, "tq2_0.json"), (34, "tq1_0.json")])
+def test_tq_quantizer_on_device(ex, kind, name):
+    """f32 -> TQ1_0 / TQ2_0 (reference src/kernels/tquants.rs:288-336): the
+    golden InputHex -> OutputHex cases, random rows, a zero block, ties at
+    +-0.5 * d, and the refusals."""
+    from oracle import oracle
+    with open(os.path.join(GOLDEN, name)) as f:
+        cases = [c for c in json.load(f)["cases"] if "InputHex" in c]
+    for c in cases:
+        x = np.frombuffer(bytes.fromhex(c["InputHex"]), "<f4")
+        assert ex.quantize_tq(kind, x).tobytes().hex() == c["OutputHex"], c["Name"]
+    rng = np.random.default_rng(kind)
+    x = (rng.standard_normal(256 * 40) * rng.uniform(1e-3, 10, 256 * 40)).astype(np.float32)
+    x[:256] = 0.0                                  # a zero block
+    x[256:512] = np.tile([1.0, 0.5, -0.5, 0.25], 64)  # exact ties at d / 2
+    assert np.array_equal(ex.quantize_tq(kind, x), oracle.tq_quantize(kind, x))
+    with pytest.raises(pb.PrismB200Error) as e:   # not a whole block
+        ex.quantize_tq(kind, x[:300])
+    assert e.value.code == pb.E_INVALID
+    bad = x[:512].copy()
+    bad[7] = np.inf
+    with pytest.raises(pb.PrismB200Error) as e:
+        ex.quantize_tq(kind, bad)
+    assert e.value.code == pb.E_INVALID
+    ex.reset()
+    assert np.array_equal(ex.quantize_tq(kind, x[:512]), oracle.tq_quantize(kind, x[:512]))

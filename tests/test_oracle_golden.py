@@ -47,6 +47,18 @@ def test_tq2_quantizer_matches_golden(oracle):
         assert oracle.tq2_quantize(x).tobytes().hex() == case["OutputHex"], case["Name"]
 
 
+@pytest.mark.parametrize("name,kind", [("tq2_0.json", 35), ("tq1_0.json", 34)])
+def test_tq_quantizer_matches_golden(oracle, name, kind):
+    n = 0
+    for case in _load(name)["cases"]:
+        if "InputHex" not in case:
+            continue
+        x = np.frombuffer(bytes.fromhex(case["InputHex"]), dtype="<f4")
+        assert oracle.tq_quantize(kind, x).tobytes().hex() == case["OutputHex"], case["Name"]
+        n += 1
+    assert n >= 1
+
+
 def test_q8k_source_and_pinned_rounding_controls(oracle):
     for case in _load("q8k_parity.json")["cases"]:
         x = np.zeros(256, dtype=np.float32)

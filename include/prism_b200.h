@@ -571,6 +571,58 @@ int prism_b200_model_step_timings(prism_b200_model *m, float *attention_ms, floa
 int64_t prism_b200_model_read_state(prism_b200_model *m, uint32_t layer, uint32_t which,
                                     void *out, size_t bytes);
 
+/* ---- GGUF model files --------------------------------------------------- */
+/* The reference's model loading (reference src/model.rs:266-420 Model::load)
+ * and Qwen35 geometry (src/graph.rs:2966-3100): gguf_open reads a GGUF file
+ * (version 2 or 3) whole and checks its header, typed metadata, tensor table
+ * and every tensor's extent and alignment (general.alignment, default 32);
+ * tensor types are F32, F16 and the packed kinds above.  On failure `err`
+ * (when given) receives the reason.  gguf_qwen35_config reads the
+ * reference's `qwen35.*` keys (embedding_length, block_count,
+ * attention.head_count[_kv], attention.key_length = value_length,
+ * rope.dimension_count, rope.dimension_sections[4], rope.freq_base,
+ * attention.layer_norm_rms_epsilon, feed_forward_length, ssm.state_size,
+ * ssm.group_count, ssm.time_step_rank, ssm.conv_kernel, ssm.inner_size,
+ * full_attention_interval (default 4) and, when present,
+ * attention.recurrent_layers, which must follow that interval); the
+ * vocabulary and weight kind come from token_embd.weight.  An untied
+ * output.weight is refused (E_UNSUPPORTED): the head is the embedding.
+ * model_load_gguf creates the model and binds every tensor by its GGUF
+ * name (F32 / F16 tensors as vectors, packed ones as weights), then
+ * finalizes it.  The file's bytes stay with the gguf handle; the model keeps
+ * its own copies in HBM. */
+typedef struct prism_b200_gguf prism_b200_gguf;
+int prism_b200_gguf_open(const char *path, prism_b200_gguf **out, char *err, size_t err_len);
+void prism_b200_gguf_close(prism_b200_gguf *g);
+int64_t prism_b200_gguf_tensor_count(const prism_b200_gguf *g);
+int prism_b200_gguf_tensor(const prism_b200_gguf *g, size_t index, const char **name,
+                           uint32_t *type, uint64_t dims[4], uint32_t *ndims, const void **data,
+                           uint64_t *bytes);
+int prism_b200_gguf_qwen35_config(const prism_b200_gguf *g, uint32_t context, uint32_t kv_policy,
+                                  prism_b200_qwen35_config *cfg, char *err, size_t err_len);
+int prism_b200_model_load_gguf(prism_b200_executor *ex, const prism_b200_gguf *g,
+                               uint32_t context, uint32_t kv_policy, prism_b200_model **out);
+
+/* ---- decoder checkpoints ----------------------------------------------- */
+/* The reference's Decoder::checkpoint / checkpoint_into / restore /
+ * checkpoint_bytes (reference src/lib.rs:105,305-319; Qwen35 at
+ * src/graph.rs:5483-5578).  A checkpoint is a device-resident copy of every
+ * piece of state a later step reads: the KV rows of positions [0, p) (in the
+ * model's KV policy), each GDN layer's recurrent matrix and convolution
+ * history, the token history through the next input and the position.  It
+ * restores only into the model that took it (the reference's provenance
+ * check), on the same device; position 0 holds no layer payload and restores
+ * as a reset.  checkpoint_into reuses the checkpoint's storage when it is
+ * large enough.  The copies are device to device on the model's stream and
+ * the calls wait for them. */
+typedef struct prism_b200_checkpoint prism_b200_checkpoint;
+int prism_b200_model_checkpoint(prism_b200_model *m, prism_b200_checkpoint **out);
+int prism_b200_model_checkpoint_into(prism_b200_model *m, prism_b200_checkpoint *cp);
+int prism_b200_model_restore(prism_b200_model *m, const prism_b200_checkpoint *cp);
+int64_t prism_b200_checkpoint_bytes(const prism_b200_checkpoint *cp);
+int64_t prism_b200_checkpoint_position(const prism_b200_checkpoint *cp);
+void prism_b200_checkpoint_destroy(prism_b200_checkpoint *cp);
+
 /* ---- batched serving -------------------------------------------------- */
 /* Many sequences decoded together over one finalized model's resident
  * weights (its config, weights and KV policy).  Every step advances each of

@@ -159,7 +159,8 @@ __global__ void __launch_bounds__(kKqWarps * 32) kquant_matvec_kernel(KquantArgs
       const float dact = __fmul_rn(dj, sj);
 #pragma unroll
       for (int l = 0; l < 8; ++l)
-        lanes[l] = __fadd_rn(lanes[l], __fmul_rn(dact, (float)__shfl_sync(0xffffffffu, ints[l], j)));
+        lanes[l] =
+            __fadd_rn(lanes[l], __fmul_rn(dact, (float)__shfl_sync(0xffffffffu, ints[l], j)));
       if (a.kind == 12 || a.kind == 13) {
         const float mj = __shfl_sync(0xffffffffu, dmin, j);
         const int msj = __shfl_sync(0xffffffffu, msum, j);

@@ -10,6 +10,7 @@
 // finishes.
 #pragma once
 
+#include <atomic>
 #include <map>
 #include <string>
 #include <vector>
@@ -51,6 +52,7 @@ struct PrefillBuffers {
 
 struct prism_b200_model {
   prism_b200_executor *ex = nullptr;
+  uint64_t serial = 0;  // process-unique: the provenance a checkpoint carries
   prism_b200_qwen35_config cfg{};
   std::vector<prism::ModelLayer> L;
   prism::DeviceWeight embd;
@@ -783,6 +785,8 @@ int prism_b200_model_create(prism_b200_executor *ex, const prism_b200_qwen35_con
   if (!ok) return ex->fail(PRISM_B200_E_UNSUPPORTED, "unsupported Qwen35 geometry");
   cudaSetDevice(ex->device);
   auto *m = new prism_b200_model();
+  static std::atomic<uint64_t> next_serial{1};
+  m->serial = next_serial.fetch_add(1);
   m->ex = ex;
   m->cfg = c;
   m->L.resize(c.layers);

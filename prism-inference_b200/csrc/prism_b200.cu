@@ -885,6 +885,8 @@ extern "C" int prism_b200_gdn_prefill_device_noalloc(prism_b200_executor *ex, in
 
 // The model entry points share this translation unit's kernels and helpers.
 #include "model.cuh"
+#include "checkpoint.cuh"
+#include "gguf.cuh"
 #include "batch.cuh"
 #include "prefill.cuh"
 #include "tp_ffn.cuh"

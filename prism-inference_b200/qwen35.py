@@ -175,6 +175,89 @@ def c_config(cfg, kv_policy=KV_F16):
     return cc
 
 
+def config_from_c(cc):
+    """A Qwen35Config of a prism_b200_qwen35_config (the inverse of c_config)."""
+    kw = {}
+    for f, _ in _CConfig._fields_:
+        if f == "rope_sections":
+            kw[f] = tuple(cc.rope_sections)
+        elif f != "kv_policy":
+            kw[f] = getattr(cc, f)
+    return Qwen35Config(**kw)
+
+
+class GgufFile:
+    """A parsed GGUF file (prism_b200_gguf): the reference's Model::load
+    checks; `config` is the Qwen35 geometry from its `qwen35.*` keys."""
+
+    def __init__(self, path):
+        import ctypes as c
+        self.h = None
+        self.L = L = pb.load()
+        _declare_gguf(L)
+        err = c.create_string_buffer(512)
+        h = c.c_void_p()
+        st = L.prism_b200_gguf_open(str(path).encode(), c.byref(h), err, len(err))
+        if st:
+            raise pb.PrismB200Error(st, err.value.decode())
+        self.h = h
+
+    def config(self, context, kv_policy=KV_F16):
+        import ctypes as c
+        cc = _CConfig()
+        err = c.create_string_buffer(512)
+        st = self.L.prism_b200_gguf_qwen35_config(self.h, context, kv_policy, c.byref(cc), err,
+                                                  len(err))
+        if st:
+            raise pb.PrismB200Error(st, err.value.decode())
+        return config_from_c(cc)
+
+    def tensors(self):
+        """[(name, type, dims, bytes)] in file order; bytes are a copy."""
+        import ctypes as c
+        out = []
+        for i in range(self.L.prism_b200_gguf_tensor_count(self.h)):
+            name, typ = c.c_char_p(), c.c_uint32()
+            dims, nd = (c.c_uint64 * 4)(), c.c_uint32()
+            data, nbytes = c.c_void_p(), c.c_uint64()
+            self.L.prism_b200_gguf_tensor(self.h, i, c.byref(name), c.byref(typ), dims,
+                                          c.byref(nd), c.byref(data), c.byref(nbytes))
+            out.append((name.value.decode(), typ.value, list(dims)[:nd.value],
+                        c.string_at(data.value, nbytes.value)))
+        return out
+
+    def close(self):
+        if self.h:
+            self.L.prism_b200_gguf_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+def _declare_gguf(L):
+    import ctypes as c
+    if getattr(L, "_gguf_declared", False):
+        return
+    vp, sz = c.c_void_p, c.c_size_t
+    for name, res, args in (
+            ("prism_b200_gguf_open", c.c_int, [c.c_char_p, c.POINTER(vp), c.c_char_p, sz]),
+            ("prism_b200_gguf_close", None, [vp]),
+            ("prism_b200_gguf_tensor_count", c.c_int64, [vp]),
+            ("prism_b200_gguf_tensor", c.c_int, [vp, sz, c.POINTER(c.c_char_p),
+                                                 c.POINTER(c.c_uint32), c.POINTER(c.c_uint64),
+                                                 c.POINTER(c.c_uint32), c.POINTER(vp),
+                                                 c.POINTER(c.c_uint64)]),
+            ("prism_b200_gguf_qwen35_config", c.c_int, [vp, c.c_uint32, c.c_uint32, vp,
+                                                        c.c_char_p, sz]),
+            ("prism_b200_model_load_gguf", c.c_int, [vp, vp, c.c_uint32, c.c_uint32,
+                                                     c.POINTER(vp)])):
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    L._gguf_declared = True
+
+
 def tp_plan(cfg, rank, size):
     """The slice of every linear rank `rank` of a `size`-way tensor-parallel
     batch owns (host only): dict of [first, end) ranges -- query heads, KV
@@ -231,6 +314,23 @@ class Qwen35Model:
         h = c.c_void_p()
         executor._check(L.prism_b200_model_create(executor.h, c.byref(cc), c.byref(h)))
         self.h = h
+
+    @classmethod
+    def from_gguf(cls, executor, gguf, context, kv_policy=KV_F16):
+        """The model of a GGUF file (prism_b200_model_load_gguf): geometry
+        from its metadata, every tensor bound by name, finalized."""
+        import ctypes as c
+        g = gguf if isinstance(gguf, GgufFile) else GgufFile(gguf)
+        self = cls.__new__(cls)
+        self.L, self.ex = g.L, executor
+        _declare_model(self.L)
+        self.cfg = g.config(context, kv_policy)
+        self._cc = c_config(self.cfg, kv_policy)
+        h = c.c_void_p()
+        executor._check(self.L.prism_b200_model_load_gguf(executor.h, g.h, context, kv_policy,
+                                                          c.byref(h)))
+        self.h = h
+        return self
 
     def close(self):
         if self.h:
@@ -314,6 +414,41 @@ class Qwen35Model:
         if n < 0:
             raise pb.PrismB200Error(-n, "state readback failed")
         return out
+
+    # -- checkpoints (reference Decoder::checkpoint / restore) --------------
+    def _declare_checkpoint(self):
+        import ctypes as c
+        L = self.L
+        if getattr(L, "_ckpt_declared", False):
+            return
+        vp = c.c_void_p
+        for name, res, args in (
+                ("prism_b200_model_checkpoint", c.c_int, [vp, c.POINTER(vp)]),
+                ("prism_b200_model_checkpoint_into", c.c_int, [vp, vp]),
+                ("prism_b200_model_restore", c.c_int, [vp, vp]),
+                ("prism_b200_checkpoint_bytes", c.c_int64, [vp]),
+                ("prism_b200_checkpoint_position", c.c_int64, [vp]),
+                ("prism_b200_checkpoint_destroy", None, [vp])):
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        L._ckpt_declared = True
+
+    def checkpoint(self):
+        """A device-resident copy of the decoder state (Checkpoint)."""
+        import ctypes as c
+        self._declare_checkpoint()
+        h = c.c_void_p()
+        self.ex._check(self.L.prism_b200_model_checkpoint(self.h, c.byref(h)))
+        return Checkpoint(self.L, h)
+
+    def checkpoint_into(self, cp):
+        self._declare_checkpoint()
+        self.ex._check(self.L.prism_b200_model_checkpoint_into(self.h, cp.h))
+
+    def restore(self, cp):
+        self._declare_checkpoint()
+        self.ex._check(self.L.prism_b200_model_restore(self.h, cp.h))
 
     def records(self, layer, value=False):
         """The rotated scalar KV records (kv_policy KV_RSQ4, _RSQ4VF,
@@ -416,6 +551,29 @@ def _declare_batch(L):
 
 EXCHANGE_HANDLE_BYTES = 64
 TP_EXACT, TP_ALLREDUCE = 0, 1
+
+
+class Checkpoint:
+    """A decoder checkpoint on the device (prism_b200_checkpoint)."""
+
+    def __init__(self, L, handle):
+        self.L, self.h = L, handle
+
+    @property
+    def bytes(self):
+        return self.L.prism_b200_checkpoint_bytes(self.h)
+
+    @property
+    def position(self):
+        return self.L.prism_b200_checkpoint_position(self.h)
+
+    def close(self):
+        if self.h:
+            self.L.prism_b200_checkpoint_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
 
 
 class Qwen35Batch:

@@ -571,6 +571,49 @@ int prism_b200_model_step_timings(prism_b200_model *m, float *attention_ms, floa
 int64_t prism_b200_model_read_state(prism_b200_model *m, uint32_t layer, uint32_t which,
                                     void *out, size_t bytes);
 
+/* ---- the batched gated-delta op (snapshots and replay) ------------------ */
+/* The reference's ggml GDN backend op (reference src/backend/gdn.rs:24-300
+ * CpuBackend::delta_values, operation 100, or 101 with `replay`).  Tensors
+ * in ggml order (first index fastest), device pointers:
+ *   q [width][q_heads][tokens][q_sequences], k [width][k_heads][tokens]
+ *   [k_sequences] (head h reads q/k head h % q_heads, sequence s reads
+ *   sequence s / (sequences / q_sequences)); v [width][heads][tokens]
+ *   [sequences]; gate [gate_width = 1 or width][heads][tokens][sequences];
+ *   beta [1][heads][tokens][sequences]; state table [width*width*heads]
+ *   [state_rows]; rows (op 100, optional) the distinct table row of each
+ *   sequence, else sequence s reads row s; bias, weight [heads] with `raw`
+ *   (beta through the sigmoid, gate through weight * softplus(gate + bias));
+ *   records [sequences][record_banks][record_bank_elems] and control
+ *   [sequences][count, bank] with `replay`.
+ * Per token: state *= exp(gate) (per column with per-column gates), delta =
+ * (v - dot(S_row, k)) * beta, S_row += k * delta, out = dot(S_row, q) /
+ * sqrt(width); dot sums exact binary64 products in column order.  `out`
+ * (prism_b200_gdn_delta_values_outputs floats) receives the attention rows,
+ * then the snapshot slots (slot tokens-1-t = the state after token t; slots
+ * past the tokens keep their contents), or in replay the state after token
+ * tokens - min(tokens, snapshots) and the later tokens' records
+ * (delta[heads*width], keys[heads*width], decay[heads]).  Widths up to 128;
+ * raw gates with replay are refused (the reference reads both from one
+ * source).  Invalid rows, control or record extents are device-side errors
+ * (E_INVALID at the next sync). */
+typedef struct prism_b200_gdn_op {
+  uint32_t width, heads, tokens, sequences;
+  uint32_t q_heads, k_heads, q_sequences, k_sequences;
+  uint32_t gate_width;
+  uint32_t snapshots;
+  int32_t raw, replay;
+  uint32_t state_rows;
+  uint32_t record_banks;
+  uint64_t record_bank_elems, records_len;
+} prism_b200_gdn_op;
+size_t prism_b200_gdn_delta_values_outputs(const prism_b200_gdn_op *op);
+int prism_b200_gdn_delta_values_device(prism_b200_executor *ex, const prism_b200_gdn_op *op,
+                                       const float *q, const float *k, const float *v,
+                                       const float *gate, const float *beta, const float *table,
+                                       const int32_t *rows, const float *bias,
+                                       const float *weight, const float *records,
+                                       const int32_t *control, float *out, void *stream);
+
 /* ---- GGUF model files --------------------------------------------------- */
 /* The reference's model loading (reference src/model.rs:266-420 Model::load)
  * and Qwen35 geometry (src/graph.rs:2966-3100): gguf_open reads a GGUF file

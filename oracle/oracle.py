@@ -76,6 +76,8 @@ def _declare(L):
         "po_ext_block_ints": (i32, [u32, vp, vp, sz, vp, vp]),
         "po_ext_dot": (i32, [u32, vp, vp, sz, vp]),
         "po_tq_quantize": (i32, [u32, vp, sz, vp]),
+        "po_gdn_delta_values": (i32, [vp] * 13),
+        "po_gdn_delta_values_outputs": (sz, [vp]),
         "po_kvq_splitmix": (ctypes.c_uint64, [vp]),
         "po_kvq_levels": (None, [i32, vp]),
         "po_kvq_record_bytes": (i32, [i32]),
@@ -361,6 +363,32 @@ def kvq_attend(policy, queries, keys, values, heads, kv_heads, attn_scale, gates
         g = np.ascontiguousarray(gates[h], np.float32)
         _check(lib().po_kvq_attend_head(kb, KVQ_KEY_SEED, vb, KVQ_VALUE_SEED, _p(q), _p(k), _p(v),
                                         n, float(attn_scale), _p(g), _p(out[h])))
+    return out
+
+
+class GdnOp(ctypes.Structure):
+    """po_gdn_op: geometry of the batched gated-delta op (gdn_op_oracle.c)."""
+    _fields_ = [(n, ctypes.c_uint32) for n in ("width", "heads", "tokens", "sequences",
+                                               "q_heads", "k_heads", "q_sequences",
+                                               "k_sequences", "gate_width", "snapshots")] + \
+               [("raw", ctypes.c_int32), ("replay", ctypes.c_int32),
+                ("state_rows", ctypes.c_uint32), ("record_banks", ctypes.c_uint32),
+                ("record_bank_elems", ctypes.c_uint64), ("records_len", ctypes.c_uint64)]
+
+
+def gdn_delta_values(op, q, k, v, gate, beta, table, rows=None, bias=None, weight=None,
+                     records=None, control=None):
+    """The reference's CpuBackend::delta_values (operation 100, or 101 when
+    op.replay): returns the flat output (attention rows, then snapshots or
+    the replay state and records)."""
+    L = lib()
+    f = lambda a: None if a is None else np.ascontiguousarray(a, np.float32)
+    i = lambda a: None if a is None else np.ascontiguousarray(a, np.int32)
+    arrs = [f(q), f(k), f(v), f(gate), f(beta), f(table), i(rows), f(bias), f(weight),
+            f(records), i(control)]
+    out = np.zeros(L.po_gdn_delta_values_outputs(ctypes.byref(op)), np.float32)
+    ptrs = [None if a is None else _p(a) for a in arrs]
+    _check(L.po_gdn_delta_values(ctypes.byref(op), *ptrs, _p(out)))
     return out
 
 

@@ -149,6 +149,23 @@ int po_ext_dot(uint32_t kind, const uint8_t *w, const po_q8k_block *a, size_t nb
                float *out);
 int po_tq_quantize(uint32_t kind, const float *x, size_t n, uint8_t *out);
 
+/* ---- batched gated-delta op with snapshots / replay (gdn_op_oracle.c) -- */
+typedef struct po_gdn_op {
+  uint32_t width, heads, tokens, sequences;
+  uint32_t q_heads, k_heads, q_sequences, k_sequences;
+  uint32_t gate_width;  /* 1 or width */
+  uint32_t snapshots;
+  int32_t raw, replay;
+  uint32_t state_rows;  /* rows of the state table */
+  uint32_t record_banks;
+  uint64_t record_bank_elems, records_len;
+} po_gdn_op;
+int po_gdn_delta_values(const po_gdn_op *op, const float *q, const float *k, const float *v,
+                        const float *gate, const float *beta, const float *table,
+                        const int32_t *rows, const float *bias, const float *weight,
+                        const float *records, const int32_t *control, float *out);
+size_t po_gdn_delta_values_outputs(const po_gdn_op *op);
+
 /* ---- rotated scalar KV codec, rsq (kvq_oracle.c) -------------------- */
 uint64_t po_kvq_splitmix(uint64_t *state);
 void po_kvq_levels(int levels, float *out);

@@ -15,6 +15,7 @@
 #include "common.cuh"
 #include "executor.cuh"
 #include "gdn.cuh"
+#include "gdn_op.cuh"
 #include "gemm.cuh"
 #include "packed.cuh"
 #include "kquant.cuh"
@@ -802,6 +803,78 @@ extern "C" int prism_b200_gdn_prefill_device(prism_b200_executor *ex, int batch,
 // a serving process that reserved all of HBM up front for weights and KV
 // pages has none left to give, and a decode loop with a latency budget
 // cannot absorb the device-wide synchronisation that cudaMalloc implies.
+// ---- the batched gated-delta op with snapshots / replay (gdn_op.cuh) ---------
+
+extern "C" size_t prism_b200_gdn_delta_values_outputs(const prism_b200_gdn_op *op) {
+  if (!op) return 0;
+  return gdn_op_outputs(op->width, op->heads, op->tokens, op->sequences, op->snapshots,
+                        op->replay != 0);
+}
+
+extern "C" int prism_b200_gdn_delta_values_device(
+    prism_b200_executor *ex, const prism_b200_gdn_op *op, const float *q, const float *k,
+    const float *v, const float *gate, const float *beta, const float *table,
+    const int32_t *rows, const float *bias, const float *weight, const float *records,
+    const int32_t *control, float *out, void *stream) {
+  int st = check_open(ex);
+  if (st) return st;
+  if (!op) return ex->fail(PRISM_B200_E_INVALID, "null op");
+  const prism_b200_gdn_op &o = *op;
+  if (o.snapshots == 0 || (o.replay && o.snapshots < 2) || (o.replay && o.raw))
+    return ex->fail(PRISM_B200_E_INVALID, "snapshot count, or raw gates with replay");
+  if (o.width == 0 || o.heads == 0 || o.sequences == 0 || (o.replay && o.tokens == 0) ||
+      o.q_heads == 0 || o.k_heads == 0 || o.q_sequences == 0 || o.k_sequences == 0 ||
+      o.sequences % o.q_sequences || o.sequences % o.k_sequences ||
+      (o.gate_width != 1 && o.gate_width != o.width) || o.state_rows == 0 ||
+      o.heads > 65535u || o.sequences > 65535u)
+    return ex->fail(PRISM_B200_E_INVALID, "gated-delta op geometry");
+  if (o.width > (uint32_t)kGdnOpMaxWidth)
+    return ex->fail(PRISM_B200_E_UNSUPPORTED, "state width %u above %d", o.width,
+                    kGdnOpMaxWidth);
+  if (!q || !k || !v || !gate || !beta || !table || !out ||
+      (o.raw && (!bias || !weight)) || (o.replay && (!records || !control || o.record_banks == 0)))
+    return ex->fail(PRISM_B200_E_INVALID, "null input");
+  GdnOpArgs a;
+  a.W = (int)o.width;
+  a.H = (int)o.heads;
+  a.T = (int)o.tokens;
+  a.S = (int)o.sequences;
+  a.qh = (int)o.q_heads;
+  a.kh = (int)o.k_heads;
+  a.qs = (int)o.q_sequences;
+  a.ks = (int)o.k_sequences;
+  a.gw = (int)o.gate_width;
+  a.snaps = (int)o.snapshots;
+  a.raw = o.raw ? 1 : 0;
+  a.replay = o.replay ? 1 : 0;
+  a.state_rows = (int)o.state_rows;
+  a.banks = (int)o.record_banks;
+  a.bank_elems = (long)o.record_bank_elems;
+  a.records_len = (long)o.records_len;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.gate = gate;
+  a.beta = beta;
+  a.table = table;
+  a.rows = o.replay ? nullptr : rows;
+  a.bias = bias;
+  a.weight = weight;
+  a.records = records;
+  a.control = control;
+  a.out = out;
+  a.status = ex->d_status;
+  const size_t smem = ((size_t)o.width * (o.width + 1) + 3 * (size_t)o.width) * 4;
+  cudaSetDevice(ex->device);
+  CK(cudaFuncSetAttribute(gdn_op_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+     "gated-delta op attribute");
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_config(dim3(o.heads, o.sequences), dim3(kGdnOpMaxWidth), smem,
+                                      pick(ex, stream), attr, ex->pdl);
+  CK(cudaLaunchKernelEx(&cfg, gdn_op_kernel, a), "gated-delta op launch");
+  return PRISM_B200_OK;
+}
+
 // This variant of prism_b200_gdn_prefill_device keeps its chunk scratch in
 // a fixed module-scope array (static_scratch.cu) instead of the executor's
 // growable buffer.  The prep kernel writes every scratch element that the

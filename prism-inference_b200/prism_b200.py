@@ -541,6 +541,35 @@ def gdn_prefill_device(ex, batch, tokens, heads, key_heads, chunk, state, q, k, 
                                               state, q, k, v, decay, beta, out, stream))
 
 
+class GdnOp(ctypes.Structure):
+    """prism_b200_gdn_op: geometry of the batched gated-delta op."""
+    _fields_ = [(n, ctypes.c_uint32) for n in ("width", "heads", "tokens", "sequences",
+                                               "q_heads", "k_heads", "q_sequences",
+                                               "k_sequences", "gate_width", "snapshots")] + \
+               [("raw", ctypes.c_int32), ("replay", ctypes.c_int32),
+                ("state_rows", ctypes.c_uint32), ("record_banks", ctypes.c_uint32),
+                ("record_bank_elems", ctypes.c_uint64), ("records_len", ctypes.c_uint64)]
+
+
+def gdn_delta_values_outputs(op):
+    L = load()
+    L.prism_b200_gdn_delta_values_outputs.restype = ctypes.c_size_t
+    L.prism_b200_gdn_delta_values_outputs.argtypes = [ctypes.c_void_p]
+    return L.prism_b200_gdn_delta_values_outputs(ctypes.byref(op))
+
+
+def gdn_delta_values_device(ex, op, q, k, v, gate, beta, table, out, rows=None, bias=None,
+                            weight=None, records=None, control=None, stream=None):
+    """The reference's gated-delta backend op (src/backend/gdn.rs:24-300) over
+    device pointers (0 / None for absent inputs)."""
+    L = load()
+    fn = L.prism_b200_gdn_delta_values_device
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p] * 15
+    ex._check(fn(ex.h, ctypes.byref(op), q, k, v, gate, beta, table, rows, bias, weight,
+                 records, control, out, stream))
+
+
 # Size of the fixed scratch of gdn_prefill_device_noalloc (include/prism_b200.h).
 GDN_STATIC_SCRATCH_BYTES = 32 * 1024 * 1024
 

@@ -33,7 +33,7 @@ def run(ex, kw, arrays):
     op = mkop(pb.GdnOp, **kw)
     out = torch.full((pb.gdn_delta_values_outputs(op),), float("nan"), device="cuda")
     # slots past the tokens keep the caller's contents: seed both sides alike
-    ptr = lambda n: None if dev[n] is None else dev[n].data_ptr()
+    ptr = lambda n: None if dev.get(n) is None else dev[n].data_ptr()
     pb.gdn_delta_values_device(ex, op, ptr("q"), ptr("k"), ptr("v"), ptr("gate"), ptr("beta"),
                                ptr("table"), out.data_ptr(), rows=ptr("rows"), bias=ptr("bias"),
                                weight=ptr("weight"), records=ptr("records"),
@@ -65,7 +65,7 @@ def ex():
                                               (8, 3, 4, 4, 8, 1), (64, 4, 1, 2, 1, 2)])
 def test_plain_op_with_rows_and_snapshots(ex, W, H, T, S, gw, snaps):
     a = inputs(W, H, T, S, gw, seed=W + T, rows=S + 2)
-    a["rows"] = np.array([(3 * s + 1) % (S + 2) for s in range(S)], np.int32)
+    a["rows"] = np.random.default_rng(S).permutation(S + 2)[:S].astype(np.int32)
     kw = dict(width=W, heads=H, tokens=T, sequences=S, q_heads=H, k_heads=H, q_sequences=S,
               k_sequences=S, gate_width=gw, snapshots=snaps, state_rows=S + 2)
     got, want = run(ex, kw, a)

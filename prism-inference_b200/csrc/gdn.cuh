@@ -265,8 +265,14 @@ __host__ __device__ constexpr size_t gdn_scan_smem() {
   // S[R][D] K,Q[C][kKS] M[C][kMS] CQ[C][kMS] V[C][R] KD,QD,DL[R][C+1] cum plast,
   // and with prefetch a second K, Q, V
   return (size_t)(R * kGdnD + (gdn_scan_prefetch<R>() ? 2 : 1) * (2 * kChunk * kKS + kChunk * R) +
-                  2 * kChunk * kMS + 3 * R * (kChunk + 1) + 2 * kChunk) *
+                  2 * kChunk * kMS + 3 * R * (kChunk + 1) +
+                  (gdn_scan_prefetch<R>() ? 2 : 1) * 2 * kChunk) *
          4;
+}
+
+__device__ __forceinline__ void gdn_cp_async4(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
 }
 
 __device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, bool valid) {
@@ -290,8 +296,7 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
   float *KD = CQ + C * kMS;               // [R][C+1]
   float *QD = KD + R * CP;                // [R][C+1]
   float *DL = QD + R * CP;                // [R][C+1]  deltas
-  float *cum = DL + R * CP;               // [C]
-  float *plast = cum + C;                 // [C]
+  float *cumb = DL + R * CP;              // [NB][2][C]: cum, then plast
   const GdnBatchArgs &a = p.g;
   const int g = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kh = h % a.key_heads;
@@ -320,7 +325,23 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  if (PF && p.nchunks > 0) issue(0, 0);
+  // chunk c's M, CQ, cum and P[C-1] from the prep kernel's scratch into M,
+  // CQ and cum/plast buffer `buf`, one asynchronous-copy group (M and CQ are
+  // free once the chunk before has formed its outputs)
+  auto issue_scr = [&](int c, int buf) {
+    const float *scr = p.scratch + (((long)b * a.heads + h) * p.nchunks + c) * kChunkScratch;
+    for (int i = tid; i < C * C; i += blockDim.x) {
+      gdn_cp_async4(M + (i / C) * kMS + i % C, scr + i);
+      gdn_cp_async4(CQ + (i / C) * kMS + i % C, scr + C * C + i);
+    }
+    for (int t = tid; t < 2 * C; t += blockDim.x)
+      gdn_cp_async4(cumb + buf * 2 * C + t, scr + 2 * C * C + t);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (PF && p.nchunks > 0) {
+    issue(0, 0);
+    issue_scr(0, 0);
+  }
   const float oscale = 1.0f / sqrtf((float)D);
   bool finite = true;
   for (int c = 0; c < p.nchunks; ++c) {
@@ -342,13 +363,13 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
       asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     const float *K = Kb + buf * C * kKS, *Q = Qb + buf * C * kKS, *V = Vb + buf * C * R;
-    for (int i = tid; i < C * C; i += blockDim.x) {
-      M[(i / C) * kMS + i % C] = scr[i];
-      CQ[(i / C) * kMS + i % C] = scr[C * C + i];
-    }
-    for (int t = tid; t < C; t += blockDim.x) {
-      cum[t] = scr[2 * C * C + t];
-      plast[t] = scr[2 * C * C + C + t];
+    const float *cum = cumb + buf * 2 * C, *plast = cum + C;
+    if (!PF) {
+      for (int i = tid; i < C * C; i += blockDim.x) {
+        M[(i / C) * kMS + i % C] = scr[i];
+        CQ[(i / C) * kMS + i % C] = scr[C * C + i];
+      }
+      for (int t = tid; t < 2 * C; t += blockDim.x) cumb[t] = scr[2 * C * C + t];
     }
     __syncthreads();
     // Register tiles: warp ti = tid / 32 owns rows r = ti + 16a (a < TR), lane
@@ -357,7 +378,31 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
     constexpr int TR = R / 16, TT = C / 32;
     const int ti = tid / 32, tj = tid % 32;
     // KD[r][t] = S_r . k_t, QD[r][t] = S_r . q_t
-    {
+    // R == 16: thread u < 256 owns rows 4g..4g+3 (g = u / 64) of token u % 64
+    // in the three tile phases, so that each K/Q/M/CQ row is read by 4 warps
+    if constexpr (R == 16) {
+      if (tid < 256) {
+        const int g4 = 4 * (tid / 64), t = tid % 64;
+        float dk[4] = {0.0f, 0.0f, 0.0f, 0.0f}, dq[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 2
+        for (int x = 0; x < D / 4; ++x) {
+          const float4 u = reinterpret_cast<const float4 *>(K + t * kKS)[x];
+          const float4 w = reinterpret_cast<const float4 *>(Q + t * kKS)[x];
+#pragma unroll
+          for (int a4 = 0; a4 < 4; ++a4) {
+            const float4 sr = reinterpret_cast<const float4 *>(S + (g4 + a4) * D)[x];
+            dk[a4] = fmaf(sr.x, u.x, fmaf(sr.y, u.y, fmaf(sr.z, u.z, fmaf(sr.w, u.w, dk[a4]))));
+            dq[a4] = fmaf(sr.x, w.x, fmaf(sr.y, w.y, fmaf(sr.z, w.z, fmaf(sr.w, w.w, dq[a4]))));
+          }
+        }
+#pragma unroll
+        for (int a4 = 0; a4 < 4; ++a4) {
+          const int r = g4 + a4;
+          KD[r * CP + t] = V[t * R + r] - cum[t] * dk[a4];
+          QD[r * CP + t] = dq[a4];
+        }
+      }
+    } else {
       float dk[TR][TT], dq[TR][TT];
 #pragma unroll
       for (int ai = 0; ai < TR; ++ai)
@@ -394,13 +439,27 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
     }
     __syncthreads();
     // delta[r][t] = sum_{j<=t} M[t][j] W[r][j]
-    {
+    if constexpr (R == 16) {
+      if (tid < 256) {
+        const int g4 = 4 * (tid / 64), t = tid % 64;
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 8
+        for (int j = 0; j <= t; ++j) {
+          const float mv = M[t * kMS + j];
+#pragma unroll
+          for (int a4 = 0; a4 < 4; ++a4) acc[a4] = fmaf(mv, KD[(g4 + a4) * CP + j], acc[a4]);
+        }
+#pragma unroll
+        for (int a4 = 0; a4 < 4; ++a4) DL[(g4 + a4) * CP + t] = t < n ? acc[a4] : 0.0f;
+      }
+    } else {
       float acc[TR][TT];
 #pragma unroll
       for (int ai = 0; ai < TR; ++ai)
 #pragma unroll
         for (int bi = 0; bi < TT; ++bi) acc[ai][bi] = 0.0f;
       const int tmax = tj + 32 * (TT - 1);
+      #pragma unroll 8
       for (int j = 0; j <= tmax; ++j) {
         float wv[TR], mv[TT];
 #pragma unroll
@@ -424,7 +483,23 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
     __syncthreads();
     // o[r][t] = (cum_t QD[r][t] + sum_{j<=t} CQ[t][j] delta[r][j]) / sqrt(d),
     // staged as [t][r] in the KD area (free now) for coalesced stores
-    {
+    if constexpr (R == 16) {
+      if (tid < 256) {
+        const int g4 = 4 * (tid / 64), t = tid % 64;
+        float acc[4];
+#pragma unroll
+        for (int a4 = 0; a4 < 4; ++a4) acc[a4] = cum[t] * QD[(g4 + a4) * CP + t];
+#pragma unroll 8
+        for (int j = 0; j <= t; ++j) {
+          const float cv = CQ[t * kMS + j];
+#pragma unroll
+          for (int a4 = 0; a4 < 4; ++a4) acc[a4] = fmaf(cv, DL[(g4 + a4) * CP + j], acc[a4]);
+        }
+        float *O = KD;  // [C][R]
+#pragma unroll
+        for (int a4 = 0; a4 < 4; ++a4) O[t * R + g4 + a4] = acc[a4] * oscale;
+      }
+    } else {
       float acc[TR][TT];
 #pragma unroll
       for (int ai = 0; ai < TR; ++ai)
@@ -432,6 +507,7 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
         for (int bi = 0; bi < TT; ++bi)
           acc[ai][bi] = cum[tj + 32 * bi] * QD[(ti + 16 * ai) * CP + tj + 32 * bi];
       const int tmax = tj + 32 * (TT - 1);
+      #pragma unroll 8
       for (int j = 0; j <= tmax; ++j) {
         float dv[TR], cv[TT];
 #pragma unroll
@@ -452,6 +528,7 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
           O[(tj + 32 * bi) * R + ti + 16 * ai] = acc[ai][bi] * oscale;
     }
     __syncthreads();
+    if (PF && c + 1 < p.nchunks) issue_scr(c + 1, buf ^ 1);  // M, CQ are free now
     for (int i = tid; i < R * C; i += blockDim.x) {
       const int t = i / R, r = i % R;  // r fastest: coalesced output stores
       if (t < n) a.out[(((long)b * a.T + t0 + t) * a.heads + h) * D + r0 + r] = KD[t * R + r];
@@ -467,6 +544,7 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
         acc[ai][0] = last * s0.x; acc[ai][1] = last * s0.y;
         acc[ai][2] = last * s0.z; acc[ai][3] = last * s0.w;
       }
+      #pragma unroll 8
       for (int j = 0; j < n; ++j) {
         float cf[TR];
 #pragma unroll

@@ -534,8 +534,46 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
       if (t < n) a.out[(((long)b * a.T + t0 + t) * a.heads + h) * D + r0 + r] = KD[t * R + r];
     }
     // S_r <- cum_last S_r + sum_j plast_j delta_rj k_j; warp ti owns rows
-    // r = ti + 16a, lane tj columns x = 4 tj .. 4 tj + 3
-    {
+    // r = ti + 16a, lane tj columns x = 4 tj .. 4 tj + 3 (R == 16: thread
+    // u < 128 owns rows 4 (u / 32) .. + 3 of columns 4 (u % 32) .. + 3, so
+    // each K row is read by 4 warps)
+    if constexpr (R == 16) {
+      const float last = cum[n - 1];
+      const int g4 = 4 * (tid / 32), x4 = 4 * (tid % 32);
+      float acc[4][4];
+      if (tid < 128) {
+#pragma unroll
+        for (int a4 = 0; a4 < 4; ++a4) {
+          const float4 s0 = reinterpret_cast<const float4 *>(S + (g4 + a4) * D + x4)[0];
+          acc[a4][0] = last * s0.x; acc[a4][1] = last * s0.y;
+          acc[a4][2] = last * s0.z; acc[a4][3] = last * s0.w;
+        }
+#pragma unroll 4
+        for (int j = 0; j < n; ++j) {
+          const float pj = plast[j];
+          const float4 k0 = reinterpret_cast<const float4 *>(K + j * kKS + x4)[0];
+          const float kx[4] = {k0.x, k0.y, k0.z, k0.w};
+#pragma unroll
+          for (int a4 = 0; a4 < 4; ++a4) {
+            const float cf = pj * DL[(g4 + a4) * CP + j];
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) acc[a4][c4] = fmaf(cf, kx[c4], acc[a4][c4]);
+          }
+        }
+      }
+      __syncthreads();  // every thread has read S before it is overwritten
+      if (tid < 128) {
+#pragma unroll
+        for (int a4 = 0; a4 < 4; ++a4) {
+          float *sr = S + (g4 + a4) * D + x4;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            finite &= is_finite_f(acc[a4][c4]);
+            sr[c4] = acc[a4][c4];
+          }
+        }
+      }
+    } else {
       const float last = cum[n - 1];
       float acc[TR][4];
 #pragma unroll

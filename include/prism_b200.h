@@ -384,17 +384,17 @@ int prism_b200_gdn_prefill_device(prism_b200_executor *ex, int batch, int tokens
  * take the device-wide synchronisation of an allocation.  Its chunk scratch
  * is a fixed array in the library's device image, of
  * PRISM_B200_GDN_STATIC_SCRATCH_BYTES; a call needing more
- * (batch x heads x ceil(tokens/chunk) x 33,280 bytes) fails with
+ * (batch x heads x ceil(tokens/chunk) x 35,328 bytes) fails with
  * PRISM_B200_E_INVALID before anything is enqueued.  The array is a device
  * module of its own: under CUDA's default lazy module loading it occupies
- * its 32 MiB on a device from the first call of this function there until
+ * its 34 MiB on a device from the first call of this function there until
  * the context is destroyed (with CUDA_MODULE_LOADING=EAGER, on every device
  * the process initialises, called or not).  The first call in a context
  * loads that module and looks the array's address up, so make it before any
  * stream capture; the address is cached per context.  All callers on a
  * device share the array: calls whose kernels can overlap in time (other
  * streams, other executors) race and must be serialised by the caller. */
-#define PRISM_B200_GDN_STATIC_SCRATCH_BYTES (32u * 1024u * 1024u)
+#define PRISM_B200_GDN_STATIC_SCRATCH_BYTES (34u * 1024u * 1024u)
 int prism_b200_gdn_prefill_device_noalloc(prism_b200_executor *ex, int batch, int tokens,
                                           int heads, int key_heads, int d, int chunk,
                                           float *state, const float *q, const float *k,

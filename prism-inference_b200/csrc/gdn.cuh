@@ -116,8 +116,14 @@ constexpr int kGdnD = 128;
 // rows in distinct bank groups, +1 does the same for scalar column walks
 constexpr int kKS = kGdnD + 4;
 constexpr int kMS = kChunk + 1;
-// scratch floats per (sequence, head, chunk): M, CQ, cum, P[C-1]
-constexpr int kChunkScratch = 2 * kChunk * kChunk + 2 * kChunk;
+// 16-byte rows (a multiple of 4 floats, 4 banks apart) for tiles read as
+// float4 along the row: the prep kernel's beta * CK and, in the prefetching
+// scan, M, CQ and the delta-side tiles
+constexpr int kMS4 = kChunk + 4;
+// scratch floats per (sequence, head, chunk): M and CQ in rows of kMS4
+// (the prefetching scan's tile layout, so that each arrives in one bulk
+// copy), then cum and P[C-1]
+constexpr int kChunkScratch = 2 * kChunk * kMS4 + 2 * kChunk;
 
 struct GdnPrefillArgs {
   GdnBatchArgs g;
@@ -135,8 +141,8 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefill
   float *K = sm;                 // [C][kKS]
   float *Q = K + C * kKS;        // [C][kKS]
   float *P = Q + C * kKS;        // [C][C+1]  decay products (padded)
-  float *Bm = P + C * (C + 1);   // [C][C+1]  beta * CK, then T
-  float *cum = Bm + C * (C + 1); // [C]
+  float *Bm = P + C * (C + 1);   // [C][kMS4]  beta * CK
+  float *cum = Bm + C * kMS4;    // [C]
   float *dec = cum + C;          // [C]
   float *bet = dec + C;          // [C]
   const GdnBatchArgs &a = p.g;
@@ -180,7 +186,7 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefill
   __syncthreads();
   // CK (strict lower) scaled by beta_t into Bm, CQ (lower) to scratch
   float *scr = p.scratch + (((long)b * a.heads + h) * p.nchunks + c) * kChunkScratch;
-  float *Mout = scr, *CQout = scr + C * C, *cumout = scr + 2 * C * C, *plast = cumout + C;
+  float *Mout = scr, *CQout = scr + C * kMS4, *cumout = scr + 2 * C * kMS4, *plast = cumout + C;
   {
     // register tiles: thread (ti, tj) owns t = ti + 16a, j = tj + 16b; the
     // dots keep the one-output-per-thread accumulation order
@@ -220,8 +226,8 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefill
           cq = pr * dkq[ai][bi];
           if (j < t) ck = pr * dkk[ai][bi];
         }
-        Bm[t * (C + 1) + j] = bet[t] * ck;
-        CQout[t * C + j] = cq;
+        Bm[t * kMS4 + j] = bet[t] * ck;
+        CQout[t * kMS4 + j] = cq;
       }
   }
   for (int t = threadIdx.x; t < C; t += blockDim.x) {
@@ -229,23 +235,37 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefill
     plast[t] = P[(n - 1) * (C + 1) + t];
   }
   __syncthreads();
-  // T = (I + Bm)^-1 (unit lower triangular), one column per thread, the
-  // column kept in shared memory over P (no longer needed):
-  // T[t][j] = -sum_{k=j}^{t-1} Bm[t][k] T[k][j]; then M = T diag(beta)
-  float *T = P;  // [C][C+1]
-  for (int j = threadIdx.x; j < C; j += blockDim.x) {
-    for (int t = 0; t <= j; ++t) T[t * (C + 1) + j] = t == j ? 1.0f : 0.0f;
-    for (int t = j + 1; t < C; ++t) {
+  // T = (I + Bm)^-1 (unit lower triangular): thread j < C holds column j in
+  // registers, T[t][j] = -sum_{k<t} Bm[t][k] T[k][j] in k order (the terms
+  // k < j add zeros to the zero start, so the sum is the one over
+  // j <= k < t); then M = T diag(beta).  Unrolled, a row's chain overlaps the
+  // rows before it, and Bm is read four entries per (broadcast) load.
+  if (threadIdx.x < C) {
+    const int j = threadIdx.x;
+    float col[C];
+#pragma unroll
+    for (int t = 0; t < C; ++t) col[t] = t == j ? 1.0f : 0.0f;
+#pragma unroll
+    for (int t = 1; t < C; ++t) {
       float s = 0.0f;
-      for (int k = j; k < t; ++k) s = fmaf(Bm[t * (C + 1) + k], T[k * (C + 1) + j], s);
-      T[t * (C + 1) + j] = -s;
+#pragma unroll
+      for (int k4 = 0; k4 < t; k4 += 4) {
+        const float4 bm = *reinterpret_cast<const float4 *>(Bm + t * kMS4 + k4);
+        s = fmaf(bm.x, col[k4], s);
+        if (k4 + 1 < t) s = fmaf(bm.y, col[k4 + 1], s);
+        if (k4 + 2 < t) s = fmaf(bm.z, col[k4 + 2], s);
+        if (k4 + 3 < t) s = fmaf(bm.w, col[k4 + 3], s);
+      }
+      if (t > j) col[t] = -s;
     }
-    for (int t = 0; t < C; ++t) Mout[t * C + j] = T[t * (C + 1) + j] * bet[j];
+    const float bj = bet[j];
+#pragma unroll
+    for (int t = 0; t < C; ++t) Mout[t * kMS4 + j] = col[t] * bj;
   }
 }
 
 __host__ __device__ constexpr size_t gdn_prep_smem() {
-  return (size_t)(2 * kChunk * kKS + 2 * kChunk * (kChunk + 1) + 3 * kChunk) * 4;
+  return (size_t)(2 * kChunk * kKS + kChunk * (kChunk + 1) + kChunk * kMS4 + 3 * kChunk) * 4;
 }
 
 // Scan over the chunks of one (sequence, head) for R state rows.
@@ -262,10 +282,11 @@ __host__ __device__ constexpr bool gdn_scan_prefetch() {
 
 template <int R>
 __host__ __device__ constexpr size_t gdn_scan_smem() {
-  // S[R][D] K,Q[C][kKS] M[C][kMS] CQ[C][kMS] V[C][R] KD,QD,DL[R][C+1] cum plast,
-  // and with prefetch a second K, Q, V
+  // S[R][D] K,Q[C][kKS] M[C][ms] CQ[C][ms] V[C][R] KD,QD,DL[R][ms] cum plast,
+  // and with prefetch a second K, Q, V (ms = kMS4 with prefetch, else kMS)
+  constexpr int ms = gdn_scan_prefetch<R>() ? kMS4 : kMS;
   return (size_t)(R * kGdnD + (gdn_scan_prefetch<R>() ? 2 : 1) * (2 * kChunk * kKS + kChunk * R) +
-                  2 * kChunk * kMS + 3 * R * (kChunk + 1) +
+                  2 * kChunk * ms + 3 * R * ms +
                   (gdn_scan_prefetch<R>() ? 2 : 1) * 2 * kChunk) *
          4;
 }
@@ -282,20 +303,23 @@ __device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, boo
 }
 
 template <int R>
-__global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefillArgs p) {
-  constexpr int D = kGdnD, C = kChunk, CP = kChunk + 1;
+__global__ void __launch_bounds__(kScanThreads, 1) gdn_chunk_scan_kernel(GdnPrefillArgs p) {
+  constexpr int D = kGdnD, C = kChunk;
   constexpr bool PF = gdn_scan_prefetch<R>();
+  // row strides of M, CQ (MS) and KD, QD, DL (CP): 16-byte rows with
+  // prefetch, where those tiles are read as float4 along the row
+  constexpr int MS = PF ? kMS4 : kMS, CP = PF ? kMS4 : kChunk + 1;
   constexpr int NB = PF ? 2 : 1;
   extern __shared__ __align__(16) float sm[];
   float *S = sm;                          // [R][D]
   float *Kb = S + R * D;                  // [NB][C][kKS]
   float *Qb = Kb + NB * C * kKS;          // [NB][C][kKS]
   float *Vb = Qb + NB * C * kKS;          // [NB][C][R]
-  float *M = Vb + NB * C * R;             // [C][kMS]
-  float *CQ = M + C * kMS;                // [C][kMS]
-  float *KD = CQ + C * kMS;               // [R][C+1]
-  float *QD = KD + R * CP;                // [R][C+1]
-  float *DL = QD + R * CP;                // [R][C+1]  deltas
+  float *M = Vb + NB * C * R;             // [C][MS]
+  float *CQ = M + C * MS;                 // [C][MS]
+  float *KD = CQ + C * MS;                // [R][CP]
+  float *QD = KD + R * CP;                // [R][CP]
+  float *DL = QD + R * CP;                // [R][CP]  deltas
   float *cumb = DL + R * CP;              // [NB][2][C]: cum, then plast
   const GdnBatchArgs &a = p.g;
   const int g = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -325,25 +349,35 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  // chunk c's M, CQ, cum and P[C-1] from the prep kernel's scratch into M,
-  // CQ and cum/plast buffer `buf`, one asynchronous-copy group (M and CQ are
-  // free once the chunk before has formed its outputs)
+  // With prefetch, chunk c's M, CQ, cum and P[C-1] arrive by three bulk
+  // copies (the scratch holds them in the tile layout) into M, CQ and
+  // cum/plast buffer `buf`, completing on sbar; M and CQ are free once the
+  // chunk before has formed its outputs.
+  __shared__ __align__(8) uint64_t sbar;
   auto issue_scr = [&](int c, int buf) {
-    const float *scr = p.scratch + (((long)b * a.heads + h) * p.nchunks + c) * kChunkScratch;
-    for (int i = tid; i < C * C; i += blockDim.x) {
-      gdn_cp_async4(M + (i / C) * kMS + i % C, scr + i);
-      gdn_cp_async4(CQ + (i / C) * kMS + i % C, scr + C * C + i);
+    if (tid == 0) {
+      const float *scr = p.scratch + (((long)b * a.heads + h) * p.nchunks + c) * kChunkScratch;
+      mbar_arrive_expect_tx(&sbar, (2 * C * MS + 2 * C) * 4);
+      fence_proxy_async_smem();
+      bulk_g2s(M, scr, C * MS * 4, &sbar);
+      bulk_g2s(CQ, scr + C * kMS4, C * MS * 4, &sbar);
+      bulk_g2s(cumb + buf * 2 * C, scr + 2 * C * kMS4, 2 * C * 4, &sbar);
     }
-    for (int t = tid; t < 2 * C; t += blockDim.x)
-      gdn_cp_async4(cumb + buf * 2 * C + t, scr + 2 * C * C + t);
-    asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  if (PF && p.nchunks > 0) {
-    issue(0, 0);
-    issue_scr(0, 0);
+  if (PF) {
+    if (tid == 0) {
+      mbar_init(&sbar, 1);
+      mbar_init_fence();
+    }
+    __syncthreads();
+    if (p.nchunks > 0) {
+      issue(0, 0);
+      issue_scr(0, 0);
+    }
   }
   const float oscale = 1.0f / sqrtf((float)D);
   bool finite = true;
+  int stalled = -1;  // with prefetch: the chunk whose copies never completed
   for (int c = 0; c < p.nchunks; ++c) {
     const int t0 = c * p.chunk;
     const int n = min(p.chunk, a.T - t0);
@@ -351,27 +385,31 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
     const float *scr = p.scratch + (((long)b * a.heads + h) * p.nchunks + c) * kChunkScratch;
     __syncthreads();
     if (PF) {
-      // the next chunk streams into the other buffer during this one
+      // the next chunk streams into the other buffer during this one; every
+      // thread waits for this chunk's copies itself
       if (c + 1 < p.nchunks) {
         issue(c + 1, buf ^ 1);
         asm volatile("cp.async.wait_group 1;" ::: "memory");
       } else {
         asm volatile("cp.async.wait_group 0;" ::: "memory");
       }
+      const bool ok = mbar_wait_bounded(&sbar, c & 1, a.status);
+      if (!__syncthreads_and(ok)) {
+        stalled = c;
+        break;
+      }
     } else {
       issue(c, 0);
       asm volatile("cp.async.wait_group 0;" ::: "memory");
+      for (int i = tid; i < C * C; i += blockDim.x) {
+        M[(i / C) * MS + i % C] = scr[(i / C) * kMS4 + i % C];
+        CQ[(i / C) * MS + i % C] = scr[C * kMS4 + (i / C) * kMS4 + i % C];
+      }
+      for (int t = tid; t < 2 * C; t += blockDim.x) cumb[t] = scr[2 * C * kMS4 + t];
+      __syncthreads();
     }
     const float *K = Kb + buf * C * kKS, *Q = Qb + buf * C * kKS, *V = Vb + buf * C * R;
     const float *cum = cumb + buf * 2 * C, *plast = cum + C;
-    if (!PF) {
-      for (int i = tid; i < C * C; i += blockDim.x) {
-        M[(i / C) * kMS + i % C] = scr[i];
-        CQ[(i / C) * kMS + i % C] = scr[C * C + i];
-      }
-      for (int t = tid; t < 2 * C; t += blockDim.x) cumb[t] = scr[2 * C * C + t];
-    }
-    __syncthreads();
     // Register tiles: warp ti = tid / 32 owns rows r = ti + 16a (a < TR), lane
     // tj = tid % 32 tokens t = tj + 32b (b < TT); every output keeps the
     // accumulation order of the one-output-per-thread form.
@@ -443,11 +481,23 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
       if (tid < 256) {
         const int g4 = 4 * (tid / 64), t = tid % 64;
         float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 8
-        for (int j = 0; j <= t; ++j) {
-          const float mv = M[t * kMS + j];
+        // four j per step (float4 along M's row and the W rows), the terms
+        // j > t masked: the warp's tokens end at (t | 31)
+        const int jend = (t | 31) + 1;
+#pragma unroll 2
+        for (int j4 = 0; j4 < jend; j4 += 4) {
+          const float4 m4 = *reinterpret_cast<const float4 *>(M + t * MS + j4);
+          float4 w4[4];
 #pragma unroll
-          for (int a4 = 0; a4 < 4; ++a4) acc[a4] = fmaf(mv, KD[(g4 + a4) * CP + j], acc[a4]);
+          for (int a4 = 0; a4 < 4; ++a4)
+            w4[a4] = *reinterpret_cast<const float4 *>(KD + (g4 + a4) * CP + j4);
+#pragma unroll
+          for (int a4 = 0; a4 < 4; ++a4) {
+            if (j4 <= t) acc[a4] = fmaf(m4.x, w4[a4].x, acc[a4]);
+            if (j4 + 1 <= t) acc[a4] = fmaf(m4.y, w4[a4].y, acc[a4]);
+            if (j4 + 2 <= t) acc[a4] = fmaf(m4.z, w4[a4].z, acc[a4]);
+            if (j4 + 3 <= t) acc[a4] = fmaf(m4.w, w4[a4].w, acc[a4]);
+          }
         }
 #pragma unroll
         for (int a4 = 0; a4 < 4; ++a4) DL[(g4 + a4) * CP + t] = t < n ? acc[a4] : 0.0f;
@@ -465,7 +515,7 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
 #pragma unroll
         for (int ai = 0; ai < TR; ++ai) wv[ai] = KD[(ti + 16 * ai) * CP + j];
 #pragma unroll
-        for (int bi = 0; bi < TT; ++bi) mv[bi] = M[(tj + 32 * bi) * kMS + j];
+        for (int bi = 0; bi < TT; ++bi) mv[bi] = M[(tj + 32 * bi) * MS + j];
 #pragma unroll
         for (int bi = 0; bi < TT; ++bi)
           if (j <= tj + 32 * bi)
@@ -489,15 +539,86 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
         float acc[4];
 #pragma unroll
         for (int a4 = 0; a4 < 4; ++a4) acc[a4] = cum[t] * QD[(g4 + a4) * CP + t];
-#pragma unroll 8
-        for (int j = 0; j <= t; ++j) {
-          const float cv = CQ[t * kMS + j];
+        const int jend = (t | 31) + 1;
+#pragma unroll 2
+        for (int j4 = 0; j4 < jend; j4 += 4) {
+          const float4 c4 = *reinterpret_cast<const float4 *>(CQ + t * MS + j4);
+          float4 d4[4];
 #pragma unroll
-          for (int a4 = 0; a4 < 4; ++a4) acc[a4] = fmaf(cv, DL[(g4 + a4) * CP + j], acc[a4]);
+          for (int a4 = 0; a4 < 4; ++a4)
+            d4[a4] = *reinterpret_cast<const float4 *>(DL + (g4 + a4) * CP + j4);
+#pragma unroll
+          for (int a4 = 0; a4 < 4; ++a4) {
+            if (j4 <= t) acc[a4] = fmaf(c4.x, d4[a4].x, acc[a4]);
+            if (j4 + 1 <= t) acc[a4] = fmaf(c4.y, d4[a4].y, acc[a4]);
+            if (j4 + 2 <= t) acc[a4] = fmaf(c4.z, d4[a4].z, acc[a4]);
+            if (j4 + 3 <= t) acc[a4] = fmaf(c4.w, d4[a4].w, acc[a4]);
+          }
         }
         float *O = KD;  // [C][R]
 #pragma unroll
         for (int a4 = 0; a4 < 4; ++a4) O[t * R + g4 + a4] = acc[a4] * oscale;
+      } else if (tid < 384) {
+        // S_r <- cum_last S_r + sum_j plast_j delta_rj k_j: thread u = tid - 256
+        // owns rows 4 (u / 32) .. + 3 of columns 4 (u % 32) .. + 3, so each K
+        // row is read by 4 warps.  It reads and writes only its own elements
+        // of S (and the O phase none), so it runs beside the O phase.
+        const int u = tid - 256, g4 = 4 * (u / 32), x4 = 4 * (u % 32);
+        const float last = cum[n - 1];
+        float acc[4][4];
+#pragma unroll
+        for (int a4 = 0; a4 < 4; ++a4) {
+          const float4 s0 = reinterpret_cast<const float4 *>(S + (g4 + a4) * D + x4)[0];
+          acc[a4][0] = last * s0.x; acc[a4][1] = last * s0.y;
+          acc[a4][2] = last * s0.z; acc[a4][3] = last * s0.w;
+        }
+        // four j per step (plast and the delta rows as float4), then the
+        // j < n left over one at a time
+        int j = 0;
+#pragma unroll 2
+        for (; j + 4 <= n; j += 4) {
+          const float4 p4 = *reinterpret_cast<const float4 *>(plast + j);
+          const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
+          float dl[4][4];
+          float4 kr[4];
+#pragma unroll
+          for (int a4 = 0; a4 < 4; ++a4) {
+            const float4 d4 = *reinterpret_cast<const float4 *>(DL + (g4 + a4) * CP + j);
+            dl[a4][0] = d4.x; dl[a4][1] = d4.y; dl[a4][2] = d4.z; dl[a4][3] = d4.w;
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            kr[e] = reinterpret_cast<const float4 *>(K + (j + e) * kKS + x4)[0];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float kx[4] = {kr[e].x, kr[e].y, kr[e].z, kr[e].w};
+#pragma unroll
+            for (int a4 = 0; a4 < 4; ++a4) {
+              const float cf = pj[e] * dl[a4][e];
+#pragma unroll
+              for (int c4 = 0; c4 < 4; ++c4) acc[a4][c4] = fmaf(cf, kx[c4], acc[a4][c4]);
+            }
+          }
+        }
+        for (; j < n; ++j) {
+          const float4 k0 = reinterpret_cast<const float4 *>(K + j * kKS + x4)[0];
+          const float kx[4] = {k0.x, k0.y, k0.z, k0.w};
+#pragma unroll
+          for (int a4 = 0; a4 < 4; ++a4) {
+            const float cf = plast[j] * DL[(g4 + a4) * CP + j];
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) acc[a4][c4] = fmaf(cf, kx[c4], acc[a4][c4]);
+          }
+        }
+#pragma unroll
+        for (int a4 = 0; a4 < 4; ++a4) {
+          float *sr = S + (g4 + a4) * D + x4;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            finite &= is_finite_f(acc[a4][c4]);
+            sr[c4] = acc[a4][c4];
+          }
+        }
       }
     } else {
       float acc[TR][TT];
@@ -513,7 +634,7 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
 #pragma unroll
         for (int ai = 0; ai < TR; ++ai) dv[ai] = DL[(ti + 16 * ai) * CP + j];
 #pragma unroll
-        for (int bi = 0; bi < TT; ++bi) cv[bi] = CQ[(tj + 32 * bi) * kMS + j];
+        for (int bi = 0; bi < TT; ++bi) cv[bi] = CQ[(tj + 32 * bi) * MS + j];
 #pragma unroll
         for (int bi = 0; bi < TT; ++bi)
           if (j <= tj + 32 * bi)
@@ -533,47 +654,10 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
       const int t = i / R, r = i % R;  // r fastest: coalesced output stores
       if (t < n) a.out[(((long)b * a.T + t0 + t) * a.heads + h) * D + r0 + r] = KD[t * R + r];
     }
-    // S_r <- cum_last S_r + sum_j plast_j delta_rj k_j; warp ti owns rows
-    // r = ti + 16a, lane tj columns x = 4 tj .. 4 tj + 3 (R == 16: thread
-    // u < 128 owns rows 4 (u / 32) .. + 3 of columns 4 (u % 32) .. + 3, so
-    // each K row is read by 4 warps)
-    if constexpr (R == 16) {
-      const float last = cum[n - 1];
-      const int g4 = 4 * (tid / 32), x4 = 4 * (tid % 32);
-      float acc[4][4];
-      if (tid < 128) {
-#pragma unroll
-        for (int a4 = 0; a4 < 4; ++a4) {
-          const float4 s0 = reinterpret_cast<const float4 *>(S + (g4 + a4) * D + x4)[0];
-          acc[a4][0] = last * s0.x; acc[a4][1] = last * s0.y;
-          acc[a4][2] = last * s0.z; acc[a4][3] = last * s0.w;
-        }
-#pragma unroll 4
-        for (int j = 0; j < n; ++j) {
-          const float pj = plast[j];
-          const float4 k0 = reinterpret_cast<const float4 *>(K + j * kKS + x4)[0];
-          const float kx[4] = {k0.x, k0.y, k0.z, k0.w};
-#pragma unroll
-          for (int a4 = 0; a4 < 4; ++a4) {
-            const float cf = pj * DL[(g4 + a4) * CP + j];
-#pragma unroll
-            for (int c4 = 0; c4 < 4; ++c4) acc[a4][c4] = fmaf(cf, kx[c4], acc[a4][c4]);
-          }
-        }
-      }
-      __syncthreads();  // every thread has read S before it is overwritten
-      if (tid < 128) {
-#pragma unroll
-        for (int a4 = 0; a4 < 4; ++a4) {
-          float *sr = S + (g4 + a4) * D + x4;
-#pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            finite &= is_finite_f(acc[a4][c4]);
-            sr[c4] = acc[a4][c4];
-          }
-        }
-      }
-    } else {
+    // S_r <- cum_last S_r + sum_j plast_j delta_rj k_j (R == 16: beside the O
+    // phase above); warp ti owns rows r = ti + 16a, lane tj columns
+    // x = 4 tj .. 4 tj + 3
+    if constexpr (R != 16) {
       const float last = cum[n - 1];
       float acc[TR][4];
 #pragma unroll
@@ -605,6 +689,15 @@ __global__ void __launch_bounds__(kScanThreads) gdn_chunk_scan_kernel(GdnPrefill
         }
       }
     }
+  }
+  if (PF && stalled >= 0) {
+    // a chunk's bulk copies never completed (reported): wait for them once
+    // more, again bounded, and for the asynchronous copies in flight, then
+    // leave the state as it was
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (tid == 0) mbar_wait_bounded(&sbar, stalled & 1, a.status);
+    __syncthreads();
+    return;
   }
   __syncthreads();
   for (int i = tid; i < R * D / 4; i += blockDim.x)

@@ -571,7 +571,7 @@ def gdn_delta_values_device(ex, op, q, k, v, gate, beta, table, out, rows=None, 
 
 
 # Size of the fixed scratch of gdn_prefill_device_noalloc (include/prism_b200.h).
-GDN_STATIC_SCRATCH_BYTES = 32 * 1024 * 1024
+GDN_STATIC_SCRATCH_BYTES = 34 * 1024 * 1024
 
 
 def gdn_prefill_device_noalloc(ex, batch, tokens, heads, key_heads, chunk, state, q, k, v, decay,

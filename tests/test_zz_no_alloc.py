@@ -17,7 +17,7 @@ import prism_b200 as pb
 pytestmark = pytest.mark.gpu
 
 D = 128
-CHUNK_SCRATCH_BYTES = (2 * 64 * 64 + 128) * 4
+CHUNK_SCRATCH_BYTES = (2 * 64 * 68 + 128) * 4   # M, CQ in 68-float rows, cum, P[C-1]
 
 
 def inputs(batch, T, heads, key_heads, seed):
@@ -72,7 +72,7 @@ def test_consecutive_calls_match_allocating_entry_point(ex):
 
 def test_largest_fitting_call_and_refusal_beyond(ex):
     units = pb.GDN_STATIC_SCRATCH_BYTES // CHUNK_SCRATCH_BYTES   # (sequence, head, chunk) units
-    assert units == 1008
+    assert units == 1009
     # exactly at the limit: one 64-token chunk for `units` heads
     heads, T = units, 64
     ins = inputs(1, T, heads, 1, 21)
@@ -107,7 +107,7 @@ def test_fresh_executor_allocates_no_device_memory(ex):
     memory unchanged, while the allocating entry point on the same executor
     then grows its scratch by at least the same chunk scratch -- the control
     showing that the measure sees an allocation of this size."""
-    heads, T = 1008, 64                      # the largest fitting call
+    heads, T = 1009, 64                      # the largest fitting call
     ins = inputs(1, T, heads, 1, 31)
     state = torch.zeros((1, heads, D, D), device="cuda")
     out = torch.zeros((1, T, heads, D), device="cuda")

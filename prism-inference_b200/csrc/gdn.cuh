@@ -332,17 +332,19 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_chunk_scan_kernel(GdnPref
   for (int i = tid; i < R * D / 4; i += blockDim.x)
     reinterpret_cast<float4 *>(S)[i] = reinterpret_cast<const float4 *>(state)[i];
   // chunk c's K and Q rows and V slice into buffer `buf` (zeros past the
-  // prompt's end), as asynchronous copies committed as one group
-  auto issue = [&](int c, int buf) {
+  // prompt's end), as asynchronous copies committed as one group by threads
+  // first, first + stride, ... (with prefetch the upper half of the CTA,
+  // which is idle while the lower one forms the state dots)
+  auto issue = [&](int c, int buf, int first, int stride) {
     const int t0 = c * p.chunk, n = min(p.chunk, a.T - t0);
     float *K = Kb + buf * C * kKS, *Q = Qb + buf * C * kKS, *V = Vb + buf * C * R;
-    for (int i = tid; i < C * D / 4; i += blockDim.x) {
+    for (int i = first; i < C * D / 4; i += stride) {
       const int t = i / (D / 4), col = i % (D / 4);
       const long off = (((long)b * a.T + t0 + min(t, n - 1)) * a.key_heads + kh) * D;
       cp_async16_zfill(K + t * kKS + 4 * col, a.k + off + 4 * col, t < n);
       cp_async16_zfill(Q + t * kKS + 4 * col, a.q + off + 4 * col, t < n);
     }
-    for (int i = tid; i < C * R / 4; i += blockDim.x) {
+    for (int i = first; i < C * R / 4; i += stride) {
       const int t = i / (R / 4), q4 = i % (R / 4);
       const long off = (((long)b * a.T + t0 + min(t, n - 1)) * a.heads + h) * D + r0;
       cp_async16_zfill(V + t * R + 4 * q4, a.v + off + 4 * q4, t < n);
@@ -371,7 +373,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_chunk_scan_kernel(GdnPref
     }
     __syncthreads();
     if (p.nchunks > 0) {
-      issue(0, 0);
+      if (tid >= kScanThreads / 2) issue(0, 0, tid - kScanThreads / 2, kScanThreads / 2);
       issue_scr(0, 0);
     }
   }
@@ -385,21 +387,16 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_chunk_scan_kernel(GdnPref
     const float *scr = p.scratch + (((long)b * a.heads + h) * p.nchunks + c) * kChunkScratch;
     __syncthreads();
     if (PF) {
-      // the next chunk streams into the other buffer during this one; every
-      // thread waits for this chunk's copies itself
-      if (c + 1 < p.nchunks) {
-        issue(c + 1, buf ^ 1);
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-      } else {
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
-      }
+      // this chunk's K, Q, V (copied by the upper half during the chunk
+      // before) and M, CQ, cum, P[C-1] (bulk copies)
+      if (tid >= kScanThreads / 2) asm volatile("cp.async.wait_group 0;" ::: "memory");
       const bool ok = mbar_wait_bounded(&sbar, c & 1, a.status);
       if (!__syncthreads_and(ok)) {
         stalled = c;
         break;
       }
     } else {
-      issue(c, 0);
+      issue(c, 0, tid, blockDim.x);
       asm volatile("cp.async.wait_group 0;" ::: "memory");
       for (int i = tid; i < C * C; i += blockDim.x) {
         M[(i / C) * MS + i % C] = scr[(i / C) * kMS4 + i % C];
@@ -416,29 +413,34 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_chunk_scan_kernel(GdnPref
     constexpr int TR = R / 16, TT = C / 32;
     const int ti = tid / 32, tj = tid % 32;
     // KD[r][t] = S_r . k_t, QD[r][t] = S_r . q_t
-    // R == 16: thread u < 256 owns rows 4g..4g+3 (g = u / 64) of token u % 64
-    // in the three tile phases, so that each K/Q/M/CQ row is read by 4 warps
+    // R == 16: thread u < 128 owns rows 8g..8g+7 (g = u / 64) of token u % 64
+    // (each K/Q row read by 2 warps, each S row load shared by K and Q),
+    // while the upper half of the CTA issues the next chunk's copies
     if constexpr (R == 16) {
-      if (tid < 256) {
-        const int g4 = 4 * (tid / 64), t = tid % 64;
-        float dk[4] = {0.0f, 0.0f, 0.0f, 0.0f}, dq[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (tid < 128) {
+        const int g8 = 8 * (tid / 64), t = tid % 64;
+        float dk[8], dq[8];
+#pragma unroll
+        for (int a8 = 0; a8 < 8; ++a8) dk[a8] = dq[a8] = 0.0f;
 #pragma unroll 2
         for (int x = 0; x < D / 4; ++x) {
           const float4 u = reinterpret_cast<const float4 *>(K + t * kKS)[x];
           const float4 w = reinterpret_cast<const float4 *>(Q + t * kKS)[x];
 #pragma unroll
-          for (int a4 = 0; a4 < 4; ++a4) {
-            const float4 sr = reinterpret_cast<const float4 *>(S + (g4 + a4) * D)[x];
-            dk[a4] = fmaf(sr.x, u.x, fmaf(sr.y, u.y, fmaf(sr.z, u.z, fmaf(sr.w, u.w, dk[a4]))));
-            dq[a4] = fmaf(sr.x, w.x, fmaf(sr.y, w.y, fmaf(sr.z, w.z, fmaf(sr.w, w.w, dq[a4]))));
+          for (int a8 = 0; a8 < 8; ++a8) {
+            const float4 sr = reinterpret_cast<const float4 *>(S + (g8 + a8) * D)[x];
+            dk[a8] = fmaf(sr.x, u.x, fmaf(sr.y, u.y, fmaf(sr.z, u.z, fmaf(sr.w, u.w, dk[a8]))));
+            dq[a8] = fmaf(sr.x, w.x, fmaf(sr.y, w.y, fmaf(sr.z, w.z, fmaf(sr.w, w.w, dq[a8]))));
           }
         }
 #pragma unroll
-        for (int a4 = 0; a4 < 4; ++a4) {
-          const int r = g4 + a4;
-          KD[r * CP + t] = V[t * R + r] - cum[t] * dk[a4];
-          QD[r * CP + t] = dq[a4];
+        for (int a8 = 0; a8 < 8; ++a8) {
+          const int r = g8 + a8;
+          KD[r * CP + t] = V[t * R + r] - cum[t] * dk[a8];
+          QD[r * CP + t] = dq[a8];
         }
+      } else if (tid >= kScanThreads / 2 && c + 1 < p.nchunks) {
+        issue(c + 1, buf ^ 1, tid - kScanThreads / 2, kScanThreads / 2);
       }
     } else {
       float dk[TR][TT], dq[TR][TT];

@@ -258,6 +258,31 @@ def phase_trace_report(model, cfg, steps=3, out=sys.stderr):
         cols = " ".join("%8.2f" % x for x in r[1:]) if len(r) > 1 else ""
         print("%-11s %3d %8.2f | %s" % (nm, len(rows), r[0], cols), file=out)
     print("critical path sum %.1f us" % total, file=out)
+    # every CTA's stamps after the previous phase's last CTA: median / max of
+    # inputs arrived, staged (RMSNorm + Q8_K done), end; and the staged time
+    # of the CTA that ends last
+    dist = {}
+    for i, nm in enumerate(names[1:], 1):
+        if nm in ("gdn_rec", "attention"):
+            continue
+        prev = ce[i - 1].max()
+        valid = ca[i] > 0
+        if not valid.any():
+            continue
+        cp_ = cc[i, :, 3]
+        a_, s_, e_, p_ = (ca[i][valid] - prev, cs[i][valid] - prev, ce[i][valid] - prev,
+                          cp_[valid] - prev)
+        last = np.argmax(e_)
+        dist.setdefault(nm, []).append([np.median(a_), a_.max(), np.median(s_), s_.max(),
+                                        np.median(e_), e_.max(), s_[last], a_[last],
+                                        np.median(p_), p_[last]])
+    print("%-11s | %8s %8s | %8s %8s | %8s %8s | %9s %9s | %8s %9s" % (
+        "per CTA", "arr_med", "arr_max", "stg_med", "stg_max", "end_med", "end_max",
+        "last_stg", "last_arr", "pln_med", "last_pln"), file=out)
+    for nm, rows in dist.items():
+        r = np.mean(np.array(rows), axis=0) / 1e3
+        print("%-11s | %8.2f %8.2f | %8.2f %8.2f | %8.2f %8.2f | %9.2f %9.2f | %8.2f %9.2f"
+              % ((nm,) + tuple(r)), file=out)
     att = [i for i, nm in enumerate(names) if nm == "attention"]
     if att:
         keys = [(1, "inputs"), (2, "norm+rope"), (3, "K pass"), (4, "scores in"), (10, "max"),

@@ -377,6 +377,22 @@ int prism_b200_gdn_prefill_device(prism_b200_executor *ex, int batch, int tokens
                                   const float *k, const float *v, const float *decay,
                                   const float *beta, float *out, void *stream);
 
+/* The reference's pinned ("Swift") GDN recurrence over device buffers in the
+ * layout above (replaces src/kernels/pinned_gdn.rs:370-455 step_row_in_place
+ * / step_row_tokens_from over a head, :853-973 step_head_tokens_in_place):
+ * every state row stepped token by token -- row *= decay, dot_k = the pinned
+ * 16-lane fused dot with the key (registers 0+2 and 1+3, then adjacent lane
+ * pairs), delta = (v - dot_k) * beta, row += delta * key fused, out = the
+ * pinned dot with the query * (1/sqrt(d)) -- bit for bit the reference's
+ * scalar contract (which its NEON paths match).  d = 128.  A nonfinite dot
+ * or state element reports PRISM_B200_E_NONFINITE at the next synchronising
+ * call, where the reference returns its error. */
+int prism_b200_gdn_prefill_pinned_device(prism_b200_executor *ex, int batch, int tokens,
+                                         int heads, int key_heads, int d, float *state,
+                                         const float *q, const float *k, const float *v,
+                                         const float *decay, const float *beta, float *out,
+                                         void *stream);
+
 /* Same computation and arguments as prism_b200_gdn_prefill_device, but it
  * never allocates device memory.  This entry point has no counterpart in
  * the reference.  It is for hosts that cannot let a library allocate:

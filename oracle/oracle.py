@@ -438,6 +438,7 @@ def _model_lib():
             ("po_qwen35_set_position", i32, [vp, ctypes.c_int32]),
             ("po_pinned_gdn_dot", ctypes.c_float, [vp, vp, ctypes.c_size_t]),
             ("po_pinned_gdn_add_scaled", i32, [vp, vp, ctypes.c_float, ctypes.c_size_t]),
+            ("po_pinned_gdn_prefill", i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
             ("po_pinned_attention_dot", i32, [vp, vp, ctypes.c_size_t, vp]),
             ("po_vector_exp", ctypes.c_float, [ctypes.c_float]),
             ("po_pinned_softmax", i32, [vp, ctypes.c_size_t, i32]),
@@ -585,6 +586,20 @@ def pinned_gdn_add_scaled(target, inp, scale):
     t, x = _f32(target).copy(), _f32(inp)
     _check(_model_lib().po_pinned_gdn_add_scaled(_p(t), _p(x), float(scale), t.size))
     return t
+
+
+def pinned_gdn_prefill(state, q, k, v, decay, beta):
+    """The pinned (Swift) GDN recurrence over every head and token in the
+    device layout: state [B][H][d][d], q, k [B][T][KH][d], v [B][T][H][d],
+    decay, beta [B][T][H]; returns (status, new state, out [B][T][H][d])."""
+    st = np.array(state, np.float32, copy=True)
+    B, H, d = st.shape[0], st.shape[1], st.shape[2]
+    T, KH = q.shape[1], q.shape[2]
+    out = np.zeros((B, T, H, d), np.float32)
+    arrs = [np.ascontiguousarray(x, np.float32) for x in (q, k, v, decay, beta)]
+    rc = _model_lib().po_pinned_gdn_prefill(_p(st), *[_p(x) for x in arrs], B, T, H, KH, d,
+                                            _p(out))
+    return rc, st, out
 
 
 def pinned_attention_dot(values, weights):

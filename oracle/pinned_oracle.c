@@ -192,3 +192,58 @@ int po_source_rope(float *x, size_t n, int head, int rotary, const float *cos_si
     if (!isfinite(x[i])) return PO_E_NONFINITE;
   return PO_OK;
 }
+
+/* One GDN state row over one token in the pinned arithmetic (reference
+ * src/kernels/pinned_gdn.rs:370-398 step_row_in_place: decay_and_dot
+ * :236-258, the unfused delta, update_and_dot :310-336): the row scaled by
+ * decay (separate multiplies), dot_k = the pinned dot with the key,
+ * delta = (value - dot_k) * beta, the row += delta * key (fused over the
+ * 16-aligned prefix), then the pinned dot with the query.  Returns
+ * PO_E_NONFINITE where the reference returns its nonfinite error. */
+static int pinned_step_row(float *row, const float *key, const float *query, float decay,
+                           float value, float beta, size_t n, float *out) {
+  for (size_t i = 0; i < n; ++i) row[i] *= decay;
+  const float dot_k = po_pinned_gdn_dot(row, key, n);
+  if (!isfinite(dot_k)) return PO_E_NONFINITE;
+  const float delta = (value - dot_k) * beta;
+  if (po_pinned_gdn_add_scaled(row, key, delta, n)) return PO_E_NONFINITE;
+  const float dot_q = po_pinned_gdn_dot(row, query, n);
+  if (!isfinite(dot_q)) return PO_E_NONFINITE;
+  *out = dot_q;
+  return PO_OK;
+}
+
+/* Every head of every sequence over `tokens` tokens in the pinned
+ * arithmetic, in the device GDN layout: q, k [batch][tokens][key_heads][d],
+ * v, out [batch][tokens][heads][d], decay, beta [batch][tokens][heads],
+ * state [batch][heads][d rows][d]; head h reads key head h % key_heads;
+ * out = dot_q * scale with scale = 1 / sqrt(d) (the reference's
+ * step_row_tokens_from, :401-455, rows of a head in any order: each row is
+ * independent).  The state of a row that fails is left partially updated, as
+ * the reference's error leaves it. */
+int po_pinned_gdn_prefill(float *state, const float *q, const float *k, const float *v,
+                          const float *decay, const float *beta, int batch, int tokens, int heads,
+                          int key_heads, int d, float *out) {
+  if (batch <= 0 || tokens <= 0 || heads <= 0 || key_heads <= 0 || heads % key_heads || d <= 0)
+    return PO_E_INVALID;
+  const float scale = 1.0f / sqrtf((float)d);
+  int status = PO_OK;
+  for (int b = 0; b < batch; ++b)
+    for (int h = 0; h < heads; ++h) {
+      float *S = state + ((size_t)b * heads + h) * (size_t)d * d;
+      const int kh = h % key_heads;
+      for (int t = 0; t < tokens; ++t) {
+        const size_t tok = (size_t)b * tokens + t;
+        const float *kk = k + (tok * key_heads + kh) * d, *qq = q + (tok * key_heads + kh) * d;
+        const float *vv = v + (tok * heads + h) * d;
+        const float g = decay[tok * heads + h], bt = beta[tok * heads + h];
+        for (int r = 0; r < d; ++r) {
+          float o = 0.0f;
+          const int st = pinned_step_row(S + (size_t)r * d, kk, qq, g, vv[r], bt, (size_t)d, &o);
+          if (st && !status) status = st;
+          out[(tok * heads + h) * d + r] = o * scale;
+        }
+      }
+    }
+  return status;
+}

@@ -52,6 +52,9 @@ typedef struct po_q8_0_block {
  * vector exponential, softmax and RoPE, for checking its native captures. */
 float po_pinned_gdn_dot(const float *a, const float *b, size_t n);
 int po_pinned_gdn_add_scaled(float *target, const float *input, float scale, size_t n);
+int po_pinned_gdn_prefill(float *state, const float *q, const float *k, const float *v,
+                          const float *decay, const float *beta, int batch, int tokens, int heads,
+                          int key_heads, int d, float *out);
 int po_pinned_attention_dot(const float *values, const float *weights, size_t n, float *out);
 float po_vector_exp(float value);
 int po_pinned_softmax(float *scores, size_t n, int round_f16);

@@ -16,6 +16,7 @@
 #include "executor.cuh"
 #include "gdn.cuh"
 #include "gdn_op.cuh"
+#include "gdn_pinned.cuh"
 #include "gemm.cuh"
 #include "packed.cuh"
 #include "kquant.cuh"
@@ -793,6 +794,37 @@ extern "C" int prism_b200_gdn_prefill_device(prism_b200_executor *ex, int batch,
     cfg = pdl_config(dim3(kGdnD / 16, heads, batch), dim3(kScanThreads), smem, s, attr, ex->pdl);
     CK(cudaLaunchKernelEx(&cfg, gdn_chunk_scan_kernel<16>, p), "GDN scan launch");
   }
+  return PRISM_B200_OK;
+}
+
+extern "C" int prism_b200_gdn_prefill_pinned_device(prism_b200_executor *ex, int batch,
+                                                    int tokens, int heads, int key_heads, int d,
+                                                    float *state, const float *q, const float *k,
+                                                    const float *v, const float *decay,
+                                                    const float *beta, float *out, void *stream) {
+  int st = check_open(ex);
+  if (st) return st;
+  const void *ptrs[] = {state, q, k, v, out};
+  if ((st = gdn_check(ex, batch, tokens, heads, key_heads, d, ptrs, 5))) return st;
+  if (!decay || !beta) return ex->fail(PRISM_B200_E_INVALID, "null gate buffer");
+  cudaSetDevice(ex->device);
+  GdnBatchArgs a;
+  a.batch = batch;
+  a.T = tokens;
+  a.heads = heads;
+  a.key_heads = key_heads;
+  a.state = state;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.decay = decay;
+  a.beta = beta;
+  a.out = out;
+  a.status = ex->d_status;
+  cudaStream_t s = pick(ex, stream);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_config(dim3(heads, batch), dim3(kPinnedD), 0, s, attr, ex->pdl);
+  CK(cudaLaunchKernelEx(&cfg, gdn_pinned_kernel, a), "pinned GDN launch");
   return PRISM_B200_OK;
 }
 

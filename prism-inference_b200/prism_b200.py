@@ -520,6 +520,8 @@ def _declare_gdn(L):
     L.prism_b200_gdn_prefill_device.argtypes = [vp, i32, i32, i32, i32, i32, i32] + [vp] * 8
     L.prism_b200_gdn_prefill_device_noalloc.restype = i32
     L.prism_b200_gdn_prefill_device_noalloc.argtypes = [vp, i32, i32, i32, i32, i32, i32] + [vp] * 8
+    L.prism_b200_gdn_prefill_pinned_device.restype = i32
+    L.prism_b200_gdn_prefill_pinned_device.argtypes = [vp, i32, i32, i32, i32, i32] + [vp] * 8
     L._gdn_declared = True
 
 
@@ -539,6 +541,16 @@ def gdn_prefill_device(ex, batch, tokens, heads, key_heads, chunk, state, q, k, 
     _declare_gdn(L)
     ex._check(L.prism_b200_gdn_prefill_device(ex.h, batch, tokens, heads, key_heads, d, chunk,
                                               state, q, k, v, decay, beta, out, stream))
+
+
+def gdn_prefill_pinned_device(ex, batch, tokens, heads, key_heads, state, q, k, v, decay, beta,
+                              out, stream=None, d=128):
+    """The reference's pinned (Swift) GDN recurrence over device buffers,
+    token by token (prism_b200_gdn_prefill_pinned_device)."""
+    L = load()
+    _declare_gdn(L)
+    ex._check(L.prism_b200_gdn_prefill_pinned_device(ex.h, batch, tokens, heads, key_heads, d,
+                                                     state, q, k, v, decay, beta, out, stream))
 
 
 class GdnOp(ctypes.Structure):

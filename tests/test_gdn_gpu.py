@@ -99,3 +99,29 @@ def test_config2_prefill_4096_tokens(ex, oracle):
                                          decay[0, :, h], beta[0, :, h])
         assert np.all(np.abs(Og[0, :, h] - oe) <= 1e-3 + 1e-3 * np.abs(oe)), h
         assert np.all(np.abs(Sg[0, h] - se) <= 1e-3 + 1e-3 * np.abs(se)), h
+
+
+def test_prefill_is_batch_invariant(ex):
+    """A sequence prefilled alone (16 state rows per CTA, with prefetch) and
+    as row 5 of a batch of 16 (64 state rows per CTA) gives the same bits:
+    both tilings keep every output's accumulation order, and the prep
+    kernel is shared.  The nonzero starting state and a ragged last chunk
+    cover the state update and the zero-filled rows."""
+    T, heads, d = 1000, 16, 128
+    q, k, v, decay, beta = inputs(16, T, heads, heads, seed=77)
+    rng = np.random.default_rng(78)
+    state = (rng.standard_normal((16, heads, d, d)) * 0.1).astype(np.float32)
+    outs = {}
+    for batch in (1, 16):
+        sl = slice(5, 6) if batch == 1 else slice(0, 16)
+        S, Q, K, V, G, B = map(dev, (state[sl], q[sl], k[sl], v[sl], decay[sl], beta[sl]))
+        O = torch.zeros((batch, T, heads, d), device="cuda")
+        pb.gdn_prefill_device(ex, batch, T, heads, heads, 64, S.data_ptr(), Q.data_ptr(),
+                              K.data_ptr(), V.data_ptr(), G.data_ptr(), B.data_ptr(),
+                              O.data_ptr())
+        torch.cuda.synchronize()
+        ex.sync()
+        i = 0 if batch == 1 else 5
+        outs[batch] = (S.cpu().numpy()[i], O.cpu().numpy()[i])
+    for a, b in zip(outs[1], outs[16]):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))

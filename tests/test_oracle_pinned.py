@@ -157,3 +157,63 @@ def test_rope_out_of_place_and_in_place(cap):
     assert b32(op[[bd["pair"], bd["pair"] + 32]]) == [bd["out_of_place_0"], bd["out_of_place_1"]]
     halves = ip[[bd["pair"], bd["pair"] + 32]].astype(np.float16).view(np.uint16).astype(np.uint32)
     assert int(halves[0] | (halves[1] << 16)) == bd["half_words"]
+
+
+def capture_head(r, rows=128, seed=0):
+    """A one-token head holding a native capture row as state row 0 (the
+    other rows random), with decay = beta = 1: the pinned step of that row
+    is then exactly the capture's recipe."""
+    rng = np.random.default_rng(seed)
+    d = len(r["q"])
+    state = (rng.standard_normal((1, 1, rows, d)) * 0.05).astype(np.float32)
+    state[0, 0, 0] = f32(r["state"])
+    q = f32(r["q"]).reshape(1, 1, 1, d)
+    k = f32(r["k"]).reshape(1, 1, 1, d)
+    v = rng.standard_normal((1, 1, 1, rows)).astype(np.float32)
+    v[0, 0, 0, 0] = f32([r["v"]])[0]
+    one = np.ones((1, 1, 1), np.float32)
+    return state, q, k, v, one, one
+
+
+def test_pinned_head_step_reproduces_the_native_rows(cap):
+    """The pinned GDN recurrence over a head (the reference's
+    step_row_in_place per row and token, src/kernels/pinned_gdn.rs:370-455)
+    gives the native capture's updated state row and output bit for bit."""
+    from oracle import oracle
+    for i, r in enumerate(cap["gdn"]["rows"]):
+        state, q, k, v, g, b = capture_head(r, seed=i)
+        rc, new, out = oracle.pinned_gdn_prefill(state, q, k, v, g, b)
+        assert rc == 0
+        assert b32(new[0, 0, 0]) == r["native_state"]
+        assert b32(out[0, 0, 0, 0]) == [r["native_out"]]
+
+
+def test_pinned_head_step_tokens_and_rows():
+    """Over several tokens the pinned recurrence of a row equals the row
+    stepped alone token by token, with the decay and beta applied as the
+    reference's step_row_in_place does (unfused multiplies around the
+    pinned dots); heads share key heads by h % key_heads."""
+    from oracle import oracle
+    rng = np.random.default_rng(3)
+    B, T, H, KH, d = 2, 5, 4, 2, 128
+    q = rng.standard_normal((B, T, KH, d)).astype(np.float32)
+    k = rng.standard_normal((B, T, KH, d)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=-1, keepdims=True)
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = rng.standard_normal((B, T, H, d)).astype(np.float32)
+    g = rng.uniform(0.5, 1.0, (B, T, H)).astype(np.float32)
+    bt = rng.uniform(0.1, 0.9, (B, T, H)).astype(np.float32)
+    s0 = (rng.standard_normal((B, H, d, d)) * 0.1).astype(np.float32)
+    rc, s, o = oracle.pinned_gdn_prefill(s0, q, k, v, g, bt)
+    assert rc == 0
+    scale = np.float32(1.0) / np.sqrt(np.float32(d))
+    for b, h, r in [(0, 0, 0), (1, 3, 77), (1, 2, 127)]:
+        row = s0[b, h, r].copy()
+        for t in range(T):
+            kk, qq = k[b, t, h % KH], q[b, t, h % KH]
+            row = (row * g[b, t, h]).astype(np.float32)
+            dk = oracle.pinned_gdn_dot(row, kk)
+            delta = np.float32(np.float32(v[b, t, h, r] - dk) * bt[b, t, h])
+            row = oracle.pinned_gdn_add_scaled(row, kk, delta)
+            assert b32(o[b, t, h, r]) == b32(np.float32(oracle.pinned_gdn_dot(row, qq) * scale))
+        assert b32(s[b, h, r]) == b32(row)

@@ -276,6 +276,19 @@ def phase_trace_report(model, cfg, steps=3, out=sys.stderr):
         dist.setdefault(nm, []).append([np.median(a_), a_.max(), np.median(s_), s_.max(),
                                         np.median(e_), e_.max(), s_[last], a_[last],
                                         np.median(p_), p_[last]])
+    # CTA 0's stage split (staged input phases): sum of squares, scale,
+    # warp 0's quantization, closing barrier
+    split = {}
+    for i, nm in enumerate(names[1:], 1):
+        c0 = t[i]
+        if nm in ("gdn_rec", "attention") or not (c0[13] and c0[14] and c0[15]):
+            continue
+        split.setdefault(nm, []).append([c0[13] - c0[0], c0[14] - c0[13], c0[15] - c0[14],
+                                         c0[1] - c0[15]])
+    for nm, rows in split.items():
+        r = np.mean(np.array(rows), axis=0) / 1e3
+        print("%-11s stage split (CTA 0, us from phase start): inputs+sumsq %.2f, scale %.2f, "
+              "quantize(w0) %.2f, barrier %.2f" % ((nm,) + tuple(r)), file=out)
     print("%-11s | %8s %8s | %8s %8s | %8s %8s | %9s %9s | %8s %9s" % (
         "per CTA", "arr_med", "arr_max", "stg_med", "stg_max", "end_med", "end_max",
         "last_stg", "last_arr", "pln_med", "last_pln"), file=out)

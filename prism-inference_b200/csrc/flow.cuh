@@ -839,11 +839,14 @@ __device__ bool flow_proj(const FProj &p, const FRing &rg, uint8_t *smem, uint32
     if (rms) {
       // block_sumsq_f64: per-thread sums, warp butterfly, warps in order
       const double sum = fsum_f64(s, red);
+      if (tr) tr[13] = global_timer_ns();
       const float mean = (float)(sum / (double)n);
       scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
       if ((!is_finite_f(scale) || !(scale > 0.0f)) && tid == 0) report(c.status, kStatusNonfinite);
     }
+    if (tr) tr[14] = global_timer_ns();
     quantize_staged(xs, nb, scale, p.norm_w, rms, act, c.status, nw0, nw1);
+    if (tr) tr[15] = global_timer_ns();
   }
   csync();
   if (tr) tr[1] = global_timer_ns();

@@ -1049,11 +1049,13 @@ __device__ bool flow_gdn(const FGdn &a, int pos, uint8_t *smem, uint32_t ep, uin
   {
     const float xq = tid < S ? q[tid] : 0.0f;
     const float xk = tid < S ? k[tid] : 0.0f;
-    const double sq = fsum_f64(tid < S ? (double)__fmul_rn(xq, xq) : 0.0, red);
-    const double sk = fsum_f64(tid < S ? (double)__fmul_rn(xk, xk) : 0.0, red);
+    // both sums in fsum_f64's order, sharing their barriers
+    double sq = tid < S ? (double)__fmul_rn(xq, xq) : 0.0;
+    double sk = tid < S ? (double)__fmul_rn(xk, xk) : 0.0;
+    fsum2_f64(sq, sk, red);
     const float scq = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sq), a.eps));
     const float sck = __fdiv_rn(1.0f, fmaxf(__fsqrt_rn((float)sk), a.eps));
-    csync();
+    // each thread rewrites only the q[tid], k[tid] it read itself
     if (tid < S) {
       q[tid] = __fmul_rn(xq, scq);
       k[tid] = __fmul_rn(xk, sck);

@@ -1,8 +1,8 @@
 """GDN prefill through the no-allocation entry point.
 
 prism_b200_gdn_prefill_device_noalloc must give what
-prism_b200_gdn_prefill_device gives on the same inputs (within the chunkwise
-bound 1e-3 + 1e-3*|ref| used for the prefill tests), on consecutive calls
+prism_b200_gdn_prefill_device gives on the same inputs, bit for bit (the same
+kernels run over the same scratch layout), on consecutive calls
 that reuse its fixed scratch, must refuse a call whose scratch would not fit
 before anything is enqueued, and must leave a fresh executor's device free
 memory unchanged.  The file name sorts last so that the test
@@ -32,8 +32,8 @@ def inputs(batch, T, heads, key_heads, seed):
     return [torch.from_numpy(a).cuda() for a in (q, k, v, decay, beta)]
 
 
-def close(got, ref):
-    return bool(torch.all((got - ref).abs() <= 1e-3 + 1e-3 * ref.abs()))
+def same(got, ref):
+    return torch.equal(got.view(torch.int32), ref.view(torch.int32))
 
 
 @pytest.fixture(scope="module")
@@ -66,8 +66,8 @@ def test_consecutive_calls_match_allocating_entry_point(ex):
         o_fix = run(ex, pb.gdn_prefill_device_noalloc, batch, T, heads, key_heads, chunk, s_fix,
                     ins)
         assert torch.isfinite(o_fix).all()
-        assert close(o_fix, o_ref), (T, chunk)
-        assert close(s_fix, s_ref), (T, chunk)
+        assert same(o_fix, o_ref), (T, chunk)
+        assert same(s_fix, s_ref), (T, chunk)
 
 
 def test_largest_fitting_call_and_refusal_beyond(ex):
@@ -80,7 +80,7 @@ def test_largest_fitting_call_and_refusal_beyond(ex):
     s_fix = s_ref.clone()
     o_ref = run(ex, pb.gdn_prefill_device, 1, T, heads, 1, 64, s_ref, ins)
     o_fix = run(ex, pb.gdn_prefill_device_noalloc, 1, T, heads, 1, 64, s_fix, ins)
-    assert close(o_fix, o_ref) and close(s_fix, s_ref)
+    assert same(o_fix, o_ref) and same(s_fix, s_ref)
     del ins, s_ref, o_ref
     # one head more does not fit: refused on the host, nothing enqueued, the
     # buffers are sized for the call all the same
@@ -99,7 +99,7 @@ def test_largest_fitting_call_and_refusal_beyond(ex):
     s_fix = s_ref.clone()
     o_ref = run(ex, pb.gdn_prefill_device, 2, 100, 4, 4, 64, s_ref, ins)
     o_fix = run(ex, pb.gdn_prefill_device_noalloc, 2, 100, 4, 4, 64, s_fix, ins)
-    assert close(o_fix, o_ref) and close(s_fix, s_ref)
+    assert same(o_fix, o_ref) and same(s_fix, s_ref)
 
 
 def test_fresh_executor_allocates_no_device_memory(ex):

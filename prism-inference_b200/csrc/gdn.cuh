@@ -134,6 +134,18 @@ struct GdnPrefillArgs {
 
 constexpr int kPrepThreads = 256;
 
+__device__ __forceinline__ void gdn_cp_async4(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+
+
 // grid (nchunks, heads, batch)
 __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefillArgs p) {
   constexpr int D = kGdnD, C = kChunk;
@@ -152,22 +164,21 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefill
   const int n = min(p.chunk, a.T - t0);
   grid_dependency_wait();
   grid_dependents_launch();
+  // the chunk's K and Q rows (zeros past the prompt's end) as asynchronous
+  // copies, all in flight at once
   for (int i = threadIdx.x; i < C * D / 4; i += blockDim.x) {
     const int t = i / (D / 4), col = i % (D / 4);
-    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
-    if (t < n) {
-      const long off = (((long)b * a.T + t0 + t) * a.key_heads + kh) * D;
-      kv = reinterpret_cast<const float4 *>(a.k + off)[col];
-      qv = reinterpret_cast<const float4 *>(a.q + off)[col];
-    }
-    reinterpret_cast<float4 *>(K + t * kKS)[col] = kv;
-    reinterpret_cast<float4 *>(Q + t * kKS)[col] = qv;
+    const long off = (((long)b * a.T + t0 + min(t, n - 1)) * a.key_heads + kh) * D;
+    cp_async16_zfill(K + t * kKS + 4 * col, a.k + off + 4 * col, t < n);
+    cp_async16_zfill(Q + t * kKS + 4 * col, a.q + off + 4 * col, t < n);
   }
+  asm volatile("cp.async.commit_group;" ::: "memory");
   for (int t = threadIdx.x; t < C; t += blockDim.x) {
     const long off = ((long)b * a.T + t0 + t) * a.heads + h;
     dec[t] = t < n ? a.decay[off] : 1.0f;
     bet[t] = t < n ? a.beta[off] : 0.0f;
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   if (threadIdx.x == 0) {
     float d = 1.0f;
@@ -289,17 +300,6 @@ __host__ __device__ constexpr size_t gdn_scan_smem() {
                   2 * kChunk * ms + 3 * R * ms +
                   (gdn_scan_prefetch<R>() ? 2 : 1) * 2 * kChunk) *
          4;
-}
-
-__device__ __forceinline__ void gdn_cp_async4(void *dst, const void *src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src)
-               : "memory");
-}
-
-__device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
-               "r"(valid ? 16 : 0)
-               : "memory");
 }
 
 template <int R>

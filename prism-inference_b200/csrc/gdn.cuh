@@ -134,11 +134,6 @@ struct GdnPrefillArgs {
 
 constexpr int kPrepThreads = 256;
 
-__device__ __forceinline__ void gdn_cp_async4(void *dst, const void *src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src)
-               : "memory");
-}
-
 __device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
                "r"(valid ? 16 : 0)
@@ -280,10 +275,13 @@ __host__ __device__ constexpr size_t gdn_prep_smem() {
 }
 
 // Scan over the chunks of one (sequence, head) for R state rows.
-// grid (128/R, heads, batch), kScanThreads threads: warp w owns state rows
-// w + 16a (a < R/16) and lane l tokens l + 32b (b < 2) of every chunk tile.
-// With R == 16 (the small-batch grid) the next chunk's K, Q and V arrive by
-// asynchronous copies into a second buffer while the current one computes.
+// grid (128/R, heads, batch), kScanThreads threads.  R == 64 (the wide
+// grid): warp w owns state rows w + 16a (a < 4) and lane l tokens l + 32b
+// (b < 2) of every chunk tile.  R == 16 (the small-batch grid): the lower
+// threads form the tiles (thread mappings at each phase) while the upper
+// half issues the next chunk's K, Q and V asynchronous copies into a second
+// buffer; the next chunk's M, CQ, cum and P[C-1] arrive by bulk copies on an
+// mbarrier once the current chunk's outputs are formed.
 constexpr int kScanThreads = 512;
 
 template <int R>

@@ -184,9 +184,12 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefill
   }
   // P[t][j] = P[t][j+1] * decay_{j+1}, P[t][t] = 1 (reference order)
   for (int t = threadIdx.x; t < C; t += blockDim.x) {
-    P[t * (C + 1) + t] = 1.0f;
-    for (int j = t - 1; j >= 0; --j)
-      P[t * (C + 1) + j] = __fmul_rn(P[t * (C + 1) + j + 1], dec[j + 1]);
+    float pr = 1.0f;  // the chain in a register, each product stored once
+    P[t * (C + 1) + t] = pr;
+    for (int j = t - 1; j >= 0; --j) {
+      pr = __fmul_rn(pr, dec[j + 1]);
+      P[t * (C + 1) + j] = pr;
+    }
     for (int j = t + 1; j < C; ++j) P[t * (C + 1) + j] = 0.0f;
   }
   __syncthreads();

@@ -104,3 +104,53 @@ def test_nonfinite_is_reported(ex):
     v[0, 1, 0, 9] = 0.5
     s, o = run(ex, state, q, k, v, one, one)
     assert np.isfinite(s).all() and np.isfinite(o).all()
+
+
+def test_long_sequence_matches_the_oracle(ex, oracle):
+    """512 tokens, a ragged head count and shared key heads: the recurrence
+    stays bit-identical over a long chain."""
+    rng = np.random.default_rng(512)
+    B, T, H, KH = 1, 512, 6, 3
+    q = rng.standard_normal((B, T, KH, 128)).astype(np.float32)
+    k = rng.standard_normal((B, T, KH, 128)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=-1, keepdims=True)
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = rng.standard_normal((B, T, H, 128)).astype(np.float32)
+    g = np.exp(-np.log1p(np.exp(rng.standard_normal((B, T, H))))).astype(np.float32)
+    bt = (1.0 / (1.0 + np.exp(-rng.standard_normal((B, T, H))))).astype(np.float32)
+    s0 = np.zeros((B, H, 128, 128), np.float32)
+    rc, se, oe = oracle.pinned_gdn_prefill(s0, q, k, v, g, bt)
+    assert rc == 0
+    s, o = run(ex, s0, q, k, v, g, bt)
+    assert np.array_equal(s.view(np.uint32), se.view(np.uint32))
+    assert np.array_equal(o.view(np.uint32), oe.view(np.uint32))
+
+
+def test_refusals_leave_the_buffers_alone(ex):
+    """Geometry the reference's pinned step rejects (no tokens, heads not a
+    multiple of the key heads), a width other than 128, a misaligned buffer
+    and missing gates are refused on the host before anything is enqueued."""
+    B, T, H, KH = 1, 2, 2, 1
+    S = torch.ones((B, H, 128, 128), device="cuda")
+    Q = torch.zeros((B, T, KH, 128), device="cuda")
+    V = torch.zeros((B, T, H, 128), device="cuda")
+    G = torch.ones((B, T, H), device="cuda")
+    O = torch.full((B, T, H, 128), 7.0, device="cuda")
+    p = lambda t: t.data_ptr()
+    cases = [
+        dict(tokens=0), dict(heads=3, key_heads=2), dict(d=64),
+        dict(state=p(S) + 4), dict(decay=0), dict(beta=0),
+    ]
+    for case in cases:
+        args = dict(batch=B, tokens=T, heads=H, key_heads=KH, state=p(S), q=p(Q), k=p(Q),
+                    v=p(V), decay=p(G), beta=p(G), out=p(O), d=128)
+        args.update(case)
+        with pytest.raises(pb.PrismB200Error) as err:
+            pb.gdn_prefill_pinned_device(ex, args["batch"], args["tokens"], args["heads"],
+                                         args["key_heads"], args["state"], args["q"], args["k"],
+                                         args["v"], args["decay"], args["beta"], args["out"],
+                                         d=args["d"])
+        assert err.value.code in (pb.E_INVALID, pb.E_UNSUPPORTED), case
+    torch.cuda.synchronize()
+    ex.sync()
+    assert bool((S == 1).all()) and bool((O == 7).all())

@@ -277,51 +277,41 @@ __host__ __device__ constexpr size_t gdn_prep_smem() {
   return (size_t)(2 * kChunk * kKS + kChunk * (kChunk + 1) + kChunk * kMS4 + 3 * kChunk) * 4;
 }
 
-// Scan over the chunks of one (sequence, head) for R state rows.
-// grid (128/R, heads, batch), kScanThreads threads.  R == 64 (the wide
-// grid): warp w owns state rows w + 16a (a < 4) and lane l tokens l + 32b
-// (b < 2) of every chunk tile.  R == 16 (the small-batch grid): the lower
-// threads form the tiles (thread mappings at each phase) while the upper
-// half issues the next chunk's K, Q and V asynchronous copies into a second
-// buffer; the next chunk's M, CQ, cum and P[C-1] arrive by bulk copies on an
-// mbarrier once the current chunk's outputs are formed.
+// Scan over the chunks of one (sequence, head) for kScanR state rows.
+// grid (128 / kScanR, heads, batch), kScanThreads threads.  In each chunk the
+// lower threads form the tiles (thread mappings at each phase) while the
+// upper half issues the next chunk's K, Q and V asynchronous copies into a
+// second buffer; the next chunk's M, CQ, cum and P[C-1] arrive by bulk
+// copies on an mbarrier once the current chunk's outputs are formed.  Small
+// row groups measured faster than 64-row groups at every batch (per row and
+// chunk the tiles and copies overlap better), so every batch uses them.
 constexpr int kScanThreads = 512;
+constexpr int kScanR = 16;
 
-template <int R>
-__host__ __device__ constexpr bool gdn_scan_prefetch() {
-  return R == 16;
-}
-
-template <int R>
-__host__ __device__ constexpr size_t gdn_scan_smem() {
-  // S[R][D] K,Q[C][kKS] M[C][ms] CQ[C][ms] V[C][R] KD,QD,DL[R][ms] cum plast,
-  // and with prefetch a second K, Q, V (ms = kMS4 with prefetch, else kMS)
-  constexpr int ms = gdn_scan_prefetch<R>() ? kMS4 : kMS;
-  return (size_t)(R * kGdnD + (gdn_scan_prefetch<R>() ? 2 : 1) * (2 * kChunk * kKS + kChunk * R) +
-                  2 * kChunk * ms + 3 * R * ms +
-                  (gdn_scan_prefetch<R>() ? 2 : 1) * 2 * kChunk) *
+__host__ __device__ constexpr size_t gdn_chunk_scan_smem() {
+  // S[R][D], two K, Q [C][kKS] and V [C][R], M, CQ [C][kMS4], KD, QD, DL
+  // [R][kMS4], two cum/plast [2][C]
+  return (size_t)(kScanR * kGdnD + 2 * (2 * kChunk * kKS + kChunk * kScanR) + 2 * kChunk * kMS4 +
+                  3 * kScanR * kMS4 + 2 * 2 * kChunk) *
          4;
 }
 
-template <int R>
 __global__ void __launch_bounds__(kScanThreads, 1) gdn_chunk_scan_kernel(GdnPrefillArgs p) {
-  constexpr int D = kGdnD, C = kChunk;
-  constexpr bool PF = gdn_scan_prefetch<R>();
-  // row strides of M, CQ (MS) and KD, QD, DL (CP): 16-byte rows with
-  // prefetch, where those tiles are read as float4 along the row
-  constexpr int MS = PF ? kMS4 : kMS, CP = PF ? kMS4 : kChunk + 1;
-  constexpr int NB = PF ? 2 : 1;
+  constexpr int D = kGdnD, C = kChunk, R = kScanR;
+  // row strides of M, CQ (MS) and KD, QD, DL (CP): 16-byte rows, read as
+  // float4 along the row
+  constexpr int MS = kMS4, CP = kMS4;
   extern __shared__ __align__(16) float sm[];
   float *S = sm;                          // [R][D]
-  float *Kb = S + R * D;                  // [NB][C][kKS]
-  float *Qb = Kb + NB * C * kKS;          // [NB][C][kKS]
-  float *Vb = Qb + NB * C * kKS;          // [NB][C][R]
-  float *M = Vb + NB * C * R;             // [C][MS]
+  float *Kb = S + R * D;                  // [2][C][kKS]
+  float *Qb = Kb + 2 * C * kKS;           // [2][C][kKS]
+  float *Vb = Qb + 2 * C * kKS;           // [2][C][R]
+  float *M = Vb + 2 * C * R;              // [C][MS]
   float *CQ = M + C * MS;                 // [C][MS]
   float *KD = CQ + C * MS;                // [R][CP]
   float *QD = KD + R * CP;                // [R][CP]
   float *DL = QD + R * CP;                // [R][CP]  deltas
-  float *cumb = DL + R * CP;              // [NB][2][C]: cum, then plast
+  float *cumb = DL + R * CP;              // [2][2][C]: cum, then plast
   const GdnBatchArgs &a = p.g;
   const int g = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kh = h % a.key_heads;
@@ -367,333 +357,187 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_chunk_scan_kernel(GdnPref
       bulk_g2s(cumb + buf * 2 * C, scr + 2 * C * kMS4, 2 * C * 4, &sbar);
     }
   };
-  if (PF) {
-    if (tid == 0) {
-      mbar_init(&sbar, 1);
-      mbar_init_fence();
-    }
-    __syncthreads();
-    if (p.nchunks > 0) {
-      if (tid >= kScanThreads / 2) issue(0, 0, tid - kScanThreads / 2, kScanThreads / 2);
-      issue_scr(0, 0);
-    }
+  if (tid == 0) {
+    mbar_init(&sbar, 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+  if (p.nchunks > 0) {
+    if (tid >= kScanThreads / 2) issue(0, 0, tid - kScanThreads / 2, kScanThreads / 2);
+    issue_scr(0, 0);
   }
   const float oscale = 1.0f / sqrtf((float)D);
   bool finite = true;
-  int stalled = -1;  // with prefetch: the chunk whose copies never completed
+  int stalled = -1;  // the chunk whose copies never completed
   for (int c = 0; c < p.nchunks; ++c) {
     const int t0 = c * p.chunk;
     const int n = min(p.chunk, a.T - t0);
-    const int buf = PF ? (c & 1) : 0;
-    const float *scr = p.scratch + (((long)b * a.heads + h) * p.nchunks + c) * kChunkScratch;
+    const int buf = c & 1;
     __syncthreads();
-    if (PF) {
-      // this chunk's K, Q, V (copied by the upper half during the chunk
-      // before) and M, CQ, cum, P[C-1] (bulk copies)
-      if (tid >= kScanThreads / 2) asm volatile("cp.async.wait_group 0;" ::: "memory");
-      const bool ok = mbar_wait_bounded(&sbar, c & 1, a.status);
-      if (!__syncthreads_and(ok)) {
-        stalled = c;
-        break;
-      }
-    } else {
-      issue(c, 0, tid, blockDim.x);
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-      for (int i = tid; i < C * C; i += blockDim.x) {
-        M[(i / C) * MS + i % C] = scr[(i / C) * kMS4 + i % C];
-        CQ[(i / C) * MS + i % C] = scr[C * kMS4 + (i / C) * kMS4 + i % C];
-      }
-      for (int t = tid; t < 2 * C; t += blockDim.x) cumb[t] = scr[2 * C * kMS4 + t];
-      __syncthreads();
+    // this chunk's K, Q, V (copied by the upper half during the chunk before)
+    // and M, CQ, cum, P[C-1] (bulk copies)
+    if (tid >= kScanThreads / 2) asm volatile("cp.async.wait_group 0;" ::: "memory");
+    const bool ok = mbar_wait_bounded(&sbar, c & 1, a.status);
+    if (!__syncthreads_and(ok)) {
+      stalled = c;
+      break;
     }
     const float *K = Kb + buf * C * kKS, *Q = Qb + buf * C * kKS, *V = Vb + buf * C * R;
     const float *cum = cumb + buf * 2 * C, *plast = cum + C;
-    // Register tiles: warp ti = tid / 32 owns rows r = ti + 16a (a < TR), lane
-    // tj = tid % 32 tokens t = tj + 32b (b < TT); every output keeps the
-    // accumulation order of the one-output-per-thread form.
-    constexpr int TR = R / 16, TT = C / 32;
-    const int ti = tid / 32, tj = tid % 32;
-    // KD[r][t] = S_r . k_t, QD[r][t] = S_r . q_t
-    // R == 16: thread u < 128 owns rows 8g..8g+7 (g = u / 64) of token u % 64
+    // Every output keeps the accumulation order of the one-output-per-thread
+    // form (so a sequence's result does not depend on its batch).
+    // KD[r][t] = S_r . k_t, QD[r][t] = S_r . q_t: thread u < 128 owns rows
+    // 8g..8g+7 (g = u / 64) of token u % 64
     // (each K/Q row read by 2 warps, each S row load shared by K and Q),
     // while the upper half of the CTA issues the next chunk's copies
-    if constexpr (R == 16) {
-      if (tid < 128) {
-        const int g8 = 8 * (tid / 64), t = tid % 64;
-        float dk[8], dq[8];
+    if (tid < 128) {
+      const int g8 = 8 * (tid / 64), t = tid % 64;
+      float dk[8], dq[8];
 #pragma unroll
-        for (int a8 = 0; a8 < 8; ++a8) dk[a8] = dq[a8] = 0.0f;
-#pragma unroll 2
-        for (int x = 0; x < D / 4; ++x) {
-          const float4 u = reinterpret_cast<const float4 *>(K + t * kKS)[x];
-          const float4 w = reinterpret_cast<const float4 *>(Q + t * kKS)[x];
-#pragma unroll
-          for (int a8 = 0; a8 < 8; ++a8) {
-            const float4 sr = reinterpret_cast<const float4 *>(S + (g8 + a8) * D)[x];
-            dk[a8] = fmaf(sr.x, u.x, fmaf(sr.y, u.y, fmaf(sr.z, u.z, fmaf(sr.w, u.w, dk[a8]))));
-            dq[a8] = fmaf(sr.x, w.x, fmaf(sr.y, w.y, fmaf(sr.z, w.z, fmaf(sr.w, w.w, dq[a8]))));
-          }
-        }
-#pragma unroll
-        for (int a8 = 0; a8 < 8; ++a8) {
-          const int r = g8 + a8;
-          KD[r * CP + t] = V[t * R + r] - cum[t] * dk[a8];
-          QD[r * CP + t] = dq[a8];
-        }
-      } else if (tid >= kScanThreads / 2 && c + 1 < p.nchunks) {
-        issue(c + 1, buf ^ 1, tid - kScanThreads / 2, kScanThreads / 2);
-      }
-    } else {
-      float dk[TR][TT], dq[TR][TT];
-#pragma unroll
-      for (int ai = 0; ai < TR; ++ai)
-#pragma unroll
-        for (int bi = 0; bi < TT; ++bi) dk[ai][bi] = dq[ai][bi] = 0.0f;
+      for (int a8 = 0; a8 < 8; ++a8) dk[a8] = dq[a8] = 0.0f;
 #pragma unroll 2
       for (int x = 0; x < D / 4; ++x) {
-        float4 sv[TR], kv[TT], qv[TT];
+        const float4 u = reinterpret_cast<const float4 *>(K + t * kKS)[x];
+        const float4 w = reinterpret_cast<const float4 *>(Q + t * kKS)[x];
 #pragma unroll
-        for (int ai = 0; ai < TR; ++ai) sv[ai] = reinterpret_cast<const float4 *>(S + (ti + 16 * ai) * D)[x];
-#pragma unroll
-        for (int bi = 0; bi < TT; ++bi) {
-          kv[bi] = reinterpret_cast<const float4 *>(K + (tj + 32 * bi) * kKS)[x];
-          qv[bi] = reinterpret_cast<const float4 *>(Q + (tj + 32 * bi) * kKS)[x];
+        for (int a8 = 0; a8 < 8; ++a8) {
+          const float4 sr = reinterpret_cast<const float4 *>(S + (g8 + a8) * D)[x];
+          dk[a8] = fmaf(sr.x, u.x, fmaf(sr.y, u.y, fmaf(sr.z, u.z, fmaf(sr.w, u.w, dk[a8]))));
+          dq[a8] = fmaf(sr.x, w.x, fmaf(sr.y, w.y, fmaf(sr.z, w.z, fmaf(sr.w, w.w, dq[a8]))));
         }
-#pragma unroll
-        for (int ai = 0; ai < TR; ++ai)
-#pragma unroll
-          for (int bi = 0; bi < TT; ++bi) {
-            const float4 sr = sv[ai], u = kv[bi], w = qv[bi];
-            dk[ai][bi] = fmaf(sr.x, u.x, fmaf(sr.y, u.y, fmaf(sr.z, u.z, fmaf(sr.w, u.w, dk[ai][bi]))));
-            dq[ai][bi] = fmaf(sr.x, w.x, fmaf(sr.y, w.y, fmaf(sr.z, w.z, fmaf(sr.w, w.w, dq[ai][bi]))));
-          }
       }
 #pragma unroll
-      for (int ai = 0; ai < TR; ++ai)
-#pragma unroll
-        for (int bi = 0; bi < TT; ++bi) {
-          const int r = ti + 16 * ai, t = tj + 32 * bi;
-          // W[r][t] = v_rt - cum_t KD[r][t]  (into KD)
-          KD[r * CP + t] = V[t * R + r] - cum[t] * dk[ai][bi];
-          QD[r * CP + t] = dq[ai][bi];
-        }
+      for (int a8 = 0; a8 < 8; ++a8) {
+        const int r = g8 + a8;
+        KD[r * CP + t] = V[t * R + r] - cum[t] * dk[a8];
+        QD[r * CP + t] = dq[a8];
+      }
+    } else if (tid >= kScanThreads / 2 && c + 1 < p.nchunks) {
+      issue(c + 1, buf ^ 1, tid - kScanThreads / 2, kScanThreads / 2);
     }
     __syncthreads();
     // delta[r][t] = sum_{j<=t} M[t][j] W[r][j]
-    if constexpr (R == 16) {
-      if (tid < 256) {
-        const int g4 = 4 * (tid / 64), t = tid % 64;
-        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        // four j per step (float4 along M's row and the W rows), the terms
-        // j > t masked: the warp's tokens end at (t | 31)
-        const int jend = (t | 31) + 1;
+    if (tid < 256) {
+      const int g4 = 4 * (tid / 64), t = tid % 64;
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      // four j per step (float4 along M's row and the W rows), the terms
+      // j > t masked: the warp's tokens end at (t | 31)
+      const int jend = (t | 31) + 1;
 #pragma unroll 2
-        for (int j4 = 0; j4 < jend; j4 += 4) {
-          const float4 m4 = *reinterpret_cast<const float4 *>(M + t * MS + j4);
-          float4 w4[4];
+      for (int j4 = 0; j4 < jend; j4 += 4) {
+        const float4 m4 = *reinterpret_cast<const float4 *>(M + t * MS + j4);
+        float4 w4[4];
 #pragma unroll
-          for (int a4 = 0; a4 < 4; ++a4)
-            w4[a4] = *reinterpret_cast<const float4 *>(KD + (g4 + a4) * CP + j4);
+        for (int a4 = 0; a4 < 4; ++a4)
+          w4[a4] = *reinterpret_cast<const float4 *>(KD + (g4 + a4) * CP + j4);
 #pragma unroll
-          for (int a4 = 0; a4 < 4; ++a4) {
-            if (j4 <= t) acc[a4] = fmaf(m4.x, w4[a4].x, acc[a4]);
-            if (j4 + 1 <= t) acc[a4] = fmaf(m4.y, w4[a4].y, acc[a4]);
-            if (j4 + 2 <= t) acc[a4] = fmaf(m4.z, w4[a4].z, acc[a4]);
-            if (j4 + 3 <= t) acc[a4] = fmaf(m4.w, w4[a4].w, acc[a4]);
-          }
+        for (int a4 = 0; a4 < 4; ++a4) {
+          if (j4 <= t) acc[a4] = fmaf(m4.x, w4[a4].x, acc[a4]);
+          if (j4 + 1 <= t) acc[a4] = fmaf(m4.y, w4[a4].y, acc[a4]);
+          if (j4 + 2 <= t) acc[a4] = fmaf(m4.z, w4[a4].z, acc[a4]);
+          if (j4 + 3 <= t) acc[a4] = fmaf(m4.w, w4[a4].w, acc[a4]);
         }
-#pragma unroll
-        for (int a4 = 0; a4 < 4; ++a4) DL[(g4 + a4) * CP + t] = t < n ? acc[a4] : 0.0f;
-      }
-    } else {
-      float acc[TR][TT];
-#pragma unroll
-      for (int ai = 0; ai < TR; ++ai)
-#pragma unroll
-        for (int bi = 0; bi < TT; ++bi) acc[ai][bi] = 0.0f;
-      const int tmax = tj + 32 * (TT - 1);
-      #pragma unroll 8
-      for (int j = 0; j <= tmax; ++j) {
-        float wv[TR], mv[TT];
-#pragma unroll
-        for (int ai = 0; ai < TR; ++ai) wv[ai] = KD[(ti + 16 * ai) * CP + j];
-#pragma unroll
-        for (int bi = 0; bi < TT; ++bi) mv[bi] = M[(tj + 32 * bi) * MS + j];
-#pragma unroll
-        for (int bi = 0; bi < TT; ++bi)
-          if (j <= tj + 32 * bi)
-#pragma unroll
-            for (int ai = 0; ai < TR; ++ai) acc[ai][bi] = fmaf(mv[bi], wv[ai], acc[ai][bi]);
       }
 #pragma unroll
-      for (int ai = 0; ai < TR; ++ai)
-#pragma unroll
-        for (int bi = 0; bi < TT; ++bi) {
-          const int t = tj + 32 * bi;
-          DL[(ti + 16 * ai) * CP + t] = t < n ? acc[ai][bi] : 0.0f;
-        }
+      for (int a4 = 0; a4 < 4; ++a4) DL[(g4 + a4) * CP + t] = t < n ? acc[a4] : 0.0f;
     }
     __syncthreads();
     // o[r][t] = (cum_t QD[r][t] + sum_{j<=t} CQ[t][j] delta[r][j]) / sqrt(d),
     // staged as [t][r] in the KD area (free now) for coalesced stores
-    if constexpr (R == 16) {
-      if (tid < 256) {
-        const int g4 = 4 * (tid / 64), t = tid % 64;
-        float acc[4];
+    if (tid < 256) {
+      const int g4 = 4 * (tid / 64), t = tid % 64;
+      float acc[4];
 #pragma unroll
-        for (int a4 = 0; a4 < 4; ++a4) acc[a4] = cum[t] * QD[(g4 + a4) * CP + t];
-        const int jend = (t | 31) + 1;
+      for (int a4 = 0; a4 < 4; ++a4) acc[a4] = cum[t] * QD[(g4 + a4) * CP + t];
+      const int jend = (t | 31) + 1;
 #pragma unroll 2
-        for (int j4 = 0; j4 < jend; j4 += 4) {
-          const float4 c4 = *reinterpret_cast<const float4 *>(CQ + t * MS + j4);
-          float4 d4[4];
+      for (int j4 = 0; j4 < jend; j4 += 4) {
+        const float4 c4 = *reinterpret_cast<const float4 *>(CQ + t * MS + j4);
+        float4 d4[4];
 #pragma unroll
-          for (int a4 = 0; a4 < 4; ++a4)
-            d4[a4] = *reinterpret_cast<const float4 *>(DL + (g4 + a4) * CP + j4);
-#pragma unroll
-          for (int a4 = 0; a4 < 4; ++a4) {
-            if (j4 <= t) acc[a4] = fmaf(c4.x, d4[a4].x, acc[a4]);
-            if (j4 + 1 <= t) acc[a4] = fmaf(c4.y, d4[a4].y, acc[a4]);
-            if (j4 + 2 <= t) acc[a4] = fmaf(c4.z, d4[a4].z, acc[a4]);
-            if (j4 + 3 <= t) acc[a4] = fmaf(c4.w, d4[a4].w, acc[a4]);
-          }
-        }
-        float *O = KD;  // [C][R]
-#pragma unroll
-        for (int a4 = 0; a4 < 4; ++a4) O[t * R + g4 + a4] = acc[a4] * oscale;
-      } else if (tid < 384) {
-        // S_r <- cum_last S_r + sum_j plast_j delta_rj k_j: thread u = tid - 256
-        // owns rows 4 (u / 32) .. + 3 of columns 4 (u % 32) .. + 3, so each K
-        // row is read by 4 warps.  It reads and writes only its own elements
-        // of S (and the O phase none), so it runs beside the O phase.
-        const int u = tid - 256, g4 = 4 * (u / 32), x4 = 4 * (u % 32);
-        const float last = cum[n - 1];
-        float acc[4][4];
+        for (int a4 = 0; a4 < 4; ++a4)
+          d4[a4] = *reinterpret_cast<const float4 *>(DL + (g4 + a4) * CP + j4);
 #pragma unroll
         for (int a4 = 0; a4 < 4; ++a4) {
-          const float4 s0 = reinterpret_cast<const float4 *>(S + (g4 + a4) * D + x4)[0];
-          acc[a4][0] = last * s0.x; acc[a4][1] = last * s0.y;
-          acc[a4][2] = last * s0.z; acc[a4][3] = last * s0.w;
+          if (j4 <= t) acc[a4] = fmaf(c4.x, d4[a4].x, acc[a4]);
+          if (j4 + 1 <= t) acc[a4] = fmaf(c4.y, d4[a4].y, acc[a4]);
+          if (j4 + 2 <= t) acc[a4] = fmaf(c4.z, d4[a4].z, acc[a4]);
+          if (j4 + 3 <= t) acc[a4] = fmaf(c4.w, d4[a4].w, acc[a4]);
         }
-        // four j per step (plast and the delta rows as float4), then the
-        // j < n left over one at a time
-        int j = 0;
+      }
+      float *O = KD;  // [C][R]
+#pragma unroll
+      for (int a4 = 0; a4 < 4; ++a4) O[t * R + g4 + a4] = acc[a4] * oscale;
+    } else if (tid < 384) {
+      // S_r <- cum_last S_r + sum_j plast_j delta_rj k_j: thread u = tid - 256
+      // owns rows 4 (u / 32) .. + 3 of columns 4 (u % 32) .. + 3, so each K
+      // row is read by 4 warps.  It reads and writes only its own elements
+      // of S (and the O phase none), so it runs beside the O phase.
+      const int u = tid - 256, g4 = 4 * (u / 32), x4 = 4 * (u % 32);
+      const float last = cum[n - 1];
+      float acc[4][4];
+#pragma unroll
+      for (int a4 = 0; a4 < 4; ++a4) {
+        const float4 s0 = reinterpret_cast<const float4 *>(S + (g4 + a4) * D + x4)[0];
+        acc[a4][0] = last * s0.x; acc[a4][1] = last * s0.y;
+        acc[a4][2] = last * s0.z; acc[a4][3] = last * s0.w;
+      }
+      // four j per step (plast and the delta rows as float4), then the
+      // j < n left over one at a time
+      int j = 0;
 #pragma unroll 2
-        for (; j + 4 <= n; j += 4) {
-          const float4 p4 = *reinterpret_cast<const float4 *>(plast + j);
-          const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
-          float dl[4][4];
-          float4 kr[4];
+      for (; j + 4 <= n; j += 4) {
+        const float4 p4 = *reinterpret_cast<const float4 *>(plast + j);
+        const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
+        float dl[4][4];
+        float4 kr[4];
 #pragma unroll
-          for (int a4 = 0; a4 < 4; ++a4) {
-            const float4 d4 = *reinterpret_cast<const float4 *>(DL + (g4 + a4) * CP + j);
-            dl[a4][0] = d4.x; dl[a4][1] = d4.y; dl[a4][2] = d4.z; dl[a4][3] = d4.w;
-          }
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            kr[e] = reinterpret_cast<const float4 *>(K + (j + e) * kKS + x4)[0];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float kx[4] = {kr[e].x, kr[e].y, kr[e].z, kr[e].w};
-#pragma unroll
-            for (int a4 = 0; a4 < 4; ++a4) {
-              const float cf = pj[e] * dl[a4][e];
-#pragma unroll
-              for (int c4 = 0; c4 < 4; ++c4) acc[a4][c4] = fmaf(cf, kx[c4], acc[a4][c4]);
-            }
-          }
+        for (int a4 = 0; a4 < 4; ++a4) {
+          const float4 d4 = *reinterpret_cast<const float4 *>(DL + (g4 + a4) * CP + j);
+          dl[a4][0] = d4.x; dl[a4][1] = d4.y; dl[a4][2] = d4.z; dl[a4][3] = d4.w;
         }
-        for (; j < n; ++j) {
-          const float4 k0 = reinterpret_cast<const float4 *>(K + j * kKS + x4)[0];
-          const float kx[4] = {k0.x, k0.y, k0.z, k0.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          kr[e] = reinterpret_cast<const float4 *>(K + (j + e) * kKS + x4)[0];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float kx[4] = {kr[e].x, kr[e].y, kr[e].z, kr[e].w};
 #pragma unroll
           for (int a4 = 0; a4 < 4; ++a4) {
-            const float cf = plast[j] * DL[(g4 + a4) * CP + j];
+            const float cf = pj[e] * dl[a4][e];
 #pragma unroll
             for (int c4 = 0; c4 < 4; ++c4) acc[a4][c4] = fmaf(cf, kx[c4], acc[a4][c4]);
           }
         }
+      }
+      for (; j < n; ++j) {
+        const float4 k0 = reinterpret_cast<const float4 *>(K + j * kKS + x4)[0];
+        const float kx[4] = {k0.x, k0.y, k0.z, k0.w};
 #pragma unroll
         for (int a4 = 0; a4 < 4; ++a4) {
-          float *sr = S + (g4 + a4) * D + x4;
+          const float cf = plast[j] * DL[(g4 + a4) * CP + j];
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            finite &= is_finite_f(acc[a4][c4]);
-            sr[c4] = acc[a4][c4];
-          }
+          for (int c4 = 0; c4 < 4; ++c4) acc[a4][c4] = fmaf(cf, kx[c4], acc[a4][c4]);
         }
       }
-    } else {
-      float acc[TR][TT];
 #pragma unroll
-      for (int ai = 0; ai < TR; ++ai)
+      for (int a4 = 0; a4 < 4; ++a4) {
+        float *sr = S + (g4 + a4) * D + x4;
 #pragma unroll
-        for (int bi = 0; bi < TT; ++bi)
-          acc[ai][bi] = cum[tj + 32 * bi] * QD[(ti + 16 * ai) * CP + tj + 32 * bi];
-      const int tmax = tj + 32 * (TT - 1);
-      #pragma unroll 8
-      for (int j = 0; j <= tmax; ++j) {
-        float dv[TR], cv[TT];
-#pragma unroll
-        for (int ai = 0; ai < TR; ++ai) dv[ai] = DL[(ti + 16 * ai) * CP + j];
-#pragma unroll
-        for (int bi = 0; bi < TT; ++bi) cv[bi] = CQ[(tj + 32 * bi) * MS + j];
-#pragma unroll
-        for (int bi = 0; bi < TT; ++bi)
-          if (j <= tj + 32 * bi)
-#pragma unroll
-            for (int ai = 0; ai < TR; ++ai) acc[ai][bi] = fmaf(cv[bi], dv[ai], acc[ai][bi]);
+        for (int c4 = 0; c4 < 4; ++c4) {
+          finite &= is_finite_f(acc[a4][c4]);
+          sr[c4] = acc[a4][c4];
+        }
       }
-      float *O = KD;  // [C][R]
-#pragma unroll
-      for (int ai = 0; ai < TR; ++ai)
-#pragma unroll
-        for (int bi = 0; bi < TT; ++bi)
-          O[(tj + 32 * bi) * R + ti + 16 * ai] = acc[ai][bi] * oscale;
     }
     __syncthreads();
-    if (PF && c + 1 < p.nchunks) issue_scr(c + 1, buf ^ 1);  // M, CQ are free now
+    if (c + 1 < p.nchunks) issue_scr(c + 1, buf ^ 1);  // M, CQ are free now
     for (int i = tid; i < R * C; i += blockDim.x) {
       const int t = i / R, r = i % R;  // r fastest: coalesced output stores
       if (t < n) a.out[(((long)b * a.T + t0 + t) * a.heads + h) * D + r0 + r] = KD[t * R + r];
     }
-    // S_r <- cum_last S_r + sum_j plast_j delta_rj k_j (R == 16: beside the O
-    // phase above); warp ti owns rows r = ti + 16a, lane tj columns
-    // x = 4 tj .. 4 tj + 3
-    if constexpr (R != 16) {
-      const float last = cum[n - 1];
-      float acc[TR][4];
-#pragma unroll
-      for (int ai = 0; ai < TR; ++ai) {
-        const float4 s0 = reinterpret_cast<const float4 *>(S + (ti + 16 * ai) * D + 4 * tj)[0];
-        acc[ai][0] = last * s0.x; acc[ai][1] = last * s0.y;
-        acc[ai][2] = last * s0.z; acc[ai][3] = last * s0.w;
-      }
-      #pragma unroll 8
-      for (int j = 0; j < n; ++j) {
-        float cf[TR];
-#pragma unroll
-        for (int ai = 0; ai < TR; ++ai) cf[ai] = plast[j] * DL[(ti + 16 * ai) * CP + j];
-        const float4 k0 = reinterpret_cast<const float4 *>(K + j * kKS + 4 * tj)[0];
-        const float kx[4] = {k0.x, k0.y, k0.z, k0.w};
-#pragma unroll
-        for (int ai = 0; ai < TR; ++ai)
-#pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) acc[ai][c4] = fmaf(cf[ai], kx[c4], acc[ai][c4]);
-      }
-      __syncthreads();  // every thread has read S before it is overwritten
-#pragma unroll
-      for (int ai = 0; ai < TR; ++ai) {
-        float *sr = S + (ti + 16 * ai) * D + 4 * tj;
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          finite &= is_finite_f(acc[ai][c4]);
-          sr[c4] = acc[ai][c4];
-        }
-      }
-    }
   }
-  if (PF && stalled >= 0) {
+  if (stalled >= 0) {
     // a chunk's bulk copies never completed (reported): wait for them once
     // more, again bounded, and for the asynchronous copies in flight, then
     // leave the state as it was

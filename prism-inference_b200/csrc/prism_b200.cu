@@ -777,22 +777,14 @@ extern "C" int prism_b200_gdn_prefill_device(prism_b200_executor *ex, int batch,
   cudaLaunchConfig_t cfg = pdl_config(dim3(p.nchunks, heads, batch), dim3(kPrepThreads),
                                       prep_smem, s, attr, ex->pdl);
   CK(cudaLaunchKernelEx(&cfg, gdn_chunk_prep_kernel, p), "GDN prep launch");
-  // 16 rows per CTA while few (sequence, head) pairs exist, else 64
-  const bool wide = (long)batch * heads * 2 >= ex->num_sms;
-  if (wide) {
-    const size_t smem = gdn_scan_smem<64>();
-    CK(cudaFuncSetAttribute(gdn_chunk_scan_kernel<64>,
-                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+  {
+    const size_t smem = gdn_chunk_scan_smem();
+    CK(cudaFuncSetAttribute(gdn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)smem),
        "GDN scan attribute");
-    cfg = pdl_config(dim3(kGdnD / 64, heads, batch), dim3(kScanThreads), smem, s, attr, ex->pdl);
-    CK(cudaLaunchKernelEx(&cfg, gdn_chunk_scan_kernel<64>, p), "GDN scan launch");
-  } else {
-    const size_t smem = gdn_scan_smem<16>();
-    CK(cudaFuncSetAttribute(gdn_chunk_scan_kernel<16>,
-                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-       "GDN scan attribute");
-    cfg = pdl_config(dim3(kGdnD / 16, heads, batch), dim3(kScanThreads), smem, s, attr, ex->pdl);
-    CK(cudaLaunchKernelEx(&cfg, gdn_chunk_scan_kernel<16>, p), "GDN scan launch");
+    cfg = pdl_config(dim3(kGdnD / kScanR, heads, batch), dim3(kScanThreads), smem, s, attr,
+                     ex->pdl);
+    CK(cudaLaunchKernelEx(&cfg, gdn_chunk_scan_kernel, p), "GDN scan launch");
   }
   return PRISM_B200_OK;
 }
@@ -970,20 +962,14 @@ extern "C" int prism_b200_gdn_prefill_device_noalloc(prism_b200_executor *ex, in
   cudaLaunchConfig_t cfg = pdl_config(dim3(p.nchunks, heads, batch), dim3(kPrepThreads),
                                       prep_smem, s, attr, ex->pdl);
   CK(cudaLaunchKernelEx(&cfg, gdn_chunk_prep_kernel, p), "GDN prep launch");
-  if ((long)batch * heads * 2 >= ex->num_sms) {
-    const size_t smem = gdn_scan_smem<64>();
-    CK(cudaFuncSetAttribute(gdn_chunk_scan_kernel<64>,
-                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+  {
+    const size_t smem = gdn_chunk_scan_smem();
+    CK(cudaFuncSetAttribute(gdn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)smem),
        "GDN scan attribute");
-    cfg = pdl_config(dim3(kGdnD / 64, heads, batch), dim3(kScanThreads), smem, s, attr, ex->pdl);
-    CK(cudaLaunchKernelEx(&cfg, gdn_chunk_scan_kernel<64>, p), "GDN scan launch");
-  } else {
-    const size_t smem = gdn_scan_smem<16>();
-    CK(cudaFuncSetAttribute(gdn_chunk_scan_kernel<16>,
-                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-       "GDN scan attribute");
-    cfg = pdl_config(dim3(kGdnD / 16, heads, batch), dim3(kScanThreads), smem, s, attr, ex->pdl);
-    CK(cudaLaunchKernelEx(&cfg, gdn_chunk_scan_kernel<16>, p), "GDN scan launch");
+    cfg = pdl_config(dim3(kGdnD / kScanR, heads, batch), dim3(kScanThreads), smem, s, attr,
+                     ex->pdl);
+    CK(cudaLaunchKernelEx(&cfg, gdn_chunk_scan_kernel, p), "GDN scan launch");
   }
   return PRISM_B200_OK;
 }

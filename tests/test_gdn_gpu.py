@@ -102,11 +102,11 @@ def test_config2_prefill_4096_tokens(ex, oracle):
 
 
 def test_prefill_is_batch_invariant(ex):
-    """A sequence prefilled alone (16 state rows per CTA, with prefetch) and
-    as row 5 of a batch of 16 (64 state rows per CTA) gives the same bits:
-    both tilings keep every output's accumulation order, and the prep
-    kernel is shared.  The nonzero starting state and a ragged last chunk
-    cover the state update and the zero-filled rows."""
+    """A sequence prefilled alone and as row 5 of a batch of 16 gives the
+    same bits: every output keeps one accumulation order whatever the grid,
+    and each (sequence, head) reads only its own chunk scratch.  The nonzero
+    starting state and a ragged last chunk cover the state update and the
+    zero-filled rows."""
     T, heads, d = 1000, 16, 128
     q, k, v, decay, beta = inputs(16, T, heads, heads, seed=77)
     rng = np.random.default_rng(78)

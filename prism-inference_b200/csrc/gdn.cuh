@@ -218,7 +218,8 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefill
 #pragma unroll
       for (int ai = 0; ai < TA; ++ai)
 #pragma unroll
-        for (int bi = 0; bi < TA; ++bi) {
+        for (int bi = 0; bi <= ai; ++bi) {
+          // bi > ai puts every j above every t: those dots are never used
           const float4 u = kj[bi], w = kt[ai], z = qt[ai];
           dkk[ai][bi] = fmaf(u.x, w.x, fmaf(u.y, w.y, fmaf(u.z, w.z, fmaf(u.w, w.w, dkk[ai][bi]))));
           dkq[ai][bi] = fmaf(u.x, z.x, fmaf(u.y, z.y, fmaf(u.z, z.z, fmaf(u.w, z.w, dkq[ai][bi]))));

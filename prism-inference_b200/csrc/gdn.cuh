@@ -142,14 +142,16 @@ __device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, boo
 
 
 // grid (nchunks, heads, batch)
-__global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefillArgs p) {
+// Three CTAs per SM: the decay products and beta * CK reuse the K and Q
+// space once the dots are in registers.
+__global__ void __launch_bounds__(kPrepThreads, 3) gdn_chunk_prep_kernel(GdnPrefillArgs p) {
   constexpr int D = kGdnD, C = kChunk;
   extern __shared__ __align__(16) float sm[];
   float *K = sm;                 // [C][kKS]
   float *Q = K + C * kKS;        // [C][kKS]
-  float *P = Q + C * kKS;        // [C][C+1]  decay products (padded)
-  float *Bm = P + C * (C + 1);   // [C][kMS4]  beta * CK
-  float *cum = Bm + C * kMS4;    // [C]
+  float *P = K;                  // [C][C+1]  decay products (padded), after the dots
+  float *Bm = Q;                 // [C][kMS4]  beta * CK, after the dots
+  float *cum = Q + C * kKS;      // [C]
   float *dec = cum + C;          // [C]
   float *bet = dec + C;          // [C]
   const GdnBatchArgs &a = p.g;
@@ -182,17 +184,6 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefill
       cum[t] = d;
     }
   }
-  // P[t][j] = P[t][j+1] * decay_{j+1}, P[t][t] = 1 (reference order)
-  for (int t = threadIdx.x; t < C; t += blockDim.x) {
-    float pr = 1.0f;  // the chain in a register, each product stored once
-    P[t * (C + 1) + t] = pr;
-    for (int j = t - 1; j >= 0; --j) {
-      pr = __fmul_rn(pr, dec[j + 1]);
-      P[t * (C + 1) + j] = pr;
-    }
-    for (int j = t + 1; j < C; ++j) P[t * (C + 1) + j] = 0.0f;
-  }
-  __syncthreads();
   // CK (strict lower) scaled by beta_t into Bm, CQ (lower) to scratch
   float *scr = p.scratch + (((long)b * a.heads + h) * p.nchunks + c) * kChunkScratch;
   float *Mout = scr, *CQout = scr + C * kMS4, *cumout = scr + 2 * C * kMS4, *plast = cumout + C;
@@ -225,6 +216,18 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefill
           dkq[ai][bi] = fmaf(u.x, z.x, fmaf(u.y, z.y, fmaf(u.z, z.z, fmaf(u.w, z.w, dkq[ai][bi]))));
         }
     }
+    __syncthreads();  // K and Q are read: their space takes P and Bm
+    // P[t][j] = P[t][j+1] * decay_{j+1}, P[t][t] = 1 (reference order)
+    for (int t = threadIdx.x; t < C; t += blockDim.x) {
+      float pr = 1.0f;  // the chain in a register, each product stored once
+      P[t * (C + 1) + t] = pr;
+      for (int j = t - 1; j >= 0; --j) {
+        pr = __fmul_rn(pr, dec[j + 1]);
+        P[t * (C + 1) + j] = pr;
+      }
+      for (int j = t + 1; j < C; ++j) P[t * (C + 1) + j] = 0.0f;
+    }
+    __syncthreads();
 #pragma unroll
     for (int ai = 0; ai < TA; ++ai)
 #pragma unroll
@@ -275,7 +278,9 @@ __global__ void __launch_bounds__(kPrepThreads) gdn_chunk_prep_kernel(GdnPrefill
 }
 
 __host__ __device__ constexpr size_t gdn_prep_smem() {
-  return (size_t)(2 * kChunk * kKS + kChunk * (kChunk + 1) + kChunk * kMS4 + 3 * kChunk) * 4;
+  static_assert(kChunk * (kChunk + 1) <= kChunk * kKS && kChunk * kMS4 <= kChunk * kKS,
+                "P and Bm fit the K and Q space");
+  return (size_t)(2 * kChunk * kKS + 3 * kChunk) * 4;
 }
 
 // Scan over the chunks of one (sequence, head) for kScanR state rows.
